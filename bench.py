@@ -1,0 +1,381 @@
+#!/usr/bin/env python
+"""bench.py -- Qwen3.6-35B-A3B MoE block on B200: the headline decode benchmark.
+
+Default workload (decode B=1): one step = one token through the full
+40-layer MoE sub-stack (``resid += moe_block_l(rmsnorm(resid))`` per layer, seeded
+synthetic Q4_K weights, ~18 GB resident) as one CUDA-graph replay of the C-ABI path.
+Every step decodes a DISTINCT token, so each step streams 40 x 9 experts' Q4_K bytes
+(637 MB of expert weights per token > the 126 MB L2: no L2 flush needed).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                  [--workload stack_decode|layer_decode|dequant] [--batch B]
+
+Multi-GPU (torchrun, one rank per GPU): batch-1 decode does not shard (a per-layer
+collective would cost more than the layer), so N ranks run N independent replicas on
+distinct tokens ("scaling": "weak", value = all ranks' tokens / max-over-ranks time).
+
+``--impl reference`` times the reference's own CPU MoE path (engine/m3_forward.py
+moe_block + rmsnorm glue, restated as the torch-f32 port in oracle/moe.py) on the host
+cores, rank 0 only, on a bounded per-step sample (a few layers of one token, scaled to the
+40-layer token).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+EXPERT_BYTES = 1_769_472            # one Q4_K expert: gate+up [1024,2048] + down [2048,512]
+ROUTER_BYTES = 256 * 2048 * 2
+WSG_BYTES = 2048 * 2
+N_LAYERS = 40
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--workload", choices=["stack_decode", "layer_decode", "dequant"], default="stack_decode")
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--layers", type=int, default=N_LAYERS)
+    p.add_argument("--seed", type=int, default=4)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--ref-layers-per-step", type=int, default=2)
+    return p.parse_args()
+
+
+def env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def committed_traffic(workload):
+    """DRAM bytes per step from the committed ncu summary (profiles/<workload>_traffic.json)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "%s_traffic.json" % workload)) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------------- clocks
+class ClockSampler(threading.Thread):
+    """Polls NVML (SM clock, throttle reasons) every ~2 ms while the timed region runs."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index):
+        super().__init__(daemon=True)
+        self.index = index
+        self.samples = []
+        self.reasons = 0
+        self.stop_ev = threading.Event()
+        self.max_mhz = None
+        self.ok = False
+
+    def run(self):
+        try:
+            import pynvml as N
+            N.nvmlInit()
+            h = N.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+            self.ok = True
+            while not self.stop_ev.is_set():
+                self.samples.append(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM))
+                try:
+                    self.reasons |= int(N.nvmlDeviceGetCurrentClocksEventReasons(h))
+                except Exception:
+                    self.reasons |= int(N.nvmlDeviceGetCurrentClocksThrottleReasons(h))
+                time.sleep(0.002)
+        except Exception:
+            self.ok = False
+
+    def result(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml_unavailable"]}
+        rs = [n for b, n in self.REASONS.items() if self.reasons & b and b != 0x1]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": rs,
+                "samples": len(self.samples)}
+
+
+def physical_index(local_rank):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            return int(vis.split(",")[local_rank])
+        except Exception:
+            return local_rank
+    return local_rank
+
+
+# ---------------------------------------------------------------------------------- CPU arm
+def cpu_sample(args, seconds_hint=None, threads=None):
+    """Time the reference's CPU path (oracle port) on a bounded sample: one token through
+    ``args.ref_layers_per_step`` layers of the stack. Returns (sec_per_layer, sample, cores)."""
+    import numpy as np
+    import torch
+    from oracle import moe as OM
+    from oracle import q4k
+    import __graft_entry__ as G
+    G.load_package()
+    from b200moe import synth
+    from b200moe.geometry import KIND_OF, stream_id
+    cores = threads or len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    nl = max(1, args.ref_layers_per_step)
+    layers = [OM.CachedLayer(lambda k, f, n, l=l: q4k.synth_blocks(args.seed, stream_id(l, KIND_OF[k]), f, n),
+                             synth.router_w(args.seed, l), synth.shared_gate_w(args.seed, l)) for l in range(nl)]
+    x0 = synth.bf16_bits_to_f32(synth.tokens(args.seed, args.batch, stream=0))
+    OM.stack_port(x0, layers, cores)          # untimed pass: fills each layer's byte cache
+    return layers, x0, cores, nl
+
+
+def run_reference(args):
+    rank, _, world = env_rank()
+    if rank != 0:
+        return 0
+    from oracle import moe as OM
+    layers, x0, cores, nl = cpu_sample(args)
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        OM.stack_port(x0, layers, cores)
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            times.append(dt)
+    sec_tok = (sum(times) / len(times)) * (args.layers / nl)
+    val = args.batch / sec_tok
+    sample = ("%d token(s) through %d of %d layers per step (torch-f32 port of engine/m3_forward.py "
+              "moe_block + rmsnorm_a; per-hit-expert Q4_K dequant inside the timed region; bytes "
+              "pre-generated), scaled x%g to the 40-layer token" % (args.batch, nl, args.layers, args.layers / nl))
+    line = {"impl": "reference", "metric": "moe_stack_decode_tok_per_s", "value": val, "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sec_tok,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded Q4_K, config-0 field law)",
+            "config": {"workload": "config4_stack_decode_b%d" % args.batch, "layers": args.layers,
+                       "batch": args.batch, "seed": args.seed},
+            "cpu_baseline": {"value": val, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------------- GPU arm
+def run_b200(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__ as G
+    G.load_package()
+    from b200moe import _abi, moe, synth
+    from b200moe.engine import DeviceEngine, DeviceLayer
+
+    rank, local_rank, world = env_rank()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    T = args.batch
+    K, W = args.steps, args.warmup
+    hbm_peak, peak_kind = peaks()
+    graph = None
+    expert_bytes = None
+
+    if args.workload == "stack_decode":
+        eng = DeviceEngine.synthetic(args.seed, args.layers, dev)
+        nl = args.layers
+        launches_per_step = 3 * nl
+        bytes_per_step = nl * (9 * EXPERT_BYTES * (1 if T == 1 else 0) + ROUTER_BYTES + WSG_BYTES + 2 * T * 2048 * 4)
+        ws = torch.empty(moe.stack_workspace_bytes(T), dtype=torch.uint8, device=dev)
+        tok_bits = synth.tokens(args.seed, (K + W) * T, stream=100 + rank)
+        tok = torch.from_numpy(synth.bf16_bits_to_f32(tok_bits).reshape(K + W, T, 2048).copy())
+        tok_dev = tok.to(dev)
+        x_in = torch.empty((T, 2048), dtype=torch.float32, device=dev)
+        resid = torch.empty_like(x_in)
+        ids_all = torch.zeros((K + W, nl, T, 8), dtype=torch.int32, device=dev)
+        ids_step = torch.zeros((nl, T, 8), dtype=torch.int32, device=dev)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            x_in.copy_(tok_dev[0])
+            resid.copy_(x_in)
+            moe.moe_stack(resid, eng, ws=ws, ids_out=ids_step)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            resid.copy_(x_in)
+            moe.moe_stack(resid, eng, ws=ws, ids_out=ids_step)
+
+        def step(i):
+            x_in.copy_(tok_dev[i], non_blocking=True)
+            graph.replay()
+            ids_all[i].copy_(ids_step, non_blocking=True)
+    elif args.workload == "layer_decode":
+        L = DeviceLayer.synthetic(args.seed, 0, dev, bias=(args.seed == 2))
+        # rotate over enough layer copies to exceed L2: per-step bytes are one layer's
+        nl = 1
+        launches_per_step = 3
+        tok_bits = synth.tokens(args.seed, (K + W) * T, stream=100 + rank)
+        tok_dev = torch.from_numpy(tok_bits.view(np.int16)).view(torch.bfloat16).reshape(K + W, T, 2048).to(dev)
+        out = torch.empty((T, 2048), dtype=torch.float32, device=dev)
+        ids_all = torch.zeros((K + W, 1, T, 8), dtype=torch.int32, device=dev)
+        bytes_per_step = None
+
+        def step(i):
+            moe.moe_block(tok_dev[i], L, 0, out=out)
+    else:
+        raise SystemExit("workload %s: use tests for dequant parity; bench focuses on decode" % args.workload)
+
+    # ---------------- value: device-resident inputs, CUDA events, max over ranks
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(physical_index(local_rank))
+    sampler.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for i in range(K):
+        step(W + i)
+    t_end.record()
+    torch.cuda.synchronize(dev)
+    sampler.stop_ev.set()
+    sampler.join()
+    ms = t_start.elapsed_time(t_end)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+        dist.barrier()
+    ms_step = ms / K
+    value = world * K * T / (ms / 1e3)
+
+    # algorithmic bytes: distinct experts actually touched per layer (+ shared, router, act)
+    ids_np = ids_all[W:].cpu().numpy()
+    if args.workload == "stack_decode":
+        uniq = [[len(np.unique(ids_np[i, l])) for l in range(nl)] for i in range(K)]
+        bytes_per_step = float(np.mean([sum((u + 1) * EXPERT_BYTES for u in row) for row in uniq])) + \
+            nl * (ROUTER_BYTES + WSG_BYTES + 2 * T * 2048 * 4)
+        expert_bytes = float(np.mean([sum((u + 1) * EXPERT_BYTES for u in row) for row in uniq]))
+    achieved = bytes_per_step / (ms_step / 1e3) / 1e9 if bytes_per_step else None
+
+    # ---------------- e2e: pinned host input -> graph -> host read of the result, every step
+    e2e = None
+    if args.workload == "stack_decode":
+        host_in = tok.pin_memory()
+        host_out = torch.empty((T, 2048), dtype=torch.float32).pin_memory()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        cur = torch.cuda.current_stream(dev)
+        for i in range(W):
+            x_in.copy_(host_in[i], non_blocking=True)
+            graph.replay()
+            host_out.copy_(resid, non_blocking=True)
+            cur.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0.record()
+        chk = 0.0
+        for i in range(K):
+            x_in.copy_(host_in[W + i], non_blocking=True)
+            graph.replay()
+            host_out.copy_(resid, non_blocking=True)
+            cur.synchronize()
+            chk += float(host_out[0, 0])
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ems = e0.elapsed_time(e1)
+        if world > 1:
+            tt = torch.tensor([ems], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ems = float(tt.item())
+        if not np.isfinite(chk):
+            raise SystemExit("non-finite result in e2e run")
+        e2e = {"value": world * K * T / (ems / 1e3), "unit": "tok/s", "h2d_bytes_per_step": T * 2048 * 4,
+               "d2h_bytes_per_step": T * 2048 * 4, "ms_per_step": ems / K,
+               "api": "b200moe.moe.moe_stack (C ABI b200moe_stack_decode) in a CUDA graph"}
+
+    # ---------------- CPU baseline (rank 0, N=1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "stack_decode":
+        from oracle import moe as OM
+        layers, x0, cores, nlp = cpu_sample(args)
+        ts = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            OM.stack_port(x0, layers, cores)
+            ts.append(time.perf_counter() - t0)
+        sec_tok = statistics.median(ts) * (args.layers / nlp)
+        cpu = {"value": T / sec_tok, "unit": "tok/s", "cores": cores, "kind": "port",
+               "sample": "1 token through %d of %d layers, median of 3, scaled x%g (torch-f32 port of "
+                         "engine/m3_forward.py moe_block + rmsnorm_a, per-hit-expert dequant timed)"
+                         % (nlp, args.layers, args.layers / nlp)}
+
+    traffic = committed_traffic(args.workload)
+    line = {
+        "metric": "moe_stack_decode_tok_per_s" if args.workload == "stack_decode" else "moe_layer_decode_tok_per_s",
+        "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Q4_K, config-0 field law; random-init weights)",
+        "config": {"workload": ("config4_stack_decode_b%d" % T) if args.workload == "stack_decode"
+                   else "config0_layer_decode_b%d" % T,
+                   "layers": nl, "batch": T, "seed": args.seed, "parallelism": "replicas%d" % world,
+                   "l2": "inputs larger than L2: distinct token per step, %.0f MB of Q4_K streamed per step"
+                         % ((bytes_per_step or 0) / 1e6)},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": (achieved / hbm_peak) if achieved else None,
+                     "traffic": traffic.get("dram_bytes_per_step") if traffic else None,
+                     "peak_kind": peak_kind,
+                     "kernel": "one graph replay = %d kernels (router/shared K1, routed gate_up K2, down+combine K3 "
+                               "per layer)" % launches_per_step},
+        "gpu_launches": launches_per_step * K,
+        "clocks": sampler.result(),
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+    }
+    if args.workload == "stack_decode":
+        line["north_star"] = {"expert_bytes_per_token": expert_bytes,
+                              "frac_of_8TBs": expert_bytes / (ms_step / 1e3) / 8e12,
+                              "target_frac": 0.60, "us_per_token": ms_step * 1e3 / T}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        graph = None
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

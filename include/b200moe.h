@@ -1,0 +1,111 @@
+/* b200moe.h -- C ABI of the B200 (sm_100a) Qwen3.6-35B-A3B MoE block.
+ *
+ * Plain pointers, sizes and an opaque `void *stream` (a cudaStream_t; NULL = legacy default
+ * stream). Every entry point returns B200MOE_OK (0) or an error code and never throws; the
+ * message of the last failure on the calling thread is b200moe_last_error(). No entry point
+ * allocates device memory: scratch comes from a caller-provided workspace whose size the
+ * matching *_workspace_size() query returns. All device pointers must be 16-byte aligned.
+ *
+ * Geometry (checkpoints/Qwen3.6-35B-A3B.config.json:17,69,73,74,93 in the reference):
+ * hidden H = 2048, 256 routed experts, top-8, expert and shared intermediate I = 512.
+ *
+ * Weight layout in HBM (GGUF order, expert axis slowest, engine/README.md:185-190):
+ *   Q4_K super-block: 144 B per 256 weights {f16 d, f16 dmin, u8 scales[12], u8 qs[128]}
+ *   routed gate / up : [256 experts][512 rows][8 blocks]   (row = 2048 weights, 1152 B)
+ *   routed down      : [256 experts][2048 rows][2 blocks]  (row = 512 weights, 288 B)
+ *   shared gate / up : [512][8] blocks,  shared down: [2048][2] blocks
+ *   router W_g       : [256][2048] bf16,  shared-expert gate w_sg: [2048] bf16
+ */
+#ifndef B200MOE_H
+#define B200MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200MOE_ABI_VERSION 1
+#define B200MOE_HIDDEN 2048
+#define B200MOE_EXPERTS 256
+#define B200MOE_TOPK 8
+#define B200MOE_INTER 512
+#define B200MOE_Q4K_BLOCK_BYTES 144
+
+enum { B200MOE_OK = 0, B200MOE_EINVAL = 1, B200MOE_ECUDA = 2, B200MOE_ESIZE = 3 };
+enum { B200MOE_F32 = 0, B200MOE_BF16 = 1 };
+
+/* One MoE layer's device-resident weights. `gate_up_expert_stride` is the byte distance
+ * between consecutive experts inside `gate` and `up`: 589,824 for the two separate GGUF
+ * tensors ffn_gate_exps / ffn_up_exps, 1,179,648 for one fused HF-style [E, 2I, H] stack
+ * (then up = gate + 589,824). `down_expert_stride` is 589,824 for ffn_down_exps. */
+typedef struct b200moe_layer {
+    const void *gate;
+    const void *up;
+    int64_t gate_up_expert_stride;
+    const void *down;
+    int64_t down_expert_stride;
+    const void *sh_gate;
+    const void *sh_up;
+    const void *sh_down;
+    const uint16_t *router_w;
+    const uint16_t *sh_gate_w;
+    const float *logit_bias; /* [256] f32 added to R1's f32 dot before the bf16 cast, or NULL */
+} b200moe_layer;
+
+/* ABI version (B200MOE_ABI_VERSION) and the last error message on this thread. */
+int b200moe_abi_version(void);
+const char *b200moe_last_error(void);
+
+/* Q4_K -> f32 (out_dtype B200MOE_F32) or bf16 (B200MOE_BF16, RNE of the f32 value) for
+ * `nblocks` consecutive super-blocks, elements in stored order.
+ * Replaces tools/gguf_fast_dequant.py:87 dequant_np (Q4_K branch :109-125) and
+ * tools/gguf_reader.py:178 dequant -> _deq_q4_k :248-267; bit-exact against both. */
+int b200moe_q4k_dequant(const void *blocks, int64_t nblocks, void *out, int out_dtype,
+                        void *stream);
+
+/* Seeded synthetic Q4_K blocks [block0, block0+nblocks) of stream `stream_id` (the
+ * benchmark's weight generator; the same bytes as oracle/q4k.py synth_blocks). No
+ * counterpart in the reference, which reads a GGUF file instead. */
+int b200moe_synth_q4k(uint64_t seed, uint32_t stream_id, int64_t block0, int64_t nblocks,
+                      void *out, void *stream);
+
+/* Router R1..R5 for T tokens: x [T][2048] (f32 or bf16), W_g [256][2048] bf16, optional f32
+ * logit bias [256]. Outputs (each may be NULL): logits [T][256] bf16, ids [T][8] int32 in
+ * top-k rank order, w_f32 [T][8] renormalised weights, w_bf16 [T][8] their R5 bf16 cast.
+ * Replaces engine/m3_forward.py:443-446 and engine/block_forward.py:614 moe_router.
+ * Deterministic declared order (R1 32x64 chunked fmaf, softmax with the library's own exp,
+ * top-8 by (p desc, index asc)); bit-exact against oracle/c/oracle.c b2o_router. */
+int b200moe_router(const void *x, int x_dtype, int T, const uint16_t *router_w,
+                   const float *logit_bias, uint16_t *logits, int32_t *ids, float *w_f32,
+                   uint16_t *w_bf16, void *stream);
+
+/* Workspace bytes for b200moe_moe_decode with T tokens. */
+size_t b200moe_decode_workspace_size(int T);
+
+/* One MoE layer over T tokens (the gather-GEMV decode path): out [T][2048] f32 =
+ * routed (8 experts, weights R5-cast, summed in ascending expert id) + sigmoid(w_sg.x) *
+ * shared expert. ids_out [T][8] / w_out [T][8] bf16 may be NULL.
+ * Replaces engine/m3_forward.py:430 moe_block (and the MoE stages of
+ * engine/block_forward.py:670 moe_block). */
+int b200moe_moe_decode(const void *x, int x_dtype, int T, const b200moe_layer *layer,
+                       float *out, int32_t *ids_out, uint16_t *w_out, void *ws,
+                       size_t ws_bytes, void *stream);
+
+/* Workspace bytes for b200moe_stack_decode. */
+size_t b200moe_stack_workspace_size(int T, int n_layers);
+
+/* The config-4 MoE sub-stack: for l in 0..n_layers-1:
+ *   resid <- resid + moe_block_l(rmsnorm(resid; eps, weight 1))
+ * in place on resid [T][2048] f32 (engine/m3_forward.py:731-737 with the mixer sublayers
+ * taken out, rmsnorm_a :303-307). `layers` is a HOST array of n_layers descriptors.
+ * ids_out [n_layers][T][8] may be NULL. */
+int b200moe_stack_decode(float *resid, int T, const b200moe_layer *layers, int n_layers,
+                         float eps, int32_t *ids_out, void *ws, size_t ws_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200MOE_H */

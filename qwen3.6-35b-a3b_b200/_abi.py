@@ -1,0 +1,139 @@
+"""ctypes binding of ``libb200moe.so`` (declared in ``include/b200moe.h``).
+
+Thin and strict: each wrapper checks the C return code and raises :class:`B200MoeError`
+with the library's own message. Tensors are passed as raw device pointers; the caller's
+current torch CUDA stream is used unless a stream is given. There is no fallback: if the
+library is missing or no CUDA device is present the call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG_DIR, "libb200moe.so")
+
+OK, EINVAL, ECUDA, ESIZE = 0, 1, 2, 3
+F32, BF16 = 0, 1
+
+# Every exported symbol of include/b200moe.h (checked by tests/test_abi_exports.py).
+EXPORTS = ("b200moe_abi_version", "b200moe_last_error", "b200moe_q4k_dequant",
+           "b200moe_synth_q4k", "b200moe_router", "b200moe_decode_workspace_size",
+           "b200moe_moe_decode", "b200moe_stack_workspace_size", "b200moe_stack_decode")
+
+
+class B200MoeError(RuntimeError):
+    def __init__(self, fn: str, code: int, msg: str):
+        super().__init__("%s failed (code %d): %s" % (fn, code, msg))
+        self.code = code
+
+
+class Layer(ctypes.Structure):
+    """``struct b200moe_layer``."""
+    _fields_ = [("gate", ctypes.c_void_p), ("up", ctypes.c_void_p),
+                ("gate_up_expert_stride", ctypes.c_int64),
+                ("down", ctypes.c_void_p), ("down_expert_stride", ctypes.c_int64),
+                ("sh_gate", ctypes.c_void_p), ("sh_up", ctypes.c_void_p),
+                ("sh_down", ctypes.c_void_p), ("router_w", ctypes.c_void_p),
+                ("sh_gate_w", ctypes.c_void_p), ("logit_bias", ctypes.c_void_p)]
+
+
+_LIB = None
+
+
+def lib():
+    """Load the shared library (no build here: ``__graft_entry__.build()`` makes it)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise B200MoeError("load", -1, "%s is missing; build it with "
+                               "qwen3.6-35b-a3b_b200/build.py" % LIB_PATH)
+        L = ctypes.CDLL(LIB_PATH)
+        vp, i64, i32, u64, sz = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_uint64,
+                                 ctypes.c_size_t)
+        L.b200moe_abi_version.restype = i32
+        L.b200moe_abi_version.argtypes = []
+        L.b200moe_last_error.restype = ctypes.c_char_p
+        L.b200moe_last_error.argtypes = []
+        L.b200moe_q4k_dequant.restype = i32
+        L.b200moe_q4k_dequant.argtypes = [vp, i64, vp, i32, vp]
+        L.b200moe_synth_q4k.restype = i32
+        L.b200moe_synth_q4k.argtypes = [u64, ctypes.c_uint32, i64, i64, vp, vp]
+        L.b200moe_router.restype = i32
+        L.b200moe_router.argtypes = [vp, i32, i32, vp, vp, vp, vp, vp, vp, vp]
+        L.b200moe_decode_workspace_size.restype = sz
+        L.b200moe_decode_workspace_size.argtypes = [i32]
+        L.b200moe_moe_decode.restype = i32
+        L.b200moe_moe_decode.argtypes = [vp, i32, i32, ctypes.POINTER(Layer), vp, vp, vp, vp, sz, vp]
+        L.b200moe_stack_workspace_size.restype = sz
+        L.b200moe_stack_workspace_size.argtypes = [i32, i32]
+        L.b200moe_stack_decode.restype = i32
+        L.b200moe_stack_decode.argtypes = [vp, i32, ctypes.POINTER(Layer), i32, ctypes.c_float,
+                                           vp, vp, sz, vp]
+        _LIB = L
+    return _LIB
+
+
+def _check(fn: str, rc: int):
+    if rc != OK:
+        msg = lib().b200moe_last_error()
+        raise B200MoeError(fn, rc, msg.decode() if msg else "")
+
+
+def _stream(stream):
+    if stream is not None:
+        return ctypes.c_void_p(int(stream))
+    import torch
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def ptr(t):
+    """Device pointer of a torch tensor (None -> NULL); refuses host tensors."""
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise B200MoeError("ptr", EINVAL, "tensor on %s; the b200moe path needs CUDA tensors" % t.device)
+    if not t.is_contiguous():
+        raise B200MoeError("ptr", EINVAL, "tensor must be contiguous")
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def abi_version() -> int:
+    return int(lib().b200moe_abi_version())
+
+
+def q4k_dequant(blocks, out, out_dtype: int, stream=None):
+    nb = blocks.numel() // 144
+    _check("b200moe_q4k_dequant", lib().b200moe_q4k_dequant(ptr(blocks), nb, ptr(out), out_dtype,
+                                                             _stream(stream)))
+
+
+def synth_q4k(seed: int, stream_id: int, block0: int, nblocks: int, out, stream=None):
+    _check("b200moe_synth_q4k", lib().b200moe_synth_q4k(int(seed), int(stream_id), int(block0),
+                                                         int(nblocks), ptr(out), _stream(stream)))
+
+
+def router(x, x_dtype: int, T: int, wg, bias, logits, ids, w_f32, w_bf16, stream=None):
+    _check("b200moe_router", lib().b200moe_router(ptr(x), x_dtype, T, ptr(wg), ptr(bias), ptr(logits),
+                                                   ptr(ids), ptr(w_f32), ptr(w_bf16), _stream(stream)))
+
+
+def decode_workspace_size(T: int) -> int:
+    return int(lib().b200moe_decode_workspace_size(T))
+
+
+def moe_decode(x, x_dtype: int, T: int, layer: Layer, out, ids_out, w_out, ws, stream=None):
+    _check("b200moe_moe_decode",
+           lib().b200moe_moe_decode(ptr(x), x_dtype, T, ctypes.byref(layer), ptr(out), ptr(ids_out),
+                                    ptr(w_out), ptr(ws), ws.numel() * ws.element_size(), _stream(stream)))
+
+
+def stack_workspace_size(T: int, n_layers: int) -> int:
+    return int(lib().b200moe_stack_workspace_size(T, n_layers))
+
+
+def stack_decode(resid, T: int, layers, eps: float, ids_out, ws, stream=None):
+    arr = (Layer * len(layers))(*layers)
+    _check("b200moe_stack_decode",
+           lib().b200moe_stack_decode(ptr(resid), T, arr, len(layers), eps, ptr(ids_out), ptr(ws),
+                                      ws.numel() * ws.element_size(), _stream(stream)))

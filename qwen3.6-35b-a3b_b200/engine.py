@@ -1,0 +1,153 @@
+"""Device-resident Q4_K weights: the B200 replacement for the reference's weight source.
+
+The reference's ``engine/m3_forward.py:173 Engine`` reads GGUF byte ranges and dequantizes
+every hit expert on the host per call (``Engine.expert`` :268 ->
+``tools/gguf_fast_dequant.py:Artifact.expert`` :218). Here the Q4_K bytes stay in HBM in
+GGUF order (expert axis slowest) and the kernels dequantize in registers.
+
+:class:`DeviceEngine` keeps the ``Engine`` surface the MoE block uses (``cfg``,
+``read(role, layer)``, ``expert(role, layer, e, shape_hf)``) so a caller written against the
+reference can hand it to :func:`b200moe.moe.moe_block`; those two accessors return
+dequantized device tensors and exist for inspection, not for the hot path.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _abi
+from . import synth
+from .geometry import (E, EXPERT_DOWN_BYTES, EXPERT_GATE_BYTES, Geometry, H, I, KIND_BLOCKS,
+                       KIND_DOWN, KIND_GATE, KIND_SH_DOWN, KIND_SH_GATE, KIND_SH_UP, KIND_UP,
+                       Q4K_BYTES, stream_id)
+
+
+def _bf16_tensor(bits: np.ndarray, device) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(bits, dtype=np.uint16).view(np.int16)).view(
+        torch.bfloat16).to(device)
+
+
+class DeviceLayer:
+    """One MoE layer in HBM. Q4_K tensors are uint8 [n_blocks * 144]."""
+
+    def __init__(self, gate, up, down, sh_gate, sh_up, sh_down, router_w, sh_gate_w,
+                 logit_bias=None, gate_up_stride: int = EXPERT_GATE_BYTES):
+        self.gate, self.up, self.down = gate, up, down
+        self.sh_gate, self.sh_up, self.sh_down = sh_gate, sh_up, sh_down
+        self.router_w, self.sh_gate_w, self.logit_bias = router_w, sh_gate_w, logit_bias
+        self.gate_up_stride = int(gate_up_stride)
+        self._abi = None
+
+    # ------------------------------------------------------------------ construction
+    @classmethod
+    def synthetic(cls, seed: int, layer: int, device="cuda", bias: bool = False,
+                  fused_gate_up: bool = False) -> "DeviceLayer":
+        """Seeded synthetic layer (BASELINE config-0 field law), Q4_K generated on device.
+
+        ``fused_gate_up`` lays gate and up out as one HF-style [E, 2I, H] stack (gate rows
+        first per expert) instead of two GGUF tensors; the bytes of each row are the same.
+        """
+        dev = torch.device(device)
+
+        def gen(kind):
+            n = KIND_BLOCKS[kind]
+            t = torch.empty(n * Q4K_BYTES, dtype=torch.uint8, device=dev)
+            _abi.synth_q4k(seed, stream_id(layer, kind), 0, n, t)
+            return t
+
+        if fused_gate_up:
+            g, u = gen(KIND_GATE).view(E, -1), gen(KIND_UP).view(E, -1)
+            fused = torch.cat([g, u], dim=1).reshape(-1).contiguous()
+            gate, up, stride = fused, fused[EXPERT_GATE_BYTES:], 2 * EXPERT_GATE_BYTES
+        else:
+            gate, up, stride = gen(KIND_GATE), gen(KIND_UP), EXPERT_GATE_BYTES
+        lb = (torch.from_numpy(synth.zipf_bias(seed, layer)).to(dev) if bias else None)
+        return cls(gate, up, gen(KIND_DOWN), gen(KIND_SH_GATE), gen(KIND_SH_UP), gen(KIND_SH_DOWN),
+                   _bf16_tensor(synth.router_w(seed, layer), dev),
+                   _bf16_tensor(synth.shared_gate_w(seed, layer), dev), lb, stride)
+
+    @classmethod
+    def from_host(cls, blocks: dict, router_w_bits, sh_gate_w_bits, logit_bias=None,
+                  device="cuda") -> "DeviceLayer":
+        """From host arrays: ``blocks[kind]`` uint8 Q4_K bytes for gate/up/down/sh_gate/sh_up/sh_down
+        (GGUF order), bf16 bit patterns for the router and shared gate."""
+        dev = torch.device(device)
+        t = {k: torch.from_numpy(np.ascontiguousarray(v, dtype=np.uint8).reshape(-1)).to(dev)
+             for k, v in blocks.items()}
+        lb = None if logit_bias is None else torch.as_tensor(np.asarray(logit_bias, np.float32)).to(dev)
+        return cls(t["gate"], t["up"], t["down"], t["sh_gate"], t["sh_up"], t["sh_down"],
+                   _bf16_tensor(router_w_bits, dev), _bf16_tensor(sh_gate_w_bits, dev), lb)
+
+    # ------------------------------------------------------------------ ABI view
+    def abi(self) -> _abi.Layer:
+        if self._abi is None:
+            p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+            self._abi = _abi.Layer(p(self.gate), p(self.up), self.gate_up_stride, p(self.down),
+                                   EXPERT_DOWN_BYTES, p(self.sh_gate), p(self.sh_up), p(self.sh_down),
+                                   p(self.router_w), p(self.sh_gate_w), p(self.logit_bias))
+        return self._abi
+
+    @property
+    def device(self):
+        return self.down.device
+
+    def nbytes(self) -> int:
+        ts = [self.down, self.sh_gate, self.sh_up, self.sh_down, self.router_w, self.sh_gate_w]
+        n = sum(t.numel() * t.element_size() for t in ts)
+        if self.gate_up_stride == 2 * EXPERT_GATE_BYTES:
+            n += self.gate.numel()
+        else:
+            n += self.gate.numel() + self.up.numel()
+        return n
+
+    # ------------------------------------------------------------------ inspection
+    def expert_blocks(self, kind: str, e: int = 0) -> torch.Tensor:
+        """The Q4_K bytes (device uint8 view) of one expert matrix or of a shared matrix."""
+        if kind == "down":
+            return self.down[e * EXPERT_DOWN_BYTES:(e + 1) * EXPERT_DOWN_BYTES]
+        if kind in ("gate", "up"):
+            base = self.gate if kind == "gate" else self.up
+            return base[e * self.gate_up_stride: e * self.gate_up_stride + EXPERT_GATE_BYTES]
+        return {"sh_gate": self.sh_gate, "sh_up": self.sh_up, "sh_down": self.sh_down}[kind]
+
+    def dequant(self, kind: str, e: int = 0, dtype=torch.float32) -> torch.Tensor:
+        blocks = self.expert_blocks(kind, e)
+        shape = (H, I) if kind.endswith("down") else (I, H)
+        out = torch.empty(shape, dtype=dtype, device=blocks.device)
+        _abi.q4k_dequant(blocks, out, _abi.BF16 if dtype == torch.bfloat16 else _abi.F32)
+        return out
+
+
+class DeviceEngine:
+    """``Engine``-shaped holder of device layers (``engine/m3_forward.py:173``)."""
+
+    ROLE = {"ffn_gate_exps": "gate", "ffn_up_exps": "up", "ffn_down_exps": "down",
+            "ffn_gate_shexp": "sh_gate", "ffn_up_shexp": "sh_up", "ffn_down_shexp": "sh_down"}
+
+    def __init__(self, layers, geometry: Geometry | None = None):
+        self.layers = list(layers)
+        self.geometry = geometry or Geometry()
+        self.cfg = self.geometry.as_cfg()
+        self.fault = None
+        self.probe_ops = []
+        self.perturb = None
+
+    @classmethod
+    def synthetic(cls, seed: int, n_layers: int, device="cuda", bias: bool = False) -> "DeviceEngine":
+        return cls([DeviceLayer.synthetic(seed, l, device, bias) for l in range(n_layers)])
+
+    def read(self, role: str, layer: int):
+        """(values, None, handle) like ``Engine.read`` :235 -- dequantized on the device."""
+        L = self.layers[layer]
+        if role == "ffn_gate_inp":
+            return L.router_w.float(), None, dict(type_name="BF16")
+        if role == "ffn_gate_inp_shexp":
+            return L.sh_gate_w.float().reshape(1, H), None, dict(type_name="BF16")
+        return L.dequant(self.ROLE[role]), None, dict(type_name="Q4_K")
+
+    def expert(self, role: str, layer: int, idx: int, shape_hf):
+        """(values, None, rec) like ``Engine.expert`` :268 -- dequantized on the device."""
+        v = self.layers[layer].dequant(self.ROLE[role], idx)
+        if tuple(v.shape) != tuple(shape_hf):
+            raise ValueError("%s expert %d is %s, caller wants %s" % (role, idx, tuple(v.shape), tuple(shape_hf)))
+        return v, None, dict(type_name="Q4_K")

@@ -1,0 +1,135 @@
+"""The MoE block behind the reference's own Python call shapes.
+
+* :func:`moe_block` -- drop-in for ``engine/m3_forward.py:430 moe_block(g, E, layer,
+  probe_row=None) -> (out [B,T,2048] f32, {"used", "ids"})``.
+* :func:`moe_router` -- the router stage set of ``engine/block_forward.py:614``:
+  ``router_logits, topk_ids, topk_weights, topk_weights_f32``.
+* :func:`moe_stack` -- the config-4 MoE sub-stack (``engine/m3_forward.py:714-737`` with
+  the mixer sublayers removed): ``resid <- resid + moe_block(rmsnorm(resid))`` per layer.
+
+Errors follow the reference: shape and dtype problems raise ``Refused`` (a ValueError with
+a tag, as ``engine/m3_forward.py:165-170`` does) before any launch; a failing library call
+raises :class:`b200moe._abi.B200MoeError`. Everything runs on the caller's current CUDA
+stream with no host synchronisation; ``info["used"]`` is computed (one sync) only when read.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _abi
+from .engine import DeviceEngine, DeviceLayer
+from .geometry import E, H, N_LAYERS, RMS_EPS, TOPK
+
+
+class Refused(ValueError):
+    """A call the block refuses, tagged like the reference's ``Refused(tag, msg)``."""
+
+    def __init__(self, tag: str, msg: str):
+        super().__init__("[%s] %s" % (tag, msg))
+        self.tag = tag
+
+
+class _Info(dict):
+    """``{"used", "ids"}`` where ``used`` (distinct experts hit) is evaluated on first read."""
+
+    def __getitem__(self, k):
+        if k == "used" and not dict.__contains__(self, "used"):
+            dict.__setitem__(self, "used", int(torch.unique(dict.__getitem__(self, "ids")).numel()))
+        return dict.__getitem__(self, k)
+
+
+_WS = {}
+
+
+def workspace(T: int, device) -> torch.Tensor:
+    """A cached workspace of ``b200moe_decode_workspace_size(T)`` bytes on ``device``."""
+    need = _abi.decode_workspace_size(T)
+    key = (torch.device(device), torch.cuda.current_stream(device).cuda_stream)
+    ws = _WS.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=device)
+        _WS[key] = ws
+    return ws
+
+
+def _layer_of(E_, layer) -> DeviceLayer:
+    if isinstance(E_, DeviceLayer):
+        return E_
+    if isinstance(E_, DeviceEngine):
+        return E_.layers[layer]
+    raise Refused("engine-kind", "moe_block needs a b200moe DeviceEngine or DeviceLayer, got %s"
+                  % type(E_).__name__)
+
+
+def _tokens(g, device) -> tuple:
+    if g.shape[-1] != H:
+        raise Refused("shape", "hidden size %d != %d" % (g.shape[-1], H))
+    if g.dtype not in (torch.float32, torch.bfloat16):
+        raise Refused("dtype", "input dtype %s: f32 or bf16 only" % g.dtype)
+    x = g.reshape(-1, H)
+    if x.device != device:
+        x = x.to(device, non_blocking=True)
+    x = x.contiguous()
+    return x, (_abi.F32 if x.dtype == torch.float32 else _abi.BF16)
+
+
+def moe_block(g: torch.Tensor, E_, layer: int = 0, probe_row=None, out: torch.Tensor | None = None):
+    """``engine/m3_forward.py:430`` on the B200 path.
+
+    ``g`` [B, T, 2048] (or [T, 2048]) f32/bf16; returns ``(out, info)`` with ``out`` f32 in
+    ``g``'s leading shape, ``info = {"ids": [B,T,8] int32 (device), "used": int}``.
+    Routing is R1-R5 with the cast before the multiply; routed outputs are summed in
+    ascending expert id; the shared expert is gated by sigmoid(w_sg . x).
+    """
+    if probe_row is not None:
+        raise Refused("probe-row", "band-operand probes are a host-oracle feature; not on the device path")
+    L = _layer_of(E_, layer)
+    x, xd = _tokens(g, L.device)
+    T = x.shape[0]
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.float32, device=L.device)
+    ids = torch.empty((T, TOPK), dtype=torch.int32, device=L.device)
+    _abi.moe_decode(x, xd, T, L.abi(), out, ids, None, workspace(T, L.device))
+    lead = tuple(g.shape[:-1])
+    return out.reshape(*lead, H), _Info(ids=ids.reshape(*lead, TOPK))
+
+
+def moe_router(g_row: torch.Tensor, E_, layer: int = 0) -> dict:
+    """Router stages (``engine/block_forward.py:614-636``) for every row of ``g_row``."""
+    L = _layer_of(E_, layer)
+    x, xd = _tokens(g_row, L.device)
+    T = x.shape[0]
+    dev = L.device
+    logits = torch.empty((T, E), dtype=torch.bfloat16, device=dev)
+    ids = torch.empty((T, TOPK), dtype=torch.int32, device=dev)
+    wf = torch.empty((T, TOPK), dtype=torch.float32, device=dev)
+    wb = torch.empty((T, TOPK), dtype=torch.bfloat16, device=dev)
+    _abi.router(x, xd, T, L.router_w, L.logit_bias, logits, ids, wf, wb)
+    return dict(router_logits=logits, topk_ids=ids, topk_weights=wb, topk_weights_f32=wf)
+
+
+def moe_stack(resid: torch.Tensor, E_: DeviceEngine, n_layers: int | None = None,
+              eps: float = RMS_EPS, ids_out: torch.Tensor | None = None,
+              ws: torch.Tensor | None = None) -> torch.Tensor:
+    """In place: for each layer, ``resid += moe_block_l(rmsnorm(resid))``. ``resid`` [T, 2048] f32.
+
+    ``ws`` (optional) is a caller-owned workspace of ``stack_workspace_bytes(T)`` bytes; pass
+    one when capturing the call into a CUDA graph so nothing is allocated during capture."""
+    if resid.dtype != torch.float32 or resid.shape[-1] != H:
+        raise Refused("shape", "resid must be f32 [T, %d]" % H)
+    n = len(E_.layers) if n_layers is None else int(n_layers)
+    if n > len(E_.layers):
+        raise Refused("layers", "%d layers requested, engine holds %d" % (n, len(E_.layers)))
+    r = resid.reshape(-1, H)
+    T = r.shape[0]
+    dev = E_.layers[0].device
+    _abi.stack_decode(r, T, [L.abi() for L in E_.layers[:n]], eps, ids_out,
+                      ws if ws is not None else workspace(T, dev))
+    return resid
+
+
+def stack_workspace_bytes(T: int) -> int:
+    return _abi.stack_workspace_size(T, 1)
+
+
+__all__ = ["moe_block", "moe_router", "moe_stack", "Refused", "N_LAYERS"]
