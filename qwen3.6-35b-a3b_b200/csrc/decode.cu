@@ -528,8 +528,10 @@ int check_layer(const b200moe_layer *L, const char *who) {
 }
 
 // One layer: K1 -> K2 -> K3 on stream s. x given (resid == NULL) or rmsnorm(resid).
+// `first`: K1 is the first launch of this API call -- its stream predecessor may be any
+// operation (a memcpy node in a captured graph), so it is launched without the PDL attribute.
 int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const b200moe_layer *L, float *out,
-              int32_t *ids_out, uint16_t *w_out, const DecodeWS &w, cudaStream_t s) {
+              int32_t *ids_out, uint16_t *w_out, const DecodeWS &w, cudaStream_t s, bool first) {
   K1Params p1;
   p1.x = x;
   p1.x_dtype = x_dtype;
@@ -545,7 +547,7 @@ int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const 
   p1.logits = w.logits;
   p1.s = w.s;
   p1.sg = w.sg;
-  B2_CUDA(launch(k_router_shared, kK1Grid, 256, k1_smem(T), s, true, p1));
+  B2_CUDA(launch(k_router_shared, kK1Grid, 256, k1_smem(T), s, !first, p1));
   K2Params p2;
   p2.T = T;
   p2.gate = (const uint8_t *)L->gate;
@@ -615,7 +617,7 @@ int b200moe_moe_decode(const void *x, int x_dtype, int T, const b200moe_layer *l
   if (rc) return rc;
   rc = ensure_attrs();
   if (rc) return rc;
-  return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, carve(ws, T), (cudaStream_t)stream);
+  return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, carve(ws, T), (cudaStream_t)stream, true);
 }
 
 size_t b200moe_stack_workspace_size(int T, int n_layers) {
@@ -639,7 +641,7 @@ int b200moe_stack_decode(float *resid, int T, const b200moe_layer *layers, int n
   const DecodeWS w = carve(ws, T);
   for (int l = 0; l < n_layers; ++l) {
     rc = run_layer(nullptr, B200MOE_F32, resid, eps, T, &layers[l], nullptr,
-                   ids_out ? ids_out + (size_t)l * T * kK : nullptr, nullptr, w, (cudaStream_t)stream);
+                   ids_out ? ids_out + (size_t)l * T * kK : nullptr, nullptr, w, (cudaStream_t)stream, l == 0);
     if (rc) return rc;
   }
   return B200MOE_OK;
