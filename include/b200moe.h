@@ -71,6 +71,9 @@ int b200moe_q4k_dequant(const void *blocks, int64_t nblocks, void *out, int out_
 int b200moe_synth_q4k(uint64_t seed, uint32_t stream_id, int64_t block0, int64_t nblocks,
                       void *out, void *stream);
 
+/* Workspace bytes for b200moe_router with T tokens. */
+size_t b200moe_router_workspace_size(int T);
+
 /* Router R1..R5 for T tokens: x [T][2048] (f32 or bf16), W_g [256][2048] bf16, optional f32
  * logit bias [256]. Outputs (each may be NULL): logits [T][256] bf16, ids [T][8] int32 in
  * top-k rank order, w_f32 [T][8] renormalised weights, w_bf16 [T][8] their R5 bf16 cast.
@@ -79,7 +82,7 @@ int b200moe_synth_q4k(uint64_t seed, uint32_t stream_id, int64_t block0, int64_t
  * top-8 by (p desc, index asc)); bit-exact against oracle/c/oracle.c b2o_router. */
 int b200moe_router(const void *x, int x_dtype, int T, const uint16_t *router_w,
                    const float *logit_bias, uint16_t *logits, int32_t *ids, float *w_f32,
-                   uint16_t *w_bf16, void *stream);
+                   uint16_t *w_bf16, void *ws, size_t ws_bytes, void *stream);
 
 /* Workspace bytes for b200moe_moe_decode with T tokens. */
 size_t b200moe_decode_workspace_size(int T);
@@ -103,6 +106,27 @@ size_t b200moe_stack_workspace_size(int T, int n_layers);
  * ids_out [n_layers][T][8] may be NULL. */
 int b200moe_stack_decode(float *resid, int T, const b200moe_layer *layers, int n_layers,
                          float eps, int32_t *ids_out, void *ws, size_t ws_bytes, void *stream);
+
+/* Workspace bytes for b200moe_moe_prefill with T tokens. */
+size_t b200moe_prefill_workspace_size(int T);
+
+/* One MoE layer over many tokens (the prefill / large-batch path; replaces
+ * engine/m3_forward.py:430 moe_block for T tokens): router R1..R5 (same declared order as
+ * b200moe_router, so the ids are bit-identical), per-expert token lists in ascending
+ * (token, slot) order, Q4_K grouped GEMMs on tcgen05 tensor cores (weights dequantised to
+ * fp16 in shared memory, fp16 activations, f32 accumulation in TMEM), and the weighted
+ * combine in ascending expert id plus the gated shared expert.
+ * If `resid` is non-NULL: x = rmsnorm(resid; eps, weight 1) and resid += block output
+ * (x, x_dtype and out are ignored). Otherwise out [T][2048] f32 = block(x).
+ * ids_out [T][8] may be NULL. Asynchronous; a pipeline wait that timed out leaves a non-zero
+ * status word that b200moe_prefill_status reads back. */
+int b200moe_moe_prefill(const void *x, int x_dtype, float *resid, float eps, int T,
+                        const b200moe_layer *layer, float *out, int32_t *ids_out, void *ws,
+                        size_t ws_bytes, void *stream);
+
+/* Copy the prefill workspace's device status word to *status (synchronises `stream`):
+ * 0 = ok, 1 / 2 = a gate_up / down GEMM pipeline wait exceeded its ~1 s budget. */
+int b200moe_prefill_status(const void *ws, int T, int *status, void *stream);
 
 #ifdef __cplusplus
 }

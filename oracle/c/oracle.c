@@ -16,8 +16,10 @@
  *                       R2  m = max logit; e_l = b2o_expf(logit_l - m);
  *                           S: s_L = sequential sum of e_{8L..8L+7} (L = 0..31), then an xor
  *                           butterfly s_L += s_{L^o} for o = 16, 8, 4, 2, 1; p_l = e_l / S
- *                       R3  top-8 by (p descending, expert index ascending)
- *                           (the reference kernel's strict-> rule, moe_router_kernels.h:289-321)
+ *                       R3  top-8 by (bf16 logit descending, expert index ascending); the
+ *                           softmax is monotone in the logit, so this is the reference's top-k
+ *                           over probabilities with its unspecified tie order fixed to the
+ *                           reference kernel's strict-> rule (moe_router_kernels.h:289-321)
  *                       R4  s8 = sequential sum of the 8 p in rank order; w_k = p_k / s8
  *                       R5  w_bf16 = bf16_rne(w_k)  (cast BEFORE any multiply,
  *                           specification/11-moe-block.md:39-60)
@@ -177,9 +179,9 @@ void b2o_router(const float *x, int T, const uint16_t *wg, const float *bias, ui
             float bv = 0.0f;
             for (int e = 0; e < E; ++e) {
                 if (used[e]) continue;
-                if (best < 0 || pr[e] > bv) {
+                if (best < 0 || lg[e] > bv) { /* strict >: an exact tie keeps the lower index */
                     best = e;
-                    bv = pr[e];
+                    bv = lg[e];
                 }
             }
             used[best] = 1;

@@ -18,8 +18,10 @@ F32, BF16 = 0, 1
 
 # Every exported symbol of include/b200moe.h (checked by tests/test_abi_exports.py).
 EXPORTS = ("b200moe_abi_version", "b200moe_last_error", "b200moe_q4k_dequant",
-           "b200moe_synth_q4k", "b200moe_router", "b200moe_decode_workspace_size",
-           "b200moe_moe_decode", "b200moe_stack_workspace_size", "b200moe_stack_decode")
+           "b200moe_synth_q4k", "b200moe_router_workspace_size", "b200moe_router",
+           "b200moe_decode_workspace_size",
+           "b200moe_moe_decode", "b200moe_stack_workspace_size", "b200moe_stack_decode",
+           "b200moe_prefill_workspace_size", "b200moe_moe_prefill", "b200moe_prefill_status")
 
 
 class B200MoeError(RuntimeError):
@@ -59,8 +61,10 @@ def lib():
         L.b200moe_q4k_dequant.argtypes = [vp, i64, vp, i32, vp]
         L.b200moe_synth_q4k.restype = i32
         L.b200moe_synth_q4k.argtypes = [u64, ctypes.c_uint32, i64, i64, vp, vp]
+        L.b200moe_router_workspace_size.restype = sz
+        L.b200moe_router_workspace_size.argtypes = [i32]
         L.b200moe_router.restype = i32
-        L.b200moe_router.argtypes = [vp, i32, i32, vp, vp, vp, vp, vp, vp, vp]
+        L.b200moe_router.argtypes = [vp, i32, i32, vp, vp, vp, vp, vp, vp, vp, sz, vp]
         L.b200moe_decode_workspace_size.restype = sz
         L.b200moe_decode_workspace_size.argtypes = [i32]
         L.b200moe_moe_decode.restype = i32
@@ -70,6 +74,13 @@ def lib():
         L.b200moe_stack_decode.restype = i32
         L.b200moe_stack_decode.argtypes = [vp, i32, ctypes.POINTER(Layer), i32, ctypes.c_float,
                                            vp, vp, sz, vp]
+        L.b200moe_prefill_workspace_size.restype = sz
+        L.b200moe_prefill_workspace_size.argtypes = [i32]
+        L.b200moe_moe_prefill.restype = i32
+        L.b200moe_moe_prefill.argtypes = [vp, i32, vp, ctypes.c_float, i32, ctypes.POINTER(Layer), vp, vp, vp,
+                                          sz, vp]
+        L.b200moe_prefill_status.restype = i32
+        L.b200moe_prefill_status.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_int), vp]
         _LIB = L
     return _LIB
 
@@ -113,9 +124,17 @@ def synth_q4k(seed: int, stream_id: int, block0: int, nblocks: int, out, stream=
                                                          int(nblocks), ptr(out), _stream(stream)))
 
 
-def router(x, x_dtype: int, T: int, wg, bias, logits, ids, w_f32, w_bf16, stream=None):
+def router_workspace_size(T: int) -> int:
+    return int(lib().b200moe_router_workspace_size(T))
+
+
+def router(x, x_dtype: int, T: int, wg, bias, logits, ids, w_f32, w_bf16, ws=None, stream=None):
+    if ws is None:
+        import torch
+        ws = torch.empty(router_workspace_size(T), dtype=torch.uint8, device=x.device)
     _check("b200moe_router", lib().b200moe_router(ptr(x), x_dtype, T, ptr(wg), ptr(bias), ptr(logits),
-                                                   ptr(ids), ptr(w_f32), ptr(w_bf16), _stream(stream)))
+                                                   ptr(ids), ptr(w_f32), ptr(w_bf16), ptr(ws),
+                                                   ws.numel() * ws.element_size(), _stream(stream)))
 
 
 def decode_workspace_size(T: int) -> int:
@@ -137,3 +156,19 @@ def stack_decode(resid, T: int, layers, eps: float, ids_out, ws, stream=None):
     _check("b200moe_stack_decode",
            lib().b200moe_stack_decode(ptr(resid), T, arr, len(layers), eps, ptr(ids_out), ptr(ws),
                                       ws.numel() * ws.element_size(), _stream(stream)))
+
+
+def prefill_workspace_size(T: int) -> int:
+    return int(lib().b200moe_prefill_workspace_size(T))
+
+
+def moe_prefill(x, x_dtype: int, resid, eps: float, T: int, layer: Layer, out, ids_out, ws, stream=None):
+    _check("b200moe_moe_prefill",
+           lib().b200moe_moe_prefill(ptr(x), x_dtype, ptr(resid), eps, T, ctypes.byref(layer), ptr(out),
+                                     ptr(ids_out), ptr(ws), ws.numel() * ws.element_size(), _stream(stream)))
+
+
+def prefill_status(ws, T: int, stream=None) -> int:
+    st = ctypes.c_int(-1)
+    _check("b200moe_prefill_status", lib().b200moe_prefill_status(ptr(ws), T, ctypes.byref(st), _stream(stream)))
+    return int(st.value)

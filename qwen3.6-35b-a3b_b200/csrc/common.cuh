@@ -69,12 +69,20 @@ __device__ __forceinline__ float b2_expf(float x) {
 __device__ __forceinline__ float silu_f(float z) { return __fdiv_rn(z, __fadd_rn(1.0f, expf(-z))); }
 
 // ---------------------------------------------------------------- memory
-// Streaming 16-byte read-only load that does not allocate in L1 (weights are touched once).
+// L2 policy for streamed weights: evict first, so the ~640 MB of Q4_K a decoded token reads
+// does not push code, activations and the router rows out of the 126 MB L2.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// Streaming 16-byte read-only load: no L1 allocation, L2 evict-first (weights are touched once).
 __device__ __forceinline__ uint4 ldg_stream(const void *p) {
   uint4 r;
-  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
       : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-      : "l"(p));
+      : "l"(p), "l"(l2_evict_first()));
   return r;
 }
 
@@ -116,25 +124,21 @@ struct XChunk {
 __device__ __forceinline__ int chunk_pos(int kb, int c) { return kb * 256 + 64 * (c >> 1) + 16 * (c & 1); }
 
 // get_scale_min_k4 for the two sub-blocks of chunk c (2g and 2g+1), folded with d / dmin.
-// hdr.x = d | dmin<<16, hdr.y/z/w = scale bytes 0-3 / 4-7 / 8-11.
+// hdr.x = d | dmin<<16, hdr.y/z/w = scale bytes 0-3 / 4-7 / 8-11. Branch-free: for sub-block
+// j with b = j & 3, q[j] / q[j+4] (j < 4) and q[j-4] / q[j] / q[j+4] (j >= 4) are byte b of
+// hdr.y / hdr.z / hdr.w.
 __device__ __forceinline__ void q4k_scales(const uint4 &h, int c, float &s0, float &m0, float &s1,
                                            float &m1) {
   const float d = f16f(h.x), dmin = f16f(h.x >> 16);
-  const int j0 = (c >> 1) * 2;
-  uint32_t sc0, mm0, sc1, mm1;
-  if (j0 < 4) {
-    sc0 = (h.y >> (8 * j0)) & 63u;
-    mm0 = (h.z >> (8 * j0)) & 63u;
-    sc1 = (h.y >> (8 * j0 + 8)) & 63u;
-    mm1 = (h.z >> (8 * j0 + 8)) & 63u;
-  } else {
-    const int b0 = 8 * (j0 - 4), b1 = b0 + 8;
-    const uint32_t w0 = (h.w >> b0) & 0xFFu, w1 = (h.w >> b1) & 0xFFu;
-    sc0 = (w0 & 15u) | (((h.y >> (b0 + 6)) & 3u) << 4);
-    mm0 = (w0 >> 4) | (((h.z >> (b0 + 6)) & 3u) << 4);
-    sc1 = (w1 & 15u) | (((h.y >> (b1 + 6)) & 3u) << 4);
-    mm1 = (w1 >> 4) | (((h.z >> (b1 + 6)) & 3u) << 4);
-  }
+  const int g = c >> 1;
+  const bool lo = g < 2;
+  const int sh0 = 16 * (g & 1), sh1 = sh0 + 8;  // byte 2(g&1) and 2(g&1)+1
+  const uint32_t y0 = (h.y >> sh0) & 0xFFu, z0 = (h.z >> sh0) & 0xFFu, w0 = (h.w >> sh0) & 0xFFu;
+  const uint32_t y1 = (h.y >> sh1) & 0xFFu, z1 = (h.z >> sh1) & 0xFFu, w1 = (h.w >> sh1) & 0xFFu;
+  const uint32_t sc0 = lo ? (y0 & 63u) : ((w0 & 15u) | ((y0 & 0xC0u) >> 2));
+  const uint32_t mm0 = lo ? (z0 & 63u) : ((w0 >> 4) | ((z0 & 0xC0u) >> 2));
+  const uint32_t sc1 = lo ? (y1 & 63u) : ((w1 & 15u) | ((y1 & 0xC0u) >> 2));
+  const uint32_t mm1 = lo ? (z1 & 63u) : ((w1 >> 4) | ((z1 & 0xC0u) >> 2));
   s0 = d * (float)sc0;
   m0 = dmin * (float)mm0;
   s1 = d * (float)sc1;
@@ -142,13 +146,20 @@ __device__ __forceinline__ void q4k_scales(const uint4 &h, int c, float &s0, flo
 }
 
 // 4-bit value of byte b (0..3) of a nibble-masked word, as an exact float: 0x4B0000qq is
-// 2^23 + q, so subtracting 2^23 leaves q.
+// 2^23 + q, so subtracting 2^23 leaves q. (Used where the result must be bit-exact.)
 __device__ __forceinline__ float nib_f(uint32_t masked, int b) {
   return __uint_as_float(__byte_perm(masked, 0x4B000000u, 0x7540u | (uint32_t)b)) - 8388608.0f;
 }
 
-// sum over the chunk's 32 weights of w_i * x_i, with w = (d*sc)*q - dmin*m factored as
-// (d*sc) * sum(q x) - (dmin*m) * sum(x).
+// 1 + q/16 for byte b of a prepared word whose bytes are 0x80 | (q << 3): one byte permute
+// builds the float 0x3F8?0000 directly (mantissa bits 19..22 = q).
+__device__ __forceinline__ float nib_1p(uint32_t prepared, int b) {
+  return __uint_as_float(__byte_perm(prepared, 0x3F000000u, 0x7054u | ((uint32_t)b << 8)));
+}
+
+// sum over the chunk's 32 weights of w_i * x_i, with w = (d*sc)*q - dmin*m. The quants enter
+// as f = 1 + q/16 (one byte permute each): sum(q x) = 16 (sum(f x) - sum(x)), so a run's
+// contribution is 16*S*sum(f x) - (16*S + M) * sum(x).
 __device__ __forceinline__ float q4k_chunk_dot(const uint4 &h, const uint4 &q, int c, const XChunk &x) {
   float s0, m0, s1, m1;
   q4k_scales(h, c, s0, m0, s1, m1);
@@ -156,14 +167,16 @@ __device__ __forceinline__ float q4k_chunk_dot(const uint4 &h, const uint4 &q, i
   const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint32_t lo = w[i] & 0x0F0F0F0Fu, hi = (w[i] >> 4) & 0x0F0F0F0Fu;
+    const uint32_t lo = ((w[i] << 3) & 0x78787878u) | 0x80808080u;
+    const uint32_t hi = ((w[i] >> 1) & 0x78787878u) | 0x80808080u;
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      al = fmaf(nib_f(lo, b), x.lo[4 * i + b], al);
-      ah = fmaf(nib_f(hi, b), x.hi[4 * i + b], ah);
+      al = fmaf(nib_1p(lo, b), x.lo[4 * i + b], al);
+      ah = fmaf(nib_1p(hi, b), x.hi[4 * i + b], ah);
     }
   }
-  return (s0 * al - m0 * x.slo) + (s1 * ah - m1 * x.shi);
+  const float S0 = 16.0f * s0, S1 = 16.0f * s1;
+  return fmaf(S0, al, -(S0 + m0) * x.slo) + fmaf(S1, ah, -(S1 + m1) * x.shi);
 }
 
 // Load the x values of chunk (kb, c) from a dense f32 row.

@@ -1,0 +1,669 @@
+// prefill.cu -- the prefill / large-batch MoE path: token sort + Q4_K grouped GEMMs on tcgen05.
+//
+//   k_prep        warp per token: x (given, or RMSNorm of the residual) -> xn f32, x16 fp16,
+//                 and the shared-expert gate sg = sigmoid(w_sg . x)
+//   k_router_gemm R1 logits for all tokens on CUDA cores, in the declared order (32 chunks of
+//                 64 sequential fmaf, chunk sums added left to right) -> bf16
+//   k_route_tok   warp per token: R2..R5 -> ids, bf16 weights, combine order; per-expert counts
+//   k_plan        one CTA: packed row offsets per expert (the shared expert is expert 256 with
+//                 every token), 256-token chunks, and the GEMM tile tables
+//   k_fill        CTA per expert: that expert's (token, slot) assignments in ascending order
+//   k_gemm<1>     gate_up: D[128 gate rows | 128 up rows][tokens] = W . x^T, s = silu(g)*u -> fp16
+//   k_gemm<2>     down:    D[128 h rows][tokens] = W_d . s^T -> y[assignment][h] = o * w (routed)
+//                 or ysh[token][h] = o (shared)
+//   k_combine     out[t] = sum over the 8 slots in ascending expert id of y + sg * ysh
+//
+// The grouped GEMMs put the dequantised weight rows in the M = 128 slot of the UMMA and the
+// expert's tokens (<= 256, padded to a multiple of 16) in N, so a ragged expert wastes at most
+// 15 token columns. Weights are Q4_K in HBM; producer warps dequantise each 128 x 64 K-slab to
+// fp16 in shared memory (half2 math: exact integer quants, fp16 sub-block scale and min), token
+// rows arrive by cp.async; one thread issues tcgen05.mma into TMEM; four warps drain TMEM.
+#include "common.cuh"
+#include "route.cuh"
+#include "tc.cuh"
+
+using namespace b2;
+
+namespace {
+
+constexpr int kNE = kE + 1;     // 256 routed experts + the shared expert
+constexpr int kChunk = 256;     // tokens per GEMM tile
+
+struct PrefillWS {
+  float *xn;
+  __half *x16;
+  uint16_t *logits;
+  float *sg;
+  int32_t *ids;
+  uint16_t *wb;
+  int32_t *order;
+  int32_t *counts;   // [257]
+  int32_t *offsets;  // [258]
+  int32_t *plist;    // [9T]
+  int4 *tiles1;
+  int4 *tiles2;
+  int32_t *ntiles;   // [2]
+  __half *s16;       // [9T][512]
+  float *y;          // [8T][2048]
+  float *ysh;        // [T][2048]
+  int32_t *err;      // [1]
+};
+
+size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+size_t max_chunks(int T) { return (size_t)(9 * (size_t)T) / kChunk + kNE + 1; }
+
+size_t prefill_ws_bytes(int T) {
+  const size_t t = (size_t)T, mc = max_chunks(T);
+  return al256(t * kH * 4) + al256(t * kH * 2) + al256(t * kE * 2) + al256(t * 4) + al256(t * kK * 4) +
+         al256(t * kK * 2) + al256(t * kK * 4) + al256(kNE * 4) + al256((kNE + 1) * 4) + al256(9 * t * 4) +
+         al256(mc * 4 * 16) + al256(mc * 16 * 16) + al256(2 * 4) + al256(9 * t * kI * 2) + al256(8 * t * kH * 4) +
+         al256(t * kH * 4) + al256(4);
+}
+
+PrefillWS carve_prefill(void *ws, int T) {
+  const size_t t = (size_t)T, mc = max_chunks(T);
+  char *p = (char *)ws;
+  PrefillWS w;
+  auto take = [&](size_t n) { char *r = p; p += al256(n); return r; };
+  w.xn = (float *)take(t * kH * 4);
+  w.x16 = (__half *)take(t * kH * 2);
+  w.logits = (uint16_t *)take(t * kE * 2);
+  w.sg = (float *)take(t * 4);
+  w.ids = (int32_t *)take(t * kK * 4);
+  w.wb = (uint16_t *)take(t * kK * 2);
+  w.order = (int32_t *)take(t * kK * 4);
+  w.counts = (int32_t *)take(kNE * 4);
+  w.offsets = (int32_t *)take((kNE + 1) * 4);
+  w.plist = (int32_t *)take(9 * t * 4);
+  w.tiles1 = (int4 *)take(mc * 4 * 16);
+  w.tiles2 = (int4 *)take(mc * 16 * 16);
+  w.ntiles = (int32_t *)take(2 * 4);
+  w.s16 = (__half *)take(9 * t * kI * 2);
+  w.y = (float *)take(8 * t * kH * 4);
+  w.ysh = (float *)take(t * kH * 4);
+  w.err = (int32_t *)take(4);
+  return w;
+}
+
+// ------------------------------------------------------------------------- k_prep
+__global__ void __launch_bounds__(256) k_prep(const void *x, int x_dtype, const float *resid, float eps, int T,
+                                              const uint16_t *wsg, float *xn, __half *x16, float *sg) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  float v[64];
+  if (resid) {
+    const float *r = resid + (size_t)t * kH + 64 * lane;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float4 a = __ldcg(reinterpret_cast<const float4 *>(r + 4 * i));
+      v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) ss = __fmaf_rn(v[i], v[i], ss);
+    float tot = __shfl_sync(0xFFFFFFFFu, ss, 0);
+#pragma unroll
+    for (int c = 1; c < 32; ++c) tot = __fadd_rn(tot, __shfl_sync(0xFFFFFFFFu, ss, c));
+    const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, 2048.0f), eps)));
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = __fmul_rn(v[i], rs);
+  } else if (x_dtype == B200MOE_BF16) {
+    const uint16_t *xb = reinterpret_cast<const uint16_t *>(x) + (size_t)t * kH + 64 * lane;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4 *>(xb + 8 * i));
+      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        v[8 * i + 2 * q] = bf16f(uw[q]);
+        v[8 * i + 2 * q + 1] = bf16f(uw[q] >> 16);
+      }
+    }
+  } else {
+    const float *xf = reinterpret_cast<const float *>(x) + (size_t)t * kH + 64 * lane;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float4 a = __ldg(reinterpret_cast<const float4 *>(xf + 4 * i));
+      v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+    }
+  }
+  float *dst = xn + (size_t)t * kH + 64 * lane;
+  __half *d16 = x16 + (size_t)t * kH + 64 * lane;
+  float z = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    *reinterpret_cast<float4 *>(dst + 4 * i) = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    const __half2 a = __floats2half2_rn(v[4 * i], v[4 * i + 1]);
+    const __half2 b = __floats2half2_rn(v[4 * i + 2], v[4 * i + 3]);
+    uint2 pk;
+    pk.x = *reinterpret_cast<const uint32_t *>(&a);
+    pk.y = *reinterpret_cast<const uint32_t *>(&b);
+    *reinterpret_cast<uint2 *>(d16 + 4 * i) = pk;
+  }
+  const uint16_t *w = wsg + 64 * lane;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4 *>(w + 8 * i));
+    const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      z = fmaf(v[8 * i + 2 * q], bf16f(uw[q]), z);
+      z = fmaf(v[8 * i + 2 * q + 1], bf16f(uw[q] >> 16), z);
+    }
+  }
+  z = warp_sum(z);
+  if (lane == 0) sg[t] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+}
+
+// ------------------------------------------------------------------------- k_router_gemm
+// CTA: 64 tokens x 64 experts, thread (ty, tx) owns tokens ty + 16i and experts tx + 16j.
+__global__ void __launch_bounds__(256) k_router_gemm(const float *__restrict__ xn, int T,
+                                                     const uint16_t *__restrict__ wg, const float *bias,
+                                                     uint16_t *logits) {
+  __shared__ __align__(16) float xs[64][68];
+  __shared__ __align__(16) float wsm[64][68];
+  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
+  float tot[4][4];
+  for (int c = 0; c < 32; ++c) {
+    // x chunk: 64 rows x 64 floats; w chunk: 64 rows x 64 bf16
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int idx = tid + 256 * q;  // 0..1023 float4 slots
+      const int row = idx >> 4, col = (idx & 15) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (t0 + row < T) v = __ldg(reinterpret_cast<const float4 *>(xn + (size_t)(t0 + row) * kH + 64 * c + col));
+      *reinterpret_cast<float4 *>(&xs[row][col]) = v;
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int idx = tid + 256 * q;  // 0..511 8-wide slots
+      const int row = idx >> 3, col = (idx & 7) * 8;
+      const uint4 u = __ldg(reinterpret_cast<const uint4 *>(wg + (size_t)(e0 + row) * kH + 64 * c + col));
+      *reinterpret_cast<float4 *>(&wsm[row][col]) = make_float4(bf16f(u.x), bf16f(u.x >> 16), bf16f(u.y), bf16f(u.y >> 16));
+      *reinterpret_cast<float4 *>(&wsm[row][col + 4]) = make_float4(bf16f(u.z), bf16f(u.z >> 16), bf16f(u.w), bf16f(u.w >> 16));
+    }
+    __syncthreads();
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+#pragma unroll 2
+    for (int k = 0; k < 64; k += 4) {
+      float4 xa[4], wa[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) xa[i] = *reinterpret_cast<const float4 *>(&xs[ty + 16 * i][k]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) wa[j] = *reinterpret_cast<const float4 *>(&wsm[tx + 16 * j][k]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[i][j] = __fmaf_rn(xa[i].x, wa[j].x, acc[i][j]);
+          acc[i][j] = __fmaf_rn(xa[i].y, wa[j].y, acc[i][j]);
+          acc[i][j] = __fmaf_rn(xa[i].z, wa[j].z, acc[i][j]);
+          acc[i][j] = __fmaf_rn(xa[i].w, wa[j].w, acc[i][j]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) tot[i][j] = (c == 0) ? acc[i][j] : __fadd_rn(tot[i][j], acc[i][j]);
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = t0 + ty + 16 * i;
+    if (t >= T) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = e0 + tx + 16 * j;
+      float v = tot[i][j];
+      if (bias) v = __fadd_rn(v, bias[e]);
+      logits[(size_t)t * kE + e] = f2bf(v);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------- k_route_tok
+__global__ void __launch_bounds__(256) k_route_tok(const uint16_t *logits, int T, int32_t *ids, uint16_t *wb,
+                                                   int32_t *order, int32_t *counts, int32_t *ids_out) {
+  __shared__ Route rr[8];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + w;
+  if (t >= T) return;
+  route_warp(logits + (size_t)t * kE, &rr[w]);
+  if (lane < kK) {
+    ids[(size_t)t * kK + lane] = rr[w].ids[lane];
+    wb[(size_t)t * kK + lane] = rr[w].wb[lane];
+    order[(size_t)t * kK + lane] = rr[w].order[lane];
+    if (ids_out) ids_out[(size_t)t * kK + lane] = rr[w].ids[lane];
+    atomicAdd(counts + rr[w].ids[lane], 1);
+  }
+}
+
+// ------------------------------------------------------------------------- k_plan
+// One CTA of 512 threads (thread e < 257 owns expert e; e = 256 is the shared expert).
+// Row offsets follow expert order 0..256; the chunk (tile) order puts the shared expert's
+// full-width chunks first, then experts 0..255, so the largest tiles are scheduled first.
+__global__ void __launch_bounds__(512) k_plan(int T, const int32_t *counts_in, int32_t *offsets, int4 *tiles1,
+                                              int4 *tiles2, int32_t *ntiles) {
+  __shared__ int sc[512], sn[512];
+  const int e = threadIdx.x;
+  const int cnt = e < kE ? counts_in[e] : (e == kE ? T : 0);
+  const int nch = (cnt + kChunk - 1) / kChunk;
+  const int pos = e == kE ? 0 : (e < kE ? e + 1 : e);  // a permutation of 0..511
+  sc[e] = cnt;
+  sn[pos] = nch;
+  __syncthreads();
+  for (int o = 1; o < 512; o <<= 1) {  // inclusive Hillis-Steele scans
+    const int a = e >= o ? sc[e - o] : 0, b = e >= o ? sn[e - o] : 0;
+    __syncthreads();
+    sc[e] += a;
+    sn[e] += b;
+    __syncthreads();
+  }
+  if (e < kNE) offsets[e] = sc[e] - cnt;
+  if (e == kNE - 1) offsets[kNE] = sc[e];
+  if (e <= kE) {
+    const int cbase = sn[pos] - nch;
+    const int r0 = sc[e] - cnt;
+    for (int c = 0; c < nch; ++c) {
+      const int n = min(kChunk, cnt - kChunk * c);
+      const int ci = cbase + c;
+      for (int jt = 0; jt < 4; ++jt) tiles1[4 * ci + jt] = make_int4(e, r0 + kChunk * c, n, jt);
+      for (int ht = 0; ht < 16; ++ht) tiles2[16 * ci + ht] = make_int4(e, r0 + kChunk * c, n, ht);
+    }
+  }
+  if (e == 0) {
+    ntiles[0] = 4 * sn[511];
+    ntiles[1] = 16 * sn[511];
+  }
+}
+
+// ------------------------------------------------------------------------- k_fill
+__global__ void __launch_bounds__(1024) k_fill(int T, const int32_t *ids, const int32_t *offsets, int32_t *plist) {
+  __shared__ int wcount[32];
+  __shared__ int running;
+  const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  if (e == kE) {
+    for (int t = tid; t < T; t += 1024) plist[offsets[kE] + t] = t;
+    return;
+  }
+  if (tid == 0) running = 0;
+  __syncthreads();
+  const int n = T * kK;
+  int32_t *dst = plist + offsets[e];
+  for (int base = 0; base < n; base += 1024) {
+    const int a = base + tid;
+    const bool f = a < n && __ldg(ids + a) == e;
+    const unsigned bal = __ballot_sync(0xFFFFFFFFu, f);
+    if (lane == 0) wcount[w] = __popc(bal);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int i = 0; i < 32; ++i) {
+      const int c = wcount[i];
+      if (i < w) before += c;
+      total += c;
+    }
+    if (f) dst[running + before + __popc(bal & ((1u << lane) - 1u))] = a;
+    __syncthreads();
+    if (tid == 0) running += total;
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------------- grouped GEMM
+template <int kMode>
+struct GemmCfg {
+  static constexpr int kA = kMode == 1 ? 2 : 1;           // A tiles per stage
+  static constexpr int kKS = kMode == 1 ? kH / 64 : kI / 64;  // K stages of 64
+  static constexpr int kStages = kMode == 1 ? 3 : 4;
+  static constexpr int kATile = 128 * 128;                  // 128 rows x 128 B
+  static constexpr int kBTile = kChunk * 128;               // 256 rows x 128 B
+  static constexpr int kStage = kA * kATile + kBTile;
+  static constexpr uint32_t kTmemCols = kMode == 1 ? 512 : 256;
+  static constexpr size_t kSmem = (size_t)kStages * kStage + 1024 + 256;
+};
+
+struct GemmParams {
+  const uint8_t *wa0;  // MODE1 gate / MODE2 down (routed)
+  const uint8_t *wa1;  // MODE1 up (routed)
+  int64_t stride;      // expert stride of wa0/wa1
+  const uint8_t *sh0;  // shared gate / shared down
+  const uint8_t *sh1;  // shared up
+  const int4 *tiles;
+  const int32_t *ntiles;
+  const int32_t *plist;
+  const __half *x16;
+  __half *s16;
+  const uint16_t *wb;
+  float *y;
+  float *ysh;
+  int32_t *err;
+};
+
+// Dequantise 64 consecutive K of one Q4_K row (block kb, sub-blocks 2g / 2g+1) into one
+// 128-row x 64-K fp16 tile, row `row`: 8 chunks of 8 halves (low nibbles -> chunks 0..3,
+// high nibbles -> chunks 4..7).
+__device__ __forceinline__ void dequant_slab(const uint8_t *blk, int g, uint8_t *tile, int row) {
+  const uint4 h = __ldg(reinterpret_cast<const uint4 *>(blk));
+  const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + 32 * g));
+  const uint4 q1 = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + 32 * g));
+  float s0, m0, s1, m1;
+  q4k_scales(h, 2 * g, s0, m0, s1, m1);
+  const __half2 S0 = __float2half2_rn(s0), M0 = __float2half2_rn(-m0);
+  const __half2 S1 = __float2half2_rn(s1), M1 = __float2half2_rn(-m1);
+  const __half2 k1024 = __float2half2_rn(1024.0f);
+  const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  uint8_t *rbase = tile + (row >> 3) * 1024 + (row & 7) * 16;
+#pragma unroll
+  for (int kc = 0; kc < 4; ++kc) {
+    uint32_t lo[4], hi[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t w = qw[2 * kc + (p >> 1)];
+      const uint32_t pr = __byte_perm(w, 0u, (p & 1) ? 0x4342u : 0x4140u);  // [b, 0, b', 0]
+      const uint32_t l = (pr & 0x000F000Fu) | 0x64006400u;
+      const uint32_t u = ((pr >> 4) & 0x000F000Fu) | 0x64006400u;
+      __half2 ql = __hsub2(*reinterpret_cast<const __half2 *>(&l), k1024);
+      __half2 qh = __hsub2(*reinterpret_cast<const __half2 *>(&u), k1024);
+      ql = __hfma2(ql, S0, M0);
+      qh = __hfma2(qh, S1, M1);
+      lo[p] = *reinterpret_cast<uint32_t *>(&ql);
+      hi[p] = *reinterpret_cast<uint32_t *>(&qh);
+    }
+    *reinterpret_cast<uint4 *>(rbase + kc * 128) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4 *>(rbase + (kc + 4) * 128) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  }
+}
+
+// Persistent, warp-specialised: warps 0-3 epilogue (TMEM lanes 32w..), warps 4-7 producers,
+// warp 8 TMEM allocation + MMA issue (lane 0).
+template <int kMode>
+__global__ void __launch_bounds__(288, 1) k_gemm(GemmParams P) {
+  using C = GemmCfg<kMode>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t *full = (uint64_t *)(smem + C::kStages * C::kStage);
+  uint64_t *empty = full + C::kStages;
+  uint64_t *acc_full = empty + C::kStages;
+  uint64_t *acc_empty = acc_full + 1;
+  uint64_t *drain = acc_empty + 1;
+  uint32_t *tmem_slot = (uint32_t *)(drain + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(full + s, 128);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 128);
+    mbar_init(drain, 1);
+    mbar_fence_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int ntiles = __ldg(P.ntiles + (kMode - 1));
+  bool ok = true;
+
+  if (warp >= 4 && warp < 8) {  // ------------------------------ producers
+    const int pt = threadIdx.x - 128;
+    uint32_t it = 0;
+    for (int ti = blockIdx.x; ti < ntiles && ok; ti += gridDim.x) {
+      const int4 tl = __ldg(P.tiles + ti);
+      const int e = tl.x, r0 = tl.y, n = tl.z, wt = tl.w;
+      const int npad = (n + 15) & ~15;
+      const uint8_t *arow0, *arow1 = nullptr;
+      if (kMode == 1) {
+        const size_t ro = (size_t)(wt * 128 + pt) * kRowUp;
+        arow0 = (e < kE ? P.wa0 + (size_t)e * P.stride : P.sh0) + ro;
+        arow1 = (e < kE ? P.wa1 + (size_t)e * P.stride : P.sh1) + ro;
+      } else {
+        arow0 = (e < kE ? P.wa0 + (size_t)e * P.stride : P.sh0) + (size_t)(wt * 128 + pt) * kRowDown;
+      }
+      for (int ks = 0; ks < C::kKS; ++ks, ++it) {
+        const int s = it % C::kStages;
+        const uint32_t round = it / C::kStages;
+        if (!mbar_wait(empty + s, (round & 1) ^ 1)) { ok = false; break; }
+        uint8_t *st = smem + s * C::kStage;
+        uint8_t *btile = st + C::kA * C::kATile;
+        // B: token rows (zero-filled past n)
+        const int kc0 = pt >> 5;
+        for (int r = pt & 31; r < npad; r += 32) {
+          const __half *src;
+          if (kMode == 1) {
+            const int pl = r < n ? __ldg(P.plist + r0 + r) : 0;
+            const int tok = e < kE ? (pl >> 3) : pl;
+            src = P.x16 + (size_t)tok * kH + ks * 64;
+          } else {
+            src = P.s16 + (size_t)(r0 + (r < n ? r : 0)) * kI + ks * 64;
+          }
+          const uint32_t nb = r < n ? 16u : 0u;
+          uint8_t *d = btile + (r >> 3) * 1024 + (r & 7) * 16;
+          cp_async16(d + kc0 * 128, src + kc0 * 8, nb);
+          cp_async16(d + (kc0 + 4) * 128, src + (kc0 + 4) * 8, nb);
+        }
+        // A: dequantised weight rows
+        const int kb = ks >> 2, g = ks & 3;
+        dequant_slab(arow0 + kb * kQB, g, st, pt);
+        if (kMode == 1) dequant_slab(arow1 + kb * kQB, g, st + C::kATile, pt);
+        cp_async_wait_all();
+        fence_proxy_async_smem();
+        mbar_arrive(full + s);
+      }
+    }
+  } else if (warp == 8) {  // --------------------------------------- MMA issue
+    if (lane == 0) {
+      uint32_t it = 0, tcount = 0;
+      for (int ti = blockIdx.x; ti < ntiles && ok; ti += gridDim.x, ++tcount) {
+        const int4 tl = __ldg(P.tiles + ti);
+        const int npad = (tl.z + 15) & ~15;
+        const uint32_t idesc = umma_idesc_f16((uint32_t)npad);
+        if (tcount > 0 && !mbar_wait(acc_empty, (tcount - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        for (int ks = 0; ks < C::kKS; ++ks, ++it) {
+          const int s = it % C::kStages;
+          const uint32_t round = it / C::kStages;
+          if (!mbar_wait(full + s, round & 1)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + s * C::kStage);
+          const uint32_t bt = st + C::kA * C::kATile;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t acc = (ks | kk) != 0;
+            const uint64_t bd = umma_desc(bt + 256 * kk);
+            umma_f16(tmem, umma_desc(st + 256 * kk), bd, idesc, acc);
+            if (kMode == 1) umma_f16(tmem + 256, umma_desc(st + C::kATile + 256 * kk), bd, idesc, acc);
+          }
+          umma_commit(empty + s);
+        }
+        if (!ok) break;
+        umma_commit(acc_full);
+      }
+      // every MMA this thread issued has completed before TMEM can be released
+      umma_commit(drain);
+      if (!mbar_wait(drain, 0)) ok = false;
+    }
+    __syncwarp();
+  } else {  // ---------------------------------------------------------- epilogue (warps 0-3)
+    uint32_t tcount = 0;
+    const int row = 32 * warp + lane;  // TMEM lane = weight row within the tile
+    for (int ti = blockIdx.x; ti < ntiles && ok; ti += gridDim.x, ++tcount) {
+      const int4 tl = __ldg(P.tiles + ti);
+      const int e = tl.x, r0 = tl.y, n = tl.z, wt = tl.w;
+      const int npad = (n + 15) & ~15;
+      if (!mbar_wait(acc_full, tcount & 1)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t lane_addr = tmem + ((uint32_t)(32 * warp) << 16);
+      for (int c0 = 0; c0 < npad; c0 += 16) {
+        float a[16];
+        tmem_ld16(lane_addr + c0, a);
+        if (kMode == 1) {
+          float u[16];
+          tmem_ld16(lane_addr + 256 + c0, u);
+          tmem_wait_ld();
+          const int j = wt * 128 + row;
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (c0 + i < n)  // stored as s / 16 (exact): headroom under fp16's 65504 for RMS-1 inputs
+              P.s16[(size_t)(r0 + c0 + i) * kI + j] = __float2half_rn(__fmul_rn(__fmul_rn(silu_f(a[i]), u[i]), 0.0625f));
+        } else {
+          tmem_wait_ld();
+          const int h = wt * 128 + row;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (c0 + i >= n) continue;
+            const int pl = __ldg(P.plist + r0 + c0 + i);
+            const float o = __fmul_rn(a[i], 16.0f);  // undo the s / 16 storage scale (exact)
+            if (e < kE) P.y[(size_t)pl * kH + h] = __fmul_rn(o, bf16f(__ldg(P.wb + pl)));
+            else P.ysh[(size_t)pl * kH + h] = o;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+    }
+  }
+  if (!ok) atomicExch(P.err, kMode);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 8) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+// ------------------------------------------------------------------------- k_combine
+__global__ void __launch_bounds__(256) k_combine(int T, const float *y, const float *ysh, const float *sg,
+                                                 const int32_t *order, float *out, int accumulate) {
+  const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;  // one float4 of one token
+  if (idx >= (int64_t)T * (kH / 4)) return;
+  const int t = (int)(idx / (kH / 4)), h = (int)(idx % (kH / 4)) * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < kK; ++i) {
+    const int slot = __ldg(order + (size_t)t * kK + i);
+    const float4 v = __ldcs(reinterpret_cast<const float4 *>(y + ((size_t)t * kK + slot) * kH + h));
+    acc.x = __fadd_rn(acc.x, v.x);
+    acc.y = __fadd_rn(acc.y, v.y);
+    acc.z = __fadd_rn(acc.z, v.z);
+    acc.w = __fadd_rn(acc.w, v.w);
+  }
+  const float g = __ldg(sg + t);
+  const float4 sh = __ldcs(reinterpret_cast<const float4 *>(ysh + (size_t)t * kH + h));
+  float4 r = make_float4(__fadd_rn(acc.x, __fmul_rn(g, sh.x)), __fadd_rn(acc.y, __fmul_rn(g, sh.y)),
+                         __fadd_rn(acc.z, __fmul_rn(g, sh.z)), __fadd_rn(acc.w, __fmul_rn(g, sh.w)));
+  float4 *dst = reinterpret_cast<float4 *>(out + (size_t)t * kH + h);
+  if (accumulate) {
+    const float4 o = *dst;
+    r = make_float4(__fadd_rn(o.x, r.x), __fadd_rn(o.y, r.y), __fadd_rn(o.z, r.z), __fadd_rn(o.w, r.w));
+  }
+  *dst = r;
+}
+
+bool a16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+int g_num_sms = 0;
+
+int ensure_gemm_attrs() {
+  static int done = 0;
+  if (done) return B200MOE_OK;
+  B2_CUDA(cudaFuncSetAttribute(k_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<1>::kSmem));
+  B2_CUDA(cudaFuncSetAttribute(k_gemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<2>::kSmem));
+  int dev = 0;
+  B2_CUDA(cudaGetDevice(&dev));
+  B2_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
+  done = 1;
+  return B200MOE_OK;
+}
+
+constexpr int kMaxTPrefill = 1 << 16;
+
+}  // namespace
+
+extern "C" {
+
+size_t b200moe_prefill_workspace_size(int T) {
+  return (T <= 0 || T > kMaxTPrefill) ? 0 : prefill_ws_bytes(T);
+}
+
+int b200moe_moe_prefill(const void *x, int x_dtype, float *resid, float eps, int T, const b200moe_layer *L,
+                        float *out, int32_t *ids_out, void *ws, size_t ws_bytes, void *stream) {
+  if (T <= 0 || T > kMaxTPrefill)
+    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: T=%d outside [1, %d]", T, kMaxTPrefill);
+  if ((!x && !resid) || (!out && !resid) || !ws || !L)
+    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: need (x and out) or resid, a layer and ws");
+  if (!resid && x_dtype != B200MOE_F32 && x_dtype != B200MOE_BF16)
+    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: x_dtype %d is neither F32 nor BF16", x_dtype);
+  if ((x && !a16(x)) || (out && !a16(out)) || (resid && !a16(resid)) || !a16(ws))
+    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: pointers must be 16-byte aligned");
+  if (ws_bytes < prefill_ws_bytes(T))
+    return b2host::set_error(B200MOE_ESIZE, "moe_prefill: workspace %zu B < required %zu B", ws_bytes,
+                             prefill_ws_bytes(T));
+  if (!L->gate || !L->up || !L->down || !L->sh_gate || !L->sh_up || !L->sh_down || !L->router_w || !L->sh_gate_w)
+    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: layer has a NULL weight pointer");
+  int rc = ensure_gemm_attrs();
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  PrefillWS w = carve_prefill(ws, T);
+  B2_CUDA(cudaMemsetAsync(w.counts, 0, kNE * 4, s));
+  B2_CUDA(cudaMemsetAsync(w.err, 0, 4, s));
+  k_prep<<<(T + 7) / 8, 256, 0, s>>>(x, x_dtype, resid, eps, T, L->sh_gate_w, w.xn, w.x16, w.sg);
+  B2_CUDA(cudaGetLastError());
+  k_router_gemm<<<dim3((T + 63) / 64, kE / 64), 256, 0, s>>>(w.xn, T, L->router_w, L->logit_bias, w.logits);
+  B2_CUDA(cudaGetLastError());
+  k_route_tok<<<(T + 7) / 8, 256, 0, s>>>(w.logits, T, w.ids, w.wb, w.order, w.counts, ids_out);
+  B2_CUDA(cudaGetLastError());
+  k_plan<<<1, 512, 0, s>>>(T, w.counts, w.offsets, w.tiles1, w.tiles2, w.ntiles);
+  B2_CUDA(cudaGetLastError());
+  k_fill<<<kNE, 1024, 0, s>>>(T, w.ids, w.offsets, w.plist);
+  B2_CUDA(cudaGetLastError());
+  GemmParams g;
+  g.wa0 = (const uint8_t *)L->gate;
+  g.wa1 = (const uint8_t *)L->up;
+  g.stride = L->gate_up_expert_stride;
+  g.sh0 = (const uint8_t *)L->sh_gate;
+  g.sh1 = (const uint8_t *)L->sh_up;
+  g.tiles = w.tiles1;
+  g.ntiles = w.ntiles;
+  g.plist = w.plist;
+  g.x16 = w.x16;
+  g.s16 = w.s16;
+  g.wb = w.wb;
+  g.y = w.y;
+  g.ysh = w.ysh;
+  g.err = w.err;
+  k_gemm<1><<<g_num_sms, 288, GemmCfg<1>::kSmem, s>>>(g);
+  B2_CUDA(cudaGetLastError());
+  g.wa0 = (const uint8_t *)L->down;
+  g.wa1 = nullptr;
+  g.stride = L->down_expert_stride;
+  g.sh0 = (const uint8_t *)L->sh_down;
+  g.sh1 = nullptr;
+  g.tiles = w.tiles2;
+  k_gemm<2><<<g_num_sms, 288, GemmCfg<2>::kSmem, s>>>(g);
+  B2_CUDA(cudaGetLastError());
+  const int64_t nthreads = (int64_t)T * (kH / 4);
+  k_combine<<<(unsigned)((nthreads + 255) / 256), 256, 0, s>>>(T, w.y, w.ysh, w.sg, w.order, resid ? resid : out,
+                                                               resid ? 1 : 0);
+  B2_CUDA(cudaGetLastError());
+  return B200MOE_OK;
+}
+
+int b200moe_prefill_status(const void *ws, int T, int *status, void *stream) {
+  if (!ws || !status || T <= 0 || T > kMaxTPrefill) return b2host::set_error(B200MOE_EINVAL, "prefill_status: bad args");
+  PrefillWS w = carve_prefill(const_cast<void *>(ws), T);
+  B2_CUDA(cudaMemcpyAsync(status, w.err, 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+  B2_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  return B200MOE_OK;
+}
+
+}  // extern "C"

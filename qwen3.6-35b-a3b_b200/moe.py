@@ -73,23 +73,45 @@ def _tokens(g, device) -> tuple:
     return x, (_abi.F32 if x.dtype == torch.float32 else _abi.BF16)
 
 
-def moe_block(g: torch.Tensor, E_, layer: int = 0, probe_row=None, out: torch.Tensor | None = None):
+PREFILL_MIN_TOKENS = 64   # at and above this many tokens the grouped-GEMM path is used
+
+
+def prefill_workspace(T: int, device) -> torch.Tensor:
+    """A cached workspace of ``b200moe_prefill_workspace_size(T)`` bytes on ``device``."""
+    need = _abi.prefill_workspace_size(T)
+    key = ("prefill", torch.device(device), torch.cuda.current_stream(device).cuda_stream)
+    ws = _WS.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=device)
+        _WS[key] = ws
+    return ws
+
+
+def moe_block(g: torch.Tensor, E_, layer: int = 0, probe_row=None, out: torch.Tensor | None = None,
+              path: str = "auto"):
     """``engine/m3_forward.py:430`` on the B200 path.
 
     ``g`` [B, T, 2048] (or [T, 2048]) f32/bf16; returns ``(out, info)`` with ``out`` f32 in
     ``g``'s leading shape, ``info = {"ids": [B,T,8] int32 (device), "used": int}``.
     Routing is R1-R5 with the cast before the multiply; routed outputs are summed in
     ascending expert id; the shared expert is gated by sigmoid(w_sg . x).
+    ``path``: "decode" (gather-GEMV, f32 CUDA cores), "prefill" (token sort + tcgen05 grouped
+    GEMMs, fp16 operands) or "auto" (prefill from ``PREFILL_MIN_TOKENS`` tokens on).
     """
     if probe_row is not None:
         raise Refused("probe-row", "band-operand probes are a host-oracle feature; not on the device path")
+    if path not in ("auto", "decode", "prefill"):
+        raise Refused("path", "path must be auto, decode or prefill, got %r" % (path,))
     L = _layer_of(E_, layer)
     x, xd = _tokens(g, L.device)
     T = x.shape[0]
     if out is None:
         out = torch.empty((T, H), dtype=torch.float32, device=L.device)
     ids = torch.empty((T, TOPK), dtype=torch.int32, device=L.device)
-    _abi.moe_decode(x, xd, T, L.abi(), out, ids, None, workspace(T, L.device))
+    if path == "prefill" or (path == "auto" and T >= PREFILL_MIN_TOKENS):
+        _abi.moe_prefill(x, xd, None, RMS_EPS, T, L.abi(), out, ids, prefill_workspace(T, L.device))
+    else:
+        _abi.moe_decode(x, xd, T, L.abi(), out, ids, None, workspace(T, L.device))
     lead = tuple(g.shape[:-1])
     return out.reshape(*lead, H), _Info(ids=ids.reshape(*lead, TOPK))
 
@@ -104,7 +126,7 @@ def moe_router(g_row: torch.Tensor, E_, layer: int = 0) -> dict:
     ids = torch.empty((T, TOPK), dtype=torch.int32, device=dev)
     wf = torch.empty((T, TOPK), dtype=torch.float32, device=dev)
     wb = torch.empty((T, TOPK), dtype=torch.bfloat16, device=dev)
-    _abi.router(x, xd, T, L.router_w, L.logit_bias, logits, ids, wf, wb)
+    _abi.router(x, xd, T, L.router_w, L.logit_bias, logits, ids, wf, wb, workspace(T, dev))
     return dict(router_logits=logits, topk_ids=ids, topk_weights=wb, topk_weights_f32=wf)
 
 
@@ -130,6 +152,29 @@ def moe_stack(resid: torch.Tensor, E_: DeviceEngine, n_layers: int | None = None
 
 def stack_workspace_bytes(T: int) -> int:
     return _abi.stack_workspace_size(T, 1)
+
+
+def moe_stack_prefill(resid: torch.Tensor, E_: DeviceEngine, n_layers: int | None = None,
+                      eps: float = RMS_EPS, ids_out: torch.Tensor | None = None,
+                      ws: torch.Tensor | None = None) -> torch.Tensor:
+    """The config-4 sub-stack on the prefill path: per layer ``resid += moe(rmsnorm(resid))``
+    through the tcgen05 grouped GEMMs. ``ids_out`` (optional) is [n_layers, T, 8] int32."""
+    if resid.dtype != torch.float32 or resid.shape[-1] != H:
+        raise Refused("shape", "resid must be f32 [T, %d]" % H)
+    n = len(E_.layers) if n_layers is None else int(n_layers)
+    r = resid.reshape(-1, H)
+    T = r.shape[0]
+    dev = E_.layers[0].device
+    ws = ws if ws is not None else prefill_workspace(T, dev)
+    for l in range(n):
+        _abi.moe_prefill(None, _abi.F32, r, eps, T, E_.layers[l].abi(), None,
+                         None if ids_out is None else ids_out[l], ws)
+    return resid
+
+
+def prefill_status(T: int, device) -> int:
+    """Device status word of the cached prefill workspace (0 = every pipeline wait completed)."""
+    return _abi.prefill_status(prefill_workspace(T, device), T)
 
 
 __all__ = ["moe_block", "moe_router", "moe_stack", "Refused", "N_LAYERS"]

@@ -1,0 +1,125 @@
+"""The prefill path (token sort + tcgen05 grouped GEMMs, b200moe_moe_prefill) vs the oracle.
+
+Parity bar (written here): routing ids bit-exact against the declared-order C restatement
+(the same router as decode); block output against the f64 restatement of
+engine/m3_forward.py:430-476 with the same ids within rel-L2 1e-3 and
+max-abs / max|ref| 2e-3. The tensor cores take fp16 operands (weights dequantised from Q4_K
+to fp16, activations rounded to fp16), so the f32-level agreement of the decode path is not
+expected here; the bar above is.
+"""
+import numpy as np
+import pytest
+
+from conftest import host_layer
+
+pytestmark = pytest.mark.gpu
+REL_L2, MAX_ABS_NORM = 1e-3, 2e-3
+
+
+@pytest.fixture(scope="module")
+def layer3(cuda):
+    from b200moe.engine import DeviceLayer
+    return DeviceLayer.synthetic(3, 0, cuda)
+
+
+def _run(cuda, L, xb):
+    import torch
+    from b200moe import moe
+    T = xb.shape[0]
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).to(cuda)
+    out, info = moe.moe_block(x, L, 0, path="prefill")
+    torch.cuda.synchronize()
+    assert moe.prefill_status(T, cuda) == 0
+    return out.cpu().numpy(), info["ids"].cpu().numpy()
+
+
+def _check(xb, out, ids, Lh, sample=None):
+    from oracle import moe as OM
+    from oracle.bf16 import bf16_bits_to_f32
+    x = bf16_bits_to_f32(xb)
+    r = OM.router(x, Lh.wg, Lh.bias)
+    assert (ids == r["ids"]).all()
+    rows = np.arange(x.shape[0]) if sample is None else sample
+    ref = OM.moe_block_f64(x[rows], Lh, ids[rows], r["w_bf16"][rows])["out"]
+    c = OM.compare(out[rows], ref)
+    assert c["rel_l2"] < REL_L2 and c["max_abs_norm"] < MAX_ABS_NORM, c
+    return c
+
+
+@pytest.mark.parametrize("T", [1, 17, 256])
+def test_prefill_vs_oracle(cuda, layer3, T):
+    from b200moe import synth
+    xb = synth.tokens(3, T, stream=0)
+    out, ids = _run(cuda, layer3, xb)
+    _check(xb, out, ids, host_layer(3, 0))
+
+
+def test_prefill_config3_4096(cuda, layer3):
+    """Config 3 size (4096 tokens; the shared expert spans 16 tiles of 256 tokens): ids for
+    every token, outputs on a seeded sample of 48 tokens, deterministic across runs."""
+    import torch
+    from b200moe import synth
+    xb = synth.tokens(3, 4096, stream=1)
+    out, ids = _run(cuda, layer3, xb)
+    out2, ids2 = _run(cuda, layer3, xb)
+    assert (ids == ids2).all() and np.array_equal(out, out2)
+    sample = np.sort(np.random.default_rng(0).choice(4096, 48, replace=False))
+    _check(xb, out, ids, host_layer(3, 0), sample)
+    assert np.isfinite(out).all()
+    del torch
+
+
+def test_prefill_matches_decode_routing_and_output(cuda, layer3):
+    import torch
+    from b200moe import moe, synth
+    xb = synth.tokens(3, 96, stream=2)
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).to(cuda)
+    a, ia = moe.moe_block(x, layer3, path="prefill")
+    b, ib = moe.moe_block(x, layer3, path="decode")
+    torch.cuda.synchronize()
+    assert torch.equal(ia["ids"], ib["ids"])
+    rel = float(torch.linalg.norm(a - b) / torch.linalg.norm(b))
+    assert rel < REL_L2
+
+
+def test_prefill_zipf_skew(cuda):
+    """Config 2 law at 512 tokens: skewed expert load (several experts above 256 tokens,
+    i.e. multi-chunk groups), many experts idle."""
+    from b200moe import synth
+    from b200moe.engine import DeviceLayer
+    L = DeviceLayer.synthetic(2, 0, cuda, bias=True)
+    xb = synth.tokens(2, 512, stream=3)
+    out, ids = _run(cuda, L, xb)
+    counts = np.bincount(ids.reshape(-1), minlength=256)
+    assert counts.max() > 256 and (counts == 0).any()
+    sample = np.sort(np.random.default_rng(1).choice(512, 32, replace=False))
+    _check(xb, out, ids, host_layer(2, 0, bias=True), sample)
+    del L
+
+
+def test_stack_prefill_teacher_forced(cuda):
+    """Two layers of the config-4 stack on the prefill path (resid += moe(rmsnorm(resid)))."""
+    import torch
+    from oracle import moe as OM
+    from oracle.bf16 import bf16_bits_to_f32
+    from b200moe import moe, synth
+    from b200moe.engine import DeviceEngine
+    eng = DeviceEngine.synthetic(4, 2, cuda)
+    T = 80
+    resid = torch.from_numpy(bf16_bits_to_f32(synth.tokens(4, T, stream=11)).copy()).to(cuda)
+    for l in range(2):
+        before = resid.cpu().numpy().copy()
+        ids = torch.empty((1, T, 8), dtype=torch.int32, device=cuda)
+        moe.moe_stack_prefill(resid, DeviceEngine([eng.layers[l]]), ids_out=ids)
+        torch.cuda.synchronize()
+        assert moe.prefill_status(T, cuda) == 0
+        Lh = host_layer(4, l)
+        xn = OM.rmsnorm(before)
+        r = OM.router(xn, Lh.wg)
+        assert (ids.cpu().numpy().reshape(T, 8) == r["ids"]).all(), l
+        sample = np.arange(0, T, 5)
+        ref = before[sample].astype(np.float64) + OM.moe_block_f64(xn[sample], Lh, r["ids"][sample],
+                                                                   r["w_bf16"][sample])["out"]
+        c = OM.compare(resid.cpu().numpy()[sample], ref)
+        assert c["rel_l2"] < REL_L2, (l, c)
+    del eng
