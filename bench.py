@@ -44,7 +44,7 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    p.add_argument("--workload", choices=["stack_decode", "layer_decode", "dequant"], default="stack_decode")
+    p.add_argument("--workload", choices=["stack_decode", "layer_decode", "prefill"], default="stack_decode")
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--layers", type=int, default=N_LAYERS)
     p.add_argument("--seed", type=int, default=4)
@@ -244,8 +244,24 @@ def run_b200(args):
 
         def step(i):
             moe.moe_block(tok_dev[i], L, 0, out=out)
+    elif args.workload == "prefill":
+        # config 3: one layer, 4096 tokens through token sort + tcgen05 grouped GEMMs
+        T = args.batch if args.batch > 1 else 4096
+        L = DeviceLayer.synthetic(3, 0, dev)
+        nl = 1
+        launches_per_step = 9
+        tok_bits = synth.tokens(3, T, stream=100 + rank)
+        tok_dev = torch.from_numpy(tok_bits.view(np.int16)).view(torch.bfloat16).reshape(T, 2048).to(dev)
+        out = torch.empty((T, 2048), dtype=torch.float32, device=dev)
+        ids_all = torch.zeros((K + W, 1, 1, 8), dtype=torch.int32, device=dev)
+        pws = moe.prefill_workspace(T, dev)
+        flops_per_step = 2.0 * T * 9 * 3 * 2048 * 512   # 8 routed + shared, gate+up+down MACs x 2
+        bytes_per_step = None
+
+        def step(i):
+            moe.moe_block(tok_dev, L, 0, out=out, path="prefill")
     else:
-        raise SystemExit("workload %s: use tests for dequant parity; bench focuses on decode" % args.workload)
+        raise SystemExit("unknown workload %s" % args.workload)
 
     # ---------------- value: device-resident inputs, CUDA events, max over ranks
     for i in range(W):
@@ -273,6 +289,10 @@ def run_b200(args):
         dist.barrier()
     ms_step = ms / K
     value = world * K * T / (ms / 1e3)
+    if args.workload == "prefill":
+        st = moe.prefill_status(T, dev)
+        if st != 0:
+            raise SystemExit("prefill status word %d (pipeline timeout or fp16 range)" % st)
 
     # algorithmic bytes: distinct experts actually touched per layer (+ shared, router, act)
     ids_np = ids_all[W:].cpu().numpy()
@@ -282,6 +302,15 @@ def run_b200(args):
             nl * (ROUTER_BYTES + WSG_BYTES + 2 * T * 2048 * 4)
         expert_bytes = float(np.mean([sum((u + 1) * EXPERT_BYTES for u in row) for row in uniq]))
     achieved = bytes_per_step / (ms_step / 1e3) / 1e9 if bytes_per_step else None
+    roof_bound, roof_unit, peak = "hbm", "GB/s", hbm_peak
+    if args.workload == "prefill":
+        roof_bound, roof_unit = "tensor", "TFLOP/s"
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peak = float(json.load(f)["bf16_tflops"])
+        except Exception:
+            peak, peak_kind = 1590.0, "fallback"
+        achieved = flops_per_step / (ms_step / 1e3) / 1e12
 
     # ---------------- e2e: pinned host input -> graph -> host read of the result, every step
     e2e = None
@@ -337,17 +366,19 @@ def run_b200(args):
 
     traffic = committed_traffic(args.workload)
     line = {
-        "metric": "moe_stack_decode_tok_per_s" if args.workload == "stack_decode" else "moe_layer_decode_tok_per_s",
+        "metric": {"stack_decode": "moe_stack_decode_tok_per_s", "layer_decode": "moe_layer_decode_tok_per_s",
+                   "prefill": "moe_prefill_tok_per_s"}[args.workload],
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Q4_K, config-0 field law; random-init weights)",
-        "config": {"workload": ("config4_stack_decode_b%d" % T) if args.workload == "stack_decode"
-                   else "config0_layer_decode_b%d" % T,
+        "config": {"workload": {"stack_decode": "config4_stack_decode_b%d" % T,
+                                "layer_decode": "config0_layer_decode_b%d" % T,
+                                "prefill": "config3_prefill_t%d" % T}[args.workload],
                    "layers": nl, "batch": T, "seed": args.seed, "parallelism": "replicas%d" % world,
                    "l2": "inputs larger than L2: distinct token per step, %.0f MB of Q4_K streamed per step"
                          % ((bytes_per_step or 0) / 1e6)},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": (achieved / hbm_peak) if achieved else None,
+        "roofline": {"bound": roof_bound, "achieved": achieved, "peak": peak, "unit": roof_unit,
+                     "frac": (achieved / peak) if achieved else None,
                      "traffic": traffic.get("dram_bytes_per_step") if traffic else None,
                      "peak_kind": peak_kind,
                      "kernel": "one graph replay = %d kernels (router/shared K1, routed gate_up K2, down+combine K3 "

@@ -124,8 +124,9 @@ int b200moe_moe_prefill(const void *x, int x_dtype, float *resid, float eps, int
                         const b200moe_layer *layer, float *out, int32_t *ids_out, void *ws,
                         size_t ws_bytes, void *stream);
 
-/* Copy the prefill workspace's device status word to *status (synchronises `stream`):
- * 0 = ok, 1 / 2 = a gate_up / down GEMM pipeline wait exceeded its ~1 s budget. */
+/* Copy the prefill workspace's device status word to *status (synchronises `stream`). Bits:
+ * 1 / 2 = a gate_up / down GEMM pipeline wait exceeded its ~1 s budget; 4 = an fp16 tensor-core
+ * operand was out of range (|x| or |silu(gate)*up| * 2^-10 above 65504). 0 = ok. */
 int b200moe_prefill_status(const void *ws, int T, int *status, void *stream);
 
 #ifdef __cplusplus

@@ -28,6 +28,8 @@ namespace {
 
 constexpr int kNE = kE + 1;     // 256 routed experts + the shared expert
 constexpr int kChunk = 256;     // tokens per GEMM tile
+constexpr float kSScale = 1.0f / 1024.0f;  // fp16 storage scale of s = silu(gate) * up
+constexpr int kErrRange = 4;    // status bit: an fp16 operand (x or s) was out of range
 
 struct PrefillWS {
   float *xn;
@@ -88,7 +90,7 @@ PrefillWS carve_prefill(void *ws, int T) {
 
 // ------------------------------------------------------------------------- k_prep
 __global__ void __launch_bounds__(256) k_prep(const void *x, int x_dtype, const float *resid, float eps, int T,
-                                              const uint16_t *wsg, float *xn, __half *x16, float *sg) {
+                                              const uint16_t *wsg, float *xn, __half *x16, float *sg, int32_t *err) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -132,6 +134,10 @@ __global__ void __launch_bounds__(256) k_prep(const void *x, int x_dtype, const 
   float *dst = xn + (size_t)t * kH + 64 * lane;
   __half *d16 = x16 + (size_t)t * kH + 64 * lane;
   float z = 0.0f;
+  bool range_bad = false;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) range_bad |= !(fabsf(v[i]) <= 65504.0f);
+  if (__any_sync(0xFFFFFFFFu, range_bad) && lane == 0) atomicOr(err, kErrRange);
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     *reinterpret_cast<float4 *>(dst + 4 * i) = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
@@ -497,6 +503,7 @@ __global__ void __launch_bounds__(288, 1) k_gemm(GemmParams P) {
     __syncwarp();
   } else {  // ---------------------------------------------------------- epilogue (warps 0-3)
     uint32_t tcount = 0;
+    bool range_bad = false;
     const int row = 32 * warp + lane;  // TMEM lane = weight row within the tile
     for (int ti = blockIdx.x; ti < ntiles && ok; ti += gridDim.x, ++tcount) {
       const int4 tl = __ldg(P.tiles + ti);
@@ -515,8 +522,11 @@ __global__ void __launch_bounds__(288, 1) k_gemm(GemmParams P) {
           const int j = wt * 128 + row;
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            if (c0 + i < n)  // stored as s / 16 (exact): headroom under fp16's 65504 for RMS-1 inputs
-              P.s16[(size_t)(r0 + c0 + i) * kI + j] = __float2half_rn(__fmul_rn(__fmul_rn(silu_f(a[i]), u[i]), 0.0625f));
+            if (c0 + i < n) {  // stored as s * 2^-10 (exact scaling): fp16 headroom up to |s| < 6.7e7
+              const float sv = __fmul_rn(__fmul_rn(silu_f(a[i]), u[i]), kSScale);
+              if (!(fabsf(sv) <= 65504.0f)) range_bad = true;
+              P.s16[(size_t)(r0 + c0 + i) * kI + j] = __float2half_rn(sv);
+            }
         } else {
           tmem_wait_ld();
           const int h = wt * 128 + row;
@@ -524,7 +534,7 @@ __global__ void __launch_bounds__(288, 1) k_gemm(GemmParams P) {
           for (int i = 0; i < 16; ++i) {
             if (c0 + i >= n) continue;
             const int pl = __ldg(P.plist + r0 + c0 + i);
-            const float o = __fmul_rn(a[i], 16.0f);  // undo the s / 16 storage scale (exact)
+            const float o = __fmul_rn(a[i], 1.0f / kSScale);  // undo the s storage scale (exact)
             if (e < kE) P.y[(size_t)pl * kH + h] = __fmul_rn(o, bf16f(__ldg(P.wb + pl)));
             else P.ysh[(size_t)pl * kH + h] = o;
           }
@@ -533,8 +543,9 @@ __global__ void __launch_bounds__(288, 1) k_gemm(GemmParams P) {
       tc_fence_before();
       mbar_arrive(acc_empty);
     }
+    if (range_bad) atomicOr(P.err, kErrRange);
   }
-  if (!ok) atomicExch(P.err, kMode);
+  if (!ok) atomicOr(P.err, kMode);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -616,7 +627,7 @@ int b200moe_moe_prefill(const void *x, int x_dtype, float *resid, float eps, int
   PrefillWS w = carve_prefill(ws, T);
   B2_CUDA(cudaMemsetAsync(w.counts, 0, kNE * 4, s));
   B2_CUDA(cudaMemsetAsync(w.err, 0, 4, s));
-  k_prep<<<(T + 7) / 8, 256, 0, s>>>(x, x_dtype, resid, eps, T, L->sh_gate_w, w.xn, w.x16, w.sg);
+  k_prep<<<(T + 7) / 8, 256, 0, s>>>(x, x_dtype, resid, eps, T, L->sh_gate_w, w.xn, w.x16, w.sg, w.err);
   B2_CUDA(cudaGetLastError());
   k_router_gemm<<<dim3((T + 63) / 64, kE / 64), 256, 0, s>>>(w.xn, T, L->router_w, L->logit_bias, w.logits);
   B2_CUDA(cudaGetLastError());
