@@ -96,6 +96,25 @@ int b200moe_moe_decode(const void *x, int x_dtype, int T, const b200moe_layer *l
                        float *out, int32_t *ids_out, uint16_t *w_out, void *ws,
                        size_t ws_bytes, void *stream);
 
+/* Largest token count b200moe_moe_decode_noalloc accepts. */
+#define B200MOE_NOALLOC_MAX_T 16
+
+/* b200moe_moe_decode without a caller workspace, for callers that cannot allocate device
+ * memory at the point of the call: a plugin inside a host framework that hands it only
+ * input/output buffers, code running while a CUDA graph is being captured (allocation is
+ * not allowed there), or an FFI caller with no device allocator of its own. No counterpart
+ * in the reference, whose CPU path allocates freely.
+ * Scratch lives in a fixed static device array inside the library, sized for at most
+ * B200MOE_NOALLOC_MAX_T (16) tokens; larger T is refused with B200MOE_ESIZE. The array is
+ * resident on every GPU that loads the library for the life of the process. The first call
+ * on each device looks up the array's device address (cudaGetSymbolAddress), so make that
+ * first call before any stream capture. All calls on a device share the one array: calls
+ * that can overlap on the GPU (different streams without ordering) race on it and must be
+ * serialised by the caller. The path keeps nothing that must start at zero between calls.
+ * Allocates nothing (no cudaMalloc / cudaFree, no allocating library routine). */
+int b200moe_moe_decode_noalloc(const void *x, int x_dtype, int T, const b200moe_layer *layer,
+                               float *out, int32_t *ids_out, uint16_t *w_out, void *stream);
+
 /* Workspace bytes for b200moe_stack_decode. */
 size_t b200moe_stack_workspace_size(int T, int n_layers);
 

@@ -303,7 +303,7 @@ cudaError_t launch(Kern k, unsigned grid, unsigned block, size_t smem, cudaStrea
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
-size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+constexpr size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 struct DecodeWS {
   float *xw;
@@ -312,7 +312,7 @@ struct DecodeWS {
   float *sg;
 };
 
-size_t decode_ws_bytes(int T) {
+constexpr size_t decode_ws_bytes(int T) {
   return align256((size_t)T * kH * 4) + align256((size_t)T * kE * 2) + align256((size_t)T * 9 * kI * 4) +
          align256((size_t)T * 4);
 }
@@ -399,6 +399,32 @@ int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const 
 
 constexpr int kMaxT = 1 << 16;
 
+// ------------------------------------------------------------------------- no-allocation entry
+// Scratch for b200moe_moe_decode_noalloc: a fixed, file-scope device array sized for
+// B200MOE_NOALLOC_MAX_T tokens (about 425 KB; every GPU that loads this library holds it
+// until the process exits). Host code may not use the array's name as a device address, so
+// its address is looked up once per device with cudaGetSymbolAddress and cached.
+constexpr int kNoAllocMaxT = B200MOE_NOALLOC_MAX_T;
+__device__ __align__(256) unsigned char g_noalloc_scratch[decode_ws_bytes(kNoAllocMaxT)];
+
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[128] = {};
+
+int noalloc_scratch(void **out) {
+  int dev = 0;
+  B2_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 128) return b2host::set_error(B200MOE_EINVAL, "moe_decode_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // current device
+    if (e != cudaSuccess) return b2host::cuda_status(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return B200MOE_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -446,6 +472,26 @@ int b200moe_moe_decode(const void *x, int x_dtype, int T, const b200moe_layer *l
   cudaStream_t s = (cudaStream_t)stream;
   const DecodeWS w = carve(ws, T);
   return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, w, s, true);
+}
+
+int b200moe_moe_decode_noalloc(const void *x, int x_dtype, int T, const b200moe_layer *layer, float *out,
+                               int32_t *ids_out, uint16_t *w_out, void *stream) {
+  if (T <= 0 || T > kNoAllocMaxT)
+    return b2host::set_error(B200MOE_ESIZE,
+                             "moe_decode_noalloc: T=%d outside [1, %d]; the built-in scratch holds at most %d tokens "
+                             "(use b200moe_moe_decode with a caller workspace for more)",
+                             T, kNoAllocMaxT, kNoAllocMaxT);
+  if (!x || !out) return b2host::set_error(B200MOE_EINVAL, "moe_decode_noalloc: x and out are required");
+  if (x_dtype != B200MOE_F32 && x_dtype != B200MOE_BF16)
+    return b2host::set_error(B200MOE_EINVAL, "moe_decode_noalloc: x_dtype %d is neither F32 nor BF16", x_dtype);
+  if (!al16(x) || !al16(out)) return b2host::set_error(B200MOE_EINVAL, "moe_decode_noalloc: pointers must be 16-byte aligned");
+  int rc = check_layer(layer, "moe_decode_noalloc");
+  if (rc) return rc;
+  void *scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, carve(scratch, T), (cudaStream_t)stream,
+                   true);
 }
 
 size_t b200moe_stack_workspace_size(int T, int n_layers) {
