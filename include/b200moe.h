@@ -143,6 +143,27 @@ int b200moe_moe_prefill(const void *x, int x_dtype, float *resid, float eps, int
                         const b200moe_layer *layer, float *out, int32_t *ids_out, void *ws,
                         size_t ws_bytes, void *stream);
 
+/* The route stage of b200moe_moe_prefill on its own (used by expert parallelism, where a rank
+ * routes its own tokens and then ships them to the ranks owning the chosen experts): x (or
+ * rmsnorm(resid)) -> x16_out [T][2048] fp16 activations, ids_out [T][8], w_out [T][8] bf16
+ * routing weights, sg_out [T] shared-expert gate sigmoid(w_sg.x). Same declared router as
+ * b200moe_router. Workspace: b200moe_prefill_workspace_size(T).
+ * Replaces engine/m3_forward.py:436-446 (router and shared gate). */
+int b200moe_moe_route(const void *x, int x_dtype, float *resid, float eps, int T,
+                      const b200moe_layer *layer, void *x16_out, int32_t *ids_out,
+                      uint16_t *w_out, float *sg_out, void *ws, size_t ws_bytes, void *stream);
+
+/* The expert stage of b200moe_moe_prefill for pre-routed tokens: for each token, the slots
+ * whose expert id lies in [e_lo, e_hi) go through the Q4_K grouped GEMMs (tcgen05), and
+ * out[t] (+)= sum over those slots in ascending expert id of w * expert(x) -- plus
+ * sg[t] * shared_expert(x) when sg is non-NULL. Slots outside the range are skipped, so a
+ * rank of an expert-parallel group passes its own expert range and sg = NULL, and the
+ * token's home rank adds the shared expert. accumulate != 0 adds into out.
+ * Replaces engine/m3_forward.py:447-475 (grouping, expert loop, combine). */
+int b200moe_moe_experts(const void *x16, int T, const int32_t *ids, const uint16_t *w_bf16,
+                        int e_lo, int e_hi, const float *sg, const b200moe_layer *layer,
+                        float *out, int accumulate, void *ws, size_t ws_bytes, void *stream);
+
 /* Copy the prefill workspace's device status word to *status (synchronises `stream`). Bits:
  * 1 / 2 = a gate_up / down GEMM pipeline wait exceeded its ~1 s budget; 4 = an fp16 tensor-core
  * operand was out of range (|x| or |silu(gate)*up| * 2^-10 above 65504). 0 = ok. */

@@ -22,7 +22,8 @@ EXPORTS = ("b200moe_abi_version", "b200moe_last_error", "b200moe_q4k_dequant",
            "b200moe_decode_workspace_size",
            "b200moe_moe_decode", "b200moe_moe_decode_noalloc", "b200moe_stack_workspace_size",
            "b200moe_stack_decode",
-           "b200moe_prefill_workspace_size", "b200moe_moe_prefill", "b200moe_prefill_status")
+           "b200moe_prefill_workspace_size", "b200moe_moe_prefill", "b200moe_moe_route",
+           "b200moe_moe_experts", "b200moe_prefill_status")
 
 
 class B200MoeError(RuntimeError):
@@ -82,6 +83,12 @@ def lib():
         L.b200moe_moe_prefill.restype = i32
         L.b200moe_moe_prefill.argtypes = [vp, i32, vp, ctypes.c_float, i32, ctypes.POINTER(Layer), vp, vp, vp,
                                           sz, vp]
+        L.b200moe_moe_route.restype = i32
+        L.b200moe_moe_route.argtypes = [vp, i32, vp, ctypes.c_float, i32, ctypes.POINTER(Layer), vp, vp, vp, vp,
+                                        vp, sz, vp]
+        L.b200moe_moe_experts.restype = i32
+        L.b200moe_moe_experts.argtypes = [vp, i32, vp, vp, i32, i32, vp, ctypes.POINTER(Layer), vp, i32, vp, sz,
+                                          vp]
         L.b200moe_prefill_status.restype = i32
         L.b200moe_prefill_status.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_int), vp]
         _LIB = L
@@ -182,3 +189,19 @@ def prefill_status(ws, T: int, stream=None) -> int:
     st = ctypes.c_int(-1)
     _check("b200moe_prefill_status", lib().b200moe_prefill_status(ptr(ws), T, ctypes.byref(st), _stream(stream)))
     return int(st.value)
+
+
+def moe_route(x, x_dtype: int, resid, eps: float, T: int, layer: Layer, x16_out, ids_out, w_out, sg_out, ws,
+              stream=None):
+    _check("b200moe_moe_route",
+           lib().b200moe_moe_route(ptr(x), x_dtype, ptr(resid), eps, T, ctypes.byref(layer), ptr(x16_out),
+                                   ptr(ids_out), ptr(w_out), ptr(sg_out), ptr(ws), ws.numel() * ws.element_size(),
+                                   _stream(stream)))
+
+
+def moe_experts(x16, T: int, ids, w_bf16, e_lo: int, e_hi: int, sg, layer: Layer, out, accumulate: bool, ws,
+                stream=None):
+    _check("b200moe_moe_experts",
+           lib().b200moe_moe_experts(ptr(x16), T, ptr(ids), ptr(w_bf16), int(e_lo), int(e_hi), ptr(sg),
+                                     ctypes.byref(layer), ptr(out), 1 if accumulate else 0, ptr(ws),
+                                     ws.numel() * ws.element_size(), _stream(stream)))

@@ -4,14 +4,19 @@
 //                 and the shared-expert gate sg = sigmoid(w_sg . x)
 //   k_router_gemm R1 logits for all tokens on CUDA cores, in the declared order (32 chunks of
 //                 64 sequential fmaf, chunk sums added left to right) -> bf16
-//   k_route_tok   warp per token: R2..R5 -> ids, bf16 weights, combine order; per-expert counts
+//   k_route_tok   warp per token: R2..R5 -> ids, bf16 routing weights
+//   k_count       per token: the slots whose expert is in the requested range, and their order
 //   k_plan        one CTA: packed row offsets per expert (the shared expert is expert 256 with
 //                 every token), 256-token chunks, and the GEMM tile tables
 //   k_fill        CTA per expert: that expert's (token, slot) assignments in ascending order
 //   k_gemm<1>     gate_up: D[128 gate rows | 128 up rows][tokens] = W . x^T, s = silu(g)*u -> fp16
 //   k_gemm<2>     down:    D[128 h rows][tokens] = W_d . s^T -> y[assignment][h] = o * w (routed)
 //                 or ysh[token][h] = o (shared)
-//   k_combine     out[t] = sum over the 8 slots in ascending expert id of y + sg * ysh
+//   k_combine     out[t] = sum over the in-range slots in ascending expert id of y (+ sg * ysh)
+//
+// Entry points: b200moe_moe_route (the first three kernels), b200moe_moe_experts (the rest,
+// for pre-routed tokens and an expert range: the expert-parallel building block) and
+// b200moe_moe_prefill (both, on one GPU).
 //
 // The grouped GEMMs put the dequantised weight rows in the M = 128 slot of the UMMA and the
 // expert's tokens (<= 256, padded to a multiple of 16) in N, so a ragged expert wastes at most
@@ -235,8 +240,7 @@ __global__ void __launch_bounds__(256) k_router_gemm(const float *__restrict__ x
 }
 
 // ------------------------------------------------------------------------- k_route_tok
-__global__ void __launch_bounds__(256) k_route_tok(const uint16_t *logits, int T, int32_t *ids, uint16_t *wb,
-                                                   int32_t *order, int32_t *counts, int32_t *ids_out) {
+__global__ void __launch_bounds__(256) k_route_tok(const uint16_t *logits, int T, int32_t *ids, uint16_t *wb) {
   __shared__ Route rr[8];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + w;
@@ -245,9 +249,26 @@ __global__ void __launch_bounds__(256) k_route_tok(const uint16_t *logits, int T
   if (lane < kK) {
     ids[(size_t)t * kK + lane] = rr[w].ids[lane];
     wb[(size_t)t * kK + lane] = rr[w].wb[lane];
-    order[(size_t)t * kK + lane] = rr[w].order[lane];
-    if (ids_out) ids_out[(size_t)t * kK + lane] = rr[w].ids[lane];
-    atomicAdd(counts + rr[w].ids[lane], 1);
+  }
+}
+
+// ------------------------------------------------------------------------- k_count
+// Per token: count its slots whose expert lies in [e_lo, e_hi), and the combine order of its
+// 8 slots (ascending expert id; ties cannot occur, top-8 ids are distinct).
+__global__ void __launch_bounds__(256) k_count(int T, const int32_t *ids, int e_lo, int e_hi, int32_t *counts,
+                                               int32_t *order) {
+  const int t = blockIdx.x * 256 + threadIdx.x;
+  if (t >= T) return;
+  int id[kK];
+#pragma unroll
+  for (int k = 0; k < kK; ++k) id[k] = __ldg(ids + (size_t)t * kK + k);
+#pragma unroll
+  for (int k = 0; k < kK; ++k) {
+    if (id[k] >= e_lo && id[k] < e_hi) atomicAdd(counts + id[k], 1);
+    int rank = 0;
+#pragma unroll
+    for (int j = 0; j < kK; ++j) rank += (id[j] < id[k] || (id[j] == id[k] && j < k)) ? 1 : 0;
+    order[(size_t)t * kK + rank] = k;
   }
 }
 
@@ -255,11 +276,11 @@ __global__ void __launch_bounds__(256) k_route_tok(const uint16_t *logits, int T
 // One CTA of 512 threads (thread e < 257 owns expert e; e = 256 is the shared expert).
 // Row offsets follow expert order 0..256; the chunk (tile) order puts the shared expert's
 // full-width chunks first, then experts 0..255, so the largest tiles are scheduled first.
-__global__ void __launch_bounds__(512) k_plan(int T, const int32_t *counts_in, int32_t *offsets, int4 *tiles1,
-                                              int4 *tiles2, int32_t *ntiles) {
+__global__ void __launch_bounds__(512) k_plan(int T, int with_shared, const int32_t *counts_in, int32_t *offsets,
+                                              int4 *tiles1, int4 *tiles2, int32_t *ntiles) {
   __shared__ int sc[512], sn[512];
   const int e = threadIdx.x;
-  const int cnt = e < kE ? counts_in[e] : (e == kE ? T : 0);
+  const int cnt = e < kE ? counts_in[e] : (e == kE && with_shared ? T : 0);
   const int nch = (cnt + kChunk - 1) / kChunk;
   const int pos = e == kE ? 0 : (e < kE ? e + 1 : e);  // a permutation of 0..511
   sc[e] = cnt;
@@ -291,14 +312,17 @@ __global__ void __launch_bounds__(512) k_plan(int T, const int32_t *counts_in, i
 }
 
 // ------------------------------------------------------------------------- k_fill
-__global__ void __launch_bounds__(1024) k_fill(int T, const int32_t *ids, const int32_t *offsets, int32_t *plist) {
+__global__ void __launch_bounds__(1024) k_fill(int T, int with_shared, const int32_t *ids, const int32_t *counts,
+                                                const int32_t *offsets, int32_t *plist) {
   __shared__ int wcount[32];
   __shared__ int running;
   const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   if (e == kE) {
-    for (int t = tid; t < T; t += 1024) plist[offsets[kE] + t] = t;
+    if (with_shared)
+      for (int t = tid; t < T; t += 1024) plist[offsets[kE] + t] = t;
     return;
   }
+  if (counts[e] == 0) return;
   if (tid == 0) running = 0;
   __syncthreads();
   const int n = T * kK;
@@ -554,7 +578,8 @@ __global__ void __launch_bounds__(288, 1) k_gemm(GemmParams P) {
 
 // ------------------------------------------------------------------------- k_combine
 __global__ void __launch_bounds__(256) k_combine(int T, const float *y, const float *ysh, const float *sg,
-                                                 const int32_t *order, float *out, int accumulate) {
+                                                 const int32_t *ids, const int32_t *order, int e_lo, int e_hi,
+                                                 float *out, int accumulate) {
   const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;  // one float4 of one token
   if (idx >= (int64_t)T * (kH / 4)) return;
   const int t = (int)(idx / (kH / 4)), h = (int)(idx % (kH / 4)) * 4;
@@ -562,16 +587,21 @@ __global__ void __launch_bounds__(256) k_combine(int T, const float *y, const fl
 #pragma unroll
   for (int i = 0; i < kK; ++i) {
     const int slot = __ldg(order + (size_t)t * kK + i);
+    const int e = __ldg(ids + (size_t)t * kK + slot);
+    if (e < e_lo || e >= e_hi) continue;
     const float4 v = __ldcs(reinterpret_cast<const float4 *>(y + ((size_t)t * kK + slot) * kH + h));
     acc.x = __fadd_rn(acc.x, v.x);
     acc.y = __fadd_rn(acc.y, v.y);
     acc.z = __fadd_rn(acc.z, v.z);
     acc.w = __fadd_rn(acc.w, v.w);
   }
-  const float g = __ldg(sg + t);
-  const float4 sh = __ldcs(reinterpret_cast<const float4 *>(ysh + (size_t)t * kH + h));
-  float4 r = make_float4(__fadd_rn(acc.x, __fmul_rn(g, sh.x)), __fadd_rn(acc.y, __fmul_rn(g, sh.y)),
-                         __fadd_rn(acc.z, __fmul_rn(g, sh.z)), __fadd_rn(acc.w, __fmul_rn(g, sh.w)));
+  float4 r = acc;
+  if (sg) {
+    const float g = __ldg(sg + t);
+    const float4 sh = __ldcs(reinterpret_cast<const float4 *>(ysh + (size_t)t * kH + h));
+    r = make_float4(__fadd_rn(acc.x, __fmul_rn(g, sh.x)), __fadd_rn(acc.y, __fmul_rn(g, sh.y)),
+                    __fadd_rn(acc.z, __fmul_rn(g, sh.z)), __fadd_rn(acc.w, __fmul_rn(g, sh.w)));
+  }
   float4 *dst = reinterpret_cast<float4 *>(out + (size_t)t * kH + h);
   if (accumulate) {
     const float4 o = *dst;
@@ -598,44 +628,40 @@ int ensure_gemm_attrs() {
 
 constexpr int kMaxTPrefill = 1 << 16;
 
-}  // namespace
-
-extern "C" {
-
-size_t b200moe_prefill_workspace_size(int T) {
-  return (T <= 0 || T > kMaxTPrefill) ? 0 : prefill_ws_bytes(T);
+int check_prefill_layer(const b200moe_layer *L, const char *who) {
+  if (!L || !L->gate || !L->up || !L->down || !L->sh_gate || !L->sh_up || !L->sh_down || !L->router_w ||
+      !L->sh_gate_w)
+    return b2host::set_error(B200MOE_EINVAL, "%s: layer is NULL or has a NULL weight pointer", who);
+  return B200MOE_OK;
 }
 
-int b200moe_moe_prefill(const void *x, int x_dtype, float *resid, float eps, int T, const b200moe_layer *L,
-                        float *out, int32_t *ids_out, void *ws, size_t ws_bytes, void *stream) {
-  if (T <= 0 || T > kMaxTPrefill)
-    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: T=%d outside [1, %d]", T, kMaxTPrefill);
-  if ((!x && !resid) || (!out && !resid) || !ws || !L)
-    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: need (x and out) or resid, a layer and ws");
-  if (!resid && x_dtype != B200MOE_F32 && x_dtype != B200MOE_BF16)
-    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: x_dtype %d is neither F32 nor BF16", x_dtype);
-  if ((x && !a16(x)) || (out && !a16(out)) || (resid && !a16(resid)) || !a16(ws))
-    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: pointers must be 16-byte aligned");
-  if (ws_bytes < prefill_ws_bytes(T))
-    return b2host::set_error(B200MOE_ESIZE, "moe_prefill: workspace %zu B < required %zu B", ws_bytes,
-                             prefill_ws_bytes(T));
-  if (!L->gate || !L->up || !L->down || !L->sh_gate || !L->sh_up || !L->sh_down || !L->router_w || !L->sh_gate_w)
-    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: layer has a NULL weight pointer");
-  int rc = ensure_gemm_attrs();
-  if (rc) return rc;
-  cudaStream_t s = (cudaStream_t)stream;
-  PrefillWS w = carve_prefill(ws, T);
-  B2_CUDA(cudaMemsetAsync(w.counts, 0, kNE * 4, s));
+// Route stage: x (or rmsnorm(resid)) -> x16, ids, wb, sg (each to the given pointer).
+int route_stage(const void *x, int x_dtype, const float *resid, float eps, int T, const b200moe_layer *L,
+                __half *x16, int32_t *ids, uint16_t *wb, float *sg, const PrefillWS &w, cudaStream_t s) {
   B2_CUDA(cudaMemsetAsync(w.err, 0, 4, s));
-  k_prep<<<(T + 7) / 8, 256, 0, s>>>(x, x_dtype, resid, eps, T, L->sh_gate_w, w.xn, w.x16, w.sg, w.err);
+  k_prep<<<(T + 7) / 8, 256, 0, s>>>(x, x_dtype, resid, eps, T, L->sh_gate_w, w.xn, x16, sg, w.err);
   B2_CUDA(cudaGetLastError());
   k_router_gemm<<<dim3((T + 63) / 64, kE / 64), 256, 0, s>>>(w.xn, T, L->router_w, L->logit_bias, w.logits);
   B2_CUDA(cudaGetLastError());
-  k_route_tok<<<(T + 7) / 8, 256, 0, s>>>(w.logits, T, w.ids, w.wb, w.order, w.counts, ids_out);
+  k_route_tok<<<(T + 7) / 8, 256, 0, s>>>(w.logits, T, ids, wb);
   B2_CUDA(cudaGetLastError());
-  k_plan<<<1, 512, 0, s>>>(T, w.counts, w.offsets, w.tiles1, w.tiles2, w.ntiles);
+  return B200MOE_OK;
+}
+
+// Expert stage: grouped GEMMs for the slots whose expert is in [e_lo, e_hi) (+ the shared
+// expert when sg != NULL), then the combine into out (accumulate: out += result).
+int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *wb, int e_lo, int e_hi,
+                  const float *sg, const b200moe_layer *L, float *out, int accumulate, const PrefillWS &w,
+                  cudaStream_t s) {
+  int rc = ensure_gemm_attrs();
+  if (rc) return rc;
+  B2_CUDA(cudaMemsetAsync(w.counts, 0, kNE * 4, s));
+  k_count<<<(T + 255) / 256, 256, 0, s>>>(T, ids, e_lo, e_hi, w.counts, w.order);
   B2_CUDA(cudaGetLastError());
-  k_fill<<<kNE, 1024, 0, s>>>(T, w.ids, w.offsets, w.plist);
+  const int with_shared = sg != nullptr;
+  k_plan<<<1, 512, 0, s>>>(T, with_shared, w.counts, w.offsets, w.tiles1, w.tiles2, w.ntiles);
+  B2_CUDA(cudaGetLastError());
+  k_fill<<<kNE, 1024, 0, s>>>(T, with_shared, ids, w.counts, w.offsets, w.plist);
   B2_CUDA(cudaGetLastError());
   GemmParams g;
   g.wa0 = (const uint8_t *)L->gate;
@@ -646,9 +672,9 @@ int b200moe_moe_prefill(const void *x, int x_dtype, float *resid, float eps, int
   g.tiles = w.tiles1;
   g.ntiles = w.ntiles;
   g.plist = w.plist;
-  g.x16 = w.x16;
+  g.x16 = x16;
   g.s16 = w.s16;
-  g.wb = w.wb;
+  g.wb = wb;
   g.y = w.y;
   g.ysh = w.ysh;
   g.err = w.err;
@@ -663,10 +689,83 @@ int b200moe_moe_prefill(const void *x, int x_dtype, float *resid, float eps, int
   k_gemm<2><<<g_num_sms, 288, GemmCfg<2>::kSmem, s>>>(g);
   B2_CUDA(cudaGetLastError());
   const int64_t nthreads = (int64_t)T * (kH / 4);
-  k_combine<<<(unsigned)((nthreads + 255) / 256), 256, 0, s>>>(T, w.y, w.ysh, w.sg, w.order, resid ? resid : out,
-                                                               resid ? 1 : 0);
+  k_combine<<<(unsigned)((nthreads + 255) / 256), 256, 0, s>>>(T, w.y, w.ysh, sg, ids, w.order, e_lo, e_hi, out,
+                                                               accumulate);
   B2_CUDA(cudaGetLastError());
   return B200MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t b200moe_prefill_workspace_size(int T) {
+  return (T <= 0 || T > kMaxTPrefill) ? 0 : prefill_ws_bytes(T);
+}
+
+int b200moe_moe_prefill(const void *x, int x_dtype, float *resid, float eps, int T, const b200moe_layer *L,
+                        float *out, int32_t *ids_out, void *ws, size_t ws_bytes, void *stream) {
+  if (T <= 0 || T > kMaxTPrefill)
+    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: T=%d outside [1, %d]", T, kMaxTPrefill);
+  if ((!x && !resid) || (!out && !resid) || !ws)
+    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: need (x and out) or resid, and ws");
+  if (!resid && x_dtype != B200MOE_F32 && x_dtype != B200MOE_BF16)
+    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: x_dtype %d is neither F32 nor BF16", x_dtype);
+  if ((x && !a16(x)) || (out && !a16(out)) || (resid && !a16(resid)) || !a16(ws))
+    return b2host::set_error(B200MOE_EINVAL, "moe_prefill: pointers must be 16-byte aligned");
+  if (ws_bytes < prefill_ws_bytes(T))
+    return b2host::set_error(B200MOE_ESIZE, "moe_prefill: workspace %zu B < required %zu B", ws_bytes,
+                             prefill_ws_bytes(T));
+  int rc = check_prefill_layer(L, "moe_prefill");
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  const PrefillWS w = carve_prefill(ws, T);
+  rc = route_stage(x, x_dtype, resid, eps, T, L, w.x16, w.ids, w.wb, w.sg, w, s);
+  if (rc) return rc;
+  if (ids_out) B2_CUDA(cudaMemcpyAsync(ids_out, w.ids, (size_t)T * kK * 4, cudaMemcpyDeviceToDevice, s));
+  return experts_stage(w.x16, T, w.ids, w.wb, 0, kE, w.sg, L, resid ? resid : out, resid ? 1 : 0, w, s);
+}
+
+int b200moe_moe_route(const void *x, int x_dtype, float *resid, float eps, int T, const b200moe_layer *L,
+                      void *x16_out, int32_t *ids_out, uint16_t *w_out, float *sg_out, void *ws, size_t ws_bytes,
+                      void *stream) {
+  if (T <= 0 || T > kMaxTPrefill)
+    return b2host::set_error(B200MOE_EINVAL, "moe_route: T=%d outside [1, %d]", T, kMaxTPrefill);
+  if ((!x && !resid) || !x16_out || !ids_out || !w_out || !sg_out || !ws)
+    return b2host::set_error(B200MOE_EINVAL, "moe_route: x or resid, all four outputs and ws are required");
+  if (!resid && x_dtype != B200MOE_F32 && x_dtype != B200MOE_BF16)
+    return b2host::set_error(B200MOE_EINVAL, "moe_route: x_dtype %d is neither F32 nor BF16", x_dtype);
+  if ((x && !a16(x)) || (resid && !a16(resid)) || !a16(x16_out) || !a16(ws))
+    return b2host::set_error(B200MOE_EINVAL, "moe_route: pointers must be 16-byte aligned");
+  if (ws_bytes < prefill_ws_bytes(T))
+    return b2host::set_error(B200MOE_ESIZE, "moe_route: workspace %zu B < required %zu B", ws_bytes,
+                             prefill_ws_bytes(T));
+  int rc = check_prefill_layer(L, "moe_route");
+  if (rc) return rc;
+  return route_stage(x, x_dtype, resid, eps, T, L, (__half *)x16_out, ids_out, w_out, sg_out, carve_prefill(ws, T),
+                     (cudaStream_t)stream);
+}
+
+int b200moe_moe_experts(const void *x16, int T, const int32_t *ids, const uint16_t *w_bf16, int e_lo, int e_hi,
+                        const float *sg, const b200moe_layer *L, float *out, int accumulate, void *ws,
+                        size_t ws_bytes, void *stream) {
+  if (T <= 0 || T > kMaxTPrefill)
+    return b2host::set_error(B200MOE_EINVAL, "moe_experts: T=%d outside [1, %d]", T, kMaxTPrefill);
+  if (!x16 || !ids || !w_bf16 || !out || !ws)
+    return b2host::set_error(B200MOE_EINVAL, "moe_experts: x16, ids, w_bf16, out and ws are required");
+  if (e_lo < 0 || e_hi > kE || e_lo > e_hi)
+    return b2host::set_error(B200MOE_EINVAL, "moe_experts: expert range [%d, %d) not within [0, 256)", e_lo, e_hi);
+  if (!a16(x16) || !a16(out) || !a16(ws))
+    return b2host::set_error(B200MOE_EINVAL, "moe_experts: pointers must be 16-byte aligned");
+  if (ws_bytes < prefill_ws_bytes(T))
+    return b2host::set_error(B200MOE_ESIZE, "moe_experts: workspace %zu B < required %zu B", ws_bytes,
+                             prefill_ws_bytes(T));
+  int rc = check_prefill_layer(L, "moe_experts");
+  if (rc) return rc;
+  const PrefillWS w = carve_prefill(ws, T);
+  B2_CUDA(cudaMemsetAsync(w.err, 0, 4, (cudaStream_t)stream));
+  return experts_stage((const __half *)x16, T, ids, w_bf16, e_lo, e_hi, sg, L, out, accumulate, w,
+                       (cudaStream_t)stream);
 }
 
 int b200moe_prefill_status(const void *ws, int T, int *status, void *stream) {
