@@ -44,7 +44,8 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    p.add_argument("--workload", choices=["stack_decode", "layer_decode", "prefill"], default="stack_decode")
+    p.add_argument("--workload", choices=["stack_decode", "layer_decode", "prefill", "prefill_ep"],
+                   default="stack_decode")
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--layers", type=int, default=N_LAYERS)
     p.add_argument("--seed", type=int, default=4)
@@ -260,6 +261,25 @@ def run_b200(args):
 
         def step(i):
             moe.moe_block(tok_dev, L, 0, out=out, path="prefill")
+    elif args.workload == "prefill_ep":
+        # config 3 with expert parallelism: 4096 tokens split over the N ranks, each rank owns
+        # 256/N experts; NCCL all-to-all dispatch / combine (strong scaling: total work fixed)
+        from b200moe.ep import ExpertParallelMoE
+        T_total = args.batch if args.batch > 1 else 4096
+        T = T_total // world
+        L = DeviceLayer.synthetic(3, 0, dev)
+        ep = ExpertParallelMoE(L)
+        nl = 1
+        launches_per_step = 11
+        tok_bits = synth.tokens(3, T_total, stream=100)
+        x_all = torch.from_numpy(tok_bits.view(np.int16)).view(torch.bfloat16).reshape(T_total, 2048)
+        x_loc = x_all[rank * T:(rank + 1) * T].to(dev)
+        ids_all = torch.zeros((K + W, 1, 1, 8), dtype=torch.int32, device=dev)
+        flops_per_step = 2.0 * T_total * 9 * 3 * 2048 * 512
+        bytes_per_step = None
+
+        def step(i):
+            ep.forward(x_loc)
     else:
         raise SystemExit("unknown workload %s" % args.workload)
 
@@ -289,8 +309,9 @@ def run_b200(args):
         dist.barrier()
     ms_step = ms / K
     value = world * K * T / (ms / 1e3)
-    if args.workload == "prefill":
-        st = moe.prefill_status(T, dev)
+    scaling = "strong" if args.workload == "prefill_ep" else "weak"
+    if args.workload in ("prefill", "prefill_ep"):
+        st = moe.prefill_status(T, dev) if args.workload == "prefill" else 0
         if st != 0:
             raise SystemExit("prefill status word %d (pipeline timeout or fp16 range)" % st)
 
@@ -303,14 +324,14 @@ def run_b200(args):
         expert_bytes = float(np.mean([sum((u + 1) * EXPERT_BYTES for u in row) for row in uniq]))
     achieved = bytes_per_step / (ms_step / 1e3) / 1e9 if bytes_per_step else None
     roof_bound, roof_unit, peak = "hbm", "GB/s", hbm_peak
-    if args.workload == "prefill":
+    if args.workload in ("prefill", "prefill_ep"):
         roof_bound, roof_unit = "tensor", "TFLOP/s"
         try:
             with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
                 peak = float(json.load(f)["bf16_tflops"])
         except Exception:
             peak, peak_kind = 1590.0, "fallback"
-        achieved = flops_per_step / (ms_step / 1e3) / 1e12
+        achieved = flops_per_step / world / (ms_step / 1e3) / 1e12   # per GPU
 
     # ---------------- e2e: pinned host input -> graph -> host read of the result, every step
     e2e = None
@@ -367,22 +388,27 @@ def run_b200(args):
     traffic = committed_traffic(args.workload)
     line = {
         "metric": {"stack_decode": "moe_stack_decode_tok_per_s", "layer_decode": "moe_layer_decode_tok_per_s",
-                   "prefill": "moe_prefill_tok_per_s"}[args.workload],
+                   "prefill": "moe_prefill_tok_per_s", "prefill_ep": "moe_prefill_ep_tok_per_s"}[args.workload],
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Q4_K, config-0 field law; random-init weights)",
         "config": {"workload": {"stack_decode": "config4_stack_decode_b%d" % T,
                                 "layer_decode": "config0_layer_decode_b%d" % T,
-                                "prefill": "config3_prefill_t%d" % T}[args.workload],
-                   "layers": nl, "batch": T, "seed": args.seed, "parallelism": "replicas%d" % world,
+                                "prefill": "config3_prefill_t%d" % T,
+                                "prefill_ep": "config3_prefill_ep_t%d" % (T * world)}[args.workload],
+                   "layers": nl, "batch": T, "seed": args.seed,
+                   "parallelism": ("ep%d" % world) if args.workload == "prefill_ep" else "replicas%d" % world,
                    "l2": "inputs larger than L2: distinct token per step, %.0f MB of Q4_K streamed per step"
                          % ((bytes_per_step or 0) / 1e6)},
         "roofline": {"bound": roof_bound, "achieved": achieved, "peak": peak, "unit": roof_unit,
                      "frac": (achieved / peak) if achieved else None,
                      "traffic": traffic.get("dram_bytes_per_step") if traffic else None,
                      "peak_kind": peak_kind,
-                     "kernel": "one graph replay = %d kernels (router/shared K1, routed gate_up K2, down+combine K3 "
-                               "per layer)" % launches_per_step},
+                     "kernel": ("one graph replay = %d kernels (router/shared K1, routed gate_up K2, down+combine K3 "
+                                "per layer)" % launches_per_step) if args.workload in ("stack_decode", "layer_decode")
+                               else ("one step = %d kernels per layer (prep, router GEMM, route, count, plan, fill, "
+                                     "tcgen05 gate_up GEMM, tcgen05 down GEMM, combine); achieved = expert FLOPs / "
+                                     "step time" % (launches_per_step // max(nl, 1)))},
         "gpu_launches": launches_per_step * K,
         "clocks": sampler.result(),
         "e2e": e2e,

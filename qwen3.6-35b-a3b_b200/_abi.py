@@ -11,7 +11,7 @@ import ctypes
 import os
 
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(PKG_DIR, "libb200moe.so")
+LIB_PATH = os.environ.get("B200MOE_LIB") or os.path.join(PKG_DIR, "libb200moe.so")
 
 OK, EINVAL, ECUDA, ESIZE = 0, 1, 2, 3
 F32, BF16 = 0, 1

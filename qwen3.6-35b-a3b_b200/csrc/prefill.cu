@@ -347,16 +347,53 @@ __global__ void __launch_bounds__(1024) k_fill(int T, int with_shared, const int
 }
 
 // ------------------------------------------------------------------------- grouped GEMM
+// Block of 15 warps, each with one job:
+//   warps 0-3    epilogue: TMEM lanes 32w..32w+31 -> s (gate_up) or y / ysh (down)
+//   warps 4-11   dequant: raw Q4_K slab (shared memory) -> fp16 A tile of the K-slab
+//   warp 12      TMEM allocation; lane 0 issues tcgen05.mma and the commits
+//   warps 13-14  B loaders: the tile's token rows (x16 gathered through the assignment list,
+//                or the contiguous s rows) -> B ring by cp.async, completion signalled with
+//                cp.async.mbarrier.arrive.noinc
+// One iteration = one K-slab of 64 of one tile; every role walks the same (tile, slab)
+// sequence: tile = blockIdx.x + j * gridDim.x, slab = 0 .. kKS-1.
+//
+// Three rings, each with full/empty mbarriers (empties are committed by the MMA thread):
+//   A ring   kAStages x kA x 16 KB     filled by the dequant warps (8 warp arrivals)
+//   B ring   kBStages x 32 KB          filled by the loaders (64 asynchronous arrivals)
+//   raw ring kRStages x 256 x 48 B     private per dequant thread: its row's 16-byte block
+//            header and the slab's 32 quant bytes, prefetched kRStages-1 slabs ahead with
+//            cp.async (only the issuing thread reads them: no cross-thread wait)
+// The down GEMM double-buffers its 256-column accumulator so the epilogue of one tile
+// overlaps the next tile's main loop; gate_up uses all 512 columns for one tile.
+constexpr int kEpiWarps = 4, kDqWarps = 8, kLdWarps = 2;
+constexpr int kDqThreads = 32 * kDqWarps;
+constexpr int kLdThreads = 32 * kLdWarps;
+constexpr int kMmaWarp = kEpiWarps + kDqWarps;  // 12
+constexpr int kLdWarp0 = kMmaWarp + 1;          // 13
+constexpr int kGemmThreads = 32 * (kLdWarp0 + kLdWarps);  // 480
+constexpr int kRawSlab = 48;                    // header 16 B + one slab's quants 32 B
+
 template <int kMode>
 struct GemmCfg {
-  static constexpr int kA = kMode == 1 ? 2 : 1;           // A tiles per stage
-  static constexpr int kKS = kMode == 1 ? kH / 64 : kI / 64;  // K stages of 64
-  static constexpr int kStages = kMode == 1 ? 3 : 4;
-  static constexpr int kATile = 128 * 128;                  // 128 rows x 128 B
-  static constexpr int kBTile = kChunk * 128;               // 256 rows x 128 B
-  static constexpr int kStage = kA * kATile + kBTile;
-  static constexpr uint32_t kTmemCols = kMode == 1 ? 512 : 256;
-  static constexpr size_t kSmem = (size_t)kStages * kStage + 1024 + 256;
+  static constexpr int kA = kMode == 1 ? 2 : 1;                // A tiles per stage (gate+up / down)
+  static constexpr int kARows = 128 * kA;                       // weight rows per tile
+  static constexpr int kTpr = kDqThreads / kARows;              // dequant threads per row (1 or 2)
+  static constexpr int kKS = (kMode == 1 ? kH : kI) / 64;       // K-slabs of 64 per tile
+  static constexpr int kAStages = kMode == 1 ? 2 : 3;
+  static constexpr int kBStages = 3;
+  static constexpr int kRStages = 4;
+  static constexpr int kATile = 128 * 128;                      // 128 rows x 128 B
+  static constexpr int kBTile = kChunk * 128;                   // 256 rows x 128 B
+  static constexpr int kRawStage = kDqThreads * kRawSlab;
+  static constexpr int kNBuf = kMode == 1 ? 1 : 2;              // TMEM accumulator buffers
+  static constexpr uint32_t kAccCols = kMode == 1 ? 512 : 256;  // columns per buffer
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr int kOffB = kAStages * kA * kATile;
+  static constexpr int kOffRaw = kOffB + kBStages * kBTile;
+  static constexpr int kOffMeta = kOffRaw + kRStages * kRawStage;       // epilogue column metadata
+  static constexpr int kOffTok = kOffMeta + kEpiWarps * kChunk * 8;      // loader token indices
+  static constexpr int kOffBar = kOffTok + kChunk * 4;
+  static constexpr size_t kSmem = (size_t)kOffBar + 512 + 1024;         // + barriers, + alignment
 };
 
 struct GemmParams {
@@ -376,66 +413,91 @@ struct GemmParams {
   int32_t *err;
 };
 
-// Dequantise 64 consecutive K of one Q4_K row (block kb, sub-blocks 2g / 2g+1) into one
-// 128-row x 64-K fp16 tile, row `row`: 8 chunks of 8 halves (low nibbles -> chunks 0..3,
-// high nibbles -> chunks 4..7).
-__device__ __forceinline__ void dequant_slab(const uint8_t *blk, int g, uint8_t *tile, int row) {
-  const uint4 h = __ldg(reinterpret_cast<const uint4 *>(blk));
-  const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + 32 * g));
-  const uint4 q1 = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + 32 * g));
+// Half (h = 0: low nibbles, sub-block 2g; h = 1: high nibbles, sub-block 2g+1) of K-slab g of
+// one Q4_K block row -> 4 chunks (16 B each) of the A tile row.
+__device__ __forceinline__ void dequant_half(const uint8_t *raw, int g, int h, uint8_t *tile, int row) {
+  const uint4 hd = *reinterpret_cast<const uint4 *>(raw);
+  const uint4 q0 = *reinterpret_cast<const uint4 *>(raw + 16);
+  const uint4 q1 = *reinterpret_cast<const uint4 *>(raw + 32);
   float s0, m0, s1, m1;
-  q4k_scales(h, 2 * g, s0, m0, s1, m1);
-  const __half2 S0 = __float2half2_rn(s0), M0 = __float2half2_rn(-m0);
-  const __half2 S1 = __float2half2_rn(s1), M1 = __float2half2_rn(-m1);
+  q4k_scales(hd, 2 * g, s0, m0, s1, m1);
+  const __half2 S = __float2half2_rn(h ? s1 : s0), M = __float2half2_rn(h ? -m1 : -m0);
   const __half2 k1024 = __float2half2_rn(1024.0f);
   const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-  uint8_t *rbase = tile + (row >> 3) * 1024 + (row & 7) * 16;
+  uint8_t *rbase = tile + (row >> 3) * 1024 + (row & 7) * 16 + h * 512;
 #pragma unroll
   for (int kc = 0; kc < 4; ++kc) {
-    uint32_t lo[4], hi[4];
+    uint32_t v[4];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       const uint32_t w = qw[2 * kc + (p >> 1)];
       const uint32_t pr = __byte_perm(w, 0u, (p & 1) ? 0x4342u : 0x4140u);  // [b, 0, b', 0]
-      const uint32_t l = (pr & 0x000F000Fu) | 0x64006400u;
-      const uint32_t u = ((pr >> 4) & 0x000F000Fu) | 0x64006400u;
-      __half2 ql = __hsub2(*reinterpret_cast<const __half2 *>(&l), k1024);
-      __half2 qh = __hsub2(*reinterpret_cast<const __half2 *>(&u), k1024);
-      ql = __hfma2(ql, S0, M0);
-      qh = __hfma2(qh, S1, M1);
-      lo[p] = *reinterpret_cast<uint32_t *>(&ql);
-      hi[p] = *reinterpret_cast<uint32_t *>(&qh);
+      const uint32_t q = (h ? ((pr >> 4) & 0x000F000Fu) : (pr & 0x000F000Fu)) | 0x64006400u;  // 1024 + q
+      __half2 x = __hsub2(*reinterpret_cast<const __half2 *>(&q), k1024);
+      x = __hfma2(x, S, M);
+      v[p] = *reinterpret_cast<uint32_t *>(&x);
     }
-    *reinterpret_cast<uint4 *>(rbase + kc * 128) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    *reinterpret_cast<uint4 *>(rbase + (kc + 4) * 128) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4 *>(rbase + kc * 128) = make_uint4(v[0], v[1], v[2], v[3]);
   }
 }
 
-// Persistent, warp-specialised: warps 0-3 epilogue (TMEM lanes 32w..), warps 4-7 producers,
-// warp 8 TMEM allocation + MMA issue (lane 0).
+// Base of weight row `row` (0 .. kARows-1) of tile (e, wt).
 template <int kMode>
-__global__ void __launch_bounds__(288, 1) k_gemm(GemmParams P) {
+__device__ __forceinline__ const uint8_t *tile_row(const GemmParams &P, int e, int wt, int row) {
+  if (kMode == 1) {
+    const bool up = row >= 128;
+    const uint8_t *base = e < kE ? (up ? P.wa1 : P.wa0) + (size_t)e * P.stride : (up ? P.sh1 : P.sh0);
+    return base + (size_t)(wt * 128 + (row & 127)) * kRowUp;
+  }
+  const uint8_t *base = e < kE ? P.wa0 + (size_t)e * P.stride : P.sh0;
+  return base + (size_t)(wt * 128 + row) * kRowDown;
+}
+
+// Raw bytes of K-slab ks of one weight row -> 48-byte slot: block header, then the slab's quants.
+__device__ __forceinline__ void issue_raw_slab(const uint8_t *rowp, int ks, uint8_t *dst) {
+  const uint8_t *blk = rowp + (ks >> 2) * kQB;
+  cp_async16(dst, blk, 16u);
+  cp_async16(dst + 16, blk + 16 + 32 * (ks & 3), 16u);
+  cp_async16(dst + 32, blk + 32 + 32 * (ks & 3), 16u);
+}
+
+template <int kMode>
+__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(GemmParams P) {
   using C = GemmCfg<kMode>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t *full = (uint64_t *)(smem + C::kStages * C::kStage);
-  uint64_t *empty = full + C::kStages;
-  uint64_t *acc_full = empty + C::kStages;
-  uint64_t *acc_empty = acc_full + 1;
-  uint64_t *drain = acc_empty + 1;
+  uint8_t *a_ring = smem;
+  uint8_t *b_ring = smem + C::kOffB;
+  uint8_t *raw_ring = smem + C::kOffRaw;
+  int *col_pl = (int *)(smem + C::kOffMeta);                // [4][kChunk] per epilogue warp
+  float *col_w = (float *)(col_pl + kEpiWarps * kChunk);     // [4][kChunk] per epilogue warp
+  int *tok_s = (int *)(smem + C::kOffTok);                   // [kChunk] loader rows' token ids
+  uint64_t *a_full = (uint64_t *)(smem + C::kOffBar);
+  uint64_t *a_empty = a_full + C::kAStages;
+  uint64_t *b_full = a_empty + C::kAStages;
+  uint64_t *b_empty = b_full + C::kBStages;
+  uint64_t *acc_full = b_empty + C::kBStages;   // [kNBuf]
+  uint64_t *acc_empty = acc_full + C::kNBuf;    // [kNBuf]
+  uint64_t *drain = acc_empty + C::kNBuf;
   uint32_t *tmem_slot = (uint32_t *)(drain + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(full + s, 128);
-      mbar_init(empty + s, 1);
+    for (int s = 0; s < C::kAStages; ++s) {
+      mbar_init(a_full + s, kDqWarps);  // one arrival per dequant warp
+      mbar_init(a_empty + s, 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 128);
+    for (int s = 0; s < C::kBStages; ++s) {
+      mbar_init(b_full + s, kLdThreads);  // one asynchronous (cp.async) arrival per loader thread
+      mbar_init(b_empty + s, 1);
+    }
+    for (int b = 0; b < C::kNBuf; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, kEpiWarps);  // one arrival per epilogue warp
+    }
     mbar_init(drain, 1);
     mbar_fence_init();
   }
-  if (warp == 8) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
@@ -444,84 +506,120 @@ __global__ void __launch_bounds__(288, 1) k_gemm(GemmParams P) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int ntiles = __ldg(P.ntiles + (kMode - 1));
+  const int my_tiles = ntiles > (int)blockIdx.x ? (ntiles - (int)blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const uint32_t n_it = (uint32_t)my_tiles * C::kKS;
   bool ok = true;
 
-  if (warp >= 4 && warp < 8) {  // ------------------------------ producers
-    const int pt = threadIdx.x - 128;
-    uint32_t it = 0;
-    for (int ti = blockIdx.x; ti < ntiles && ok; ti += gridDim.x) {
-      const int4 tl = __ldg(P.tiles + ti);
-      const int e = tl.x, r0 = tl.y, n = tl.z, wt = tl.w;
-      const int npad = (n + 15) & ~15;
-      const uint8_t *arow0, *arow1 = nullptr;
-      if (kMode == 1) {
-        const size_t ro = (size_t)(wt * 128 + pt) * kRowUp;
-        arow0 = (e < kE ? P.wa0 + (size_t)e * P.stride : P.sh0) + ro;
-        arow1 = (e < kE ? P.wa1 + (size_t)e * P.stride : P.sh1) + ro;
-      } else {
-        arow0 = (e < kE ? P.wa0 + (size_t)e * P.stride : P.sh0) + (size_t)(wt * 128 + pt) * kRowDown;
-      }
-      for (int ks = 0; ks < C::kKS; ++ks, ++it) {
-        const int s = it % C::kStages;
-        const uint32_t round = it / C::kStages;
-        if (!mbar_wait(empty + s, (round & 1) ^ 1)) { ok = false; break; }
-        uint8_t *st = smem + s * C::kStage;
-        uint8_t *btile = st + C::kA * C::kATile;
-        // B: token rows (zero-filled past n)
-        const int kc0 = pt >> 5;
-        for (int r = pt & 31; r < npad; r += 32) {
-          const __half *src;
-          if (kMode == 1) {
-            const int pl = r < n ? __ldg(P.plist + r0 + r) : 0;
-            const int tok = e < kE ? (pl >> 3) : pl;
-            src = P.x16 + (size_t)tok * kH + ks * 64;
-          } else {
-            src = P.s16 + (size_t)(r0 + (r < n ? r : 0)) * kI + ks * 64;
-          }
-          const uint32_t nb = r < n ? 16u : 0u;
-          uint8_t *d = btile + (r >> 3) * 1024 + (r & 7) * 16;
-          cp_async16(d + kc0 * 128, src + kc0 * 8, nb);
-          cp_async16(d + (kc0 + 4) * 128, src + (kc0 + 4) * 8, nb);
-        }
-        // A: dequantised weight rows
-        const int kb = ks >> 2, g = ks & 3;
-        dequant_slab(arow0 + kb * kQB, g, st, pt);
-        if (kMode == 1) dequant_slab(arow1 + kb * kQB, g, st + C::kATile, pt);
-        cp_async_wait_all();
-        fence_proxy_async_smem();
-        mbar_arrive(full + s);
-      }
+  if (warp >= kEpiWarps && warp < kMmaWarp) {  // ----------------------------- dequant
+    const int pt = threadIdx.x - 32 * kEpiWarps;
+    const int row = pt / C::kTpr, half = pt % C::kTpr;  // kTpr == 1: this thread does both halves
+    uint8_t *myraw = raw_ring + pt * kRawSlab;
+    auto raw_src = [&](uint32_t j) -> const uint8_t * {  // row base for iteration j
+      const int4 tl = __ldg(P.tiles + blockIdx.x + (j / C::kKS) * gridDim.x);
+      return tile_row<kMode>(P, tl.x, tl.w, row);
+    };
+    // prologue: raw slabs of iterations 0 .. kRStages-2
+    for (uint32_t j = 0; j + 1 < (uint32_t)C::kRStages; ++j) {
+      if (j < n_it) issue_raw_slab(raw_src(j), j % C::kKS, myraw + (j % C::kRStages) * C::kRawStage);
+      cp_async_commit();
     }
-  } else if (warp == 8) {  // --------------------------------------- MMA issue
+    const uint8_t *rowp = nullptr;
+    for (uint32_t it = 0; it < n_it && ok; ++it) {
+      const int ks = it % C::kKS;
+      const int s = it % C::kAStages;
+      const uint32_t j = it + C::kRStages - 1;  // slab to prefetch this iteration
+      if (j < n_it) {
+        if (j % C::kKS == 0 || rowp == nullptr) rowp = raw_src(j);
+        issue_raw_slab(rowp, j % C::kKS, myraw + (j % C::kRStages) * C::kRawStage);
+      }
+      cp_async_commit();
+      cp_async_wait_group<C::kRStages - 1>();  // iteration it's slab has landed
+      // warp-uniform outcome: a lane that timed out never leaves its warp behind in __syncwarp
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(a_empty + s, ((it / C::kAStages) & 1) ^ 1))) { ok = false; break; }
+      uint8_t *at = a_ring + s * (C::kA * C::kATile) + (row >> 7) * C::kATile;
+      const uint8_t *rs = myraw + (it % C::kRStages) * C::kRawStage;
+      if (C::kTpr == 1) {
+        dequant_half(rs, ks & 3, 0, at, row & 127);
+        dequant_half(rs, ks & 3, 1, at, row & 127);
+      } else {
+        dequant_half(rs, ks & 3, half, at, row & 127);
+      }
+      fence_proxy_async_smem();  // this thread's generic smem writes -> async proxy
+      __syncwarp();
+      if (lane == 0) mbar_arrive(a_full + s);
+    }
+    cp_async_wait_all();
+  } else if (warp >= kLdWarp0) {  // ------------------------------------------ B loaders
+    const int lw = warp - kLdWarp0;
+    const int kc = lane & 7, rsub = lane >> 3;  // 16-byte chunk of the slab row; row within 4
+    int *tok = tok_s + lw * (kChunk / kLdWarps);  // this warp's rows: 128 lw .. 128 lw + 127
+    int4 tl = make_int4(0, 0, 0, 0);
+    for (uint32_t it = 0; it < n_it && ok; ++it) {
+      const int ks = it % C::kKS;
+      const int s = it % C::kBStages;
+      if (ks == 0) {  // new tile: this warp's token rows
+        tl = __ldg(P.tiles + blockIdx.x + (it / C::kKS) * gridDim.x);
+        __syncwarp();
+        for (int r = lane; r < kChunk / kLdWarps; r += 32) {
+          const int rr = lw * (kChunk / kLdWarps) + r;
+          int t = 0;
+          if (rr < tl.z) {
+            if (kMode == 1) {
+              const int pl = __ldg(P.plist + tl.y + rr);
+              t = tl.x < kE ? (pl >> 3) : pl;
+            } else {
+              t = tl.y + rr;
+            }
+          }
+          tok[r] = t;
+        }
+        __syncwarp();
+      }
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(b_empty + s, ((it / C::kBStages) & 1) ^ 1))) { ok = false; break; }
+      uint8_t *bt = b_ring + s * C::kBTile;
+      const int nrow = min(tl.z - lw * (kChunk / kLdWarps), kChunk / kLdWarps);
+      for (int r = rsub; r < nrow; r += 4) {
+        const int rr = lw * (kChunk / kLdWarps) + r;
+        const __half *src = kMode == 1 ? P.x16 + (size_t)tok[r] * kH + ks * 64 + kc * 8
+                                       : P.s16 + (size_t)tok[r] * kI + ks * 64 + kc * 8;
+        cp_async16(bt + (rr >> 3) * 1024 + kc * 128 + (rr & 7) * 16, src, 16u);
+      }
+      cp_async_mbar_arrive_noinc(b_full + s);
+    }
+    cp_async_wait_all();
+  } else if (warp == kMmaWarp) {  // -------------------------------------------- MMA issue
     if (lane == 0) {
       uint32_t it = 0, tcount = 0;
       for (int ti = blockIdx.x; ti < ntiles && ok; ti += gridDim.x, ++tcount) {
         const int4 tl = __ldg(P.tiles + ti);
         const int npad = (tl.z + 15) & ~15;
         const uint32_t idesc = umma_idesc_f16((uint32_t)npad);
-        if (tcount > 0 && !mbar_wait(acc_empty, (tcount - 1) & 1)) { ok = false; break; }
+        const uint32_t buf = tcount % C::kNBuf, use = tcount / C::kNBuf;
+        if (use > 0 && !mbar_wait(acc_empty + buf, (use - 1) & 1)) { ok = false; break; }
         tc_fence_after();
+        const uint32_t dacc = tmem + buf * C::kAccCols;
         for (int ks = 0; ks < C::kKS; ++ks, ++it) {
-          const int s = it % C::kStages;
-          const uint32_t round = it / C::kStages;
-          if (!mbar_wait(full + s, round & 1)) { ok = false; break; }
+          const int sa = it % C::kAStages, sb = it % C::kBStages;
+          if (!mbar_wait(a_full + sa, (it / C::kAStages) & 1)) { ok = false; break; }
+          if (!mbar_wait(b_full + sb, (it / C::kBStages) & 1)) { ok = false; break; }
+          fence_proxy_async_smem();  // cp.async (generic proxy) B rows -> tensor-core reads
           tc_fence_after();
-          const uint32_t st = smem_u32(smem + s * C::kStage);
-          const uint32_t bt = st + C::kA * C::kATile;
+          const uint32_t at = smem_u32(a_ring + sa * (C::kA * C::kATile));
+          const uint32_t bt = smem_u32(b_ring + sb * C::kBTile);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t acc = (ks | kk) != 0;
             const uint64_t bd = umma_desc(bt + 256 * kk);
-            umma_f16(tmem, umma_desc(st + 256 * kk), bd, idesc, acc);
-            if (kMode == 1) umma_f16(tmem + 256, umma_desc(st + C::kATile + 256 * kk), bd, idesc, acc);
+            umma_f16(dacc, umma_desc(at + 256 * kk), bd, idesc, acc);
+            if (kMode == 1) umma_f16(dacc + 256, umma_desc(at + C::kATile + 256 * kk), bd, idesc, acc);
           }
-          umma_commit(empty + s);
+          umma_commit(a_empty + sa);
+          umma_commit(b_empty + sb);
         }
         if (!ok) break;
-        umma_commit(acc_full);
+        umma_commit(acc_full + buf);
       }
-      // every MMA this thread issued has completed before TMEM can be released
-      umma_commit(drain);
+      umma_commit(drain);  // every MMA this thread issued has completed before TMEM is released
       if (!mbar_wait(drain, 0)) ok = false;
     }
     __syncwarp();
@@ -533,9 +631,20 @@ __global__ void __launch_bounds__(288, 1) k_gemm(GemmParams P) {
       const int4 tl = __ldg(P.tiles + ti);
       const int e = tl.x, r0 = tl.y, n = tl.z, wt = tl.w;
       const int npad = (n + 15) & ~15;
-      if (!mbar_wait(acc_full, tcount & 1)) { ok = false; break; }
+      const uint32_t buf = tcount % C::kNBuf, use = tcount / C::kNBuf;
+      int *wpl = col_pl + warp * kChunk;
+      float *ww = col_w + warp * kChunk;
+      if (kMode == 2) {  // this warp's copy of the tile's column metadata, loaded while the MMAs run
+        for (int c = lane; c < n; c += 32) {
+          const int pl = __ldg(P.plist + r0 + c);
+          wpl[c] = pl;
+          ww[c] = e < kE ? bf16f(__ldg(P.wb + pl)) : 1.0f;
+        }
+        __syncwarp();
+      }
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(acc_full + buf, use & 1))) { ok = false; break; }
       tc_fence_after();
-      const uint32_t lane_addr = tmem + ((uint32_t)(32 * warp) << 16);
+      const uint32_t lane_addr = tmem + buf * C::kAccCols + ((uint32_t)(32 * warp) << 16);
       for (int c0 = 0; c0 < npad; c0 += 16) {
         float a[16];
         tmem_ld16(lane_addr + c0, a);
@@ -544,28 +653,33 @@ __global__ void __launch_bounds__(288, 1) k_gemm(GemmParams P) {
           tmem_ld16(lane_addr + 256 + c0, u);
           tmem_wait_ld();
           const int j = wt * 128 + row;
+          __half hv[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {  // silu(g) * u, stored as s * 2^-10 (exact scaling)
+            const float sil = __fdividef(a[i], 1.0f + __expf(-a[i]));
+            const float sv = sil * u[i] * kSScale;
+            if (c0 + i < n && !(fabsf(sv) <= 65504.0f)) range_bad = true;
+            hv[i] = __float2half_rn(sv);
+          }
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            if (c0 + i < n) {  // stored as s * 2^-10 (exact scaling): fp16 headroom up to |s| < 6.7e7
-              const float sv = __fmul_rn(__fmul_rn(silu_f(a[i]), u[i]), kSScale);
-              if (!(fabsf(sv) <= 65504.0f)) range_bad = true;
-              P.s16[(size_t)(r0 + c0 + i) * kI + j] = __float2half_rn(sv);
-            }
+            if (c0 + i < n) P.s16[(size_t)(r0 + c0 + i) * kI + j] = hv[i];
         } else {
           tmem_wait_ld();
           const int h = wt * 128 + row;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            if (c0 + i >= n) continue;
-            const int pl = __ldg(P.plist + r0 + c0 + i);
+            if (c0 + i >= n) break;
             const float o = __fmul_rn(a[i], 1.0f / kSScale);  // undo the s storage scale (exact)
-            if (e < kE) P.y[(size_t)pl * kH + h] = __fmul_rn(o, bf16f(__ldg(P.wb + pl)));
+            const int pl = wpl[c0 + i];
+            if (e < kE) P.y[(size_t)pl * kH + h] = __fmul_rn(o, ww[c0 + i]);
             else P.ysh[(size_t)pl * kH + h] = o;
           }
         }
       }
       tc_fence_before();
-      mbar_arrive(acc_empty);
+      __syncwarp();  // also: this warp's metadata is read before the next tile overwrites it
+      if (lane == 0) mbar_arrive(acc_empty + buf);
     }
     if (range_bad) atomicOr(P.err, kErrRange);
   }
@@ -573,7 +687,7 @@ __global__ void __launch_bounds__(288, 1) k_gemm(GemmParams P) {
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 8) tmem_dealloc(tmem, C::kTmemCols);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, C::kTmemCols);
 }
 
 // ------------------------------------------------------------------------- k_combine
@@ -678,7 +792,7 @@ int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *
   g.y = w.y;
   g.ysh = w.ysh;
   g.err = w.err;
-  k_gemm<1><<<g_num_sms, 288, GemmCfg<1>::kSmem, s>>>(g);
+  k_gemm<1><<<g_num_sms, kGemmThreads, GemmCfg<1>::kSmem, s>>>(g);
   B2_CUDA(cudaGetLastError());
   g.wa0 = (const uint8_t *)L->down;
   g.wa1 = nullptr;
@@ -686,7 +800,7 @@ int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *
   g.sh0 = (const uint8_t *)L->sh_down;
   g.sh1 = nullptr;
   g.tiles = w.tiles2;
-  k_gemm<2><<<g_num_sms, 288, GemmCfg<2>::kSmem, s>>>(g);
+  k_gemm<2><<<g_num_sms, kGemmThreads, GemmCfg<2>::kSmem, s>>>(g);
   B2_CUDA(cudaGetLastError());
   const int64_t nthreads = (int64_t)T * (kH / 4);
   k_combine<<<(unsigned)((nthreads + 255) / 256), 256, 0, s>>>(T, w.y, w.ysh, sg, ids, w.order, e_lo, e_hi, out,

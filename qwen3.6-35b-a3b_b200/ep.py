@@ -61,8 +61,9 @@ class ExpertParallelMoE:
 
     def __init__(self, layer, group=None, route_fn=None, experts_fn=None, device=None):
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        grouped = dist.is_available() and dist.is_initialized()
+        self.rank = dist.get_rank(group) if grouped else 0
+        self.world = dist.get_world_size(group) if grouped else 1
         if E % self.world:
             raise ValueError("256 experts do not split over %d ranks" % self.world)
         self.per = E // self.world
@@ -95,10 +96,13 @@ class ExpertParallelMoE:
             send_tok.append(tok)
             send_ids.append(torch.where(m[tok], ids[tok], torch.full_like(ids[tok], -1)))
         send_counts = [int(t.numel()) for t in send_tok]
-        cnt = torch.tensor(send_counts, dtype=torch.int64, device=self.device)
-        rcnt = torch.empty_like(cnt)
-        dist.all_to_all_single(rcnt, cnt, group=self.group)
-        recv_counts = [int(c) for c in rcnt.tolist()]
+        if W > 1:
+            cnt = torch.tensor(send_counts, dtype=torch.int64, device=self.device)
+            rcnt = torch.empty_like(cnt)
+            dist.all_to_all_single(rcnt, cnt, group=self.group)
+            recv_counts = [int(c) for c in rcnt.tolist()]
+        else:
+            recv_counts = list(send_counts)
         R = sum(recv_counts)
         x_send = torch.cat([x16[t] for t in send_tok]) if T else x16[:0]
         i_send = torch.cat(send_ids) if T else ids[:0]
@@ -108,12 +112,18 @@ class ExpertParallelMoE:
         w_recv = torch.empty((R, TOPK), dtype=wb.dtype, device=self.device)
         for dst, src in ((x_recv, x_send), (i_recv, i_send), (w_recv, w_send)):
             # rows travel as raw bytes (every backend moves uint8; not every one moves fp16)
-            dist.all_to_all_single(dst.view(torch.uint8), src.contiguous().view(torch.uint8), recv_counts,
-                                   send_counts, group=self.group)
+            if W > 1:
+                dist.all_to_all_single(dst.view(torch.uint8), src.contiguous().view(torch.uint8), recv_counts,
+                                       send_counts, group=self.group)
+            else:
+                dst.copy_(src)
         partial = torch.zeros((R, H), dtype=torch.float32, device=self.device)
         self.experts_fn(x_recv, i_recv, w_recv, self.e_lo, self.e_hi, None, partial)
-        back = torch.empty((sum(send_counts), H), dtype=torch.float32, device=self.device)
-        dist.all_to_all_single(back, partial, send_counts, recv_counts, group=self.group)
+        if W > 1:
+            back = torch.empty((sum(send_counts), H), dtype=torch.float32, device=self.device)
+            dist.all_to_all_single(back, partial, send_counts, recv_counts, group=self.group)
+        else:
+            back = partial
         acc = torch.zeros((T, H), dtype=torch.float32, device=self.device)
         off = 0
         for r in range(W):            # ascending rank = ascending expert range; indices unique per r
