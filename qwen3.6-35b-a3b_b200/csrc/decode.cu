@@ -20,6 +20,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "mega.cuh"
 #include "route.cuh"
 
 using namespace b2;
@@ -310,11 +311,12 @@ struct DecodeWS {
   uint16_t *logits;
   float *s;
   float *sg;
+  void *xchg;  // cross-CTA exchange area of the persistent single-token kernel
 };
 
 constexpr size_t decode_ws_bytes(int T) {
   return align256((size_t)T * kH * 4) + align256((size_t)T * kE * 2) + align256((size_t)T * 9 * kI * 4) +
-         align256((size_t)T * 4);
+         align256((size_t)T * 4) + align256(b2mega::kScratchBytes);
 }
 
 DecodeWS carve(void *ws, int T) {
@@ -327,6 +329,8 @@ DecodeWS carve(void *ws, int T) {
   w.s = (float *)p;
   p += align256((size_t)T * 9 * kI * 4);
   w.sg = (float *)p;
+  p += align256((size_t)T * 4);
+  w.xchg = p;
   return w;
 }
 
@@ -398,6 +402,24 @@ int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const 
 }
 
 constexpr int kMaxT = 1 << 16;
+
+// One token through n_layers layers with the persistent kernel (persist.cu): x mode (one
+// layer, out = block(x)) when resid is NULL, else resid mode. Same bits as run_layer.
+int run_persistent(const void *x, int x_dtype, float *resid, float eps, int n_layers, const b200moe_layer *layers,
+                   float *out, int32_t *ids_out, uint16_t *w_out, const DecodeWS &w, cudaStream_t s) {
+  b2mega::Args a = {};
+  a.n_layers = n_layers;
+  a.eps = eps;
+  a.x = x;
+  a.x_dtype = x_dtype;
+  a.resid = resid;
+  a.out = out;
+  a.ids_out = ids_out;
+  a.w_out = w_out;
+  a.scratch = w.xchg;
+  a.layers = layers;
+  return b2mega::launch(a, s);
+}
 
 // ------------------------------------------------------------------------- no-allocation entry
 // Scratch for b200moe_moe_decode_noalloc: a fixed, file-scope device array sized for
@@ -471,6 +493,7 @@ int b200moe_moe_decode(const void *x, int x_dtype, int T, const b200moe_layer *l
   if (rc) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   const DecodeWS w = carve(ws, T);
+  if (T == 1 && b2mega::usable()) return run_persistent(x, x_dtype, nullptr, 0.f, 1, layer, out, ids_out, w_out, w, s);
   return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, w, s, true);
 }
 
@@ -490,6 +513,9 @@ int b200moe_moe_decode_noalloc(const void *x, int x_dtype, int T, const b200moe_
   void *scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc) return rc;
+  if (T == 1 && b2mega::usable())
+    return run_persistent(x, x_dtype, nullptr, 0.f, 1, layer, out, ids_out, w_out, carve(scratch, T),
+                          (cudaStream_t)stream);
   return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, carve(scratch, T), (cudaStream_t)stream,
                    true);
 }
@@ -512,6 +538,8 @@ int b200moe_stack_decode(float *resid, int T, const b200moe_layer *layers, int n
   }
   cudaStream_t s = (cudaStream_t)stream;
   const DecodeWS w = carve(ws, T);
+  if (T == 1 && b2mega::usable())
+    return run_persistent(nullptr, B200MOE_F32, resid, eps, n_layers, layers, nullptr, ids_out, nullptr, w, s);
   for (int l = 0; l < n_layers; ++l) {
     int rc = run_layer(nullptr, B200MOE_F32, resid, eps, T, &layers[l], nullptr,
                        ids_out ? ids_out + (size_t)l * T * kK : nullptr, nullptr, w, s, l == 0);

@@ -1,0 +1,45 @@
+// mega.cuh -- host interface of the persistent single-token decode kernel (persist.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "b200moe.h"
+
+namespace b2mega {
+
+constexpr int kMaxCtas = 256;  // grid cap (one CTA per SM)
+// Cross-CTA exchange area. Every value one CTA hands to the others travels as one 64-bit word
+// (phase tag << 32 | value bits, single-copy atomic), in per-CTA line-aligned slots -- no two
+// CTAs ever store into the same 128-byte line:
+//   [0, 128)                 abort word, status word
+//   logits [c][16] u64       CTA c's logit pair (or the shared-expert gate)
+//   s      [c][32] u64       CTA c's activations s
+//   deltas [c][16] u64       CTA c's residual deltas
+// Everything is cleared before each launch (tags are launch-local).
+constexpr size_t kXLogits = 128;
+constexpr size_t kXS = kXLogits + (size_t)kMaxCtas * 128;
+constexpr size_t kXDelta = kXS + (size_t)kMaxCtas * 256;
+constexpr size_t kScratchBytes = kXDelta + (size_t)kMaxCtas * 128;
+constexpr size_t kScratchClear = kScratchBytes;
+
+struct Args {
+  int n_layers;
+  float eps;
+  const void *x;      // x mode (resid == NULL, one layer): the block input, one token
+  int x_dtype;
+  float *resid;       // resid mode: x_l = rmsnorm(resid), resid += block_l(x_l)
+  float *out;         // x mode: out = block(x)
+  int32_t *ids_out;   // [n_layers][8] or NULL
+  uint16_t *w_out;    // [n_layers][8] bf16 routing weights or NULL
+  void *scratch;      // kScratchBytes, 16-byte aligned; cleared by launch() on the stream
+  const b200moe_layer *layers;  // host array of n_layers
+};
+
+// 1 if the current device can run the persistent kernel (enough SMs, one resident CTA per SM).
+bool usable();
+
+// Enqueue the flag reset and the persistent kernel(s) on `stream`. Returns a B200MOE_* code.
+int launch(const Args &a, cudaStream_t stream);
+
+}  // namespace b2mega

@@ -107,4 +107,89 @@ __device__ __forceinline__ void route_warp(const uint16_t *logits_t, Route *rr) 
   __syncwarp();
 }
 
+
+// ---------------------------------------------------------------- split form (persistent decode)
+// The same R2..R5 as route_warp, in two steps so a caller can act on the winners' ids before
+// the weights exist. Lane L passes logits 8L..8L+7 as four bf16 pairs.
+//   route_select: R3 -> lane r (< 8) gets rank r's key (id = 255 - (key & 0xFF)).
+//   route_finish: R2, R4, R5 and the combine order; every value equals route_warp's (the
+//                 winner's exp is recomputed from its bf16 logit, an identical input).
+__device__ __forceinline__ void key_cas(uint32_t &a, uint32_t &b) {  // a >= b afterwards
+  const uint32_t hi = max(a, b), lo = min(a, b);
+  a = hi;
+  b = lo;
+}
+
+__device__ __forceinline__ uint32_t route_select(const uint32_t (&rw)[4]) {
+  const int lane = threadIdx.x & 31;
+  uint32_t k[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    k[2 * i] = (bf16_mono(rw[i]) << 8) | (uint32_t)(255 - (8 * lane + 2 * i));
+    k[2 * i + 1] = (bf16_mono(rw[i] >> 16) << 8) | (uint32_t)(255 - (8 * lane + 2 * i + 1));
+  }
+  // the lane's 8 keys in descending order (19-comparator network); keys are unique
+  key_cas(k[0], k[2]); key_cas(k[1], k[3]); key_cas(k[4], k[6]); key_cas(k[5], k[7]);
+  key_cas(k[0], k[4]); key_cas(k[1], k[5]); key_cas(k[2], k[6]); key_cas(k[3], k[7]);
+  key_cas(k[0], k[1]); key_cas(k[2], k[3]); key_cas(k[4], k[5]); key_cas(k[6], k[7]);
+  key_cas(k[2], k[4]); key_cas(k[3], k[5]);
+  key_cas(k[1], k[4]); key_cas(k[3], k[6]);
+  key_cas(k[1], k[2]); key_cas(k[3], k[4]); key_cas(k[5], k[6]);
+  uint32_t mine = 0;
+#pragma unroll
+  for (int r = 0; r < kK; ++r) {
+    const uint32_t w = __reduce_max_sync(0xFFFFFFFFu, k[0]);
+    if (k[0] == w) {  // the owner retires its best key
+#pragma unroll
+      for (int i = 0; i < 7; ++i) k[i] = k[i + 1];
+      k[7] = 0u;
+    }
+    if (lane == r) mine = w;
+  }
+  return mine;
+}
+
+// bf16 bits back from bf16_mono (the folded -0 comes back as +0: same value).
+__device__ __forceinline__ uint32_t bf16_unmono(uint32_t m) { return (m & 0x8000u) ? (m & 0x7FFFu) : (~m & 0xFFFFu); }
+
+__device__ __forceinline__ void route_finish(const uint32_t (&rw)[4], uint32_t mine, Route *rr) {
+  const int lane = threadIdx.x & 31;
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = bf16f(rw[i]);
+    v[2 * i + 1] = bf16f(rw[i] >> 16);
+  }
+  float m = v[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) m = fmaxf(m, v[i]);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  float s = b2_expf(__fsub_rn(v[0], m));
+#pragma unroll
+  for (int i = 1; i < 8; ++i) s = __fadd_rn(s, b2_expf(__fsub_rn(v[i], m)));
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, o));
+  const int my_id = 255 - (int)(mine & 0xFFu);
+  const float my_e = b2_expf(__fsub_rn(bf16f(bf16_unmono(mine >> 8)), m));
+  const float pk = __fdiv_rn(my_e, s);
+  float s8 = 0.0f;
+#pragma unroll
+  for (int r = 0; r < kK; ++r) s8 = __fadd_rn(s8, __shfl_sync(0xFFFFFFFFu, pk, r));
+  const float wk = (s8 == 0.0f) ? 0.0f : __fdiv_rn(pk, s8);
+  int rank = 0;
+#pragma unroll
+  for (int r = 0; r < kK; ++r) {
+    const int other = __shfl_sync(0xFFFFFFFFu, my_id, r);
+    rank += (other < my_id) ? 1 : 0;
+  }
+  if (lane < kK) {
+    rr->ids[lane] = my_id;
+    rr->wf[lane] = wk;
+    rr->wb[lane] = f2bf(wk);
+    rr->order[rank] = lane;
+  }
+  __syncwarp();
+}
+
 }  // namespace b2
