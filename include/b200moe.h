@@ -115,6 +115,14 @@ int b200moe_moe_decode(const void *x, int x_dtype, int T, const b200moe_layer *l
 int b200moe_moe_decode_noalloc(const void *x, int x_dtype, int T, const b200moe_layer *layer,
                                float *out, int32_t *ids_out, uint16_t *w_out, void *stream);
 
+/* Which single-token decode path this device runs. At T = 1, b200moe_moe_decode,
+ * b200moe_moe_decode_noalloc and b200moe_stack_decode run one persistent kernel per call
+ * (ctas CTAs, one per SM, launched in thread-block clusters of `cluster` CTAs; cluster 1 =
+ * a cooperative launch) when the device can keep all of them resident, else the
+ * three-kernel-per-layer path (ctas = cluster = 0). Both give identical bits. Introspection
+ * only; no counterpart in the reference. Call with the device current. */
+int b200moe_decode_persistent_info(int *ctas, int *cluster);
+
 /* Workspace bytes for b200moe_stack_decode. */
 size_t b200moe_stack_workspace_size(int T, int n_layers);
 

@@ -20,7 +20,8 @@ F32, BF16 = 0, 1
 EXPORTS = ("b200moe_abi_version", "b200moe_last_error", "b200moe_q4k_dequant",
            "b200moe_synth_q4k", "b200moe_router_workspace_size", "b200moe_router",
            "b200moe_decode_workspace_size",
-           "b200moe_moe_decode", "b200moe_moe_decode_noalloc", "b200moe_stack_workspace_size",
+           "b200moe_moe_decode", "b200moe_moe_decode_noalloc", "b200moe_decode_persistent_info",
+           "b200moe_stack_workspace_size",
            "b200moe_stack_decode",
            "b200moe_prefill_workspace_size", "b200moe_moe_prefill", "b200moe_moe_route",
            "b200moe_moe_experts", "b200moe_prefill_status")
@@ -73,6 +74,8 @@ def lib():
         L.b200moe_moe_decode.argtypes = [vp, i32, i32, ctypes.POINTER(Layer), vp, vp, vp, vp, sz, vp]
         L.b200moe_moe_decode_noalloc.restype = i32
         L.b200moe_moe_decode_noalloc.argtypes = [vp, i32, i32, ctypes.POINTER(Layer), vp, vp, vp, vp]
+        L.b200moe_decode_persistent_info.restype = i32
+        L.b200moe_decode_persistent_info.argtypes = [ctypes.POINTER(i32), ctypes.POINTER(i32)]
         L.b200moe_stack_workspace_size.restype = sz
         L.b200moe_stack_workspace_size.argtypes = [i32, i32]
         L.b200moe_stack_decode.restype = i32
@@ -155,6 +158,14 @@ def moe_decode(x, x_dtype: int, T: int, layer: Layer, out, ids_out, w_out, ws, s
     _check("b200moe_moe_decode",
            lib().b200moe_moe_decode(ptr(x), x_dtype, T, ctypes.byref(layer), ptr(out), ptr(ids_out),
                                     ptr(w_out), ptr(ws), ws.numel() * ws.element_size(), _stream(stream)))
+
+
+def decode_persistent_info():
+    """(ctas, cluster) of the persistent single-token decode kernel on the current device, or
+    (0, 0) when the device runs the three-kernel path."""
+    a, c = ctypes.c_int(0), ctypes.c_int(0)
+    _check("b200moe_decode_persistent_info", lib().b200moe_decode_persistent_info(ctypes.byref(a), ctypes.byref(c)))
+    return a.value, c.value
 
 
 def moe_decode_noalloc(x, x_dtype: int, T: int, layer: Layer, out, ids_out, w_out, stream=None):

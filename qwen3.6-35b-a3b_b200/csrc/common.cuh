@@ -159,22 +159,28 @@ __device__ __forceinline__ float nib_1p(uint32_t prepared, int b) {
 
 // sum over the chunk's 32 weights of w_i * x_i, with w = (d*sc)*q - dmin*m. The quants enter
 // as f = 1 + q/16 (one byte permute each): sum(q x) = 16 (sum(f x) - sum(x)), so a run's
-// contribution is 16*S*sum(f x) - (16*S + M) * sum(x).
+// contribution is 16*S*sum(f x) - (16*S + M) * sum(x). Each 16-element run is accumulated in
+// two interleaved chains (words 0-1 and 2-3, added at the end) to halve the dependent latency.
 __device__ __forceinline__ float q4k_chunk_dot(const uint4 &h, const uint4 &q, int c, const XChunk &x) {
   float s0, m0, s1, m1;
   q4k_scales(h, c, s0, m0, s1, m1);
-  float al = 0.f, ah = 0.f;
+  float al0 = 0.f, ah0 = 0.f, al1 = 0.f, ah1 = 0.f;
   const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t lo = ((w[i] << 3) & 0x78787878u) | 0x80808080u;
-    const uint32_t hi = ((w[i] >> 1) & 0x78787878u) | 0x80808080u;
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t lo0 = ((w[i] << 3) & 0x78787878u) | 0x80808080u;
+    const uint32_t hi0 = ((w[i] >> 1) & 0x78787878u) | 0x80808080u;
+    const uint32_t lo1 = ((w[i + 2] << 3) & 0x78787878u) | 0x80808080u;
+    const uint32_t hi1 = ((w[i + 2] >> 1) & 0x78787878u) | 0x80808080u;
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      al = fmaf(nib_1p(lo, b), x.lo[4 * i + b], al);
-      ah = fmaf(nib_1p(hi, b), x.hi[4 * i + b], ah);
+      al0 = fmaf(nib_1p(lo0, b), x.lo[4 * i + b], al0);
+      ah0 = fmaf(nib_1p(hi0, b), x.hi[4 * i + b], ah0);
+      al1 = fmaf(nib_1p(lo1, b), x.lo[4 * (i + 2) + b], al1);
+      ah1 = fmaf(nib_1p(hi1, b), x.hi[4 * (i + 2) + b], ah1);
     }
   }
+  const float al = al0 + al1, ah = ah0 + ah1;
   const float S0 = 16.0f * s0, S1 = 16.0f * s1;
   return fmaf(S0, al, -(S0 + m0) * x.slo) + fmaf(S1, ah, -(S1 + m1) * x.shi);
 }

@@ -520,6 +520,13 @@ int b200moe_moe_decode_noalloc(const void *x, int x_dtype, int T, const b200moe_
                    true);
 }
 
+int b200moe_decode_persistent_info(int *ctas, int *cluster) {
+  const int C = b2mega::cluster_ctas();
+  if (ctas) *ctas = C ? b2mega::kCtas : 0;
+  if (cluster) *cluster = C;
+  return B200MOE_OK;
+}
+
 size_t b200moe_stack_workspace_size(int T, int n_layers) {
   return (T <= 0 || T > kMaxT || n_layers <= 0) ? 0 : decode_ws_bytes(T);
 }

@@ -8,19 +8,20 @@
 
 namespace b2mega {
 
-constexpr int kMaxCtas = 256;  // grid cap (one CTA per SM)
+constexpr int kCtas = 128;  // the persistent grid: 128 CTAs, one per SM
 // Cross-CTA exchange area. Every value one CTA hands to the others travels as one 64-bit word
 // (phase tag << 32 | value bits, single-copy atomic), in per-CTA line-aligned slots -- no two
 // CTAs ever store into the same 128-byte line:
 //   [0, 128)                 abort word, status word
-//   logits [c][16] u64       CTA c's logit pair (or the shared-expert gate)
-//   s      [c][32] u64       CTA c's activations s
+//   logits [c][16] u64       CTA c's logit pair
+//   s      [c][48] u64       CTA c's activations s (32 routed, 4 shared)
 //   deltas [c][16] u64       CTA c's residual deltas
 // Everything is cleared before each launch (tags are launch-local).
+constexpr int kSlotLogits = 16, kSlotS = 48, kSlotDelta = 16;  // 64-bit words per CTA
 constexpr size_t kXLogits = 128;
-constexpr size_t kXS = kXLogits + (size_t)kMaxCtas * 128;
-constexpr size_t kXDelta = kXS + (size_t)kMaxCtas * 256;
-constexpr size_t kScratchBytes = kXDelta + (size_t)kMaxCtas * 128;
+constexpr size_t kXS = kXLogits + (size_t)kCtas * kSlotLogits * 8;
+constexpr size_t kXDelta = kXS + (size_t)kCtas * kSlotS * 8;
+constexpr size_t kScratchBytes = kXDelta + (size_t)kCtas * kSlotDelta * 8;
 constexpr size_t kScratchClear = kScratchBytes;
 
 struct Args {
@@ -36,8 +37,11 @@ struct Args {
   const b200moe_layer *layers;  // host array of n_layers
 };
 
-// 1 if the current device can run the persistent kernel (enough SMs, one resident CTA per SM).
+// 1 if the current device can run the persistent kernel (128 CTAs resident at once).
 bool usable();
+
+// Cluster size the launches use on the current device (1: cooperative launch; 0: unusable).
+int cluster_ctas();
 
 // Enqueue the flag reset and the persistent kernel(s) on `stream`. Returns a B200MOE_* code.
 int launch(const Args &a, cudaStream_t stream);

@@ -1,30 +1,48 @@
 // persist.cu -- single-token MoE decode as ONE persistent kernel over a whole layer stack.
 //
-// Grid: one CTA per SM (cooperative launch, so every CTA is resident), 288 threads (9 warps).
-// Every value one CTA hands to the others travels as a single 64-bit word
-// (phase tag << 32 | value bits) written with one relaxed store: a reader polls the words it
-// needs until each carries the expected tag, so no fence, no flag and no second round trip
-// sits between producer and consumer. Tags are 3l + p + 1 (layer l, phase p); the exchange
-// area is cleared before every launch. Every poll and mbarrier wait is bounded (~1 s); a CTA
-// that gives up raises the abort word, which ends every other CTA's polls.
+// Grid: 128 CTAs of 384 threads (12 warps), one per SM, launched in thread-block clusters of
+// C CTAs (C = 8, 4 or 2: the largest whose clusters all fit at once; C = 1 falls back to a
+// cooperative launch). CTA c owns fixed, aligned slices of the layer's work:
+//   * router: logits 2c, 2c+1 (every CTA also computes the shared-expert gate itself);
+//   * gate/up: routed row pairs q = 32c .. 32c+31 of the flattened (slot, j) space -- all in
+//     expert slot c / 16 -- and shared-expert row pairs j = 4c .. 4c+3;
+//   * down: rows h = 16c .. 16c+15 of all 9 experts, and their combine.
+// Per layer l, three phases and three all-to-all exchanges:
+//   R  resid += the 2048 deltas of layer l-1 (every CTA keeps the whole residual in shared
+//      memory and applies every delta itself, so all CTAs hold identical residuals);
+//      rs = 1/sqrt(mean(resid^2) + eps) in the declared chunk order (each warp derives it);
+//      the CTA's two router rows and the gate row (staged in shared memory one layer ahead)
+//      -> published logit pair.                                                   exchange 1
+//   S  top 8 (R3); the CTA issues the bulk copies of its routed rows of this layer at once --
+//      its 32 gate and 32 up rows in 4 chunks (one mbarrier each) and its 16 down rows of each
+//      of the 8 experts -- then finishes R2, R4, R5.
+//   G  s = silu(gate . x) * (up . x) for its 4 shared-expert pairs (prefetched one layer
+//      ahead) and 32 routed pairs, chunk by chunk as they land -> published s.  exchange 2
+//   D  o[k][h] = down_k[h] . s_k for the 9 experts and its 16 h rows; combine in ascending
+//      expert id + sg * shared -> published deltas (last layer: the final residual rows, or
+//      out in single-layer mode).                                                 exchange 3
 //
-// Each CTA keeps the whole residual in shared memory and applies every layer's 2048 deltas
-// itself, so all CTAs hold identical residuals. Per layer l:
-//   R  poll the 2048 deltas of layer l-1; resid += delta; rs = 1/sqrt(mean(resid^2) + eps)
-//      (declared chunk order); this CTA's router rows (c and c + n of the 257 = 256 logits +
-//      the shared-expert gate, staged in shared memory one layer ahead) -> tagged logits.
-//   S  one warp polls the 256 logits and selects the top 8 (R3); the CTA then issues all
-//      bulk copies of its routed rows of this layer at once -- gate/up row pairs [q0, q0+nq)
-//      of the flattened (slot, j) space in 4 chunks with one mbarrier each, and down rows
-//      [h0, h0+nh) of the 8 experts -- and the warp finishes R2, R4, R5 meanwhile.
-//   G  s[k][j] = silu(gate . x) * (up . x) for the CTA's shared-expert row pairs (prefetched
-//      one layer ahead) and routed row pairs, chunk by chunk as they land -> tagged s.
-//   D  poll the 9 x 512 s; o[k][h] = down_k[h] . s_k for the 9 experts and the CTA's h rows;
-//      combine in ascending expert id + sg * shared -> tagged deltas (last layer: the final
-//      residual rows, or out in single-layer mode).
-// Shared-memory vectors use a padded layout (64-float segments at a 68-float pitch) so the
-// per-lane sequential reads of the declared orders and the Q4_K chunk gathers are free of
-// bank conflicts.
+// Exchange mechanics (no fences on the critical path):
+//   * publish: each value is one 64-bit word (phase tag << 32 | value bits) in the writer's own
+//     line-aligned slot, written with one relaxed store (single-copy atomic: the tag vouches
+//     for the value);
+//   * gather: the cluster reads every writer's slot from L2 ONCE. Cluster rank r owns the
+//     writers [r 128/C, (r+1) 128/C), whose values form one contiguous slice of each gathered
+//     array (logit pairs, routed s, shared s, deltas). It polls the owned slots (re-reading only
+//     words whose tag has not arrived) straight into that slice of its own shared memory, then
+//     copies the
+//     slice to the same offset in each of the C-1 peers with one shared-to-shared bulk copy,
+//     completing bytes on the peer's exchange mbarrier. Each exchange mbarrier is armed with
+//     the bytes the peers will send before any peer can send them; a bounded wait on it ends
+//     the gather. Nothing is unpacked. A slice is overwritten (next layer) only after every
+//     peer has received it: a peer's next contribution to any exchange implies it.
+// Every poll and mbarrier wait is bounded (~1 s); a CTA that gives up raises the abort word,
+// which ends every other CTA's polls. Every CTA ends with a cluster barrier, so no CTA exits
+// while a peer may still write into its shared memory.
+//
+// The residual uses a padded layout (64-float segments at a 68-float pitch) so the per-lane
+// sequential reads of the declared orders and the Q4_K chunk gathers are free of bank
+// conflicts.
 //
 // The arithmetic of every value (RMSNorm, R1 logits in the declared chunk order, R2..R5,
 // per-lane Q4_K chunk dots, warp sums, SiLU, combine order, residual add) is the same sequence
@@ -38,46 +56,29 @@ using namespace b2;
 
 namespace {
 
-constexpr int kThreads = 288;
+constexpr int kThreads = 384;  // 12 warps: 3 per SM sub-partition (168 registers each)
 constexpr int kWarps = kThreads / 32;
-constexpr int kMaxLayers = 64;             // layers per launch (kernel parameter space)
-constexpr int kRouterUnits = kE / 2 + 1;   // 128 logit pairs + the shared-expert gate
-constexpr int kMinCtas = kRouterUnits;     // one router unit per CTA
-constexpr int kRowPair = 2 * kRowUp;       // 2304 B: gate row + up row
-constexpr int kRouterRowBytes = kH * 2;    // 4096 B of bf16
-constexpr int kGuChunks = 4;               // routed gate/up arrival chunks (one mbarrier each)
-constexpr int kGuChunk = 8;                // row pairs per chunk (capq <= 32)
-constexpr int kPadSeg = 68;                // padded pitch of a 64-float segment
-constexpr int kResPad = kH / 64 * kPadSeg;   // 2176 floats
-constexpr int kSPad = kI / 64 * kPadSeg;     // 544 floats per expert slot
+constexpr int kMaxLayers = 64;           // layers per launch (kernel parameter space)
+constexpr int kN = b2mega::kCtas;        // 128 CTAs
+constexpr int kQ = kK * kI / kN;         // 32 routed row pairs per CTA
+constexpr int kJ = kI / kN;              // 4 shared row pairs per CTA
+constexpr int kHr = kH / kN;             // 16 down rows per CTA
+constexpr int kRowPair = 2 * kRowUp;     // 2304 B: gate row + up row
+constexpr int kRouterRowBytes = kH * 2;  // 4096 B of bf16
+constexpr int kRtRows = 3;               // per layer: the CTA's 2 router rows + the gate row
+constexpr int kGuChunks = 4;             // routed gate/up arrival chunks (one mbarrier each)
+constexpr int kGuChunk = kQ / kGuChunks; // 8 row pairs per chunk
+constexpr int kPadSeg = 68;              // padded pitch of a 64-float segment
+constexpr int kResPad = kH / 64 * kPadSeg;  // 2176 floats
 
-// exchange area slots (see mega.cuh): per CTA c, line-aligned, written by c only
-//   logits: word 0 = logits 2c | 2c+1 << 16 (c < 128) or the shared-expert gate (c = 128)
-//   s:      its routed s values (flattened (slot, j) order from q0), then its shared ones
-//   deltas: its residual deltas h0 .. h0+nh-1
-constexpr int kSlotLogits = 16, kSlotS = 32, kSlotDelta = 16;  // 64-bit words
+// exchange slots (64-bit words, see mega.cuh): per CTA c, line-aligned, written by c only
+using b2mega::kSlotLogits;  // word 0: logits 2c | 2c+1 << 16
+using b2mega::kSlotS;       // words 0..31: routed s (q = 32c + i), 32..35: shared s (j = 4c + i - 32)
+using b2mega::kSlotDelta;   // words 0..15: deltas h = 16c + i
+static_assert(kQ == 32 && kJ == 4 && kHr == 16, "the fixed 128-CTA partition");
+static_assert(kSlotS >= kQ + kJ && kSlotDelta >= kHr, "exchange slots");
 
-__host__ __device__ inline int split_at(int total, int n, int c) { return (int)(((long long)total * c) / n); }
 __host__ __device__ inline int pad(int i) { return (i >> 6) * kPadSeg + (i & 63); }
-
-struct Geo {
-  int q0, nq;  // routed gate/up row pairs: flattened (slot, j) indices [q0, q0 + nq)
-  int j0, nj;  // shared-expert gate/up row pairs [j0, j0 + nj)
-  int h0, nh;  // down rows [h0, h0 + nh)
-  int nrt;     // router rows of unit c: 2 (logits 2c, 2c+1), 1 (c == 128: gate), 0
-};
-
-__host__ __device__ inline Geo geo(int c, int n) {
-  Geo g;
-  g.q0 = split_at(kK * kI, n, c);
-  g.nq = split_at(kK * kI, n, c + 1) - g.q0;
-  g.j0 = split_at(kI, n, c);
-  g.nj = split_at(kI, n, c + 1) - g.j0;
-  g.h0 = split_at(kH, n, c);
-  g.nh = split_at(kH, n, c + 1) - g.h0;
-  g.nrt = c < kE / 2 ? 2 : (c == kE / 2 ? 1 : 0);
-  return g;
-}
 
 struct MegaParams {
   int n_layers;
@@ -88,11 +89,25 @@ struct MegaParams {
   float *out;
   int32_t *ids_out;
   uint16_t *w_out;
-  uint8_t *xchg;         // exchange area (mega.cuh layout)
-  int capq, capj, caph;  // per-CTA maxima of nq, nj, nh for this grid
-  int off_s, off_rt, off_gu, off_dn, off_o, off_rr, off_tab, off_bar;
+  uint8_t *xchg;  // exchange area (mega.cuh layout)
   b200moe_layer L[kMaxLayers];
 };
+
+// dynamic shared memory layout (bytes)
+constexpr int kOffRes = 0;                                   // [kResPad] f32 residual (or x)
+constexpr int kOffS = kOffRes + kResPad * 4;                 // [4096] f32 routed s, flat (slot, j)
+constexpr int kOffSsh = kOffS + kK * kI * 4;                 // [512] f32 shared-expert s
+constexpr int kOffDl = kOffSsh + kI * 4;                     // [2048] f32 gathered deltas
+constexpr int kOffLg = kOffDl + kH * 4;                      // [128] u32 gathered logit pairs
+constexpr int kOffRt = kOffLg + kN * 4;                      // [2 layers][3 rows][4096] router rows
+constexpr int kOffGu = kOffRt + 2 * kRtRows * kRouterRowBytes;  // [36] gate rows, then [36] up rows
+constexpr int kOffDn = kOffGu + (kQ + kJ) * kRowPair;        // [9][16] down rows
+constexpr int kOffO = kOffDn + (kK + 1) * kHr * kRowDown;    // [9][16] f32 down outputs
+constexpr int kOffRr = kOffO + (kK + 1) * kHr * 4;           // Route
+constexpr int kOffMisc = kOffRr + 128;                       // [3] router row results, [36] s out
+constexpr int kOffScr = kOffMisc + 256;                      // [12][32] f32 per-warp scratch
+constexpr int kOffBar = kOffScr + 12 * 32 * 4;               // mbarriers
+constexpr int kSmem = kOffBar + 256;
 
 // ---------------------------------------------------------------- device helpers
 __device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t *p) {
@@ -107,23 +122,40 @@ __device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t *p) {
   return v;
 }
 
+// Two tagged words (each 64-bit element is single-copy atomic on its own).
+__device__ __forceinline__ void ld_relaxed_v2u64(const uint64_t *p, uint64_t &a, uint64_t &b) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
 __device__ __forceinline__ void st_tagged(uint64_t *p, uint32_t tag, uint32_t bits) {
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(((uint64_t)tag << 32) | bits) : "memory");
 }
 
-// Bounded mbarrier wait that suspends the thread (hint: 20 us) instead of spinning, so idle
-// warps leave the issue slots to the working ones.
-__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity) {
+// Bounded mbarrier wait (try_wait without a suspend-time hint: a waiter resumes as soon as the
+// phase completes). kCluster: acquire at cluster scope (the phase is completed by peers' bulk
+// copies).
+template <bool kCluster>
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
   const long long t0 = clock64();
   for (;;) {
     uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
-        : "memory");
+    if (kCluster) {
+      asm volatile(
+          "{\n\t.reg .pred p;\n\t"
+          "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+          "selp.u32 %0, 1, 0, p;\n\t}"
+          : "=r"(ok)
+          : "r"(smem_u32(bar)), "r"(parity)
+          : "memory");
+    } else {
+      asm volatile(
+          "{\n\t.reg .pred p;\n\t"
+          "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+          "selp.u32 %0, 1, 0, p;\n\t}"
+          : "=r"(ok)
+          : "r"(smem_u32(bar)), "r"(parity)
+          : "memory");
+    }
     if (ok) return true;
     if (clock64() - t0 > kWaitBudgetCycles) return false;
   }
@@ -143,72 +175,45 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
       : "memory");
 }
 
+// Shared-to-shared bulk copy into a peer CTA (cluster addresses), completing bytes on the peer's
+// mbarrier.
+__device__ __forceinline__ void bulk_s2s(uint32_t rdst, uint32_t src, uint32_t bytes, uint32_t rbar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   rdst),
+               "r"(src), "r"(bytes), "r"(rbar)
+               : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_evict_normal() {
   uint64_t pol;
   asm("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
   return pol;
 }
 
-__device__ __forceinline__ void ld_relaxed_v2u64(const uint64_t *p, uint64_t &a, uint64_t &b) {
-  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
 }
 
-// Gather the tagged words of every CTA's slot (slot pitch `pitch` words, cnt(c) words used) into
-// the CTA, in two stages: (1) thread t < n polls word 0 of slot t until it carries `tag` -- one
-// cheap load per writer while the writers are still busy; (2) after a barrier every thread reads
-// its share of all slots' words (64-bit pairs, coalesced) and re-polls only words whose tag is
-// not there yet. sink(c, i, bits) receives word i of slot c. Returns false (CTA-uniform) on abort
-// or after the wait budget.
-template <int kPitch, int kMaxPer, typename Cnt, typename Sink>
-__device__ __forceinline__ bool gather_slots(const uint64_t *base, int n, uint32_t tag, const uint32_t *abort_word,
-                                             Cnt cnt, Sink sink) {
-  const long long t0 = clock64();
-  bool fail = false;
-  if ((int)threadIdx.x < n) {
-    const uint64_t *w0 = base + (size_t)threadIdx.x * kPitch;
-    for (int it = 1; (uint32_t)(ld_relaxed_u64(w0) >> 32) != tag; ++it) {
-      if ((it & 15) == 0 && (ld_relaxed_u32(abort_word) != 0u || clock64() - t0 > kWaitBudgetCycles)) {
-        fail = true;
-        break;
-      }
-    }
-  }
-  if (__syncthreads_or(fail)) return false;
-  constexpr int kPairs = kPitch / 2;
-  uint32_t pending = 0;  // two bits per pair
-#pragma unroll
-  for (int k = 0; k < kMaxPer; ++k) {
-    const int pr = threadIdx.x + k * kThreads;
-    if (pr < n * kPairs) {
-      const int i = 2 * (pr % kPairs), m = cnt(pr / kPairs);
-      pending |= ((i < m ? 1u : 0u) | (i + 1 < m ? 2u : 0u)) << (2 * k);
-    }
-  }
-  for (int it = 1; pending && !fail; ++it) {
-#pragma unroll
-    for (int k = 0; k < kMaxPer; ++k) {
-      const uint32_t want = (pending >> (2 * k)) & 3u;
-      if (!want) continue;
-      const int pr = threadIdx.x + k * kThreads;
-      uint64_t a, b;
-      ld_relaxed_v2u64(base + 2 * (size_t)pr, a, b);
-      const int c = pr / kPairs, i = 2 * (pr % kPairs);
-      if ((want & 1u) && (uint32_t)(a >> 32) == tag) {
-        sink(c, i, (uint32_t)a);
-        pending &= ~(1u << (2 * k));
-      }
-      if ((want & 2u) && (uint32_t)(b >> 32) == tag) {
-        sink(c, i + 1, (uint32_t)b);
-        pending &= ~(2u << (2 * k));
-      }
-    }
-    if (pending && (it & 15) == 0 && (ld_relaxed_u32(abort_word) != 0u || clock64() - t0 > kWaitBudgetCycles))
-      fail = true;
-  }
-  return !__syncthreads_or(fail);
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
 }
 
-// x values of chunk (kb, c) from a padded row, each scaled by rs (1.0f: unscaled).
+// Address of this CTA's shared-memory location `saddr` in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+  return d;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// x values of chunk (kb, c) from the padded residual, each scaled by rs.
 __device__ __forceinline__ void xchunk_pad(const float *row, float rs, int kb, int c, XChunk &x) {
   const int p = (4 * kb + (c >> 1)) * kPadSeg + 16 * (c & 1);
 #pragma unroll
@@ -227,83 +232,201 @@ __device__ __forceinline__ void xchunk_pad(const float *row, float rs, int kb, i
   x.shi = sh;
 }
 
-__device__ __forceinline__ float chunk_total32(float acc) {
-  float tot = __shfl_sync(0xFFFFFFFFu, acc, 0);
+// The declared R1 / RMSNorm order: the 32 lanes' partials added left to right. They go through
+// a 32-float shared-memory scratch of the warp (one store, eight vector loads) instead of 31
+// dependent shuffles; the result is broadcast to every lane.
+__device__ __forceinline__ float chunk_total32(float acc, float *scratch) {
+  const int lane = threadIdx.x & 31;
+  scratch[lane] = acc;
+  __syncwarp();
+  float tot = 0.0f;
+  if (lane == 0) {
+    float v[32];
 #pragma unroll
-  for (int c = 1; c < 32; ++c) tot = __fadd_rn(tot, __shfl_sync(0xFFFFFFFFu, acc, c));
+    for (int i = 0; i < 8; ++i) {
+      const float4 q = reinterpret_cast<const float4 *>(scratch)[i];
+      v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
+    }
+    tot = v[0];
+#pragma unroll
+    for (int c = 1; c < 32; ++c) tot = __fadd_rn(tot, v[c]);
+  }
+  tot = __shfl_sync(0xFFFFFFFFu, tot, 0);
+  __syncwarp();
   return tot;
 }
 
-enum { kBarRt0 = 0, kBarRt1, kBarGu0, kBarDn = kBarGu0 + kGuChunks, kBarShGu, kBarShDn, kNumBars };
+// One router row staged in shared memory: R1 in the declared order (bf16 logit bits) or, for
+// the shared-expert gate, sigmoid(w_sg . x) with the decode path's arithmetic (f32 bits).
+// Lane 0 holds the result.
+__device__ __forceinline__ uint32_t router_row(const uint8_t *row, const float *res, float rs, int lane, bool gate,
+                                               float bias, float *scratch) {
+  const uint4 *rp = reinterpret_cast<const uint4 *>(row) + 8 * lane;
+  const float *xv = res + lane * kPadSeg;
+  float acc = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint4 u = rp[i];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    const float4 x0 = *reinterpret_cast<const float4 *>(xv + 8 * i);
+    const float4 x1 = *reinterpret_cast<const float4 *>(xv + 8 * i + 4);
+    const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      acc = __fmaf_rn(__fmul_rn(xs[2 * q], rs), bf16f(w[q]), acc);
+      acc = __fmaf_rn(__fmul_rn(xs[2 * q + 1], rs), bf16f(w[q] >> 16), acc);
+    }
+  }
+  if (gate) {
+    const float z = warp_sum(acc);
+    return __float_as_uint(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z))));
+  }
+  const float tot = __fadd_rn(chunk_total32(acc, scratch), bias);
+  return f2bf(tot);
+}
+
+enum {
+  kBarRt0 = 0, kBarRt1, kBarGu0, kBarDn = kBarGu0 + kGuChunks, kBarShGu, kBarShDn,
+  kBarXLg, kBarXS, kBarXDl,  // exchange barriers: bytes from the cluster peers
+  kNumBars
+};
+
+// ---------------------------------------------------------------- the gather
+// One exchange (see the file comment). This rank owns writers [w0, w0 + 128/C); every writer has
+// kCnt used words in its slot (pitch kPitch). put(w, i, bits) stores word i of writer w into
+// this CTA's gathered arrays; `slices` (nsl of them: shared-memory address, bytes) are this
+// rank's contiguous slices, sent to every peer. Returns false (CTA-uniform) on abort or after
+// the wait budget.
+struct Slice {
+  uint32_t addr, bytes;
+};
+
+template <int kPitch, int kCnt, typename Put>
+__device__ __forceinline__ bool gather(const uint64_t *base, uint32_t tag, const uint32_t *abort_word, int C, int r,
+                                       uint64_t *xbar, uint32_t parity, const Slice *slices, int nsl, Put put) {
+  const long long t0 = clock64();
+  const int per = kN / C, w0 = r * per;
+  bool fail = false;
+  constexpr int kPairs = (kCnt + 1) / 2;                            // used pairs per writer
+  constexpr int kMaxPer = (kN * kPairs + kThreads - 1) / kThreads;  // the C = 1 bound
+  uint32_t pending = 0;  // two bits per pair
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) {
+    const int pr = threadIdx.x + k * kThreads;
+    if (pr < per * kPairs) {
+      const int i = 2 * (pr % kPairs);
+      pending |= ((i < kCnt ? 1u : 0u) | (i + 1 < kCnt ? 2u : 0u)) << (2 * k);
+    }
+  }
+  for (int it = 1; pending && !fail; ++it) {  // the owned slots -> this rank's slices (re-poll the rest)
+#pragma unroll
+    for (int k = 0; k < kMaxPer; ++k) {
+      const uint32_t want = (pending >> (2 * k)) & 3u;
+      if (!want) continue;
+      const int pr = threadIdx.x + k * kThreads;
+      const int w = w0 + pr / kPairs, i = 2 * (pr % kPairs);
+      uint64_t a, b;
+      ld_relaxed_v2u64(base + (size_t)w * kPitch + i, a, b);
+      if ((want & 1u) && (uint32_t)(a >> 32) == tag) {
+        put(w, i, (uint32_t)a);
+        pending &= ~(1u << (2 * k));
+      }
+      if ((want & 2u) && (uint32_t)(b >> 32) == tag) {
+        put(w, i + 1, (uint32_t)b);
+        pending &= ~(2u << (2 * k));
+      }
+    }
+    if (pending && (it & 15) == 0 && (ld_relaxed_u32(abort_word) != 0u || clock64() - t0 > kWaitBudgetCycles))
+      fail = true;
+  }
+  fence_proxy_async_smem();  // the slices are read by the bulk copies below (async proxy)
+  if (__syncthreads_or(fail)) return false;
+  if (threadIdx.x == 0) {
+    const uint32_t lbar = smem_u32(xbar);
+    for (int q = 1; q < C; ++q) {
+      const uint32_t peer = (uint32_t)((r + q) % C);
+      for (int s = 0; s < nsl; ++s)
+        bulk_s2s(mapa(slices[s].addr, peer), slices[s].addr, slices[s].bytes, mapa(lbar, peer));
+    }
+  }
+  // the peers' slices: bytes completed on this CTA's exchange barrier
+  fail = !mbar_wait_bounded<true>(xbar, parity);
+  return !__syncthreads_or(fail);
+}
 
 __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ MegaParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
-  float *res_s = reinterpret_cast<float *>(smem);                 // [kResPad] residual (or x)
-  float *s_s = reinterpret_cast<float *>(smem + P.off_s);         // [9][kSPad]
-  uint8_t *rt = smem + P.off_rt;   // [2 layers][2 rows][4096]
-  uint8_t *gu_g = smem + P.off_gu;                            // [capq routed + capj shared] gate rows
-  uint8_t *gu_u = gu_g + (size_t)(P.capq + P.capj) * kRowUp;  // the matching up rows
-  uint8_t *dn = smem + P.off_dn;   // [9][caph] down rows
-  float *o_s = reinterpret_cast<float *>(smem + P.off_o);  // [9][caph]
-  Route *rr = reinterpret_cast<Route *>(smem + P.off_rr);
-  uint2 *lg16 = reinterpret_cast<uint2 *>(smem + P.off_rr + 128);  // [64] the 256 bf16 logits
-  Geo *tab = reinterpret_cast<Geo *>(smem + P.off_tab);              // [n] every CTA's work ranges
-  uint16_t *lgp = reinterpret_cast<uint16_t *>(lg16 + 64);           // [2] this CTA's logit pair
-  float *s_out = reinterpret_cast<float *>(lg16 + 66);               // [32] this CTA's s values
-  uint64_t *bar = reinterpret_cast<uint64_t *>(smem + P.off_bar);
-  float *misc = reinterpret_cast<float *>(bar + kNumBars);  // [1] sg
+  float *res_s = reinterpret_cast<float *>(smem + kOffRes);
+  float *s_s = reinterpret_cast<float *>(smem + kOffS);
+  float *ssh_s = reinterpret_cast<float *>(smem + kOffSsh);
+  float *dl_s = reinterpret_cast<float *>(smem + kOffDl);
+  uint32_t *lg_s = reinterpret_cast<uint32_t *>(smem + kOffLg);
+  uint8_t *rt = smem + kOffRt;
+  uint8_t *gu_g = smem + kOffGu;                  // [32 routed + 4 shared] gate rows
+  uint8_t *gu_u = gu_g + (kQ + kJ) * kRowUp;      // the matching up rows
+  uint8_t *dn = smem + kOffDn;                    // [9][16] down rows
+  float *o_s = reinterpret_cast<float *>(smem + kOffO);
+  Route *rr = reinterpret_cast<Route *>(smem + kOffRr);
+  uint32_t *row_out = reinterpret_cast<uint32_t *>(smem + kOffMisc);  // [3] router row results
+  float *s_out = reinterpret_cast<float *>(smem + kOffMisc + 16);      // [36] this CTA's s values
+  float *warp_scr = reinterpret_cast<float *>(smem + kOffScr);
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem + kOffBar);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int c = blockIdx.x, n = gridDim.x;
-  const Geo G = geo(c, n);
+  const int c = blockIdx.x;
+  const int C = (int)cluster_size(), r = (int)cluster_rank();
+  const int slot_c = c / (kI / kQ), j_c = (c * kQ) % kI;  // this CTA's routed expert slot, first row
   uint32_t *abort_word = reinterpret_cast<uint32_t *>(P.xchg);  // [1]: status for the host
   uint64_t *tl = reinterpret_cast<uint64_t *>(P.xchg + b2mega::kXLogits);
   uint64_t *ts = reinterpret_cast<uint64_t *>(P.xchg + b2mega::kXS);
   uint64_t *td = reinterpret_cast<uint64_t *>(P.xchg + b2mega::kXDelta);
   const uint64_t pol_first = l2_evict_first(), pol_normal = l2_evict_normal();
 
-  uint32_t armed = 0;  // thread 0: barriers with a phase in flight
+  uint32_t armed = 0;  // thread 0: copy barriers with a phase in flight
   uint32_t ph[kNumBars];
 #pragma unroll
   for (int b = 0; b < kNumBars; ++b) ph[b] = 0;
 
-  auto issue_router_rows = [&](int l) {  // thread 0: layer l's router rows -> rt[l & 1], one copy
+  auto issue_router_rows = [&](int l) {  // thread 0: layer l's 2 router rows + gate row -> rt[l & 1]
     uint64_t *b = bar + kBarRt0 + (l & 1);
-    mbar_expect_tx(b, (uint32_t)G.nrt * kRouterRowBytes);
-    if (G.nrt > 0) {
-      const void *src = G.nrt == 2 ? (const void *)((const uint16_t *)P.L[l].router_w + (size_t)(2 * c) * kH)
-                                   : P.L[l].sh_gate_w;
-      bulk_g2s(rt + (l & 1) * 2 * kRouterRowBytes, src, (uint32_t)G.nrt * kRouterRowBytes, b, pol_normal);
-    }
+    mbar_expect_tx(b, kRtRows * kRouterRowBytes);
+    uint8_t *d = rt + (size_t)(l & 1) * kRtRows * kRouterRowBytes;
+    bulk_g2s(d, (const uint16_t *)P.L[l].router_w + (size_t)(2 * c) * kH, 2 * kRouterRowBytes, b, pol_normal);
+    bulk_g2s(d + 2 * kRouterRowBytes, P.L[l].sh_gate_w, kRouterRowBytes, b, pol_normal);
     armed |= 1u << (kBarRt0 + (l & 1));
   };
   auto issue_shared_gu = [&](int l) {  // thread 0: layer l's shared-expert gate/up rows, 2 copies
-    mbar_expect_tx(bar + kBarShGu, (uint32_t)G.nj * kRowPair);
-    if (G.nj > 0) {
-      const size_t off = (size_t)G.j0 * kRowUp;
-      bulk_g2s(gu_g + (size_t)P.capq * kRowUp, (const uint8_t *)P.L[l].sh_gate + off, G.nj * kRowUp, bar + kBarShGu,
-               pol_normal);
-      bulk_g2s(gu_u + (size_t)P.capq * kRowUp, (const uint8_t *)P.L[l].sh_up + off, G.nj * kRowUp, bar + kBarShGu,
-               pol_normal);
-    }
+    mbar_expect_tx(bar + kBarShGu, kJ * kRowPair);
+    const size_t off = (size_t)(kJ * c) * kRowUp;
+    bulk_g2s(gu_g + kQ * kRowUp, (const uint8_t *)P.L[l].sh_gate + off, kJ * kRowUp, bar + kBarShGu, pol_normal);
+    bulk_g2s(gu_u + kQ * kRowUp, (const uint8_t *)P.L[l].sh_up + off, kJ * kRowUp, bar + kBarShGu, pol_normal);
     armed |= 1u << kBarShGu;
   };
   auto issue_shared_dn = [&](int l) {  // thread 0: layer l's shared-expert down rows (slot 8), 1 copy
-    mbar_expect_tx(bar + kBarShDn, (uint32_t)G.nh * kRowDown);
-    if (G.nh > 0)
-      bulk_g2s(dn + (size_t)8 * P.caph * kRowDown, (const uint8_t *)P.L[l].sh_down + (size_t)G.h0 * kRowDown,
-               G.nh * kRowDown, bar + kBarShDn, pol_normal);
+    mbar_expect_tx(bar + kBarShDn, kHr * kRowDown);
+    bulk_g2s(dn + 8 * kHr * kRowDown, (const uint8_t *)P.L[l].sh_down + (size_t)(kHr * c) * kRowDown,
+             kHr * kRowDown, bar + kBarShDn, pol_normal);
     armed |= 1u << kBarShDn;
   };
-  // bounded wait on barrier b's pending phase; flips this thread's parity only on success
+  // bounded wait on copy barrier b's pending phase; flips this thread's parity only on success
   auto wait_bar = [&](int b) -> bool {
-    const bool ok = mbar_wait_sleep(bar + b, ph[b]);
+    const bool ok = mbar_wait_bounded<false>(bar + b, ph[b]);
     if (ok) {
       ph[b] ^= 1u;
       if (tid == 0) armed &= ~(1u << b);
     }
     return ok;
   };
+
+  // this rank's slices of the gathered arrays (owned writers [r 128/C, (r+1) 128/C))
+  const int per = kN / C, w0 = r * per;
+  const Slice sl_lg[1] = {{smem_u32(lg_s + w0), (uint32_t)(per * 4)}};
+  const Slice sl_s[2] = {{smem_u32(s_s + w0 * kQ), (uint32_t)(per * kQ * 4)},
+                         {smem_u32(ssh_s + w0 * kJ), (uint32_t)(per * kJ * 4)}};
+  const Slice sl_dl[1] = {{smem_u32(dl_s + w0 * kHr), (uint32_t)(per * kHr * 4)}};
+  // every exchange brings (C - 1) peer slices
+  const uint32_t rx_lg = (uint32_t)(C - 1) * per * 4, rx_s = (uint32_t)(C - 1) * per * (kQ + kJ) * 4,
+                 rx_dl = (uint32_t)(C - 1) * per * kHr * 4;
 
   if (tid == 0) {
     for (int b = 0; b < kNumBars; ++b) mbar_init(bar + b, 1);
@@ -320,13 +443,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
     const float *xf = reinterpret_cast<const float *>(P.x);
     for (int i = tid; i < kH; i += kThreads) res_s[pad(i)] = __ldcg(xf + i);
   }
-  for (int i = tid; i < n; i += kThreads) tab[i] = geo(i, n);
   __syncthreads();
   if (tid == 0) {
+    // the first phase of each exchange barrier (the deltas are first consumed by layer 1)
+    mbar_expect_tx(bar + kBarXLg, rx_lg);
+    mbar_expect_tx(bar + kBarXS, rx_s);
+    if (P.n_layers > 1) mbar_expect_tx(bar + kBarXDl, rx_dl);
     issue_router_rows(0);
     issue_shared_gu(0);
     issue_shared_dn(0);
   }
+  // every peer's barriers are initialised and armed before anyone can send into them
+  cluster_sync_all();
 
   bool fail = false, aborted = false;
   const int kb0 = lane >> 3, cc = lane & 7;  // gate/up lane mapping (blocks kb0, kb0 + 4; chunk cc)
@@ -336,15 +464,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
     const bool last = l + 1 == P.n_layers;
     // ---------------------------------------------------------------- phase R
     if (l > 0) {  // resid += the previous layer's deltas (every CTA applies all of them)
-      if (!gather_slots<kSlotDelta, (b2mega::kMaxCtas * kSlotDelta / 2 + kThreads - 1) / kThreads>(
-              td, n, ep, abort_word, [&](int src) { return tab[src].nh; },
-              [&](int src, int i, uint32_t v) {
-                float *r = res_s + pad(tab[src].h0 + i);
-                *r = __fadd_rn(*r, __uint_as_float(v));
-              })) {
+      if (!gather<kSlotDelta, kHr>(td, ep, abort_word, C, r, bar + kBarXDl, ph[kBarXDl], sl_dl, 1,
+                                   [&](int w, int i, uint32_t v) { dl_s[w * kHr + i] = __uint_as_float(v); })) {
         aborted = true;
         break;
       }
+      ph[kBarXDl] ^= 1u;
+      if (tid == 0 && !last) mbar_expect_tx(bar + kBarXDl, rx_dl);  // the next layer's deltas
+      for (int h = tid; h < kH; h += kThreads) {
+        float *rp = res_s + pad(h);
+        *rp = __fadd_rn(*rp, dl_s[h]);
+      }
+      __syncthreads();
     }
     if (tid == 0 && !last) issue_router_rows(l + 1);
     float rs = 1.0f;  // every warp derives the RMSNorm scale itself (identical bits, no barrier)
@@ -359,185 +490,116 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
         ss = __fmaf_rn(a.z, a.z, ss);
         ss = __fmaf_rn(a.w, a.w, ss);
       }
-      const float tot = chunk_total32(ss);
+      const float tot = chunk_total32(ss, warp_scr + 32 * warp);
       rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, 2048.0f), P.eps)));
     }
     fail = !__all_sync(0xFFFFFFFFu, wait_bar(kBarRt0 + (l & 1)));  // every thread consumes the phase
-    if (warp < G.nrt && !fail) {
-      {
-        const uint4 *rp = reinterpret_cast<const uint4 *>(rt + ((l & 1) * 2 + warp) * kRouterRowBytes) + 8 * lane;
-        const float *xv = res_s + lane * kPadSeg;
-        float acc = 0.0f;
-        if (G.nrt == 2) {  // R1 for logit 2c + warp: sequential fmaf over the lane's 64 elements
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint4 u = rp[i];
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-            const float4 x0 = *reinterpret_cast<const float4 *>(xv + 8 * i);
-            const float4 x1 = *reinterpret_cast<const float4 *>(xv + 8 * i + 4);
-            const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              acc = __fmaf_rn(__fmul_rn(xs[2 * q], rs), bf16f(w[q]), acc);
-              acc = __fmaf_rn(__fmul_rn(xs[2 * q + 1], rs), bf16f(w[q] >> 16), acc);
-            }
-          }
-          float tot = chunk_total32(acc);
-          if (Lp.logit_bias) tot = __fadd_rn(tot, Lp.logit_bias[2 * c + warp]);
-          if (lane == 0) lgp[warp] = f2bf(tot);
-        } else {  // shared-expert gate: sigmoid(w_sg . x), the decode path's arithmetic
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint4 u = rp[i];
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-            const float4 x0 = *reinterpret_cast<const float4 *>(xv + 8 * i);
-            const float4 x1 = *reinterpret_cast<const float4 *>(xv + 8 * i + 4);
-            const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              acc = fmaf(__fmul_rn(xs[2 * q], rs), bf16f(w[q]), acc);
-              acc = fmaf(__fmul_rn(xs[2 * q + 1], rs), bf16f(w[q] >> 16), acc);
-            }
-          }
-          const float z = warp_sum(acc);
-          if (lane == 0)
-            st_tagged(tl + (size_t)c * kSlotLogits, ep + 1, __float_as_uint(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)))));
-        }
-      }
+    if (!fail && warp < kRtRows) {  // warps 0, 1: logits 2c, 2c+1; warp 2: the gate
+      const bool gate = warp == 2;
+      const float bias = (!gate && Lp.logit_bias) ? Lp.logit_bias[2 * c + warp] : 0.0f;
+      const uint32_t v =
+          router_row(rt + ((size_t)(l & 1) * kRtRows + warp) * kRouterRowBytes, res_s, rs, lane, gate, bias,
+                     warp_scr + 32 * warp);
+      if (lane == 0) row_out[warp] = v;
     }
     if (__syncthreads_or(fail)) { aborted = true; break; }
-    if (tid == 0 && G.nrt == 2)
-      st_tagged(tl + (size_t)c * kSlotLogits, ep + 1, (uint32_t)lgp[0] | ((uint32_t)lgp[1] << 16));
+    if (tid == 0) st_tagged(tl + (size_t)c * kSlotLogits, ep + 1, row_out[0] | (row_out[1] << 16));
     // ---------------------------------------------------------------- phase S
-    uint32_t rw[4] = {0, 0, 0, 0}, mine = 0;
-    if (warp == 0) {  // lane L polls word 0 of the logit slots of CTAs L, L+32, ..., (<= 128)
-      const long long t0 = clock64();
-      uint32_t got = 0, want = 0;
+    if (!gather<kSlotLogits, 1>(tl, ep + 1, abort_word, C, r, bar + kBarXLg, ph[kBarXLg], sl_lg, 1,
+                                [&](int w, int, uint32_t v) { lg_s[w] = v; })) {
+      aborted = true;
+      break;
+    }
+    ph[kBarXLg] ^= 1u;
+    if (tid == 0 && !last) mbar_expect_tx(bar + kBarXLg, rx_lg);  // the next layer's logits
+    if (warp == 0) {  // lane L: logits 8L .. 8L+7
+      const uint4 v = reinterpret_cast<const uint4 *>(lg_s)[lane];
+      uint32_t rw[4] = {v.x, v.y, v.z, v.w};
+      const uint32_t mine = route_select(rw);
+      const int my_sel = 255 - (int)(mine & 0xFFu);
+      if (lane == 0) {
 #pragma unroll
-      for (int m = 0; m < 5; ++m)
-        if (lane + 32 * m <= kE / 2) want |= 1u << m;
-      for (int it = 1; got != want && !fail; ++it) {
-#pragma unroll
-        for (int m = 0; m < 5; ++m) {
-          if (!(want & ~got & (1u << m))) continue;
-          const int src = lane + 32 * m;
-          const uint64_t w = ld_relaxed_u64(tl + (size_t)src * kSlotLogits);
-          if ((uint32_t)(w >> 32) == ep + 1) {
-            if (src < kE / 2) reinterpret_cast<uint32_t *>(lg16)[src] = (uint32_t)w;  // logits 2src, 2src+1
-            else misc[1] = __uint_as_float((uint32_t)w);                             // the shared-expert gate
-            got |= 1u << m;
-          }
-        }
-        if (got != want && (it & 15) == 0 &&
-            (ld_relaxed_u32(abort_word) != 0u || clock64() - t0 > kWaitBudgetCycles))
-          fail = true;
+        for (int g = 0; g < kGuChunks; ++g) mbar_expect_tx(bar + kBarGu0 + g, kGuChunk * kRowPair);
+        mbar_expect_tx(bar + kBarDn, kK * kHr * kRowDown);
+        armed |= (((1u << kGuChunks) - 1u) << kBarGu0) | (1u << kBarDn);
       }
       __syncwarp();
-      {  // lane L: logits 8L .. 8L+7 for the route
-        const uint4 v = reinterpret_cast<const uint4 *>(lg16)[lane];
-        rw[0] = v.x; rw[1] = v.y; rw[2] = v.z; rw[3] = v.w;
+      // Routed bulk copies, one per lane: lanes 0..7 -> chunk lane >> 1 of the gate (even) or
+      // up (odd) rows of this CTA's expert; lanes 8..15 -> the 16 down rows of slot lane - 8.
+      const int k = lane < 8 ? slot_c : (lane - 8) & 7;
+      const int e = __shfl_sync(0xFFFFFFFFu, my_sel, k);
+      if (lane < 8) {
+        const int g = lane >> 1, which = lane & 1;
+        const uint8_t *src = (const uint8_t *)(which ? Lp.up : Lp.gate) + (size_t)e * Lp.gate_up_expert_stride +
+                             (size_t)(j_c + g * kGuChunk) * kRowUp;
+        bulk_g2s((which ? gu_u : gu_g) + g * kGuChunk * kRowUp, src, kGuChunk * kRowUp, bar + kBarGu0 + g,
+                 pol_first);
+      } else if (lane < 16) {
+        const uint8_t *src =
+            (const uint8_t *)Lp.down + (size_t)e * Lp.down_expert_stride + (size_t)(kHr * c) * kRowDown;
+        bulk_g2s(dn + (size_t)k * kHr * kRowDown, src, kHr * kRowDown, bar + kBarDn, pol_first);
       }
-      fail = !__all_sync(0xFFFFFFFFu, !fail);
-      if (!fail) {
-        mine = route_select(rw);
-        const int my_sel = 255 - (int)(mine & 0xFFu);
-        if (lane == 0) {
-#pragma unroll
-          for (int g = 0; g < kGuChunks; ++g) {
-            const int cnt = min(kGuChunk, max(0, G.nq - g * kGuChunk));
-            mbar_expect_tx(bar + kBarGu0 + g, (uint32_t)cnt * kRowPair);
-          }
-          mbar_expect_tx(bar + kBarDn, (uint32_t)(kK * G.nh * kRowDown));
-          armed |= (((1u << kGuChunks) - 1u) << kBarGu0) | (1u << kBarDn);
-        }
-        __syncwarp();
-        // Routed bulk copies, one per lane, each a contiguous row range:
-        //   lanes 0..15: chunk g = lane >> 2, piece (lane >> 1) & 1 (the part of the chunk in its
-        //                first / second expert slot), matrix lane & 1 (gate / up);
-        //   lanes 16..23: down rows [h0, h0 + nh) of slot lane - 16.
-        int a0 = 0, b0 = 0, slot = 0;  // gate/up lanes: chunk rows [a0, b0) of one expert slot
-        if (lane < 16) {
-          const int g = lane >> 2, piece = (lane >> 1) & 1;
-          const int r0 = g * kGuChunk, r1 = min(G.nq, r0 + kGuChunk);
-          a0 = r0;
-          b0 = r1;
-          if (r0 < r1) {
-            const int split = ((G.q0 + r0) / kI + 1) * kI - G.q0;  // first row of the next slot
-            if (piece == 0) b0 = min(r1, split);
-            else a0 = max(r0, split);
-          }
-          slot = a0 < b0 ? (G.q0 + a0) / kI : 0;
-        } else {
-          slot = (lane - 16) & 7;
-        }
-        const int e = __shfl_sync(0xFFFFFFFFu, my_sel, slot);
-        const uint8_t *src = nullptr;
-        uint8_t *dst = nullptr;
-        uint32_t bytes = 0;
-        uint64_t *cb = bar + kBarDn;
-        if (lane < 16) {
-          if (a0 < b0) {
-            const int which = lane & 1, j = (G.q0 + a0) % kI;
-            src = (const uint8_t *)(which ? Lp.up : Lp.gate) + (size_t)e * Lp.gate_up_expert_stride + (size_t)j * kRowUp;
-            dst = (which ? gu_u : gu_g) + (size_t)a0 * kRowUp;
-            bytes = (uint32_t)(b0 - a0) * kRowUp;
-            cb = bar + kBarGu0 + (lane >> 2);
-          }
-        } else if (lane < 24 && G.nh > 0) {
-          src = (const uint8_t *)Lp.down + (size_t)e * Lp.down_expert_stride + (size_t)G.h0 * kRowDown;
-          dst = dn + (size_t)slot * P.caph * kRowDown;
-          bytes = (uint32_t)G.nh * kRowDown;
-        }
-        if (bytes) bulk_g2s(dst, src, bytes, cb, pol_first);
-        route_finish(rw, mine, rr);  // R2, R4, R5 while the rows stream in
-        if (c == 0 && lane < kK) {
-          if (P.ids_out) P.ids_out[(size_t)l * kK + lane] = rr->ids[lane];
-          if (P.w_out) P.w_out[(size_t)l * kK + lane] = rr->wb[lane];
-        }
+      route_finish(rw, mine, rr);  // R2, R4, R5 while the rows stream in
+      if (c == 0 && lane < kK) {
+        if (P.ids_out) P.ids_out[(size_t)l * kK + lane] = rr->ids[lane];
+        if (P.w_out) P.w_out[(size_t)l * kK + lane] = rr->wb[lane];
       }
     }
     // ---------------------------------------------------------------- phase G
-    {  // warps 1..8 (warp 0 routes above); shared pairs first: their rows are already resident
-      const int total = G.nj + G.nq;
+    {  // warps 1..11 (warp 0 routes above), two row pairs per iteration; shared pairs first
       uint32_t have = 0;  // bit 0: shared, bit 1 + g: routed chunk g
       if (warp > 0) {
         XChunk X0, X1;
         xchunk_pad(res_s, rs, kb0, cc, X0);
         xchunk_pad(res_s, rs, kb0 + 4, cc, X1);
-        for (int idx = warp - 1; idx < total && !fail; idx += kWarps - 1) {
-          const bool shared = idx < G.nj;
-          const int rp = idx - G.nj;
-          const int need = shared ? 0 : 1 + rp / kGuChunk;
-          if (!(have & (1u << need))) {  // warp-uniform outcome: the warp reduces together below
-            fail = !__all_sync(0xFFFFFFFFu, wait_bar(shared ? kBarShGu : kBarGu0 + need - 1));
-            have |= 1u << need;
+        constexpr int kStep = kWarps - 1;
+        for (int ia = warp - 1; ia < kJ + kQ && !fail; ia += 2 * kStep) {
+          const int ib = ia + kStep;  // the second pair of this iteration (if any)
+          const bool two = ib < kJ + kQ;
+          uint32_t need = 1u << (ia < kJ ? 0 : 1 + (ia - kJ) / kGuChunk);
+          if (two) need |= 1u << (ib < kJ ? 0 : 1 + (ib - kJ) / kGuChunk);
+          for (int bit = 0; bit < 1 + kGuChunks; ++bit) {  // warp-uniform outcomes
+            if (!(need & ~have & (1u << bit))) continue;
+            fail = !__all_sync(0xFFFFFFFFu, wait_bar(bit == 0 ? kBarShGu : kBarGu0 + bit - 1));
+            have |= 1u << bit;
             if (fail) break;
           }
-          const int row = shared ? P.capq + idx : rp;
-          const uint8_t *gp = gu_g + (size_t)row * kRowUp, *up = gu_u + (size_t)row * kRowUp;
-          int k, j;
-          if (shared) {
-            k = kK;
-            j = G.j0 + idx;
-          } else {
-            const int qq = G.q0 + rp;
-            k = qq / kI;
-            j = qq % kI;
-          }
-          uint4 hq[8];
+          if (fail) break;
+          const uint8_t *rowp[2];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int kb = kb0 + 4 * h;
-            hq[4 * h + 0] = *reinterpret_cast<const uint4 *>(gp + kb * kQB);
-            hq[4 * h + 1] = *reinterpret_cast<const uint4 *>(gp + kb * kQB + 16 + 16 * cc);
-            hq[4 * h + 2] = *reinterpret_cast<const uint4 *>(up + kb * kQB);
-            hq[4 * h + 3] = *reinterpret_cast<const uint4 *>(up + kb * kQB + 16 + 16 * cc);
+          for (int p = 0; p < 2; ++p) {
+            const int idx = p ? ib : ia;
+            const int row = !two && p ? kQ : (idx < kJ ? kQ + idx : idx - kJ);  // a spare read when !two
+            rowp[p] = gu_g + (size_t)row * kRowUp;
           }
-          float g = q4k_chunk_dot(hq[0], hq[1], cc, X0) + q4k_chunk_dot(hq[4], hq[5], cc, X1);
-          float u = q4k_chunk_dot(hq[2], hq[3], cc, X0) + q4k_chunk_dot(hq[6], hq[7], cc, X1);
-          g = warp_sum(g);
-          u = warp_sum(u);
-          if (lane == 0) s_out[shared ? G.nq + idx : rp] = __fmul_rn(silu_f(g), u);
+          float g[2], u[2];
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {  // gate rows of both pairs, then their up rows
+            uint4 hq[2][4];
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+              const uint8_t *rp = rowp[p] + m * (size_t)(kQ + kJ) * kRowUp;
+              hq[p][0] = *reinterpret_cast<const uint4 *>(rp + kb0 * kQB);
+              hq[p][1] = *reinterpret_cast<const uint4 *>(rp + kb0 * kQB + 16 + 16 * cc);
+              hq[p][2] = *reinterpret_cast<const uint4 *>(rp + (kb0 + 4) * kQB);
+              hq[p][3] = *reinterpret_cast<const uint4 *>(rp + (kb0 + 4) * kQB + 16 + 16 * cc);
+            }
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+              const float v = q4k_chunk_dot(hq[p][0], hq[p][1], cc, X0) + q4k_chunk_dot(hq[p][2], hq[p][3], cc, X1);
+              if (m == 0) g[p] = v;
+              else u[p] = v;
+            }
+          }
+#pragma unroll
+          for (int p = 0; p < 2; ++p) {
+            g[p] = warp_sum(g[p]);
+            u[p] = warp_sum(u[p]);
+          }
+          if (lane == 0) {
+            s_out[ia < kJ ? kQ + ia : ia - kJ] = __fmul_rn(silu_f(g[0]), u[0]);
+            if (two) s_out[ib < kJ ? kQ + ib : ib - kJ] = __fmul_rn(silu_f(g[1]), u[1]);
+          }
         }
       }
       // every thread consumes every phase of this layer (thread 0 tracks them for the drain)
@@ -546,56 +608,57 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
         if (!(have & (2u << g))) fail = !wait_bar(kBarGu0 + g);
     }
     if (__syncthreads_or(fail)) { aborted = true; break; }
-    if (warp == 0 && lane < G.nq + G.nj)  // this CTA's s values, one coalesced 256-byte store
-      st_tagged(ts + (size_t)c * kSlotS + lane, ep + 2, __float_as_uint(s_out[lane]));
+    if (tid < kQ + kJ)  // this CTA's s values: one coalesced store
+      st_tagged(ts + (size_t)c * kSlotS + tid, ep + 2, __float_as_uint(s_out[tid]));
     if (tid == 0 && !last) issue_shared_gu(l + 1);  // this layer's shared gate/up reads are done
     // ---------------------------------------------------------------- phase D
-    if (!gather_slots<kSlotS, (b2mega::kMaxCtas * kSlotS / 2 + kThreads - 1) / kThreads>(
-            ts, n, ep + 2, abort_word, [&](int src) { return tab[src].nq + tab[src].nj; },
-            [&](int src, int w, uint32_t v) {
-              const Geo &g2 = tab[src];
-              int k, j;
-              if (w < g2.nq) {
-                const int qq = g2.q0 + w;
-                k = qq / kI;
-                j = qq % kI;
-              } else {
-                k = kK;
-                j = g2.j0 + (w - g2.nq);
-              }
-              s_s[k * kSPad + pad(j)] = __uint_as_float(v);
-            })) {
+    if (!gather<kSlotS, kQ + kJ>(ts, ep + 2, abort_word, C, r, bar + kBarXS, ph[kBarXS], sl_s, 2,
+                                 [&](int w, int i, uint32_t v) {
+                                   if (i < kQ) s_s[w * kQ + i] = __uint_as_float(v);
+                                   else ssh_s[w * kJ + i - kQ] = __uint_as_float(v);
+                                 })) {
       aborted = true;
       break;
     }
-    if (!fail) fail = !wait_bar(kBarDn);
-    if (!fail) fail = !wait_bar(kBarShDn);
+    ph[kBarXS] ^= 1u;
+    if (tid == 0 && !last) mbar_expect_tx(bar + kBarXS, rx_s);  // the next layer's s
+    fail = !wait_bar(kBarDn);
+    fail = !wait_bar(kBarShDn) || fail;
     if (__syncthreads_or(fail)) { aborted = true; break; }
-    {
-      const int slot = warp;  // 9 warps: routed slots 0..7, shared expert 8
+    if (warp <= kK) {
+      const int slot = warp;  // warps 0..8: routed slots 0..7, shared expert 8
       const int half = lane >> 4, kb = (lane >> 3) & 1;
       XChunk X;
-      xchunk_pad(s_s + slot * kSPad, 1.0f, kb, cc, X);
-      for (int it = 0; 2 * it < G.nh; ++it) {
-        const int hh = 2 * it + half;
-        const int hr = hh < G.nh ? hh : G.nh - 1;  // odd count: the spare half-warp repeats a row
-        const uint8_t *p = dn + (size_t)(slot * P.caph + hr) * kRowDown + kb * kQB;
-        const uint4 h4 = *reinterpret_cast<const uint4 *>(p);
-        const uint4 q4 = *reinterpret_cast<const uint4 *>(p + 16 + 16 * cc);
-        const float v = half_warp_sum(q4k_chunk_dot(h4, q4, cc, X));
-        if ((lane & 15) == 0 && hh < G.nh) o_s[slot * P.caph + hh] = v;
+      load_xchunk(slot < kK ? s_s + slot * kI : ssh_s, kb, cc, X);
+#pragma unroll 1
+      for (int it = 0; it < kHr / 4; ++it) {  // rows 2it + half and 2it + 8 + half: two in flight
+        float v[2];
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const int hh = 2 * it + 8 * p + half;
+          const uint8_t *pp = dn + (size_t)(slot * kHr + hh) * kRowDown + kb * kQB;
+          const uint4 h4 = *reinterpret_cast<const uint4 *>(pp);
+          const uint4 q4 = *reinterpret_cast<const uint4 *>(pp + 16 + 16 * cc);
+          v[p] = q4k_chunk_dot(h4, q4, cc, X);
+        }
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          v[p] = half_warp_sum(v[p]);
+          if ((lane & 15) == 0) o_s[slot * kHr + 2 * it + 8 * p + half] = v[p];
+        }
       }
     }
     __syncthreads();
-    if (tid < G.nh) {
+    if (tid < kHr) {
       float acc = 0.0f;
 #pragma unroll
       for (int i = 0; i < kK; ++i) {
         const int slot = rr->order[i];
-        acc = __fadd_rn(acc, __fmul_rn(o_s[slot * P.caph + tid], bf16f(rr->wb[slot])));
+        acc = __fadd_rn(acc, __fmul_rn(o_s[slot * kHr + tid], bf16f(rr->wb[slot])));
       }
-      const float res = __fadd_rn(acc, __fmul_rn(misc[1], o_s[8 * P.caph + tid]));
-      const int h = G.h0 + tid;
+      const float sg = __uint_as_float(row_out[2]);
+      const float res = __fadd_rn(acc, __fmul_rn(sg, o_s[8 * kHr + tid]));
+      const int h = kHr * c + tid;
       if (!last) {
         st_tagged(td + (size_t)c * kSlotDelta + tid, ep + 3, __float_as_uint(res));
       } else if (P.resid) {
@@ -610,58 +673,61 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
   if (aborted && tid == 0) {
     atomicExch(abort_word, 1u);      // ends every other CTA's polls
     atomicExch(abort_word + 1, 1u);  // status for the host
-    // every armed phase completes on its own (its copies were issued together with it):
+    // every armed copy phase completes on its own (its copies were issued together with it):
     // let them land before this CTA's shared memory is released
-    for (int b = 0; b < kNumBars; ++b)
+    for (int b = 0; b < kBarXLg; ++b)
       if (armed & (1u << b)) mbar_wait(bar + b, ph[b]);
   }
+  // no CTA leaves while a cluster peer may still deliver into its shared memory
+  __syncthreads();
+  cluster_sync_all();
 }
 
 // ---------------------------------------------------------------- host side
 struct DevInfo {
   bool init = false, ok = false;
-  int n = 0;
-  size_t smem = 0;
-  MegaParams layout;  // offsets and capacities only
+  int C = 1;
 };
 
 DevInfo g_dev[64];
 
-size_t al16(size_t v) { return (v + 15) & ~(size_t)15; }
-
 bool prepare(int dev, DevInfo &d) {
   if (d.init) return d.ok;
   d.init = true;
-  int sms = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return false;
-  int coop = 0;
-  if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess || !coop) return false;
-  const int n = sms < b2mega::kMaxCtas ? sms : b2mega::kMaxCtas;
-  if (n < kMinCtas) return false;
-  MegaParams &p = d.layout;
-  p.capq = (kK * kI + n - 1) / n;
-  p.capj = (kI + n - 1) / n;
-  p.caph = (kH + n - 1) / n;
-  if (p.capq > kGuChunks * kGuChunk) return false;
-  size_t off = (size_t)kResPad * 4;                  // residual / x, padded
-  p.off_s = (int)off; off += (size_t)(kK + 1) * kSPad * 4;
-  p.off_rt = (int)off; off += 4 * (size_t)kRouterRowBytes;
-  p.off_gu = (int)off; off += (size_t)(p.capq + p.capj) * kRowPair;
-  p.off_dn = (int)off; off += (size_t)(kK + 1) * p.caph * kRowDown;
-  p.off_o = (int)off; off += al16((size_t)(kK + 1) * p.caph * 4);
-  p.off_rr = (int)off; off += 128 + 64 * 8 + 16 + 128;  // Route, the 256 logits, the CTA's pair, its s
-  p.off_tab = (int)off; off += al16(sizeof(Geo) * (size_t)n);
-  if (p.capq + p.capj > kSlotS || p.caph > kSlotDelta) return false;
-  p.off_bar = (int)off; off += kNumBars * 8 + 16;
-  d.smem = off;
-  int maxsm = 0;
-  if (cudaDeviceGetAttribute(&maxsm, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return false;
-  if ((size_t)maxsm < d.smem) return false;
-  if (cudaFuncSetAttribute(k_mega, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d.smem) != cudaSuccess) return false;
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega, kThreads, d.smem) != cudaSuccess || per_sm < 1)
+  int sms = 0, maxsm = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < kN) return false;
+  if (cudaDeviceGetAttribute(&maxsm, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || maxsm < kSmem)
     return false;
-  d.n = n;
+  if (cudaFuncSetAttribute(k_mega, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess) return false;
+  // the largest cluster size whose 128 / C clusters are all resident at once
+  for (int C : {8, 4, 2}) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kN);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, k_mega, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      continue;
+    }
+    if (clusters * C >= kN) {
+      d.C = C;
+      d.ok = true;
+      return true;
+    }
+  }
+  int coop = 0, per_sm = 0;
+  if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess || !coop) return false;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega, kThreads, kSmem) != cudaSuccess || per_sm < 1)
+    return false;
+  d.C = 1;
   d.ok = true;
   return true;
 }
@@ -676,13 +742,19 @@ bool usable() {
   return prepare(dev, g_dev[dev]);
 }
 
+int cluster_ctas() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || !prepare(dev, g_dev[dev])) return 0;
+  return g_dev[dev].C;
+}
+
 int launch(const Args &a, cudaStream_t stream) {
   int dev = 0;
   B2_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64 || !prepare(dev, g_dev[dev]))
-    return b2host::set_error(B200MOE_EINVAL, "persistent decode: device %d cannot host one resident CTA per SM", dev);
+    return b2host::set_error(B200MOE_EINVAL, "persistent decode: device %d cannot host %d resident CTAs", dev, kN);
   const DevInfo &d = g_dev[dev];
-  MegaParams p = d.layout;
+  MegaParams p;
   p.eps = a.eps;
   p.x = a.x;
   p.x_dtype = a.x_dtype;
@@ -697,13 +769,20 @@ int launch(const Args &a, cudaStream_t stream) {
     for (int l = 0; l < nl; ++l) p.L[l] = a.layers[l0 + l];
     B2_CUDA(cudaMemsetAsync(a.scratch, 0, kScratchClear, stream));
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)d.n);
+    cfg.gridDim = dim3(kN);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = d.smem;
+    cfg.dynamicSmemBytes = kSmem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
+    if (d.C > 1) {  // clusters: every cluster co-scheduled; all 128 / C clusters fit at once
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = (unsigned)d.C;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+    } else {        // one CTA per SM, all resident
+      attr[0].id = cudaLaunchAttributeCooperative;
+      attr[0].val.cooperative = 1;
+    }
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     B2_CUDA(cudaLaunchKernelEx(&cfg, k_mega, p));

@@ -25,6 +25,14 @@ def _token(seed, stream, cuda):
     return torch.from_numpy(bf16_bits_to_f32(synth.tokens(seed, 1, stream=stream)).copy()).to(cuda)
 
 
+def test_persistent_path_is_active(cuda):
+    """On a B200 the single-token path must be the persistent kernel (the comparisons below
+    would otherwise compare the three-kernel path with itself)."""
+    from b200moe import _abi
+    ctas, cluster = _abi.decode_persistent_info()
+    assert ctas == 128 and cluster in (1, 2, 4, 8), (ctas, cluster)
+
+
 def test_stack_persistent_equals_three_kernel_path(cuda, engine4):
     import torch
     from b200moe import moe
