@@ -199,13 +199,16 @@ def run_b200(args):
     T = args.batch
     K, W = args.steps, args.warmup
     hbm_peak, peak_kind = peaks()
+    persist_ctas, persist_cluster = 0, 0
     graph = None
     expert_bytes = None
 
     if args.workload == "stack_decode":
         eng = DeviceEngine.synthetic(args.seed, args.layers, dev)
         nl = args.layers
-        launches_per_step = 3 * nl
+        persist_ctas, persist_cluster = _abi.decode_persistent_info() if T == 1 else (0, 0)
+        # one persistent kernel for the whole stack (T = 1), else 3 kernels per layer
+        launches_per_step = 1 if persist_ctas else 3 * nl
         bytes_per_step = nl * (9 * EXPERT_BYTES * (1 if T == 1 else 0) + ROUTER_BYTES + WSG_BYTES + 2 * T * 2048 * 4)
         ws = torch.empty(moe.stack_workspace_bytes(T), dtype=torch.uint8, device=dev)
         tok_bits = synth.tokens(args.seed, (K + W) * T, stream=100 + rank)
@@ -236,7 +239,8 @@ def run_b200(args):
         L = DeviceLayer.synthetic(args.seed, 0, dev, bias=(args.seed == 2))
         # rotate over enough layer copies to exceed L2: per-step bytes are one layer's
         nl = 1
-        launches_per_step = 3
+        persist_ctas, persist_cluster = _abi.decode_persistent_info() if T == 1 else (0, 0)
+        launches_per_step = 1 if persist_ctas else 3
         tok_bits = synth.tokens(args.seed, (K + W) * T, stream=100 + rank)
         tok_dev = torch.from_numpy(tok_bits.view(np.int16)).view(torch.bfloat16).reshape(K + W, T, 2048).to(dev)
         out = torch.empty((T, 2048), dtype=torch.float32, device=dev)
@@ -404,8 +408,12 @@ def run_b200(args):
                      "frac": (achieved / peak) if achieved else None,
                      "traffic": traffic.get("dram_bytes_per_step") if traffic else None,
                      "peak_kind": peak_kind,
-                     "kernel": ("one graph replay = %d kernels (router/shared K1, routed gate_up K2, down+combine K3 "
-                                "per layer)" % launches_per_step) if args.workload in ("stack_decode", "layer_decode")
+                     "kernel": (("one graph replay = 1 persistent kernel over all %d layers (%d CTAs in clusters "
+                                 "of %d; router, routing, bulk-copied Q4_K gate/up and down rows, combine)"
+                                 % (nl, persist_ctas, persist_cluster)) if persist_ctas
+                                else "one graph replay = %d kernels (router/shared K1, routed gate_up K2, down+combine "
+                                     "K3 per layer)" % launches_per_step)
+                               if args.workload in ("stack_decode", "layer_decode")
                                else ("one step = %d kernels per layer (prep, router GEMM, route, count, plan, fill, "
                                      "tcgen05 gate_up GEMM, tcgen05 down GEMM, combine); achieved = expert FLOPs / "
                                      "step time" % (launches_per_step // max(nl, 1)))},

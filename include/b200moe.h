@@ -163,14 +163,16 @@ int b200moe_moe_route(const void *x, int x_dtype, float *resid, float eps, int T
 
 /* The expert stage of b200moe_moe_prefill for pre-routed tokens: for each token, the slots
  * whose expert id lies in [e_lo, e_hi) go through the Q4_K grouped GEMMs (tcgen05), and
- * out[t] (+)= sum over those slots in ascending expert id of w * expert(x) -- plus
- * sg[t] * shared_expert(x) when sg is non-NULL. Slots outside the range are skipped, so a
- * rank of an expert-parallel group passes its own expert range and sg = NULL, and the
- * token's home rank adds the shared expert. accumulate != 0 adds into out.
+ * out[t] (+)= sum over those slots in ascending expert id of w * expert(x) -- plus, for rows
+ * t in [sh_lo, sh_hi) when sg is non-NULL, sg[t - sh_lo] * shared_expert(x[t]) (its tiles
+ * share the GEMM launches with the routed ones). Slots outside the range are skipped, so a
+ * rank of an expert-parallel group passes its own expert range over every gathered token and
+ * the shared-expert rows of its own tokens. accumulate != 0 adds into out.
  * Replaces engine/m3_forward.py:447-475 (grouping, expert loop, combine). */
 int b200moe_moe_experts(const void *x16, int T, const int32_t *ids, const uint16_t *w_bf16,
-                        int e_lo, int e_hi, const float *sg, const b200moe_layer *layer,
-                        float *out, int accumulate, void *ws, size_t ws_bytes, void *stream);
+                        int e_lo, int e_hi, const float *sg, int sh_lo, int sh_hi,
+                        const b200moe_layer *layer, float *out, int accumulate, void *ws,
+                        size_t ws_bytes, void *stream);
 
 /* Copy the prefill workspace's device status word to *status (synchronises `stream`). Bits:
  * 1 / 2 = a gate_up / down GEMM pipeline wait exceeded its ~1 s budget; 4 = an fp16 tensor-core

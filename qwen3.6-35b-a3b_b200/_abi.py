@@ -90,8 +90,8 @@ def lib():
         L.b200moe_moe_route.argtypes = [vp, i32, vp, ctypes.c_float, i32, ctypes.POINTER(Layer), vp, vp, vp, vp,
                                         vp, sz, vp]
         L.b200moe_moe_experts.restype = i32
-        L.b200moe_moe_experts.argtypes = [vp, i32, vp, vp, i32, i32, vp, ctypes.POINTER(Layer), vp, i32, vp, sz,
-                                          vp]
+        L.b200moe_moe_experts.argtypes = [vp, i32, vp, vp, i32, i32, vp, i32, i32, ctypes.POINTER(Layer), vp, i32,
+                                          vp, sz, vp]
         L.b200moe_prefill_status.restype = i32
         L.b200moe_prefill_status.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_int), vp]
         _LIB = L
@@ -211,8 +211,11 @@ def moe_route(x, x_dtype: int, resid, eps: float, T: int, layer: Layer, x16_out,
 
 
 def moe_experts(x16, T: int, ids, w_bf16, e_lo: int, e_hi: int, sg, layer: Layer, out, accumulate: bool, ws,
-                stream=None):
+                stream=None, sh_rows=None):
+    """b200moe_moe_experts; ``sh_rows`` = (lo, hi): the rows that get sg[t - lo] * shared expert
+    (default: all T rows when sg is given)."""
+    lo, hi = sh_rows if sh_rows is not None else (0, T)
     _check("b200moe_moe_experts",
-           lib().b200moe_moe_experts(ptr(x16), T, ptr(ids), ptr(w_bf16), int(e_lo), int(e_hi), ptr(sg),
-                                     ctypes.byref(layer), ptr(out), 1 if accumulate else 0, ptr(ws),
+           lib().b200moe_moe_experts(ptr(x16), T, ptr(ids), ptr(w_bf16), int(e_lo), int(e_hi), ptr(sg), int(lo),
+                                     int(hi), ctypes.byref(layer), ptr(out), 1 if accumulate else 0, ptr(ws),
                                      ws.numel() * ws.element_size(), _stream(stream)))

@@ -276,11 +276,11 @@ __global__ void __launch_bounds__(256) k_count(int T, const int32_t *ids, int e_
 // One CTA of 512 threads (thread e < 257 owns expert e; e = 256 is the shared expert).
 // Row offsets follow expert order 0..256; the chunk (tile) order puts the shared expert's
 // full-width chunks first, then experts 0..255, so the largest tiles are scheduled first.
-__global__ void __launch_bounds__(512) k_plan(int T, int with_shared, const int32_t *counts_in, int32_t *offsets,
+__global__ void __launch_bounds__(512) k_plan(int n_shared, const int32_t *counts_in, int32_t *offsets,
                                               int4 *tiles1, int4 *tiles2, int32_t *ntiles) {
   __shared__ int sc[512], sn[512];
   const int e = threadIdx.x;
-  const int cnt = e < kE ? counts_in[e] : (e == kE && with_shared ? T : 0);
+  const int cnt = e < kE ? counts_in[e] : (e == kE ? n_shared : 0);
   const int nch = (cnt + kChunk - 1) / kChunk;
   const int pos = e == kE ? 0 : (e < kE ? e + 1 : e);  // a permutation of 0..511
   sc[e] = cnt;
@@ -312,14 +312,13 @@ __global__ void __launch_bounds__(512) k_plan(int T, int with_shared, const int3
 }
 
 // ------------------------------------------------------------------------- k_fill
-__global__ void __launch_bounds__(1024) k_fill(int T, int with_shared, const int32_t *ids, const int32_t *counts,
-                                                const int32_t *offsets, int32_t *plist) {
+__global__ void __launch_bounds__(1024) k_fill(int T, int sh_lo, int sh_hi, const int32_t *ids,
+                                                const int32_t *counts, const int32_t *offsets, int32_t *plist) {
   __shared__ int wcount[32];
   __shared__ int running;
   const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  if (e == kE) {
-    if (with_shared)
-      for (int t = tid; t < T; t += 1024) plist[offsets[kE] + t] = t;
+  if (e == kE) {  // the shared expert's rows: tokens sh_lo .. sh_hi-1
+    for (int t = sh_lo + tid; t < sh_hi; t += 1024) plist[offsets[kE] + t - sh_lo] = t;
     return;
   }
   if (counts[e] == 0) return;
@@ -692,8 +691,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(GemmParams P) {
 
 // ------------------------------------------------------------------------- k_combine
 __global__ void __launch_bounds__(256) k_combine(int T, const float *y, const float *ysh, const float *sg,
-                                                 const int32_t *ids, const int32_t *order, int e_lo, int e_hi,
-                                                 float *out, int accumulate) {
+                                                 int sh_lo, int sh_hi, const int32_t *ids, const int32_t *order,
+                                                 int e_lo, int e_hi, float *out, int accumulate) {
   const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;  // one float4 of one token
   if (idx >= (int64_t)T * (kH / 4)) return;
   const int t = (int)(idx / (kH / 4)), h = (int)(idx % (kH / 4)) * 4;
@@ -710,8 +709,8 @@ __global__ void __launch_bounds__(256) k_combine(int T, const float *y, const fl
     acc.w = __fadd_rn(acc.w, v.w);
   }
   float4 r = acc;
-  if (sg) {
-    const float g = __ldg(sg + t);
+  if (sg && t >= sh_lo && t < sh_hi) {
+    const float g = __ldg(sg + (t - sh_lo));
     const float4 sh = __ldcs(reinterpret_cast<const float4 *>(ysh + (size_t)t * kH + h));
     r = make_float4(__fadd_rn(acc.x, __fmul_rn(g, sh.x)), __fadd_rn(acc.y, __fmul_rn(g, sh.y)),
                     __fadd_rn(acc.z, __fmul_rn(g, sh.z)), __fadd_rn(acc.w, __fmul_rn(g, sh.w)));
@@ -765,17 +764,17 @@ int route_stage(const void *x, int x_dtype, const float *resid, float eps, int T
 // Expert stage: grouped GEMMs for the slots whose expert is in [e_lo, e_hi) (+ the shared
 // expert when sg != NULL), then the combine into out (accumulate: out += result).
 int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *wb, int e_lo, int e_hi,
-                  const float *sg, const b200moe_layer *L, float *out, int accumulate, const PrefillWS &w,
-                  cudaStream_t s) {
+                  const float *sg, int sh_lo, int sh_hi, const b200moe_layer *L, float *out, int accumulate,
+                  const PrefillWS &w, cudaStream_t s) {
   int rc = ensure_gemm_attrs();
   if (rc) return rc;
   B2_CUDA(cudaMemsetAsync(w.counts, 0, kNE * 4, s));
   k_count<<<(T + 255) / 256, 256, 0, s>>>(T, ids, e_lo, e_hi, w.counts, w.order);
   B2_CUDA(cudaGetLastError());
-  const int with_shared = sg != nullptr;
-  k_plan<<<1, 512, 0, s>>>(T, with_shared, w.counts, w.offsets, w.tiles1, w.tiles2, w.ntiles);
+  if (!sg) sh_lo = sh_hi = 0;
+  k_plan<<<1, 512, 0, s>>>(sh_hi - sh_lo, w.counts, w.offsets, w.tiles1, w.tiles2, w.ntiles);
   B2_CUDA(cudaGetLastError());
-  k_fill<<<kNE, 1024, 0, s>>>(T, with_shared, ids, w.counts, w.offsets, w.plist);
+  k_fill<<<kNE, 1024, 0, s>>>(T, sh_lo, sh_hi, ids, w.counts, w.offsets, w.plist);
   B2_CUDA(cudaGetLastError());
   GemmParams g;
   g.wa0 = (const uint8_t *)L->gate;
@@ -803,7 +802,8 @@ int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *
   k_gemm<2><<<g_num_sms, kGemmThreads, GemmCfg<2>::kSmem, s>>>(g);
   B2_CUDA(cudaGetLastError());
   const int64_t nthreads = (int64_t)T * (kH / 4);
-  k_combine<<<(unsigned)((nthreads + 255) / 256), 256, 0, s>>>(T, w.y, w.ysh, sg, ids, w.order, e_lo, e_hi, out,
+  k_combine<<<(unsigned)((nthreads + 255) / 256), 256, 0, s>>>(T, w.y, w.ysh, sg, sh_lo, sh_hi, ids, w.order, e_lo,
+                                                               e_hi, out,
                                                                accumulate);
   B2_CUDA(cudaGetLastError());
   return B200MOE_OK;
@@ -837,7 +837,7 @@ int b200moe_moe_prefill(const void *x, int x_dtype, float *resid, float eps, int
   rc = route_stage(x, x_dtype, resid, eps, T, L, w.x16, w.ids, w.wb, w.sg, w, s);
   if (rc) return rc;
   if (ids_out) B2_CUDA(cudaMemcpyAsync(ids_out, w.ids, (size_t)T * kK * 4, cudaMemcpyDeviceToDevice, s));
-  return experts_stage(w.x16, T, w.ids, w.wb, 0, kE, w.sg, L, resid ? resid : out, resid ? 1 : 0, w, s);
+  return experts_stage(w.x16, T, w.ids, w.wb, 0, kE, w.sg, 0, T, L, resid ? resid : out, resid ? 1 : 0, w, s);
 }
 
 int b200moe_moe_route(const void *x, int x_dtype, float *resid, float eps, int T, const b200moe_layer *L,
@@ -861,14 +861,16 @@ int b200moe_moe_route(const void *x, int x_dtype, float *resid, float eps, int T
 }
 
 int b200moe_moe_experts(const void *x16, int T, const int32_t *ids, const uint16_t *w_bf16, int e_lo, int e_hi,
-                        const float *sg, const b200moe_layer *L, float *out, int accumulate, void *ws,
-                        size_t ws_bytes, void *stream) {
+                        const float *sg, int sh_lo, int sh_hi, const b200moe_layer *L, float *out, int accumulate,
+                        void *ws, size_t ws_bytes, void *stream) {
   if (T <= 0 || T > kMaxTPrefill)
     return b2host::set_error(B200MOE_EINVAL, "moe_experts: T=%d outside [1, %d]", T, kMaxTPrefill);
   if (!x16 || !ids || !w_bf16 || !out || !ws)
     return b2host::set_error(B200MOE_EINVAL, "moe_experts: x16, ids, w_bf16, out and ws are required");
   if (e_lo < 0 || e_hi > kE || e_lo > e_hi)
     return b2host::set_error(B200MOE_EINVAL, "moe_experts: expert range [%d, %d) not within [0, 256)", e_lo, e_hi);
+  if (sg && (sh_lo < 0 || sh_hi > T || sh_lo > sh_hi))
+    return b2host::set_error(B200MOE_EINVAL, "moe_experts: shared rows [%d, %d) not within [0, %d)", sh_lo, sh_hi, T);
   if (!a16(x16) || !a16(out) || !a16(ws))
     return b2host::set_error(B200MOE_EINVAL, "moe_experts: pointers must be 16-byte aligned");
   if (ws_bytes < prefill_ws_bytes(T))
@@ -878,7 +880,7 @@ int b200moe_moe_experts(const void *x16, int T, const int32_t *ids, const uint16
   if (rc) return rc;
   const PrefillWS w = carve_prefill(ws, T);
   B2_CUDA(cudaMemsetAsync(w.err, 0, 4, (cudaStream_t)stream));
-  return experts_stage((const __half *)x16, T, ids, w_bf16, e_lo, e_hi, sg, L, out, accumulate, w,
+  return experts_stage((const __half *)x16, T, ids, w_bf16, e_lo, e_hi, sg, sh_lo, sh_hi, L, out, accumulate, w,
                        (cudaStream_t)stream);
 }
 

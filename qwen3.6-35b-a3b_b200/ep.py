@@ -1,22 +1,25 @@
 """Expert parallelism for the prefill path: one process per GPU, torch.distributed over NCCL.
 
 The 256 routed experts are split evenly over the W ranks of the group (256/128/64/32 per GPU at
-W = 1/2/4/8); router and shared expert are replicated. For one layer, each rank:
+W = 1/2/4/8); router and shared expert are replicated. Every rank passes the same number of
+tokens T. For one layer, each rank:
 
 1. routes its own tokens (``b200moe_moe_route``: fp16 activations, ids, bf16 weights, gate);
-2. dispatch: for every destination rank, picks (ascending token order) the tokens with at least
-   one slot among that rank's experts and masks the other slots to -1; counts are exchanged with
-   ``all_to_all_single``, then the fp16 rows, ids and weights. A token crosses the link once per
-   destination rank, whatever number of its experts live there;
-3. runs its experts on what it received (``b200moe_moe_experts`` with its expert range,
-   no shared expert) -> one f32 partial row per received token (its slots summed in ascending
-   expert id);
-4. combine: partials return along the reversed splits and are added per token in ascending
-   rank order, i.e. ascending expert ranges; the token's own rank adds sg * shared expert.
+2. dispatch: ``all_gather`` of the fp16 rows, ids and weights -- every rank sees all W*T tokens;
+3. runs its experts on all of them in one ``b200moe_moe_experts`` call: the slots in its
+   expert range for every gathered token, plus the shared expert for its own tokens' rows (one
+   set of GEMM launches). The stage keeps only the slots in range, so each token costs GEMM
+   work on the ranks that own its experts and nothing elsewhere; one f32 partial row per
+   gathered token (its in-range slots summed in ascending expert id, + sg * shared on its own
+   rows, zero when it has none);
+4. combine: ``all_to_all_single`` with equal splits sends the partial rows of rank r's tokens
+   back to rank r, which adds the W partials per token in ascending rank order (ascending
+   expert ranges).
 
-The only host synchronisation per layer is the count exchange (split sizes must be host ints).
-Deterministic: every addition has a fixed order. Relative to one GPU, only the association of
-the routed sum changes (per-rank partial sums, then the ranks in order).
+No host synchronisation: every size is known from T and W, so the whole layer is a fixed
+sequence of kernels and collectives (capturable in a CUDA graph). Deterministic: every
+addition has a fixed order. Relative to one GPU, only the association of the routed sum
+changes (per-rank partial sums, then the ranks in order).
 
 ``route_fn`` / ``experts_fn`` can be replaced (the CPU tests run this exact dispatch/combine code
 on gloo ranks with oracle-backed stage functions).
@@ -46,12 +49,13 @@ def device_route_fn(layer, ws):
 
 
 def device_experts_fn(layer, ws):
-    """``b200moe_moe_experts`` for pre-routed tokens and an expert range."""
-    def experts(x16, ids, wb, e_lo, e_hi, sg, out, accumulate=False):
+    """``b200moe_moe_experts`` for pre-routed tokens, an expert range and the shared-expert rows
+    ``sh_rows`` = (lo, hi) (sg[t - lo] applies to row t; default all rows)."""
+    def experts(x16, ids, wb, e_lo, e_hi, sg, out, accumulate=False, sh_rows=None):
         T = x16.shape[0]
         if T == 0:
             return out
-        _abi.moe_experts(x16, T, ids, wb, e_lo, e_hi, sg, layer.abi(), out, accumulate, ws(T))
+        _abi.moe_experts(x16, T, ids, wb, e_lo, e_hi, sg, layer.abi(), out, accumulate, ws(T), sh_rows=sh_rows)
         return out
     return experts
 
@@ -83,57 +87,31 @@ class ExpertParallelMoE:
         return ws
 
     def forward(self, x=None, resid=None):
-        """``x`` [T_local, 2048] (bf16/f32) -> (out [T_local, 2048] f32, ids [T_local, 8]).
-        With ``resid`` instead of ``x``: routes rmsnorm(resid) and returns resid + out."""
+        """``x`` [T, 2048] (bf16/f32) -> (out [T, 2048] f32, ids [T, 8]); T is the same on every
+        rank. With ``resid`` instead of ``x``: routes rmsnorm(resid) and returns resid + out."""
         x16, ids, wb, sg = self.route_fn(x, resid) if resid is not None else self.route_fn(x)
         T = x16.shape[0]
         W = self.world
-        dest = torch.div(ids, self.per, rounding_mode="floor")
-        send_tok, send_ids = [], []
-        for r in range(W):
-            m = dest == r
-            tok = m.any(dim=1).nonzero().flatten()
-            send_tok.append(tok)
-            send_ids.append(torch.where(m[tok], ids[tok], torch.full_like(ids[tok], -1)))
-        send_counts = [int(t.numel()) for t in send_tok]
-        if W > 1:
-            cnt = torch.tensor(send_counts, dtype=torch.int64, device=self.device)
-            rcnt = torch.empty_like(cnt)
-            dist.all_to_all_single(rcnt, cnt, group=self.group)
-            recv_counts = [int(c) for c in rcnt.tolist()]
-        else:
-            recv_counts = list(send_counts)
-        R = sum(recv_counts)
-        x_send = torch.cat([x16[t] for t in send_tok]) if T else x16[:0]
-        i_send = torch.cat(send_ids) if T else ids[:0]
-        w_send = torch.cat([wb[t] for t in send_tok]) if T else wb[:0]
-        x_recv = torch.empty((R, H), dtype=x16.dtype, device=self.device)
-        i_recv = torch.empty((R, TOPK), dtype=ids.dtype, device=self.device)
-        w_recv = torch.empty((R, TOPK), dtype=wb.dtype, device=self.device)
-        for dst, src in ((x_recv, x_send), (i_recv, i_send), (w_recv, w_send)):
-            # rows travel as raw bytes (every backend moves uint8; not every one moves fp16)
-            if W > 1:
-                dist.all_to_all_single(dst.view(torch.uint8), src.contiguous().view(torch.uint8), recv_counts,
-                                       send_counts, group=self.group)
-            else:
-                dst.copy_(src)
-        partial = torch.zeros((R, H), dtype=torch.float32, device=self.device)
-        self.experts_fn(x_recv, i_recv, w_recv, self.e_lo, self.e_hi, None, partial)
-        if W > 1:
-            back = torch.empty((sum(send_counts), H), dtype=torch.float32, device=self.device)
-            dist.all_to_all_single(back, partial, send_counts, recv_counts, group=self.group)
-        else:
-            back = partial
-        acc = torch.zeros((T, H), dtype=torch.float32, device=self.device)
-        off = 0
-        for r in range(W):            # ascending rank = ascending expert range; indices unique per r
-            n = send_counts[r]
-            if n:
-                acc.index_add_(0, send_tok[r], back[off:off + n])
-            off += n
         out = torch.zeros((T, H), dtype=torch.float32, device=self.device)
-        self.experts_fn(x16, ids, wb, 0, 0, sg, out)        # sg * shared expert only
-        out = acc + out
+        if W == 1:  # every expert is local: routed + shared in one stage call
+            self.experts_fn(x16, ids, wb, 0, E, sg, out)
+        else:
+            # dispatch: all tokens to every rank (rows travel as raw bytes: every backend moves
+            # uint8, not every one moves fp16)
+            xg = torch.empty((W * T, H), dtype=x16.dtype, device=self.device)
+            ig = torch.empty((W * T, TOPK), dtype=ids.dtype, device=self.device)
+            wg = torch.empty((W * T, TOPK), dtype=wb.dtype, device=self.device)
+            for dst, src in ((xg, x16), (ig, ids), (wg, wb)):
+                dist.all_gather_into_tensor(dst.view(torch.uint8), src.contiguous().view(torch.uint8),
+                                            group=self.group)
+            partial = torch.empty((W * T, H), dtype=torch.float32, device=self.device)
+            own = (self.rank * T, (self.rank + 1) * T)  # this rank's rows get sg * shared expert
+            self.experts_fn(xg, ig, wg, self.e_lo, self.e_hi, sg, partial, sh_rows=own)
+            back = torch.empty((W, T, H), dtype=torch.float32, device=self.device)
+            dist.all_to_all_single(back.view(torch.uint8), partial.view(torch.uint8), group=self.group)
+            out = back[0].clone()
+            for r in range(1, W):  # ascending rank = ascending expert range
+                out += back[r]
         if resid is not None:
             resid += out
             return resid, ids

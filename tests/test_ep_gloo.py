@@ -44,18 +44,19 @@ def _stage_fns():
         return (torch.from_numpy(xf.astype(np.float16)), torch.from_numpy(r["ids"].astype(np.int32)),
                 torch.from_numpy(r["w_bf16"].view(np.int16).copy()), torch.from_numpy(sg))
 
-    def experts(x16, ids, wb, e_lo, e_hi, sg, out, accumulate=False):
+    def experts(x16, ids, wb, e_lo, e_hi, sg, out, accumulate=False, sh_rows=None):
         x = x16.numpy().astype(np.float64)
         idn = ids.numpy()
         w = bf16_bits_to_f32(wb.numpy().view(np.uint16)).astype(np.float64)
         res = np.zeros_like(x)
+        lo, hi = sh_rows if sh_rows is not None else (0, x.shape[0])
         for t in range(x.shape[0]):
             for k in np.argsort(idn[t], kind="stable"):
                 e = int(idn[t, k])
                 if e_lo <= e < e_hi:
                     res[t] += w[t, k] * (x[t] * (1.0 + e / 256.0) + e / 64.0)
-            if sg is not None:
-                res[t] += float(sg[t]) * (x[t] * 0.5)
+            if sg is not None and lo <= t < hi:
+                res[t] += float(sg[t - lo]) * (x[t] * 0.5)
         r32 = torch.from_numpy(res.astype(np.float32))
         if accumulate:
             out += r32
