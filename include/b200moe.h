@@ -110,7 +110,7 @@ int b200moe_moe_decode(const void *x, int x_dtype, int T, const b200moe_layer *l
  * on each device looks up the array's device address (cudaGetSymbolAddress), so make that
  * first call before any stream capture. All calls on a device share the one array: calls
  * that can overlap on the GPU (different streams without ordering) race on it and must be
- * serialised by the caller. The path keeps nothing that must start at zero between calls.
+ * serialised by the caller. Whatever must start at zero is cleared by each call itself.
  * Allocates nothing (no cudaMalloc / cudaFree, no allocating library routine). */
 int b200moe_moe_decode_noalloc(const void *x, int x_dtype, int T, const b200moe_layer *layer,
                                float *out, int32_t *ids_out, uint16_t *w_out, void *stream);
