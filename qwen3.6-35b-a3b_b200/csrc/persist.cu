@@ -14,8 +14,8 @@
 //      the CTA's two router rows and the gate row (staged in shared memory one layer ahead)
 //      -> published logit pair.                                                   exchange 1
 //   S  top 8 (R3); the CTA issues the bulk copies of its routed rows of this layer at once --
-//      its 32 gate and 32 up rows in 4 chunks (one mbarrier each) and its 16 down rows of each
-//      of the 8 experts -- then finishes R2, R4, R5.
+//      its 32 gate and 32 up rows in 8 chunks (one mbarrier each), then its 16 down rows of
+//      each of the 8 experts -- then finishes R2, R4, R5.
 //   G  s = silu(gate . x) * (up . x) for its 4 shared-expert pairs (prefetched one layer
 //      ahead) and 32 routed pairs, chunk by chunk as they land -> published s.  exchange 2
 //   D  o[k][h] = down_k[h] . s_k for the 9 experts and its 16 h rows; combine in ascending
@@ -66,8 +66,8 @@ constexpr int kHr = kH / kN;             // 16 down rows per CTA
 constexpr int kRowPair = 2 * kRowUp;     // 2304 B: gate row + up row
 constexpr int kRouterRowBytes = kH * 2;  // 4096 B of bf16
 constexpr int kRtRows = 3;               // per layer: the CTA's 2 router rows + the gate row
-constexpr int kGuChunks = 4;             // routed gate/up arrival chunks (one mbarrier each)
-constexpr int kGuChunk = kQ / kGuChunks; // 8 row pairs per chunk
+constexpr int kGuChunks = 8;             // routed gate/up arrival chunks (one mbarrier each)
+constexpr int kGuChunk = kQ / kGuChunks; // 4 row pairs per chunk
 constexpr int kPadSeg = 68;              // padded pitch of a 64-float segment
 constexpr int kResPad = kH / 64 * kPadSeg;  // 2176 floats
 
@@ -113,12 +113,6 @@ constexpr int kSmem = kOffBar + 256;
 __device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t *p) {
   uint32_t v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t *p) {
-  uint64_t v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -478,6 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       __syncthreads();
     }
     if (tid == 0 && !last) issue_router_rows(l + 1);
+    __syncwarp();
     float rs = 1.0f;  // every warp derives the RMSNorm scale itself (identical bits, no barrier)
     if (P.resid) {    // sum of squares in the declared chunk order
       const float *v = res_s + lane * kPadSeg;
@@ -524,21 +519,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
         armed |= (((1u << kGuChunks) - 1u) << kBarGu0) | (1u << kBarDn);
       }
       __syncwarp();
-      // Routed bulk copies, one per lane: lanes 0..7 -> chunk lane >> 1 of the gate (even) or
-      // up (odd) rows of this CTA's expert; lanes 8..15 -> the 16 down rows of slot lane - 8.
-      const int k = lane < 8 ? slot_c : (lane - 8) & 7;
+      // Routed bulk copies, one per lane, in the order they are consumed: lanes 0..15 -> chunk
+      // lane >> 1 of the gate (even) or up (odd) rows of this CTA's expert; lanes 16..23 -> the
+      // 16 down rows of slot lane - 16 (not needed before the s exchange).
+      const int k = lane < 2 * kGuChunks ? slot_c : (lane - 2 * kGuChunks) & 7;
       const int e = __shfl_sync(0xFFFFFFFFu, my_sel, k);
-      if (lane < 8) {
+      if (lane < 2 * kGuChunks) {
         const int g = lane >> 1, which = lane & 1;
         const uint8_t *src = (const uint8_t *)(which ? Lp.up : Lp.gate) + (size_t)e * Lp.gate_up_expert_stride +
                              (size_t)(j_c + g * kGuChunk) * kRowUp;
         bulk_g2s((which ? gu_u : gu_g) + g * kGuChunk * kRowUp, src, kGuChunk * kRowUp, bar + kBarGu0 + g,
                  pol_first);
-      } else if (lane < 16) {
+      }
+      __syncwarp();
+      if (lane >= 2 * kGuChunks && lane < 2 * kGuChunks + kK) {
         const uint8_t *src =
             (const uint8_t *)Lp.down + (size_t)e * Lp.down_expert_stride + (size_t)(kHr * c) * kRowDown;
         bulk_g2s(dn + (size_t)k * kHr * kRowDown, src, kHr * kRowDown, bar + kBarDn, pol_first);
       }
+      __syncwarp();
       route_finish(rw, mine, rr);  // R2, R4, R5 while the rows stream in
       if (c == 0 && lane < kK) {
         if (P.ids_out) P.ids_out[(size_t)l * kK + lane] = rr->ids[lane];
@@ -546,15 +545,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       }
     }
     // ---------------------------------------------------------------- phase G
-    {  // warps 1..11 (warp 0 routes above), two row pairs per iteration; shared pairs first
+    {  // warps 1..11 (warp 0 routes above), two adjacent row pairs per iteration, in arrival
+       // order: items 0..3 are the shared pairs (prefetched), items 4..35 the routed pairs in
+       // chunk order; warp w takes items 2(w-1), 2(w-1)+1, then the same 22 items later
       uint32_t have = 0;  // bit 0: shared, bit 1 + g: routed chunk g
       if (warp > 0) {
+        __syncwarp();
         XChunk X0, X1;
         xchunk_pad(res_s, rs, kb0, cc, X0);
         xchunk_pad(res_s, rs, kb0 + 4, cc, X1);
-        constexpr int kStep = kWarps - 1;
-        for (int ia = warp - 1; ia < kJ + kQ && !fail; ia += 2 * kStep) {
-          const int ib = ia + kStep;  // the second pair of this iteration (if any)
+        constexpr int kStep = 2 * (kWarps - 1);
+        for (int ia = 2 * (warp - 1); ia < kJ + kQ && !fail; ia += kStep) {
+          const int ib = ia + 1;  // the second pair of this iteration (if any)
           const bool two = ib < kJ + kQ;
           uint32_t need = 1u << (ia < kJ ? 0 : 1 + (ia - kJ) / kGuChunk);
           if (two) need |= 1u << (ib < kJ ? 0 : 1 + (ib - kJ) / kGuChunk);
@@ -626,6 +628,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
     fail = !wait_bar(kBarShDn) || fail;
     if (__syncthreads_or(fail)) { aborted = true; break; }
     if (warp <= kK) {
+      // reconverge the warp first: thread 0's solo branches (copy issue, barrier arming) can
+      // leave warp 0 split, and a split warp runs this loop once per part
+      __syncwarp();
       const int slot = warp;  // warps 0..8: routed slots 0..7, shared expert 8
       const int half = lane >> 4, kb = (lane >> 3) & 1;
       XChunk X;
