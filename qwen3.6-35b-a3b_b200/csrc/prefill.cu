@@ -8,11 +8,14 @@
 //   k_count       per token: the slots whose expert is in the requested range, and their order
 //   k_plan        one CTA: packed row offsets per expert (the shared expert is expert 256 with
 //                 every token), 256-token chunks, and the GEMM tile tables
-//   k_fill        CTA per expert: that expert's (token, slot) assignments in ascending order
+//   k_fill        CTA per expert: that expert's (token, slot) assignments in ascending order,
+//                 and each assignment's row position (inv)
+//   k_gather_x    the x16 rows in assignment-list order (the gate_up GEMM's B operand)
 //   k_gemm<1>     gate_up: D[128 gate rows | 128 up rows][tokens] = W . x^T, s = silu(g)*u -> fp16
-//   k_gemm<2>     down:    D[128 h rows][tokens] = W_d . s^T -> y[assignment][h] = o * w (routed)
-//                 or ysh[token][h] = o (shared)
-//   k_combine     out[t] = sum over the in-range slots in ascending expert id of y (+ sg * ysh)
+//   k_gemm<2>     down:    D[128 h rows][tokens] = W_d . s^T -> y[position][h] = o * w (routed)
+//                 or o (shared): every tile writes contiguous rows
+//   k_combine     out[t] = sum over the in-range slots in ascending expert id of y[inv] (+ sg * the
+//                 shared row)
 //
 // Entry points: b200moe_moe_route (the first three kernels), b200moe_moe_experts (the rest,
 // for pre-routed tokens and an expert range: the expert-parallel building block) and
@@ -22,7 +25,11 @@
 // expert's tokens (<= 256, padded to a multiple of 16) in N, so a ragged expert wastes at most
 // 15 token columns. Weights are Q4_K in HBM; producer warps dequantise each 128 x 64 K-slab to
 // fp16 in shared memory (half2 math: exact integer quants, fp16 sub-block scale and min), token
-// rows arrive by cp.async; one thread issues tcgen05.mma into TMEM; four warps drain TMEM.
+// rows arrive by TMA; one thread issues tcgen05.mma into TMEM; four warps drain TMEM.
+#include <cuda.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "route.cuh"
 #include "tc.cuh"
@@ -47,12 +54,13 @@ struct PrefillWS {
   int32_t *counts;   // [257]
   int32_t *offsets;  // [258]
   int32_t *plist;    // [9T]
+  __half *x16p;      // [9T][2048] the gate_up GEMM's B rows: x16 rows in assignment-list order
   int4 *tiles1;
   int4 *tiles2;
   int32_t *ntiles;   // [2]
   __half *s16;       // [9T][512]
-  float *y;          // [8T][2048]
-  float *ysh;        // [T][2048]
+  float *y;          // [9T][2048] down outputs by row position (routed: times the routing weight)
+  int32_t *inv;      // [8T] row position of assignment t * 8 + slot (in-range experts only)
   int32_t *err;      // [1]
 };
 
@@ -64,8 +72,8 @@ size_t prefill_ws_bytes(int T) {
   const size_t t = (size_t)T, mc = max_chunks(T);
   return al256(t * kH * 4) + al256(t * kH * 2) + al256(t * kE * 2) + al256(t * 4) + al256(t * kK * 4) +
          al256(t * kK * 2) + al256(t * kK * 4) + al256(kNE * 4) + al256((kNE + 1) * 4) + al256(9 * t * 4) +
-         al256(mc * 4 * 16) + al256(mc * 16 * 16) + al256(2 * 4) + al256(9 * t * kI * 2) + al256(8 * t * kH * 4) +
-         al256(t * kH * 4) + al256(4);
+         al256(9 * t * kH * 2) + al256(mc * 4 * 16) + al256(mc * 16 * 16) + al256(2 * 4) + al256(9 * t * kI * 2) +
+         al256(9 * t * kH * 4) + al256(8 * t * 4) + al256(4);
 }
 
 PrefillWS carve_prefill(void *ws, int T) {
@@ -83,12 +91,13 @@ PrefillWS carve_prefill(void *ws, int T) {
   w.counts = (int32_t *)take(kNE * 4);
   w.offsets = (int32_t *)take((kNE + 1) * 4);
   w.plist = (int32_t *)take(9 * t * 4);
+  w.x16p = (__half *)take(9 * t * kH * 2);
   w.tiles1 = (int4 *)take(mc * 4 * 16);
   w.tiles2 = (int4 *)take(mc * 16 * 16);
   w.ntiles = (int32_t *)take(2 * 4);
   w.s16 = (__half *)take(9 * t * kI * 2);
-  w.y = (float *)take(8 * t * kH * 4);
-  w.ysh = (float *)take(t * kH * 4);
+  w.y = (float *)take(9 * t * kH * 4);
+  w.inv = (int32_t *)take(8 * t * 4);
   w.err = (int32_t *)take(4);
   return w;
 }
@@ -313,7 +322,8 @@ __global__ void __launch_bounds__(512) k_plan(int n_shared, const int32_t *count
 
 // ------------------------------------------------------------------------- k_fill
 __global__ void __launch_bounds__(1024) k_fill(int T, int sh_lo, int sh_hi, const int32_t *ids,
-                                                const int32_t *counts, const int32_t *offsets, int32_t *plist) {
+                                                const int32_t *counts, const int32_t *offsets, int32_t *plist,
+                                                int32_t *inv) {
   __shared__ int wcount[32];
   __shared__ int running;
   const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
@@ -338,39 +348,74 @@ __global__ void __launch_bounds__(1024) k_fill(int T, int sh_lo, int sh_hi, cons
       if (i < w) before += c;
       total += c;
     }
-    if (f) dst[running + before + __popc(bal & ((1u << lane) - 1u))] = a;
+    if (f) {
+      const int q = running + before + __popc(bal & ((1u << lane) - 1u));
+      dst[q] = a;
+      inv[a] = offsets[e] + q;
+    }
     __syncthreads();
     if (tid == 0) running += total;
     __syncthreads();
   }
 }
 
+// ------------------------------------------------------------------------- k_gather_x
+// x16p[pos] = x16[token of assignment-list entry pos], one warp per row (4 KB), so the gate_up
+// GEMM reads its B operand as contiguous 64-row TMA boxes. Rows from offsets[kE] on belong to
+// the shared expert (entries are token ids); the others hold t * 8 + slot.
+__global__ void __launch_bounds__(256) k_gather_x(int max_rows, const int32_t *offsets, const int32_t *plist,
+                                                  const __half *x16, __half *x16p) {
+  const int total = __ldg(offsets + kNE), sh0 = __ldg(offsets + kE);
+  const int lane = threadIdx.x & 31;
+  for (int pos = (blockIdx.x * 256 + threadIdx.x) >> 5; pos < total && pos < max_rows; pos += gridDim.x * 8) {
+    const int pl = __ldg(plist + pos);
+    const int t = pos >= sh0 ? pl : (pl >> 3);
+    const uint4 *src = reinterpret_cast<const uint4 *>(x16 + (size_t)t * kH);
+    uint4 *dst = reinterpret_cast<uint4 *>(x16p + (size_t)pos * kH);
+#pragma unroll
+    for (int i = 0; i < kH / 8 / 32; ++i) dst[lane + 32 * i] = __ldg(src + lane + 32 * i);
+  }
+}
+
 // ------------------------------------------------------------------------- grouped GEMM
 // Block of 15 warps, each with one job:
-//   warps 0-3    epilogue: TMEM lanes 32w..32w+31 -> s (gate_up) or y / ysh (down)
+//   warps 0-3    epilogue: TMEM lanes 32w..32w+31 -> s (gate_up) or y (down)
 //   warps 4-11   dequant: raw Q4_K slab (shared memory) -> fp16 A tile of the K-slab
 //   warp 12      TMEM allocation; lane 0 issues tcgen05.mma and the commits
-//   warps 13-14  B loaders: the tile's token rows (x16 gathered through the assignment list,
-//                or the contiguous s rows) -> B ring by cp.async, completion signalled with
-//                cp.async.mbarrier.arrive.noinc
-// One iteration = one K-slab of 64 of one tile; every role walks the same (tile, slab)
-// sequence: tile = blockIdx.x + j * gridDim.x, slab = 0 .. kKS-1.
+//   warp 13      raw producer (lane 0): per K-slab and 128-row weight tile, two TMA loads of
+//                the Q4_K bytes -- the 16-byte block headers and the slab's 32 quant bytes of
+//                all 128 rows -- through 3-D tensor maps (bytes, row, expert)
+//   warp 14      B producer (lane 0): the tile's token rows -> B ring as 64-row TMA boxes,
+//                128-byte swizzled, from the contiguous rows of x16p (gate_up: x in
+//                assignment-list order) or s16 (down). (Gathering the x16 rows per K-slab -- TMA
+//                gather4 per 4 rows, or 16-byte cp.async -- was tried: one SM sustains only
+//                ~7-11 B/cycle of such small requests, a third of what the MMA consumes.)
+// No load is multicast. One iteration = one K-slab of 64 of one tile; every role walks the
+// same (tile, slab) sequence: tile = blockIdx.x + j * gridDim.x, slab = 0 .. kKS-1.
 //
-// Three rings, each with full/empty mbarriers (empties are committed by the MMA thread):
-//   A ring   kAStages x kA x 16 KB     filled by the dequant warps (8 warp arrivals)
-//   B ring   kBStages x 32 KB          filled by the loaders (64 asynchronous arrivals)
-//   raw ring kRStages x 256 x 48 B     private per dequant thread: its row's 16-byte block
-//            header and the slab's 32 quant bytes, prefetched kRStages-1 slabs ahead with
-//            cp.async (only the issuing thread reads them: no cross-thread wait)
+// Three rings, each with full/empty mbarriers:
+//   A ring   kAStages x kA x 16 KB   written by the dequant warps (8 arrivals); emptied by the
+//                                    MMA commit
+//   B ring   kBStages x 32 KB        TMA bytes (one arming arrival); emptied by the MMA commit
+//   raw ring kRStages x kA x 6 KB    TMA bytes (one arming arrival); emptied by the 8 dequant
+//                                    warps once their rows are in registers
 // The down GEMM double-buffers its 256-column accumulator so the epilogue of one tile
 // overlaps the next tile's main loop; gate_up uses all 512 columns for one tile.
-constexpr int kEpiWarps = 4, kDqWarps = 8, kLdWarps = 2;
+//
+// Epilogue writes go out as TMA tensor stores: a warp stages its 32 rows x 16 tokens in
+// shared memory (double-buffered) and lane 0 stores them as one 16-row box of s16 / y rows
+// (a tile's rows are contiguous row positions). A ragged last chunk is split into 8-, 4-, 2-
+// and 1-row boxes, so no store reaches past the tile into another expert's rows. (Plain
+// per-column 128-byte stores ran at ~6 B/cycle per SM: the epilogue, not the MMA, bounded
+// the down GEMM.)
+constexpr int kEpiWarps = 4, kDqWarps = 8;
 constexpr int kDqThreads = 32 * kDqWarps;
-constexpr int kLdThreads = 32 * kLdWarps;
 constexpr int kMmaWarp = kEpiWarps + kDqWarps;  // 12
-constexpr int kLdWarp0 = kMmaWarp + 1;          // 13
-constexpr int kGemmThreads = 32 * (kLdWarp0 + kLdWarps);  // 480
-constexpr int kRawSlab = 48;                    // header 16 B + one slab's quants 32 B
+constexpr int kRawWarp = kMmaWarp + 1;          // 13
+constexpr int kBWarp = kRawWarp + 1;            // 14
+constexpr int kGemmThreads = 32 * (kBWarp + 1);  // 480
+constexpr int kRawHdr = 128 * 16;               // per 128-row tile: the rows' block headers
+constexpr int kRawTile = kRawHdr + 128 * 32;    // + the rows' 32 quant bytes of the slab
 
 template <int kMode>
 struct GemmCfg {
@@ -383,41 +428,44 @@ struct GemmCfg {
   static constexpr int kRStages = 4;
   static constexpr int kATile = 128 * 128;                      // 128 rows x 128 B
   static constexpr int kBTile = kChunk * 128;                   // 256 rows x 128 B
-  static constexpr int kRawStage = kDqThreads * kRawSlab;
+  static constexpr int kRawStage = kA * kRawTile;
   static constexpr int kNBuf = kMode == 1 ? 1 : 2;              // TMEM accumulator buffers
   static constexpr uint32_t kAccCols = kMode == 1 ? 512 : 256;  // columns per buffer
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr int kOffB = kAStages * kA * kATile;
-  static constexpr int kOffRaw = kOffB + kBStages * kBTile;
-  static constexpr int kOffMeta = kOffRaw + kRStages * kRawStage;       // epilogue column metadata
-  static constexpr int kOffTok = kOffMeta + kEpiWarps * kChunk * 8;      // loader token indices
-  static constexpr int kOffBar = kOffTok + kChunk * 4;
+  static constexpr int kOffB = 0;                                       // 1024-aligned stages
+  static constexpr int kOffA = kOffB + kBStages * kBTile;
+  static constexpr int kOffRaw = kOffA + kAStages * kA * kATile;
+  static constexpr int kOffMeta = kOffRaw + kRStages * kRawStage;       // epilogue routing weights
+  static constexpr int kStageBytes = 16 * 32 * (kMode == 1 ? 2 : 4);     // one warp's staged chunk
+  static constexpr int kOffStage = kOffMeta + kEpiWarps * kChunk * 4;    // [4 warps][2][16 x 32]
+  static constexpr int kOffBar = kOffStage + kEpiWarps * 2 * kStageBytes;
   static constexpr size_t kSmem = (size_t)kOffBar + 512 + 1024;         // + barriers, + alignment
 };
 
+// Tensor maps of one launch (kernel parameter space; each 64-byte aligned).
+struct GemmMaps {
+  CUtensorMap hdr[2][2];  // [routed, shared][A tile: gate|down, up] -> block headers
+  CUtensorMap qnt[2][2];  // same weights -> the 32 quant bytes of a slab
+  CUtensorMap b;          // B rows (box 64 x 64, 128-byte swizzle): x16p (gate_up) or s16 (down)
+  CUtensorMap st[5];      // epilogue stores into s16 (gate_up) or y (down): box 32 x 16, 8, 4, 2, 1
+};
+
 struct GemmParams {
-  const uint8_t *wa0;  // MODE1 gate / MODE2 down (routed)
-  const uint8_t *wa1;  // MODE1 up (routed)
-  int64_t stride;      // expert stride of wa0/wa1
-  const uint8_t *sh0;  // shared gate / shared down
-  const uint8_t *sh1;  // shared up
+  GemmMaps m;
   const int4 *tiles;
   const int32_t *ntiles;
   const int32_t *plist;
-  const __half *x16;
   __half *s16;
   const uint16_t *wb;
   float *y;
-  float *ysh;
   int32_t *err;
 };
 
 // Half (h = 0: low nibbles, sub-block 2g; h = 1: high nibbles, sub-block 2g+1) of K-slab g of
-// one Q4_K block row -> 4 chunks (16 B each) of the A tile row.
-__device__ __forceinline__ void dequant_half(const uint8_t *raw, int g, int h, uint8_t *tile, int row) {
-  const uint4 hd = *reinterpret_cast<const uint4 *>(raw);
-  const uint4 q0 = *reinterpret_cast<const uint4 *>(raw + 16);
-  const uint4 q1 = *reinterpret_cast<const uint4 *>(raw + 32);
+// one Q4_K block row -> 4 chunks (16 B each) of the A tile row. hd: the block header; q0, q1:
+// the slab's 32 quant bytes.
+__device__ __forceinline__ void dequant_half(const uint4 &hd, const uint4 &q0, const uint4 &q1, int g, int h,
+                                             uint8_t *tile, int row) {
   float s0, m0, s1, m1;
   q4k_scales(hd, 2 * g, s0, m0, s1, m1);
   const __half2 S = __float2half2_rn(h ? s1 : s0), M = __float2half2_rn(h ? -m1 : -m0);
@@ -440,42 +488,22 @@ __device__ __forceinline__ void dequant_half(const uint8_t *raw, int g, int h, u
   }
 }
 
-// Base of weight row `row` (0 .. kARows-1) of tile (e, wt).
 template <int kMode>
-__device__ __forceinline__ const uint8_t *tile_row(const GemmParams &P, int e, int wt, int row) {
-  if (kMode == 1) {
-    const bool up = row >= 128;
-    const uint8_t *base = e < kE ? (up ? P.wa1 : P.wa0) + (size_t)e * P.stride : (up ? P.sh1 : P.sh0);
-    return base + (size_t)(wt * 128 + (row & 127)) * kRowUp;
-  }
-  const uint8_t *base = e < kE ? P.wa0 + (size_t)e * P.stride : P.sh0;
-  return base + (size_t)(wt * 128 + row) * kRowDown;
-}
-
-// Raw bytes of K-slab ks of one weight row -> 48-byte slot: block header, then the slab's quants.
-__device__ __forceinline__ void issue_raw_slab(const uint8_t *rowp, int ks, uint8_t *dst) {
-  const uint8_t *blk = rowp + (ks >> 2) * kQB;
-  cp_async16(dst, blk, 16u);
-  cp_async16(dst + 16, blk + 16 + 32 * (ks & 3), 16u);
-  cp_async16(dst + 32, blk + 32 + 32 * (ks & 3), 16u);
-}
-
-template <int kMode>
-__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(GemmParams P) {
+__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant__ GemmParams P) {
   using C = GemmCfg<kMode>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t *a_ring = smem;
   uint8_t *b_ring = smem + C::kOffB;
+  uint8_t *a_ring = smem + C::kOffA;
   uint8_t *raw_ring = smem + C::kOffRaw;
-  int *col_pl = (int *)(smem + C::kOffMeta);                // [4][kChunk] per epilogue warp
-  float *col_w = (float *)(col_pl + kEpiWarps * kChunk);     // [4][kChunk] per epilogue warp
-  int *tok_s = (int *)(smem + C::kOffTok);                   // [kChunk] loader rows' token ids
+  float *col_w = (float *)(smem + C::kOffMeta);              // [4][kChunk] per epilogue warp
   uint64_t *a_full = (uint64_t *)(smem + C::kOffBar);
   uint64_t *a_empty = a_full + C::kAStages;
   uint64_t *b_full = a_empty + C::kAStages;
   uint64_t *b_empty = b_full + C::kBStages;
-  uint64_t *acc_full = b_empty + C::kBStages;   // [kNBuf]
+  uint64_t *r_full = b_empty + C::kBStages;     // [kRStages]
+  uint64_t *r_empty = r_full + C::kRStages;     // [kRStages]
+  uint64_t *acc_full = r_empty + C::kRStages;   // [kNBuf]
   uint64_t *acc_empty = acc_full + C::kNBuf;    // [kNBuf]
   uint64_t *drain = acc_empty + C::kNBuf;
   uint32_t *tmem_slot = (uint32_t *)(drain + 1);
@@ -486,8 +514,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(GemmParams P) {
       mbar_init(a_empty + s, 1);
     }
     for (int s = 0; s < C::kBStages; ++s) {
-      mbar_init(b_full + s, kLdThreads);  // one asynchronous (cp.async) arrival per loader thread
+      mbar_init(b_full + s, 1);  // the producer's arming arrival (+ the TMA bytes)
       mbar_init(b_empty + s, 1);
+    }
+    for (int s = 0; s < C::kRStages; ++s) {
+      mbar_init(r_full + s, 1);
+      mbar_init(r_empty + s, kDqWarps);
     }
     for (int b = 0; b < C::kNBuf; ++b) {
       mbar_init(acc_full + b, 1);
@@ -512,80 +544,73 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(GemmParams P) {
   if (warp >= kEpiWarps && warp < kMmaWarp) {  // ----------------------------- dequant
     const int pt = threadIdx.x - 32 * kEpiWarps;
     const int row = pt / C::kTpr, half = pt % C::kTpr;  // kTpr == 1: this thread does both halves
-    uint8_t *myraw = raw_ring + pt * kRawSlab;
-    auto raw_src = [&](uint32_t j) -> const uint8_t * {  // row base for iteration j
-      const int4 tl = __ldg(P.tiles + blockIdx.x + (j / C::kKS) * gridDim.x);
-      return tile_row<kMode>(P, tl.x, tl.w, row);
-    };
-    // prologue: raw slabs of iterations 0 .. kRStages-2
-    for (uint32_t j = 0; j + 1 < (uint32_t)C::kRStages; ++j) {
-      if (j < n_it) issue_raw_slab(raw_src(j), j % C::kKS, myraw + (j % C::kRStages) * C::kRawStage);
-      cp_async_commit();
-    }
-    const uint8_t *rowp = nullptr;
+    const int tl = row >> 7, tr = row & 127;               // A tile, row within it
     for (uint32_t it = 0; it < n_it && ok; ++it) {
       const int ks = it % C::kKS;
-      const int s = it % C::kAStages;
-      const uint32_t j = it + C::kRStages - 1;  // slab to prefetch this iteration
-      if (j < n_it) {
-        if (j % C::kKS == 0 || rowp == nullptr) rowp = raw_src(j);
-        issue_raw_slab(rowp, j % C::kKS, myraw + (j % C::kRStages) * C::kRawStage);
-      }
-      cp_async_commit();
-      cp_async_wait_group<C::kRStages - 1>();  // iteration it's slab has landed
-      // warp-uniform outcome: a lane that timed out never leaves its warp behind in __syncwarp
+      const int s = it % C::kAStages, rs = it % C::kRStages;
+      // warp-uniform outcomes: a lane that timed out never leaves its warp behind in __syncwarp
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(r_full + rs, (it / C::kRStages) & 1))) { ok = false; break; }
+      const uint8_t *rt = raw_ring + rs * C::kRawStage + tl * kRawTile;
+      const uint4 hd = *reinterpret_cast<const uint4 *>(rt + tr * 16);
+      const uint4 q0 = *reinterpret_cast<const uint4 *>(rt + kRawHdr + tr * 32);
+      const uint4 q1 = *reinterpret_cast<const uint4 *>(rt + kRawHdr + tr * 32 + 16);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(r_empty + rs);  // this warp's rows are in registers
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(a_empty + s, ((it / C::kAStages) & 1) ^ 1))) { ok = false; break; }
-      uint8_t *at = a_ring + s * (C::kA * C::kATile) + (row >> 7) * C::kATile;
-      const uint8_t *rs = myraw + (it % C::kRStages) * C::kRawStage;
+      uint8_t *at = a_ring + s * (C::kA * C::kATile) + tl * C::kATile;
       if (C::kTpr == 1) {
-        dequant_half(rs, ks & 3, 0, at, row & 127);
-        dequant_half(rs, ks & 3, 1, at, row & 127);
+        dequant_half(hd, q0, q1, ks & 3, 0, at, tr);
+        dequant_half(hd, q0, q1, ks & 3, 1, at, tr);
       } else {
-        dequant_half(rs, ks & 3, half, at, row & 127);
+        dequant_half(hd, q0, q1, ks & 3, half, at, tr);
       }
       fence_proxy_async_smem();  // this thread's generic smem writes -> async proxy
       __syncwarp();
       if (lane == 0) mbar_arrive(a_full + s);
     }
-    cp_async_wait_all();
-  } else if (warp >= kLdWarp0) {  // ------------------------------------------ B loaders
-    const int lw = warp - kLdWarp0;
-    const int kc = lane & 7, rsub = lane >> 3;  // 16-byte chunk of the slab row; row within 4
-    int *tok = tok_s + lw * (kChunk / kLdWarps);  // this warp's rows: 128 lw .. 128 lw + 127
-    int4 tl = make_int4(0, 0, 0, 0);
-    for (uint32_t it = 0; it < n_it && ok; ++it) {
-      const int ks = it % C::kKS;
-      const int s = it % C::kBStages;
-      if (ks == 0) {  // new tile: this warp's token rows
-        tl = __ldg(P.tiles + blockIdx.x + (it / C::kKS) * gridDim.x);
-        __syncwarp();
-        for (int r = lane; r < kChunk / kLdWarps; r += 32) {
-          const int rr = lw * (kChunk / kLdWarps) + r;
-          int t = 0;
-          if (rr < tl.z) {
-            if (kMode == 1) {
-              const int pl = __ldg(P.plist + tl.y + rr);
-              t = tl.x < kE ? (pl >> 3) : pl;
-            } else {
-              t = tl.y + rr;
-            }
+  } else if (warp == kRawWarp) {  // ----------------------------------------- raw producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int ti = blockIdx.x; ti < ntiles && ok; ti += gridDim.x) {
+        const int4 tl = __ldg(P.tiles + ti);
+        const int sh = tl.x < kE ? 0 : 1, z = tl.x < kE ? tl.x : 0, y = tl.w * 128;
+        for (int ks = 0; ks < C::kKS; ++ks, ++it) {
+          const int rs = it % C::kRStages;
+          if (!mbar_wait(r_empty + rs, ((it / C::kRStages) & 1) ^ 1)) { ok = false; break; }
+          mbar_expect_tx(r_full + rs, C::kRawStage);
+          const int xh = (ks >> 2) * kQB, xq = xh + 16 + 32 * (ks & 3);
+#pragma unroll
+          for (int a = 0; a < C::kA; ++a) {
+            uint8_t *d = raw_ring + rs * C::kRawStage + a * kRawTile;
+            tma_load_3d(d, &P.m.hdr[sh][a], xh, y, z, r_full + rs);
+            tma_load_3d(d + kRawHdr, &P.m.qnt[sh][a], xq, y, z, r_full + rs);
           }
-          tok[r] = t;
         }
-        __syncwarp();
       }
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(b_empty + s, ((it / C::kBStages) & 1) ^ 1))) { ok = false; break; }
-      uint8_t *bt = b_ring + s * C::kBTile;
-      const int nrow = min(tl.z - lw * (kChunk / kLdWarps), kChunk / kLdWarps);
-      for (int r = rsub; r < nrow; r += 4) {
-        const int rr = lw * (kChunk / kLdWarps) + r;
-        const __half *src = kMode == 1 ? P.x16 + (size_t)tok[r] * kH + ks * 64 + kc * 8
-                                       : P.s16 + (size_t)tok[r] * kI + ks * 64 + kc * 8;
-        cp_async16(bt + (rr >> 3) * 1024 + kc * 128 + (rr & 7) * 16, src, 16u);
-      }
-      cp_async_mbar_arrive_noinc(b_full + s);
+      // every issued load lands before the CTA can exit (their stages' last phases complete)
+      for (uint32_t j = it > (uint32_t)C::kRStages ? it - C::kRStages : 0; j < it; ++j)
+        if (!mbar_wait(r_full + j % C::kRStages, (j / C::kRStages) & 1)) ok = false;
     }
-    cp_async_wait_all();
+    __syncwarp();
+  } else if (warp == kBWarp) {  // -------------------------------------------- B producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int ti = blockIdx.x; ti < ntiles && ok; ti += gridDim.x) {
+        const int4 tl = __ldg(P.tiles + ti);
+        const int nbox = (tl.z + 63) / 64;
+        for (int ks = 0; ks < C::kKS; ++ks, ++it) {
+          const int s = it % C::kBStages;
+          if (!mbar_wait(b_empty + s, ((it / C::kBStages) & 1) ^ 1)) { ok = false; break; }
+          mbar_expect_tx(b_full + s, (uint32_t)nbox * 64u * 128u);
+          for (int g = 0; g < nbox; ++g)
+            tma_load_2d(b_ring + s * C::kBTile + g * 64 * 128, &P.m.b, ks * 64, tl.y + 64 * g, b_full + s);
+        }
+      }
+      // every issued load lands before the CTA can exit
+      for (uint32_t j = it > (uint32_t)C::kBStages ? it - C::kBStages : 0; j < it; ++j)
+        if (!mbar_wait(b_full + j % C::kBStages, (j / C::kBStages) & 1)) ok = false;
+    }
+    __syncwarp();
   } else if (warp == kMmaWarp) {  // -------------------------------------------- MMA issue
     if (lane == 0) {
       uint32_t it = 0, tcount = 0;
@@ -601,14 +626,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(GemmParams P) {
           const int sa = it % C::kAStages, sb = it % C::kBStages;
           if (!mbar_wait(a_full + sa, (it / C::kAStages) & 1)) { ok = false; break; }
           if (!mbar_wait(b_full + sb, (it / C::kBStages) & 1)) { ok = false; break; }
-          fence_proxy_async_smem();  // cp.async (generic proxy) B rows -> tensor-core reads
           tc_fence_after();
           const uint32_t at = smem_u32(a_ring + sa * (C::kA * C::kATile));
           const uint32_t bt = smem_u32(b_ring + sb * C::kBTile);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t acc = (ks | kk) != 0;
-            const uint64_t bd = umma_desc(bt + 256 * kk);
+            const uint64_t bd = umma_desc_sw128(bt + 32 * kk);
             umma_f16(dacc, umma_desc(at + 256 * kk), bd, idesc, acc);
             if (kMode == 1) umma_f16(dacc + 256, umma_desc(at + C::kATile + 256 * kk), bd, idesc, acc);
           }
@@ -623,63 +647,81 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(GemmParams P) {
     }
     __syncwarp();
   } else {  // ---------------------------------------------------------- epilogue (warps 0-3)
-    uint32_t tcount = 0;
+    uint32_t tcount = 0, chunk = 0;
     bool range_bad = false;
-    const int row = 32 * warp + lane;  // TMEM lane = weight row within the tile
+    uint8_t *stage = smem + C::kOffStage;
     for (int ti = blockIdx.x; ti < ntiles && ok; ti += gridDim.x, ++tcount) {
       const int4 tl = __ldg(P.tiles + ti);
       const int e = tl.x, r0 = tl.y, n = tl.z, wt = tl.w;
       const int npad = (n + 15) & ~15;
       const uint32_t buf = tcount % C::kNBuf, use = tcount / C::kNBuf;
-      int *wpl = col_pl + warp * kChunk;
       float *ww = col_w + warp * kChunk;
-      if (kMode == 2) {  // this warp's copy of the tile's column metadata, loaded while the MMAs run
-        for (int c = lane; c < n; c += 32) {
-          const int pl = __ldg(P.plist + r0 + c);
-          wpl[c] = pl;
-          ww[c] = e < kE ? bf16f(__ldg(P.wb + pl)) : 1.0f;
-        }
+      if (kMode == 2) {  // this warp's copy of the tile's routing weights, loaded while the MMAs run
+        for (int c = lane; c < n; c += 32) ww[c] = e < kE ? bf16f(__ldg(P.wb + __ldg(P.plist + r0 + c))) : 1.0f;
         __syncwarp();
       }
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(acc_full + buf, use & 1))) { ok = false; break; }
       tc_fence_after();
       const uint32_t lane_addr = tmem + buf * C::kAccCols + ((uint32_t)(32 * warp) << 16);
-      for (int c0 = 0; c0 < npad; c0 += 16) {
+      const int col0 = wt * 128 + 32 * warp;  // this warp's first s16 column (gate_up) or y column (down)
+      for (int c0 = 0; c0 < npad; c0 += 16, ++chunk) {
         float a[16];
         tmem_ld16(lane_addr + c0, a);
+        float v[16];
         if (kMode == 1) {
           float u[16];
           tmem_ld16(lane_addr + 256 + c0, u);
           tmem_wait_ld();
-          const int j = wt * 128 + row;
-          __half hv[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {  // silu(g) * u, stored as s * 2^-10 (exact scaling)
             const float sil = __fdividef(a[i], 1.0f + __expf(-a[i]));
-            const float sv = sil * u[i] * kSScale;
-            if (c0 + i < n && !(fabsf(sv) <= 65504.0f)) range_bad = true;
-            hv[i] = __float2half_rn(sv);
+            v[i] = sil * u[i] * kSScale;
+            if (c0 + i < n && !(fabsf(v[i]) <= 65504.0f)) range_bad = true;
           }
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            if (c0 + i < n) P.s16[(size_t)(r0 + c0 + i) * kI + j] = hv[i];
         } else {
           tmem_wait_ld();
-          const int h = wt * 128 + row;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            if (c0 + i >= n) break;
             const float o = __fmul_rn(a[i], 1.0f / kSScale);  // undo the s storage scale (exact)
-            const int pl = wpl[c0 + i];
-            if (e < kE) P.y[(size_t)pl * kH + h] = __fmul_rn(o, ww[c0 + i]);
-            else P.ysh[(size_t)pl * kH + h] = o;
+            v[i] = (e < kE && c0 + i < n) ? __fmul_rn(o, ww[c0 + i]) : o;
           }
+        }
+        // stage [16 tokens][32 columns] in this warp's buffer (the store that read it two chunks
+        // ago has finished reading), then one box store (pieces for a ragged tail)
+        uint8_t *stg = stage + (warp * 2 + (chunk & 1)) * C::kStageBytes;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if (kMode == 1) reinterpret_cast<__half *>(stg)[i * 32 + lane] = __float2half_rn(v[i]);
+          else reinterpret_cast<float *>(stg)[i * 32 + lane] = v[i];
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int m = min(16, n - c0);
+          if (m == 16) {
+            tma_store_2d(&P.m.st[0], col0, r0 + c0, stg);
+          } else {
+            int q = 0;
+#pragma unroll
+            for (int p = 1; p < 5; ++p) {  // boxes of 8, 4, 2, 1 rows
+              const int hgt = 16 >> p;
+              if (m & hgt) {
+                tma_store_2d(&P.m.st[p], col0, r0 + c0 + q, stg + q * 32 * (kMode == 1 ? 2 : 4));
+                q += hgt;
+              }
+            }
+          }
+          bulk_commit_group();
         }
       }
       tc_fence_before();
       __syncwarp();  // also: this warp's metadata is read before the next tile overwrites it
       if (lane == 0) mbar_arrive(acc_empty + buf);
     }
+    if (lane == 0) bulk_wait_group_all();  // this warp's stores are complete before the CTA exits
+    __syncwarp();
     if (range_bad) atomicOr(P.err, kErrRange);
   }
   if (!ok) atomicOr(P.err, kMode);
@@ -690,9 +732,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(GemmParams P) {
 }
 
 // ------------------------------------------------------------------------- k_combine
-__global__ void __launch_bounds__(256) k_combine(int T, const float *y, const float *ysh, const float *sg,
-                                                 int sh_lo, int sh_hi, const int32_t *ids, const int32_t *order,
-                                                 int e_lo, int e_hi, float *out, int accumulate) {
+__global__ void __launch_bounds__(256) k_combine(int T, const float *y, const int32_t *inv, const int32_t *offsets,
+                                                 const float *sg, int sh_lo, int sh_hi, const int32_t *ids,
+                                                 const int32_t *order, int e_lo, int e_hi, float *out,
+                                                 int accumulate) {
   const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;  // one float4 of one token
   if (idx >= (int64_t)T * (kH / 4)) return;
   const int t = (int)(idx / (kH / 4)), h = (int)(idx % (kH / 4)) * 4;
@@ -702,7 +745,8 @@ __global__ void __launch_bounds__(256) k_combine(int T, const float *y, const fl
     const int slot = __ldg(order + (size_t)t * kK + i);
     const int e = __ldg(ids + (size_t)t * kK + slot);
     if (e < e_lo || e >= e_hi) continue;
-    const float4 v = __ldcs(reinterpret_cast<const float4 *>(y + ((size_t)t * kK + slot) * kH + h));
+    const int pos = __ldg(inv + (size_t)t * kK + slot);
+    const float4 v = __ldcs(reinterpret_cast<const float4 *>(y + (size_t)pos * kH + h));
     acc.x = __fadd_rn(acc.x, v.x);
     acc.y = __fadd_rn(acc.y, v.y);
     acc.z = __fadd_rn(acc.z, v.z);
@@ -711,7 +755,8 @@ __global__ void __launch_bounds__(256) k_combine(int T, const float *y, const fl
   float4 r = acc;
   if (sg && t >= sh_lo && t < sh_hi) {
     const float g = __ldg(sg + (t - sh_lo));
-    const float4 sh = __ldcs(reinterpret_cast<const float4 *>(ysh + (size_t)t * kH + h));
+    const int pos = __ldg(offsets + kE) + (t - sh_lo);  // the shared expert's rows come last
+    const float4 sh = __ldcs(reinterpret_cast<const float4 *>(y + (size_t)pos * kH + h));
     r = make_float4(__fadd_rn(acc.x, __fmul_rn(g, sh.x)), __fadd_rn(acc.y, __fmul_rn(g, sh.y)),
                     __fadd_rn(acc.z, __fmul_rn(g, sh.z)), __fadd_rn(acc.w, __fmul_rn(g, sh.w)));
   }
@@ -740,6 +785,102 @@ int ensure_gemm_attrs() {
 }
 
 constexpr int kMaxTPrefill = 1 << 16;
+
+// ---------------------------------------------------------------- tensor maps
+// Encoded maps are cached by their full description (a layer's weights and a workspace are
+// reused call after call), so steady-state calls encode nothing.
+struct MapKey {
+  const void *base;
+  int dtype, swz;
+  uint64_t d0, d1, d2, s1, s2;
+  uint32_t b0, b1;
+  bool operator==(const MapKey &o) const {
+    return base == o.base && dtype == o.dtype && swz == o.swz && d0 == o.d0 && d1 == o.d1 && d2 == o.d2 &&
+           s1 == o.s1 && s2 == o.s2 && b0 == o.b0 && b1 == o.b1;
+  }
+};
+
+int encode_map(const MapKey &k, CUtensorMap *out) {
+  static std::mutex mu;
+  static MapKey keys[128];
+  static CUtensorMap maps[128];
+  static int n = 0, next = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n; ++i)
+    if (keys[i] == k) {
+      *out = maps[i];
+      return B200MOE_OK;
+    }
+  const cuuint64_t dims[3] = {k.d0, k.d1, k.d2};
+  const cuuint64_t strides[2] = {k.s1, k.s2};
+  const cuuint32_t box[3] = {k.b0, k.b1, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const int rank = k.d2 > 0 ? 3 : 2;
+  const CUresult r = cuTensorMapEncodeTiled(
+      out,
+      k.dtype == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                   : (k.dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8),
+      (cuuint32_t)rank,
+      const_cast<void *>(k.base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      k.swz ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return b2host::set_error(B200MOE_EINVAL, "tensor map encode failed (%d) for %p, dims %llu x %llu x %llu", (int)r,
+                             k.base, (unsigned long long)k.d0, (unsigned long long)k.d1, (unsigned long long)k.d2);
+  keys[next] = k;
+  maps[next] = *out;
+  next = (next + 1) % 128;
+  if (n < 128) ++n;
+  return B200MOE_OK;
+}
+
+// Header and quant maps of one Q4_K weight matrix [experts][rows][row_bytes] (3-D, bytes).
+int weight_maps(const void *base, int row_bytes, int rows, int experts, int64_t expert_stride, CUtensorMap *hdr,
+                CUtensorMap *qnt) {
+  if (((uintptr_t)base & 15) || (expert_stride & 15))
+    return b2host::set_error(B200MOE_EINVAL, "prefill: weight base %p / expert stride %lld not 16-byte aligned", base,
+                             (long long)expert_stride);
+  MapKey k{base, 0, 0, (uint64_t)row_bytes, (uint64_t)rows, (uint64_t)experts, (uint64_t)row_bytes,
+           (uint64_t)(experts > 1 ? expert_stride : (int64_t)rows * row_bytes), 16, 128};
+  int rc = encode_map(k, hdr);
+  if (rc) return rc;
+  k.b0 = 32;
+  return encode_map(k, qnt);
+}
+
+// All maps of one GEMM launch: kMode 1 (gate_up: the four weight matrices, B = the 9Ts rows of
+// x16p, stores into s16) or 2 (down: the two weight matrices, B = the 9Ts rows of s16, stores
+// into y).
+int gemm_maps(int mode, const b200moe_layer *L, const __half *x16p, const __half *s16, const float *y, int Ts,
+              GemmMaps &m) {
+  int rc;
+  if (mode == 1) {
+    if ((rc = weight_maps(L->gate, kRowUp, kI, kE, L->gate_up_expert_stride, &m.hdr[0][0], &m.qnt[0][0]))) return rc;
+    if ((rc = weight_maps(L->up, kRowUp, kI, kE, L->gate_up_expert_stride, &m.hdr[0][1], &m.qnt[0][1]))) return rc;
+    if ((rc = weight_maps(L->sh_gate, kRowUp, kI, 1, 0, &m.hdr[1][0], &m.qnt[1][0]))) return rc;
+    if ((rc = weight_maps(L->sh_up, kRowUp, kI, 1, 0, &m.hdr[1][1], &m.qnt[1][1]))) return rc;
+    const MapKey kb{x16p, 1, 1, (uint64_t)kH, (uint64_t)9 * Ts, 0, (uint64_t)kH * 2, 0, 64, 64};
+    if ((rc = encode_map(kb, &m.b))) return rc;
+    for (int p = 0; p < 5; ++p) {
+      const MapKey ks{s16, 1, 0, (uint64_t)kI, (uint64_t)9 * Ts, 0, (uint64_t)kI * 2, 0, 32, (uint32_t)(16 >> p)};
+      if ((rc = encode_map(ks, &m.st[p]))) return rc;
+    }
+    return B200MOE_OK;
+  }
+  if ((rc = weight_maps(L->down, kRowDown, kH, kE, L->down_expert_stride, &m.hdr[0][0], &m.qnt[0][0]))) return rc;
+  if ((rc = weight_maps(L->sh_down, kRowDown, kH, 1, 0, &m.hdr[1][0], &m.qnt[1][0]))) return rc;
+  m.hdr[0][1] = m.hdr[0][0];
+  m.qnt[0][1] = m.qnt[0][0];
+  m.hdr[1][1] = m.hdr[1][0];
+  m.qnt[1][1] = m.qnt[1][0];
+  const MapKey kb{s16, 1, 1, (uint64_t)kI, (uint64_t)9 * Ts, 0, (uint64_t)kI * 2, 0, 64, 64};
+  if ((rc = encode_map(kb, &m.b))) return rc;
+  for (int p = 0; p < 5; ++p) {
+    const MapKey ky{y, 2, 0, (uint64_t)kH, (uint64_t)9 * Ts, 0, (uint64_t)kH * 4, 0, 32, (uint32_t)(16 >> p)};
+    if ((rc = encode_map(ky, &m.st[p]))) return rc;
+  }
+  return B200MOE_OK;
+}
 
 int check_prefill_layer(const b200moe_layer *L, const char *who) {
   if (!L || !L->gate || !L->up || !L->down || !L->sh_gate || !L->sh_up || !L->sh_down || !L->router_w ||
@@ -774,37 +915,30 @@ int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *
   if (!sg) sh_lo = sh_hi = 0;
   k_plan<<<1, 512, 0, s>>>(sh_hi - sh_lo, w.counts, w.offsets, w.tiles1, w.tiles2, w.ntiles);
   B2_CUDA(cudaGetLastError());
-  k_fill<<<kNE, 1024, 0, s>>>(T, sh_lo, sh_hi, ids, w.counts, w.offsets, w.plist);
+  k_fill<<<kNE, 1024, 0, s>>>(T, sh_lo, sh_hi, ids, w.counts, w.offsets, w.plist, w.inv);
   B2_CUDA(cudaGetLastError());
   GemmParams g;
-  g.wa0 = (const uint8_t *)L->gate;
-  g.wa1 = (const uint8_t *)L->up;
-  g.stride = L->gate_up_expert_stride;
-  g.sh0 = (const uint8_t *)L->sh_gate;
-  g.sh1 = (const uint8_t *)L->sh_up;
+  k_gather_x<<<4 * g_num_sms, 256, 0, s>>>(9 * T, w.offsets, w.plist, x16, w.x16p);
+  B2_CUDA(cudaGetLastError());
+  rc = gemm_maps(1, L, w.x16p, w.s16, w.y, T, g.m);
+  if (rc) return rc;
   g.tiles = w.tiles1;
   g.ntiles = w.ntiles;
   g.plist = w.plist;
-  g.x16 = x16;
   g.s16 = w.s16;
   g.wb = wb;
   g.y = w.y;
-  g.ysh = w.ysh;
   g.err = w.err;
   k_gemm<1><<<g_num_sms, kGemmThreads, GemmCfg<1>::kSmem, s>>>(g);
   B2_CUDA(cudaGetLastError());
-  g.wa0 = (const uint8_t *)L->down;
-  g.wa1 = nullptr;
-  g.stride = L->down_expert_stride;
-  g.sh0 = (const uint8_t *)L->sh_down;
-  g.sh1 = nullptr;
+  rc = gemm_maps(2, L, w.x16p, w.s16, w.y, T, g.m);
+  if (rc) return rc;
   g.tiles = w.tiles2;
   k_gemm<2><<<g_num_sms, kGemmThreads, GemmCfg<2>::kSmem, s>>>(g);
   B2_CUDA(cudaGetLastError());
   const int64_t nthreads = (int64_t)T * (kH / 4);
-  k_combine<<<(unsigned)((nthreads + 255) / 256), 256, 0, s>>>(T, w.y, w.ysh, sg, sh_lo, sh_hi, ids, w.order, e_lo,
-                                                               e_hi, out,
-                                                               accumulate);
+  k_combine<<<(unsigned)((nthreads + 255) / 256), 256, 0, s>>>(T, w.y, w.inv, w.offsets, sg, sh_lo, sh_hi, ids,
+                                                               w.order, e_lo, e_hi, out, accumulate);
   B2_CUDA(cudaGetLastError());
   return B200MOE_OK;
 }
