@@ -8,8 +8,8 @@
 //   k_count       per token: the slots whose expert is in the requested range, and their order
 //   k_plan        one CTA: packed row offsets per expert (the shared expert is expert 256 with
 //                 every token), 256-token chunks, and the GEMM tile tables
-//   k_fill        CTA per expert: that expert's (token, slot) assignments in ascending order,
-//                 and each assignment's row position (inv)
+//   k_fill        thread per assignment: a row in its expert's range (plist), and the
+//                 assignment's row position (inv)
 //   k_gather_x    the x16 rows in assignment-list order (the gate_up GEMM's B operand)
 //   k_gemm<1>     gate_up: D[128 gate rows | 128 up rows][tokens] = W . x^T, s = silu(g)*u -> fp16
 //   k_gemm<2>     down:    D[128 h rows][tokens] = W_d . s^T -> y[position][h] = o * w (routed)
@@ -321,42 +321,23 @@ __global__ void __launch_bounds__(512) k_plan(int n_shared, const int32_t *count
 }
 
 // ------------------------------------------------------------------------- k_fill
-__global__ void __launch_bounds__(1024) k_fill(int T, int sh_lo, int sh_hi, const int32_t *ids,
-                                                const int32_t *counts, const int32_t *offsets, int32_t *plist,
-                                                int32_t *inv) {
-  __shared__ int wcount[32];
-  __shared__ int running;
-  const int e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  if (e == kE) {  // the shared expert's rows: tokens sh_lo .. sh_hi-1
-    for (int t = sh_lo + tid; t < sh_hi; t += 1024) plist[offsets[kE] + t - sh_lo] = t;
-    return;
-  }
-  if (counts[e] == 0) return;
-  if (tid == 0) running = 0;
-  __syncthreads();
-  const int n = T * kK;
-  int32_t *dst = plist + offsets[e];
-  for (int base = 0; base < n; base += 1024) {
-    const int a = base + tid;
-    const bool f = a < n && __ldg(ids + a) == e;
-    const unsigned bal = __ballot_sync(0xFFFFFFFFu, f);
-    if (lane == 0) wcount[w] = __popc(bal);
-    __syncthreads();
-    int before = 0, total = 0;
-    for (int i = 0; i < 32; ++i) {
-      const int c = wcount[i];
-      if (i < w) before += c;
-      total += c;
+// One thread per assignment a = t * 8 + slot whose expert is in range: it takes a row of its
+// expert's range by an atomic countdown of that expert's count (which ends at zero), and
+// records plist[row] = a, inv[a] = row. The order of rows inside an expert changes no result:
+// every GEMM column, and every token's combine, is computed on its own. Rows from
+// offsets[kE] on are the shared expert's: tokens sh_lo .. sh_hi-1 in order.
+__global__ void __launch_bounds__(256) k_fill(int T, int sh_lo, int sh_hi, const int32_t *ids, int e_lo, int e_hi,
+                                              const int32_t *offsets, int32_t *counts, int32_t *plist, int32_t *inv) {
+  const int a = blockIdx.x * 256 + threadIdx.x;
+  if (a < T * kK) {
+    const int e = __ldg(ids + a);
+    if (e >= e_lo && e < e_hi) {
+      const int row = __ldg(offsets + e) + atomicSub(counts + e, 1) - 1;
+      plist[row] = a;
+      inv[a] = row;
     }
-    if (f) {
-      const int q = running + before + __popc(bal & ((1u << lane) - 1u));
-      dst[q] = a;
-      inv[a] = offsets[e] + q;
-    }
-    __syncthreads();
-    if (tid == 0) running += total;
-    __syncthreads();
   }
+  if (a < sh_hi - sh_lo) plist[__ldg(offsets + kE) + a] = sh_lo + a;
 }
 
 // ------------------------------------------------------------------------- k_gather_x
@@ -380,7 +361,8 @@ __global__ void __launch_bounds__(256) k_gather_x(int max_rows, const int32_t *o
 // ------------------------------------------------------------------------- grouped GEMM
 // Block of 15 warps, each with one job:
 //   warps 0-3    epilogue: TMEM lanes 32w..32w+31 -> s (gate_up) or y (down)
-//   warps 4-11   dequant: raw Q4_K slab (shared memory) -> fp16 A tile of the K-slab
+//   warps 4-11   dequant: raw Q4_K slab (shared memory) -> fp16 A tile of the K-slab, each
+//                thread a whole row's 64 elements (gate_up) or one half of them (down)
 //   warp 12      TMEM allocation; lane 0 issues tcgen05.mma and the commits
 //   warp 13      raw producer (lane 0): per K-slab and 128-row weight tile, two TMA loads of
 //                the Q4_K bytes -- the 16-byte block headers and the slab's 32 quant bytes of
@@ -398,7 +380,7 @@ __global__ void __launch_bounds__(256) k_gather_x(int max_rows, const int32_t *o
 //                                    MMA commit
 //   B ring   kBStages x 32 KB        TMA bytes (one arming arrival); emptied by the MMA commit
 //   raw ring kRStages x kA x 6 KB    TMA bytes (one arming arrival); emptied by the 8 dequant
-//                                    warps once their rows are in registers
+//                                    warps once their rows are dequantised
 // The down GEMM double-buffers its 256-column accumulator so the epilogue of one tile
 // overlaps the next tile's main loop; gate_up uses all 512 columns for one tile.
 //
@@ -408,12 +390,17 @@ __global__ void __launch_bounds__(256) k_gather_x(int max_rows, const int32_t *o
 // and 1-row boxes, so no store reaches past the tile into another expert's rows. (Plain
 // per-column 128-byte stores ran at ~6 B/cycle per SM: the epilogue, not the MMA, bounded
 // the down GEMM.)
-constexpr int kEpiWarps = 4, kDqWarps = 8;
+// 8 dequant warps: measured faster than 16 (0.80 vs 0.87 ms per 4096-token layer), whose extra
+// shared-memory traffic and spinning waiters cost more than the latency they hide.
+#ifndef B2_DQ_WARPS
+#define B2_DQ_WARPS 8
+#endif
+constexpr int kEpiWarps = 4, kDqWarps = B2_DQ_WARPS;
 constexpr int kDqThreads = 32 * kDqWarps;
-constexpr int kMmaWarp = kEpiWarps + kDqWarps;  // 12
-constexpr int kRawWarp = kMmaWarp + 1;          // 13
-constexpr int kBWarp = kRawWarp + 1;            // 14
-constexpr int kGemmThreads = 32 * (kBWarp + 1);  // 480
+constexpr int kMmaWarp = kEpiWarps + kDqWarps;
+constexpr int kRawWarp = kMmaWarp + 1;
+constexpr int kBWarp = kRawWarp + 1;
+constexpr int kGemmThreads = 32 * (kBWarp + 1);
 constexpr int kRawHdr = 128 * 16;               // per 128-row tile: the rows' block headers
 constexpr int kRawTile = kRawHdr + 128 * 32;    // + the rows' 32 quant bytes of the slab
 
@@ -421,7 +408,9 @@ template <int kMode>
 struct GemmCfg {
   static constexpr int kA = kMode == 1 ? 2 : 1;                // A tiles per stage (gate+up / down)
   static constexpr int kARows = 128 * kA;                       // weight rows per tile
-  static constexpr int kTpr = kDqThreads / kARows;              // dequant threads per row (1 or 2)
+  static constexpr int kTpr = kDqThreads / kARows;              // dequant threads per row (1, 2 or 4)
+  static constexpr int kHalves = kTpr == 1 ? 2 : 1;             // halves of the row per thread
+  static constexpr int kNkc = kTpr == 1 ? 4 : 8 / kTpr;         // 16-byte chunks per half per thread
   static constexpr int kKS = (kMode == 1 ? kH : kI) / 64;       // K-slabs of 64 per tile
   static constexpr int kAStages = kMode == 1 ? 2 : 3;
   static constexpr int kBStages = 3;
@@ -461,25 +450,25 @@ struct GemmParams {
   int32_t *err;
 };
 
-// Half (h = 0: low nibbles, sub-block 2g; h = 1: high nibbles, sub-block 2g+1) of K-slab g of
-// one Q4_K block row -> 4 chunks (16 B each) of the A tile row. hd: the block header; q0, q1:
-// the slab's 32 quant bytes.
-__device__ __forceinline__ void dequant_half(const uint4 &hd, const uint4 &q0, const uint4 &q1, int g, int h,
+// Chunks kc0 .. kc0+nkc-1 (16 B = 8 elements each) of half h (h = 0: low nibbles, sub-block
+// 2g; h = 1: high nibbles, sub-block 2g+1) of K-slab g of one Q4_K block row -> the A tile
+// row. hd: the block header; qw: the quant words of those chunks (two per chunk).
+template <int nkc>
+__device__ __forceinline__ void dequant_part(const uint4 &hd, const uint32_t (&qw)[2 * nkc], int g, int h, int kc0,
                                              uint8_t *tile, int row) {
   float s0, m0, s1, m1;
   q4k_scales(hd, 2 * g, s0, m0, s1, m1);
   const __half2 S = __float2half2_rn(h ? s1 : s0), M = __float2half2_rn(h ? -m1 : -m0);
   const __half2 k1024 = __float2half2_rn(1024.0f);
-  const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-  uint8_t *rbase = tile + (row >> 3) * 1024 + (row & 7) * 16 + h * 512;
+  uint8_t *rbase = tile + (row >> 3) * 1024 + (row & 7) * 16 + h * 512 + kc0 * 128;
 #pragma unroll
-  for (int kc = 0; kc < 4; ++kc) {
+  for (int kc = 0; kc < nkc; ++kc) {
     uint32_t v[4];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       const uint32_t w = qw[2 * kc + (p >> 1)];
       const uint32_t pr = __byte_perm(w, 0u, (p & 1) ? 0x4342u : 0x4140u);  // [b, 0, b', 0]
-      const uint32_t q = (h ? ((pr >> 4) & 0x000F000Fu) : (pr & 0x000F000Fu)) | 0x64006400u;  // 1024 + q
+      const uint32_t q = ((pr >> (4 * h)) & 0x000F000Fu) | 0x64006400u;  // 1024 + q
       __half2 x = __hsub2(*reinterpret_cast<const __half2 *>(&q), k1024);
       x = __hfma2(x, S, M);
       v[p] = *reinterpret_cast<uint32_t *>(&x);
@@ -543,7 +532,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
 
   if (warp >= kEpiWarps && warp < kMmaWarp) {  // ----------------------------- dequant
     const int pt = threadIdx.x - 32 * kEpiWarps;
-    const int row = pt / C::kTpr, half = pt % C::kTpr;  // kTpr == 1: this thread does both halves
+    const int row = pt / C::kTpr, part = pt % C::kTpr;  // which half (and quarter) of the row's slab
+    const int half = C::kTpr == 1 ? 0 : part / (C::kTpr / 2);
+    const int kc0 = C::kTpr == 1 ? 0 : (part % (C::kTpr / 2)) * C::kNkc;
     const int tl = row >> 7, tr = row & 127;               // A tile, row within it
     for (uint32_t it = 0; it < n_it && ok; ++it) {
       const int ks = it % C::kKS;
@@ -552,21 +543,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(r_full + rs, (it / C::kRStages) & 1))) { ok = false; break; }
       const uint8_t *rt = raw_ring + rs * C::kRawStage + tl * kRawTile;
       const uint4 hd = *reinterpret_cast<const uint4 *>(rt + tr * 16);
-      const uint4 q0 = *reinterpret_cast<const uint4 *>(rt + kRawHdr + tr * 32);
-      const uint4 q1 = *reinterpret_cast<const uint4 *>(rt + kRawHdr + tr * 32 + 16);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(r_empty + rs);  // this warp's rows are in registers
+      uint32_t qw[2 * C::kNkc];  // the quant words of this thread's chunks (both halves share them)
+      if (C::kNkc == 4) {
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(rt + kRawHdr + tr * 32);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(rt + kRawHdr + tr * 32 + 16);
+        const uint32_t w8[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int i = 0; i < 2 * C::kNkc; ++i) qw[i] = w8[i];
+      } else {
+        const uint4 q = *reinterpret_cast<const uint4 *>(rt + kRawHdr + tr * 32 + 8 * kc0);
+        const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 2 * C::kNkc; ++i) qw[i] = w4[i];
+      }
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(a_empty + s, ((it / C::kAStages) & 1) ^ 1))) { ok = false; break; }
       uint8_t *at = a_ring + s * (C::kA * C::kATile) + tl * C::kATile;
-      if (C::kTpr == 1) {
-        dequant_half(hd, q0, q1, ks & 3, 0, at, tr);
-        dequant_half(hd, q0, q1, ks & 3, 1, at, tr);
-      } else {
-        dequant_half(hd, q0, q1, ks & 3, half, at, tr);
-      }
+#pragma unroll
+      for (int hh = 0; hh < C::kHalves; ++hh) dequant_part<C::kNkc>(hd, qw, ks & 3, half + hh, kc0, at, tr);
       fence_proxy_async_smem();  // this thread's generic smem writes -> async proxy
       __syncwarp();
-      if (lane == 0) mbar_arrive(a_full + s);
+      if (lane == 0) {
+        mbar_arrive(a_full + s);
+        // The raw stage is released only now, after the dequant has CONSUMED the loaded words:
+        // released right after the loads were issued, a load still in flight could read bytes
+        // that the producer's next TMA load had already overwritten.
+        mbar_arrive(r_empty + rs);
+      }
     }
   } else if (warp == kRawWarp) {  // ----------------------------------------- raw producer
     if (lane == 0) {
@@ -915,7 +917,8 @@ int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *
   if (!sg) sh_lo = sh_hi = 0;
   k_plan<<<1, 512, 0, s>>>(sh_hi - sh_lo, w.counts, w.offsets, w.tiles1, w.tiles2, w.ntiles);
   B2_CUDA(cudaGetLastError());
-  k_fill<<<kNE, 1024, 0, s>>>(T, sh_lo, sh_hi, ids, w.counts, w.offsets, w.plist, w.inv);
+  k_fill<<<(unsigned)(((int64_t)T * kK + 255) / 256), 256, 0, s>>>(T, sh_lo, sh_hi, ids, e_lo, e_hi, w.offsets,
+                                                                   w.counts, w.plist, w.inv);
   B2_CUDA(cudaGetLastError());
   GemmParams g;
   k_gather_x<<<4 * g_num_sms, 256, 0, s>>>(9 * T, w.offsets, w.plist, x16, w.x16p);
