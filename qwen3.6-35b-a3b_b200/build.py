@@ -48,7 +48,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_v: bool = False) -> 
         subprocess.run(cmd, check=True)
         objs.append(obj)
     tmp = LIB + ".tmp"
-    subprocess.run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcuda"], check=True)
+    subprocess.run([NVCC, *ARCH, "-shared", "-o", tmp, *objs], check=True)
     os.replace(tmp, LIB)
     return LIB
 

@@ -802,12 +802,27 @@ struct MapKey {
   }
 };
 
+// The driver's encoder, found at run time through the runtime API, so the library itself does
+// not depend on libcuda (it loads on a machine without a driver; calls then fail cleanly).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
 int encode_map(const MapKey &k, CUtensorMap *out) {
   static std::mutex mu;
   static MapKey keys[128];
   static CUtensorMap maps[128];
   static int n = 0, next = 0;
+  static EncodeTiledFn encode = nullptr;
   std::lock_guard<std::mutex> lock(mu);
+  if (!encode) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    B2_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !fn)
+      return b2host::set_error(B200MOE_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    encode = (EncodeTiledFn)fn;
+  }
   for (int i = 0; i < n; ++i)
     if (keys[i] == k) {
       *out = maps[i];
@@ -818,7 +833,7 @@ int encode_map(const MapKey &k, CUtensorMap *out) {
   const cuuint32_t box[3] = {k.b0, k.b1, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   const int rank = k.d2 > 0 ? 3 : 2;
-  const CUresult r = cuTensorMapEncodeTiled(
+  const CUresult r = encode(
       out,
       k.dtype == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                    : (k.dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8),
