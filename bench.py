@@ -254,7 +254,7 @@ def run_b200(args):
         T = args.batch if args.batch > 1 else 4096
         L = DeviceLayer.synthetic(3, 0, dev)
         nl = 1
-        launches_per_step = 9
+        launches_per_step = 10
         tok_bits = synth.tokens(3, T, stream=100 + rank)
         tok_dev = torch.from_numpy(tok_bits.view(np.int16)).view(torch.bfloat16).reshape(T, 2048).to(dev)
         out = torch.empty((T, 2048), dtype=torch.float32, device=dev)
@@ -274,7 +274,7 @@ def run_b200(args):
         L = DeviceLayer.synthetic(3, 0, dev)
         ep = ExpertParallelMoE(L)
         nl = 1
-        launches_per_step = 11
+        launches_per_step = 12
         tok_bits = synth.tokens(3, T_total, stream=100)
         x_all = torch.from_numpy(tok_bits.view(np.int16)).view(torch.bfloat16).reshape(T_total, 2048)
         x_loc = x_all[rank * T:(rank + 1) * T].to(dev)
@@ -414,7 +414,7 @@ def run_b200(args):
                                 else "one graph replay = %d kernels (router/shared K1, routed gate_up K2, down+combine "
                                      "K3 per layer)" % launches_per_step)
                                if args.workload in ("stack_decode", "layer_decode")
-                               else ("one step = %d kernels per layer (prep, router GEMM, route, count, plan, fill, "
+                               else ("one step = %d kernels per layer (prep, router GEMM, route, count, plan, fill, x gather, "
                                      "tcgen05 gate_up GEMM, tcgen05 down GEMM, combine); achieved = expert FLOPs / "
                                      "step time" % (launches_per_step // max(nl, 1)))},
         "gpu_launches": launches_per_step * K,

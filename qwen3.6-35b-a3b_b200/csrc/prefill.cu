@@ -178,48 +178,49 @@ __global__ void __launch_bounds__(256) k_prep(const void *x, int x_dtype, const 
 }
 
 // ------------------------------------------------------------------------- k_router_gemm
-// CTA: 64 tokens x 64 experts, thread (ty, tx) owns tokens ty + 16i and experts tx + 16j.
-__global__ void __launch_bounds__(256) k_router_gemm(const float *__restrict__ xn, int T,
+// CTA: 64 tokens x 64 experts, 128 threads; thread (ty, tx) owns tokens ty + 8i (i < 8) and
+// experts tx + 16j (j < 4): 32 outputs, 128 FMAs per 12 shared-memory vector loads.
+__global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ xn, int T,
                                                      const uint16_t *__restrict__ wg, const float *bias,
                                                      uint16_t *logits) {
   __shared__ __align__(16) float xs[64][68];
   __shared__ __align__(16) float wsm[64][68];
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
   const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
-  float tot[4][4];
+  float tot[8][4];
   for (int c = 0; c < 32; ++c) {
-    // x chunk: 64 rows x 64 floats; w chunk: 64 rows x 64 bf16
+    // x chunk: 64 rows x 64 floats; w chunk: 64 rows x 64 bf16 (widened to f32)
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int idx = tid + 256 * q;  // 0..1023 float4 slots
+    for (int q = 0; q < 8; ++q) {
+      const int idx = tid + 128 * q;  // 0..1023 float4 slots
       const int row = idx >> 4, col = (idx & 15) * 4;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (t0 + row < T) v = __ldg(reinterpret_cast<const float4 *>(xn + (size_t)(t0 + row) * kH + 64 * c + col));
       *reinterpret_cast<float4 *>(&xs[row][col]) = v;
     }
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int idx = tid + 256 * q;  // 0..511 8-wide slots
+    for (int q = 0; q < 4; ++q) {
+      const int idx = tid + 128 * q;  // 0..511 8-wide slots
       const int row = idx >> 3, col = (idx & 7) * 8;
       const uint4 u = __ldg(reinterpret_cast<const uint4 *>(wg + (size_t)(e0 + row) * kH + 64 * c + col));
       *reinterpret_cast<float4 *>(&wsm[row][col]) = make_float4(bf16f(u.x), bf16f(u.x >> 16), bf16f(u.y), bf16f(u.y >> 16));
       *reinterpret_cast<float4 *>(&wsm[row][col + 4]) = make_float4(bf16f(u.z), bf16f(u.z >> 16), bf16f(u.w), bf16f(u.w >> 16));
     }
     __syncthreads();
-    float acc[4][4];
+    float acc[8][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
 #pragma unroll 2
-    for (int k = 0; k < 64; k += 4) {
-      float4 xa[4], wa[4];
+    for (int k = 0; k < 64; k += 4) {  // the chunk's 64 products of every output, in k order
+      float4 xa[8], wa[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) xa[i] = *reinterpret_cast<const float4 *>(&xs[ty + 16 * i][k]);
+      for (int i = 0; i < 8; ++i) xa[i] = *reinterpret_cast<const float4 *>(&xs[ty + 8 * i][k]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) wa[j] = *reinterpret_cast<const float4 *>(&wsm[tx + 16 * j][k]);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           acc[i][j] = __fmaf_rn(xa[i].x, wa[j].x, acc[i][j]);
@@ -229,14 +230,14 @@ __global__ void __launch_bounds__(256) k_router_gemm(const float *__restrict__ x
         }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) tot[i][j] = (c == 0) ? acc[i][j] : __fadd_rn(tot[i][j], acc[i][j]);
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = t0 + ty + 16 * i;
+  for (int i = 0; i < 8; ++i) {
+    const int t = t0 + ty + 8 * i;
     if (t >= T) continue;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -912,7 +913,7 @@ int route_stage(const void *x, int x_dtype, const float *resid, float eps, int T
   B2_CUDA(cudaMemsetAsync(w.err, 0, 4, s));
   k_prep<<<(T + 7) / 8, 256, 0, s>>>(x, x_dtype, resid, eps, T, L->sh_gate_w, w.xn, x16, sg, w.err);
   B2_CUDA(cudaGetLastError());
-  k_router_gemm<<<dim3((T + 63) / 64, kE / 64), 256, 0, s>>>(w.xn, T, L->router_w, L->logit_bias, w.logits);
+  k_router_gemm<<<dim3((T + 63) / 64, kE / 64), 128, 0, s>>>(w.xn, T, L->router_w, L->logit_bias, w.logits);
   B2_CUDA(cudaGetLastError());
   k_route_tok<<<(T + 7) / 8, 256, 0, s>>>(w.logits, T, ids, wb);
   B2_CUDA(cudaGetLastError());

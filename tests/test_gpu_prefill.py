@@ -123,3 +123,34 @@ def test_stack_prefill_teacher_forced(cuda):
         c = OM.compare(resid.cpu().numpy()[sample], ref)
         assert c["rel_l2"] < REL_L2, (l, c)
     del eng
+
+
+@pytest.mark.parametrize("W", [2, 4])
+def test_expert_ranges_as_in_expert_parallelism(cuda, layer3, W):
+    """The expert-parallel decomposition on one GPU, through the same C-ABI calls the NCCL path
+    makes: route all tokens once; for each rank r, one b200moe_moe_experts call over all tokens
+    with its expert range [256r/W, 256(r+1)/W) and the shared expert on its own rows only; the
+    sum of the W partial rows in ascending rank order must equal the single-call prefill
+    (rel-L2 1e-5: only the association of the routed sum differs)."""
+    import torch
+    from b200moe import moe, synth
+    from b200moe.ep import device_experts_fn, device_route_fn
+    T = 512
+    xb = synth.tokens(3, T, stream=5)
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).to(cuda)
+    ref, info = moe.moe_block(x, layer3, 0, path="prefill")
+    ws = lambda n: moe.prefill_workspace(n, cuda)
+    x16, ids, wb, sg = device_route_fn(layer3, ws)(x)
+    experts = device_experts_fn(layer3, ws)
+    Tr = T // W
+    out = None
+    for r in range(W):
+        part = torch.empty((T, 2048), dtype=torch.float32, device=cuda)
+        experts(x16, ids, wb, 256 * r // W, 256 * (r + 1) // W, sg[r * Tr:(r + 1) * Tr], part,
+                sh_rows=(r * Tr, (r + 1) * Tr))
+        out = part if out is None else out + part
+    torch.cuda.synchronize()
+    assert moe.prefill_status(T, cuda) == 0
+    assert torch.equal(ids, info["ids"].reshape(T, 8))
+    rel = float(torch.linalg.norm(out - ref.reshape(T, 2048)) / torch.linalg.norm(ref))
+    assert torch.isfinite(out).all() and rel < 1e-5, rel
