@@ -468,9 +468,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
     }
     if (tid == 0 && !last) issue_router_rows(l + 1);
     __syncwarp();
-    float rs = 1.0f;  // every warp derives the RMSNorm scale itself (identical bits, no barrier)
-    if (P.resid) {    // sum of squares in the declared chunk order
-      const float *v = res_s + lane * kPadSeg;
+    // Every warp derives the RMSNorm scale itself (identical bits, no barrier): the router warps
+    // now, the others at the start of phase G, where they would wait for rows anyway (so they do
+    // not compete for shared memory with the router on the critical path).
+    auto rms_scale = [&]() -> float {
+      if (!P.resid) return 1.0f;
+      const float *v = res_s + lane * kPadSeg;  // sum of squares in the declared chunk order
       float ss = 0.0f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -481,8 +484,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
         ss = __fmaf_rn(a.w, a.w, ss);
       }
       const float tot = chunk_total32(ss, warp_scr + 32 * warp);
-      rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, 2048.0f), P.eps)));
-    }
+      return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, 2048.0f), P.eps)));
+    };
+    float rs = warp < kRtRows ? rms_scale() : 1.0f;
     fail = !__all_sync(0xFFFFFFFFu, wait_bar(kBarRt0 + (l & 1)));  // every thread consumes the phase
     if (!fail && warp < kRtRows) {  // warps 0, 1: logits 2c, 2c+1; warp 2: the gate
       const bool gate = warp == 2;
@@ -546,6 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       uint32_t have = 0;  // bit 0: shared, bit 1 + g: routed chunk g
       if (warp > 0) {
         __syncwarp();
+        if (warp >= kRtRows) rs = rms_scale();
         XChunk X0, X1;
         xchunk_pad(res_s, rs, kb0, cc, X0);
         xchunk_pad(res_s, rs, kb0 + 4, cc, X1);
