@@ -179,34 +179,64 @@ __global__ void __launch_bounds__(256) k_prep(const void *x, int x_dtype, const 
 
 // ------------------------------------------------------------------------- k_router_gemm
 // CTA: 64 tokens x 64 experts, 128 threads; thread (ty, tx) owns tokens ty + 8i (i < 8) and
-// experts tx + 16j (j < 4): 32 outputs, 128 FMAs per 12 shared-memory vector loads.
+// experts tx + 16j (j < 4): 32 outputs, 128 FMAs per 12 shared-memory vector loads. The K
+// chunks are double-buffered: chunk c+1's x rows arrive by cp.async and its weights are held in
+// registers while chunk c is multiplied.
+constexpr int kRgPitch = 68;                                  // padded row pitch (floats)
+constexpr int kRgBuf = 64 * kRgPitch;                         // one 64 x 64 chunk
+constexpr size_t kRgSmem = (size_t)4 * kRgBuf * sizeof(float);  // x and w, two buffers each
+
 __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ xn, int T,
                                                      const uint16_t *__restrict__ wg, const float *bias,
                                                      uint16_t *logits) {
-  __shared__ __align__(16) float xs[64][68];
-  __shared__ __align__(16) float wsm[64][68];
+  extern __shared__ __align__(16) float rg_smem[];
+  float *xs = rg_smem, *wsm = rg_smem + 2 * kRgBuf;  // [2][64][kRgPitch] each
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
   const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
-  float tot[8][4];
-  for (int c = 0; c < 32; ++c) {
-    // x chunk: 64 rows x 64 floats; w chunk: 64 rows x 64 bf16 (widened to f32)
+  auto load_x = [&](int c, float *dst) {  // 64 rows x 64 floats by cp.async (zero rows past T)
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const int idx = tid + 128 * q;  // 0..1023 float4 slots
       const int row = idx >> 4, col = (idx & 15) * 4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (t0 + row < T) v = __ldg(reinterpret_cast<const float4 *>(xn + (size_t)(t0 + row) * kH + 64 * c + col));
-      *reinterpret_cast<float4 *>(&xs[row][col]) = v;
+      const bool in = t0 + row < T;
+      cp_async16(dst + row * kRgPitch + col, xn + (size_t)(in ? t0 + row : 0) * kH + 64 * c + col, in ? 16u : 0u);
     }
+    cp_async_commit();
+  };
+  auto load_w = [&](int c, uint4 (&u)[4]) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int idx = tid + 128 * q;  // 0..511 8-wide slots
-      const int row = idx >> 3, col = (idx & 7) * 8;
-      const uint4 u = __ldg(reinterpret_cast<const uint4 *>(wg + (size_t)(e0 + row) * kH + 64 * c + col));
-      *reinterpret_cast<float4 *>(&wsm[row][col]) = make_float4(bf16f(u.x), bf16f(u.x >> 16), bf16f(u.y), bf16f(u.y >> 16));
-      *reinterpret_cast<float4 *>(&wsm[row][col + 4]) = make_float4(bf16f(u.z), bf16f(u.z >> 16), bf16f(u.w), bf16f(u.w >> 16));
+      u[q] = __ldg(reinterpret_cast<const uint4 *>(wg + (size_t)(e0 + (idx >> 3)) * kH + 64 * c + (idx & 7) * 8));
     }
+  };
+  auto store_w = [&](const uint4 (&u)[4], float *dst) {  // bf16 -> f32 (exact)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int idx = tid + 128 * q;
+      float *d = dst + (idx >> 3) * kRgPitch + (idx & 7) * 8;
+      *reinterpret_cast<float4 *>(d) = make_float4(bf16f(u[q].x), bf16f(u[q].x >> 16), bf16f(u[q].y), bf16f(u[q].y >> 16));
+      *reinterpret_cast<float4 *>(d + 4) =
+          make_float4(bf16f(u[q].z), bf16f(u[q].z >> 16), bf16f(u[q].w), bf16f(u[q].w >> 16));
+    }
+  };
+  {
+    uint4 u[4];
+    load_x(0, xs);
+    load_w(0, u);
+    store_w(u, wsm);
+    cp_async_wait_all();
     __syncthreads();
+  }
+  float tot[8][4];
+  for (int c = 0; c < 32; ++c) {
+    const int buf = c & 1;
+    uint4 un[4];
+    if (c + 1 < 32) {  // the next chunk, in flight while this one is multiplied
+      load_x(c + 1, xs + (buf ^ 1) * kRgBuf);
+      load_w(c + 1, un);
+    }
+    const float *xb = xs + buf * kRgBuf, *wb = wsm + buf * kRgBuf;
     float acc[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
@@ -216,9 +246,9 @@ __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ x
     for (int k = 0; k < 64; k += 4) {  // the chunk's 64 products of every output, in k order
       float4 xa[8], wa[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) xa[i] = *reinterpret_cast<const float4 *>(&xs[ty + 8 * i][k]);
+      for (int i = 0; i < 8; ++i) xa[i] = *reinterpret_cast<const float4 *>(xb + (ty + 8 * i) * kRgPitch + k);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) wa[j] = *reinterpret_cast<const float4 *>(&wsm[tx + 16 * j][k]);
+      for (int j = 0; j < 4; ++j) wa[j] = *reinterpret_cast<const float4 *>(wb + (tx + 16 * j) * kRgPitch + k);
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -233,7 +263,11 @@ __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ x
     for (int i = 0; i < 8; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) tot[i][j] = (c == 0) ? acc[i][j] : __fadd_rn(tot[i][j], acc[i][j]);
-    __syncthreads();
+    if (c + 1 < 32) {
+      store_w(un, wsm + (buf ^ 1) * kRgBuf);
+      cp_async_wait_all();
+    }
+    __syncthreads();  // the next chunk is in place; this chunk's buffers may be refilled
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -780,6 +814,7 @@ int ensure_gemm_attrs() {
   if (done) return B200MOE_OK;
   B2_CUDA(cudaFuncSetAttribute(k_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<1>::kSmem));
   B2_CUDA(cudaFuncSetAttribute(k_gemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<2>::kSmem));
+  B2_CUDA(cudaFuncSetAttribute(k_router_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
   int dev = 0;
   B2_CUDA(cudaGetDevice(&dev));
   B2_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
@@ -910,10 +945,12 @@ int check_prefill_layer(const b200moe_layer *L, const char *who) {
 // Route stage: x (or rmsnorm(resid)) -> x16, ids, wb, sg (each to the given pointer).
 int route_stage(const void *x, int x_dtype, const float *resid, float eps, int T, const b200moe_layer *L,
                 __half *x16, int32_t *ids, uint16_t *wb, float *sg, const PrefillWS &w, cudaStream_t s) {
+  int rc = ensure_gemm_attrs();  // (also the router GEMM's shared-memory size)
+  if (rc) return rc;
   B2_CUDA(cudaMemsetAsync(w.err, 0, 4, s));
   k_prep<<<(T + 7) / 8, 256, 0, s>>>(x, x_dtype, resid, eps, T, L->sh_gate_w, w.xn, x16, sg, w.err);
   B2_CUDA(cudaGetLastError());
-  k_router_gemm<<<dim3((T + 63) / 64, kE / 64), 128, 0, s>>>(w.xn, T, L->router_w, L->logit_bias, w.logits);
+  k_router_gemm<<<dim3((T + 63) / 64, kE / 64), 128, kRgSmem, s>>>(w.xn, T, L->router_w, L->logit_bias, w.logits);
   B2_CUDA(cudaGetLastError());
   k_route_tok<<<(T + 7) / 8, 256, 0, s>>>(w.logits, T, ids, wb);
   B2_CUDA(cudaGetLastError());

@@ -4,6 +4,10 @@
   probe_row=None) -> (out [B,T,2048] f32, {"used", "ids"})``.
 * :func:`moe_router` -- the router stage set of ``engine/block_forward.py:614``:
   ``router_logits, topk_ids, topk_weights, topk_weights_f32``.
+* :func:`moe_shared`, :func:`moe_routed`, :func:`moe_block_stages` -- the stage dictionaries of
+  ``engine/block_forward.py:639-670`` (``shared_raw, shared_gate_prob, shared_out``;
+  ``expert_raw`` in top-k slot order, ``routed_sum``; all of them plus the router stages and
+  ``combined_out``), for stage-level parity gates.
 * :func:`moe_stack` -- the config-4 MoE sub-stack (``engine/m3_forward.py:714-737`` with
   the mixer sublayers removed): ``resid <- resid + moe_block(rmsnorm(resid))`` per layer.
 
@@ -172,9 +176,75 @@ def moe_stack_prefill(resid: torch.Tensor, E_: DeviceEngine, n_layers: int | Non
     return resid
 
 
+def _stage_route(g_row, E_, layer):
+    """fp16 rows, ids, bf16 weights and the shared-expert gate of every row of ``g_row``."""
+    L = _layer_of(E_, layer)
+    x, xd = _tokens(g_row, L.device)
+    T = x.shape[0]
+    dev = L.device
+    x16 = torch.empty((T, H), dtype=torch.float16, device=dev)
+    ids = torch.empty((T, TOPK), dtype=torch.int32, device=dev)
+    wb = torch.empty((T, TOPK), dtype=torch.int16, device=dev)
+    sg = torch.empty((T,), dtype=torch.float32, device=dev)
+    _abi.moe_route(x, xd, None, RMS_EPS, T, L.abi(), x16, ids, wb, sg, prefill_workspace(T, dev))
+    return L, x16, ids, wb, sg
+
+
+def _stage_experts(L, x16, ids, wb, e_lo, e_hi, sg):
+    T = x16.shape[0]
+    out = torch.empty((T, H), dtype=torch.float32, device=L.device)
+    _abi.moe_experts(x16, T, ids, wb, e_lo, e_hi, sg, L.abi(), out, False, prefill_workspace(T, L.device))
+    return out
+
+
+def moe_shared(g_row: torch.Tensor, E_, layer: int = 0, _routed=None) -> dict:
+    """``engine/block_forward.py:639 moe_shared``: ``shared_raw`` = W_ds (silu(W_gs x) * W_us x)
+    [T, 2048], ``shared_gate_prob`` = sigmoid(w_sg . x) [T, 1], ``shared_out`` = their product;
+    all f32. Computed by the expert stage of the prefill path (fp16 operands, f32 accumulate):
+    the shared expert alone with a unit gate gives ``shared_raw`` exactly as the block adds it."""
+    L, x16, ids, wb, sg = _routed if _routed is not None else _stage_route(g_row, E_, layer)
+    ones = torch.ones_like(sg)
+    raw = _stage_experts(L, x16, ids, wb, 0, 0, ones)  # no routed expert in range: 0 + 1 * shared
+    prob = sg.reshape(-1, 1)
+    return dict(shared_raw=raw, shared_gate_prob=prob, shared_out=prob * raw)
+
+
+def moe_routed(g_row: torch.Tensor, E_, route: dict | None = None, layer: int = 0, _routed=None) -> dict:
+    """``engine/block_forward.py:652 moe_routed``: ``expert_raw`` [T, 8, 2048] (each slot's
+    expert output before weighting, in top-k slot order) and ``routed_sum`` [T, 2048] (the
+    weighted outputs added in ascending expert id, the f32 form of ``engine/m3_forward.py:452,
+    464-465``). The routing is this library's own (``route`` is accepted for call-shape parity
+    and must match it: ``topk_ids`` are checked when given)."""
+    L, x16, ids, wb, sg = _routed if _routed is not None else _stage_route(g_row, E_, layer)
+    if route is not None and "topk_ids" in route:
+        if not torch.equal(route["topk_ids"].reshape(ids.shape).to(ids.dtype), ids):
+            raise Refused("route", "topk_ids differ from the device routing of these rows")
+    T = x16.shape[0]
+    unit = torch.full_like(wb, 0x3F80)  # bf16 1.0: y = o * 1
+    raw = torch.empty((T, TOPK, H), dtype=torch.float32, device=L.device)
+    for k in range(TOPK):  # one slot at a time: the other slots' ids are out of every range
+        ids_k = torch.full_like(ids, -1)
+        ids_k[:, k] = ids[:, k]
+        raw[:, k] = _stage_experts(L, x16, ids_k, unit, 0, E, None)
+    return dict(expert_raw=raw, routed_sum=_stage_experts(L, x16, ids, wb, 0, E, None))
+
+
+def moe_block_stages(g_row: torch.Tensor, E_, layer: int = 0) -> dict:
+    """``engine/block_forward.py:670 moe_block`` (stage order of its section 11.1): the shared
+    stages, the router stages (:func:`moe_router`), the routed stages, and ``combined_out`` =
+    ``routed_sum + shared_out`` -- bit-identical to :func:`moe_block` with ``path="prefill"``."""
+    r = _stage_route(g_row, E_, layer)
+    st = moe_shared(g_row, E_, layer, _routed=r)
+    st.update(moe_router(g_row, E_, layer))
+    st.update(moe_routed(g_row, E_, None, layer, _routed=r))
+    st["combined_out"] = st["routed_sum"] + st["shared_out"]
+    return st
+
+
 def prefill_status(T: int, device) -> int:
     """Device status word of the cached prefill workspace (0 = every pipeline wait completed)."""
     return _abi.prefill_status(prefill_workspace(T, device), T)
 
 
-__all__ = ["moe_block", "moe_router", "moe_stack", "Refused", "N_LAYERS"]
+__all__ = ["moe_block", "moe_router", "moe_shared", "moe_routed", "moe_block_stages", "moe_stack", "Refused",
+           "N_LAYERS"]

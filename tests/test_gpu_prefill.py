@@ -154,3 +154,42 @@ def test_expert_ranges_as_in_expert_parallelism(cuda, layer3, W):
     assert torch.equal(ids, info["ids"].reshape(T, 8))
     rel = float(torch.linalg.norm(out - ref.reshape(T, 2048)) / torch.linalg.norm(ref))
     assert torch.isfinite(out).all() and rel < 1e-5, rel
+
+
+def test_block_stages_match_oracle_stages(cuda, layer3):
+    """moe_block_stages (engine/block_forward.py:670's stage dictionary) against the f64
+    restatement's stage tensors on the same ids: router stages bit-exact, every numeric stage
+    within the prefill bar, combined_out bit-identical to the prefill block output."""
+    import torch
+    from oracle import moe as OM
+    from oracle.bf16 import bf16_bits_to_f32
+    from b200moe import moe, synth
+    T = 5
+    xb = synth.tokens(3, T, stream=6)
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).to(cuda)
+    st = moe.moe_block_stages(x, layer3, 0)
+    blk, _ = moe.moe_block(x, layer3, 0, path="prefill")
+    torch.cuda.synchronize()
+    assert moe.prefill_status(T, cuda) == 0
+    for k in ("shared_raw", "shared_gate_prob", "shared_out", "router_logits", "topk_ids", "topk_weights",
+              "topk_weights_f32", "expert_raw", "routed_sum", "combined_out"):
+        assert k in st, k
+    assert st["expert_raw"].shape == (T, 8, 2048) and st["shared_gate_prob"].shape == (T, 1)
+    assert torch.equal(st["combined_out"], blk.reshape(T, 2048))
+    Lh = host_layer(3, 0)
+    xf = bf16_bits_to_f32(xb)
+    r = OM.router(xf, Lh.wg, Lh.bias)
+    ids = st["topk_ids"].cpu().numpy()
+    assert (ids == r["ids"]).all()
+    assert (st["topk_weights"].view(torch.int16).cpu().numpy().view(np.uint16) == r["w_bf16"]).all()
+    ref = OM.moe_block_f64(xf, Lh, ids, r["w_bf16"])
+    pairs = (("shared_raw", "shared_raw"), ("shared_out", "shared_out"), ("routed_sum", "routed"),
+             ("combined_out", "out"))
+    for mine, theirs in pairs:
+        c = OM.compare(st[mine].cpu().numpy(), ref[theirs])
+        assert c["rel_l2"] < REL_L2 and c["max_abs_norm"] < MAX_ABS_NORM, (mine, c)
+    for k in range(8):
+        c = OM.compare(st["expert_raw"][:, k].cpu().numpy(), ref["expert_raw"][:, k])
+        assert c["rel_l2"] < REL_L2 and c["max_abs_norm"] < MAX_ABS_NORM, ("expert_raw", k, c)
+    g = st["shared_gate_prob"].reshape(T).cpu().numpy().astype(np.float64)
+    assert np.max(np.abs(g - ref["shared_gate_prob"])) < 1e-6
