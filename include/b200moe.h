@@ -65,6 +65,17 @@ const char *b200moe_last_error(void);
 int b200moe_q4k_dequant(const void *blocks, int64_t nblocks, void *out, int out_dtype,
                         void *stream);
 
+/* GGML block type ids (as stored in GGUF tensor infos) accepted by b200moe_dequant. */
+enum { B200MOE_TYPE_Q8_0 = 8, B200MOE_TYPE_Q4_K = 12, B200MOE_TYPE_Q5_K = 13, B200MOE_TYPE_Q6_K = 14 };
+
+/* Q4_K, Q5_K, Q6_K or Q8_0 (`type`, GGML id) -> f32 or bf16 for `nblocks` consecutive blocks,
+ * elements in stored order; `out` 16-byte aligned (and Q5_K `blocks`). The published Q4_K_M
+ * file stores most expert down matrices as Q5_K, three as Q6_K and the shared expert as Q8_0.
+ * Replaces tools/gguf_reader.py:178 dequant (_deq_q8_0 :238, _deq_q5_k :271, _deq_q6_k :299)
+ * and tools/gguf_fast_dequant.py:87 dequant_np (:109-150); bit-exact against both. */
+int b200moe_dequant(const void *blocks, int type, int64_t nblocks, void *out, int out_dtype,
+                    void *stream);
+
 /* Seeded synthetic Q4_K blocks [block0, block0+nblocks) of stream `stream_id` (the
  * benchmark's weight generator; the same bytes as oracle/q4k.py synth_blocks). No
  * counterpart in the reference, which reads a GGUF file instead. */

@@ -17,7 +17,7 @@ OK, EINVAL, ECUDA, ESIZE = 0, 1, 2, 3
 F32, BF16 = 0, 1
 
 # Every exported symbol of include/b200moe.h (checked by tests/test_abi_exports.py).
-EXPORTS = ("b200moe_abi_version", "b200moe_last_error", "b200moe_q4k_dequant",
+EXPORTS = ("b200moe_abi_version", "b200moe_last_error", "b200moe_q4k_dequant", "b200moe_dequant",
            "b200moe_synth_q4k", "b200moe_router_workspace_size", "b200moe_router",
            "b200moe_decode_workspace_size",
            "b200moe_moe_decode", "b200moe_moe_decode_noalloc", "b200moe_decode_persistent_info",
@@ -62,6 +62,8 @@ def lib():
         L.b200moe_last_error.argtypes = []
         L.b200moe_q4k_dequant.restype = i32
         L.b200moe_q4k_dequant.argtypes = [vp, i64, vp, i32, vp]
+        L.b200moe_dequant.restype = i32
+        L.b200moe_dequant.argtypes = [vp, i32, i64, vp, i32, vp]
         L.b200moe_synth_q4k.restype = i32
         L.b200moe_synth_q4k.argtypes = [u64, ctypes.c_uint32, i64, i64, vp, vp]
         L.b200moe_router_workspace_size.restype = sz
@@ -130,6 +132,18 @@ def q4k_dequant(blocks, out, out_dtype: int, stream=None):
     nb = blocks.numel() // 144
     _check("b200moe_q4k_dequant", lib().b200moe_q4k_dequant(ptr(blocks), nb, ptr(out), out_dtype,
                                                              _stream(stream)))
+
+
+# GGML block type ids accepted by b200moe_dequant, and their block sizes (bytes, elements).
+TYPE_IDS = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
+BLOCK_GEOM = {"Q8_0": (34, 32), "Q4_K": (144, 256), "Q5_K": (176, 256), "Q6_K": (210, 256)}
+
+
+def dequant(blocks, tname: str, out, out_dtype: int, stream=None):
+    """``b200moe_dequant`` of every whole block in the uint8 tensor ``blocks``."""
+    nb = blocks.numel() // BLOCK_GEOM[tname][0]
+    _check("b200moe_dequant", lib().b200moe_dequant(ptr(blocks), TYPE_IDS[tname], nb, ptr(out), out_dtype,
+                                                     _stream(stream)))
 
 
 def synth_q4k(seed: int, stream_id: int, block0: int, nblocks: int, out, stream=None):

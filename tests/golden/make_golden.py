@@ -15,6 +15,9 @@ files committed beside this script:
   duck-typed weight provider that serves the seeded synthetic Q4_K bytes through the
   reference's ``gguf_fast_dequant.dequant_np`` (4 tokens, config-0 field law, seed 0).
 * ``rmsnorm.npz`` -- ``engine/m3_forward.py:303 rmsnorm_a`` (weight 1) on seeded rows.
+* ``kquant_dequant.npz`` -- seeded and edge-case Q5_K, Q6_K and Q8_0 blocks decoded by the
+  reference's ``tools/gguf_reader.py:dequant`` (checked identical to
+  ``tools/gguf_fast_dequant.py:dequant_np``). ``python make_golden.py kquants`` makes only this.
 
 The Q4_K import chain needs ``tools/ggml_block_geom.py``'s un-vendored third-party header
 (llama.cpp ``ggml/src/ggml-common.h`` @ d327bf1f0780f87b8c01b367b61853b0c291d7c4); a shim
@@ -215,8 +218,50 @@ def make_rmsnorm(M3):
     print("rmsnorm.npz")
 
 
+def kquant_cases(tname):
+    from oracle import kquants as KQ
+    bb = KQ.BLOCK_BYTES[tname]
+    blocks = [KQ.random_blocks(tname, 24, seed={"Q5_K": 51, "Q6_K": 61, "Q8_0": 81}[tname])]
+    edge = np.zeros((4, bb), dtype=np.uint8)
+    dcol = {"Q8_0": 0, "Q5_K": 0, "Q6_K": 208}[tname]
+    one = np.array([1.0], dtype=np.float16).view(np.uint8)
+    edge[0, dcol:dcol + 2] = one                     # d = 1, every quant 0 (Q6_K: q - 32 = -32)
+    edge[1] = 0xFF                                   # every field saturated (d = NaN bits)
+    edge[1, dcol:dcol + 2] = np.array([-2.0], dtype=np.float16).view(np.uint8)
+    if tname == "Q5_K":
+        edge[1, 2:4] = np.array([0.5], dtype=np.float16).view(np.uint8)
+    edge[2] = edge[1]
+    edge[2, dcol:dcol + 2] = np.array([6.1e-5], dtype=np.float16).view(np.uint8)   # near-subnormal d
+    edge[3, dcol:dcol + 2] = np.array([0.0], dtype=np.float16).view(np.uint8)      # d = 0
+    edge[3, dcol + 2:] = 0x5A if dcol == 0 else edge[3, dcol + 2:]
+    if tname == "Q6_K":
+        edge[3, 192:208] = 0x80                       # scales = -128
+        edge[3, 208:210] = np.array([3.0e-3], dtype=np.float16).view(np.uint8)
+    blocks.append(edge)
+    return np.concatenate(blocks)
+
+
+def make_kquants(GR, FD):
+    out = {}
+    for tname in ("Q5_K", "Q6_K", "Q8_0"):
+        blocks = kquant_cases(tname)
+        n = blocks.shape[0] * (32 if tname == "Q8_0" else 256)
+        ref = np.array(GR.dequant(blocks.tobytes(), tname, n), dtype=np.float32)
+        fast = FD.dequant_np(blocks.tobytes(), tname, n)
+        same = (ref.view(np.uint32) == fast.view(np.uint32)) | (np.isnan(ref) & np.isnan(fast))
+        assert same.all(), "reference slow and fast %s decoders disagree" % tname
+        out[tname + "_blocks"] = blocks
+        out[tname + "_ref_f32_bits"] = ref.view(np.uint32)
+    np.savez_compressed(os.path.join(HERE, "kquant_dequant.npz"), **out)
+    print("kquant_dequant.npz:", {k: v.shape for k, v in out.items()})
+
+
 if __name__ == "__main__":
     GR, FD, M3 = import_reference()
+    if sys.argv[1:] == ["kquants"]:
+        make_kquants(GR, FD)
+        sys.exit(0)
+    make_kquants(GR, FD)
     make_dequant(GR, FD)
     make_router(M3)
     make_block(M3, FD)

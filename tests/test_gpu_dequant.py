@@ -98,3 +98,31 @@ def test_dequant_edges(cuda):
         _abi.q4k_dequant(blocks[8:8 + 144], out, _abi.F32)           # unaligned source
     with pytest.raises(_abi.B200MoeError):
         _abi.q4k_dequant(blocks[:144], out, 7)                        # bad dtype
+
+
+@pytest.mark.parametrize("tname", ["Q5_K", "Q6_K", "Q8_0"])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_kquant_dequant_matches_reference_decoder(cuda, tname, dtype):
+    """b200moe_dequant for the published file's other block formats against the reference's
+    own decoder outputs (tests/golden/kquant_dequant.npz): bit-exact f32; bf16 = RNE of those."""
+    import os
+    import torch
+    from oracle.bf16 import f32_to_bf16_bits
+    from b200moe import _abi
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "kquant_dequant.npz"))
+    blocks = g[tname + "_blocks"]
+    ref = g[tname + "_ref_f32_bits"]
+    dev = torch.from_numpy(blocks.reshape(-1).copy()).to(cuda)
+    if dtype == "f32":
+        out = torch.full((ref.size,), float("nan"), dtype=torch.float32, device=cuda)
+        _abi.dequant(dev, tname, out, _abi.F32)
+        torch.cuda.synchronize()
+        assert _bits_equal(out.cpu().numpy(), ref).all()
+    else:
+        out = torch.zeros((ref.size,), dtype=torch.int16, device=cuda)
+        _abi.dequant(dev, tname, out, _abi.BF16)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy().view(np.uint16)
+        want = f32_to_bf16_bits(ref.view(np.float32))
+        nan = ((got & 0x7FFF) > 0x7F80) & ((want & 0x7FFF) > 0x7F80)
+        assert ((got == want) | nan).all()
