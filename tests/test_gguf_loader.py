@@ -1,0 +1,140 @@
+"""The GGUF reader (qwen3.6-35b-a3b_b200/gguf.py) on files written here by a minimal GGUF v3
+writer: header and metadata parse, tensor byte views at the right offsets (checked by marker
+bytes at both ends of every tensor), the Q4_K / bf16 type rules, the F32-router rounding
+switch, and the refusals (wrong type, wrong shape, missing tensor, truncated file). Full-size
+tensors are sparse holes in the file, so the test writes little and reads little."""
+import struct
+
+import numpy as np
+import pytest
+
+H, I, E = 2048, 512, 256
+Q4K, Q5K, F32, BF16 = 12, 13, 0, 30
+SIZES = {Q4K: (256, 144), Q5K: (256, 176), F32: (1, 4), BF16: (1, 2)}
+
+
+def _s(x: str) -> bytes:
+    b = x.encode()
+    return struct.pack("<Q", len(b)) + b
+
+
+def write_gguf(path, tensors, align=32, truncate=False):
+    """tensors: list of (name, dims (GGUF order), type, {offset_in_tensor: bytes})."""
+    kv = [("general.architecture", 8, _s("qwen35moe")), ("general.alignment", 4, struct.pack("<I", align)),
+          ("qwen35moe.expert_count", 4, struct.pack("<I", E)),
+          ("tokenizer.ggml.tokens", 9, struct.pack("<IQ", 8, 2) + _s("a") + _s("b"))]
+    head = b"GGUF" + struct.pack("<IQQ", 3, len(tensors), len(kv))
+    for k, t, v in kv:
+        head += _s(k) + struct.pack("<I", t) + v
+    offs, off = [], 0
+    for name, dims, typ, _ in tensors:
+        n = int(np.prod(dims))
+        nbytes = n // SIZES[typ][0] * SIZES[typ][1]
+        offs.append((off, nbytes))
+        head += _s(name) + struct.pack("<I", len(dims)) + b"".join(struct.pack("<Q", d) for d in dims)
+        head += struct.pack("<IQ", typ, off)
+        off = (off + nbytes + align - 1) // align * align
+    data0 = (len(head) + align - 1) // align * align
+    with open(path, "wb") as f:
+        f.write(head)
+        for (name, dims, typ, marks), (o, nb) in zip(tensors, offs):
+            for at, b in marks.items():
+                f.seek(data0 + o + (at if at >= 0 else nb + at))
+                f.write(b)
+        end = data0 + offs[-1][0] + offs[-1][1]
+        f.truncate(end - 100 if truncate else end)
+    return data0
+
+
+def layer_tensors(l, down_type=Q4K, router_type=BF16, router_dims=(H, E)):
+    p = "blk.%d." % l
+    mk = lambda tag: {0: tag * 16, -16: tag[::-1] * 16}  # noqa: E731
+    t = [(p + "ffn_gate_exps.weight", (H, I, E), Q4K, mk(b"G")), (p + "ffn_up_exps.weight", (H, I, E), Q4K, mk(b"U")),
+         (p + "ffn_down_exps.weight", (I, H, E), down_type, mk(b"D")),
+         (p + "ffn_gate_shexp.weight", (H, I), Q4K, mk(b"g")), (p + "ffn_up_shexp.weight", (H, I), Q4K, mk(b"u")),
+         (p + "ffn_down_shexp.weight", (I, H), Q4K, mk(b"d"))]
+    rng = np.random.default_rng(l)
+    w = rng.normal(0, 0.02, size=E * H).astype(np.float32)
+    g = rng.normal(0, 0.02, size=H).astype(np.float32)
+    if router_type == BF16:
+        from oracle.bf16 import f32_to_bf16_bits
+        t.append((p + "ffn_gate_inp.weight", router_dims, BF16, {0: f32_to_bf16_bits(w).tobytes()}))
+        t.append((p + "ffn_gate_inp_shexp.weight", (H, 1), BF16, {0: f32_to_bf16_bits(g).tobytes()}))
+    else:
+        t.append((p + "ffn_gate_inp.weight", router_dims, F32, {0: w.tobytes()}))
+        t.append((p + "ffn_gate_inp_shexp.weight", (H,), F32, {0: g.tobytes()}))
+    return t, w, g
+
+
+def _mod():
+    import __graft_entry__ as G
+    G.load_package()
+    from b200moe import gguf
+    return gguf
+
+
+def test_header_and_layer_views(tmp_path):
+    gguf = _mod()
+    t, w, g = layer_tensors(3)
+    path = str(tmp_path / "m.gguf")
+    write_gguf(path, t)
+    with gguf.GgufFile(path) as gf:
+        assert gf.version == 3 and gf.meta["general.architecture"] == "qwen35moe"
+        assert gf.meta["tokenizer.ggml.tokens"] == ["a", "b"]
+        assert gf.info("blk.3.ffn_down_exps.weight").dims == (I, H, E)
+        blocks, router, shgate = gguf.layer_host(gf, 3)
+        sizes = {"gate": E * I * 8 * 144, "up": E * I * 8 * 144, "down": E * H * 2 * 144,
+                 "sh_gate": I * 8 * 144, "sh_up": I * 8 * 144, "sh_down": H * 2 * 144}
+        tags = {"gate": b"G", "up": b"U", "down": b"D", "sh_gate": b"g", "sh_up": b"u", "sh_down": b"d"}
+        for k, v in blocks.items():
+            assert v.dtype == np.uint8 and v.size == sizes[k], k
+            assert bytes(v[:16]) == tags[k] * 16 and bytes(v[-16:]) == tags[k] * 16, k
+        from oracle.bf16 import f32_to_bf16_bits
+        assert np.array_equal(router, f32_to_bf16_bits(w)) and np.array_equal(shgate, f32_to_bf16_bits(g))
+        del blocks
+
+
+def test_f32_router_needs_explicit_rounding(tmp_path):
+    gguf = _mod()
+    t, w, g = layer_tensors(0, router_type=F32)
+    path = str(tmp_path / "m.gguf")
+    write_gguf(path, t)
+    with gguf.GgufFile(path) as gf:
+        with pytest.raises(gguf.GgufError) as ei:
+            gguf.layer_host(gf, 0)
+        assert ei.value.tag == "type" and "F32" in str(ei.value)
+        blocks, router, shgate = gguf.layer_host(gf, 0, round_router=True)
+        from oracle.bf16 import f32_to_bf16_bits
+        assert np.array_equal(router, f32_to_bf16_bits(w)) and np.array_equal(shgate, f32_to_bf16_bits(g))
+        del blocks
+
+
+def test_refusals(tmp_path):
+    gguf = _mod()
+    t, _, _ = layer_tensors(1, down_type=Q5K)
+    p1 = str(tmp_path / "q5.gguf")
+    write_gguf(p1, t)
+    with gguf.GgufFile(p1) as gf:
+        with pytest.raises(gguf.GgufError) as ei:
+            gguf.layer_host(gf, 1)
+        assert ei.value.tag == "type" and "Q5_K" in str(ei.value) and "b200moe_dequant" in str(ei.value)
+        with pytest.raises(gguf.GgufError) as ei:
+            gguf.layer_host(gf, 2)
+        assert ei.value.tag == "missing"
+    t, _, _ = layer_tensors(1, router_dims=(H, 128))
+    p2 = str(tmp_path / "shape.gguf")
+    write_gguf(p2, t)
+    with gguf.GgufFile(p2) as gf:
+        with pytest.raises(gguf.GgufError) as ei:
+            gguf.layer_host(gf, 1)
+        assert ei.value.tag == "shape"
+    t, _, _ = layer_tensors(1)
+    p3 = str(tmp_path / "short.gguf")
+    write_gguf(p3, t, truncate=True)
+    with pytest.raises(gguf.GgufError) as ei:
+        gguf.GgufFile(p3)
+    assert ei.value.tag == "format"
+    p4 = str(tmp_path / "bad.gguf")
+    open(p4, "wb").write(b"GGML" + b"\0" * 64)
+    with pytest.raises(gguf.GgufError):
+        gguf.GgufFile(p4)
