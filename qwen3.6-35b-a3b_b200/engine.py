@@ -12,6 +12,8 @@ dequantized device tensors and exist for inspection, not for the hot path.
 """
 from __future__ import annotations
 
+import warnings
+
 import numpy as np
 import torch
 
@@ -72,8 +74,10 @@ class DeviceLayer:
         """From host arrays: ``blocks[kind]`` uint8 Q4_K bytes for gate/up/down/sh_gate/sh_up/sh_down
         (GGUF order), bf16 bit patterns for the router and shared gate."""
         dev = torch.device(device)
-        t = {k: torch.from_numpy(np.ascontiguousarray(v, dtype=np.uint8).reshape(-1)).to(dev)
-             for k, v in blocks.items()}
+        with warnings.catch_warnings():  # read-only views (e.g. a memory-mapped GGUF): only read, then copied
+            warnings.filterwarnings("ignore", message="The given NumPy array is not writable")
+            t = {k: torch.from_numpy(np.ascontiguousarray(v, dtype=np.uint8).reshape(-1)).to(dev)
+                 for k, v in blocks.items()}
         lb = None if logit_bias is None else torch.as_tensor(np.asarray(logit_bias, np.float32)).to(dev)
         return cls(t["gate"], t["up"], t["down"], t["sh_gate"], t["sh_up"], t["sh_down"],
                    _bf16_tensor(router_w_bits, dev), _bf16_tensor(sh_gate_w_bits, dev), lb)
