@@ -103,19 +103,54 @@ PrefillWS carve_prefill(void *ws, int T) {
 }
 
 // ------------------------------------------------------------------------- k_prep
-__global__ void __launch_bounds__(256) k_prep(const void *x, int x_dtype, const float *resid, float eps, int T,
-                                              const uint16_t *wsg, float *xn, __half *x16, float *sg, int32_t *err) {
-  const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+// Warp per token. The arithmetic is per lane over its 64-element chunk (the declared RMSNorm
+// order; the shared-expert gate as the decode path computes it), but global memory is read and
+// written in whole coalesced rows: the row is staged in shared memory as 32 segments of 64 at a
+// 68-float pitch (conflict-free both ways).
+constexpr int kPrepWarps = 4;
+constexpr int kPrepPitch = 68;
+
+__global__ void __launch_bounds__(32 * kPrepWarps) k_prep(const void *x, int x_dtype, const float *resid, float eps,
+                                                          int T, const uint16_t *wsg, float *xn, __half *x16,
+                                                          float *sg, int32_t *err) {
+  __shared__ __align__(16) float rows[kPrepWarps][32 * kPrepPitch];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int t = blockIdx.x * kPrepWarps + wp;
   if (t >= T) return;
-  float v[64];
-  if (resid) {
-    const float *r = resid + (size_t)t * kH + 64 * lane;
+  float *row = rows[wp];
+  auto at = [](int e) { return (e >> 6) * kPrepPitch + (e & 63); };  // element -> staged position
+  // coalesced load of the token's row into the staging row
+  if (resid || x_dtype != B200MOE_BF16) {
+    const float *src = resid ? resid + (size_t)t * kH : reinterpret_cast<const float *>(x) + (size_t)t * kH;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float4 a = __ldcg(reinterpret_cast<const float4 *>(r + 4 * i));
+      const int e = 4 * (32 * i + lane);
+      const float4 a = resid ? __ldcg(reinterpret_cast<const float4 *>(src + e))
+                             : __ldg(reinterpret_cast<const float4 *>(src + e));
+      *reinterpret_cast<float4 *>(row + at(e)) = a;
+    }
+  } else {
+    const uint16_t *xb = reinterpret_cast<const uint16_t *>(x) + (size_t)t * kH;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = 8 * (32 * i + lane);
+      const uint4 u = __ldg(reinterpret_cast<const uint4 *>(xb + e));
+      *reinterpret_cast<float4 *>(row + at(e)) = make_float4(bf16f(u.x), bf16f(u.x >> 16), bf16f(u.y), bf16f(u.y >> 16));
+      *reinterpret_cast<float4 *>(row + at(e + 4)) =
+          make_float4(bf16f(u.z), bf16f(u.z >> 16), bf16f(u.w), bf16f(u.w >> 16));
+    }
+  }
+  __syncwarp();
+  float v[64];
+  {
+    const float *c = row + lane * kPrepPitch;  // this lane's chunk: elements 64 lane .. 64 lane + 63
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float4 a = *reinterpret_cast<const float4 *>(c + 4 * i);
       v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
     }
+  }
+  if (resid) {
     float ss = 0.0f;
 #pragma unroll
     for (int i = 0; i < 64; ++i) ss = __fmaf_rn(v[i], v[i], ss);
@@ -125,43 +160,17 @@ __global__ void __launch_bounds__(256) k_prep(const void *x, int x_dtype, const 
     const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, 2048.0f), eps)));
 #pragma unroll
     for (int i = 0; i < 64; ++i) v[i] = __fmul_rn(v[i], rs);
-  } else if (x_dtype == B200MOE_BF16) {
-    const uint16_t *xb = reinterpret_cast<const uint16_t *>(x) + (size_t)t * kH + 64 * lane;
+    float *c = row + lane * kPrepPitch;  // the normalised chunk back into the staging row
+    __syncwarp();
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4 *>(xb + 8 * i));
-      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        v[8 * i + 2 * q] = bf16f(uw[q]);
-        v[8 * i + 2 * q + 1] = bf16f(uw[q] >> 16);
-      }
-    }
-  } else {
-    const float *xf = reinterpret_cast<const float *>(x) + (size_t)t * kH + 64 * lane;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float4 a = __ldg(reinterpret_cast<const float4 *>(xf + 4 * i));
-      v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
-    }
+    for (int i = 0; i < 16; ++i)
+      *reinterpret_cast<float4 *>(c + 4 * i) = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
   }
-  float *dst = xn + (size_t)t * kH + 64 * lane;
-  __half *d16 = x16 + (size_t)t * kH + 64 * lane;
-  float z = 0.0f;
   bool range_bad = false;
 #pragma unroll
   for (int i = 0; i < 64; ++i) range_bad |= !(fabsf(v[i]) <= 65504.0f);
   if (__any_sync(0xFFFFFFFFu, range_bad) && lane == 0) atomicOr(err, kErrRange);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    *reinterpret_cast<float4 *>(dst + 4 * i) = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-    const __half2 a = __floats2half2_rn(v[4 * i], v[4 * i + 1]);
-    const __half2 b = __floats2half2_rn(v[4 * i + 2], v[4 * i + 3]);
-    uint2 pk;
-    pk.x = *reinterpret_cast<const uint32_t *>(&a);
-    pk.y = *reinterpret_cast<const uint32_t *>(&b);
-    *reinterpret_cast<uint2 *>(d16 + 4 * i) = pk;
-  }
+  float z = 0.0f;
   const uint16_t *w = wsg + 64 * lane;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -175,6 +184,21 @@ __global__ void __launch_bounds__(256) k_prep(const void *x, int x_dtype, const 
   }
   z = warp_sum(z);
   if (lane == 0) sg[t] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+  __syncwarp();
+  // coalesced stores of the f32 row and its fp16 copy
+  float *dst = xn + (size_t)t * kH;
+  __half *d16 = x16 + (size_t)t * kH;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int e = 4 * (32 * i + lane);
+    const float4 a = *reinterpret_cast<const float4 *>(row + at(e));
+    *reinterpret_cast<float4 *>(dst + e) = a;
+    const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+    uint2 pk;
+    pk.x = *reinterpret_cast<const uint32_t *>(&h0);
+    pk.y = *reinterpret_cast<const uint32_t *>(&h1);
+    *reinterpret_cast<uint2 *>(d16 + e) = pk;
+  }
 }
 
 // ------------------------------------------------------------------------- k_router_gemm
@@ -948,7 +972,8 @@ int route_stage(const void *x, int x_dtype, const float *resid, float eps, int T
   int rc = ensure_gemm_attrs();  // (also the router GEMM's shared-memory size)
   if (rc) return rc;
   B2_CUDA(cudaMemsetAsync(w.err, 0, 4, s));
-  k_prep<<<(T + 7) / 8, 256, 0, s>>>(x, x_dtype, resid, eps, T, L->sh_gate_w, w.xn, x16, sg, w.err);
+  k_prep<<<(T + kPrepWarps - 1) / kPrepWarps, 32 * kPrepWarps, 0, s>>>(x, x_dtype, resid, eps, T, L->sh_gate_w,
+                                                                   w.xn, x16, sg, w.err);
   B2_CUDA(cudaGetLastError());
   k_router_gemm<<<dim3((T + 63) / 64, kE / 64), 128, kRgSmem, s>>>(w.xn, T, L->router_w, L->logit_bias, w.logits);
   B2_CUDA(cudaGetLastError());
