@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define B200MOE_ABI_VERSION 1
+#define B200MOE_ABI_VERSION 2
 #define B200MOE_HIDDEN 2048
 #define B200MOE_EXPERTS 256
 #define B200MOE_TOPK 8
@@ -49,9 +49,11 @@ typedef struct b200moe_layer {
     const void *sh_gate;
     const void *sh_up;
     const void *sh_down;
-    const uint16_t *router_w;
-    const uint16_t *sh_gate_w;
+    const void *router_w;    /* [256][2048] router weights, bf16 or f32 (router_f32) */
+    const void *sh_gate_w;   /* [2048] shared-expert gate weights, same type */
     const float *logit_bias; /* [256] f32 added to R1's f32 dot before the bf16 cast, or NULL */
+    int32_t router_f32;      /* 0: router_w / sh_gate_w are bf16; 1: f32 (the published file's
+                                F32 ffn_gate_inp / ffn_gate_inp_shexp, used exactly) */
 } b200moe_layer;
 
 /* ABI version (B200MOE_ABI_VERSION) and the last error message on this thread. */
@@ -85,13 +87,13 @@ int b200moe_synth_q4k(uint64_t seed, uint32_t stream_id, int64_t block0, int64_t
 /* Workspace bytes for b200moe_router with T tokens. */
 size_t b200moe_router_workspace_size(int T);
 
-/* Router R1..R5 for T tokens: x [T][2048] (f32 or bf16), W_g [256][2048] bf16, optional f32
- * logit bias [256]. Outputs (each may be NULL): logits [T][256] bf16, ids [T][8] int32 in
+/* Router R1..R5 for T tokens: x [T][2048] (f32 or bf16), W_g [256][2048] bf16 (router_dtype
+ * B200MOE_BF16) or f32 (B200MOE_F32), optional f32 logit bias [256]. Outputs (each may be NULL): logits [T][256] bf16, ids [T][8] int32 in
  * top-k rank order, w_f32 [T][8] renormalised weights, w_bf16 [T][8] their R5 bf16 cast.
  * Replaces engine/m3_forward.py:443-446 and engine/block_forward.py:614 moe_router.
  * Deterministic declared order (R1 32x64 chunked fmaf, softmax with the library's own exp,
  * top-8 by (p desc, index asc)); bit-exact against oracle/c/oracle.c b2o_router. */
-int b200moe_router(const void *x, int x_dtype, int T, const uint16_t *router_w,
+int b200moe_router(const void *x, int x_dtype, int T, const void *router_w, int router_dtype,
                    const float *logit_bias, uint16_t *logits, int32_t *ids, float *w_f32,
                    uint16_t *w_bf16, void *ws, size_t ws_bytes, void *stream);
 

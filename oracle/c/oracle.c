@@ -9,7 +9,8 @@
  *                     f32 route: d*sc, *q and dmin*m are exact in f32, so the one rounding at the
  *                     subtraction equals the reference's f64-then-f32 rounding
  *                     (prototype/q4k_dequant/q4k_dequant_kernels.h:43-60 argues the same).
- *   b2o_router        R1..R5 of engine/m3_forward.py:443-446 and engine/block_forward.py:631-635,
+ *   b2o_router        R1..R5 of engine/m3_forward.py:443-446 and engine/block_forward.py:631-635
+ *   (b2o_router_f32w  the same with f32 router weights),
  *                     under the DECLARED deterministic order that the CUDA router also follows:
  *                       R1  logit[e] = bf16_rne( (((c_0 + c_1) + c_2) + ... + c_31) [+ bias[e]] )
  *                           c_j = fmaf-chain over k = 64j .. 64j+63 ascending, starting at 0.0f
@@ -126,24 +127,40 @@ void b2o_q4k_dequant(const uint8_t *blk, int64_t nb, float *out) {
     }
 }
 
-/* R1 for one (token, expert): the declared 32-chunk order. */
-static float logit_f32(const float *x, const uint16_t *w) {
+/* R1 for one (token, expert): the declared 32-chunk order, weights as f32 values (a bf16 router
+ * widens exactly, so both router widths share this arithmetic). */
+static float logit_f32(const float *x, const float *w) {
     float tot = 0.0f;
     for (int c = 0; c < 32; ++c) {
         float acc = 0.0f;
         for (int i = 0; i < 64; ++i) {
             const int k = 64 * c + i;
-            acc = fmaf(x[k], bf16_to_f32(w[k]), acc);
+            acc = fmaf(x[k], w[k], acc);
         }
         tot = (c == 0) ? acc : tot + acc;
     }
     return tot;
 }
 
-float b2o_dot_chunked(const float *x, const uint16_t *w) { return logit_f32(x, w); }
+float b2o_dot_chunked(const float *x, const uint16_t *w) {
+    float wf[H];
+    for (int k = 0; k < H; ++k) wf[k] = bf16_to_f32(w[k]);
+    return logit_f32(x, wf);
+}
+
+/* The router with f32 router weights (the published file stores ffn_gate_inp as F32). */
+void b2o_router_f32w(const float *x, int T, const float *wg, const float *bias, uint16_t *logits_out,
+                     float *probs_out, int32_t *ids, float *w_f32, uint16_t *w_bf16);
 
 void b2o_router(const float *x, int T, const uint16_t *wg, const float *bias, uint16_t *logits_out,
                 float *probs_out, int32_t *ids, float *w_f32, uint16_t *w_bf16) {
+    static float wf[(int64_t)E * H];
+    for (int64_t k = 0; k < (int64_t)E * H; ++k) wf[k] = bf16_to_f32(wg[k]);
+    b2o_router_f32w(x, T, wf, bias, logits_out, probs_out, ids, w_f32, w_bf16);
+}
+
+void b2o_router_f32w(const float *x, int T, const float *wg, const float *bias, uint16_t *logits_out,
+                     float *probs_out, int32_t *ids, float *w_f32, uint16_t *w_bf16) {
     for (int t = 0; t < T; ++t) {
         const float *xt = x + (int64_t)t * H;
         float lg[E], ev[E], pr[E];

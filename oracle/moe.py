@@ -40,6 +40,7 @@ def lib():
         L.b2o_expf.argtypes = [ctypes.c_float]
         L.b2o_q4k_dequant.argtypes = [ctypes.c_void_p, ctypes.c_int64, f32p]
         L.b2o_router.argtypes = [f32p, ctypes.c_int, u16p, f32p, u16p, f32p, i32p, f32p, u16p]
+        L.b2o_router_f32w.argtypes = [f32p, ctypes.c_int, f32p, f32p, u16p, f32p, i32p, f32p, u16p]
         L.b2o_rmsnorm.argtypes = [f32p, ctypes.c_int, ctypes.c_float, f32p]
         L.b2o_dot_chunked.restype = ctypes.c_float
         L.b2o_dot_chunked.argtypes = [f32p, u16p]
@@ -65,10 +66,18 @@ def dequant_c(blocks: np.ndarray) -> np.ndarray:
     return out
 
 
+def wvals(w) -> np.ndarray:
+    """Router / shared-gate weights as f32 values: bf16 bits (uint16) widen exactly; f32 as is."""
+    w = np.asarray(w)
+    return w.astype(np.float32) if w.dtype == np.float32 else bf16_bits_to_f32(w.astype(np.uint16))
+
+
 def router(x_f32: np.ndarray, wg_bits: np.ndarray, bias: np.ndarray | None = None) -> dict:
-    """Declared-order R1..R5 for x [T, 2048] (f32 values), W_g [256, 2048] bf16 bits."""
+    """Declared-order R1..R5 for x [T, 2048] (f32 values), W_g [256, 2048] as bf16 bits
+    (uint16) or as f32 values (float32: the published file's F32 router)."""
     x = np.ascontiguousarray(x_f32, dtype=np.float32).reshape(-1, H)
-    wg = np.ascontiguousarray(wg_bits, dtype=np.uint16).reshape(E, H)
+    f32w = np.asarray(wg_bits).dtype == np.float32
+    wg = np.ascontiguousarray(wg_bits, dtype=np.float32 if f32w else np.uint16).reshape(E, H)
     T = x.shape[0]
     logits = np.empty((T, E), dtype=np.uint16)
     probs = np.empty((T, E), dtype=np.float32)
@@ -76,7 +85,8 @@ def router(x_f32: np.ndarray, wg_bits: np.ndarray, bias: np.ndarray | None = Non
     wf = np.empty((T, TOPK), dtype=np.float32)
     wb = np.empty((T, TOPK), dtype=np.uint16)
     b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
-    lib().b2o_router(_p(x, ctypes.c_float), T, _p(wg, ctypes.c_uint16),
+    (lib().b2o_router_f32w if f32w else lib().b2o_router)(
+                     _p(x, ctypes.c_float), T, _p(wg, ctypes.c_float if f32w else ctypes.c_uint16),
                      None if b is None else _p(b, ctypes.c_float), _p(logits, ctypes.c_uint16),
                      _p(probs, ctypes.c_float), _p(ids, ctypes.c_int32), _p(wf, ctypes.c_float),
                      _p(wb, ctypes.c_uint16))
@@ -105,8 +115,9 @@ class HostLayer:
 
     def __init__(self, block_fn, wg, wsg, bias=None):
         self._block_fn = block_fn     # (kind, first_block, nblocks) -> uint8 [n, 144]
-        self.wg = np.ascontiguousarray(wg, dtype=np.uint16).reshape(E, H)
-        self.wsg = np.ascontiguousarray(wsg, dtype=np.uint16).reshape(H)
+        keep = lambda a: np.asarray(a) if np.asarray(a).dtype == np.float32 else np.asarray(a, np.uint16)  # noqa
+        self.wg = np.ascontiguousarray(keep(wg)).reshape(E, H)      # bf16 bits, or f32 values
+        self.wsg = np.ascontiguousarray(keep(wsg)).reshape(H)
         self.bias = None if bias is None else np.asarray(bias, dtype=np.float32)
 
     def matrix(self, kind: str, e: int = 0) -> np.ndarray:
@@ -137,7 +148,7 @@ def moe_block_f64(x_f32: np.ndarray, layer: HostLayer, ids: np.ndarray, w_bf16: 
     wsg_u = layer.matrix("sh_up").astype(np.float64)
     wsg_d = layer.matrix("sh_down").astype(np.float64)
     shared_raw = (silu64(x @ wsg_g.T) * (x @ wsg_u.T)) @ wsg_d.T
-    gate_prob = 1.0 / (1.0 + np.exp(-(x @ bf16_bits_to_f32(layer.wsg).astype(np.float64))))
+    gate_prob = 1.0 / (1.0 + np.exp(-(x @ wvals(layer.wsg).astype(np.float64))))
     shared = gate_prob[:, None] * shared_raw
     w = bf16_bits_to_f32(np.asarray(w_bf16, dtype=np.uint16)).astype(np.float64).reshape(T, TOPK)
     ids = np.asarray(ids).reshape(T, TOPK)
@@ -172,10 +183,10 @@ def moe_block_port(x_f32, layer: HostLayer, threads: int | None = None) -> tuple
     wd = torch.from_numpy(layer.matrix("sh_down"))
     up = F.linear(x, wg)
     shared = F.linear(F.silu(up) * F.linear(x, wu), wd)
-    wsg = torch.from_numpy(bf16_bits_to_f32(layer.wsg).copy()).reshape(1, H)
+    wsg = torch.from_numpy(wvals(layer.wsg).copy()).reshape(1, H)
     shgate = torch.sigmoid(F.linear(x, wsg)).view(x.shape[0], 1)
     shared = shgate * shared
-    wr = torch.from_numpy(bf16_bits_to_f32(layer.wg).copy())
+    wr = torch.from_numpy(wvals(layer.wg).copy())
     lf = F.linear(x, wr)
     if layer.bias is not None:
         lf = lf + torch.from_numpy(layer.bias)

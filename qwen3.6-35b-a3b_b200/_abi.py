@@ -40,7 +40,8 @@ class Layer(ctypes.Structure):
                 ("down", ctypes.c_void_p), ("down_expert_stride", ctypes.c_int64),
                 ("sh_gate", ctypes.c_void_p), ("sh_up", ctypes.c_void_p),
                 ("sh_down", ctypes.c_void_p), ("router_w", ctypes.c_void_p),
-                ("sh_gate_w", ctypes.c_void_p), ("logit_bias", ctypes.c_void_p)]
+                ("sh_gate_w", ctypes.c_void_p), ("logit_bias", ctypes.c_void_p),
+                ("router_f32", ctypes.c_int32)]
 
 
 _LIB = None
@@ -69,7 +70,7 @@ def lib():
         L.b200moe_router_workspace_size.restype = sz
         L.b200moe_router_workspace_size.argtypes = [i32]
         L.b200moe_router.restype = i32
-        L.b200moe_router.argtypes = [vp, i32, i32, vp, vp, vp, vp, vp, vp, vp, sz, vp]
+        L.b200moe_router.argtypes = [vp, i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, sz, vp]
         L.b200moe_decode_workspace_size.restype = sz
         L.b200moe_decode_workspace_size.argtypes = [i32]
         L.b200moe_moe_decode.restype = i32
@@ -156,10 +157,11 @@ def router_workspace_size(T: int) -> int:
 
 
 def router(x, x_dtype: int, T: int, wg, bias, logits, ids, w_f32, w_bf16, ws=None, stream=None):
+    import torch
     if ws is None:
-        import torch
         ws = torch.empty(router_workspace_size(T), dtype=torch.uint8, device=x.device)
-    _check("b200moe_router", lib().b200moe_router(ptr(x), x_dtype, T, ptr(wg), ptr(bias), ptr(logits),
+    wdt = F32 if wg.dtype == torch.float32 else BF16
+    _check("b200moe_router", lib().b200moe_router(ptr(x), x_dtype, T, ptr(wg), wdt, ptr(bias), ptr(logits),
                                                    ptr(ids), ptr(w_f32), ptr(w_bf16), ptr(ws),
                                                    ws.numel() * ws.element_size(), _stream(stream)))
 

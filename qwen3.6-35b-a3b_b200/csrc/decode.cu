@@ -36,9 +36,10 @@ struct K1Params {
   const float *resid;  // non-NULL: x = rmsnorm(resid)
   float eps;
   int T;
-  const uint16_t *wg;
+  const void *wg;        // router weights, bf16 or f32 (wf32)
   const float *bias;
-  const uint16_t *wsg;   // NULL: router only
+  const void *wsg;       // NULL: router only
+  int wf32;              // 1: wg / wsg are f32
   float *xw;             // [T][2048] f32 copy of x for K2 (or NULL)
   uint16_t *logits;      // [T][256]
   float *sg;             // [T]
@@ -91,18 +92,36 @@ __device__ __forceinline__ void load_x_slice(const K1Params &P, int t, int lane,
   }
 }
 
+// kF32: router weights stored as f32 (held as 64 floats per lane) instead of bf16 (32 words).
+template <bool kF32>
 __global__ void __launch_bounds__(128) k_router(K1Params P) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool gate_cta = blockIdx.x == kK1Ctas - 1;
   if (gate_cta && (warp != 0 || !P.wsg)) return;
   const int e = 4 * blockIdx.x + warp;
-  // This warp's weight slice (router row e, or w_sg), independent of the previous grid.
-  uint32_t wr[32];
-  const uint16_t *src = gate_cta ? P.wsg : P.wg + (size_t)e * kH;
+  // This warp's weight slice (router row e, or w_sg) as f32 values, independent of the previous
+  // grid (bf16 widens exactly).
+  float wv[64];
+  if (kF32) {
+    const float *src = gate_cta ? (const float *)P.wsg : (const float *)P.wg + (size_t)e * kH;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint4 u = ldg_stream(src + 64 * lane + 8 * i);
-    wr[4 * i] = u.x; wr[4 * i + 1] = u.y; wr[4 * i + 2] = u.z; wr[4 * i + 3] = u.w;
+    for (int i = 0; i < 16; ++i) {
+      const uint4 u = ldg_stream(src + 64 * lane + 4 * i);
+      wv[4 * i] = __uint_as_float(u.x); wv[4 * i + 1] = __uint_as_float(u.y);
+      wv[4 * i + 2] = __uint_as_float(u.z); wv[4 * i + 3] = __uint_as_float(u.w);
+    }
+  } else {
+    const uint16_t *src = gate_cta ? (const uint16_t *)P.wsg : (const uint16_t *)P.wg + (size_t)e * kH;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint4 u = ldg_stream(src + 64 * lane + 8 * i);
+      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        wv[8 * i + 2 * q] = bf16f(w4[q]);
+        wv[8 * i + 2 * q + 1] = bf16f(w4[q] >> 16);
+      }
+    }
   }
   const float bias = (!gate_cta && P.bias) ? P.bias[e] : 0.0f;
   pdl_wait();
@@ -119,19 +138,13 @@ __global__ void __launch_bounds__(128) k_router(K1Params P) {
     float acc = 0.0f;
     if (gate_cta) {  // shared-expert gate: any summation order (tolerance-checked)
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        acc = fmaf(v[2 * i], bf16f(wr[i]), acc);
-        acc = fmaf(v[2 * i + 1], bf16f(wr[i] >> 16), acc);
-      }
+      for (int i = 0; i < 64; ++i) acc = fmaf(v[i], wv[i], acc);
       const float z = warp_sum(acc);
       if (lane == 0) P.sg[t] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
       continue;
     }
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {  // R1: sequential fmaf over the lane's 64 elements
-      acc = __fmaf_rn(v[2 * i], bf16f(wr[i]), acc);
-      acc = __fmaf_rn(v[2 * i + 1], bf16f(wr[i] >> 16), acc);
-    }
+    for (int i = 0; i < 64; ++i) acc = __fmaf_rn(v[i], wv[i], acc);  // R1: sequential over the lane's 64
     float tot = chunk_total(acc);
     if (P.bias) tot = __fadd_rn(tot, bias);
     if (lane == 0) P.logits[(size_t)t * kE + e] = f2bf(tot);
@@ -363,6 +376,7 @@ K1Params k1_params(const void *x, int x_dtype, const float *resid, float eps, in
   p.wg = L->router_w;
   p.bias = L->logit_bias;
   p.wsg = L->sh_gate_w;
+  p.wf32 = L->router_f32 ? 1 : 0;
   p.xw = w.xw;
   p.logits = w.logits;
   p.sg = w.sg;
@@ -375,7 +389,8 @@ K1Params k1_params(const void *x, int x_dtype, const float *resid, float eps, in
 int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const b200moe_layer *L, float *out,
               int32_t *ids_out, uint16_t *w_out, const DecodeWS &w, cudaStream_t s, bool first) {
   const K1Params p1 = k1_params(x, x_dtype, resid, eps, T, L, w);
-  B2_CUDA(launch(k_router, (unsigned)kK1Ctas, 128, 0, s, !first, p1));
+  if (p1.wf32) B2_CUDA(launch(k_router<true>, (unsigned)kK1Ctas, 128, 0, s, !first, p1));
+  else B2_CUDA(launch(k_router<false>, (unsigned)kK1Ctas, 128, 0, s, !first, p1));
   K2Params p2;
   p2.gate = (const uint8_t *)L->gate;
   p2.up = (const uint8_t *)L->up;
@@ -453,13 +468,15 @@ extern "C" {
 
 size_t b200moe_router_workspace_size(int T) { return (T <= 0 || T > kMaxT) ? 0 : decode_ws_bytes(T); }
 
-int b200moe_router(const void *x, int x_dtype, int T, const uint16_t *router_w, const float *logit_bias,
+int b200moe_router(const void *x, int x_dtype, int T, const void *router_w, int router_dtype, const float *logit_bias,
                    uint16_t *logits, int32_t *ids, float *w_f32, uint16_t *w_bf16, void *ws, size_t ws_bytes,
                    void *stream) {
   if (T <= 0 || T > kMaxT) return b2host::set_error(B200MOE_EINVAL, "router: T=%d outside [1, %d]", T, kMaxT);
   if (!x || !router_w || !ws) return b2host::set_error(B200MOE_EINVAL, "router: x, router_w and ws are required");
   if (x_dtype != B200MOE_F32 && x_dtype != B200MOE_BF16)
     return b2host::set_error(B200MOE_EINVAL, "router: x_dtype %d is neither F32 nor BF16", x_dtype);
+  if (router_dtype != B200MOE_F32 && router_dtype != B200MOE_BF16)
+    return b2host::set_error(B200MOE_EINVAL, "router: router_dtype %d is neither F32 nor BF16", router_dtype);
   if (!al16(x) || !al16(router_w) || !al16(ws) || (logits && !al16(logits)))
     return b2host::set_error(B200MOE_EINVAL, "router: pointers must be 16-byte aligned");
   if (ws_bytes < decode_ws_bytes(T))
@@ -470,10 +487,12 @@ int b200moe_router(const void *x, int x_dtype, int T, const uint16_t *router_w, 
   b200moe_layer L = {};
   L.router_w = router_w;
   L.logit_bias = logit_bias;
+  L.router_f32 = router_dtype == B200MOE_F32;
   K1Params p1 = k1_params(x, x_dtype, nullptr, 0.f, T, &L, w);
   p1.wsg = nullptr;
   p1.xw = nullptr;
-  B2_CUDA(launch(k_router, (unsigned)kK1Ctas, 128, 0, s, false, p1));
+  if (p1.wf32) B2_CUDA(launch(k_router<true>, (unsigned)kK1Ctas, 128, 0, s, false, p1));
+  else B2_CUDA(launch(k_router<false>, (unsigned)kK1Ctas, 128, 0, s, false, p1));
   B2_CUDA(launch(k_route_tail, (unsigned)T, 32, 0, s, true, (const uint16_t *)w.logits, ids, w_f32, w_bf16));
   return B200MOE_OK;
 }

@@ -64,7 +64,7 @@ constexpr int kQ = kK * kI / kN;         // 32 routed row pairs per CTA
 constexpr int kJ = kI / kN;              // 4 shared row pairs per CTA
 constexpr int kHr = kH / kN;             // 16 down rows per CTA
 constexpr int kRowPair = 2 * kRowUp;     // 2304 B: gate row + up row
-constexpr int kRouterRowBytes = kH * 2;  // 4096 B of bf16
+constexpr int kRouterRowBytes = kH * 4;  // room for one f32 router row (a bf16 row uses half)
 constexpr int kRtRows = 3;               // per layer: the CTA's 2 router rows + the gate row
 constexpr int kGuChunks = 8;             // routed gate/up arrival chunks (one mbarrier each)
 constexpr int kGuChunk = kQ / kGuChunks; // 4 row pairs per chunk
@@ -99,7 +99,7 @@ constexpr int kOffS = kOffRes + kResPad * 4;                 // [4096] f32 route
 constexpr int kOffSsh = kOffS + kK * kI * 4;                 // [512] f32 shared-expert s
 constexpr int kOffDl = kOffSsh + kI * 4;                     // [2048] f32 gathered deltas
 constexpr int kOffLg = kOffDl + kH * 4;                      // [128] u32 gathered logit pairs
-constexpr int kOffRt = kOffLg + kN * 4;                      // [2 layers][3 rows][4096] router rows
+constexpr int kOffRt = kOffLg + kN * 4;                      // [2 layers][3 rows][8192 B] router rows
 constexpr int kOffGu = kOffRt + 2 * kRtRows * kRouterRowBytes;  // [36] gate rows, then [36] up rows
 constexpr int kOffDn = kOffGu + (kQ + kJ) * kRowPair;        // [9][16] down rows
 constexpr int kOffO = kOffDn + (kK + 1) * kHr * kRowDown;    // [9][16] f32 down outputs
@@ -245,25 +245,38 @@ __device__ __forceinline__ float chunk_total32(float acc, float *scratch) {
   return tot;
 }
 
-// One router row staged in shared memory: R1 in the declared order (bf16 logit bits) or, for
-// the shared-expert gate, sigmoid(w_sg . x) with the decode path's arithmetic (f32 bits).
-// Lane 0 holds the result.
-__device__ __forceinline__ uint32_t router_row(const uint8_t *row, const float *res, float rs, int lane, bool gate,
-                                               float bias, float *scratch) {
-  const uint4 *rp = reinterpret_cast<const uint4 *>(row) + 8 * lane;
+// One router row staged in shared memory (bf16, or f32 when wf32): R1 in the declared order
+// (bf16 logit bits) or, for the shared-expert gate, sigmoid(w_sg . x) with the decode path's
+// arithmetic (f32 bits). Lane 0 holds the result.
+__device__ __forceinline__ uint32_t router_row(const uint8_t *row, bool wf32, const float *res, float rs, int lane,
+                                               bool gate, float bias, float *scratch) {
   const float *xv = res + lane * kPadSeg;
   float acc = 0.0f;
+  if (wf32) {
+    const float4 *rp = reinterpret_cast<const float4 *>(row) + 16 * lane;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint4 u = rp[i];
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-    const float4 x0 = *reinterpret_cast<const float4 *>(xv + 8 * i);
-    const float4 x1 = *reinterpret_cast<const float4 *>(xv + 8 * i + 4);
-    const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    for (int i = 0; i < 16; ++i) {
+      const float4 w = rp[i];
+      const float4 x = *reinterpret_cast<const float4 *>(xv + 4 * i);
+      acc = __fmaf_rn(__fmul_rn(x.x, rs), w.x, acc);
+      acc = __fmaf_rn(__fmul_rn(x.y, rs), w.y, acc);
+      acc = __fmaf_rn(__fmul_rn(x.z, rs), w.z, acc);
+      acc = __fmaf_rn(__fmul_rn(x.w, rs), w.w, acc);
+    }
+  } else {
+    const uint4 *rp = reinterpret_cast<const uint4 *>(row) + 8 * lane;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      acc = __fmaf_rn(__fmul_rn(xs[2 * q], rs), bf16f(w[q]), acc);
-      acc = __fmaf_rn(__fmul_rn(xs[2 * q + 1], rs), bf16f(w[q] >> 16), acc);
+    for (int i = 0; i < 8; ++i) {
+      const uint4 u = rp[i];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      const float4 x0 = *reinterpret_cast<const float4 *>(xv + 8 * i);
+      const float4 x1 = *reinterpret_cast<const float4 *>(xv + 8 * i + 4);
+      const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc = __fmaf_rn(__fmul_rn(xs[2 * q], rs), bf16f(w[q]), acc);
+        acc = __fmaf_rn(__fmul_rn(xs[2 * q + 1], rs), bf16f(w[q] >> 16), acc);
+      }
     }
   }
   if (gate) {
@@ -378,10 +391,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
 
   auto issue_router_rows = [&](int l) {  // thread 0: layer l's 2 router rows + gate row -> rt[l & 1]
     uint64_t *b = bar + kBarRt0 + (l & 1);
-    mbar_expect_tx(b, kRtRows * kRouterRowBytes);
+    const uint32_t rb = P.L[l].router_f32 ? kH * 4 : kH * 2;  // bytes of one row as stored
+    mbar_expect_tx(b, kRtRows * rb);
     uint8_t *d = rt + (size_t)(l & 1) * kRtRows * kRouterRowBytes;
-    bulk_g2s(d, (const uint16_t *)P.L[l].router_w + (size_t)(2 * c) * kH, 2 * kRouterRowBytes, b, pol_normal);
-    bulk_g2s(d + 2 * kRouterRowBytes, P.L[l].sh_gate_w, kRouterRowBytes, b, pol_normal);
+    bulk_g2s(d, (const uint8_t *)P.L[l].router_w + (size_t)(2 * c) * rb, rb, b, pol_normal);
+    bulk_g2s(d + kRouterRowBytes, (const uint8_t *)P.L[l].router_w + (size_t)(2 * c + 1) * rb, rb, b, pol_normal);
+    bulk_g2s(d + 2 * kRouterRowBytes, P.L[l].sh_gate_w, rb, b, pol_normal);
     armed |= 1u << (kBarRt0 + (l & 1));
   };
   auto issue_shared_gu = [&](int l) {  // thread 0: layer l's shared-expert gate/up rows, 2 copies
@@ -492,8 +507,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       const bool gate = warp == 2;
       const float bias = (!gate && Lp.logit_bias) ? Lp.logit_bias[2 * c + warp] : 0.0f;
       const uint32_t v =
-          router_row(rt + ((size_t)(l & 1) * kRtRows + warp) * kRouterRowBytes, res_s, rs, lane, gate, bias,
-                     warp_scr + 32 * warp);
+          router_row(rt + ((size_t)(l & 1) * kRtRows + warp) * kRouterRowBytes, Lp.router_f32 != 0, res_s, rs, lane,
+                     gate, bias, warp_scr + 32 * warp);
       if (lane == 0) row_out[warp] = v;
     }
     if (__syncthreads_or(fail)) { aborted = true; break; }

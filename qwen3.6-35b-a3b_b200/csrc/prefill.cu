@@ -111,8 +111,8 @@ constexpr int kPrepWarps = 4;
 constexpr int kPrepPitch = 68;
 
 __global__ void __launch_bounds__(32 * kPrepWarps) k_prep(const void *x, int x_dtype, const float *resid, float eps,
-                                                          int T, const uint16_t *wsg, float *xn, __half *x16,
-                                                          float *sg, int32_t *err) {
+                                                          int T, const void *wsg, int wf32, float *xn,
+                                                          __half *x16, float *sg, int32_t *err) {
   __shared__ __align__(16) float rows[kPrepWarps][32 * kPrepPitch];
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
   const int t = blockIdx.x * kPrepWarps + wp;
@@ -171,15 +171,27 @@ __global__ void __launch_bounds__(32 * kPrepWarps) k_prep(const void *x, int x_d
   for (int i = 0; i < 64; ++i) range_bad |= !(fabsf(v[i]) <= 65504.0f);
   if (__any_sync(0xFFFFFFFFu, range_bad) && lane == 0) atomicOr(err, kErrRange);
   float z = 0.0f;
-  const uint16_t *w = wsg + 64 * lane;
+  if (wf32) {  // f32 gate weights
+    const float *w = reinterpret_cast<const float *>(wsg) + 64 * lane;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint4 u = __ldg(reinterpret_cast<const uint4 *>(w + 8 * i));
-    const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+    for (int i = 0; i < 16; ++i) {
+      const float4 a = __ldg(reinterpret_cast<const float4 *>(w + 4 * i));
+      z = fmaf(v[4 * i], a.x, z);
+      z = fmaf(v[4 * i + 1], a.y, z);
+      z = fmaf(v[4 * i + 2], a.z, z);
+      z = fmaf(v[4 * i + 3], a.w, z);
+    }
+  } else {
+    const uint16_t *w = reinterpret_cast<const uint16_t *>(wsg) + 64 * lane;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      z = fmaf(v[8 * i + 2 * q], bf16f(uw[q]), z);
-      z = fmaf(v[8 * i + 2 * q + 1], bf16f(uw[q] >> 16), z);
+    for (int i = 0; i < 8; ++i) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4 *>(w + 8 * i));
+      const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        z = fmaf(v[8 * i + 2 * q], bf16f(uw[q]), z);
+        z = fmaf(v[8 * i + 2 * q + 1], bf16f(uw[q] >> 16), z);
+      }
     }
   }
   z = warp_sum(z);
@@ -210,9 +222,12 @@ constexpr int kRgPitch = 68;                                  // padded row pitc
 constexpr int kRgBuf = 64 * kRgPitch;                         // one 64 x 64 chunk
 constexpr size_t kRgSmem = (size_t)4 * kRgBuf * sizeof(float);  // x and w, two buffers each
 
+template <bool kF32>
 __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ xn, int T,
-                                                     const uint16_t *__restrict__ wg, const float *bias,
+                                                     const void *__restrict__ wg_, const float *bias,
                                                      uint16_t *logits) {
+  const uint16_t *wg = reinterpret_cast<const uint16_t *>(wg_);  // bf16 router
+  const float *wgf = reinterpret_cast<const float *>(wg_);        // f32 router (kF32)
   extern __shared__ __align__(16) float rg_smem[];
   float *xs = rg_smem, *wsm = rg_smem + 2 * kRgBuf;  // [2][64][kRgPitch] each
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
@@ -227,25 +242,38 @@ __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ x
     }
     cp_async_commit();
   };
-  auto load_w = [&](int c, uint4 (&u)[4]) {
+  // a chunk's weights: 64 rows x 64 values, 8 values per slot (bf16: one uint4; f32: two)
+  auto load_w = [&](int c, uint4 (&u)[8]) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int idx = tid + 128 * q;  // 0..511 8-wide slots
-      u[q] = __ldg(reinterpret_cast<const uint4 *>(wg + (size_t)(e0 + (idx >> 3)) * kH + 64 * c + (idx & 7) * 8));
+      const size_t off = (size_t)(e0 + (idx >> 3)) * kH + 64 * c + (idx & 7) * 8;
+      if (kF32) {
+        u[2 * q] = __ldg(reinterpret_cast<const uint4 *>(wgf + off));
+        u[2 * q + 1] = __ldg(reinterpret_cast<const uint4 *>(wgf + off + 4));
+      } else {
+        u[q] = __ldg(reinterpret_cast<const uint4 *>(wg + off));
+      }
     }
   };
-  auto store_w = [&](const uint4 (&u)[4], float *dst) {  // bf16 -> f32 (exact)
+  auto store_w = [&](const uint4 (&u)[8], float *dst) {  // bf16 -> f32 (exact), or f32 as is
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int idx = tid + 128 * q;
       float *d = dst + (idx >> 3) * kRgPitch + (idx & 7) * 8;
-      *reinterpret_cast<float4 *>(d) = make_float4(bf16f(u[q].x), bf16f(u[q].x >> 16), bf16f(u[q].y), bf16f(u[q].y >> 16));
-      *reinterpret_cast<float4 *>(d + 4) =
-          make_float4(bf16f(u[q].z), bf16f(u[q].z >> 16), bf16f(u[q].w), bf16f(u[q].w >> 16));
+      if (kF32) {
+        *reinterpret_cast<uint4 *>(d) = u[2 * q];
+        *reinterpret_cast<uint4 *>(d + 4) = u[2 * q + 1];
+      } else {
+        *reinterpret_cast<float4 *>(d) =
+            make_float4(bf16f(u[q].x), bf16f(u[q].x >> 16), bf16f(u[q].y), bf16f(u[q].y >> 16));
+        *reinterpret_cast<float4 *>(d + 4) =
+            make_float4(bf16f(u[q].z), bf16f(u[q].z >> 16), bf16f(u[q].w), bf16f(u[q].w >> 16));
+      }
     }
   };
   {
-    uint4 u[4];
+    uint4 u[8];
     load_x(0, xs);
     load_w(0, u);
     store_w(u, wsm);
@@ -255,7 +283,7 @@ __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ x
   float tot[8][4];
   for (int c = 0; c < 32; ++c) {
     const int buf = c & 1;
-    uint4 un[4];
+    uint4 un[8];
     if (c + 1 < 32) {  // the next chunk, in flight while this one is multiplied
       load_x(c + 1, xs + (buf ^ 1) * kRgBuf);
       load_w(c + 1, un);
@@ -838,7 +866,8 @@ int ensure_gemm_attrs() {
   if (done) return B200MOE_OK;
   B2_CUDA(cudaFuncSetAttribute(k_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<1>::kSmem));
   B2_CUDA(cudaFuncSetAttribute(k_gemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<2>::kSmem));
-  B2_CUDA(cudaFuncSetAttribute(k_router_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
+  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
+  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
   int dev = 0;
   B2_CUDA(cudaGetDevice(&dev));
   B2_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
@@ -973,9 +1002,14 @@ int route_stage(const void *x, int x_dtype, const float *resid, float eps, int T
   if (rc) return rc;
   B2_CUDA(cudaMemsetAsync(w.err, 0, 4, s));
   k_prep<<<(T + kPrepWarps - 1) / kPrepWarps, 32 * kPrepWarps, 0, s>>>(x, x_dtype, resid, eps, T, L->sh_gate_w,
-                                                                   w.xn, x16, sg, w.err);
+                                                                   L->router_f32, w.xn, x16, sg, w.err);
   B2_CUDA(cudaGetLastError());
-  k_router_gemm<<<dim3((T + 63) / 64, kE / 64), 128, kRgSmem, s>>>(w.xn, T, L->router_w, L->logit_bias, w.logits);
+  if (L->router_f32)
+    k_router_gemm<true><<<dim3((T + 63) / 64, kE / 64), 128, kRgSmem, s>>>(w.xn, T, L->router_w, L->logit_bias,
+                                                                           w.logits);
+  else
+    k_router_gemm<false><<<dim3((T + 63) / 64, kE / 64), 128, kRgSmem, s>>>(w.xn, T, L->router_w, L->logit_bias,
+                                                                            w.logits);
   B2_CUDA(cudaGetLastError());
   k_route_tok<<<(T + 7) / 8, 256, 0, s>>>(w.logits, T, ids, wb);
   B2_CUDA(cudaGetLastError());

@@ -29,6 +29,15 @@ def _bf16_tensor(bits: np.ndarray, device) -> torch.Tensor:
         torch.bfloat16).to(device)
 
 
+def _router_tensor(w: np.ndarray, device) -> torch.Tensor:
+    """Router / shared-gate weights on the device: uint16 arrays are bf16 bits, float32 arrays
+    f32 values (kept exactly; the kernels take either)."""
+    w = np.asarray(w)
+    if w.dtype == np.float32:
+        return torch.from_numpy(np.ascontiguousarray(w)).to(device)
+    return _bf16_tensor(w, device)
+
+
 class DeviceLayer:
     """One MoE layer in HBM. Q4_K tensors are uint8 [n_blocks * 144]."""
 
@@ -37,6 +46,9 @@ class DeviceLayer:
         self.gate, self.up, self.down = gate, up, down
         self.sh_gate, self.sh_up, self.sh_down = sh_gate, sh_up, sh_down
         self.router_w, self.sh_gate_w, self.logit_bias = router_w, sh_gate_w, logit_bias
+        if router_w.dtype not in (torch.bfloat16, torch.float32) or sh_gate_w.dtype != router_w.dtype:
+            raise ValueError("router and shared-gate weights must both be bf16 or both f32, got %s / %s"
+                             % (router_w.dtype, sh_gate_w.dtype))
         self.gate_up_stride = int(gate_up_stride)
         self._abi = None
 
@@ -72,7 +84,8 @@ class DeviceLayer:
     def from_host(cls, blocks: dict, router_w_bits, sh_gate_w_bits, logit_bias=None,
                   device="cuda") -> "DeviceLayer":
         """From host arrays: ``blocks[kind]`` uint8 Q4_K bytes for gate/up/down/sh_gate/sh_up/sh_down
-        (GGUF order), bf16 bit patterns for the router and shared gate."""
+        (GGUF order); the router and shared gate as bf16 bit patterns (uint16) or f32 values
+        (float32, both the same type)."""
         dev = torch.device(device)
         with warnings.catch_warnings():  # read-only views (e.g. a memory-mapped GGUF): only read, then copied
             warnings.filterwarnings("ignore", message="The given NumPy array is not writable")
@@ -80,7 +93,7 @@ class DeviceLayer:
                  for k, v in blocks.items()}
         lb = None if logit_bias is None else torch.as_tensor(np.asarray(logit_bias, np.float32)).to(dev)
         return cls(t["gate"], t["up"], t["down"], t["sh_gate"], t["sh_up"], t["sh_down"],
-                   _bf16_tensor(router_w_bits, dev), _bf16_tensor(sh_gate_w_bits, dev), lb)
+                   _router_tensor(router_w_bits, dev), _router_tensor(sh_gate_w_bits, dev), lb)
 
     # ------------------------------------------------------------------ ABI view
     def abi(self) -> _abi.Layer:
@@ -88,7 +101,8 @@ class DeviceLayer:
             p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
             self._abi = _abi.Layer(p(self.gate), p(self.up), self.gate_up_stride, p(self.down),
                                    EXPERT_DOWN_BYTES, p(self.sh_gate), p(self.sh_up), p(self.sh_down),
-                                   p(self.router_w), p(self.sh_gate_w), p(self.logit_bias))
+                                   p(self.router_w), p(self.sh_gate_w), p(self.logit_bias),
+                                   1 if self.router_w.dtype == torch.float32 else 0)
         return self._abi
 
     @property
@@ -144,9 +158,10 @@ class DeviceEngine:
         """(values, None, handle) like ``Engine.read`` :235 -- dequantized on the device."""
         L = self.layers[layer]
         if role == "ffn_gate_inp":
-            return L.router_w.float(), None, dict(type_name="BF16")
+            return L.router_w.float(), None, dict(type_name="F32" if L.router_w.dtype == torch.float32 else "BF16")
         if role == "ffn_gate_inp_shexp":
-            return L.sh_gate_w.float().reshape(1, H), None, dict(type_name="BF16")
+            return L.sh_gate_w.float().reshape(1, H), None, dict(
+                type_name="F32" if L.sh_gate_w.dtype == torch.float32 else "BF16")
         return L.dequant(self.ROLE[role]), None, dict(type_name="Q4_K")
 
     def expert(self, role: str, layer: int, idx: int, shape_hf):

@@ -13,10 +13,10 @@ Replaces the reference's ``tools/gguf_reader.py:492 Gguf`` (header parse) and th
     data section at the next multiple of ``general.alignment`` (default 32)
 
 Block types the device paths take: the expert GEMMs and decode GEMVs read Q4_K (type 12);
-the router and shared-expert gate are bf16 (type 30). Other types are refused by name with
-the reason (Q5_K / Q6_K / Q8_0 tensors of the published Q4_K_M file decode through
-``b200moe_dequant`` but have no GEMM path); an F32 router is rounded to bf16 only when the
-caller asks for it.
+the router and shared-expert gate are used as stored, bf16 (type 30) or F32 (type 0; F16 is
+widened to f32 exactly). Other types are refused by name with the reason (Q5_K / Q6_K / Q8_0
+tensors of the published Q4_K_M file decode through ``b200moe_dequant`` but have no GEMM
+path).
 """
 from __future__ import annotations
 
@@ -179,9 +179,9 @@ def layer_host(gf: GgufFile, layer: int, round_router: bool = False) -> tuple:
     ``ffn_{gate,up,down}_shexp`` (views into the memory map: valid while ``gf`` is open) and the
     bf16 router / shared-gate vectors (copies).
 
-    ``round_router``: accept F32 / F16 router and gate weights, rounded to bf16 (RNE). The
-    device router multiplies bf16 weights; without the flag such a file is refused, because the
-    rounding changes the logits the reference computes from the stored F32 values."""
+    The router and gate keep their stored type (F32, or F16 widened exactly, as f32 values;
+    BF16 as bits). ``round_router``: round F32 / F16 router and gate weights to bf16 (RNE)
+    instead -- half the router bytes, but different logits from the stored values'."""
     p = "blk.%d." % layer
     blocks = {}
     for kind, nm, dims in (("gate", "ffn_gate_exps", (H, I, E)), ("up", "ffn_up_exps", (H, I, E)),
@@ -195,11 +195,15 @@ def layer_host(gf: GgufFile, layer: int, round_router: bool = False) -> tuple:
 
 
 def _vector_bf16(gf: GgufFile, name: str, dims, round_ok: bool) -> np.ndarray:
-    ti = _want(gf, name, ("BF16", "F32", "F16") if round_ok else ("BF16",), dims)
+    """bf16 bits (uint16) of a BF16 tensor; f32 values (float32) of an F32 / F16 one, or their
+    bf16 rounding when ``round_ok``."""
+    ti = _want(gf, name, ("BF16", "F32", "F16"), dims)
     raw = gf.raw(name)
     if ti.type_name == "BF16":
         return raw.view(np.uint16).copy()
     f = raw.view(np.float32) if ti.type_name == "F32" else raw.view(np.float16).astype(np.float32)
+    if not round_ok:
+        return f.copy()
     u = f.view(np.uint32).astype(np.uint64)
     nan = (u & 0x7FFFFFFF) > 0x7F800000
     r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)   # round to nearest even
