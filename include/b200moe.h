@@ -54,6 +54,10 @@ typedef struct b200moe_layer {
     const float *logit_bias; /* [256] f32 added to R1's f32 dot before the bf16 cast, or NULL */
     int32_t router_f32;      /* 0: router_w / sh_gate_w are bf16; 1: f32 (the published file's
                                 F32 ffn_gate_inp / ffn_gate_inp_shexp, used exactly) */
+    const float *norm_w;     /* [2048] f32 post-attention RMSNorm weight as stored (Form A: the
+                                GGUF post_attention_norm holds 1 + w), applied where the library
+                                normalises the residual itself (resid / stack modes):
+                                x = (resid * rs) * norm_w, two roundings; NULL: weight 1 */
 } b200moe_layer;
 
 /* ABI version (B200MOE_ABI_VERSION) and the last error message on this thread. */

@@ -93,10 +93,14 @@ def router(x_f32: np.ndarray, wg_bits: np.ndarray, bias: np.ndarray | None = Non
     return dict(logits=logits, probs=probs, ids=ids, w_f32=wf, w_bf16=wb)
 
 
-def rmsnorm(x: np.ndarray, eps: float = 1e-6) -> np.ndarray:
+def rmsnorm(x: np.ndarray, eps: float = 1e-6, w: np.ndarray | None = None) -> np.ndarray:
+    """Declared-order RMSNorm (``engine/m3_forward.py:303 rmsnorm_a``): x * r, then * w when a
+    Form A weight (as stored: 1 + w) is given -- two f32 roundings, as the reference's torch."""
     x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, H)
     y = np.empty_like(x)
     lib().b2o_rmsnorm(_p(x, ctypes.c_float), x.shape[0], eps, _p(y, ctypes.c_float))
+    if w is not None:
+        y = (y * np.asarray(w, dtype=np.float32).reshape(1, H)).astype(np.float32)
     return y
 
 

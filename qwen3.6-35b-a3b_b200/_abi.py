@@ -41,7 +41,7 @@ class Layer(ctypes.Structure):
                 ("sh_gate", ctypes.c_void_p), ("sh_up", ctypes.c_void_p),
                 ("sh_down", ctypes.c_void_p), ("router_w", ctypes.c_void_p),
                 ("sh_gate_w", ctypes.c_void_p), ("logit_bias", ctypes.c_void_p),
-                ("router_f32", ctypes.c_int32)]
+                ("router_f32", ctypes.c_int32), ("norm_w", ctypes.c_void_p)]
 
 
 _LIB = None

@@ -33,7 +33,8 @@ constexpr int kK1Ctas = kE / 4 + 1;  // 64 router CTAs of 4 warps + 1 shared-gat
 struct K1Params {
   const void *x;
   int x_dtype;
-  const float *resid;  // non-NULL: x = rmsnorm(resid)
+  const float *resid;  // non-NULL: x = rmsnorm(resid) (* nw)
+  const float *nw;     // RMSNorm weight (resid mode) or NULL
   float eps;
   int T;
   const void *wg;        // router weights, bf16 or f32 (wf32)
@@ -70,6 +71,14 @@ __device__ __forceinline__ void load_x_slice(const K1Params &P, int t, int lane,
     const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, 2048.0f), P.eps)));
 #pragma unroll
     for (int i = 0; i < 64; ++i) v[i] = __fmul_rn(v[i], rs);
+    if (P.nw) {  // Form A weight, a second rounding
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 w = __ldg(reinterpret_cast<const float4 *>(P.nw + 64 * lane + 4 * i));
+        v[4 * i] = __fmul_rn(v[4 * i], w.x); v[4 * i + 1] = __fmul_rn(v[4 * i + 1], w.y);
+        v[4 * i + 2] = __fmul_rn(v[4 * i + 2], w.z); v[4 * i + 3] = __fmul_rn(v[4 * i + 3], w.w);
+      }
+    }
   } else if (P.x_dtype == B200MOE_BF16) {
     const uint16_t *xb = reinterpret_cast<const uint16_t *>(P.x) + (size_t)t * kH + 64 * lane;
 #pragma unroll
@@ -377,6 +386,7 @@ K1Params k1_params(const void *x, int x_dtype, const float *resid, float eps, in
   p.bias = L->logit_bias;
   p.wsg = L->sh_gate_w;
   p.wf32 = L->router_f32 ? 1 : 0;
+  p.nw = resid ? L->norm_w : nullptr;
   p.xw = w.xw;
   p.logits = w.logits;
   p.sg = w.sg;

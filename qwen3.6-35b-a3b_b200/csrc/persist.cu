@@ -202,9 +202,11 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// x values of chunk (kb, c) from the padded residual, each scaled by rs.
-__device__ __forceinline__ void xchunk_pad(const float *row, float rs, int kb, int c, XChunk &x) {
+// x values of chunk (kb, c) from the padded residual, each scaled by rs (and by the RMSNorm
+// weight nw, a second rounding, when given).
+__device__ __forceinline__ void xchunk_pad(const float *row, float rs, const float *nw, int kb, int c, XChunk &x) {
   const int p = (4 * kb + (c >> 1)) * kPadSeg + 16 * (c & 1);
+  const int e = (4 * kb + (c >> 1)) * 64 + 16 * (c & 1);  // element index of the run's start
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const float4 a = *reinterpret_cast<const float4 *>(row + p + 4 * i);
@@ -213,6 +215,14 @@ __device__ __forceinline__ void xchunk_pad(const float *row, float rs, int kb, i
     x.lo[4 * i + 2] = __fmul_rn(a.z, rs); x.lo[4 * i + 3] = __fmul_rn(a.w, rs);
     x.hi[4 * i] = __fmul_rn(b.x, rs); x.hi[4 * i + 1] = __fmul_rn(b.y, rs);
     x.hi[4 * i + 2] = __fmul_rn(b.z, rs); x.hi[4 * i + 3] = __fmul_rn(b.w, rs);
+    if (nw) {
+      const float4 wa = __ldg(reinterpret_cast<const float4 *>(nw + e + 4 * i));
+      const float4 wb = __ldg(reinterpret_cast<const float4 *>(nw + e + 32 + 4 * i));
+      x.lo[4 * i] = __fmul_rn(x.lo[4 * i], wa.x); x.lo[4 * i + 1] = __fmul_rn(x.lo[4 * i + 1], wa.y);
+      x.lo[4 * i + 2] = __fmul_rn(x.lo[4 * i + 2], wa.z); x.lo[4 * i + 3] = __fmul_rn(x.lo[4 * i + 3], wa.w);
+      x.hi[4 * i] = __fmul_rn(x.hi[4 * i], wb.x); x.hi[4 * i + 1] = __fmul_rn(x.hi[4 * i + 1], wb.y);
+      x.hi[4 * i + 2] = __fmul_rn(x.hi[4 * i + 2], wb.z); x.hi[4 * i + 3] = __fmul_rn(x.hi[4 * i + 3], wb.w);
+    }
   }
   float sl = 0.f, sh = 0.f;
 #pragma unroll
@@ -248,20 +258,35 @@ __device__ __forceinline__ float chunk_total32(float acc, float *scratch) {
 // One router row staged in shared memory (bf16, or f32 when wf32): R1 in the declared order
 // (bf16 logit bits) or, for the shared-expert gate, sigmoid(w_sg . x) with the decode path's
 // arithmetic (f32 bits). Lane 0 holds the result.
-__device__ __forceinline__ uint32_t router_row(const uint8_t *row, bool wf32, const float *res, float rs, int lane,
-                                               bool gate, float bias, float *scratch) {
+__device__ __forceinline__ uint32_t router_row(const uint8_t *row, bool wf32, const float *res, float rs,
+                                               const float *nw, int lane, bool gate, float bias, float *scratch) {
   const float *xv = res + lane * kPadSeg;
+  // the lane's 64 inputs: resid * rs (* nw), in element order
+  float xs[64];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float4 x = *reinterpret_cast<const float4 *>(xv + 4 * i);
+    xs[4 * i] = __fmul_rn(x.x, rs); xs[4 * i + 1] = __fmul_rn(x.y, rs);
+    xs[4 * i + 2] = __fmul_rn(x.z, rs); xs[4 * i + 3] = __fmul_rn(x.w, rs);
+  }
+  if (nw) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float4 w = __ldg(reinterpret_cast<const float4 *>(nw + 64 * lane + 4 * i));
+      xs[4 * i] = __fmul_rn(xs[4 * i], w.x); xs[4 * i + 1] = __fmul_rn(xs[4 * i + 1], w.y);
+      xs[4 * i + 2] = __fmul_rn(xs[4 * i + 2], w.z); xs[4 * i + 3] = __fmul_rn(xs[4 * i + 3], w.w);
+    }
+  }
   float acc = 0.0f;
   if (wf32) {
     const float4 *rp = reinterpret_cast<const float4 *>(row) + 16 * lane;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const float4 w = rp[i];
-      const float4 x = *reinterpret_cast<const float4 *>(xv + 4 * i);
-      acc = __fmaf_rn(__fmul_rn(x.x, rs), w.x, acc);
-      acc = __fmaf_rn(__fmul_rn(x.y, rs), w.y, acc);
-      acc = __fmaf_rn(__fmul_rn(x.z, rs), w.z, acc);
-      acc = __fmaf_rn(__fmul_rn(x.w, rs), w.w, acc);
+      acc = __fmaf_rn(xs[4 * i], w.x, acc);
+      acc = __fmaf_rn(xs[4 * i + 1], w.y, acc);
+      acc = __fmaf_rn(xs[4 * i + 2], w.z, acc);
+      acc = __fmaf_rn(xs[4 * i + 3], w.w, acc);
     }
   } else {
     const uint4 *rp = reinterpret_cast<const uint4 *>(row) + 8 * lane;
@@ -269,13 +294,10 @@ __device__ __forceinline__ uint32_t router_row(const uint8_t *row, bool wf32, co
     for (int i = 0; i < 8; ++i) {
       const uint4 u = rp[i];
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-      const float4 x0 = *reinterpret_cast<const float4 *>(xv + 8 * i);
-      const float4 x1 = *reinterpret_cast<const float4 *>(xv + 8 * i + 4);
-      const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        acc = __fmaf_rn(__fmul_rn(xs[2 * q], rs), bf16f(w[q]), acc);
-        acc = __fmaf_rn(__fmul_rn(xs[2 * q + 1], rs), bf16f(w[q] >> 16), acc);
+        acc = __fmaf_rn(xs[8 * i + 2 * q], bf16f(w[q]), acc);
+        acc = __fmaf_rn(xs[8 * i + 2 * q + 1], bf16f(w[q] >> 16), acc);
       }
     }
   }
@@ -507,8 +529,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       const bool gate = warp == 2;
       const float bias = (!gate && Lp.logit_bias) ? Lp.logit_bias[2 * c + warp] : 0.0f;
       const uint32_t v =
-          router_row(rt + ((size_t)(l & 1) * kRtRows + warp) * kRouterRowBytes, Lp.router_f32 != 0, res_s, rs, lane,
-                     gate, bias, warp_scr + 32 * warp);
+          router_row(rt + ((size_t)(l & 1) * kRtRows + warp) * kRouterRowBytes, Lp.router_f32 != 0, res_s, rs,
+                     P.resid ? Lp.norm_w : nullptr, lane, gate, bias, warp_scr + 32 * warp);
       if (lane == 0) row_out[warp] = v;
     }
     if (__syncthreads_or(fail)) { aborted = true; break; }
@@ -567,8 +589,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
         __syncwarp();
         if (warp >= kRtRows) rs = rms_scale();
         XChunk X0, X1;
-        xchunk_pad(res_s, rs, kb0, cc, X0);
-        xchunk_pad(res_s, rs, kb0 + 4, cc, X1);
+        const float *nw = P.resid ? Lp.norm_w : nullptr;
+        xchunk_pad(res_s, rs, nw, kb0, cc, X0);
+        xchunk_pad(res_s, rs, nw, kb0 + 4, cc, X1);
         constexpr int kStep = 2 * (kWarps - 1);
         for (int ia = 2 * (warp - 1); ia < kJ + kQ && !fail; ia += kStep) {
           const int ib = ia + 1;  // the second pair of this iteration (if any)

@@ -111,8 +111,8 @@ constexpr int kPrepWarps = 4;
 constexpr int kPrepPitch = 68;
 
 __global__ void __launch_bounds__(32 * kPrepWarps) k_prep(const void *x, int x_dtype, const float *resid, float eps,
-                                                          int T, const void *wsg, int wf32, float *xn,
-                                                          __half *x16, float *sg, int32_t *err) {
+                                                          int T, const void *wsg, int wf32, const float *nw,
+                                                          float *xn, __half *x16, float *sg, int32_t *err) {
   __shared__ __align__(16) float rows[kPrepWarps][32 * kPrepPitch];
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
   const int t = blockIdx.x * kPrepWarps + wp;
@@ -160,6 +160,14 @@ __global__ void __launch_bounds__(32 * kPrepWarps) k_prep(const void *x, int x_d
     const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, 2048.0f), eps)));
 #pragma unroll
     for (int i = 0; i < 64; ++i) v[i] = __fmul_rn(v[i], rs);
+    if (nw) {  // Form A weight, a second rounding
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 w = __ldg(reinterpret_cast<const float4 *>(nw + 64 * lane + 4 * i));
+        v[4 * i] = __fmul_rn(v[4 * i], w.x); v[4 * i + 1] = __fmul_rn(v[4 * i + 1], w.y);
+        v[4 * i + 2] = __fmul_rn(v[4 * i + 2], w.z); v[4 * i + 3] = __fmul_rn(v[4 * i + 3], w.w);
+      }
+    }
     float *c = row + lane * kPrepPitch;  // the normalised chunk back into the staging row
     __syncwarp();
 #pragma unroll
@@ -1002,7 +1010,8 @@ int route_stage(const void *x, int x_dtype, const float *resid, float eps, int T
   if (rc) return rc;
   B2_CUDA(cudaMemsetAsync(w.err, 0, 4, s));
   k_prep<<<(T + kPrepWarps - 1) / kPrepWarps, 32 * kPrepWarps, 0, s>>>(x, x_dtype, resid, eps, T, L->sh_gate_w,
-                                                                   L->router_f32, w.xn, x16, sg, w.err);
+                                                                   L->router_f32, resid ? L->norm_w : nullptr,
+                                                                   w.xn, x16, sg, w.err);
   B2_CUDA(cudaGetLastError());
   if (L->router_f32)
     k_router_gemm<true><<<dim3((T + 63) / 64, kE / 64), 128, kRgSmem, s>>>(w.xn, T, L->router_w, L->logit_bias,

@@ -42,7 +42,7 @@ class DeviceLayer:
     """One MoE layer in HBM. Q4_K tensors are uint8 [n_blocks * 144]."""
 
     def __init__(self, gate, up, down, sh_gate, sh_up, sh_down, router_w, sh_gate_w,
-                 logit_bias=None, gate_up_stride: int = EXPERT_GATE_BYTES):
+                 logit_bias=None, gate_up_stride: int = EXPERT_GATE_BYTES, norm_w=None):
         self.gate, self.up, self.down = gate, up, down
         self.sh_gate, self.sh_up, self.sh_down = sh_gate, sh_up, sh_down
         self.router_w, self.sh_gate_w, self.logit_bias = router_w, sh_gate_w, logit_bias
@@ -50,6 +50,11 @@ class DeviceLayer:
             raise ValueError("router and shared-gate weights must both be bf16 or both f32, got %s / %s"
                              % (router_w.dtype, sh_gate_w.dtype))
         self.gate_up_stride = int(gate_up_stride)
+        # post-attention RMSNorm weight as stored (Form A: 1 + w), f32 [2048]; None = 1. Used where
+        # the library normalises the residual itself (moe_stack, moe_stack_prefill).
+        if norm_w is not None and (norm_w.dtype != torch.float32 or norm_w.numel() != H):
+            raise ValueError("norm_w must be f32 [%d]" % H)
+        self.norm_w = norm_w
         self._abi = None
 
     # ------------------------------------------------------------------ construction
@@ -82,7 +87,7 @@ class DeviceLayer:
 
     @classmethod
     def from_host(cls, blocks: dict, router_w_bits, sh_gate_w_bits, logit_bias=None,
-                  device="cuda") -> "DeviceLayer":
+                  device="cuda", norm_w=None) -> "DeviceLayer":
         """From host arrays: ``blocks[kind]`` uint8 Q4_K bytes for gate/up/down/sh_gate/sh_up/sh_down
         (GGUF order); the router and shared gate as bf16 bit patterns (uint16) or f32 values
         (float32, both the same type)."""
@@ -93,7 +98,9 @@ class DeviceLayer:
                  for k, v in blocks.items()}
         lb = None if logit_bias is None else torch.as_tensor(np.asarray(logit_bias, np.float32)).to(dev)
         return cls(t["gate"], t["up"], t["down"], t["sh_gate"], t["sh_up"], t["sh_down"],
-                   _router_tensor(router_w_bits, dev), _router_tensor(sh_gate_w_bits, dev), lb)
+                   _router_tensor(router_w_bits, dev), _router_tensor(sh_gate_w_bits, dev), lb,
+                   norm_w=None if norm_w is None else torch.from_numpy(
+                       np.ascontiguousarray(norm_w, dtype=np.float32)).to(dev))
 
     # ------------------------------------------------------------------ ABI view
     def abi(self) -> _abi.Layer:
@@ -102,7 +109,7 @@ class DeviceLayer:
             self._abi = _abi.Layer(p(self.gate), p(self.up), self.gate_up_stride, p(self.down),
                                    EXPERT_DOWN_BYTES, p(self.sh_gate), p(self.sh_up), p(self.sh_down),
                                    p(self.router_w), p(self.sh_gate_w), p(self.logit_bias),
-                                   1 if self.router_w.dtype == torch.float32 else 0)
+                                   1 if self.router_w.dtype == torch.float32 else 0, p(self.norm_w))
         return self._abi
 
     @property

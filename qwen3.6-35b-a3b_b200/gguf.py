@@ -211,11 +211,27 @@ def _vector_bf16(gf: GgufFile, name: str, dims, round_ok: bool) -> np.ndarray:
     return r
 
 
+def layer_norm(gf: GgufFile, layer: int):
+    """f32 values of ``blk.<layer>.post_attention_norm.weight`` (Form A: the file holds 1 + w;
+    F32 as stored, BF16 / F16 widened exactly), or None when the file has no such tensor."""
+    name = "blk.%d.post_attention_norm.weight" % layer
+    if name not in gf.tensors:
+        return None
+    ti = _want(gf, name, ("F32", "BF16", "F16"), (H,))
+    raw = gf.raw(name)
+    if ti.type_name == "F32":
+        return raw.view(np.float32).copy()
+    if ti.type_name == "F16":
+        return raw.view(np.float16).astype(np.float32)
+    return (raw.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
 def device_layer(gf: GgufFile, layer: int, device="cuda", round_router: bool = False):
-    """:class:`DeviceLayer` of layer ``layer`` read from ``gf`` (Q4_K bytes uploaded as stored)."""
+    """:class:`DeviceLayer` of layer ``layer`` read from ``gf`` (Q4_K bytes uploaded as stored,
+    the post-attention norm weight when the file has it)."""
     from .engine import DeviceLayer
     blocks, router, shgate = layer_host(gf, layer, round_router)
-    return DeviceLayer.from_host(blocks, router, shgate, device=device)
+    return DeviceLayer.from_host(blocks, router, shgate, device=device, norm_w=layer_norm(gf, layer))
 
 
 def device_engine(path: str, layers=None, device="cuda", round_router: bool = False):

@@ -137,3 +137,17 @@ def test_refusals(tmp_path):
     open(p4, "wb").write(b"GGML" + b"\0" * 64)
     with pytest.raises(gguf.GgufError):
         gguf.GgufFile(p4)
+
+
+def test_post_attention_norm_weight(tmp_path):
+    """blk.N.post_attention_norm.weight (Form A: the file holds 1 + w) is read as f32 values;
+    a file without it gives None (weight 1)."""
+    gguf = _mod()
+    t, _, _ = layer_tensors(2)
+    w = (1.0 + np.random.default_rng(3).normal(0, 0.05, H)).astype(np.float32)
+    t.append(("blk.2.post_attention_norm.weight", (H,), F32, {0: w.tobytes()}))
+    path = str(tmp_path / "n.gguf")
+    write_gguf(path, t)
+    with gguf.GgufFile(path) as gf:
+        assert np.array_equal(gguf.layer_norm(gf, 2), w)
+        assert gguf.layer_norm(gf, 5) is None
