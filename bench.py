@@ -49,6 +49,11 @@ def parse():
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--layers", type=int, default=N_LAYERS)
     p.add_argument("--seed", type=int, default=4)
+    p.add_argument("--path", choices=["auto", "decode", "prefill"], default="auto",
+                   help="stack_decode with T >= 2: the decode kernels or the grouped-GEMM path (auto: the "
+                        "block's own choice by token count)")
+    p.add_argument("--zipf", action="store_true",
+                   help="config 2's routing law: a per-expert Zipf(1.1) logit bias on every layer")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--ref-layers-per-step", type=int, default=2)
     return p.parse_args()
@@ -204,13 +209,17 @@ def run_b200(args):
     expert_bytes = None
 
     if args.workload == "stack_decode":
-        eng = DeviceEngine.synthetic(args.seed, args.layers, dev)
+        eng = DeviceEngine.synthetic(args.seed, args.layers, dev, bias=args.zipf)
         nl = args.layers
         persist_ctas, persist_cluster = _abi.decode_persistent_info() if T == 1 else (0, 0)
-        # one persistent kernel for the whole stack (T = 1), else 3 kernels per layer
-        launches_per_step = 1 if persist_ctas else 3 * nl
+        # the block's own path choice: grouped GEMMs (10 kernels per layer) from
+        # moe.PREFILL_MIN_TOKENS tokens on, else one persistent kernel (T = 1) or 3 per layer
+        use_prefill = (T >= moe.PREFILL_MIN_TOKENS) if args.path == "auto" else (args.path == "prefill" and T > 1)
+        launches_per_step = 10 * nl if use_prefill else (1 if persist_ctas else 3 * nl)
+        stack_fn = moe.moe_stack_prefill if use_prefill else moe.moe_stack
         bytes_per_step = nl * (9 * EXPERT_BYTES * (1 if T == 1 else 0) + ROUTER_BYTES + WSG_BYTES + 2 * T * 2048 * 4)
-        ws = torch.empty(moe.stack_workspace_bytes(T), dtype=torch.uint8, device=dev)
+        ws = (torch.empty(_abi.prefill_workspace_size(T), dtype=torch.uint8, device=dev) if use_prefill
+              else torch.empty(moe.stack_workspace_bytes(T), dtype=torch.uint8, device=dev))
         tok_bits = synth.tokens(args.seed, (K + W) * T, stream=100 + rank)
         tok = torch.from_numpy(synth.bf16_bits_to_f32(tok_bits).reshape(K + W, T, 2048).copy())
         tok_dev = tok.to(dev)
@@ -223,13 +232,13 @@ def run_b200(args):
         with torch.cuda.stream(s):
             x_in.copy_(tok_dev[0])
             resid.copy_(x_in)
-            moe.moe_stack(resid, eng, ws=ws, ids_out=ids_step)
+            stack_fn(resid, eng, ws=ws, ids_out=ids_step)
         torch.cuda.current_stream(dev).wait_stream(s)
         torch.cuda.synchronize(dev)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             resid.copy_(x_in)
-            moe.moe_stack(resid, eng, ws=ws, ids_out=ids_step)
+            stack_fn(resid, eng, ws=ws, ids_out=ids_step)
 
         def step(i):
             x_in.copy_(tok_dev[i], non_blocking=True)
@@ -371,7 +380,8 @@ def run_b200(args):
             raise SystemExit("non-finite result in e2e run")
         e2e = {"value": world * K * T / (ems / 1e3), "unit": "tok/s", "h2d_bytes_per_step": T * 2048 * 4,
                "d2h_bytes_per_step": T * 2048 * 4, "ms_per_step": ems / K,
-               "api": "b200moe.moe.moe_stack (C ABI b200moe_stack_decode) in a CUDA graph"}
+               "api": ("b200moe.moe.moe_stack_prefill (C ABI b200moe_moe_prefill per layer)" if use_prefill else
+                       "b200moe.moe.moe_stack (C ABI b200moe_stack_decode)") + " in a CUDA graph"}
 
     # ---------------- CPU baseline (rank 0, N=1 only)
     cpu = None
@@ -396,7 +406,8 @@ def run_b200(args):
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Q4_K, config-0 field law; random-init weights)",
-        "config": {"workload": {"stack_decode": "config4_stack_decode_b%d" % T,
+        "config": {"workload": {"stack_decode": ("config2_zipf_stack_decode_b%d" if args.zipf
+                                                 else "config4_stack_decode_b%d") % T,
                                 "layer_decode": "config0_layer_decode_b%d" % T,
                                 "prefill": "config3_prefill_t%d" % T,
                                 "prefill_ep": "config3_prefill_ep_t%d" % (T * world)}[args.workload],
@@ -411,8 +422,10 @@ def run_b200(args):
                      "kernel": (("one graph replay = 1 persistent kernel over all %d layers (%d CTAs in clusters "
                                  "of %d; router, routing, bulk-copied Q4_K gate/up and down rows, combine)"
                                  % (nl, persist_ctas, persist_cluster)) if persist_ctas
-                                else "one graph replay = %d kernels (router/shared K1, routed gate_up K2, down+combine "
-                                     "K3 per layer)" % launches_per_step)
+                                else ("one graph replay = %d kernels (10 per layer: the grouped-GEMM path)"
+                                      % launches_per_step if args.workload == "stack_decode" and use_prefill else
+                                      "one graph replay = %d kernels (router/shared K1, routed gate_up K2, "
+                                      "down+combine K3 per layer)" % launches_per_step))
                                if args.workload in ("stack_decode", "layer_decode")
                                else ("one step = %d kernels per layer (prep, router GEMM, route, count, plan, fill, x gather, "
                                      "tcgen05 gate_up GEMM, tcgen05 down GEMM, combine); achieved = expert FLOPs / "

@@ -77,7 +77,11 @@ def _tokens(g, device) -> tuple:
     return x, (_abi.F32 if x.dtype == torch.float32 else _abi.BF16)
 
 
-PREFILL_MIN_TOKENS = 64   # at and above this many tokens the grouped-GEMM path is used
+# At and above this many tokens the grouped-GEMM path is used. Measured on the 40-layer stack
+# (config 2 routing law): the decode kernels re-read each token's expert rows, ~0.58 ms per
+# token over 40 layers (5.15 ms at 8 tokens, 9.76 ms at 16), while the grouped GEMMs cost a
+# nearly flat ~6 ms (6.0 ms at 2 tokens, 6.9 ms at 32): they cross near 10 tokens.
+PREFILL_MIN_TOKENS = 10
 
 
 def prefill_workspace(T: int, device) -> torch.Tensor:
