@@ -99,7 +99,8 @@ def test_decode_zipf_batch(cuda):
     from b200moe.engine import DeviceLayer
     L = DeviceLayer.synthetic(2, 0, cuda, bias=True)
     xb = synth.tokens(2, 32, stream=0)
-    out, info = moe.moe_block(torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).to(cuda), L)
+    out, info = moe.moe_block(torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).to(cuda), L,
+                              path="decode")
     ids = info["ids"].cpu().numpy()
     Lh = host_layer(2, 0, bias=True)
     r = OM.router(bf16_bits_to_f32(xb), Lh.wg, Lh.bias)
