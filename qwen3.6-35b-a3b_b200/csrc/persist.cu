@@ -64,7 +64,6 @@ constexpr int kQ = kK * kI / kN;         // 32 routed row pairs per CTA
 constexpr int kJ = kI / kN;              // 4 shared row pairs per CTA
 constexpr int kHr = kH / kN;             // 16 down rows per CTA
 constexpr int kRowPair = 2 * kRowUp;     // 2304 B: gate row + up row
-constexpr int kRouterRowBytes = kH * 4;  // room for one f32 router row (a bf16 row uses half)
 constexpr int kRtRows = 3;               // per layer: the CTA's 2 router rows + the gate row
 constexpr int kGuChunks = 8;             // routed gate/up arrival chunks (one mbarrier each)
 constexpr int kGuChunk = kQ / kGuChunks; // 4 row pairs per chunk
@@ -93,21 +92,27 @@ struct MegaParams {
   b200moe_layer L[kMaxLayers];
 };
 
-// dynamic shared memory layout (bytes)
+// dynamic shared memory layout (bytes). Two instantiations of the kernel: kGen (some layer has
+// f32 router rows or an RMSNorm weight) with 8 KB router slots, and the bf16 / unweighted one
+// with 4 KB slots, whose code has neither the dtype nor the weight branches.
 constexpr int kOffRes = 0;                                   // [kResPad] f32 residual (or x)
 constexpr int kOffS = kOffRes + kResPad * 4;                 // [4096] f32 routed s, flat (slot, j)
 constexpr int kOffSsh = kOffS + kK * kI * 4;                 // [512] f32 shared-expert s
 constexpr int kOffDl = kOffSsh + kI * 4;                     // [2048] f32 gathered deltas
 constexpr int kOffLg = kOffDl + kH * 4;                      // [128] u32 gathered logit pairs
-constexpr int kOffRt = kOffLg + kN * 4;                      // [2 layers][3 rows][8192 B] router rows
-constexpr int kOffGu = kOffRt + 2 * kRtRows * kRouterRowBytes;  // [36] gate rows, then [36] up rows
-constexpr int kOffDn = kOffGu + (kQ + kJ) * kRowPair;        // [9][16] down rows
-constexpr int kOffO = kOffDn + (kK + 1) * kHr * kRowDown;    // [9][16] f32 down outputs
-constexpr int kOffRr = kOffO + (kK + 1) * kHr * 4;           // Route
-constexpr int kOffMisc = kOffRr + 128;                       // [3] router row results, [36] s out
-constexpr int kOffScr = kOffMisc + 256;                      // [12][32] f32 per-warp scratch
-constexpr int kOffBar = kOffScr + 12 * 32 * 4;               // mbarriers
-constexpr int kSmem = kOffBar + 256;
+constexpr int kOffRt = kOffLg + kN * 4;                      // [2 layers][3 rows][slot] router rows
+template <bool kGen>
+struct Lay {
+  static constexpr int kRouterSlot = kGen ? kH * 4 : kH * 2;              // bytes per router row slot
+  static constexpr int kOffGu = kOffRt + 2 * kRtRows * kRouterSlot;       // [36] gate rows, then [36] up rows
+  static constexpr int kOffDn = kOffGu + (kQ + kJ) * kRowPair;            // [9][16] down rows
+  static constexpr int kOffO = kOffDn + (kK + 1) * kHr * kRowDown;        // [9][16] f32 down outputs
+  static constexpr int kOffRr = kOffO + (kK + 1) * kHr * 4;               // Route
+  static constexpr int kOffMisc = kOffRr + 128;                           // [3] router row results, [36] s out
+  static constexpr int kOffScr = kOffMisc + 256;                          // [12][32] f32 per-warp scratch
+  static constexpr int kOffBar = kOffScr + 12 * 32 * 4;                   // mbarriers
+  static constexpr int kSmem = kOffBar + 256;
+};
 
 // ---------------------------------------------------------------- device helpers
 __device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t *p) {
@@ -202,8 +207,9 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// x values of chunk (kb, c) from the padded residual, each scaled by rs (and by the RMSNorm
-// weight nw, a second rounding, when given).
+// x values of chunk (kb, c) from the padded residual, each scaled by rs (and, kGen only, by the
+// RMSNorm weight nw, a second rounding, when given).
+template <bool kGen>
 __device__ __forceinline__ void xchunk_pad(const float *row, float rs, const float *nw, int kb, int c, XChunk &x) {
   const int p = (4 * kb + (c >> 1)) * kPadSeg + 16 * (c & 1);
   const int e = (4 * kb + (c >> 1)) * 64 + 16 * (c & 1);  // element index of the run's start
@@ -215,7 +221,7 @@ __device__ __forceinline__ void xchunk_pad(const float *row, float rs, const flo
     x.lo[4 * i + 2] = __fmul_rn(a.z, rs); x.lo[4 * i + 3] = __fmul_rn(a.w, rs);
     x.hi[4 * i] = __fmul_rn(b.x, rs); x.hi[4 * i + 1] = __fmul_rn(b.y, rs);
     x.hi[4 * i + 2] = __fmul_rn(b.z, rs); x.hi[4 * i + 3] = __fmul_rn(b.w, rs);
-    if (nw) {
+    if (kGen && nw) {
       const float4 wa = __ldg(reinterpret_cast<const float4 *>(nw + e + 4 * i));
       const float4 wb = __ldg(reinterpret_cast<const float4 *>(nw + e + 32 + 4 * i));
       x.lo[4 * i] = __fmul_rn(x.lo[4 * i], wa.x); x.lo[4 * i + 1] = __fmul_rn(x.lo[4 * i + 1], wa.y);
@@ -257,47 +263,66 @@ __device__ __forceinline__ float chunk_total32(float acc, float *scratch) {
 
 // One router row staged in shared memory (bf16, or f32 when wf32): R1 in the declared order
 // (bf16 logit bits) or, for the shared-expert gate, sigmoid(w_sg . x) with the decode path's
-// arithmetic (f32 bits). Lane 0 holds the result.
+// arithmetic (f32 bits). Lane 0 holds the result. The !kGen form takes bf16 rows and no weight
+// (wf32 and nw ignored) and scales x inside the dot product: the same roundings in the same order.
+template <bool kGen>
 __device__ __forceinline__ uint32_t router_row(const uint8_t *row, bool wf32, const float *res, float rs,
                                                const float *nw, int lane, bool gate, float bias, float *scratch) {
   const float *xv = res + lane * kPadSeg;
-  // the lane's 64 inputs: resid * rs (* nw), in element order
-  float xs[64];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float4 x = *reinterpret_cast<const float4 *>(xv + 4 * i);
-    xs[4 * i] = __fmul_rn(x.x, rs); xs[4 * i + 1] = __fmul_rn(x.y, rs);
-    xs[4 * i + 2] = __fmul_rn(x.z, rs); xs[4 * i + 3] = __fmul_rn(x.w, rs);
-  }
-  if (nw) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float4 w = __ldg(reinterpret_cast<const float4 *>(nw + 64 * lane + 4 * i));
-      xs[4 * i] = __fmul_rn(xs[4 * i], w.x); xs[4 * i + 1] = __fmul_rn(xs[4 * i + 1], w.y);
-      xs[4 * i + 2] = __fmul_rn(xs[4 * i + 2], w.z); xs[4 * i + 3] = __fmul_rn(xs[4 * i + 3], w.w);
-    }
-  }
   float acc = 0.0f;
-  if (wf32) {
-    const float4 *rp = reinterpret_cast<const float4 *>(row) + 16 * lane;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float4 w = rp[i];
-      acc = __fmaf_rn(xs[4 * i], w.x, acc);
-      acc = __fmaf_rn(xs[4 * i + 1], w.y, acc);
-      acc = __fmaf_rn(xs[4 * i + 2], w.z, acc);
-      acc = __fmaf_rn(xs[4 * i + 3], w.w, acc);
-    }
-  } else {
+  if constexpr (!kGen) {
     const uint4 *rp = reinterpret_cast<const uint4 *>(row) + 8 * lane;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const uint4 u = rp[i];
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      const float4 x0 = *reinterpret_cast<const float4 *>(xv + 8 * i);
+      const float4 x1 = *reinterpret_cast<const float4 *>(xv + 8 * i + 4);
+      const float x8[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        acc = __fmaf_rn(xs[8 * i + 2 * q], bf16f(w[q]), acc);
-        acc = __fmaf_rn(xs[8 * i + 2 * q + 1], bf16f(w[q] >> 16), acc);
+        acc = __fmaf_rn(__fmul_rn(x8[2 * q], rs), bf16f(w[q]), acc);
+        acc = __fmaf_rn(__fmul_rn(x8[2 * q + 1], rs), bf16f(w[q] >> 16), acc);
+      }
+    }
+  } else {
+    // the lane's 64 inputs: resid * rs (* nw), in element order
+    float xs[64];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float4 x = *reinterpret_cast<const float4 *>(xv + 4 * i);
+      xs[4 * i] = __fmul_rn(x.x, rs); xs[4 * i + 1] = __fmul_rn(x.y, rs);
+      xs[4 * i + 2] = __fmul_rn(x.z, rs); xs[4 * i + 3] = __fmul_rn(x.w, rs);
+    }
+    if (nw) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 w = __ldg(reinterpret_cast<const float4 *>(nw + 64 * lane + 4 * i));
+        xs[4 * i] = __fmul_rn(xs[4 * i], w.x); xs[4 * i + 1] = __fmul_rn(xs[4 * i + 1], w.y);
+        xs[4 * i + 2] = __fmul_rn(xs[4 * i + 2], w.z); xs[4 * i + 3] = __fmul_rn(xs[4 * i + 3], w.w);
+      }
+    }
+    if (wf32) {
+      const float4 *rp = reinterpret_cast<const float4 *>(row) + 16 * lane;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 w = rp[i];
+        acc = __fmaf_rn(xs[4 * i], w.x, acc);
+        acc = __fmaf_rn(xs[4 * i + 1], w.y, acc);
+        acc = __fmaf_rn(xs[4 * i + 2], w.z, acc);
+        acc = __fmaf_rn(xs[4 * i + 3], w.w, acc);
+      }
+    } else {
+      const uint4 *rp = reinterpret_cast<const uint4 *>(row) + 8 * lane;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint4 u = rp[i];
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc = __fmaf_rn(xs[8 * i + 2 * q], bf16f(w[q]), acc);
+          acc = __fmaf_rn(xs[8 * i + 2 * q + 1], bf16f(w[q] >> 16), acc);
+        }
       }
     }
   }
@@ -378,7 +403,9 @@ __device__ __forceinline__ bool gather(const uint64_t *base, uint32_t tag, const
   return !__syncthreads_or(fail);
 }
 
+template <bool kGen>
 __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ MegaParams P) {
+  using SL = Lay<kGen>;
   extern __shared__ __align__(128) uint8_t smem[];
   float *res_s = reinterpret_cast<float *>(smem + kOffRes);
   float *s_s = reinterpret_cast<float *>(smem + kOffS);
@@ -386,15 +413,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
   float *dl_s = reinterpret_cast<float *>(smem + kOffDl);
   uint32_t *lg_s = reinterpret_cast<uint32_t *>(smem + kOffLg);
   uint8_t *rt = smem + kOffRt;
-  uint8_t *gu_g = smem + kOffGu;                  // [32 routed + 4 shared] gate rows
+  uint8_t *gu_g = smem + SL::kOffGu;                  // [32 routed + 4 shared] gate rows
   uint8_t *gu_u = gu_g + (kQ + kJ) * kRowUp;      // the matching up rows
-  uint8_t *dn = smem + kOffDn;                    // [9][16] down rows
-  float *o_s = reinterpret_cast<float *>(smem + kOffO);
-  Route *rr = reinterpret_cast<Route *>(smem + kOffRr);
-  uint32_t *row_out = reinterpret_cast<uint32_t *>(smem + kOffMisc);  // [3] router row results
-  float *s_out = reinterpret_cast<float *>(smem + kOffMisc + 16);      // [36] this CTA's s values
-  float *warp_scr = reinterpret_cast<float *>(smem + kOffScr);
-  uint64_t *bar = reinterpret_cast<uint64_t *>(smem + kOffBar);
+  uint8_t *dn = smem + SL::kOffDn;                    // [9][16] down rows
+  float *o_s = reinterpret_cast<float *>(smem + SL::kOffO);
+  Route *rr = reinterpret_cast<Route *>(smem + SL::kOffRr);
+  uint32_t *row_out = reinterpret_cast<uint32_t *>(smem + SL::kOffMisc);  // [3] router row results
+  float *s_out = reinterpret_cast<float *>(smem + SL::kOffMisc + 16);      // [36] this CTA's s values
+  float *warp_scr = reinterpret_cast<float *>(smem + SL::kOffScr);
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem + SL::kOffBar);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x;
@@ -413,12 +440,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
 
   auto issue_router_rows = [&](int l) {  // thread 0: layer l's 2 router rows + gate row -> rt[l & 1]
     uint64_t *b = bar + kBarRt0 + (l & 1);
-    const uint32_t rb = P.L[l].router_f32 ? kH * 4 : kH * 2;  // bytes of one row as stored
+    // bytes of one row as stored; the rows sit at that pitch, the CTA's two router rows one copy
+    const uint32_t rb = (kGen && P.L[l].router_f32) ? kH * 4 : kH * 2;
     mbar_expect_tx(b, kRtRows * rb);
-    uint8_t *d = rt + (size_t)(l & 1) * kRtRows * kRouterRowBytes;
-    bulk_g2s(d, (const uint8_t *)P.L[l].router_w + (size_t)(2 * c) * rb, rb, b, pol_normal);
-    bulk_g2s(d + kRouterRowBytes, (const uint8_t *)P.L[l].router_w + (size_t)(2 * c + 1) * rb, rb, b, pol_normal);
-    bulk_g2s(d + 2 * kRouterRowBytes, P.L[l].sh_gate_w, rb, b, pol_normal);
+    uint8_t *d = rt + (size_t)(l & 1) * kRtRows * SL::kRouterSlot;
+    bulk_g2s(d, (const uint8_t *)P.L[l].router_w + (size_t)(2 * c) * rb, 2 * rb, b, pol_normal);
+    bulk_g2s(d + 2 * rb, P.L[l].sh_gate_w, rb, b, pol_normal);
     armed |= 1u << (kBarRt0 + (l & 1));
   };
   auto issue_shared_gu = [&](int l) {  // thread 0: layer l's shared-expert gate/up rows, 2 copies
@@ -528,9 +555,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
     if (!fail && warp < kRtRows) {  // warps 0, 1: logits 2c, 2c+1; warp 2: the gate
       const bool gate = warp == 2;
       const float bias = (!gate && Lp.logit_bias) ? Lp.logit_bias[2 * c + warp] : 0.0f;
-      const uint32_t v =
-          router_row(rt + ((size_t)(l & 1) * kRtRows + warp) * kRouterRowBytes, Lp.router_f32 != 0, res_s, rs,
-                     P.resid ? Lp.norm_w : nullptr, lane, gate, bias, warp_scr + 32 * warp);
+      const bool wf32 = kGen && Lp.router_f32 != 0;
+      const uint32_t v = router_row<kGen>(rt + (size_t)(l & 1) * kRtRows * SL::kRouterSlot +
+                                              (size_t)warp * (wf32 ? kH * 4 : kH * 2),
+                                          wf32, res_s, rs, P.resid ? Lp.norm_w : nullptr, lane, gate, bias,
+                                          warp_scr + 32 * warp);
       if (lane == 0) row_out[warp] = v;
     }
     if (__syncthreads_or(fail)) { aborted = true; break; }
@@ -590,8 +619,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
         if (warp >= kRtRows) rs = rms_scale();
         XChunk X0, X1;
         const float *nw = P.resid ? Lp.norm_w : nullptr;
-        xchunk_pad(res_s, rs, nw, kb0, cc, X0);
-        xchunk_pad(res_s, rs, nw, kb0 + 4, cc, X1);
+        xchunk_pad<kGen>(res_s, rs, nw, kb0, cc, X0);
+        xchunk_pad<kGen>(res_s, rs, nw, kb0 + 4, cc, X1);
         constexpr int kStep = 2 * (kWarps - 1);
         for (int ia = 2 * (warp - 1); ia < kJ + kQ && !fail; ia += kStep) {
           const int ib = ia + 1;  // the second pair of this iteration (if any)
@@ -739,9 +768,13 @@ bool prepare(int dev, DevInfo &d) {
   d.init = true;
   int sms = 0, maxsm = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < kN) return false;
+  constexpr int kSmem = Lay<true>::kSmem;  // the larger footprint decides residency for both
   if (cudaDeviceGetAttribute(&maxsm, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || maxsm < kSmem)
     return false;
-  if (cudaFuncSetAttribute(k_mega, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess) return false;
+  if (cudaFuncSetAttribute(k_mega<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess ||
+      cudaFuncSetAttribute(k_mega<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay<false>::kSmem) !=
+          cudaSuccess)
+    return false;
   // the largest cluster size whose 128 / C clusters are all resident at once
   for (int C : {8, 4, 2}) {
     cudaLaunchConfig_t cfg = {};
@@ -756,7 +789,7 @@ bool prepare(int dev, DevInfo &d) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, k_mega, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&clusters, k_mega<true>, &cfg) != cudaSuccess) {
       (void)cudaGetLastError();
       continue;
     }
@@ -768,7 +801,8 @@ bool prepare(int dev, DevInfo &d) {
   }
   int coop = 0, per_sm = 0;
   if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess || !coop) return false;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega, kThreads, kSmem) != cudaSuccess || per_sm < 1)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega<true>, kThreads, kSmem) != cudaSuccess ||
+      per_sm < 1)
     return false;
   d.C = 1;
   d.ok = true;
@@ -809,12 +843,16 @@ int launch(const Args &a, cudaStream_t stream) {
     p.n_layers = nl;
     p.ids_out = a.ids_out ? a.ids_out + (size_t)l0 * kK : nullptr;
     p.w_out = a.w_out ? a.w_out + (size_t)l0 * kK : nullptr;
-    for (int l = 0; l < nl; ++l) p.L[l] = a.layers[l0 + l];
+    bool gen = false;  // f32 router rows or an applied RMSNorm weight somewhere in this launch
+    for (int l = 0; l < nl; ++l) {
+      p.L[l] = a.layers[l0 + l];
+      gen |= p.L[l].router_f32 != 0 || (a.resid && p.L[l].norm_w);
+    }
     B2_CUDA(cudaMemsetAsync(a.scratch, 0, kScratchClear, stream));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kN);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmem;
+    cfg.dynamicSmemBytes = gen ? Lay<true>::kSmem : Lay<false>::kSmem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     if (d.C > 1) {  // clusters: every cluster co-scheduled; all 128 / C clusters fit at once
@@ -828,7 +866,8 @@ int launch(const Args &a, cudaStream_t stream) {
     }
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    B2_CUDA(cudaLaunchKernelEx(&cfg, k_mega, p));
+    if (gen) B2_CUDA(cudaLaunchKernelEx(&cfg, k_mega<true>, p));
+    else B2_CUDA(cudaLaunchKernelEx(&cfg, k_mega<false>, p));
   }
   return B200MOE_OK;
 }
