@@ -15,6 +15,10 @@
  *   routed down      : [256 experts][2048 rows][2 blocks]  (row = 512 weights, 288 B)
  *   shared gate / up : [512][8] blocks,  shared down: [2048][2] blocks
  *   router W_g       : [256][2048] bf16,  shared-expert gate w_sg: [2048] bf16
+ * The published Q4_K_M file mixes block formats per tensor (down Q5_K, or Q6_K at three
+ * layers; the shared expert Q8_0): b200moe_layer.down_type / sh_type say which, rows keep the
+ * GGUF order with the format's own row bytes (down row: Q4_K 288, Q5_K 352, Q6_K 420 B;
+ * Q8_0 shared gate/up row 2176 B, down row 544 B).
  */
 #ifndef B200MOE_H
 #define B200MOE_H
@@ -26,7 +30,7 @@
 extern "C" {
 #endif
 
-#define B200MOE_ABI_VERSION 2
+#define B200MOE_ABI_VERSION 3
 #define B200MOE_HIDDEN 2048
 #define B200MOE_EXPERTS 256
 #define B200MOE_TOPK 8
@@ -35,6 +39,10 @@ extern "C" {
 
 enum { B200MOE_OK = 0, B200MOE_EINVAL = 1, B200MOE_ECUDA = 2, B200MOE_ESIZE = 3 };
 enum { B200MOE_F32 = 0, B200MOE_BF16 = 1 };
+
+/* GGML block type ids (as stored in GGUF tensor infos): b200moe_dequant's `type`, and
+ * b200moe_layer.down_type / sh_type. */
+enum { B200MOE_TYPE_Q8_0 = 8, B200MOE_TYPE_Q4_K = 12, B200MOE_TYPE_Q5_K = 13, B200MOE_TYPE_Q6_K = 14 };
 
 /* One MoE layer's device-resident weights. `gate_up_expert_stride` is the byte distance
  * between consecutive experts inside `gate` and `up`: 589,824 for the two separate GGUF
@@ -58,6 +66,13 @@ typedef struct b200moe_layer {
                                 GGUF post_attention_norm holds 1 + w), applied where the library
                                 normalises the residual itself (resid / stack modes):
                                 x = (resid * rs) * norm_w, two roundings; NULL: weight 1 */
+    int32_t down_type;       /* block type of `down`: 0 or B200MOE_TYPE_Q4_K, B200MOE_TYPE_Q5_K,
+                                B200MOE_TYPE_Q6_K. down_expert_stride >= 2048 rows x row bytes */
+    int32_t sh_type;         /* block type of sh_gate / sh_up / sh_down: 0 or B200MOE_TYPE_Q4_K,
+                                B200MOE_TYPE_Q8_0. A layer with any type other than Q4_K runs on
+                                the gather-GEMV decode kernels only: the single-token persistent
+                                kernel and the grouped GEMMs (moe_prefill, moe_experts) take
+                                Q4_K, and the latter refuse such a layer (B200MOE_EINVAL) */
 } b200moe_layer;
 
 /* ABI version (B200MOE_ABI_VERSION) and the last error message on this thread. */
@@ -70,9 +85,6 @@ const char *b200moe_last_error(void);
  * tools/gguf_reader.py:178 dequant -> _deq_q4_k :248-267; bit-exact against both. */
 int b200moe_q4k_dequant(const void *blocks, int64_t nblocks, void *out, int out_dtype,
                         void *stream);
-
-/* GGML block type ids (as stored in GGUF tensor infos) accepted by b200moe_dequant. */
-enum { B200MOE_TYPE_Q8_0 = 8, B200MOE_TYPE_Q4_K = 12, B200MOE_TYPE_Q5_K = 13, B200MOE_TYPE_Q6_K = 14 };
 
 /* Q4_K, Q5_K, Q6_K or Q8_0 (`type`, GGML id) -> f32 or bf16 for `nblocks` consecutive blocks,
  * elements in stored order; `out` 16-byte aligned (and Q5_K `blocks`). The published Q4_K_M

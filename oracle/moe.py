@@ -20,7 +20,7 @@ import os
 
 import numpy as np
 
-from . import q4k
+from . import kquants, q4k
 from .bf16 import bf16_bits_to_f32
 
 H, E, TOPK, I = 2048, 256, 8, 512
@@ -114,11 +114,15 @@ class HostLayer:
     shared expert in the same per-expert shapes; ``wg`` [256, 2048] and ``wsg`` [2048]
     bf16 bits; ``bias`` an optional f32 [256] logit offset. Expert matrices are produced
     lazily (``expert_blocks``) so a test can hold a full 256-expert layer without
-    materialising 453 MB.
+    materialising 453 MB. ``types`` (optional) names other block formats per kind, as the
+    published Q4_K_M file has them: ``{"down": "Q5_K" | "Q6_K", "sh_gate" / "sh_up" /
+    "sh_down": "Q8_0"}`` (kquants.py decodes them); ``block_fn`` then serves those kinds'
+    blocks in their own sizes.
     """
 
-    def __init__(self, block_fn, wg, wsg, bias=None):
-        self._block_fn = block_fn     # (kind, first_block, nblocks) -> uint8 [n, 144]
+    def __init__(self, block_fn, wg, wsg, bias=None, types=None):
+        self._block_fn = block_fn     # (kind, first_block, nblocks) -> uint8 [n, block bytes]
+        self.types = dict(types or {})
         keep = lambda a: np.asarray(a) if np.asarray(a).dtype == np.float32 else np.asarray(a, np.uint16)  # noqa
         self.wg = np.ascontiguousarray(keep(wg)).reshape(E, H)      # bf16 bits, or f32 values
         self.wsg = np.ascontiguousarray(keep(wsg)).reshape(H)
@@ -127,13 +131,13 @@ class HostLayer:
     def matrix(self, kind: str, e: int = 0) -> np.ndarray:
         """Dequantized f32 matrix: gate/up [512, 2048], down [2048, 512] of expert e, or the
         shared ``sh_gate``/``sh_up``/``sh_down``."""
-        rows, kb = {"gate": (I, H // 256), "up": (I, H // 256), "down": (H, I // 256),
-                    "sh_gate": (I, H // 256), "sh_up": (I, H // 256),
-                    "sh_down": (H, I // 256)}[kind]
-        per = rows * kb
+        rows, cols = {"gate": (I, H), "up": (I, H), "down": (H, I),
+                      "sh_gate": (I, H), "sh_up": (I, H), "sh_down": (H, I)}[kind]
+        tname = self.types.get(kind, "Q4_K")
+        per = rows * cols // kquants.BLOCK_ELTS[tname]
         first = 0 if kind.startswith("sh_") else e * per
         blocks = self._block_fn(kind, first, per)
-        return q4k.dequant(blocks.tobytes(), per).reshape(rows, kb * 256)
+        return kquants.dequant(np.ascontiguousarray(blocks).tobytes(), tname, per).reshape(rows, cols)
 
 
 def silu64(z):

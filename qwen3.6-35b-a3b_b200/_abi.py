@@ -41,7 +41,8 @@ class Layer(ctypes.Structure):
                 ("sh_gate", ctypes.c_void_p), ("sh_up", ctypes.c_void_p),
                 ("sh_down", ctypes.c_void_p), ("router_w", ctypes.c_void_p),
                 ("sh_gate_w", ctypes.c_void_p), ("logit_bias", ctypes.c_void_p),
-                ("router_f32", ctypes.c_int32), ("norm_w", ctypes.c_void_p)]
+                ("router_f32", ctypes.c_int32), ("norm_w", ctypes.c_void_p),
+                ("down_type", ctypes.c_int32), ("sh_type", ctypes.c_int32)]
 
 
 _LIB = None
@@ -136,8 +137,7 @@ def q4k_dequant(blocks, out, out_dtype: int, stream=None):
 
 
 # GGML block type ids accepted by b200moe_dequant, and their block sizes (bytes, elements).
-TYPE_IDS = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
-BLOCK_GEOM = {"Q8_0": (34, 32), "Q4_K": (144, 256), "Q5_K": (176, 256), "Q6_K": (210, 256)}
+from .geometry import BLOCK_GEOM, TYPE_IDS  # noqa: E402
 
 
 def dequant(blocks, tname: str, out, out_dtype: int, stream=None):

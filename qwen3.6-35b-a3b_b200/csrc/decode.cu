@@ -16,10 +16,13 @@
 //                  for the 9 experts and the combine: ascending expert id, product and sum
 //                  rounded separately, + gate * shared (engine/m3_forward.py:452-475).
 // Q4_K is dequantised in registers straight from 16-byte streaming loads; every weight byte
-// is read once per token.
+// is read once per token. K2 / K3 are templates on the layer's block types: Q5_K / Q6_K down
+// and a Q8_0 shared expert (the published Q4_K_M file) go through kq_dot.cuh's chunk dots,
+// loaded after the dependency resolves.
 #include <mutex>
 
 #include "common.cuh"
+#include "kq_dot.cuh"
 #include "mega.cuh"
 #include "route.cuh"
 
@@ -204,6 +207,8 @@ __device__ __forceinline__ void load_rowpair(const uint8_t *rg, const uint8_t *r
   }
 }
 
+// kShQ8: the shared expert's gate / up rows are Q8_0 (2176 B), dotted chunk by chunk.
+template <bool kShQ8>
 __global__ void __launch_bounds__(128) k_gateup(K2Params P) {
   __shared__ Route rr;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -211,6 +216,25 @@ __global__ void __launch_bounds__(128) k_gateup(K2Params P) {
   const int k = r / kK2CtasPerSlot;
   const int jbase = (r % kK2CtasPerSlot) * kK2RowsPerCta + warp * kK2RowsPerWarp;
   const int kb0 = lane >> 3, cc = lane & 7;
+  if (kShQ8 && k == kK) {  // the whole CTA is in the shared slot
+    pdl_wait();
+    pdl_trigger();
+    XChunk X0, X1;
+    load_xchunk(P.xw + (size_t)t * kH, kb0, cc, X0);
+    load_xchunk(P.xw + (size_t)t * kH, kb0 + 4, cc, X1);
+    constexpr int64_t kRow = row_bytes(B200MOE_TYPE_Q8_0, kH);
+    float *sdst = P.s + ((size_t)t * 9 + kK) * kI + jbase;
+#pragma unroll 1
+    for (int jj = 0; jj < kK2RowsPerWarp; ++jj) {
+      const uint8_t *rg = P.sh_gate + (size_t)(jbase + jj) * kRow, *ru = P.sh_up + (size_t)(jbase + jj) * kRow;
+      float g = q80_chunk_dot(rg, kb0, cc, X0) + q80_chunk_dot(rg, kb0 + 4, cc, X1);
+      float u = q80_chunk_dot(ru, kb0, cc, X0) + q80_chunk_dot(ru, kb0 + 4, cc, X1);
+      g = warp_sum(g);
+      u = warp_sum(u);
+      if (lane == 0) sdst[jj] = __fmul_rn(silu_f(g), u);
+    }
+    return;
+  }
   const uint8_t *gb, *ub;
   uint4 cur[8];
   if (k == kK) {  // shared expert: static rows, load before the dependency resolves
@@ -264,6 +288,10 @@ struct K3Params {
   uint16_t *w_out;
 };
 
+// kDn: block type of the routed down rows (Q4_K / Q5_K / Q6_K); kSh: of the shared down rows
+// (Q4_K / Q8_0). Q4_K rows are loaded into registers before the dependency resolves, the
+// others read after it.
+template <int kDn, int kSh>
 __global__ void __launch_bounds__(288) k_down(K3Params P) {
   __shared__ Route rr;
   __shared__ float o[9][kK3Rows];
@@ -274,13 +302,17 @@ __global__ void __launch_bounds__(288) k_down(K3Params P) {
   if (warp == 0) route_warp(P.logits + (size_t)t * kE, &rr);
   __syncthreads();
   const int half = lane >> 4, kb = (lane >> 3) & 1, cc = lane & 7;
-  const uint8_t *base = warp < kK ? P.down + (size_t)rr.ids[warp] * P.stride : P.sh_down;
+  const bool routed = warp < kK;
+  const uint8_t *base = routed ? P.down + (size_t)rr.ids[warp] * P.stride : P.sh_down;
+  const bool q4 = routed ? kDn == B200MOE_TYPE_Q4_K : kSh == B200MOE_TYPE_Q4_K;
   uint4 hq[kK3Rows / 2][2];
+  if (q4) {
 #pragma unroll
-  for (int it = 0; it < kK3Rows / 2; ++it) {
-    const uint8_t *p = base + (size_t)(h0 + 2 * it + half) * kRowDown + kb * kQB;
-    hq[it][0] = ldg_stream(p);
-    hq[it][1] = ldg_stream(p + 16 + 16 * cc);
+    for (int it = 0; it < kK3Rows / 2; ++it) {
+      const uint8_t *p = base + (size_t)(h0 + 2 * it + half) * kRowDown + kb * kQB;
+      hq[it][0] = ldg_stream(p);
+      hq[it][1] = ldg_stream(p + 16 + 16 * cc);
+    }
   }
   pdl_wait();
   pdl_trigger();
@@ -288,7 +320,12 @@ __global__ void __launch_bounds__(288) k_down(K3Params P) {
   load_xchunk(P.s + ((size_t)t * 9 + warp) * kI, kb, cc, X);
 #pragma unroll
   for (int it = 0; it < kK3Rows / 2; ++it) {
-    const float v = half_warp_sum(q4k_chunk_dot(hq[it][0], hq[it][1], cc, X));
+    const int h = h0 + 2 * it + half;
+    float v;
+    if (q4) v = q4k_chunk_dot(hq[it][0], hq[it][1], cc, X);
+    else if (routed) v = row_chunk_dot<kDn>(base + (size_t)h * row_bytes(kDn, kI), kb, cc, X);
+    else v = row_chunk_dot<kSh>(base + (size_t)h * row_bytes(kSh, kI), kb, cc, X);
+    v = half_warp_sum(v);
     if ((lane & 15) == 0) o[warp][2 * it + half] = v;
   }
   __syncthreads();
@@ -365,14 +402,23 @@ int check_layer(const b200moe_layer *L, const char *who) {
   if (!al16(L->gate) || !al16(L->up) || !al16(L->down) || !al16(L->sh_gate) || !al16(L->sh_up) ||
       !al16(L->sh_down) || !al16(L->router_w) || !al16(L->sh_gate_w))
     return b2host::set_error(B200MOE_EINVAL, "%s: weight pointers must be 16-byte aligned", who);
+  const int dt = layer_down_type(L), st = layer_sh_type(L);
+  if (dt != B200MOE_TYPE_Q4_K && dt != B200MOE_TYPE_Q5_K && dt != B200MOE_TYPE_Q6_K)
+    return b2host::set_error(B200MOE_EINVAL, "%s: down_type %d is not Q4_K(12), Q5_K(13) or Q6_K(14)", who,
+                             L->down_type);
+  if (st != B200MOE_TYPE_Q4_K && st != B200MOE_TYPE_Q8_0)
+    return b2host::set_error(B200MOE_EINVAL, "%s: sh_type %d is not Q4_K(12) or Q8_0(8)", who, L->sh_type);
   if (L->gate_up_expert_stride < (int64_t)kI * kRowUp || (L->gate_up_expert_stride & 15))
     return b2host::set_error(B200MOE_EINVAL, "%s: gate_up_expert_stride %lld invalid", who,
                              (long long)L->gate_up_expert_stride);
-  if (L->down_expert_stride < (int64_t)kH * kRowDown || (L->down_expert_stride & 15))
-    return b2host::set_error(B200MOE_EINVAL, "%s: down_expert_stride %lld invalid", who,
-                             (long long)L->down_expert_stride);
+  if (L->down_expert_stride < (int64_t)kH * row_bytes(dt, kI) || (L->down_expert_stride & 15))
+    return b2host::set_error(B200MOE_EINVAL, "%s: down_expert_stride %lld invalid for down_type %d (at least %lld)",
+                             who, (long long)L->down_expert_stride, dt, (long long)(kH * row_bytes(dt, kI)));
   return B200MOE_OK;
 }
+
+// K3 for the layer's (down, shared) block types.
+cudaError_t launch_down(const b200moe_layer *L, unsigned grid, cudaStream_t s, const K3Params &p);
 
 K1Params k1_params(const void *x, int x_dtype, const float *resid, float eps, int T, const b200moe_layer *L,
                    const DecodeWS &w) {
@@ -410,7 +456,10 @@ int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const 
   p2.logits = w.logits;
   p2.xw = w.xw;
   p2.s = w.s;
-  B2_CUDA(launch(k_gateup, (unsigned)(T * kK2CtasPerToken), 32 * kK2Warps, 0, s, true, p2));
+  if (layer_sh_type(L) == B200MOE_TYPE_Q8_0)
+    B2_CUDA(launch(k_gateup<true>, (unsigned)(T * kK2CtasPerToken), 32 * kK2Warps, 0, s, true, p2));
+  else
+    B2_CUDA(launch(k_gateup<false>, (unsigned)(T * kK2CtasPerToken), 32 * kK2Warps, 0, s, true, p2));
   K3Params p3;
   p3.down = (const uint8_t *)L->down;
   p3.stride = L->down_expert_stride;
@@ -422,8 +471,21 @@ int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const 
   p3.accumulate = resid ? 1 : 0;
   p3.ids_out = ids_out;
   p3.w_out = w_out;
-  B2_CUDA(launch(k_down, (unsigned)(T * kK3CtasPerToken), 288, 0, s, true, p3));
+  B2_CUDA(launch_down(L, (unsigned)(T * kK3CtasPerToken), s, p3));
   return B200MOE_OK;
+}
+
+cudaError_t launch_down(const b200moe_layer *L, unsigned grid, cudaStream_t s, const K3Params &p) {
+  constexpr int Q4 = B200MOE_TYPE_Q4_K, Q5 = B200MOE_TYPE_Q5_K, Q6 = B200MOE_TYPE_Q6_K, Q8 = B200MOE_TYPE_Q8_0;
+  const int dt = layer_down_type(L);
+  if (layer_sh_type(L) == Q8) {
+    if (dt == Q5) return launch(k_down<Q5, Q8>, grid, 288, 0, s, true, p);
+    if (dt == Q6) return launch(k_down<Q6, Q8>, grid, 288, 0, s, true, p);
+    return launch(k_down<Q4, Q8>, grid, 288, 0, s, true, p);
+  }
+  if (dt == Q5) return launch(k_down<Q5, Q4>, grid, 288, 0, s, true, p);
+  if (dt == Q6) return launch(k_down<Q6, Q4>, grid, 288, 0, s, true, p);
+  return launch(k_down<Q4, Q4>, grid, 288, 0, s, true, p);
 }
 
 constexpr int kMaxT = 1 << 16;
@@ -522,7 +584,8 @@ int b200moe_moe_decode(const void *x, int x_dtype, int T, const b200moe_layer *l
   if (rc) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   const DecodeWS w = carve(ws, T);
-  if (T == 1 && b2mega::usable()) return run_persistent(x, x_dtype, nullptr, 0.f, 1, layer, out, ids_out, w_out, w, s);
+  if (T == 1 && layer_all_q4k(layer) && b2mega::usable())
+    return run_persistent(x, x_dtype, nullptr, 0.f, 1, layer, out, ids_out, w_out, w, s);
   return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, w, s, true);
 }
 
@@ -542,7 +605,7 @@ int b200moe_moe_decode_noalloc(const void *x, int x_dtype, int T, const b200moe_
   void *scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc) return rc;
-  if (T == 1 && b2mega::usable())
+  if (T == 1 && layer_all_q4k(layer) && b2mega::usable())
     return run_persistent(x, x_dtype, nullptr, 0.f, 1, layer, out, ids_out, w_out, carve(scratch, T),
                           (cudaStream_t)stream);
   return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, carve(scratch, T), (cudaStream_t)stream,
@@ -568,13 +631,15 @@ int b200moe_stack_decode(float *resid, int T, const b200moe_layer *layers, int n
   if (!al16(resid) || !al16(ws)) return b2host::set_error(B200MOE_EINVAL, "stack_decode: pointers must be 16-byte aligned");
   if (ws_bytes < decode_ws_bytes(T))
     return b2host::set_error(B200MOE_ESIZE, "stack_decode: workspace %zu B < required %zu B", ws_bytes, decode_ws_bytes(T));
+  bool q4 = true;  // every layer Q4_K throughout: the persistent kernel takes the stack
   for (int l = 0; l < n_layers; ++l) {
     int rc = check_layer(&layers[l], "stack_decode");
     if (rc) return rc;
+    q4 = q4 && layer_all_q4k(&layers[l]);
   }
   cudaStream_t s = (cudaStream_t)stream;
   const DecodeWS w = carve(ws, T);
-  if (T == 1 && b2mega::usable())
+  if (T == 1 && q4 && b2mega::usable())
     return run_persistent(nullptr, B200MOE_F32, resid, eps, n_layers, layers, nullptr, ids_out, nullptr, w, s);
   for (int l = 0; l < n_layers; ++l) {
     int rc = run_layer(nullptr, B200MOE_F32, resid, eps, T, &layers[l], nullptr,

@@ -1,0 +1,126 @@
+// kq_dot.cuh -- chunk dot products for the other block formats of the published Q4_K_M file
+// (expert down Q5_K / Q6_K, shared expert Q8_0) on the gather-GEMV decode kernels.
+//
+// Each function takes the same lane work as q4k_chunk_dot: chunk (kb, c) of a row, i.e. the 16
+// elements chunk_pos(kb, c) + i ("lo") and the 16 elements 32 later ("hi"), with their x values
+// in an XChunk, and returns sum_i w_i * x_i over those 32 elements in f32. The weights are the
+// exact f32 values the dequantisers give (oracle/kquants.py); the sum is a plain f32 chain per
+// run times the run's scale, the kernels' rounding, not a declared order.
+//
+// Layouts (tools/gguf_reader.py:238-333 in the reference; llama.cpp dequantize_row_*):
+//   Q5_K 176 B / 256: f16 d | f16 dmin | 12 B scales+mins (Q4_K packing) | qh[32] | qs[128]
+//        element e: j = e>>5, q = nibble (j&1) of qs[32(e>>6) + (e&31)] | bit j of qh[e&31] << 4
+//        value (d*sc[j])*q - dmin*m[j]. Blocks 16-byte aligned (176 = 11 x 16).
+//   Q6_K 210 B / 256: ql[128] | qh[64] | int8 sc[16] | f16 d
+//        element e: G = e>>7, k = (e>>5)&3, l = e&31
+//        q = (ql[64G + 32(k&1) + l] >> 4(k>>1)) & 15 | ((qh[32G + l] >> 2k) & 3) << 4
+//        value (d*sc[e>>4])*(q - 32). Blocks only 2-byte aligned: 16-bit loads.
+//   Q8_0  34 B / 32:  f16 d | int8 q[32]; value d*q. Blocks 2-byte aligned: 16-bit loads.
+#pragma once
+
+#include "common.cuh"
+
+namespace b2 {
+
+// Bytes of one row of `n` weights (n a multiple of 256) in GGML block type t (0 = Q4_K).
+__host__ __device__ constexpr int64_t row_bytes(int t, int n) {
+  return t == B200MOE_TYPE_Q5_K   ? (int64_t)n / 256 * 176
+         : t == B200MOE_TYPE_Q6_K ? (int64_t)n / 256 * 210
+         : t == B200MOE_TYPE_Q8_0 ? (int64_t)n / 32 * 34
+                                  : (int64_t)n / 256 * 144;
+}
+
+// The layer's block types with 0 read as Q4_K.
+inline int layer_down_type(const b200moe_layer *L) { return L->down_type ? L->down_type : B200MOE_TYPE_Q4_K; }
+inline int layer_sh_type(const b200moe_layer *L) { return L->sh_type ? L->sh_type : B200MOE_TYPE_Q4_K; }
+inline bool layer_all_q4k(const b200moe_layer *L) {
+  return layer_down_type(L) == B200MOE_TYPE_Q4_K && layer_sh_type(L) == B200MOE_TYPE_Q4_K;
+}
+
+// 16 bytes from a 2-byte aligned address (eight 16-bit read-only loads).
+__device__ __forceinline__ uint4 ld16_a2(const uint8_t *p) {
+  const unsigned short *q = reinterpret_cast<const unsigned short *>(p);
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = (uint32_t)__ldg(q + 2 * i) | ((uint32_t)__ldg(q + 2 * i + 1) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ uint32_t byte_of(const uint4 &v, int i) {  // byte i (0..15)
+  const uint32_t w = i < 4 ? v.x : i < 8 ? v.y : i < 12 ? v.z : v.w;
+  return (w >> (8 * (i & 3))) & 0xFFu;
+}
+
+// Q5_K: block kb of the row at `row` (16-byte aligned).
+__device__ __forceinline__ float q5k_chunk_dot(const uint8_t *row, int kb, int c, const XChunk &x) {
+  const uint8_t *blk = row + (size_t)kb * 176;
+  const uint4 h = ldg_stream(blk);
+  const uint4 qh = ldg_stream(blk + 16 + 16 * (c & 1));
+  const uint4 qs = ldg_stream(blk + 48 + 16 * c);
+  float s0, m0, s1, m1;
+  q4k_scales(h, c, s0, m0, s1, m1);  // sub-blocks 2g and 2g+1, g = c >> 1 (the Q4_K scale packing)
+  const int j0 = 2 * (c >> 1);
+  float al = 0.f, ah = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t b = byte_of(qs, i), hb = byte_of(qh, i);
+    const uint32_t ql = (b & 15u) | (((hb >> j0) & 1u) << 4);
+    const uint32_t qu = (b >> 4) | (((hb >> (j0 + 1)) & 1u) << 4);
+    al = fmaf((float)ql, x.lo[i], al);
+    ah = fmaf((float)qu, x.hi[i], ah);
+  }
+  return fmaf(s0, al, -m0 * x.slo) + fmaf(s1, ah, -m1 * x.shi);
+}
+
+// Q6_K: block kb of the row at `row` (2-byte aligned).
+__device__ __forceinline__ float q6k_chunk_dot(const uint8_t *row, int kb, int c, const XChunk &x) {
+  const uint8_t *blk = row + (size_t)kb * 210;
+  const int g = c >> 1, G = g >> 1, l0 = 16 * (c & 1), sh = 4 * (g & 1);
+  const uint4 qlo = ld16_a2(blk + 64 * G + l0);       // k = 2(g&1): ql[64G + l], nibble g&1
+  const uint4 qhi = ld16_a2(blk + 64 * G + 32 + l0);  // k = 2(g&1)+1: ql[64G + 32 + l]
+  const uint4 qh = ld16_a2(blk + 128 + 32 * G + l0);  // bits 2k, 2k+1 of qh[32G + l]
+  const float d = f16f(__ldg(reinterpret_cast<const unsigned short *>(blk + 208)));
+  const float s_lo = d * (float)(int8_t)__ldg(blk + 192 + 4 * g + (c & 1));      // sc[e >> 4], exact
+  const float s_hi = d * (float)(int8_t)__ldg(blk + 192 + 4 * g + 2 + (c & 1));
+  float al = 0.f, ah = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t hb = byte_of(qh, i);
+    const int ql = (int)(((byte_of(qlo, i) >> sh) & 15u) | (((hb >> sh) & 3u) << 4)) - 32;
+    const int qu = (int)(((byte_of(qhi, i) >> sh) & 15u) | (((hb >> (sh + 2)) & 3u) << 4)) - 32;
+    al = fmaf((float)ql, x.lo[i], al);
+    ah = fmaf((float)qu, x.hi[i], ah);
+  }
+  return fmaf(s_lo, al, s_hi * ah);
+}
+
+// Q8_0: the chunk's lo run is positions l0..l0+15 of block 8kb + 2g, its hi run the same
+// positions of the next block (row 2-byte aligned).
+__device__ __forceinline__ float q80_chunk_dot(const uint8_t *row, int kb, int c, const XChunk &x) {
+  const int b0 = 8 * kb + 2 * (c >> 1), l0 = 16 * (c & 1);
+  const uint8_t *p0 = row + (size_t)b0 * 34, *p1 = p0 + 34;
+  const float d0 = f16f(__ldg(reinterpret_cast<const unsigned short *>(p0)));
+  const float d1 = f16f(__ldg(reinterpret_cast<const unsigned short *>(p1)));
+  const uint4 q0 = ld16_a2(p0 + 2 + l0), q1 = ld16_a2(p1 + 2 + l0);
+  float al = 0.f, ah = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    al = fmaf((float)(int8_t)byte_of(q0, i), x.lo[i], al);
+    ah = fmaf((float)(int8_t)byte_of(q1, i), x.hi[i], ah);
+  }
+  return fmaf(d0, al, d1 * ah);
+}
+
+// Chunk (kb, c) of a row stored in block type kT (B200MOE_TYPE_*), loads included.
+template <int kT>
+__device__ __forceinline__ float row_chunk_dot(const uint8_t *row, int kb, int c, const XChunk &x) {
+  if constexpr (kT == B200MOE_TYPE_Q5_K) return q5k_chunk_dot(row, kb, c, x);
+  else if constexpr (kT == B200MOE_TYPE_Q6_K) return q6k_chunk_dot(row, kb, c, x);
+  else if constexpr (kT == B200MOE_TYPE_Q8_0) return q80_chunk_dot(row, kb, c, x);
+  else {
+    const uint4 h = ldg_stream(row + (size_t)kb * kQB), q = ldg_stream(row + (size_t)kb * kQB + 16 + 16 * c);
+    return q4k_chunk_dot(h, q, c, x);
+  }
+}
+
+}  // namespace b2

@@ -31,6 +31,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "kq_dot.cuh"
 #include "route.cuh"
 #include "tc.cuh"
 
@@ -996,10 +997,16 @@ int gemm_maps(int mode, const b200moe_layer *L, const __half *x16p, const __half
   return B200MOE_OK;
 }
 
-int check_prefill_layer(const b200moe_layer *L, const char *who) {
+// experts: the call runs the grouped GEMMs, which take Q4_K expert and shared rows only.
+int check_prefill_layer(const b200moe_layer *L, const char *who, bool experts = true) {
   if (!L || !L->gate || !L->up || !L->down || !L->sh_gate || !L->sh_up || !L->sh_down || !L->router_w ||
       !L->sh_gate_w)
     return b2host::set_error(B200MOE_EINVAL, "%s: layer is NULL or has a NULL weight pointer", who);
+  if (experts && !layer_all_q4k(L))
+    return b2host::set_error(B200MOE_EINVAL,
+                             "%s: the grouped GEMMs take Q4_K expert and shared rows; this layer has down type %d, "
+                             "shared type %d (run it through b200moe_moe_decode)",
+                             who, layer_down_type(L), layer_sh_type(L));
   return B200MOE_OK;
 }
 
@@ -1112,7 +1119,7 @@ int b200moe_moe_route(const void *x, int x_dtype, float *resid, float eps, int T
   if (ws_bytes < prefill_ws_bytes(T))
     return b2host::set_error(B200MOE_ESIZE, "moe_route: workspace %zu B < required %zu B", ws_bytes,
                              prefill_ws_bytes(T));
-  int rc = check_prefill_layer(L, "moe_route");
+  int rc = check_prefill_layer(L, "moe_route", false);
   if (rc) return rc;
   return route_stage(x, x_dtype, resid, eps, T, L, (__half *)x16_out, ids_out, w_out, sg_out, carve_prefill(ws, T),
                      (cudaStream_t)stream);

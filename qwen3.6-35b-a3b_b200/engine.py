@@ -19,9 +19,9 @@ import torch
 
 from . import _abi
 from . import synth
-from .geometry import (E, EXPERT_DOWN_BYTES, EXPERT_GATE_BYTES, Geometry, H, I, KIND_BLOCKS,
-                       KIND_DOWN, KIND_GATE, KIND_SH_DOWN, KIND_SH_GATE, KIND_SH_UP, KIND_UP,
-                       Q4K_BYTES, stream_id)
+from .geometry import (DOWN_TYPES, E, EXPERT_GATE_BYTES, SHARED_TYPES, TYPE_IDS, Geometry, H, I,
+                       KIND_BLOCKS, KIND_DOWN, KIND_GATE, KIND_SH_DOWN, KIND_SH_GATE, KIND_SH_UP,
+                       KIND_UP, Q4K_BYTES, row_bytes, stream_id)
 
 
 def _bf16_tensor(bits: np.ndarray, device) -> torch.Tensor:
@@ -39,10 +39,13 @@ def _router_tensor(w: np.ndarray, device) -> torch.Tensor:
 
 
 class DeviceLayer:
-    """One MoE layer in HBM. Q4_K tensors are uint8 [n_blocks * 144]."""
+    """One MoE layer in HBM. Weight tensors are uint8 block bytes in GGUF order: gate / up
+    Q4_K; down Q4_K, Q5_K or Q6_K (``down_type``); the shared expert Q4_K or Q8_0
+    (``sh_type``). A layer with a type other than Q4_K runs on the decode kernels only."""
 
     def __init__(self, gate, up, down, sh_gate, sh_up, sh_down, router_w, sh_gate_w,
-                 logit_bias=None, gate_up_stride: int = EXPERT_GATE_BYTES, norm_w=None):
+                 logit_bias=None, gate_up_stride: int = EXPERT_GATE_BYTES, norm_w=None,
+                 down_type: str = "Q4_K", sh_type: str = "Q4_K"):
         self.gate, self.up, self.down = gate, up, down
         self.sh_gate, self.sh_up, self.sh_down = sh_gate, sh_up, sh_down
         self.router_w, self.sh_gate_w, self.logit_bias = router_w, sh_gate_w, logit_bias
@@ -55,7 +58,25 @@ class DeviceLayer:
         if norm_w is not None and (norm_w.dtype != torch.float32 or norm_w.numel() != H):
             raise ValueError("norm_w must be f32 [%d]" % H)
         self.norm_w = norm_w
+        if down_type not in DOWN_TYPES or sh_type not in SHARED_TYPES:
+            raise ValueError("down_type %r / sh_type %r: the kernels take down %s, shared %s"
+                             % (down_type, sh_type, "/".join(DOWN_TYPES), "/".join(SHARED_TYPES)))
+        self.down_type, self.sh_type = down_type, sh_type
+        self.down_stride = H * row_bytes(down_type, I)   # bytes per expert of ffn_down_exps
+        if down.numel() != E * self.down_stride:
+            raise ValueError("down holds %d B; %d experts of %s need %d" % (down.numel(), E, down_type,
+                                                                             E * self.down_stride))
+        for name, t, n in (("sh_gate", sh_gate, I * row_bytes(sh_type, H)),
+                           ("sh_up", sh_up, I * row_bytes(sh_type, H)),
+                           ("sh_down", sh_down, H * row_bytes(sh_type, I))):
+            if t.numel() != n:
+                raise ValueError("%s holds %d B; %s needs %d" % (name, t.numel(), sh_type, n))
         self._abi = None
+
+    @property
+    def all_q4k(self) -> bool:
+        """Every expert and shared matrix is Q4_K (the persistent and grouped-GEMM paths)."""
+        return self.down_type == "Q4_K" and self.sh_type == "Q4_K"
 
     # ------------------------------------------------------------------ construction
     @classmethod
@@ -87,10 +108,11 @@ class DeviceLayer:
 
     @classmethod
     def from_host(cls, blocks: dict, router_w_bits, sh_gate_w_bits, logit_bias=None,
-                  device="cuda", norm_w=None) -> "DeviceLayer":
-        """From host arrays: ``blocks[kind]`` uint8 Q4_K bytes for gate/up/down/sh_gate/sh_up/sh_down
-        (GGUF order); the router and shared gate as bf16 bit patterns (uint16) or f32 values
-        (float32, both the same type)."""
+                  device="cuda", norm_w=None, down_type: str = "Q4_K",
+                  sh_type: str = "Q4_K") -> "DeviceLayer":
+        """From host arrays: ``blocks[kind]`` uint8 block bytes for gate/up/down/sh_gate/sh_up/sh_down
+        (GGUF order; down in ``down_type``, the shared expert in ``sh_type``); the router and
+        shared gate as bf16 bit patterns (uint16) or f32 values (float32, both the same type)."""
         dev = torch.device(device)
         with warnings.catch_warnings():  # read-only views (e.g. a memory-mapped GGUF): only read, then copied
             warnings.filterwarnings("ignore", message="The given NumPy array is not writable")
@@ -100,16 +122,18 @@ class DeviceLayer:
         return cls(t["gate"], t["up"], t["down"], t["sh_gate"], t["sh_up"], t["sh_down"],
                    _router_tensor(router_w_bits, dev), _router_tensor(sh_gate_w_bits, dev), lb,
                    norm_w=None if norm_w is None else torch.from_numpy(
-                       np.ascontiguousarray(norm_w, dtype=np.float32)).to(dev))
+                       np.ascontiguousarray(norm_w, dtype=np.float32)).to(dev),
+                   down_type=down_type, sh_type=sh_type)
 
     # ------------------------------------------------------------------ ABI view
     def abi(self) -> _abi.Layer:
         if self._abi is None:
             p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
             self._abi = _abi.Layer(p(self.gate), p(self.up), self.gate_up_stride, p(self.down),
-                                   EXPERT_DOWN_BYTES, p(self.sh_gate), p(self.sh_up), p(self.sh_down),
+                                   self.down_stride, p(self.sh_gate), p(self.sh_up), p(self.sh_down),
                                    p(self.router_w), p(self.sh_gate_w), p(self.logit_bias),
-                                   1 if self.router_w.dtype == torch.float32 else 0, p(self.norm_w))
+                                   1 if self.router_w.dtype == torch.float32 else 0, p(self.norm_w),
+                                   TYPE_IDS[self.down_type], TYPE_IDS[self.sh_type])
         return self._abi
 
     @property
@@ -126,10 +150,14 @@ class DeviceLayer:
         return n
 
     # ------------------------------------------------------------------ inspection
+    def type_of(self, kind: str) -> str:
+        """Block format of ``kind`` (gate / up / down / sh_gate / sh_up / sh_down)."""
+        return "Q4_K" if kind in ("gate", "up") else self.down_type if kind == "down" else self.sh_type
+
     def expert_blocks(self, kind: str, e: int = 0) -> torch.Tensor:
-        """The Q4_K bytes (device uint8 view) of one expert matrix or of a shared matrix."""
+        """The block bytes (device uint8 view) of one expert matrix or of a shared matrix."""
         if kind == "down":
-            return self.down[e * EXPERT_DOWN_BYTES:(e + 1) * EXPERT_DOWN_BYTES]
+            return self.down[e * self.down_stride:(e + 1) * self.down_stride]
         if kind in ("gate", "up"):
             base = self.gate if kind == "gate" else self.up
             return base[e * self.gate_up_stride: e * self.gate_up_stride + EXPERT_GATE_BYTES]
@@ -139,7 +167,7 @@ class DeviceLayer:
         blocks = self.expert_blocks(kind, e)
         shape = (H, I) if kind.endswith("down") else (I, H)
         out = torch.empty(shape, dtype=dtype, device=blocks.device)
-        _abi.q4k_dequant(blocks, out, _abi.BF16 if dtype == torch.bfloat16 else _abi.F32)
+        _abi.dequant(blocks, self.type_of(kind), out, _abi.BF16 if dtype == torch.bfloat16 else _abi.F32)
         return out
 
 
@@ -169,11 +197,12 @@ class DeviceEngine:
         if role == "ffn_gate_inp_shexp":
             return L.sh_gate_w.float().reshape(1, H), None, dict(
                 type_name="F32" if L.sh_gate_w.dtype == torch.float32 else "BF16")
-        return L.dequant(self.ROLE[role]), None, dict(type_name="Q4_K")
+        return L.dequant(self.ROLE[role]), None, dict(type_name=L.type_of(self.ROLE[role]))
 
     def expert(self, role: str, layer: int, idx: int, shape_hf):
         """(values, None, rec) like ``Engine.expert`` :268 -- dequantized on the device."""
-        v = self.layers[layer].dequant(self.ROLE[role], idx)
+        L = self.layers[layer]
+        v = L.dequant(self.ROLE[role], idx)
         if tuple(v.shape) != tuple(shape_hf):
             raise ValueError("%s expert %d is %s, caller wants %s" % (role, idx, tuple(v.shape), tuple(shape_hf)))
-        return v, None, dict(type_name="Q4_K")
+        return v, None, dict(type_name=L.type_of(self.ROLE[role]))

@@ -23,6 +23,20 @@ EXPERT_DOWN_BYTES = H * ROW_DOWN        # 589,824 B (ffn_down_exps per expert)
 EXPERT_BYTES = 2 * EXPERT_GATE_BYTES + EXPERT_DOWN_BYTES   # 1,769,472 B
 ROUTER_BYTES = E * H * 2                # 1,048,576 B bf16
 
+# Block formats the kernels take (GGML type ids as in GGUF): (bytes, elements) per block. The
+# published Q4_K_M file stores expert gate/up as Q4_K, expert down as Q5_K (Q6_K at three layers)
+# and the shared expert as Q8_0.
+TYPE_IDS = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
+BLOCK_GEOM = {"Q8_0": (34, 32), "Q4_K": (144, 256), "Q5_K": (176, 256), "Q6_K": (210, 256)}
+DOWN_TYPES = ("Q4_K", "Q5_K", "Q6_K")      # ffn_down_exps
+SHARED_TYPES = ("Q4_K", "Q8_0")            # ffn_{gate,up,down}_shexp
+
+
+def row_bytes(tname: str, n: int) -> int:
+    """Bytes of one row of ``n`` weights in block format ``tname``."""
+    bb, be = BLOCK_GEOM[tname]
+    return n // be * bb
+
 # Synthetic Q4_K streams: stream id = 8*layer + kind.
 KIND_GATE, KIND_UP, KIND_DOWN, KIND_SH_GATE, KIND_SH_UP, KIND_SH_DOWN = range(6)
 KIND_BLOCKS = {KIND_GATE: E * I * 8, KIND_UP: E * I * 8, KIND_DOWN: E * H * 2,

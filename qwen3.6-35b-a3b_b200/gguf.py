@@ -12,11 +12,11 @@ Replaces the reference's ``tools/gguf_reader.py:492 Gguf`` (header parse) and th
                  u64 offset from the data section)
     data section at the next multiple of ``general.alignment`` (default 32)
 
-Block types the device paths take: the expert GEMMs and decode GEMVs read Q4_K (type 12);
-the router and shared-expert gate are used as stored, bf16 (type 30) or F32 (type 0; F16 is
-widened to f32 exactly). Other types are refused by name with the reason (Q5_K / Q6_K / Q8_0
-tensors of the published Q4_K_M file decode through ``b200moe_dequant`` but have no GEMM
-path).
+Block types the device paths take, as stored: expert gate / up Q4_K (type 12); expert down
+Q4_K, Q5_K (13) or Q6_K (14); the shared expert Q4_K or Q8_0 (8) -- the published Q4_K_M file
+has Q5_K down (Q6_K at three layers) and a Q8_0 shared expert, which run on the decode kernels
+(the grouped GEMMs take Q4_K layers). The router and shared-expert gate are used as stored,
+bf16 (type 30) or F32 (type 0; F16 is widened to f32 exactly). Other types are refused by name.
 """
 from __future__ import annotations
 
@@ -25,7 +25,7 @@ import struct
 
 import numpy as np
 
-from .geometry import E, H, I
+from .geometry import DOWN_TYPES, E, H, I, SHARED_TYPES
 
 GGML_TYPES = {0: "F32", 1: "F16", 2: "Q4_0", 3: "Q4_1", 6: "Q5_0", 7: "Q5_1", 8: "Q8_0", 9: "Q8_1",
               10: "Q2_K", 11: "Q3_K", 12: "Q4_K", 13: "Q5_K", 14: "Q6_K", 15: "Q8_K", 30: "BF16"}
@@ -163,31 +163,43 @@ class GgufFile:
 def _want(gf: GgufFile, name: str, types, dims) -> TensorInfo:
     ti = gf.info(name)
     if ti.type_name not in types:
-        raise GgufError("type", "%s is %s; the device path takes %s%s" % (
-            name, ti.type_name, "/".join(types),
-            " (Q5_K / Q6_K / Q8_0 decode with b200moe_dequant but have no GEMM path)"
-            if ti.type_name in ("Q5_K", "Q6_K", "Q8_0") else ""))
+        raise GgufError("type", "%s is %s; the device path takes %s" % (name, ti.type_name, "/".join(types)))
     strip = lambda t: tuple(t[:max([i + 1 for i, d in enumerate(t) if d != 1] or [0])])  # noqa: E731
     if strip(ti.dims) != strip(tuple(dims)):  # trailing unit dims are immaterial
         raise GgufError("shape", "%s has dims %s (GGUF order), expected %s" % (name, ti.dims, tuple(dims)))
     return ti
 
 
+_TENSORS = (("gate", "ffn_gate_exps", (H, I, E), ("Q4_K",)), ("up", "ffn_up_exps", (H, I, E), ("Q4_K",)),
+            ("down", "ffn_down_exps", (I, H, E), DOWN_TYPES), ("sh_gate", "ffn_gate_shexp", (H, I), SHARED_TYPES),
+            ("sh_up", "ffn_up_shexp", (H, I), SHARED_TYPES), ("sh_down", "ffn_down_shexp", (I, H), SHARED_TYPES))
+
+
+def layer_types(gf: GgufFile, layer: int) -> dict:
+    """{"down_type": ..., "sh_type": ...} of layer ``layer`` (block type names as stored). The
+    three shared tensors must share one type."""
+    p = "blk.%d." % layer
+    t = {kind: _want(gf, p + nm + ".weight", types, dims).type_name for kind, nm, dims, types in _TENSORS}
+    if len({t["sh_gate"], t["sh_up"], t["sh_down"]}) != 1:
+        raise GgufError("type", "blk.%d shared expert mixes block types %s / %s / %s" % (
+            layer, t["sh_gate"], t["sh_up"], t["sh_down"]))
+    return dict(down_type=t["down"], sh_type=t["sh_gate"])
+
+
 def layer_host(gf: GgufFile, layer: int, round_router: bool = False) -> tuple:
     """(blocks dict, router bf16 bits [256*2048], shared-gate bf16 bits [2048]) of layer
-    ``layer``: the Q4_K byte views of ``blk.<layer>.ffn_{gate,up,down}_exps`` and
-    ``ffn_{gate,up,down}_shexp`` (views into the memory map: valid while ``gf`` is open) and the
-    bf16 router / shared-gate vectors (copies).
+    ``layer``: the block-byte views of ``blk.<layer>.ffn_{gate,up,down}_exps`` and
+    ``ffn_{gate,up,down}_shexp`` in their stored formats (:func:`layer_types` names them;
+    views into the memory map: valid while ``gf`` is open) and the router / shared-gate
+    vectors (copies).
 
     The router and gate keep their stored type (F32, or F16 widened exactly, as f32 values;
     BF16 as bits). ``round_router``: round F32 / F16 router and gate weights to bf16 (RNE)
     instead -- half the router bytes, but different logits from the stored values'."""
     p = "blk.%d." % layer
     blocks = {}
-    for kind, nm, dims in (("gate", "ffn_gate_exps", (H, I, E)), ("up", "ffn_up_exps", (H, I, E)),
-                           ("down", "ffn_down_exps", (I, H, E)), ("sh_gate", "ffn_gate_shexp", (H, I)),
-                           ("sh_up", "ffn_up_shexp", (H, I)), ("sh_down", "ffn_down_shexp", (I, H))):
-        _want(gf, p + nm + ".weight", ("Q4_K",), dims)
+    for kind, nm, dims, types in _TENSORS:
+        _want(gf, p + nm + ".weight", types, dims)
         blocks[kind] = gf.raw(p + nm + ".weight")
     router = _vector_bf16(gf, p + "ffn_gate_inp.weight", (H, E), round_router)
     shgate = _vector_bf16(gf, p + "ffn_gate_inp_shexp.weight", (H,), round_router)
@@ -227,11 +239,12 @@ def layer_norm(gf: GgufFile, layer: int):
 
 
 def device_layer(gf: GgufFile, layer: int, device="cuda", round_router: bool = False):
-    """:class:`DeviceLayer` of layer ``layer`` read from ``gf`` (Q4_K bytes uploaded as stored,
-    the post-attention norm weight when the file has it)."""
+    """:class:`DeviceLayer` of layer ``layer`` read from ``gf`` (block bytes uploaded as stored,
+    with their types; the post-attention norm weight when the file has it)."""
     from .engine import DeviceLayer
+    types = layer_types(gf, layer)
     blocks, router, shgate = layer_host(gf, layer, round_router)
-    return DeviceLayer.from_host(blocks, router, shgate, device=device, norm_w=layer_norm(gf, layer))
+    return DeviceLayer.from_host(blocks, router, shgate, device=device, norm_w=layer_norm(gf, layer), **types)
 
 
 def device_engine(path: str, layers=None, device="cuda", round_router: bool = False):

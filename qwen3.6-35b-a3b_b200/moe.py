@@ -104,7 +104,9 @@ def moe_block(g: torch.Tensor, E_, layer: int = 0, probe_row=None, out: torch.Te
     Routing is R1-R5 with the cast before the multiply; routed outputs are summed in
     ascending expert id; the shared expert is gated by sigmoid(w_sg . x).
     ``path``: "decode" (gather-GEMV, f32 CUDA cores), "prefill" (token sort + tcgen05 grouped
-    GEMMs, fp16 operands) or "auto" (prefill from ``PREFILL_MIN_TOKENS`` tokens on).
+    GEMMs, fp16 operands) or "auto" (prefill from ``PREFILL_MIN_TOKENS`` tokens on). A layer
+    with Q5_K / Q6_K down or a Q8_0 shared expert (the published Q4_K_M file) runs on the
+    decode kernels at every token count; ``path="prefill"`` refuses it.
     """
     if probe_row is not None:
         raise Refused("probe-row", "band-operand probes are a host-oracle feature; not on the device path")
@@ -116,7 +118,10 @@ def moe_block(g: torch.Tensor, E_, layer: int = 0, probe_row=None, out: torch.Te
     if out is None:
         out = torch.empty((T, H), dtype=torch.float32, device=L.device)
     ids = torch.empty((T, TOPK), dtype=torch.int32, device=L.device)
-    if path == "prefill" or (path == "auto" and T >= PREFILL_MIN_TOKENS):
+    if path == "prefill" and not L.all_q4k:
+        raise Refused("format", "the grouped GEMMs take Q4_K experts; this layer has down %s, shared %s"
+                      % (L.down_type, L.sh_type))
+    if path == "prefill" or (path == "auto" and T >= PREFILL_MIN_TOKENS and L.all_q4k):
         _abi.moe_prefill(x, xd, None, RMS_EPS, T, L.abi(), out, ids, prefill_workspace(T, L.device))
     else:
         _abi.moe_decode(x, xd, T, L.abi(), out, ids, None, workspace(T, L.device))
@@ -166,7 +171,9 @@ def moe_stack_prefill(resid: torch.Tensor, E_: DeviceEngine, n_layers: int | Non
                       eps: float = RMS_EPS, ids_out: torch.Tensor | None = None,
                       ws: torch.Tensor | None = None) -> torch.Tensor:
     """The config-4 sub-stack on the prefill path: per layer ``resid += moe(rmsnorm(resid))``
-    through the tcgen05 grouped GEMMs. ``ids_out`` (optional) is [n_layers, T, 8] int32."""
+    through the tcgen05 grouped GEMMs. ``ids_out`` (optional) is [n_layers, T, 8] int32.
+    Layers that are not Q4_K throughout go through the decode kernels (``b200moe_stack_decode``
+    of that one layer)."""
     if resid.dtype != torch.float32 or resid.shape[-1] != H:
         raise Refused("shape", "resid must be f32 [T, %d]" % H)
     n = len(E_.layers) if n_layers is None else int(n_layers)
@@ -175,8 +182,12 @@ def moe_stack_prefill(resid: torch.Tensor, E_: DeviceEngine, n_layers: int | Non
     dev = E_.layers[0].device
     ws = ws if ws is not None else prefill_workspace(T, dev)
     for l in range(n):
-        _abi.moe_prefill(None, _abi.F32, r, eps, T, E_.layers[l].abi(), None,
-                         None if ids_out is None else ids_out[l], ws)
+        L = E_.layers[l]
+        ids_l = None if ids_out is None else ids_out[l]
+        if L.all_q4k:
+            _abi.moe_prefill(None, _abi.F32, r, eps, T, L.abi(), None, ids_l, ws)
+        else:
+            _abi.stack_decode(r, T, [L.abi()], eps, ids_l, workspace(T, dev))
     return resid
 
 

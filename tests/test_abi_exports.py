@@ -21,7 +21,7 @@ def test_library_exports_every_symbol():
     lib = ctypes.CDLL(_abi.LIB_PATH)
     for name in declared():
         assert hasattr(lib, name), name
-    assert _abi.abi_version() == 2
+    assert _abi.abi_version() == 3
 
 
 def test_errors_without_device_work():
@@ -34,3 +34,32 @@ def test_errors_without_device_work():
     assert L.b200moe_moe_decode(None, 0, 0, None, None, None, None, None, 0, None) == _abi.EINVAL
     assert L.b200moe_decode_workspace_size(0) == 0
     assert L.b200moe_decode_workspace_size(1) > 0
+
+
+def test_block_type_validation_without_device_work():
+    """The layer's block types and the down stride they imply are checked before any CUDA
+    call: unknown types, a Q4_K-sized stride for Q5_K rows, and a grouped-GEMM call on a layer
+    that is not Q4_K throughout are refused with EINVAL. (Fake 16-byte aligned addresses: the
+    refusals come before anything reads them.)"""
+    import ctypes as C
+    from b200moe import _abi
+    lib = _abi.lib()
+    a = 1 << 20  # aligned placeholder address, never dereferenced on these paths
+    ws = 1 << 40
+
+    def layer(down_type=0, sh_type=0, down_stride=2048 * 288):
+        return _abi.Layer(a, a, 512 * 1152, a, down_stride, a, a, a, a, a, None, 0, None, down_type, sh_type)
+
+    def decode(Lr):
+        return lib.b200moe_moe_decode(C.c_void_p(a), _abi.BF16, 1, C.byref(Lr), C.c_void_p(a), None, None,
+                                      C.c_void_p(a), ws, None)
+
+    for Lr, why in ((layer(down_type=99), b"down_type 99"), (layer(sh_type=13), b"sh_type 13"),
+                    (layer(down_type=13), b"down_expert_stride"), (layer(down_type=14, down_stride=2048 * 352),
+                                                                   b"down_expert_stride")):
+        assert decode(Lr) == _abi.EINVAL, why
+        assert why in lib.b200moe_last_error(), (why, lib.b200moe_last_error())
+    Lr = layer(down_type=13, down_stride=2048 * 352, sh_type=8)
+    rc = lib.b200moe_moe_prefill(C.c_void_p(a), _abi.BF16, None, C.c_float(1e-6), 16, C.byref(Lr), C.c_void_p(a),
+                                 None, C.c_void_p(a), ws, None)
+    assert rc == _abi.EINVAL and b"Q4_K" in lib.b200moe_last_error()

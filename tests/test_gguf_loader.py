@@ -1,7 +1,9 @@
 """The GGUF reader (qwen3.6-35b-a3b_b200/gguf.py) on files written here by a minimal GGUF v3
 writer: header and metadata parse, tensor byte views at the right offsets (checked by marker
-bytes at both ends of every tensor), the Q4_K / bf16 type rules, the F32-router rounding
-switch, and the refusals (wrong type, wrong shape, missing tensor, truncated file). Full-size
+bytes at both ends of every tensor), the block-type rules (Q4_K gate/up; Q4_K / Q5_K / Q6_K
+down; Q4_K / Q8_0 shared expert, as the published Q4_K_M file mixes them; bf16 / F32 router),
+the F32-router rounding switch, and the refusals (wrong type, wrong shape, missing tensor,
+truncated file). Full-size
 tensors are sparse holes in the file, so the test writes little and reads little."""
 import struct
 
@@ -9,8 +11,9 @@ import numpy as np
 import pytest
 
 H, I, E = 2048, 512, 256
-Q4K, Q5K, F32, BF16 = 12, 13, 0, 30
-SIZES = {Q4K: (256, 144), Q5K: (256, 176), F32: (1, 4), BF16: (1, 2)}
+Q80, Q4K, Q5K, Q6K, F32, BF16 = 8, 12, 13, 14, 0, 30
+SIZES = {Q80: (32, 34), Q4K: (256, 144), Q5K: (256, 176), Q6K: (256, 210), F32: (1, 4), BF16: (1, 2)}
+NAMES = {Q80: "Q8_0", Q4K: "Q4_K", Q5K: "Q5_K", Q6K: "Q6_K"}
 
 
 def _s(x: str) -> bytes:
@@ -46,13 +49,15 @@ def write_gguf(path, tensors, align=32, truncate=False):
     return data0
 
 
-def layer_tensors(l, down_type=Q4K, router_type=BF16, router_dims=(H, E)):
+def layer_tensors(l, down_type=Q4K, router_type=BF16, router_dims=(H, E), sh_type=Q4K, gate_type=Q4K,
+                  sh_down_type=None):
     p = "blk.%d." % l
     mk = lambda tag: {0: tag * 16, -16: tag[::-1] * 16}  # noqa: E731
-    t = [(p + "ffn_gate_exps.weight", (H, I, E), Q4K, mk(b"G")), (p + "ffn_up_exps.weight", (H, I, E), Q4K, mk(b"U")),
+    t = [(p + "ffn_gate_exps.weight", (H, I, E), gate_type, mk(b"G")),
+         (p + "ffn_up_exps.weight", (H, I, E), Q4K, mk(b"U")),
          (p + "ffn_down_exps.weight", (I, H, E), down_type, mk(b"D")),
-         (p + "ffn_gate_shexp.weight", (H, I), Q4K, mk(b"g")), (p + "ffn_up_shexp.weight", (H, I), Q4K, mk(b"u")),
-         (p + "ffn_down_shexp.weight", (I, H), Q4K, mk(b"d"))]
+         (p + "ffn_gate_shexp.weight", (H, I), sh_type, mk(b"g")), (p + "ffn_up_shexp.weight", (H, I), sh_type, mk(b"u")),
+         (p + "ffn_down_shexp.weight", (I, H), sh_down_type or sh_type, mk(b"d"))]
     rng = np.random.default_rng(l)
     w = rng.normal(0, 0.02, size=E * H).astype(np.float32)
     g = rng.normal(0, 0.02, size=H).astype(np.float32)
@@ -108,18 +113,46 @@ def test_f32_router_kept_exactly_or_rounded_on_request(tmp_path):
         del blocks
 
 
+@pytest.mark.parametrize("down", [Q5K, Q6K])
+def test_published_formats(tmp_path, down):
+    """The published Q4_K_M file's layer formats: Q5_K (or Q6_K) expert down and a Q8_0 shared
+    expert are read as stored, with their types named for the device layer."""
+    gguf = _mod()
+    t, _, _ = layer_tensors(4, down_type=down, sh_type=Q80)
+    path = str(tmp_path / "pub.gguf")
+    write_gguf(path, t)
+    with gguf.GgufFile(path) as gf:
+        assert gguf.layer_types(gf, 4) == dict(down_type=NAMES[down], sh_type="Q8_0")
+        blocks, _, _ = gguf.layer_host(gf, 4)
+        bd, be = SIZES[down][1], SIZES[down][0]
+        sizes = {"gate": E * I * 8 * 144, "up": E * I * 8 * 144, "down": E * H * I // be * bd,
+                 "sh_gate": I * H // 32 * 34, "sh_up": I * H // 32 * 34, "sh_down": H * I // 32 * 34}
+        tags = {"gate": b"G", "up": b"U", "down": b"D", "sh_gate": b"g", "sh_up": b"u", "sh_down": b"d"}
+        for k, v in blocks.items():
+            assert v.size == sizes[k], k
+            assert bytes(v[:16]) == tags[k] * 16 and bytes(v[-16:]) == tags[k] * 16, k
+        del blocks
+
+
 def test_refusals(tmp_path):
     gguf = _mod()
-    t, _, _ = layer_tensors(1, down_type=Q5K)
+    t, _, _ = layer_tensors(1, gate_type=Q5K)
     p1 = str(tmp_path / "q5.gguf")
     write_gguf(p1, t)
     with gguf.GgufFile(p1) as gf:
         with pytest.raises(gguf.GgufError) as ei:
             gguf.layer_host(gf, 1)
-        assert ei.value.tag == "type" and "Q5_K" in str(ei.value) and "b200moe_dequant" in str(ei.value)
+        assert ei.value.tag == "type" and "Q5_K" in str(ei.value) and "ffn_gate_exps" in str(ei.value)
         with pytest.raises(gguf.GgufError) as ei:
             gguf.layer_host(gf, 2)
         assert ei.value.tag == "missing"
+    t, _, _ = layer_tensors(1, sh_type=Q80, sh_down_type=Q4K)
+    p0 = str(tmp_path / "mixed_shared.gguf")
+    write_gguf(p0, t)
+    with gguf.GgufFile(p0) as gf:
+        with pytest.raises(gguf.GgufError) as ei:
+            gguf.layer_types(gf, 1)
+        assert ei.value.tag == "type" and "mixes" in str(ei.value)
     t, _, _ = layer_tensors(1, router_dims=(H, 128))
     p2 = str(tmp_path / "shape.gguf")
     write_gguf(p2, t)

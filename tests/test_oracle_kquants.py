@@ -47,3 +47,18 @@ def test_q5k_fifth_bit_known_answer():
     raw[4:16] = q4k.pack_scale_min(np.ones(8, dtype=np.int64), np.zeros(8, dtype=np.int64))[0]
     raw[16:48] = 0xFF
     assert np.array_equal(KQ.dequant_q5_k(raw), np.full(256, 16.0, dtype=np.float32))
+
+
+def test_host_layer_decodes_typed_kinds():
+    """HostLayer with block types (the published file's down Q5_K / Q6_K, shared Q8_0) serves
+    each kind's matrix through the pinned decoders, at the kind's own block count."""
+    from oracle import kquants
+    from oracle.moe import HostLayer
+    H, I = 2048, 512
+    blk = {"down": kquants.random_blocks("Q6_K", 3 * H * I // 256, 5),
+           "sh_gate": kquants.random_blocks("Q8_0", I * H // 32, 6)}
+    L = HostLayer(lambda k, f, n: blk[k][f:f + n], np.zeros(256 * H, np.uint16), np.zeros(H, np.uint16),
+                  types={"down": "Q6_K", "sh_gate": "Q8_0"})
+    per = H * I // 256
+    assert np.array_equal(L.matrix("down", 2), kquants.dequant_q6_k(blk["down"][2 * per:3 * per]).reshape(H, I))
+    assert np.array_equal(L.matrix("sh_gate"), kquants.dequant_q8_0(blk["sh_gate"]).reshape(I, H))
