@@ -36,6 +36,46 @@ EXPERT_BYTES = 1_769_472            # one Q4_K expert: gate+up [1024,2048] + dow
 ROUTER_BYTES = 256 * 2048 * 2
 WSG_BYTES = 2048 * 2
 N_LAYERS = 40
+Q6K_LAYERS = (34, 38, 39)           # the published file's Q6_K expert-down layers
+
+
+def published_engine(seed, n_layers, dev):
+    """A layer stack in the published Q4_K_M file's layout: Q4_K gate / up (the synthetic
+    generator), Q5_K expert down (Q6_K at layers 34, 38, 39), a Q8_0 shared expert, F32 router and
+    shared-gate weights, a post-attention RMSNorm weight. Block bytes are seeded random with
+    finite f16 scales sized so 40 layers stay finite."""
+    import torch
+    from b200moe.engine import DeviceEngine, DeviceLayer
+    from b200moe.geometry import BLOCK_GEOM, E, H, I
+    g = torch.Generator(device=dev).manual_seed(seed)
+
+    def blocks(tname, n):
+        bb = BLOCK_GEOM[tname][0]
+        t = torch.randint(0, 256, (n, bb), dtype=torch.uint8, device=dev, generator=g)
+        for col, lo, hi in {"Q5_K": ((0, 5e-4, 5e-3), (2, 0.0, 2.5e-3)), "Q6_K": ((208, 1e-4, 1e-3),),
+                            "Q8_0": ((0, 1e-4, 1e-3),)}[tname]:
+            v = (torch.rand(n, device=dev, generator=g) * (hi - lo) + lo).to(torch.float16)
+            t[:, col:col + 2] = v.view(torch.uint8).view(n, 2)
+        return t.reshape(-1)
+
+    layers = []
+    for l in range(n_layers):
+        base = DeviceLayer.synthetic(seed, l, dev)
+        dt = "Q6_K" if l in Q6K_LAYERS else "Q5_K"
+        nw = 1.0 + 0.05 * torch.randn(H, device=dev, generator=g)
+        layers.append(DeviceLayer(base.gate, base.up, blocks(dt, E * H * I // 256), blocks("Q8_0", I * H // 32),
+                                  blocks("Q8_0", I * H // 32), blocks("Q8_0", H * I // 32), base.router_w.float(),
+                                  base.sh_gate_w.float(), norm_w=nw, down_type=dt, sh_type="Q8_0"))
+    return DeviceEngine(layers)
+
+
+def layer_bytes(L) -> tuple:
+    """(bytes of one routed expert, of the shared expert, of the router + shared gate) of a layer."""
+    from b200moe.geometry import H, I, row_bytes
+    routed = 2 * I * row_bytes("Q4_K", H) + H * row_bytes(L.down_type, I)
+    shared = 2 * I * row_bytes(L.sh_type, H) + H * row_bytes(L.sh_type, I)
+    router = L.router_w.numel() * L.router_w.element_size() + L.sh_gate_w.numel() * L.sh_gate_w.element_size()
+    return routed, shared, router
 
 
 def parse():
@@ -54,6 +94,10 @@ def parse():
                         "block's own choice by token count)")
     p.add_argument("--zipf", action="store_true",
                    help="config 2's routing law: a per-expert Zipf(1.1) logit bias on every layer")
+    p.add_argument("--formats", choices=["q4k", "published"], default="q4k",
+                   help="stack_decode weights: Q4_K throughout (the BASELINE configs), or the published "
+                        "Q4_K_M file's layout (Q5_K down, Q6_K at layers 34/38/39, Q8_0 shared expert, F32 "
+                        "router, RMSNorm weight) with seeded random block bytes")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--ref-layers-per-step", type=int, default=2)
     return p.parse_args()
@@ -209,9 +253,12 @@ def run_b200(args):
     expert_bytes = None
 
     if args.workload == "stack_decode":
-        eng = DeviceEngine.synthetic(args.seed, args.layers, dev, bias=args.zipf)
+        eng = (published_engine(args.seed, args.layers, dev) if args.formats == "published"
+               else DeviceEngine.synthetic(args.seed, args.layers, dev, bias=args.zipf))
         nl = args.layers
         persist_ctas, persist_cluster = _abi.decode_persistent_info() if T == 1 else (0, 0)
+        if args.formats == "published" and not _abi.decode_persistent_formats():
+            persist_ctas, persist_cluster = 0, 0  # such layers take the three-kernel path
         # the block's own path choice: grouped GEMMs (10 kernels per layer) from
         # moe.PREFILL_MIN_TOKENS tokens on, else one persistent kernel (T = 1) or 3 per layer
         use_prefill = (T >= moe.PREFILL_MIN_TOKENS) if args.path == "auto" else (args.path == "prefill" and T > 1)
@@ -332,9 +379,9 @@ def run_b200(args):
     ids_np = ids_all[W:].cpu().numpy()
     if args.workload == "stack_decode":
         uniq = [[len(np.unique(ids_np[i, l])) for l in range(nl)] for i in range(K)]
-        bytes_per_step = float(np.mean([sum((u + 1) * EXPERT_BYTES for u in row) for row in uniq])) + \
-            nl * (ROUTER_BYTES + WSG_BYTES + 2 * T * 2048 * 4)
-        expert_bytes = float(np.mean([sum((u + 1) * EXPERT_BYTES for u in row) for row in uniq]))
+        lb = [layer_bytes(eng.layers[l]) for l in range(nl)]  # Q4_K: (EXPERT_BYTES, EXPERT_BYTES, router)
+        expert_bytes = float(np.mean([sum(u * lb[l][0] + lb[l][1] for l, u in enumerate(row)) for row in uniq]))
+        bytes_per_step = expert_bytes + sum(r for _, _, r in lb) + nl * 2 * T * 2048 * 4
     achieved = bytes_per_step / (ms_step / 1e3) / 1e9 if bytes_per_step else None
     roof_bound, roof_unit, peak = "hbm", "GB/s", hbm_peak
     if args.workload in ("prefill", "prefill_ep"):
@@ -399,29 +446,35 @@ def run_b200(args):
                          "engine/m3_forward.py moe_block + rmsnorm_a, per-hit-expert dequant timed)"
                          % (nlp, args.layers, args.layers / nlp)}
 
-    traffic = committed_traffic(args.workload)
+    # the committed ncu traffic is the Q4_K workload's (none recorded for the published layout)
+    traffic = committed_traffic(args.workload) if args.formats == "q4k" else None
     line = {
         "metric": {"stack_decode": "moe_stack_decode_tok_per_s", "layer_decode": "moe_layer_decode_tok_per_s",
                    "prefill": "moe_prefill_tok_per_s", "prefill_ep": "moe_prefill_ep_tok_per_s"}[args.workload],
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded Q4_K, config-0 field law; random-init weights)",
-        "config": {"workload": {"stack_decode": ("config2_zipf_stack_decode_b%d" if args.zipf
+        "data": ("synthetic (seeded Q4_K, config-0 field law; random-init weights)" if args.formats == "q4k" else
+                 "synthetic, published-file layout (Q4_K gate/up, Q5_K/Q6_K down, Q8_0 shared, F32 router; "
+                 "seeded random block bytes)"),
+        "config": {"workload": {"stack_decode": ("published_formats_stack_decode_b%d" if args.formats == "published"
+                                                 else "config2_zipf_stack_decode_b%d" if args.zipf
                                                  else "config4_stack_decode_b%d") % T,
                                 "layer_decode": "config0_layer_decode_b%d" % T,
                                 "prefill": "config3_prefill_t%d" % T,
                                 "prefill_ep": "config3_prefill_ep_t%d" % (T * world)}[args.workload],
                    "layers": nl, "batch": T, "seed": args.seed,
                    "parallelism": ("ep%d" % world) if args.workload == "prefill_ep" else "replicas%d" % world,
-                   "l2": "inputs larger than L2: distinct token per step, %.0f MB of Q4_K streamed per step"
+                   "l2": "inputs larger than L2: distinct token per step, %.0f MB of weights streamed per step"
                          % ((bytes_per_step or 0) / 1e6)},
         "roofline": {"bound": roof_bound, "achieved": achieved, "peak": peak, "unit": roof_unit,
                      "frac": (achieved / peak) if achieved else None,
                      "traffic": traffic.get("dram_bytes_per_step") if traffic else None,
                      "peak_kind": peak_kind,
                      "kernel": (("one graph replay = 1 persistent kernel over all %d layers (%d CTAs in clusters "
-                                 "of %d; router, routing, bulk-copied Q4_K gate/up and down rows, combine)"
-                                 % (nl, persist_ctas, persist_cluster)) if persist_ctas
+                                 "of %d; router, routing, bulk-copied %s gate/up and down rows, combine)"
+                                 % (nl, persist_ctas, persist_cluster,
+                                    "Q4_K" if args.formats == "q4k" else "Q4_K / Q5_K / Q6_K / Q8_0"))
+                                if persist_ctas
                                 else ("one graph replay = %d kernels (10 per layer: the grouped-GEMM path)"
                                       % launches_per_step if args.workload == "stack_decode" and use_prefill else
                                       "one graph replay = %d kernels (router/shared K1, routed gate_up K2, "

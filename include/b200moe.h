@@ -152,6 +152,11 @@ int b200moe_moe_decode_noalloc(const void *x, int x_dtype, int T, const b200moe_
  * only; no counterpart in the reference. Call with the device current. */
 int b200moe_decode_persistent_info(int *ctas, int *cluster);
 
+/* *formats = 1 when the persistent kernel also runs single-token layers in the other block
+ * formats (Q5_K / Q6_K down, Q8_0 shared: its larger-footprint variant is resident with the
+ * same cluster size), else 0 (such layers then take the three-kernel path). Introspection only. */
+int b200moe_decode_persistent_formats(int *formats);
+
 /* Workspace bytes for b200moe_stack_decode. */
 size_t b200moe_stack_workspace_size(int T, int n_layers);
 

@@ -21,6 +21,7 @@ EXPORTS = ("b200moe_abi_version", "b200moe_last_error", "b200moe_q4k_dequant", "
            "b200moe_synth_q4k", "b200moe_router_workspace_size", "b200moe_router",
            "b200moe_decode_workspace_size",
            "b200moe_moe_decode", "b200moe_moe_decode_noalloc", "b200moe_decode_persistent_info",
+           "b200moe_decode_persistent_formats",
            "b200moe_stack_workspace_size",
            "b200moe_stack_decode",
            "b200moe_prefill_workspace_size", "b200moe_moe_prefill", "b200moe_moe_route",
@@ -80,6 +81,8 @@ def lib():
         L.b200moe_moe_decode_noalloc.argtypes = [vp, i32, i32, ctypes.POINTER(Layer), vp, vp, vp, vp]
         L.b200moe_decode_persistent_info.restype = i32
         L.b200moe_decode_persistent_info.argtypes = [ctypes.POINTER(i32), ctypes.POINTER(i32)]
+        L.b200moe_decode_persistent_formats.restype = i32
+        L.b200moe_decode_persistent_formats.argtypes = [ctypes.POINTER(i32)]
         L.b200moe_stack_workspace_size.restype = sz
         L.b200moe_stack_workspace_size.argtypes = [i32, i32]
         L.b200moe_stack_decode.restype = i32
@@ -182,6 +185,13 @@ def decode_persistent_info():
     a, c = ctypes.c_int(0), ctypes.c_int(0)
     _check("b200moe_decode_persistent_info", lib().b200moe_decode_persistent_info(ctypes.byref(a), ctypes.byref(c)))
     return a.value, c.value
+
+
+def decode_persistent_formats() -> bool:
+    """Whether single-token layers in the other block formats also run on the persistent kernel."""
+    f = ctypes.c_int(0)
+    _check("b200moe_decode_persistent_formats", lib().b200moe_decode_persistent_formats(ctypes.byref(f)))
+    return bool(f.value)
 
 
 def moe_decode_noalloc(x, x_dtype: int, T: int, layer: Layer, out, ids_out, w_out, stream=None):

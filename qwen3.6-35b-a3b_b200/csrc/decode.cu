@@ -584,7 +584,7 @@ int b200moe_moe_decode(const void *x, int x_dtype, int T, const b200moe_layer *l
   if (rc) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   const DecodeWS w = carve(ws, T);
-  if (T == 1 && layer_all_q4k(layer) && b2mega::usable())
+  if (T == 1 && b2mega::usable(!layer_all_q4k(layer)))
     return run_persistent(x, x_dtype, nullptr, 0.f, 1, layer, out, ids_out, w_out, w, s);
   return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, w, s, true);
 }
@@ -605,11 +605,17 @@ int b200moe_moe_decode_noalloc(const void *x, int x_dtype, int T, const b200moe_
   void *scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc) return rc;
-  if (T == 1 && layer_all_q4k(layer) && b2mega::usable())
+  if (T == 1 && b2mega::usable(!layer_all_q4k(layer)))
     return run_persistent(x, x_dtype, nullptr, 0.f, 1, layer, out, ids_out, w_out, carve(scratch, T),
                           (cudaStream_t)stream);
   return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, carve(scratch, T), (cudaStream_t)stream,
                    true);
+}
+
+int b200moe_decode_persistent_formats(int *formats) {
+  if (!formats) return b2host::set_error(B200MOE_EINVAL, "decode_persistent_formats: NULL pointer");
+  *formats = b2mega::usable(true) ? 1 : 0;
+  return B200MOE_OK;
 }
 
 int b200moe_decode_persistent_info(int *ctas, int *cluster) {
@@ -631,7 +637,7 @@ int b200moe_stack_decode(float *resid, int T, const b200moe_layer *layers, int n
   if (!al16(resid) || !al16(ws)) return b2host::set_error(B200MOE_EINVAL, "stack_decode: pointers must be 16-byte aligned");
   if (ws_bytes < decode_ws_bytes(T))
     return b2host::set_error(B200MOE_ESIZE, "stack_decode: workspace %zu B < required %zu B", ws_bytes, decode_ws_bytes(T));
-  bool q4 = true;  // every layer Q4_K throughout: the persistent kernel takes the stack
+  bool q4 = true;  // every layer Q4_K throughout (else the persistent kernel's format variant)
   for (int l = 0; l < n_layers; ++l) {
     int rc = check_layer(&layers[l], "stack_decode");
     if (rc) return rc;
@@ -639,7 +645,7 @@ int b200moe_stack_decode(float *resid, int T, const b200moe_layer *layers, int n
   }
   cudaStream_t s = (cudaStream_t)stream;
   const DecodeWS w = carve(ws, T);
-  if (T == 1 && q4 && b2mega::usable())
+  if (T == 1 && b2mega::usable(!q4))
     return run_persistent(nullptr, B200MOE_F32, resid, eps, n_layers, layers, nullptr, ids_out, nullptr, w, s);
   for (int l = 0; l < n_layers; ++l) {
     int rc = run_layer(nullptr, B200MOE_F32, resid, eps, T, &layers[l], nullptr,

@@ -31,18 +31,39 @@ __host__ __device__ constexpr int64_t row_bytes(int t, int n) {
 }
 
 // The layer's block types with 0 read as Q4_K.
-inline int layer_down_type(const b200moe_layer *L) { return L->down_type ? L->down_type : B200MOE_TYPE_Q4_K; }
-inline int layer_sh_type(const b200moe_layer *L) { return L->sh_type ? L->sh_type : B200MOE_TYPE_Q4_K; }
-inline bool layer_all_q4k(const b200moe_layer *L) {
+__host__ __device__ inline int layer_down_type(const b200moe_layer *L) {
+  return L->down_type ? L->down_type : B200MOE_TYPE_Q4_K;
+}
+__host__ __device__ inline int layer_sh_type(const b200moe_layer *L) {
+  return L->sh_type ? L->sh_type : B200MOE_TYPE_Q4_K;
+}
+__host__ __device__ inline bool layer_all_q4k(const b200moe_layer *L) {
   return layer_down_type(L) == B200MOE_TYPE_Q4_K && layer_sh_type(L) == B200MOE_TYPE_Q4_K;
 }
 
-// 16 bytes from a 2-byte aligned address (eight 16-bit read-only loads).
+// Load policies: global memory (read-only, streamed: weights are read once per token) and
+// shared memory (rows a kernel staged there). The arithmetic does not depend on the policy.
+struct LdGlobal {
+  static __device__ __forceinline__ uint4 v16(const uint8_t *p) { return ldg_stream(p); }
+  static __device__ __forceinline__ uint32_t u16(const uint8_t *p) {
+    return __ldg(reinterpret_cast<const unsigned short *>(p));
+  }
+  static __device__ __forceinline__ uint32_t u8(const uint8_t *p) { return __ldg(p); }
+};
+struct LdShared {
+  static __device__ __forceinline__ uint4 v16(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+  static __device__ __forceinline__ uint32_t u16(const uint8_t *p) {
+    return *reinterpret_cast<const unsigned short *>(p);
+  }
+  static __device__ __forceinline__ uint32_t u8(const uint8_t *p) { return *p; }
+};
+
+// 16 bytes from a 2-byte aligned address (eight 16-bit loads).
+template <typename Ld>
 __device__ __forceinline__ uint4 ld16_a2(const uint8_t *p) {
-  const unsigned short *q = reinterpret_cast<const unsigned short *>(p);
   uint32_t w[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) w[i] = (uint32_t)__ldg(q + 2 * i) | ((uint32_t)__ldg(q + 2 * i + 1) << 16);
+  for (int i = 0; i < 4; ++i) w[i] = Ld::u16(p + 4 * i) | (Ld::u16(p + 4 * i + 2) << 16);
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
@@ -52,11 +73,12 @@ __device__ __forceinline__ uint32_t byte_of(const uint4 &v, int i) {  // byte i 
 }
 
 // Q5_K: block kb of the row at `row` (16-byte aligned).
+template <typename Ld = LdGlobal>
 __device__ __forceinline__ float q5k_chunk_dot(const uint8_t *row, int kb, int c, const XChunk &x) {
   const uint8_t *blk = row + (size_t)kb * 176;
-  const uint4 h = ldg_stream(blk);
-  const uint4 qh = ldg_stream(blk + 16 + 16 * (c & 1));
-  const uint4 qs = ldg_stream(blk + 48 + 16 * c);
+  const uint4 h = Ld::v16(blk);
+  const uint4 qh = Ld::v16(blk + 16 + 16 * (c & 1));
+  const uint4 qs = Ld::v16(blk + 48 + 16 * c);
   float s0, m0, s1, m1;
   q4k_scales(h, c, s0, m0, s1, m1);  // sub-blocks 2g and 2g+1, g = c >> 1 (the Q4_K scale packing)
   const int j0 = 2 * (c >> 1);
@@ -73,15 +95,16 @@ __device__ __forceinline__ float q5k_chunk_dot(const uint8_t *row, int kb, int c
 }
 
 // Q6_K: block kb of the row at `row` (2-byte aligned).
+template <typename Ld = LdGlobal>
 __device__ __forceinline__ float q6k_chunk_dot(const uint8_t *row, int kb, int c, const XChunk &x) {
   const uint8_t *blk = row + (size_t)kb * 210;
   const int g = c >> 1, G = g >> 1, l0 = 16 * (c & 1), sh = 4 * (g & 1);
-  const uint4 qlo = ld16_a2(blk + 64 * G + l0);       // k = 2(g&1): ql[64G + l], nibble g&1
-  const uint4 qhi = ld16_a2(blk + 64 * G + 32 + l0);  // k = 2(g&1)+1: ql[64G + 32 + l]
-  const uint4 qh = ld16_a2(blk + 128 + 32 * G + l0);  // bits 2k, 2k+1 of qh[32G + l]
-  const float d = f16f(__ldg(reinterpret_cast<const unsigned short *>(blk + 208)));
-  const float s_lo = d * (float)(int8_t)__ldg(blk + 192 + 4 * g + (c & 1));      // sc[e >> 4], exact
-  const float s_hi = d * (float)(int8_t)__ldg(blk + 192 + 4 * g + 2 + (c & 1));
+  const uint4 qlo = ld16_a2<Ld>(blk + 64 * G + l0);       // k = 2(g&1): ql[64G + l], nibble g&1
+  const uint4 qhi = ld16_a2<Ld>(blk + 64 * G + 32 + l0);  // k = 2(g&1)+1: ql[64G + 32 + l]
+  const uint4 qh = ld16_a2<Ld>(blk + 128 + 32 * G + l0);  // bits 2k, 2k+1 of qh[32G + l]
+  const float d = f16f(Ld::u16(blk + 208));
+  const float s_lo = d * (float)(int8_t)Ld::u8(blk + 192 + 4 * g + (c & 1));  // sc[e >> 4], exact
+  const float s_hi = d * (float)(int8_t)Ld::u8(blk + 192 + 4 * g + 2 + (c & 1));
   float al = 0.f, ah = 0.f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
@@ -96,12 +119,12 @@ __device__ __forceinline__ float q6k_chunk_dot(const uint8_t *row, int kb, int c
 
 // Q8_0: the chunk's lo run is positions l0..l0+15 of block 8kb + 2g, its hi run the same
 // positions of the next block (row 2-byte aligned).
+template <typename Ld = LdGlobal>
 __device__ __forceinline__ float q80_chunk_dot(const uint8_t *row, int kb, int c, const XChunk &x) {
   const int b0 = 8 * kb + 2 * (c >> 1), l0 = 16 * (c & 1);
   const uint8_t *p0 = row + (size_t)b0 * 34, *p1 = p0 + 34;
-  const float d0 = f16f(__ldg(reinterpret_cast<const unsigned short *>(p0)));
-  const float d1 = f16f(__ldg(reinterpret_cast<const unsigned short *>(p1)));
-  const uint4 q0 = ld16_a2(p0 + 2 + l0), q1 = ld16_a2(p1 + 2 + l0);
+  const float d0 = f16f(Ld::u16(p0)), d1 = f16f(Ld::u16(p1));
+  const uint4 q0 = ld16_a2<Ld>(p0 + 2 + l0), q1 = ld16_a2<Ld>(p1 + 2 + l0);
   float al = 0.f, ah = 0.f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
@@ -111,16 +134,29 @@ __device__ __forceinline__ float q80_chunk_dot(const uint8_t *row, int kb, int c
   return fmaf(d0, al, d1 * ah);
 }
 
+// Q4_K through a load policy (the same arithmetic as q4k_chunk_dot on registers).
+template <typename Ld = LdGlobal>
+__device__ __forceinline__ float q4k_row_chunk_dot(const uint8_t *row, int kb, int c, const XChunk &x) {
+  const uint4 h = Ld::v16(row + (size_t)kb * kQB), q = Ld::v16(row + (size_t)kb * kQB + 16 + 16 * c);
+  return q4k_chunk_dot(h, q, c, x);
+}
+
+// Chunk (kb, c) of a row in a block type known only at run time (warp-uniform).
+template <typename Ld>
+__device__ __forceinline__ float any_chunk_dot(int type, const uint8_t *row, int kb, int c, const XChunk &x) {
+  if (type == B200MOE_TYPE_Q5_K) return q5k_chunk_dot<Ld>(row, kb, c, x);
+  if (type == B200MOE_TYPE_Q6_K) return q6k_chunk_dot<Ld>(row, kb, c, x);
+  if (type == B200MOE_TYPE_Q8_0) return q80_chunk_dot<Ld>(row, kb, c, x);
+  return q4k_row_chunk_dot<Ld>(row, kb, c, x);
+}
+
 // Chunk (kb, c) of a row stored in block type kT (B200MOE_TYPE_*), loads included.
 template <int kT>
 __device__ __forceinline__ float row_chunk_dot(const uint8_t *row, int kb, int c, const XChunk &x) {
   if constexpr (kT == B200MOE_TYPE_Q5_K) return q5k_chunk_dot(row, kb, c, x);
   else if constexpr (kT == B200MOE_TYPE_Q6_K) return q6k_chunk_dot(row, kb, c, x);
   else if constexpr (kT == B200MOE_TYPE_Q8_0) return q80_chunk_dot(row, kb, c, x);
-  else {
-    const uint4 h = ldg_stream(row + (size_t)kb * kQB), q = ldg_stream(row + (size_t)kb * kQB + 16 + 16 * c);
-    return q4k_chunk_dot(h, q, c, x);
-  }
+  else return q4k_row_chunk_dot(row, kb, c, x);
 }
 
 }  // namespace b2

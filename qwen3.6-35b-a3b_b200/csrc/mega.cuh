@@ -37,8 +37,9 @@ struct Args {
   const b200moe_layer *layers;  // host array of n_layers
 };
 
-// 1 if the current device can run the persistent kernel (128 CTAs resident at once).
-bool usable();
+// 1 if the current device can run the persistent kernel (128 CTAs resident at once); with
+// `formats`, also its variant for layers in other block formats (Q5_K / Q6_K down, Q8_0 shared).
+bool usable(bool formats = false);
 
 // Cluster size the launches use on the current device (1: cooperative launch; 0: unusable).
 int cluster_ctas();

@@ -48,6 +48,7 @@
 // per-lane Q4_K chunk dots, warp sums, SiLU, combine order, residual add) is the same sequence
 // of operations as the three-kernel path in decode.cu, so both paths give identical bits.
 #include "common.cuh"
+#include "kq_dot.cuh"
 #include "mega.cuh"
 #include "route.cuh"
 #include "tc.cuh"
@@ -92,27 +93,43 @@ struct MegaParams {
   b200moe_layer L[kMaxLayers];
 };
 
-// dynamic shared memory layout (bytes). Two instantiations of the kernel: kGen (some layer has
-// f32 router rows or an RMSNorm weight) with 8 KB router slots, and the bf16 / unweighted one
-// with 4 KB slots, whose code has neither the dtype nor the weight branches.
+// dynamic shared memory layout (bytes). Three instantiations of the kernel (kMode):
+//   0  bf16 router rows, no RMSNorm weight, Q4_K throughout: 4 KB router slots, none of the
+//      branches below;
+//   1  f32 router rows or an RMSNorm weight (kGen): 8 KB router slots;
+//   2  kGen plus layers in the published file's other block formats (down Q5_K / Q6_K, shared
+//      expert Q8_0; per layer at run time): the down slots sized for Q6_K rows, a separate
+//      region for the shared gate / up rows at the Q8_0 width, and single-buffered router rows
+//      (layer l+1's are issued once layer l's router has read them) to stay within 227 KB.
 constexpr int kOffRes = 0;                                   // [kResPad] f32 residual (or x)
 constexpr int kOffS = kOffRes + kResPad * 4;                 // [4096] f32 routed s, flat (slot, j)
 constexpr int kOffSsh = kOffS + kK * kI * 4;                 // [512] f32 shared-expert s
 constexpr int kOffDl = kOffSsh + kI * 4;                     // [2048] f32 gathered deltas
 constexpr int kOffLg = kOffDl + kH * 4;                      // [128] u32 gathered logit pairs
 constexpr int kOffRt = kOffLg + kN * 4;                      // [2 layers][3 rows][slot] router rows
-template <bool kGen>
+template <int kMode>
 struct Lay {
-  static constexpr int kRouterSlot = kGen ? kH * 4 : kH * 2;              // bytes per router row slot
-  static constexpr int kOffGu = kOffRt + 2 * kRtRows * kRouterSlot;       // [36] gate rows, then [36] up rows
-  static constexpr int kOffDn = kOffGu + (kQ + kJ) * kRowPair;            // [9][16] down rows
-  static constexpr int kOffO = kOffDn + (kK + 1) * kHr * kRowDown;        // [9][16] f32 down outputs
+  static constexpr bool kFmt = kMode == 2;
+  static constexpr int kRouterSlot = kMode >= 1 ? kH * 4 : kH * 2;       // bytes per router row slot
+  static constexpr int kRouterBufs = kFmt ? 1 : 2;
+  static constexpr int kOffGu = kOffRt + kRouterBufs * kRtRows * kRouterSlot;  // [36] gate rows, then [36] up rows
+  static constexpr int kShRow = (int)row_bytes(B200MOE_TYPE_Q8_0, kH);   // mode 2: shared gate / up row slot
+  static constexpr int kOffShGu = kOffGu + (kQ + kJ) * kRowPair;         // mode 2: [4] gate rows, then [4] up rows
+  static constexpr int kOffDn = kOffShGu + (kFmt ? 2 * kJ * kShRow : 0);  // [8] routed down slots of 16 rows
+  static constexpr int kDnSlot = kHr * (kFmt ? (int)row_bytes(B200MOE_TYPE_Q6_K, kI) : kRowDown);
+  static constexpr int kOffDnSh = kOffDn + kK * kDnSlot;                  // the shared expert's 16 down rows
+  static constexpr int kOffO = kOffDnSh + kHr * (kFmt ? (int)row_bytes(B200MOE_TYPE_Q8_0, kI) : kRowDown);
   static constexpr int kOffRr = kOffO + (kK + 1) * kHr * 4;               // Route
   static constexpr int kOffMisc = kOffRr + 128;                           // [3] router row results, [36] s out
   static constexpr int kOffScr = kOffMisc + 256;                          // [12][32] f32 per-warp scratch
   static constexpr int kOffBar = kOffScr + 12 * 32 * 4;                   // mbarriers
   static constexpr int kSmem = kOffBar + 256;
 };
+static_assert(Lay<0>::kOffDnSh == Lay<0>::kOffDn + 8 * kHr * kRowDown && Lay<1>::kOffO == Lay<1>::kOffDnSh + kHr * kRowDown,
+              "modes 0 / 1: the [9][16] down rows of one array");
+static_assert(Lay<2>::kSmem <= 232448 && Lay<1>::kSmem <= 232448, "227 KB of shared memory per CTA");
+static_assert(Lay<2>::kOffShGu % 128 == 0 && Lay<2>::kOffDn % 128 == 0 && Lay<2>::kOffDnSh % 128 == 0,
+              "bulk-copy destinations");
 
 // ---------------------------------------------------------------- device helpers
 __device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t *p) {
@@ -403,9 +420,10 @@ __device__ __forceinline__ bool gather(const uint64_t *base, uint32_t tag, const
   return !__syncthreads_or(fail);
 }
 
-template <bool kGen>
+template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ MegaParams P) {
-  using SL = Lay<kGen>;
+  using SL = Lay<kMode>;
+  constexpr bool kGen = kMode >= 1, kFmt = kMode == 2;
   extern __shared__ __align__(128) uint8_t smem[];
   float *res_s = reinterpret_cast<float *>(smem + kOffRes);
   float *s_s = reinterpret_cast<float *>(smem + kOffS);
@@ -415,7 +433,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
   uint8_t *rt = smem + kOffRt;
   uint8_t *gu_g = smem + SL::kOffGu;                  // [32 routed + 4 shared] gate rows
   uint8_t *gu_u = gu_g + (kQ + kJ) * kRowUp;      // the matching up rows
-  uint8_t *dn = smem + SL::kOffDn;                    // [9][16] down rows
+  uint8_t *dn = smem + SL::kOffDn;                    // [8][16] routed down rows
+  uint8_t *dn_sh = smem + SL::kOffDnSh;               // the shared expert's 16 down rows
+  uint8_t *shg = smem + SL::kOffShGu, *shu = shg + kJ * SL::kShRow;  // mode 2: shared gate / up rows
   float *o_s = reinterpret_cast<float *>(smem + SL::kOffO);
   Route *rr = reinterpret_cast<Route *>(smem + SL::kOffRr);
   uint32_t *row_out = reinterpret_cast<uint32_t *>(smem + SL::kOffMisc);  // [3] router row results
@@ -438,27 +458,41 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
 #pragma unroll
   for (int b = 0; b < kNumBars; ++b) ph[b] = 0;
 
-  auto issue_router_rows = [&](int l) {  // thread 0: layer l's 2 router rows + gate row -> rt[l & 1]
-    uint64_t *b = bar + kBarRt0 + (l & 1);
+  // the router-row buffer of layer l (mode 2: one buffer)
+  auto rt_buf = [&](int l) -> int { return kFmt ? 0 : (l & 1); };
+  // layer l's block types (modes 0 / 1: Q4_K)
+  auto down_t = [&](int l) -> int { return kFmt ? layer_down_type(&P.L[l]) : B200MOE_TYPE_Q4_K; };
+  auto sh_t = [&](int l) -> int { return kFmt ? layer_sh_type(&P.L[l]) : B200MOE_TYPE_Q4_K; };
+  auto issue_router_rows = [&](int l) {  // thread 0: layer l's 2 router rows + gate row -> its buffer
+    uint64_t *b = bar + kBarRt0 + rt_buf(l);
     // bytes of one row as stored; the rows sit at that pitch, the CTA's two router rows one copy
     const uint32_t rb = (kGen && P.L[l].router_f32) ? kH * 4 : kH * 2;
     mbar_expect_tx(b, kRtRows * rb);
-    uint8_t *d = rt + (size_t)(l & 1) * kRtRows * SL::kRouterSlot;
+    uint8_t *d = rt + (size_t)rt_buf(l) * kRtRows * SL::kRouterSlot;
     bulk_g2s(d, (const uint8_t *)P.L[l].router_w + (size_t)(2 * c) * rb, 2 * rb, b, pol_normal);
     bulk_g2s(d + 2 * rb, P.L[l].sh_gate_w, rb, b, pol_normal);
-    armed |= 1u << (kBarRt0 + (l & 1));
+    armed |= 1u << (kBarRt0 + rt_buf(l));
   };
   auto issue_shared_gu = [&](int l) {  // thread 0: layer l's shared-expert gate/up rows, 2 copies
-    mbar_expect_tx(bar + kBarShGu, kJ * kRowPair);
-    const size_t off = (size_t)(kJ * c) * kRowUp;
-    bulk_g2s(gu_g + kQ * kRowUp, (const uint8_t *)P.L[l].sh_gate + off, kJ * kRowUp, bar + kBarShGu, pol_normal);
-    bulk_g2s(gu_u + kQ * kRowUp, (const uint8_t *)P.L[l].sh_up + off, kJ * kRowUp, bar + kBarShGu, pol_normal);
+    if constexpr (kFmt) {
+      const uint32_t rg = (uint32_t)row_bytes(sh_t(l), kH);
+      mbar_expect_tx(bar + kBarShGu, 2 * kJ * rg);
+      const size_t off = (size_t)(kJ * c) * rg;
+      bulk_g2s(shg, (const uint8_t *)P.L[l].sh_gate + off, kJ * rg, bar + kBarShGu, pol_normal);
+      bulk_g2s(shu, (const uint8_t *)P.L[l].sh_up + off, kJ * rg, bar + kBarShGu, pol_normal);
+    } else {
+      mbar_expect_tx(bar + kBarShGu, kJ * kRowPair);
+      const size_t off = (size_t)(kJ * c) * kRowUp;
+      bulk_g2s(gu_g + kQ * kRowUp, (const uint8_t *)P.L[l].sh_gate + off, kJ * kRowUp, bar + kBarShGu, pol_normal);
+      bulk_g2s(gu_u + kQ * kRowUp, (const uint8_t *)P.L[l].sh_up + off, kJ * kRowUp, bar + kBarShGu, pol_normal);
+    }
     armed |= 1u << kBarShGu;
   };
   auto issue_shared_dn = [&](int l) {  // thread 0: layer l's shared-expert down rows (slot 8), 1 copy
-    mbar_expect_tx(bar + kBarShDn, kHr * kRowDown);
-    bulk_g2s(dn + 8 * kHr * kRowDown, (const uint8_t *)P.L[l].sh_down + (size_t)(kHr * c) * kRowDown,
-             kHr * kRowDown, bar + kBarShDn, pol_normal);
+    const uint32_t rd = (uint32_t)row_bytes(sh_t(l), kI);
+    mbar_expect_tx(bar + kBarShDn, kHr * rd);
+    bulk_g2s(dn_sh, (const uint8_t *)P.L[l].sh_down + (size_t)(kHr * c) * rd, kHr * rd, bar + kBarShDn,
+             pol_normal);
     armed |= 1u << kBarShDn;
   };
   // bounded wait on copy barrier b's pending phase; flips this thread's parity only on success
@@ -530,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       }
       __syncthreads();
     }
-    if (tid == 0 && !last) issue_router_rows(l + 1);
+    if (!kFmt && tid == 0 && !last) issue_router_rows(l + 1);
     __syncwarp();
     // Every warp derives the RMSNorm scale itself (identical bits, no barrier): the router warps
     // now, the others at the start of phase G, where they would wait for rows anyway (so they do
@@ -551,12 +585,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, 2048.0f), P.eps)));
     };
     float rs = warp < kRtRows ? rms_scale() : 1.0f;
-    fail = !__all_sync(0xFFFFFFFFu, wait_bar(kBarRt0 + (l & 1)));  // every thread consumes the phase
+    fail = !__all_sync(0xFFFFFFFFu, wait_bar(kBarRt0 + rt_buf(l)));  // every thread consumes the phase
     if (!fail && warp < kRtRows) {  // warps 0, 1: logits 2c, 2c+1; warp 2: the gate
       const bool gate = warp == 2;
       const float bias = (!gate && Lp.logit_bias) ? Lp.logit_bias[2 * c + warp] : 0.0f;
       const bool wf32 = kGen && Lp.router_f32 != 0;
-      const uint32_t v = router_row<kGen>(rt + (size_t)(l & 1) * kRtRows * SL::kRouterSlot +
+      const uint32_t v = router_row<kGen>(rt + (size_t)rt_buf(l) * kRtRows * SL::kRouterSlot +
                                               (size_t)warp * (wf32 ? kH * 4 : kH * 2),
                                           wf32, res_s, rs, P.resid ? Lp.norm_w : nullptr, lane, gate, bias,
                                           warp_scr + 32 * warp);
@@ -564,6 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
     }
     if (__syncthreads_or(fail)) { aborted = true; break; }
     if (tid == 0) st_tagged(tl + (size_t)c * kSlotLogits, ep + 1, row_out[0] | (row_out[1] << 16));
+    if (kFmt && tid == 0 && !last) issue_router_rows(l + 1);  // the one buffer is read (barrier above)
     // ---------------------------------------------------------------- phase S
     if (!gather<kSlotLogits, 1>(tl, ep + 1, abort_word, C, r, bar + kBarXLg, ph[kBarXLg], sl_lg, 1,
                                 [&](int w, int, uint32_t v) { lg_s[w] = v; })) {
@@ -580,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       if (lane == 0) {
 #pragma unroll
         for (int g = 0; g < kGuChunks; ++g) mbar_expect_tx(bar + kBarGu0 + g, kGuChunk * kRowPair);
-        mbar_expect_tx(bar + kBarDn, kK * kHr * kRowDown);
+        mbar_expect_tx(bar + kBarDn, kK * kHr * (uint32_t)row_bytes(down_t(l), kI));
         armed |= (((1u << kGuChunks) - 1u) << kBarGu0) | (1u << kBarDn);
       }
       __syncwarp();
@@ -598,9 +633,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       }
       __syncwarp();
       if (lane >= 2 * kGuChunks && lane < 2 * kGuChunks + kK) {
-        const uint8_t *src =
-            (const uint8_t *)Lp.down + (size_t)e * Lp.down_expert_stride + (size_t)(kHr * c) * kRowDown;
-        bulk_g2s(dn + (size_t)k * kHr * kRowDown, src, kHr * kRowDown, bar + kBarDn, pol_first);
+        const uint32_t rd = (uint32_t)row_bytes(down_t(l), kI);  // down row bytes (kRowDown for Q4_K)
+        const uint8_t *src = (const uint8_t *)Lp.down + (size_t)e * Lp.down_expert_stride + (size_t)(kHr * c) * rd;
+        bulk_g2s(dn + (size_t)k * kHr * rd, src, kHr * rd, bar + kBarDn, pol_first);
       }
       __syncwarp();
       route_finish(rw, mine, rr);  // R2, R4, R5 while the rows stream in
@@ -642,6 +677,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
             rowp[p] = gu_g + (size_t)row * kRowUp;
           }
           float g[2], u[2];
+          if (kFmt && ia < kJ) {  // mode 2: shared pairs ia, ia + 1 (kJ is even: never mixed with routed)
+            const int st = sh_t(l);
+            const size_t rg = (size_t)row_bytes(st, kH);  // rows staged at their own pitch
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+              const uint8_t *rgp = shg + (size_t)(ia + p) * rg, *rup = shu + (size_t)(ia + p) * rg;
+              g[p] = any_chunk_dot<LdShared>(st, rgp, kb0, cc, X0) + any_chunk_dot<LdShared>(st, rgp, kb0 + 4, cc, X1);
+              u[p] = any_chunk_dot<LdShared>(st, rup, kb0, cc, X0) + any_chunk_dot<LdShared>(st, rup, kb0 + 4, cc, X1);
+            }
+          } else {
 #pragma unroll
           for (int m = 0; m < 2; ++m) {  // gate rows of both pairs, then their up rows
             uint4 hq[2][4];
@@ -659,6 +704,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
               if (m == 0) g[p] = v;
               else u[p] = v;
             }
+          }
           }
 #pragma unroll
           for (int p = 0; p < 2; ++p) {
@@ -708,10 +754,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
           const int hh = 2 * it + 8 * p + half;
-          const uint8_t *pp = dn + (size_t)(slot * kHr + hh) * kRowDown + kb * kQB;
-          const uint4 h4 = *reinterpret_cast<const uint4 *>(pp);
-          const uint4 q4 = *reinterpret_cast<const uint4 *>(pp + 16 + 16 * cc);
-          v[p] = q4k_chunk_dot(h4, q4, cc, X);
+          if constexpr (kFmt) {  // the layer's row formats, staged at their own pitch
+            const int t = slot < kK ? down_t(l) : sh_t(l);
+            const size_t rb = (size_t)row_bytes(t, kI);
+            const uint8_t *row = (slot < kK ? dn + (size_t)slot * kHr * rb : dn_sh) + (size_t)hh * rb;
+            v[p] = any_chunk_dot<LdShared>(t, row, kb, cc, X);
+          } else {
+            const uint8_t *pp = dn + (size_t)(slot * kHr + hh) * kRowDown + kb * kQB;
+            const uint4 h4 = *reinterpret_cast<const uint4 *>(pp);
+            const uint4 q4 = *reinterpret_cast<const uint4 *>(pp + 16 + 16 * cc);
+            v[p] = q4k_chunk_dot(h4, q4, cc, X);
+          }
         }
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
@@ -757,55 +810,74 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
 
 // ---------------------------------------------------------------- host side
 struct DevInfo {
-  bool init = false, ok = false;
+  bool init = false, ok = false, fmt_ok = false;  // fmt_ok: mode 2 is resident with the same C
   int C = 1;
 };
 
 DevInfo g_dev[64];
+
+// Whether all kN CTAs of k_mega<kMode> are resident at once with clusters of C (C = 1: one CTA
+// per SM, the cooperative launch's condition).
+template <int kMode>
+bool resident(int C) {
+  if (C == 1) {
+    int per_sm = 0;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega<kMode>, kThreads, Lay<kMode>::kSmem) ==
+               cudaSuccess &&
+           per_sm >= 1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kN);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = Lay<kMode>::kSmem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, k_mega<kMode>, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  return clusters * C >= kN;
+}
+
+template <int kMode>
+bool set_smem(int maxsm) {
+  return maxsm >= Lay<kMode>::kSmem &&
+         cudaFuncSetAttribute(k_mega<kMode>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay<kMode>::kSmem) ==
+             cudaSuccess;
+}
 
 bool prepare(int dev, DevInfo &d) {
   if (d.init) return d.ok;
   d.init = true;
   int sms = 0, maxsm = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < kN) return false;
-  constexpr int kSmem = Lay<true>::kSmem;  // the larger footprint decides residency for both
-  if (cudaDeviceGetAttribute(&maxsm, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || maxsm < kSmem)
-    return false;
-  if (cudaFuncSetAttribute(k_mega<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess ||
-      cudaFuncSetAttribute(k_mega<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay<false>::kSmem) !=
-          cudaSuccess)
-    return false;
-  // the largest cluster size whose 128 / C clusters are all resident at once
-  for (int C : {8, 4, 2}) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kN);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmem;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)C;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, k_mega<true>, &cfg) != cudaSuccess) {
-      (void)cudaGetLastError();
-      continue;
+  if (cudaDeviceGetAttribute(&maxsm, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return false;
+  if (!set_smem<0>(maxsm) || !set_smem<1>(maxsm)) return false;
+  // the largest cluster size whose 128 / C clusters are all resident at once (mode 1 has the
+  // larger footprint of modes 0 and 1), else a cooperative launch
+  int C = 0;
+  for (int c : {8, 4, 2})
+    if (resident<1>(c)) {
+      C = c;
+      break;
     }
-    if (clusters * C >= kN) {
-      d.C = C;
-      d.ok = true;
-      return true;
-    }
+  if (!C) {
+    int coop = 0;
+    if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess || !coop ||
+        !resident<1>(1))
+      return false;
+    C = 1;
   }
-  int coop = 0, per_sm = 0;
-  if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess || !coop) return false;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_mega<true>, kThreads, kSmem) != cudaSuccess ||
-      per_sm < 1)
-    return false;
-  d.C = 1;
+  d.C = C;
   d.ok = true;
+  d.fmt_ok = set_smem<2>(maxsm) && resident<2>(C);
+  (void)cudaGetLastError();
   return true;
 }
 
@@ -813,10 +885,10 @@ bool prepare(int dev, DevInfo &d) {
 
 namespace b2mega {
 
-bool usable() {
+bool usable(bool formats) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
-  return prepare(dev, g_dev[dev]);
+  return prepare(dev, g_dev[dev]) && (!formats || g_dev[dev].fmt_ok);
 }
 
 int cluster_ctas() {
@@ -843,16 +915,20 @@ int launch(const Args &a, cudaStream_t stream) {
     p.n_layers = nl;
     p.ids_out = a.ids_out ? a.ids_out + (size_t)l0 * kK : nullptr;
     p.w_out = a.w_out ? a.w_out + (size_t)l0 * kK : nullptr;
-    bool gen = false;  // f32 router rows or an applied RMSNorm weight somewhere in this launch
+    int mode = 0;  // 1: f32 router rows or an applied RMSNorm weight; 2: a layer not Q4_K throughout
     for (int l = 0; l < nl; ++l) {
       p.L[l] = a.layers[l0 + l];
-      gen |= p.L[l].router_f32 != 0 || (a.resid && p.L[l].norm_w);
+      if (!layer_all_q4k(&p.L[l])) mode = 2;
+      else if (mode == 0 && (p.L[l].router_f32 != 0 || (a.resid && p.L[l].norm_w))) mode = 1;
     }
+    if (mode == 2 && !d.fmt_ok)
+      return b2host::set_error(B200MOE_EINVAL, "persistent decode: device %d cannot host the block-format variant",
+                               dev);
     B2_CUDA(cudaMemsetAsync(a.scratch, 0, kScratchClear, stream));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kN);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = gen ? Lay<true>::kSmem : Lay<false>::kSmem;
+    cfg.dynamicSmemBytes = mode == 2 ? Lay<2>::kSmem : mode == 1 ? Lay<1>::kSmem : Lay<0>::kSmem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     if (d.C > 1) {  // clusters: every cluster co-scheduled; all 128 / C clusters fit at once
@@ -866,8 +942,9 @@ int launch(const Args &a, cudaStream_t stream) {
     }
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (gen) B2_CUDA(cudaLaunchKernelEx(&cfg, k_mega<true>, p));
-    else B2_CUDA(cudaLaunchKernelEx(&cfg, k_mega<false>, p));
+    if (mode == 2) B2_CUDA(cudaLaunchKernelEx(&cfg, k_mega<2>, p));
+    else if (mode == 1) B2_CUDA(cudaLaunchKernelEx(&cfg, k_mega<1>, p));
+    else B2_CUDA(cudaLaunchKernelEx(&cfg, k_mega<0>, p));
   }
   return B200MOE_OK;
 }

@@ -1,12 +1,14 @@
 """Layers in the published Q4_K_M file's block formats on the decode kernels: Q5_K / Q6_K expert
-down matrices and a Q8_0 shared expert (k_gateup<true>, k_down<Q5_K|Q6_K, Q8_0|Q4_K>).
+down matrices and a Q8_0 shared expert (k_gateup<true>, k_down<Q5_K|Q6_K, Q8_0|Q4_K>, and the
+persistent kernel's block-format variant k_mega<2>).
 
 Parity bar (as for the Q4_K decode path): routing ids bit-exact against the declared-order C
 restatement; the f32 block output against the f64 restatement of engine/m3_forward.py:430-476
 (fed the same ids, weights decoded by oracle/kquants.py, itself pinned to the reference's
 decoders) within rel-L2 1e-5 and max-abs / max|ref| 1e-5. A single token goes through the
-three-kernel path here (the persistent kernel takes Q4_K layers only), a stack through
-b200moe_stack_decode, and the grouped GEMMs refuse the layer."""
+persistent kernel's format variant, several through the three-kernel path, a stack through
+b200moe_stack_decode; the two decode paths agree bit for bit; the grouped GEMMs refuse the
+layer."""
 import numpy as np
 import pytest
 
@@ -89,8 +91,9 @@ def test_q6k_down(cuda, q6_q4, T):
 
 
 def test_stack_of_published_format_layers(cuda, q5_q8, q6_q4):
-    """Two such layers through moe_stack (T=1: three-kernel path) and moe_stack_prefill (its
-    decode fallback for these layers), teacher-forced against the oracle per layer."""
+    """Two such layers through moe_stack (T=1: the persistent kernel's format variant) and
+    moe_stack_prefill (its decode fallback for these layers), teacher-forced against the oracle
+    per layer."""
     import torch
     from oracle import moe as OM
     from oracle.bf16 import bf16_bits_to_f32
@@ -130,3 +133,48 @@ def test_device_dequant_matches_oracle_matrix(cuda, q5_q8):
     L, Lh = q5_q8
     for kind, e in (("down", 7), ("sh_gate", 0), ("sh_down", 0)):
         assert np.array_equal(L.dequant(kind, e).cpu().numpy(), Lh.matrix(kind, e)), kind
+
+
+def _published(layers, cuda):
+    """The same layers with what the published file also has: F32 router / shared-gate weights
+    and a post-attention RMSNorm weight."""
+    import torch
+    from b200moe.engine import DeviceLayer
+    rng = np.random.default_rng(7)
+    out = []
+    for L in layers:
+        nw = torch.from_numpy((1.0 + rng.normal(0, 0.05, 2048)).astype(np.float32)).to(cuda)
+        out.append(DeviceLayer(L.gate, L.up, L.down, L.sh_gate, L.sh_up, L.sh_down, L.router_w.float(),
+                               L.sh_gate_w.float(), norm_w=nw, down_type=L.down_type, sh_type=L.sh_type))
+    return out
+
+
+@pytest.mark.parametrize("published", [False, True])
+def test_persistent_variant_equals_three_kernel_path(cuda, q5_q8, q6_q4, published):
+    """At T = 1 the persistent kernel's block-format variant runs these layers (a plain Q4_K
+    layer included); at T = 2 the three-kernel path runs each token independently. Fed two
+    copies of the token, the two must agree bit for bit, ids included."""
+    import torch
+    from oracle.bf16 import bf16_bits_to_f32
+    from b200moe import _abi, moe, synth
+    from b200moe.engine import DeviceEngine, DeviceLayer
+    assert _abi.decode_persistent_info()[0] == 128 and _abi.decode_persistent_formats()
+    layers = [q5_q8[0], DeviceLayer.synthetic(11, 2, cuda), q6_q4[0]]
+    if published:
+        layers = _published(layers, cuda)
+    eng = DeviceEngine(layers)
+    x0 = torch.from_numpy(bf16_bits_to_f32(synth.tokens(11, 1, stream=60)).copy()).to(cuda)
+    a = x0.clone()
+    ids_a = torch.empty((3, 1, 8), dtype=torch.int32, device=cuda)
+    moe.moe_stack(a, eng, ids_out=ids_a)
+    b = x0.repeat(2, 1)
+    ids_b = torch.empty((3, 2, 8), dtype=torch.int32, device=cuda)
+    moe.moe_stack(b, eng, ids_out=ids_b)
+    torch.cuda.synchronize()
+    assert torch.isfinite(a).all()
+    assert torch.equal(a[0], b[0]) and torch.equal(b[0], b[1])
+    assert torch.equal(ids_a[:, 0], ids_b[:, 0])
+    xb = x0.to(torch.bfloat16)
+    o1, i1 = moe.moe_block(xb.reshape(1, 2048), layers[0])
+    o2, i2 = moe.moe_block(xb.repeat(2, 1), layers[0])
+    assert torch.equal(o1[0], o2[0]) and torch.equal(i1["ids"][0], i2["ids"][0])
