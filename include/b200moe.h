@@ -70,9 +70,10 @@ typedef struct b200moe_layer {
                                 B200MOE_TYPE_Q6_K. down_expert_stride >= 2048 rows x row bytes */
     int32_t sh_type;         /* block type of sh_gate / sh_up / sh_down: 0 or B200MOE_TYPE_Q4_K,
                                 B200MOE_TYPE_Q8_0. A layer with any type other than Q4_K runs on
-                                the gather-GEMV decode kernels only: the single-token persistent
-                                kernel and the grouped GEMMs (moe_prefill, moe_experts) take
-                                Q4_K, and the latter refuse such a layer (B200MOE_EINVAL) */
+                                the decode paths only (the single-token persistent kernel's
+                                format variant, or the gather-GEMV kernels): the grouped GEMMs
+                                (moe_prefill, moe_experts) take Q4_K and refuse such a layer
+                                (B200MOE_EINVAL) */
 } b200moe_layer;
 
 /* ABI version (B200MOE_ABI_VERSION) and the last error message on this thread. */

@@ -1,5 +1,7 @@
 // kq_dot.cuh -- chunk dot products for the other block formats of the published Q4_K_M file
-// (expert down Q5_K / Q6_K, shared expert Q8_0) on the gather-GEMV decode kernels.
+// (expert down Q5_K / Q6_K, shared expert Q8_0) on the decode kernels: straight from global
+// memory in the gather-GEMV kernels (LdGlobal), from rows staged in shared memory in the
+// persistent kernel (LdShared) -- the same arithmetic, so both paths give the same bits.
 //
 // Each function takes the same lane work as q4k_chunk_dot: chunk (kb, c) of a row, i.e. the 16
 // elements chunk_pos(kb, c) + i ("lo") and the 16 elements 32 later ("hi"), with their x values

@@ -46,7 +46,10 @@
 //
 // The arithmetic of every value (RMSNorm, R1 logits in the declared chunk order, R2..R5,
 // per-lane Q4_K chunk dots, warp sums, SiLU, combine order, residual add) is the same sequence
-// of operations as the three-kernel path in decode.cu, so both paths give identical bits.
+// of operations as the three-kernel path in decode.cu, so both paths give identical bits. Layers
+// in the published file's other block formats (Q5_K / Q6_K down, Q8_0 shared) run in the
+// kMode = 2 instantiation with kq_dot.cuh's chunk dots over the staged rows, likewise
+// bit-identical to the gather-GEMV kernels.
 #include "common.cuh"
 #include "kq_dot.cuh"
 #include "mega.cuh"
