@@ -1,7 +1,7 @@
 """Generate the golden fixtures under tests/golden/ by running the REFERENCE's own Python.
 
-Run in the build container only (it imports the reference from ``REF_ROOT``, default
-``/root/reference``, read-only); the GPU box never runs this. Outputs are small ``.npz``
+Run only where the reference checkout is present (it imports the reference from the directory
+``REF_ROOT`` names, read-only); the GPU box never runs this. Outputs are small ``.npz``
 files committed beside this script:
 
 * ``q4k_dequant.npz`` -- edge-case, hand-built and seeded-random Q4_K blocks decoded by the
