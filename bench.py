@@ -178,9 +178,25 @@ def physical_index(local_rank):
 
 
 # ---------------------------------------------------------------------------------- CPU arm
-def cpu_sample(args, seconds_hint=None, threads=None):
+def host_layer_of(L):
+    """The oracle's view of a device layer: its block bytes copied to the host, with their types,
+    router / shared-gate values and norm weight (for the published-layout sample)."""
+    from oracle import moe as OM
+    from b200moe.geometry import BLOCK_GEOM
+    src = {"gate": L.gate, "up": L.up, "down": L.down, "sh_gate": L.sh_gate, "sh_up": L.sh_up,
+           "sh_down": L.sh_down}
+    arr = {k: t.cpu().numpy().reshape(-1, BLOCK_GEOM[L.type_of(k)][0]) for k, t in src.items()}
+    f32 = lambda t: t.float().cpu().numpy()  # noqa: E731
+    return OM.HostLayer(lambda k, f, n: arr[k][f:f + n], f32(L.router_w), f32(L.sh_gate_w),
+                        types={k: L.type_of(k) for k in src},
+                        norm_w=None if L.norm_w is None else L.norm_w.cpu().numpy())
+
+
+def cpu_sample(args, seconds_hint=None, threads=None, eng=None):
     """Time the reference's CPU path (oracle port) on a bounded sample: one token through
-    ``args.ref_layers_per_step`` layers of the stack. Returns (sec_per_layer, sample, cores)."""
+    ``args.ref_layers_per_step`` layers of the stack (the Q4_K synthetic layers, or with
+    ``--formats published`` the device engine's own first layers copied to the host). Returns
+    (layers, x0, cores, n_layers)."""
     import numpy as np
     import torch
     from oracle import moe as OM
@@ -192,8 +208,12 @@ def cpu_sample(args, seconds_hint=None, threads=None):
     cores = threads or len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
     nl = max(1, args.ref_layers_per_step)
-    layers = [OM.CachedLayer(lambda k, f, n, l=l: q4k.synth_blocks(args.seed, stream_id(l, KIND_OF[k]), f, n),
-                             synth.router_w(args.seed, l), synth.shared_gate_w(args.seed, l)) for l in range(nl)]
+    if getattr(args, "formats", "q4k") == "published" and eng is not None:
+        layers = [host_layer_of(eng.layers[l]) for l in range(nl)]
+    else:
+        layers = [OM.CachedLayer(lambda k, f, n, l=l: q4k.synth_blocks(args.seed, stream_id(l, KIND_OF[k]), f, n),
+                                 synth.router_w(args.seed, l), synth.shared_gate_w(args.seed, l))
+                  for l in range(nl)]
     x0 = synth.bf16_bits_to_f32(synth.tokens(args.seed, args.batch, stream=0))
     OM.stack_port(x0, layers, cores)          # untimed pass: fills each layer's byte cache
     return layers, x0, cores, nl
@@ -434,7 +454,7 @@ def run_b200(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "stack_decode":
         from oracle import moe as OM
-        layers, x0, cores, nlp = cpu_sample(args)
+        layers, x0, cores, nlp = cpu_sample(args, eng=eng)
         ts = []
         for _ in range(3):
             t0 = time.perf_counter()
@@ -443,8 +463,10 @@ def run_b200(args):
         sec_tok = statistics.median(ts) * (args.layers / nlp)
         cpu = {"value": T / sec_tok, "unit": "tok/s", "cores": cores, "kind": "port",
                "sample": "1 token through %d of %d layers, median of 3, scaled x%g (torch-f32 port of "
-                         "engine/m3_forward.py moe_block + rmsnorm_a, per-hit-expert dequant timed)"
-                         % (nlp, args.layers, args.layers / nlp)}
+                         "engine/m3_forward.py moe_block + rmsnorm_a, per-hit-expert dequant timed%s)"
+                         % (nlp, args.layers, args.layers / nlp,
+                            "; the published layout's first layers: Q5_K down, Q8_0 shared, F32 router, "
+                            "norm weight" if args.formats == "published" else "")}
 
     # the committed ncu traffic is the Q4_K workload's (none recorded for the published layout)
     traffic = committed_traffic(args.workload) if args.formats == "q4k" else None

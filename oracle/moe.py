@@ -120,9 +120,11 @@ class HostLayer:
     blocks in their own sizes.
     """
 
-    def __init__(self, block_fn, wg, wsg, bias=None, types=None):
+    def __init__(self, block_fn, wg, wsg, bias=None, types=None, norm_w=None):
         self._block_fn = block_fn     # (kind, first_block, nblocks) -> uint8 [n, block bytes]
         self.types = dict(types or {})
+        # post-attention RMSNorm weight as stored (Form A: 1 + w), f32 [2048]; None = 1
+        self.norm_w = None if norm_w is None else np.asarray(norm_w, dtype=np.float32).reshape(H)
         keep = lambda a: np.asarray(a) if np.asarray(a).dtype == np.float32 else np.asarray(a, np.uint16)  # noqa
         self.wg = np.ascontiguousarray(keep(wg)).reshape(E, H)      # bf16 bits, or f32 values
         self.wsg = np.ascontiguousarray(keep(wsg)).reshape(H)
@@ -230,11 +232,13 @@ def compare(out: np.ndarray, ref: np.ndarray) -> dict:
     return dict(rel_l2=rel, max_abs=mx, max_abs_norm=mx / max(scale, 1e-300))
 
 
-def rmsnorm_port(x, eps: float = 1e-6):
-    """``engine/m3_forward.py:303-307`` rmsnorm_a with weight 1, torch f32 (the reference's CPU op)."""
+def rmsnorm_port(x, eps: float = 1e-6, w=None):
+    """``engine/m3_forward.py:303-307`` rmsnorm_a, torch f32 (the reference's CPU op); ``w`` the
+    stored weight (Form A: 1 + w) or None for weight 1."""
     import torch
     xf = torch.as_tensor(x).float()
-    return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return y if w is None else y * torch.as_tensor(w).float()
 
 
 def stack_port(resid, layers, threads: int | None = None, eps: float = 1e-6):
@@ -244,7 +248,7 @@ def stack_port(resid, layers, threads: int | None = None, eps: float = 1e-6):
     import torch
     x = torch.as_tensor(np.asarray(resid, dtype=np.float32)).reshape(-1, H).clone()
     for L in layers:
-        h = rmsnorm_port(x, eps)
+        h = rmsnorm_port(x, eps, getattr(L, "norm_w", None))
         out, _ = moe_block_port(h.numpy(), L, threads)
         x = x + torch.from_numpy(out)
     return x.numpy()
@@ -254,8 +258,8 @@ class CachedLayer(HostLayer):
     """A HostLayer whose expert bytes are pre-generated (so a timed run measures the
     reference's dequant + math, not the synthetic generator). ``prefetch(e)`` fills it."""
 
-    def __init__(self, block_fn, wg, wsg, bias=None):
-        super().__init__(self._serve, wg, wsg, bias)
+    def __init__(self, block_fn, wg, wsg, bias=None, types=None, norm_w=None):
+        super().__init__(self._serve, wg, wsg, bias, types, norm_w)
         self._gen = block_fn
         self._cache = {}
 
