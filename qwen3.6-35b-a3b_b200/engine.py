@@ -75,7 +75,7 @@ class DeviceLayer:
 
     @property
     def all_q4k(self) -> bool:
-        """Every expert and shared matrix is Q4_K (the persistent and grouped-GEMM paths)."""
+        """Every expert and shared matrix is Q4_K (the grouped-GEMM path takes only such layers)."""
         return self.down_type == "Q4_K" and self.sh_type == "Q4_K"
 
     # ------------------------------------------------------------------ construction

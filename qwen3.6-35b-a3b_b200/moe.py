@@ -173,7 +173,7 @@ def moe_stack_prefill(resid: torch.Tensor, E_: DeviceEngine, n_layers: int | Non
     """The config-4 sub-stack on the prefill path: per layer ``resid += moe(rmsnorm(resid))``
     through the tcgen05 grouped GEMMs. ``ids_out`` (optional) is [n_layers, T, 8] int32.
     Layers that are not Q4_K throughout go through the decode kernels (``b200moe_stack_decode``
-    of that one layer)."""
+    of that one layer, on ``ws`` when it is large enough: the prefill workspace is)."""
     if resid.dtype != torch.float32 or resid.shape[-1] != H:
         raise Refused("shape", "resid must be f32 [T, %d]" % H)
     n = len(E_.layers) if n_layers is None else int(n_layers)
@@ -181,13 +181,16 @@ def moe_stack_prefill(resid: torch.Tensor, E_: DeviceEngine, n_layers: int | Non
     T = r.shape[0]
     dev = E_.layers[0].device
     ws = ws if ws is not None else prefill_workspace(T, dev)
+    dws = None  # the decode fallback's workspace (stream-ordered after the previous layer's use of ws)
     for l in range(n):
         L = E_.layers[l]
         ids_l = None if ids_out is None else ids_out[l]
         if L.all_q4k:
             _abi.moe_prefill(None, _abi.F32, r, eps, T, L.abi(), None, ids_l, ws)
         else:
-            _abi.stack_decode(r, T, [L.abi()], eps, ids_l, workspace(T, dev))
+            if dws is None:
+                dws = ws if ws.numel() * ws.element_size() >= _abi.decode_workspace_size(T) else workspace(T, dev)
+            _abi.stack_decode(r, T, [L.abi()], eps, ids_l, dws)
     return resid
 
 
