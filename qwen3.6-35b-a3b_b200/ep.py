@@ -72,6 +72,10 @@ class ExpertParallelMoE:
             raise ValueError("256 experts do not split over %d ranks" % self.world)
         self.per = E // self.world
         self.e_lo, self.e_hi = self.rank * self.per, (self.rank + 1) * self.per
+        if experts_fn is None and not getattr(layer, "all_q4k", True):
+            # refused here, before any collective, on every rank alike (the grouped GEMMs take Q4_K)
+            raise ValueError("expert parallelism runs the grouped GEMMs, which take Q4_K layers; this layer "
+                             "has down %s, shared %s" % (layer.down_type, layer.sh_type))
         self.layer = layer
         self.device = device if device is not None else layer.device
         self._ws = {}

@@ -112,3 +112,14 @@ def test_ep_dispatch_combine_matches_single_process(tmp_path, world):
     # every rank's experts took part (the test would be vacuous otherwise)
     owners = np.unique(ids.numpy() // (256 // world))
     assert len(owners) == world
+
+
+def test_refuses_non_q4k_layer_before_any_collective():
+    """A layer in the published file's other block formats is refused at construction (every rank
+    alike, before a collective could leave the others waiting): the grouped GEMMs take Q4_K."""
+    import torch
+    from b200moe.ep import ExpertParallelMoE
+    from test_bench_accounting import _layer
+    with pytest.raises(ValueError, match="Q4_K"):
+        ExpertParallelMoE(_layer("Q5_K", "Q8_0"), device=torch.device("cpu"))
+    assert ExpertParallelMoE(_layer(), device=torch.device("cpu")).e_hi == 256
