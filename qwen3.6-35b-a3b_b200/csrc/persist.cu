@@ -109,7 +109,7 @@ constexpr int kOffS = kOffRes + kResPad * 4;                 // [4096] f32 route
 constexpr int kOffSsh = kOffS + kK * kI * 4;                 // [512] f32 shared-expert s
 constexpr int kOffDl = kOffSsh + kI * 4;                     // [2048] f32 gathered deltas
 constexpr int kOffLg = kOffDl + kH * 4;                      // [128] u32 gathered logit pairs
-constexpr int kOffRt = kOffLg + kN * 4;                      // [2 layers][3 rows][slot] router rows
+constexpr int kOffRt = kOffLg + kN * 4;                      // [kRouterBufs][3 rows][slot] router rows
 template <int kMode>
 struct Lay {
   static constexpr bool kFmt = kMode == 2;
