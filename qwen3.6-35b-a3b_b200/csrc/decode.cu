@@ -510,7 +510,7 @@ int run_persistent(const void *x, int x_dtype, float *resid, float eps, int n_la
 
 // ------------------------------------------------------------------------- no-allocation entry
 // Scratch for b200moe_moe_decode_noalloc: a fixed, file-scope device array sized for
-// B200MOE_NOALLOC_MAX_T tokens (about 425 KB; every GPU that loads this library holds it
+// B200MOE_NOALLOC_MAX_T tokens (about 505 KB; every GPU that loads this library holds it
 // until the process exits). Host code may not use the array's name as a device address, so
 // its address is looked up once per device with cudaGetSymbolAddress and cached.
 constexpr int kNoAllocMaxT = B200MOE_NOALLOC_MAX_T;
