@@ -63,3 +63,37 @@ def test_block_type_validation_without_device_work():
     rc = lib.b200moe_moe_prefill(C.c_void_p(a), _abi.BF16, None, C.c_float(1e-6), 16, C.byref(Lr), C.c_void_p(a),
                                  None, C.c_void_p(a), ws, None)
     assert rc == _abi.EINVAL and b"Q4_K" in lib.b200moe_last_error()
+
+
+def test_plain_c_host(tmp_path):
+    """A C99 program includes the header and links the library (static CUDA runtime, no other
+    CUDA dependency): version, argument refusals and the error message, no device work."""
+    import shutil
+    import subprocess
+    from b200moe import _abi
+    if not shutil.which("gcc"):
+        import pytest
+        pytest.skip("no C compiler")
+    src = tmp_path / "host.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include <string.h>
+#include "b200moe.h"
+int main(void) {
+  b200moe_layer L;
+  memset(&L, 0, sizeof L);
+  if (b200moe_abi_version() != B200MOE_ABI_VERSION) return 1;
+  if (b200moe_q4k_dequant(NULL, 5, NULL, B200MOE_F32, NULL) != B200MOE_EINVAL) return 2;
+  if (!strstr(b200moe_last_error(), "NULL")) return 3;
+  if (b200moe_moe_decode(NULL, B200MOE_BF16, 1, &L, NULL, NULL, NULL, NULL, 0, NULL) != B200MOE_EINVAL) return 4;
+  if (b200moe_decode_workspace_size(1) == 0 || b200moe_decode_workspace_size(0) != 0) return 5;
+  printf("ok %d\n", b200moe_abi_version());
+  return 0;
+}
+''')
+    lib_dir = os.path.dirname(_abi.LIB_PATH)
+    exe = tmp_path / "host"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"), str(src),
+                    "-L", lib_dir, "-lb200moe", "-Wl,-rpath," + lib_dir, "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0 and out.stdout.strip() == "ok %d" % _abi.abi_version(), (out.returncode, out.stdout)
