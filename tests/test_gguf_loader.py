@@ -11,8 +11,9 @@ import numpy as np
 import pytest
 
 H, I, E = 2048, 512, 256
-Q80, Q4K, Q5K, Q6K, F32, BF16 = 8, 12, 13, 14, 0, 30
-SIZES = {Q80: (32, 34), Q4K: (256, 144), Q5K: (256, 176), Q6K: (256, 210), F32: (1, 4), BF16: (1, 2)}
+Q80, Q4K, Q5K, Q6K, F32, F16, BF16 = 8, 12, 13, 14, 0, 1, 30
+SIZES = {Q80: (32, 34), Q4K: (256, 144), Q5K: (256, 176), Q6K: (256, 210), F32: (1, 4), F16: (1, 2),
+         BF16: (1, 2)}
 NAMES = {Q80: "Q8_0", Q4K: "Q4_K", Q5K: "Q5_K", Q6K: "Q6_K"}
 
 
@@ -21,12 +22,12 @@ def _s(x: str) -> bytes:
     return struct.pack("<Q", len(b)) + b
 
 
-def write_gguf(path, tensors, align=32, truncate=False):
+def write_gguf(path, tensors, align=32, truncate=False, version=3):
     """tensors: list of (name, dims (GGUF order), type, {offset_in_tensor: bytes})."""
     kv = [("general.architecture", 8, _s("qwen35moe")), ("general.alignment", 4, struct.pack("<I", align)),
           ("qwen35moe.expert_count", 4, struct.pack("<I", E)),
           ("tokenizer.ggml.tokens", 9, struct.pack("<IQ", 8, 2) + _s("a") + _s("b"))]
-    head = b"GGUF" + struct.pack("<IQQ", 3, len(tensors), len(kv))
+    head = b"GGUF" + struct.pack("<IQQ", version, len(tensors), len(kv))
     for k, t, v in kv:
         head += _s(k) + struct.pack("<I", t) + v
     offs, off = [], 0
@@ -65,6 +66,10 @@ def layer_tensors(l, down_type=Q4K, router_type=BF16, router_dims=(H, E), sh_typ
         from oracle.bf16 import f32_to_bf16_bits
         t.append((p + "ffn_gate_inp.weight", router_dims, BF16, {0: f32_to_bf16_bits(w).tobytes()}))
         t.append((p + "ffn_gate_inp_shexp.weight", (H, 1), BF16, {0: f32_to_bf16_bits(g).tobytes()}))
+    elif router_type == F16:
+        w, g = w.astype(np.float16).astype(np.float32), g.astype(np.float16).astype(np.float32)
+        t.append((p + "ffn_gate_inp.weight", router_dims, F16, {0: w.astype(np.float16).tobytes()}))
+        t.append((p + "ffn_gate_inp_shexp.weight", (H,), F16, {0: g.astype(np.float16).tobytes()}))
     else:
         t.append((p + "ffn_gate_inp.weight", router_dims, F32, {0: w.tobytes()}))
         t.append((p + "ffn_gate_inp_shexp.weight", (H,), F32, {0: g.tobytes()}))
@@ -184,3 +189,38 @@ def test_post_attention_norm_weight(tmp_path):
     with gguf.GgufFile(path) as gf:
         assert np.array_equal(gguf.layer_norm(gf, 2), w)
         assert gguf.layer_norm(gf, 5) is None
+
+
+@pytest.mark.parametrize("version,align", [(2, 32), (3, 64)])
+def test_f16_router_widened_exactly_v2_and_alignment(tmp_path, version, align):
+    """An F16 router / shared gate is widened to f32 exactly; a GGUF v2 header and a data
+    alignment other than 32 place every tensor where the writer put it."""
+    gguf = _mod()
+    t, w, g = layer_tensors(6, router_type=F16)
+    path = str(tmp_path / "f16.gguf")
+    data0 = write_gguf(path, t, align=align, version=version)
+    with gguf.GgufFile(path) as gf:
+        assert gf.version == version and gf.data_start == data0 and data0 % align == 0
+        blocks, router, shgate = gguf.layer_host(gf, 6)
+        assert router.dtype == np.float32 and np.array_equal(router, w) and np.array_equal(shgate, g)
+        assert bytes(blocks["down"][:16]) == b"D" * 16 and bytes(blocks["sh_down"][-16:]) == b"d" * 16
+        del blocks
+
+
+@pytest.mark.parametrize("typ", [BF16, F16])
+def test_norm_weight_other_types(tmp_path, typ):
+    """BF16 / F16 post-attention norm weights are widened to f32 exactly."""
+    gguf = _mod()
+    t, _, _ = layer_tensors(2)
+    w = (1.0 + np.random.default_rng(4).normal(0, 0.05, H)).astype(np.float32)
+    if typ == BF16:
+        from oracle.bf16 import bf16_bits_to_f32, f32_to_bf16_bits
+        raw, want = f32_to_bf16_bits(w).tobytes(), bf16_bits_to_f32(f32_to_bf16_bits(w))
+    else:
+        raw, want = w.astype(np.float16).tobytes(), w.astype(np.float16).astype(np.float32)
+    t.append(("blk.2.post_attention_norm.weight", (H,), typ, {0: raw}))
+    path = str(tmp_path / "n.gguf")
+    write_gguf(path, t)
+    with gguf.GgufFile(path) as gf:
+        got = gguf.layer_norm(gf, 2)
+        assert got.dtype == np.float32 and np.array_equal(got, want)
