@@ -140,3 +140,104 @@ def test_rank_order_accumulation_is_below_the_output_bars(case):
             rank[t] = rank[t] + raw[t, k] * w[t, k]
     c = OM.compare(rank, asc)
     assert 0 < c["rel_l2"] < DECODE_BAR, c
+
+
+# ---------------------------------------------------------------------------------------------
+# The three-arm discipline of the reference's self-test (speccheck/selftest_moe.py:8-28, its
+# injection -> affected-stage table :57-67): per injection, the stages it must change (caught)
+# and the stages that must stay bit-identical (kept).
+#   honest  -- every injection changes its caught stages and no kept stage;
+#   stub    -- with the difference predicate forced to "no difference", every catch is lost
+#              (the checks are not vacuous: they rest on the comparison);
+#   crossed -- a table that wrongly lists a changed stage as kept is flagged.
+STAGES = ("ids", "w", "expert_raw", "shared_raw", "shared_gate_prob", "routed", "out")
+
+
+def _stages(L, x, ids, w):
+    """Stage values of the block with routing (ids, w: the weights applied, f64)."""
+    from oracle.bf16 import f32_to_bf16_bits
+    d = OM.moe_block_f64(x, L, ids, f32_to_bf16_bits(np.asarray(w, np.float32)))
+    routed = np.einsum("tkh,tk->th", d["expert_raw"], np.asarray(w, np.float64))
+    return dict(ids=np.asarray(ids), w=np.asarray(w, np.float64), expert_raw=d["expert_raw"],
+                shared_raw=d["shared_raw"], shared_gate_prob=d["shared_gate_prob"], routed=routed,
+                out=routed + d["shared_out"])
+
+
+def _route_bf16_softmax(r):
+    """Top-8 and renormalisation over the softmax probabilities rounded to bf16."""
+    from oracle.bf16 import bf16_bits_to_f32 as b2f, f32_to_bf16_bits as f2b
+    pb = b2f(f2b(r["probs"])).astype(np.float64)
+    ids = np.stack([np.lexsort((np.arange(pb.shape[1]), -row))[:8] for row in pb]).astype(np.int32)
+    p = np.take_along_axis(pb, ids, 1)
+    return ids, b2f(f2b((p / p.sum(1, keepdims=True)).astype(np.float32)))
+
+
+ROUTED = {"expert_raw", "routed", "out"}
+WEIGHTS = {"w", "routed", "out"}
+
+
+def _table(L, r):
+    """name -> (layer, ids, w applied, caught stages, kept stages)."""
+    from oracle.bf16 import bf16_bits_to_f32 as b2f, f32_to_bf16_bits as f2b
+    ids, w = r["ids"], b2f(r["w_bf16"])
+    swap_routed = {"gate": "up", "up": "gate"}
+    swap_shared = {"sh_gate": "sh_up", "sh_up": "sh_gate"}
+    p_top = np.take_along_axis(r["probs"], r["ids"].astype(np.int64), 1)
+    sb_ids, sb_w = _route_bf16_softmax(r)
+    every = set(STAGES)
+    t = {
+        "wrong expert index": (_wrong_expert(L), ids, w, ROUTED),
+        "gate/up swap": (_planted(L, matrix_fn=lambda k, e, base: base(swap_routed.get(k, k), e)), ids, w, ROUTED),
+        "transposed expert stack": (_planted(L, matrix_fn=lambda k, e, base: (
+            lambda m: m.reshape(m.shape[1], m.shape[0]).T if k == "down" else m)(base(k, e))), ids, w, ROUTED),
+        "shared gate/up swap": (_planted(L, matrix_fn=lambda k, e, base: base(swap_shared.get(k, k), e)), ids, w,
+                                {"shared_raw", "out"}),
+        "renorm omitted": (L, ids, b2f(f2b(p_top)), WEIGHTS),
+        "cast after multiply": (L, ids, r["w_f32"], WEIGHTS),
+        "softmax in bf16": (L, sb_ids, sb_w, WEIGHTS),
+        "wrong sub-block scale": (_swap_subblock_scales(L), ids, w, ROUTED | {"shared_raw"}),
+        "dropped min": (_drop_min(L), ids, w, ROUTED | {"shared_raw"}),
+        "block off by one": (_block_off_by_one(L), ids, w, ROUTED | {"shared_raw"}),
+    }
+    kept_always = {"softmax in bf16": {"shared_raw", "shared_gate_prob"}}  # its ids may move with the ties
+    return {n: (Lp, i, ww, caught, kept_always.get(n, every - caught)) for n, (Lp, i, ww, caught) in t.items()}
+
+
+def _differs(a, b):
+    return not np.array_equal(np.asarray(a), np.asarray(b))
+
+
+@pytest.fixture(scope="module")
+def arms(case):
+    L, x, r, _ = case
+    from oracle.bf16 import bf16_bits_to_f32 as b2f
+    good = _stages(L, x, r["ids"], b2f(r["w_bf16"]))
+    runs = {n: (_stages(Lp, x, i, ww), caught, kept) for n, (Lp, i, ww, caught, kept) in _table(L, r).items()}
+    return good, runs
+
+
+def _verdict(good, bad, caught, kept, differs):
+    missed = [s for s in sorted(caught) if not differs(good[s], bad[s])]
+    breached = [s for s in sorted(kept) if differs(good[s], bad[s])]
+    return missed, breached
+
+
+def test_honest_arm(arms):
+    good, runs = arms
+    for name, (bad, caught, kept) in runs.items():
+        assert _verdict(good, bad, caught, kept, _differs) == ([], []), name
+
+
+def test_stub_arm_loses_every_catch(arms):
+    good, runs = arms
+    for name, (bad, caught, kept) in runs.items():
+        missed, breached = _verdict(good, bad, caught, kept, lambda a, b: False)
+        assert missed == sorted(caught) and breached == [], name
+
+
+def test_crossed_arm_flags_a_misdeclared_stage(arms):
+    good, runs = arms
+    for name, (bad, caught, kept) in runs.items():
+        stage = sorted(caught)[0]                      # declare one changed stage as kept
+        missed, breached = _verdict(good, bad, caught - {stage}, kept | {stage}, _differs)
+        assert missed == [] and breached == [stage], name
