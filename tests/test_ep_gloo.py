@@ -123,3 +123,52 @@ def test_refuses_non_q4k_layer_before_any_collective():
     with pytest.raises(ValueError, match="Q4_K"):
         ExpertParallelMoE(_layer("Q5_K", "Q8_0"), device=torch.device("cpu"))
     assert ExpertParallelMoE(_layer(), device=torch.device("cpu")).e_hi == 256
+
+
+def _worker_peer_lost(rank, world, port, path):
+    """Rank 1 leaves right after joining (between steps, with nothing in flight); rank 0 runs an
+    expert-parallel step, whose first collective must end with an error, not wait for good."""
+    import datetime
+    import json
+    import time
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(0)
+    from conftest import _load_pkg
+    _load_pkg()
+    from b200moe.ep import ExpertParallelMoE
+    route, experts = _stage_fns()
+    x = _tokens(world)[:T_PER_RANK]
+    ep = ExpertParallelMoE(layer=None, route_fn=route, experts_fn=experts, device=torch.device("cpu"))
+    t0 = time.monotonic()
+    try:
+        ep.forward(x)
+        res = dict(detected=False)
+    except Exception as e:  # the collective's error: the peer's connection closed, or the timeout
+        res = dict(detected=True, error=type(e).__name__, msg=str(e)[:200])
+    res["seconds"] = time.monotonic() - t0
+    with open(path, "w") as f:
+        json.dump(res, f)
+    os._exit(0)  # no teardown handshake with a peer that is gone
+
+
+def test_lost_rank_ends_the_collective_with_an_error(tmp_path):
+    import json
+    import time
+    import torch.multiprocessing as mp
+    path = str(tmp_path / "rank0.json")
+    ctx = mp.start_processes(_worker_peer_lost, args=(2, _free_port(), path), nprocs=2, start_method="spawn",
+                             join=False)
+    deadline = time.monotonic() + 120
+    try:
+        while not ctx.join(timeout=1):
+            assert time.monotonic() < deadline, "rank 0 did not finish: the lost peer was not detected"
+    finally:
+        for p in ctx.processes:  # only the processes this test started
+            if p.is_alive():
+                p.kill()
+    res = json.load(open(path))
+    assert res["detected"] and res["seconds"] < 60, res
