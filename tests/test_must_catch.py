@@ -124,9 +124,9 @@ def test_rank_order_accumulation_is_below_the_output_bars(case):
     """Summing the weighted expert outputs in rank order instead of ascending expert id changes
     an f32 combine only in its last bits -- below every output bar, so no output comparison
     pins the order. (The reference pins it through a bf16 accumulator, where the order shows.)
-    Recorded here so the limit of the output bars is explicit: the ascending order is the
-    declared order of every combine in the kernels, and a stage-level bit-exact check of it is
-    listed as next work."""
+    Recorded here so the limit of the output bars is explicit; the order itself is pinned bit
+    for bit at the stage level instead (tests/test_gpu_combine_order.py: routed_sum equals the
+    ascending-id fold and differs from the rank-order one)."""
     L, x, r, good = case
     exp = OM.moe_block_f64(x, L, r["ids"], r["w_bf16"])
     raw = exp["expert_raw"].astype(np.float32)
