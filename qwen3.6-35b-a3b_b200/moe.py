@@ -106,7 +106,8 @@ def moe_block(g: torch.Tensor, E_, layer: int = 0, probe_row=None, out: torch.Te
     ``path``: "decode" (gather-GEMV, f32 CUDA cores), "prefill" (token sort + tcgen05 grouped
     GEMMs, fp16 operands) or "auto" (prefill from ``PREFILL_MIN_TOKENS`` tokens on). A layer
     with Q5_K / Q6_K down or a Q8_0 shared expert (the published Q4_K_M file) runs on the
-    decode kernels at every token count; ``path="prefill"`` refuses it.
+    decode kernels at every token count; ``path="prefill"`` refuses it. No tokens give empty
+    results (as the reference's own loop does), with no device work.
     """
     if probe_row is not None:
         raise Refused("probe-row", "band-operand probes are a host-oracle feature; not on the device path")
@@ -121,7 +122,9 @@ def moe_block(g: torch.Tensor, E_, layer: int = 0, probe_row=None, out: torch.Te
     if path == "prefill" and not L.all_q4k:
         raise Refused("format", "the grouped GEMMs take Q4_K experts; this layer has down %s, shared %s"
                       % (L.down_type, L.sh_type))
-    if path == "prefill" or (path == "auto" and T >= PREFILL_MIN_TOKENS and L.all_q4k):
+    if T == 0:
+        pass
+    elif path == "prefill" or (path == "auto" and T >= PREFILL_MIN_TOKENS and L.all_q4k):
         _abi.moe_prefill(x, xd, None, RMS_EPS, T, L.abi(), out, ids, prefill_workspace(T, L.device))
     else:
         _abi.moe_decode(x, xd, T, L.abi(), out, ids, None, workspace(T, L.device))
@@ -139,7 +142,8 @@ def moe_router(g_row: torch.Tensor, E_, layer: int = 0) -> dict:
     ids = torch.empty((T, TOPK), dtype=torch.int32, device=dev)
     wf = torch.empty((T, TOPK), dtype=torch.float32, device=dev)
     wb = torch.empty((T, TOPK), dtype=torch.bfloat16, device=dev)
-    _abi.router(x, xd, T, L.router_w, L.logit_bias, logits, ids, wf, wb, workspace(T, dev))
+    if T:
+        _abi.router(x, xd, T, L.router_w, L.logit_bias, logits, ids, wf, wb, workspace(T, dev))
     return dict(router_logits=logits, topk_ids=ids, topk_weights=wb, topk_weights_f32=wf)
 
 
@@ -157,6 +161,8 @@ def moe_stack(resid: torch.Tensor, E_: DeviceEngine, n_layers: int | None = None
         raise Refused("layers", "%d layers requested, engine holds %d" % (n, len(E_.layers)))
     r = resid.reshape(-1, H)
     T = r.shape[0]
+    if T == 0:
+        return resid
     dev = E_.layers[0].device
     _abi.stack_decode(r, T, [L.abi() for L in E_.layers[:n]], eps, ids_out,
                       ws if ws is not None else workspace(T, dev))
@@ -179,6 +185,8 @@ def moe_stack_prefill(resid: torch.Tensor, E_: DeviceEngine, n_layers: int | Non
     n = len(E_.layers) if n_layers is None else int(n_layers)
     r = resid.reshape(-1, H)
     T = r.shape[0]
+    if T == 0:
+        return resid
     dev = E_.layers[0].device
     ws = ws if ws is not None else prefill_workspace(T, dev)
     dws = None  # the decode fallback's workspace (stream-ordered after the previous layer's use of ws)
@@ -204,13 +212,16 @@ def _stage_route(g_row, E_, layer):
     ids = torch.empty((T, TOPK), dtype=torch.int32, device=dev)
     wb = torch.empty((T, TOPK), dtype=torch.int16, device=dev)
     sg = torch.empty((T,), dtype=torch.float32, device=dev)
-    _abi.moe_route(x, xd, None, RMS_EPS, T, L.abi(), x16, ids, wb, sg, prefill_workspace(T, dev))
+    if T:
+        _abi.moe_route(x, xd, None, RMS_EPS, T, L.abi(), x16, ids, wb, sg, prefill_workspace(T, dev))
     return L, x16, ids, wb, sg
 
 
 def _stage_experts(L, x16, ids, wb, e_lo, e_hi, sg):
     T = x16.shape[0]
     out = torch.empty((T, H), dtype=torch.float32, device=L.device)
+    if T == 0:
+        return out
     _abi.moe_experts(x16, T, ids, wb, e_lo, e_hi, sg, L.abi(), out, False, prefill_workspace(T, L.device))
     return out
 

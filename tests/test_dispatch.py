@@ -75,3 +75,21 @@ def test_refusals_before_any_call(rec):
     with pytest.raises(moe.Refused):
         moe.moe_block(torch.zeros((2, 2048)), L, probe_row=0)
     assert rec == []
+
+
+def test_no_tokens_give_empty_results_without_device_work(rec):
+    """As the reference's loop does for B*T = 0: empty outputs in the input's leading shape."""
+    import torch
+    from b200moe import moe
+    from b200moe.engine import DeviceEngine
+    L = _layer()
+    out, info = moe.moe_block(torch.zeros((1, 0, 2048)), L)
+    assert tuple(out.shape) == (1, 0, 2048) and tuple(info["ids"].shape) == (1, 0, 8) and info["used"] == 0
+    r = moe.moe_router(torch.zeros((0, 2048)), L)
+    assert tuple(r["router_logits"].shape) == (0, 256) and tuple(r["topk_ids"].shape) == (0, 8)
+    resid = torch.zeros((0, 2048), dtype=torch.float32)
+    assert moe.moe_stack(resid, DeviceEngine([L])) is resid
+    assert moe.moe_stack_prefill(resid, DeviceEngine([L])) is resid
+    st = moe.moe_block_stages(torch.zeros((0, 2048)), L)
+    assert tuple(st["expert_raw"].shape) == (0, 8, 2048) and tuple(st["combined_out"].shape) == (0, 2048)
+    assert rec == []
