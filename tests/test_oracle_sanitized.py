@@ -70,5 +70,8 @@ def test_oracle_under_asan_ubsan(tmp_path):
         raise
     env = dict(os.environ, ASAN_OPTIONS="detect_leaks=1:abort_on_error=0", UBSAN_OPTIONS="print_stacktrace=1")
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300, env=env)
+    if "LeakSanitizer has encountered a fatal error" in r.stderr:  # no ptrace here: leaks unchecked
+        env["ASAN_OPTIONS"] = "detect_leaks=0:abort_on_error=0"
+        r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300, env=env)
     assert r.returncode == 0 and r.stdout.startswith("ok"), (r.returncode, r.stdout, r.stderr[-2000:])
     assert "runtime error" not in r.stderr and "ERROR: AddressSanitizer" not in r.stderr, r.stderr[-2000:]
