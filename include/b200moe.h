@@ -141,9 +141,31 @@ int b200moe_moe_decode(const void *x, int x_dtype, int T, const b200moe_layer *l
  * first call before any stream capture. All calls on a device share the one array: calls
  * that can overlap on the GPU (different streams without ordering) race on it and must be
  * serialised by the caller. Whatever must start at zero is cleared by each call itself.
+ * The looked-up address is cached per device ordinal for the life of the process and does not
+ * survive cudaDeviceReset (or any re-creation of the device's primary context): do not call
+ * this entry point after such a reset. b200moe_decode_noalloc_status reads its status word.
  * Allocates nothing (no cudaMalloc / cudaFree, no allocating library routine). */
 int b200moe_moe_decode_noalloc(const void *x, int x_dtype, int T, const b200moe_layer *layer,
                                float *out, int32_t *ids_out, uint16_t *w_out, void *stream);
+
+/* Decode status of the last b200moe_moe_decode / b200moe_stack_decode call made with
+ * workspace `ws` and T tokens (b200moe_decode_noalloc_status: of the last
+ * b200moe_moe_decode_noalloc call with T tokens), copied to *status; synchronises `stream`.
+ * 0 = complete. Bit 1 = a bounded wait of the single-token persistent kernel ran out (a
+ * cross-CTA exchange or a weight copy did not complete within its ~1 s budget, e.g. when other
+ * work kept some of its CTAs from being resident): that call's outputs are incomplete and must
+ * not be used; the three-kernel path (T >= 2) has no such waits and always leaves 0.
+ * The reference refuses such a state loudly (engine/m3_forward.py:165-170 Refused); this is the
+ * device path's stream-ordered equivalent, like b200moe_prefill_status. */
+int b200moe_decode_status(const void *ws, int T, int *status, void *stream);
+int b200moe_decode_noalloc_status(int T, int *status, void *stream);
+
+/* Test hook for the persistent decode kernel's failure path (no counterpart in the reference).
+ * Every later persistent launch in this process uses a wait budget of `wait_budget_cycles`
+ * clock cycles (0 = the default, ~1 s), and CTA `withhold_cta` (0..127; -1 = none) never
+ * publishes its first logit pair, so every other CTA's gather runs out of budget: the kernel
+ * then ends on every CTA with status bit 1 set and the device context intact. Reset with (0, -1). */
+int b200moe_debug_decode_faults(long long wait_budget_cycles, int withhold_cta);
 
 /* Which single-token decode path this device runs. At T = 1, b200moe_moe_decode,
  * b200moe_moe_decode_noalloc and b200moe_stack_decode run one persistent kernel per call

@@ -20,7 +20,8 @@ F32, BF16 = 0, 1
 EXPORTS = ("b200moe_abi_version", "b200moe_last_error", "b200moe_q4k_dequant", "b200moe_dequant",
            "b200moe_synth_q4k", "b200moe_router_workspace_size", "b200moe_router",
            "b200moe_decode_workspace_size",
-           "b200moe_moe_decode", "b200moe_moe_decode_noalloc", "b200moe_decode_persistent_info",
+           "b200moe_moe_decode", "b200moe_moe_decode_noalloc", "b200moe_decode_status",
+           "b200moe_decode_noalloc_status", "b200moe_debug_decode_faults", "b200moe_decode_persistent_info",
            "b200moe_decode_persistent_formats",
            "b200moe_stack_workspace_size",
            "b200moe_stack_decode",
@@ -79,6 +80,12 @@ def lib():
         L.b200moe_moe_decode.argtypes = [vp, i32, i32, ctypes.POINTER(Layer), vp, vp, vp, vp, sz, vp]
         L.b200moe_moe_decode_noalloc.restype = i32
         L.b200moe_moe_decode_noalloc.argtypes = [vp, i32, i32, ctypes.POINTER(Layer), vp, vp, vp, vp]
+        L.b200moe_decode_status.restype = i32
+        L.b200moe_decode_status.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_int), vp]
+        L.b200moe_decode_noalloc_status.restype = i32
+        L.b200moe_decode_noalloc_status.argtypes = [i32, ctypes.POINTER(ctypes.c_int), vp]
+        L.b200moe_debug_decode_faults.restype = i32
+        L.b200moe_debug_decode_faults.argtypes = [ctypes.c_longlong, i32]
         L.b200moe_decode_persistent_info.restype = i32
         L.b200moe_decode_persistent_info.argtypes = [ctypes.POINTER(i32), ctypes.POINTER(i32)]
         L.b200moe_decode_persistent_formats.restype = i32
@@ -199,6 +206,27 @@ def moe_decode_noalloc(x, x_dtype: int, T: int, layer: Layer, out, ids_out, w_ou
     _check("b200moe_moe_decode_noalloc",
            lib().b200moe_moe_decode_noalloc(ptr(x), x_dtype, T, ctypes.byref(layer), ptr(out), ptr(ids_out),
                                             ptr(w_out), _stream(stream)))
+
+
+def decode_status(ws, T: int, stream=None) -> int:
+    """Status word of the last decode call on workspace ``ws`` with T tokens (0 = complete)."""
+    st = ctypes.c_int(-1)
+    _check("b200moe_decode_status", lib().b200moe_decode_status(ptr(ws), T, ctypes.byref(st), _stream(stream)))
+    return int(st.value)
+
+
+def decode_noalloc_status(T: int, stream=None) -> int:
+    """Status word of the last ``b200moe_moe_decode_noalloc`` call with T tokens (0 = complete)."""
+    st = ctypes.c_int(-1)
+    _check("b200moe_decode_noalloc_status", lib().b200moe_decode_noalloc_status(T, ctypes.byref(st),
+                                                                                 _stream(stream)))
+    return int(st.value)
+
+
+def debug_decode_faults(wait_budget_cycles: int = 0, withhold_cta: int = -1):
+    """Test hook of the persistent decode kernel's failure path (reset with the defaults)."""
+    _check("b200moe_debug_decode_faults", lib().b200moe_debug_decode_faults(int(wait_budget_cycles),
+                                                                             int(withhold_cta)))
 
 
 def stack_workspace_size(T: int, n_layers: int) -> int:

@@ -47,6 +47,7 @@ struct K1Params {
   float *xw;             // [T][2048] f32 copy of x for K2 (or NULL)
   uint16_t *logits;      // [T][256]
   float *sg;             // [T]
+  uint32_t *status;      // decode status word to clear (the call's first router launch), or NULL
 };
 
 // R1's declared order for one value: lane L holds chunk L's sequential sum; the 32 chunk
@@ -138,6 +139,7 @@ __global__ void __launch_bounds__(128) k_router(K1Params P) {
   const float bias = (!gate_cta && P.bias) ? P.bias[e] : 0.0f;
   pdl_wait();
   pdl_trigger();
+  if (P.status && blockIdx.x == 0 && threadIdx.x == 0) *P.status = 0u;  // no bounded waits on this path
   for (int t = 0; t < P.T; ++t) {
     float v[64];
     load_x_slice(P, t, lane, v);
@@ -395,6 +397,22 @@ DecodeWS carve(void *ws, int T) {
 
 bool al16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
+// The decode status word of a carved workspace: inside the persistent kernel's exchange area,
+// which that kernel clears before each launch; the three-kernel path's first router launch
+// clears it too, so it always describes the last call made on the workspace.
+uint32_t *status_word(const DecodeWS &w) {
+  return reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(w.xchg) + b2mega::kStatusOffset);
+}
+
+int read_status(const DecodeWS &w, int *status, cudaStream_t s, const char *who) {
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, status_word(w), 4, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return b2host::cuda_status(e, who);
+  *status = (int)v;
+  return B200MOE_OK;
+}
+
 int check_layer(const b200moe_layer *L, const char *who) {
   if (!L) return b2host::set_error(B200MOE_EINVAL, "%s: NULL layer", who);
   if (!L->gate || !L->up || !L->down || !L->sh_gate || !L->sh_up || !L->sh_down || !L->router_w || !L->sh_gate_w)
@@ -444,7 +462,8 @@ K1Params k1_params(const void *x, int x_dtype, const float *resid, float eps, in
 // operation (a memcpy node in a captured graph), so it is launched without the PDL attribute.
 int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const b200moe_layer *L, float *out,
               int32_t *ids_out, uint16_t *w_out, const DecodeWS &w, cudaStream_t s, bool first) {
-  const K1Params p1 = k1_params(x, x_dtype, resid, eps, T, L, w);
+  K1Params p1 = k1_params(x, x_dtype, resid, eps, T, L, w);
+  if (first) p1.status = status_word(w);
   if (p1.wf32) B2_CUDA(launch(k_router<true>, (unsigned)kK1Ctas, 128, 0, s, !first, p1));
   else B2_CUDA(launch(k_router<false>, (unsigned)kK1Ctas, 128, 0, s, !first, p1));
   K2Params p2;
@@ -622,6 +641,30 @@ int b200moe_decode_persistent_info(int *ctas, int *cluster) {
   const int C = b2mega::cluster_ctas();
   if (ctas) *ctas = C ? b2mega::kCtas : 0;
   if (cluster) *cluster = C;
+  return B200MOE_OK;
+}
+
+int b200moe_decode_status(const void *ws, int T, int *status, void *stream) {
+  if (!ws || !status || T <= 0 || T > kMaxT)
+    return b2host::set_error(B200MOE_EINVAL, "decode_status: ws and status required, T=%d outside [1, %d]", T, kMaxT);
+  return read_status(carve(const_cast<void *>(ws), T), status, (cudaStream_t)stream, "decode_status");
+}
+
+int b200moe_decode_noalloc_status(int T, int *status, void *stream) {
+  if (!status || T <= 0 || T > kNoAllocMaxT)
+    return b2host::set_error(B200MOE_EINVAL, "decode_noalloc_status: status required, T=%d outside [1, %d]", T,
+                             kNoAllocMaxT);
+  void *scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return read_status(carve(scratch, T), status, (cudaStream_t)stream, "decode_noalloc_status");
+}
+
+int b200moe_debug_decode_faults(long long wait_budget_cycles, int withhold_cta) {
+  if (wait_budget_cycles < 0 || withhold_cta < -1 || withhold_cta >= b2mega::kCtas)
+    return b2host::set_error(B200MOE_EINVAL, "debug_decode_faults: budget %lld < 0 or CTA %d outside [-1, %d)",
+                             wait_budget_cycles, withhold_cta, b2mega::kCtas);
+  b2mega::set_fault_hook(wait_budget_cycles, withhold_cta);
   return B200MOE_OK;
 }
 

@@ -44,6 +44,15 @@ bool usable(bool formats = false);
 // Cluster size the launches use on the current device (1: cooperative launch; 0: unusable).
 int cluster_ctas();
 
+// Test hook for the failure path: every later launch uses `budget_cycles` (> 0; else the default
+// ~1 s) as its wait budget, and CTA `withhold_cta` (>= 0; else none) never publishes its first
+// logit pair, so the other CTAs' gathers run out of budget and the kernel ends with its status set.
+void set_fault_hook(long long budget_cycles, int withhold_cta);
+
+// Status word (u32) in the exchange area: bit 1 = a bounded wait ran out (the launch's outputs
+// are incomplete). Cleared with the exchange area before each launch.
+constexpr size_t kStatusOffset = 4;
+
 // Enqueue the flag reset and the persistent kernel(s) on `stream`. Returns a B200MOE_* code.
 int launch(const Args &a, cudaStream_t stream);
 

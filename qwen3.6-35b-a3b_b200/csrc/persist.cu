@@ -50,6 +50,8 @@
 // in the published file's other block formats (Q5_K / Q6_K down, Q8_0 shared) run in the
 // kMode = 2 instantiation with kq_dot.cuh's chunk dots over the staged rows, likewise
 // bit-identical to the gather-GEMV kernels.
+#include <atomic>
+
 #include "common.cuh"
 #include "kq_dot.cuh"
 #include "mega.cuh"
@@ -93,6 +95,8 @@ struct MegaParams {
   int32_t *ids_out;
   uint16_t *w_out;
   uint8_t *xchg;  // exchange area (mega.cuh layout)
+  long long budget;  // clock cycles a poll or mbarrier wait may take before the CTA gives up
+  int withhold;      // test hook: this CTA (>= 0) never publishes its layer-0 logit pair
   b200moe_layer L[kMaxLayers];
 };
 
@@ -154,7 +158,7 @@ __device__ __forceinline__ void st_tagged(uint64_t *p, uint32_t tag, uint32_t bi
 // phase completes). kCluster: acquire at cluster scope (the phase is completed by peers' bulk
 // copies).
 template <bool kCluster>
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, long long budget) {
   const long long t0 = clock64();
   for (;;) {
     uint32_t ok;
@@ -176,7 +180,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
           : "memory");
     }
     if (ok) return true;
-    if (clock64() - t0 > kWaitBudgetCycles) return false;
+    if (clock64() - t0 > budget) return false;
   }
 }
 
@@ -372,7 +376,8 @@ struct Slice {
 
 template <int kPitch, int kCnt, typename Put>
 __device__ __forceinline__ bool gather(const uint64_t *base, uint32_t tag, const uint32_t *abort_word, int C, int r,
-                                       uint64_t *xbar, uint32_t parity, const Slice *slices, int nsl, Put put) {
+                                       uint64_t *xbar, uint32_t parity, const Slice *slices, int nsl, long long budget,
+                                       Put put) {
   const long long t0 = clock64();
   const int per = kN / C, w0 = r * per;
   bool fail = false;
@@ -405,7 +410,7 @@ __device__ __forceinline__ bool gather(const uint64_t *base, uint32_t tag, const
         pending &= ~(2u << (2 * k));
       }
     }
-    if (pending && (it & 15) == 0 && (ld_relaxed_u32(abort_word) != 0u || clock64() - t0 > kWaitBudgetCycles))
+    if (pending && (it & 15) == 0 && (ld_relaxed_u32(abort_word) != 0u || clock64() - t0 > budget))
       fail = true;
   }
   fence_proxy_async_smem();  // the slices are read by the bulk copies below (async proxy)
@@ -419,7 +424,7 @@ __device__ __forceinline__ bool gather(const uint64_t *base, uint32_t tag, const
     }
   }
   // the peers' slices: bytes completed on this CTA's exchange barrier
-  fail = !mbar_wait_bounded<true>(xbar, parity);
+  fail = !mbar_wait_bounded<true>(xbar, parity, budget);
   return !__syncthreads_or(fail);
 }
 
@@ -500,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
   };
   // bounded wait on copy barrier b's pending phase; flips this thread's parity only on success
   auto wait_bar = [&](int b) -> bool {
-    const bool ok = mbar_wait_bounded<false>(bar + b, ph[b]);
+    const bool ok = mbar_wait_bounded<false>(bar + b, ph[b], P.budget);
     if (ok) {
       ph[b] ^= 1u;
       if (tid == 0) armed &= ~(1u << b);
@@ -554,7 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
     const bool last = l + 1 == P.n_layers;
     // ---------------------------------------------------------------- phase R
     if (l > 0) {  // resid += the previous layer's deltas (every CTA applies all of them)
-      if (!gather<kSlotDelta, kHr>(td, ep, abort_word, C, r, bar + kBarXDl, ph[kBarXDl], sl_dl, 1,
+      if (!gather<kSlotDelta, kHr>(td, ep, abort_word, C, r, bar + kBarXDl, ph[kBarXDl], sl_dl, 1, P.budget,
                                    [&](int w, int i, uint32_t v) { dl_s[w * kHr + i] = __uint_as_float(v); })) {
         aborted = true;
         break;
@@ -600,10 +605,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       if (lane == 0) row_out[warp] = v;
     }
     if (__syncthreads_or(fail)) { aborted = true; break; }
-    if (tid == 0) st_tagged(tl + (size_t)c * kSlotLogits, ep + 1, row_out[0] | (row_out[1] << 16));
+    if (tid == 0 && !(l == 0 && c == P.withhold))
+      st_tagged(tl + (size_t)c * kSlotLogits, ep + 1, row_out[0] | (row_out[1] << 16));
     if (kFmt && tid == 0 && !last) issue_router_rows(l + 1);  // the one buffer is read (barrier above)
     // ---------------------------------------------------------------- phase S
-    if (!gather<kSlotLogits, 1>(tl, ep + 1, abort_word, C, r, bar + kBarXLg, ph[kBarXLg], sl_lg, 1,
+    if (!gather<kSlotLogits, 1>(tl, ep + 1, abort_word, C, r, bar + kBarXLg, ph[kBarXLg], sl_lg, 1, P.budget,
                                 [&](int w, int, uint32_t v) { lg_s[w] = v; })) {
       aborted = true;
       break;
@@ -730,7 +736,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       st_tagged(ts + (size_t)c * kSlotS + tid, ep + 2, __float_as_uint(s_out[tid]));
     if (tid == 0 && !last) issue_shared_gu(l + 1);  // this layer's shared gate/up reads are done
     // ---------------------------------------------------------------- phase D
-    if (!gather<kSlotS, kQ + kJ>(ts, ep + 2, abort_word, C, r, bar + kBarXS, ph[kBarXS], sl_s, 2,
+    if (!gather<kSlotS, kQ + kJ>(ts, ep + 2, abort_word, C, r, bar + kBarXS, ph[kBarXS], sl_s, 2, P.budget,
                                  [&](int w, int i, uint32_t v) {
                                    if (i < kQ) s_s[w * kQ + i] = __uint_as_float(v);
                                    else ssh_s[w * kJ + i - kQ] = __uint_as_float(v);
@@ -888,6 +894,16 @@ bool prepare(int dev, DevInfo &d) {
 
 namespace b2mega {
 
+// The failure-path test hook (b200moe_debug_decode_faults): a shorter wait budget and a CTA that
+// withholds its first logit pair. Process-wide; read at every launch.
+std::atomic<long long> g_hook_budget{0};
+std::atomic<int> g_hook_withhold{-1};
+
+void set_fault_hook(long long budget_cycles, int withhold_cta) {
+  g_hook_budget.store(budget_cycles > 0 ? budget_cycles : 0);
+  g_hook_withhold.store(withhold_cta >= 0 && withhold_cta < kCtas ? withhold_cta : -1);
+}
+
 bool usable(bool formats) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
@@ -913,6 +929,9 @@ int launch(const Args &a, cudaStream_t stream) {
   p.resid = a.resid;
   p.out = a.out;
   p.xchg = reinterpret_cast<uint8_t *>(a.scratch);
+  const long long hb = g_hook_budget.load();
+  p.budget = hb > 0 ? hb : kWaitBudgetCycles;
+  p.withhold = g_hook_withhold.load();
   for (int l0 = 0; l0 < a.n_layers; l0 += kMaxLayers) {
     const int nl = a.n_layers - l0 < kMaxLayers ? a.n_layers - l0 : kMaxLayers;
     p.n_layers = nl;

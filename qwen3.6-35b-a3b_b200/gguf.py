@@ -32,8 +32,9 @@ GGML_TYPES = {0: "F32", 1: "F16", 2: "Q4_0", 3: "Q4_1", 6: "Q5_0", 7: "Q5_1", 8:
 # (elements, bytes) per block of the types whose sizes the reader needs
 BLOCK = {"F32": (1, 4), "F16": (1, 2), "BF16": (1, 2), "Q4_K": (256, 144), "Q5_K": (256, 176),
          "Q6_K": (256, 210), "Q8_0": (32, 34), "Q4_0": (32, 18)}
-_SCALAR = {0: ("<B", 1), 1: ("<b", 1), 2: ("<H", 2), 3: ("<h", 2), 4: ("<I", 4), 5: ("<i", 4),
-           6: ("<f", 4), 7: ("<?", 1), 10: ("<Q", 8), 11: ("<q", 8), 12: ("<d", 8)}
+# struct format and size of each fixed-width GGUF metadata value type (GGUF spec value-type ids)
+_VALUE_TYPE_FMT = {0: ("<B", 1), 1: ("<b", 1), 2: ("<H", 2), 3: ("<h", 2), 4: ("<I", 4), 5: ("<i", 4),
+                   6: ("<f", 4), 7: ("<?", 1), 10: ("<Q", 8), 11: ("<q", 8), 12: ("<d", 8)}
 
 
 class GgufError(ValueError):
@@ -116,8 +117,8 @@ class GgufFile:
             if vt == 9:
                 et, cnt = u32(), u64()
                 return [value(et) for _ in range(cnt)]
-            if vt in _SCALAR:
-                f, k = _SCALAR[vt]
+            if vt in _VALUE_TYPE_FMT:
+                f, k = _VALUE_TYPE_FMT[vt]
                 return struct.unpack(f, take(k))[0]
             raise GgufError("format", "unknown metadata value type %d at byte %d" % (vt, pos[0]))
 

@@ -95,8 +95,15 @@ def prefill_workspace(T: int, device) -> torch.Tensor:
     return ws
 
 
+def _raise_status(who: str, status: int):
+    if status != 0:
+        raise _abi.B200MoeError(who, _abi.ECUDA, "device status word %d: a bounded pipeline or exchange wait ran "
+                                "out (or an fp16 operand overflowed, prefill bit 4); the outputs of this call are "
+                                "incomplete" % status)
+
+
 def moe_block(g: torch.Tensor, E_, layer: int = 0, probe_row=None, out: torch.Tensor | None = None,
-              path: str = "auto"):
+              path: str = "auto", check: bool = False):
     """``engine/m3_forward.py:430`` on the B200 path.
 
     ``g`` [B, T, 2048] (or [T, 2048]) f32/bf16; returns ``(out, info)`` with ``out`` f32 in
@@ -107,7 +114,10 @@ def moe_block(g: torch.Tensor, E_, layer: int = 0, probe_row=None, out: torch.Te
     GEMMs, fp16 operands) or "auto" (prefill from ``PREFILL_MIN_TOKENS`` tokens on). A layer
     with Q5_K / Q6_K down or a Q8_0 shared expert (the published Q4_K_M file) runs on the
     decode kernels at every token count; ``path="prefill"`` refuses it. No tokens give empty
-    results (as the reference's own loop does), with no device work.
+    results (as the reference's own loop does), with no device work. ``check=True`` reads the
+    call's device status word back (one stream synchronisation) and raises
+    :class:`b200moe._abi.B200MoeError` if a bounded wait ran out, as the reference refuses a
+    broken state loudly (``engine/m3_forward.py:165-170``).
     """
     if probe_row is not None:
         raise Refused("probe-row", "band-operand probes are a host-oracle feature; not on the device path")
@@ -125,9 +135,15 @@ def moe_block(g: torch.Tensor, E_, layer: int = 0, probe_row=None, out: torch.Te
     if T == 0:
         pass
     elif path == "prefill" or (path == "auto" and T >= PREFILL_MIN_TOKENS and L.all_q4k):
-        _abi.moe_prefill(x, xd, None, RMS_EPS, T, L.abi(), out, ids, prefill_workspace(T, L.device))
+        pws = prefill_workspace(T, L.device)
+        _abi.moe_prefill(x, xd, None, RMS_EPS, T, L.abi(), out, ids, pws)
+        if check:
+            _raise_status("moe_block (prefill)", _abi.prefill_status(pws, T))
     else:
-        _abi.moe_decode(x, xd, T, L.abi(), out, ids, None, workspace(T, L.device))
+        dws = workspace(T, L.device)
+        _abi.moe_decode(x, xd, T, L.abi(), out, ids, None, dws)
+        if check:
+            _raise_status("moe_block (decode)", _abi.decode_status(dws, T))
     lead = tuple(g.shape[:-1])
     return out.reshape(*lead, H), _Info(ids=ids.reshape(*lead, TOPK))
 
@@ -149,11 +165,12 @@ def moe_router(g_row: torch.Tensor, E_, layer: int = 0) -> dict:
 
 def moe_stack(resid: torch.Tensor, E_: DeviceEngine, n_layers: int | None = None,
               eps: float = RMS_EPS, ids_out: torch.Tensor | None = None,
-              ws: torch.Tensor | None = None) -> torch.Tensor:
+              ws: torch.Tensor | None = None, check: bool = False) -> torch.Tensor:
     """In place: for each layer, ``resid += moe_block_l(rmsnorm(resid))``. ``resid`` [T, 2048] f32.
 
     ``ws`` (optional) is a caller-owned workspace of ``stack_workspace_bytes(T)`` bytes; pass
-    one when capturing the call into a CUDA graph so nothing is allocated during capture."""
+    one when capturing the call into a CUDA graph so nothing is allocated during capture.
+    ``check=True`` (not inside a capture: it synchronises) raises if a bounded wait ran out."""
     if resid.dtype != torch.float32 or resid.shape[-1] != H:
         raise Refused("shape", "resid must be f32 [T, %d]" % H)
     n = len(E_.layers) if n_layers is None else int(n_layers)
@@ -164,8 +181,10 @@ def moe_stack(resid: torch.Tensor, E_: DeviceEngine, n_layers: int | None = None
     if T == 0:
         return resid
     dev = E_.layers[0].device
-    _abi.stack_decode(r, T, [L.abi() for L in E_.layers[:n]], eps, ids_out,
-                      ws if ws is not None else workspace(T, dev))
+    ws = ws if ws is not None else workspace(T, dev)
+    _abi.stack_decode(r, T, [L.abi() for L in E_.layers[:n]], eps, ids_out, ws)
+    if check:
+        _raise_status("moe_stack", _abi.decode_status(ws, T))
     return resid
 
 

@@ -34,7 +34,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("REF_ROOT")  # the reference checkout (required: no default path)
 sys.dont_write_bytecode = True
 sys.path.insert(0, REPO)
 
@@ -43,6 +43,8 @@ from oracle.bf16 import bf16_bits_to_f32  # noqa: E402
 
 
 def import_reference():
+    if not REF_ROOT or not os.path.isdir(REF_ROOT):
+        raise SystemExit("set REF_ROOT to the reference checkout (read only) to regenerate the fixtures")
     for p in (REF_ROOT, os.path.join(REF_ROOT, "tools"), os.path.join(REF_ROOT, "engine")):
         if p not in sys.path:
             sys.path.insert(0, p)
