@@ -8,16 +8,31 @@ Every step decodes a DISTINCT token, so each step streams 40 x 9 experts' Q4_K b
 (637 MB of expert weights per token > the 126 MB L2: no L2 flush needed).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                  [--workload stack_decode|layer_decode|dequant] [--batch B]
+                  [--workload stack_decode|layer_decode|prefill|prefill_ep] [--batch B]
 
 Multi-GPU (torchrun, one rank per GPU): batch-1 decode does not shard (a per-layer
 collective would cost more than the layer), so N ranks run N independent replicas on
 distinct tokens ("scaling": "weak", value = all ranks' tokens / max-over-ranks time).
 
+The default line also carries nested sub-results, each timed with CUDA events after the
+headline's timed region:
+  prefill_ep      (every N) BASELINE config 3: 4096 tokens through one layer with the experts
+                  sharded over the N ranks (ExpertParallelMoE: route, per-destination pack,
+                  all-to-all dispatch, grouped GEMMs, all-to-all return, ordered combine) as
+                  one CUDA-graph replay; per-stage times from an eager pass; on rank 0 a parity
+                  check against the single-GPU prefill of the same tokens. Also decode_b256:
+                  the same path at config 2's largest batch.
+  dequant_config1 (N = 1) config 1: the Q4_K -> bf16 dequant of one layer's expert stack.
+  decode_config2  (N = 1) config 2: one MoE layer at B in {1, 8, 32, 64, 256} under the Zipf
+                  routing law, rotated over 40 layer copies (> L2), with U(B) and the HBM
+                  roofline fraction per B.
+  config4         (N = 1) config 4's other cells: decode at B = 32 and a prefill of 8192
+                  tokens through the 40-layer stack.
+
 ``--impl reference`` times the reference's own CPU MoE path (engine/m3_forward.py
 moe_block + rmsnorm glue, restated as the torch-f32 port in oracle/moe.py) on the host
-cores, rank 0 only, on a bounded per-step sample (a few layers of one token, scaled to the
-40-layer token).
+cores, rank 0 only: whole 40-layer tokens, as many steps as fit a bounded time budget
+(the line's ``steps`` is the count actually timed).
 """
 from __future__ import annotations
 
@@ -99,7 +114,13 @@ def parse():
                         "Q4_K_M file's layout (Q5_K down, Q6_K at layers 34/38/39, Q8_0 shared expert, F32 "
                         "router, RMSNorm weight) with seeded random block bytes")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--ref-layers-per-step", type=int, default=2)
+    p.add_argument("--no-extras", action="store_true", help="only the headline (no nested sub-results)")
+    p.add_argument("--ref-layers-per-step", type=int, default=N_LAYERS,
+                   help="reference arm: layers of the stack per timed step (default: the whole token)")
+    p.add_argument("--ref-seconds", type=float, default=100.0,
+                   help="reference arm: time budget of the timed steps (the step count is cut to fit)")
+    p.add_argument("--cpu-layers", type=int, default=2,
+                   help="the GPU arm's cpu_baseline sample: layers of one token")
     return p.parse_args()
 
 
@@ -192,11 +213,11 @@ def host_layer_of(L):
                         norm_w=None if L.norm_w is None else L.norm_w.cpu().numpy())
 
 
-def cpu_sample(args, seconds_hint=None, threads=None, eng=None):
-    """Time the reference's CPU path (oracle port) on a bounded sample: one token through
-    ``args.ref_layers_per_step`` layers of the stack (the Q4_K synthetic layers, or with
-    ``--formats published`` the device engine's own first layers copied to the host). Returns
-    (layers, x0, cores, n_layers)."""
+def cpu_sample(args, n_layers, threads=None, eng=None):
+    """Prepare the reference's CPU path (oracle port) on a sample: one token through ``n_layers``
+    layers of the stack (the Q4_K synthetic layers, or with ``--formats published`` the device
+    engine's own first layers copied to the host), with one untimed pass that fills each layer's
+    byte cache. Returns (layers, x0, cores, n_layers, seconds of the untimed pass)."""
     import numpy as np
     import torch
     from oracle import moe as OM
@@ -207,7 +228,7 @@ def cpu_sample(args, seconds_hint=None, threads=None, eng=None):
     from b200moe.geometry import KIND_OF, stream_id
     cores = threads or len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    nl = max(1, args.ref_layers_per_step)
+    nl = max(1, min(int(n_layers), args.layers))
     if getattr(args, "formats", "q4k") == "published" and eng is not None:
         layers = [host_layer_of(eng.layers[l]) for l in range(nl)]
     else:
@@ -215,8 +236,9 @@ def cpu_sample(args, seconds_hint=None, threads=None, eng=None):
                                  synth.router_w(args.seed, l), synth.shared_gate_w(args.seed, l))
                   for l in range(nl)]
     x0 = synth.bf16_bits_to_f32(synth.tokens(args.seed, args.batch, stream=0))
+    t0 = time.perf_counter()
     OM.stack_port(x0, layers, cores)          # untimed pass: fills each layer's byte cache
-    return layers, x0, cores, nl
+    return layers, x0, cores, nl, time.perf_counter() - t0
 
 
 def run_reference(args):
@@ -224,29 +246,283 @@ def run_reference(args):
     if rank != 0:
         return 0
     from oracle import moe as OM
-    layers, x0, cores, nl = cpu_sample(args)
+    layers, x0, cores, nl, t_first = cpu_sample(args, args.ref_layers_per_step)
+    # untimed warm-up passes (the first, above, also filled the byte caches), then as many timed
+    # steps as fit the time budget
+    for _ in range(max(0, min(args.warmup, 1) - 1)):
+        OM.stack_port(x0, layers, cores)
+    steps = max(1, min(args.steps, int(args.ref_seconds / max(t_first, 1e-3))))
     times = []
-    for i in range(args.warmup + args.steps):
+    for _ in range(steps):
         t0 = time.perf_counter()
         OM.stack_port(x0, layers, cores)
-        dt = time.perf_counter() - t0
-        if i >= args.warmup:
-            times.append(dt)
-    sec_tok = (sum(times) / len(times)) * (args.layers / nl)
+        times.append(time.perf_counter() - t0)
+    sec_step = sum(times) / len(times)
+    sec_tok = sec_step * (args.layers / nl)
     val = args.batch / sec_tok
-    sample = ("%d token(s) through %d of %d layers per step (torch-f32 port of engine/m3_forward.py "
-              "moe_block + rmsnorm_a; per-hit-expert Q4_K dequant inside the timed region; bytes "
-              "pre-generated), scaled x%g to the 40-layer token" % (args.batch, nl, args.layers, args.layers / nl))
+    whole = nl == args.layers
+    sample = ("%d token(s) through %s per step (torch-f32 port of engine/m3_forward.py moe_block + rmsnorm_a; "
+              "per-hit-expert Q4_K dequant inside the timed region; bytes pre-generated)%s; %d of the %d requested "
+              "steps timed (a %.0f s budget), 1 untimed warm-up"
+              % (args.batch, ("all %d layers" % nl) if whole else ("%d of %d layers" % (nl, args.layers)),
+                 "" if whole else ", scaled x%g to the 40-layer token" % (args.layers / nl), steps, args.steps,
+                 args.ref_seconds))
     line = {"impl": "reference", "metric": "moe_stack_decode_tok_per_s", "value": val, "unit": "tok/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sec_tok,
+            "n_gpus": world, "steps": steps, "warmup": 1, "ms_per_step": 1e3 * sec_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded Q4_K, config-0 field law)",
             "config": {"workload": "config4_stack_decode_b%d" % args.batch, "layers": args.layers,
-                       "batch": args.batch, "seed": args.seed},
+                       "layers_per_step": nl, "batch": args.batch, "seed": args.seed},
             "cpu_baseline": {"value": val, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ---------------------------------------------------------------------------------- sub-results
+def _tf_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return 1590.0
+
+
+def _events_time(fn, K, W, dev):
+    """fn() W times untimed (at least 3), then K times between two CUDA events on the current
+    stream; returns ms per call."""
+    import torch
+    for _ in range(max(3, W)):
+        fn()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        fn()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / K
+
+
+def _graph_of(fn, dev):
+    """Capture fn() (after one eager call on a side stream) into a CUDA graph."""
+    import torch
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g
+
+
+def bench_dequant(dev, K, W, hbm_peak):
+    """b200moe_q4k_dequant of one layer's whole expert stack (gate, up, down of
+    the 256 experts, fields from seed 1) to bf16: three launches per step."""
+    import torch
+    from b200moe import _abi
+    from b200moe.engine import DeviceLayer
+    L = DeviceLayer.synthetic(1, 0, dev)
+    srcs = [L.gate, L.up, L.down]
+    nel = [t.numel() // 144 * 256 for t in srcs]
+    out = torch.empty(sum(nel), dtype=torch.bfloat16, device=dev)
+    views, o = [], 0
+    for n in nel:
+        views.append(out[o:o + n])
+        o += n
+
+    def step():
+        for src, v in zip(srcs, views):
+            _abi.q4k_dequant(src, v, _abi.BF16)
+
+    ms = _events_time(step, max(K, 10), W, dev)
+    nblocks = sum(t.numel() for t in srcs) // 144
+    rd, wr = nblocks * 144, nblocks * 256 * 2
+    gbs = (rd + wr) / (ms / 1e3) / 1e9
+    del out, L
+    torch.cuda.empty_cache()
+    return {"blocks": nblocks, "read_bytes": rd, "write_bytes": wr, "ms_per_step": ms, "launches_per_step": 3,
+            "achieved_gbs": gbs, "peak_gbs": hbm_peak, "frac": gbs / hbm_peak,
+            "note": "BASELINE quotes 786,432 blocks for these shapes; the shapes [256,1024,2048] + [256,2048,512] "
+                    "hold 3,145,728 blocks, which is what runs"}
+
+
+def bench_config2(eng, dev, K, W, hbm_peak, batches=(1, 8, 32, 64, 256)):
+    """one MoE layer at batch B under the Zipf(1.1) routing law (per-expert
+    logit bias), one call per layer rotated over the stack's 40 layer copies so the weights
+    streamed per step exceed L2; the block's own path choice per B."""
+    import numpy as np
+    import torch
+    from b200moe import moe, synth
+    from b200moe.engine import DeviceLayer
+    layers = []
+    for l, L in enumerate(eng.layers):
+        bias = torch.from_numpy(synth.zipf_bias(2, l)).to(dev)
+        layers.append(DeviceLayer(L.gate, L.up, L.down, L.sh_gate, L.sh_up, L.sh_down, L.router_w, L.sh_gate_w,
+                                  logit_bias=bias, gate_up_stride=L.gate_up_stride))
+    nl = len(layers)
+    res = {}
+    for B in batches:
+        x = torch.from_numpy(synth.tokens(2, B, stream=60 + B).view(np.int16)).view(torch.bfloat16).to(dev)
+        out = torch.empty((B, 2048), dtype=torch.float32, device=dev)
+        uniq = []
+        for L in layers:
+            _, info = moe.moe_block(x, L, 0, out=out)
+            uniq.append(int(torch.unique(info["ids"]).numel()))
+
+        def step():
+            for L in layers:
+                moe.moe_block(x, L, 0, out=out)
+
+        g = _graph_of(step, dev)
+        ms = _events_time(g.replay, max(K, 5), W, dev)
+        del g
+        per_layer_ms = ms / nl
+        u = float(np.mean(uniq))
+        byts = u * EXPERT_BYTES + EXPERT_BYTES + ROUTER_BYTES + WSG_BYTES + B * 2048 * (2 + 4)
+        gbs = byts / (per_layer_ms / 1e3) / 1e9
+        path = ("persistent kernel (one layer per launch)" if B == 1 else
+                "decode kernels (3 per layer)" if B < moe.PREFILL_MIN_TOKENS else "grouped GEMMs (10 per layer)")
+        res["b%d" % B] = {"us_per_layer": per_layer_ms * 1e3, "tok_per_s": B / (per_layer_ms / 1e3),
+                          "distinct_experts": u, "bytes_per_layer": byts, "achieved_gbs": gbs,
+                          "frac": gbs / hbm_peak, "path": path}
+    return res
+
+
+def bench_config4(eng, dev, K, W, tf_peak):
+    """BASELINE config 4's other cells: decode at B = 32 and a prefill of 8192 tokens through the
+    40-layer stack (``resid += moe(rmsnorm(resid))`` per layer, the block's own path choice)."""
+    import numpy as np
+    import torch
+    from b200moe import moe, synth
+    nl = len(eng.layers)
+    res = {}
+    for name, T in (("decode_b32", 32), ("prefill_t8192", 8192)):
+        x0 = torch.from_numpy(synth.bf16_bits_to_f32(synth.tokens(4, T, stream=80)).reshape(T, 2048).copy()).to(dev)
+        resid = x0.clone()
+        fn = moe.moe_stack_prefill if T >= moe.PREFILL_MIN_TOKENS else moe.moe_stack
+        ws = (torch.empty(moe._abi.prefill_workspace_size(T), dtype=torch.uint8, device=dev)
+              if fn is moe.moe_stack_prefill else torch.empty(moe.stack_workspace_bytes(T), dtype=torch.uint8,
+                                                                device=dev))
+
+        def step():
+            resid.copy_(x0)
+            fn(resid, eng, ws=ws)
+
+        g = _graph_of(step, dev)
+        ms = _events_time(g.replay, max(3, min(K, 10 if T > 64 else 50)), min(W, 3), dev)
+        del g
+        fin = bool(torch.isfinite(resid).all())
+        flops = nl * 2.0 * T * (9 * 3 * 2048 * 512 + 256 * 2048)
+        res[name] = {"tokens": T, "layers": nl, "ms_per_step": ms, "tok_per_s": T / (ms / 1e3),
+                     "tflops": flops / (ms / 1e3) / 1e12, "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / tf_peak,
+                     "path": "grouped GEMMs (10 kernels per layer)", "finite": fin}
+        del ws, resid, x0
+        torch.cuda.empty_cache()
+    return res
+
+
+def bench_prefill_ep(dev, rank, world, K, W, tf_peak, T_total=4096, seed=3, check=True, bias=False):
+    """Config 3 under expert parallelism: T_total tokens split over the ranks, 256/world experts per
+    rank, one layer per step as one CUDA-graph replay (eager if capture is refused), max over ranks.
+    Stage times come from a separate eager pass with events between the stages. On rank 0 the
+    gathered outputs are compared with the single-GPU prefill of all tokens."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from b200moe import moe, synth
+    from b200moe.engine import DeviceLayer
+    from b200moe.ep import ExpertParallelMoE
+    T = T_total // world
+    L = DeviceLayer.synthetic(seed, 0, dev, bias=bias)
+    ep = ExpertParallelMoE(L)
+    xb = synth.tokens(seed, T_total, stream=100)
+    x_all = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).reshape(T_total, 2048)
+    x_loc = x_all[rank * T:(rank + 1) * T].to(dev)
+    out = torch.empty((T, 2048), dtype=torch.float32, device=dev)
+
+    def step():
+        ep.forward(x_loc, out=out)
+
+    for _ in range(2):  # eager warm-up: communicators, tensor maps, buffers
+        step()
+    torch.cuda.synchronize(dev)
+    graph, how = None, "cuda_graph"
+    try:
+        graph = _graph_of(step, dev)
+        ok = 1
+    except Exception as e:  # noqa: BLE001 -- any capture refusal falls back to eager launches
+        ok, how = 0, "eager (graph capture refused: %s)" % type(e).__name__
+        graph = None
+    if world > 1:
+        t = torch.tensor([ok], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        if int(t.item()) == 0 and graph is not None:
+            graph, how = None, "eager (graph capture refused on another rank)"
+    run = graph.replay if graph is not None else step
+    if world > 1:
+        dist.barrier()
+    ms = _events_time(run, max(K, 10), W, dev)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    # per-stage times: eager steps with an event after each stage
+    names = ("route", "dispatch", "experts", "combine", "sum")
+    acc = {n: 0.0 for n in names}
+    reps = 5
+    for _ in range(reps):
+        evs = [torch.cuda.Event(enable_timing=True)]
+        evs[0].record()
+
+        def mark(stage):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            evs.append(e)
+
+        ep.forward(x_loc, out=out, mark=mark)
+        torch.cuda.synchronize(dev)
+        for i, n in enumerate(names):
+            acc[n] += evs[i].elapsed_time(evs[i + 1]) / reps
+    stages = {n: acc[n] for n in names}
+    if world > 1:
+        tt = torch.tensor([stages[n] for n in names], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        stages = {n: float(v) for n, v in zip(names, tt.tolist())}
+    stages["sum_of_stages_eager"] = sum(stages[n] for n in names)
+    status = moe._abi.prefill_status(ep.workspace(T), world * T if world > 1 else T)
+    flops = 2.0 * T_total * 9 * 3 * 2048 * 512
+    res = {"tokens": T_total, "tokens_per_rank": T, "experts_per_rank": 256 // world, "n_gpus": world,
+           "ms_per_step": ms, "tok_per_s": T_total / (ms / 1e3), "tflops_per_gpu": flops / world / (ms / 1e3) / 1e12,
+           "frac_of_bf16_peak": flops / world / (ms / 1e3) / 1e12 / tf_peak, "timing": how,
+           "stages_ms_max_over_ranks": stages, "status": status}
+    if check:
+        step()
+        ids = torch.empty((T, 8), dtype=torch.int32, device=dev)
+        o, i = ep.forward(x_loc)
+        ids.copy_(i)
+        if world > 1:
+            outs = [torch.empty_like(o) for _ in range(world)]
+            idss = [torch.empty_like(ids) for _ in range(world)]
+            dist.all_gather(outs, o)
+            dist.all_gather(idss, ids)
+        else:
+            outs, idss = [o], [ids]
+        if rank == 0:
+            ref, info = moe.moe_block(x_all.to(dev), L, path="prefill")
+            got = torch.cat(outs)
+            res["parity_vs_single_gpu"] = {
+                "ids_equal": bool(torch.equal(torch.cat(idss), info["ids"])),
+                "rel_l2": float(torch.linalg.norm(got - ref) / torch.linalg.norm(ref)),
+                "finite": bool(torch.isfinite(got).all())}
+        if world > 1:
+            dist.barrier()
+    del graph, ep, L
+    torch.cuda.empty_cache()
+    return res
 
 
 # ---------------------------------------------------------------------------------- GPU arm
@@ -313,7 +589,8 @@ def run_b200(args):
             ids_all[i].copy_(ids_step, non_blocking=True)
     elif args.workload == "layer_decode":
         L = DeviceLayer.synthetic(args.seed, 0, dev, bias=(args.seed == 2))
-        # rotate over enough layer copies to exceed L2: per-step bytes are one layer's
+        # one layer, called again every step: after the first step its rows sit in L2, so this
+        # workload times latency, not HBM bandwidth (no roofline; decode_config2 rotates layers)
         nl = 1
         persist_ctas, persist_cluster = _abi.decode_persistent_info() if T == 1 else (0, 0)
         launches_per_step = 1 if persist_ctas else 3
@@ -342,24 +619,19 @@ def run_b200(args):
         def step(i):
             moe.moe_block(tok_dev, L, 0, out=out, path="prefill")
     elif args.workload == "prefill_ep":
-        # config 3 with expert parallelism: 4096 tokens split over the N ranks, each rank owns
-        # 256/N experts; NCCL all-to-all dispatch / combine (strong scaling: total work fixed)
-        from b200moe.ep import ExpertParallelMoE
-        T_total = args.batch if args.batch > 1 else 4096
-        T = T_total // world
-        L = DeviceLayer.synthetic(3, 0, dev)
-        ep = ExpertParallelMoE(L)
-        nl = 1
-        launches_per_step = 12
-        tok_bits = synth.tokens(3, T_total, stream=100)
-        x_all = torch.from_numpy(tok_bits.view(np.int16)).view(torch.bfloat16).reshape(T_total, 2048)
-        x_loc = x_all[rank * T:(rank + 1) * T].to(dev)
-        ids_all = torch.zeros((K + W, 1, 1, 8), dtype=torch.int32, device=dev)
-        flops_per_step = 2.0 * T_total * 9 * 3 * 2048 * 512
-        bytes_per_step = None
-
-        def step(i):
-            ep.forward(x_loc)
+        # config 3 with expert parallelism (strong scaling: total work fixed), as the sub-result
+        res = bench_prefill_ep(dev, rank, world, K, W, _tf_peak(), T_total=args.batch if args.batch > 1 else 4096)
+        if rank == 0:
+            print(json.dumps({"metric": "moe_prefill_ep_tok_per_s", "value": res["tok_per_s"], "unit": "tok/s",
+                              "n_gpus": world, "steps": max(K, 10), "warmup": max(3, W),
+                              "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+                              "vs_baseline": None, "dtype": "fp16 operands, f32 accumulate", "data": "synthetic",
+                              "config": {"workload": "config3_prefill_ep_t%d" % res["tokens"],
+                                         "parallelism": "ep%d" % world}, "prefill_ep": res}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
     else:
         raise SystemExit("unknown workload %s" % args.workload)
 
@@ -454,7 +726,7 @@ def run_b200(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "stack_decode":
         from oracle import moe as OM
-        layers, x0, cores, nlp = cpu_sample(args, eng=eng)
+        layers, x0, cores, nlp, _ = cpu_sample(args, args.cpu_layers, eng=eng)
         ts = []
         for _ in range(3):
             t0 = time.perf_counter()
@@ -514,6 +786,27 @@ def run_b200(args):
         line["north_star"] = {"expert_bytes_per_token": expert_bytes,
                               "frac_of_8TBs": expert_bytes / (ms_step / 1e3) / 8e12,
                               "target_frac": 0.60, "us_per_token": ms_step * 1e3 / T}
+        st = _abi.decode_status(ws, T) if not use_prefill else _abi.prefill_status(ws, T)
+        if st != 0:
+            raise SystemExit("decode status word %d after the timed region" % st)
+
+    # ---------------- nested sub-results (after the headline's timed region)
+    if (args.workload == "stack_decode" and args.formats == "q4k" and not args.zipf and T == 1
+            and args.layers == N_LAYERS and not args.no_extras):
+        graph = None
+        tf_peak = _tf_peak()
+        xs = ClockSampler(physical_index(local_rank))
+        xs.start()
+        line["prefill_ep"] = bench_prefill_ep(dev, rank, world, K, W, tf_peak)
+        line["prefill_ep"]["decode_b256"] = bench_prefill_ep(dev, rank, world, K, W, tf_peak, T_total=256, seed=2,
+                                                           bias=True)
+        if world == 1:
+            line["dequant_config1"] = bench_dequant(dev, K, W, hbm_peak)
+            line["decode_config2"] = bench_config2(eng, dev, K, W, hbm_peak)
+            line["config4"] = bench_config4(eng, dev, K, W, tf_peak)
+        xs.stop_ev.set()
+        xs.join()
+        line["extras_clocks"] = xs.result()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

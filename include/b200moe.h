@@ -231,6 +231,40 @@ int b200moe_moe_experts(const void *x16, int T, const int32_t *ids, const uint16
                         const b200moe_layer *layer, float *out, int accumulate, void *ws,
                         size_t ws_bytes, void *stream);
 
+/* ---- Expert parallelism (one process per GPU; the caller moves the buffers between ranks,
+ * e.g. with two equal-split all-to-alls). The reference runs every expert in one process
+ * (engine/m3_forward.py:447-475: group the (token, slot) pairs by expert, run each hit expert,
+ * combine in ascending expert id); these three calls split that loop across `world` ranks that
+ * each own the experts [rank 256/world, (rank+1) 256/world) and T tokens of their own.
+ *
+ * Dispatch row (B200MOE_EP_ROW_BYTES): 2048 fp16 x values, the token's 8 expert ids (int32),
+ * its 8 bf16 routing weights, 16 bytes of padding. */
+#define B200MOE_EP_ROW_BYTES 4160
+
+/* Source side, after b200moe_moe_route: fills send_rows [world][T] dispatch rows -- block d holds,
+ * in ascending token order, the tokens with at least one slot in d's expert range (every token
+ * for d = rank: the shared expert runs there), then rows with ids -1 -- and pos [T][world], the
+ * row of token t in block d or -1. Exchange block d with rank d (equal splits of
+ * T x B200MOE_EP_ROW_BYTES bytes). */
+int b200moe_ep_pack(const void *x16, const int32_t *ids, const uint16_t *w_bf16, int T, int rank, int world,
+                    void *send_rows, int32_t *pos, void *stream);
+
+/* Receiver side: recv_rows [world][T] dispatch rows (block s from rank s) -> partial [world][T]
+ * [2048] f32: per row, its slots in this rank's expert range through the Q4_K grouped GEMMs,
+ * summed in ascending expert id, plus sg[t] * shared_expert(x) on the own block (rows
+ * rank T .. rank T + T - 1 = this rank's tokens, sg [T] from b200moe_moe_route); 0 for rows
+ * without work. Send block s back to rank s. Workspace: b200moe_prefill_workspace_size(world T).
+ * Asynchronous; b200moe_prefill_status(ws, world T, ...) reads its status word. */
+int b200moe_ep_experts(const void *recv_rows, int T, int rank, int world, const float *sg,
+                       const b200moe_layer *layer, float *partial, void *ws, size_t ws_bytes,
+                       void *stream);
+
+/* Source side: out[t] (+= when accumulate) the sum over d = 0 .. world-1 (ascending expert
+ * ranges) of ret[d][pos[t][d]] for pos >= 0, where ret [world][T][2048] f32 holds the partial
+ * rows sent back by every rank. */
+int b200moe_ep_combine(const float *ret, const int32_t *pos, int T, int world, float *out, int accumulate,
+                       void *stream);
+
 /* Copy the prefill workspace's device status word to *status (synchronises `stream`). Bits:
  * 1 / 2 = a gate_up / down GEMM pipeline wait exceeded its ~1 s budget; 4 = an fp16 tensor-core
  * operand was out of range (|x| or |silu(gate)*up| * 2^-10 above 65504). 0 = ok. */

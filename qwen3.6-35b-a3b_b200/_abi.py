@@ -26,7 +26,10 @@ EXPORTS = ("b200moe_abi_version", "b200moe_last_error", "b200moe_q4k_dequant", "
            "b200moe_stack_workspace_size",
            "b200moe_stack_decode",
            "b200moe_prefill_workspace_size", "b200moe_moe_prefill", "b200moe_moe_route",
-           "b200moe_moe_experts", "b200moe_prefill_status")
+           "b200moe_moe_experts", "b200moe_prefill_status", "b200moe_ep_pack", "b200moe_ep_experts",
+           "b200moe_ep_combine")
+
+EP_ROW_BYTES = 4160   # B200MOE_EP_ROW_BYTES: 2048 fp16 x, 8 int32 ids, 8 bf16 weights, 16 B pad
 
 
 class B200MoeError(RuntimeError):
@@ -108,6 +111,12 @@ def lib():
                                           vp, sz, vp]
         L.b200moe_prefill_status.restype = i32
         L.b200moe_prefill_status.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_int), vp]
+        L.b200moe_ep_pack.restype = i32
+        L.b200moe_ep_pack.argtypes = [vp, vp, vp, i32, i32, i32, vp, vp, vp]
+        L.b200moe_ep_experts.restype = i32
+        L.b200moe_ep_experts.argtypes = [vp, i32, i32, i32, vp, ctypes.POINTER(Layer), vp, vp, sz, vp]
+        L.b200moe_ep_combine.restype = i32
+        L.b200moe_ep_combine.argtypes = [vp, vp, i32, i32, vp, i32, vp]
         _LIB = L
     return _LIB
 
@@ -273,3 +282,22 @@ def moe_experts(x16, T: int, ids, w_bf16, e_lo: int, e_hi: int, sg, layer: Layer
            lib().b200moe_moe_experts(ptr(x16), T, ptr(ids), ptr(w_bf16), int(e_lo), int(e_hi), ptr(sg), int(lo),
                                      int(hi), ctypes.byref(layer), ptr(out), 1 if accumulate else 0, ptr(ws),
                                      ws.numel() * ws.element_size(), _stream(stream)))
+
+
+def ep_pack(x16, ids, w_bf16, T: int, rank: int, world: int, send_rows, pos, stream=None):
+    """``b200moe_ep_pack``: send_rows [world, T, EP_ROW_BYTES] uint8, pos [T, world] int32."""
+    _check("b200moe_ep_pack", lib().b200moe_ep_pack(ptr(x16), ptr(ids), ptr(w_bf16), T, rank, world,
+                                                     ptr(send_rows), ptr(pos), _stream(stream)))
+
+
+def ep_experts(recv_rows, T: int, rank: int, world: int, sg, layer: Layer, partial, ws, stream=None):
+    """``b200moe_ep_experts``: partial [world, T, 2048] f32 from recv_rows [world, T, EP_ROW_BYTES]."""
+    _check("b200moe_ep_experts",
+           lib().b200moe_ep_experts(ptr(recv_rows), T, rank, world, ptr(sg), ctypes.byref(layer), ptr(partial),
+                                    ptr(ws), ws.numel() * ws.element_size(), _stream(stream)))
+
+
+def ep_combine(ret, pos, T: int, world: int, out, accumulate: bool, stream=None):
+    """``b200moe_ep_combine``: out [T, 2048] f32 (+)= ascending-rank sum of the returned partial rows."""
+    _check("b200moe_ep_combine", lib().b200moe_ep_combine(ptr(ret), ptr(pos), T, world, ptr(out),
+                                                           1 if accumulate else 0, _stream(stream)))

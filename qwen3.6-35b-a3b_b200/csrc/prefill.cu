@@ -437,17 +437,18 @@ __global__ void __launch_bounds__(256) k_fill(int T, int sh_lo, int sh_hi, const
 }
 
 // ------------------------------------------------------------------------- k_gather_x
-// x16p[pos] = x16[token of assignment-list entry pos], one warp per row (4 KB), so the gate_up
+// x16p[pos] = x16[token of assignment-list entry pos] (x16 rows `pitch` halves apart: kH, or the
+// expert-parallel dispatch rows), one warp per row (4 KB), so the gate_up
 // GEMM reads its B operand as contiguous 64-row TMA boxes. Rows from offsets[kE] on belong to
 // the shared expert (entries are token ids); the others hold t * 8 + slot.
 __global__ void __launch_bounds__(256) k_gather_x(int max_rows, const int32_t *offsets, const int32_t *plist,
-                                                  const __half *x16, __half *x16p) {
+                                                  const __half *x16, int64_t pitch, __half *x16p) {
   const int total = __ldg(offsets + kNE), sh0 = __ldg(offsets + kE);
   const int lane = threadIdx.x & 31;
   for (int pos = (blockIdx.x * 256 + threadIdx.x) >> 5; pos < total && pos < max_rows; pos += gridDim.x * 8) {
     const int pl = __ldg(plist + pos);
     const int t = pos >= sh0 ? pl : (pl >> 3);
-    const uint4 *src = reinterpret_cast<const uint4 *>(x16 + (size_t)t * kH);
+    const uint4 *src = reinterpret_cast<const uint4 *>(x16 + (size_t)t * pitch);
     uint4 *dst = reinterpret_cast<uint4 *>(x16p + (size_t)pos * kH);
 #pragma unroll
     for (int i = 0; i < kH / 8 / 32; ++i) dst[lane + 32 * i] = __ldg(src + lane + 32 * i);
@@ -866,6 +867,117 @@ __global__ void __launch_bounds__(256) k_combine(int T, const float *y, const in
   *dst = r;
 }
 
+// ------------------------------------------------------------------------- expert parallelism
+// Dispatch rows: one per (source token, destination rank) pair that has work there -- 2048 fp16
+// x values, then the token's 8 expert ids (int32), its 8 bf16 routing weights and 16 bytes of
+// padding (4160 B, 16-byte aligned). A source rank with T tokens fills a [world][T] grid of
+// rows: destination d's rows 0 .. n_d - 1 are its tokens with a slot in d's expert range, in
+// ascending token order (every token for d = rank, where the shared expert runs); rows from n_d
+// on carry ids -1 and no work. pos[t][d] is token t's row at d (-1: none).
+constexpr int kEpRowHalves = kH + 32;
+constexpr int kEpIdsOff = kH * 2;          // byte offset of the ids in a row
+constexpr int kEpWOff = kEpIdsOff + 32;    // byte offset of the weights
+static_assert(kEpRowHalves * 2 == B200MOE_EP_ROW_BYTES, "dispatch row size");
+
+// CTA d = destination: a block-wide scan over the tokens gives every row position; writes pos
+// and the rows' ids / weights (the x values are copied by k_ep_copy).
+__global__ void __launch_bounds__(1024) k_ep_plan(int T, const int32_t *ids, const uint16_t *wb, int rank, int world,
+                                                  uint8_t *send, int32_t *pos) {
+  __shared__ int wsum[32];
+  const int d = blockIdx.x, per = kE / world, lo = d * per, hi = lo + per;
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  uint8_t *seg = send + (size_t)d * T * B200MOE_EP_ROW_BYTES;
+  int carry = 0;
+  for (int base = 0; base < T; base += 1024) {
+    const int t = base + threadIdx.x;
+    bool f = false;
+    int4 i0 = make_int4(-1, -1, -1, -1), i1 = i0;
+    if (t < T) {
+      i0 = __ldg(reinterpret_cast<const int4 *>(ids + (size_t)t * kK));
+      i1 = __ldg(reinterpret_cast<const int4 *>(ids + (size_t)t * kK) + 1);
+      const int id[8] = {i0.x, i0.y, i0.z, i0.w, i1.x, i1.y, i1.z, i1.w};
+      f = d == rank;
+#pragma unroll
+      for (int k = 0; k < kK; ++k) f |= id[k] >= lo && id[k] < hi;
+    }
+    const unsigned b = __ballot_sync(0xFFFFFFFFu, f);
+    if (lane == 0) wsum[wp] = __popc(b);
+    __syncthreads();
+    if (wp == 0) {  // inclusive scan of the 32 warp counts
+      int v = wsum[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xFFFFFFFFu, v, o);
+        if (lane >= o) v += u;
+      }
+      wsum[lane] = v;
+    }
+    __syncthreads();
+    const int p = carry + (wp ? wsum[wp - 1] : 0) + __popc(b & ((1u << lane) - 1u));
+    if (t < T) {
+      pos[(size_t)t * world + d] = f ? p : -1;
+      if (f) {
+        uint8_t *row = seg + (size_t)p * B200MOE_EP_ROW_BYTES;
+        reinterpret_cast<int4 *>(row + kEpIdsOff)[0] = i0;
+        reinterpret_cast<int4 *>(row + kEpIdsOff)[1] = i1;
+        *reinterpret_cast<uint4 *>(row + kEpWOff) = __ldg(reinterpret_cast<const uint4 *>(wb + (size_t)t * kK));
+      }
+    }
+    carry += wsum[31];
+    __syncthreads();  // wsum is rewritten by the next round
+  }
+  const int4 none = make_int4(-1, -1, -1, -1);
+  for (int p = carry + threadIdx.x; p < T; p += 1024) {  // rows without work
+    uint8_t *row = seg + (size_t)p * B200MOE_EP_ROW_BYTES;
+    reinterpret_cast<int4 *>(row + kEpIdsOff)[0] = none;
+    reinterpret_cast<int4 *>(row + kEpIdsOff)[1] = none;
+  }
+}
+
+// CTA t: token t's 4 KB of x16 into its row at every destination that takes it.
+__global__ void __launch_bounds__(256) k_ep_copy(int T, const __half *x16, int world, const int32_t *pos,
+                                                 uint8_t *send) {
+  const int t = blockIdx.x;
+  const uint4 v = __ldg(reinterpret_cast<const uint4 *>(x16 + (size_t)t * kH) + threadIdx.x);
+  for (int d = 0; d < world; ++d) {
+    const int p = __ldg(pos + (size_t)t * world + d);
+    if (p >= 0)
+      reinterpret_cast<uint4 *>(send + ((size_t)d * T + p) * B200MOE_EP_ROW_BYTES)[threadIdx.x] = v;
+  }
+}
+
+// Receiver: the ids and weights of the R gathered rows into contiguous arrays.
+__global__ void __launch_bounds__(256) k_ep_unpack(int R, const uint8_t *rows, int32_t *ids, uint16_t *wb) {
+  const int r = blockIdx.x * 256 + threadIdx.x;
+  if (r >= R) return;
+  const uint8_t *row = rows + (size_t)r * B200MOE_EP_ROW_BYTES;
+  reinterpret_cast<int4 *>(ids + (size_t)r * kK)[0] = reinterpret_cast<const int4 *>(row + kEpIdsOff)[0];
+  reinterpret_cast<int4 *>(ids + (size_t)r * kK)[1] = reinterpret_cast<const int4 *>(row + kEpIdsOff)[1];
+  *reinterpret_cast<uint4 *>(wb + (size_t)r * kK) = *reinterpret_cast<const uint4 *>(row + kEpWOff);
+}
+
+// Source: out[t] (+)= sum over destinations d = 0, 1, ... (ascending expert ranges) of the partial
+// row ret[d][pos[t][d]]; one thread per float4.
+__global__ void __launch_bounds__(256) k_ep_sum(int T, int world, const float *ret, const int32_t *pos, float *out,
+                                                int accumulate) {
+  const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (idx >= (int64_t)T * (kH / 4)) return;
+  const int t = (int)(idx / (kH / 4)), h = (int)(idx % (kH / 4)) * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int d = 0; d < world; ++d) {
+    const int p = __ldg(pos + (size_t)t * world + d);
+    if (p < 0) continue;
+    const float4 v = __ldcs(reinterpret_cast<const float4 *>(ret + ((size_t)d * T + p) * kH + h));
+    acc = make_float4(__fadd_rn(acc.x, v.x), __fadd_rn(acc.y, v.y), __fadd_rn(acc.z, v.z), __fadd_rn(acc.w, v.w));
+  }
+  float4 *dst = reinterpret_cast<float4 *>(out + (size_t)t * kH + h);
+  if (accumulate) {
+    const float4 o = *dst;
+    acc = make_float4(__fadd_rn(o.x, acc.x), __fadd_rn(o.y, acc.y), __fadd_rn(o.z, acc.z), __fadd_rn(o.w, acc.w));
+  }
+  *dst = acc;
+}
+
 bool a16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
 int g_num_sms = 0;
@@ -1036,7 +1148,7 @@ int route_stage(const void *x, int x_dtype, const float *resid, float eps, int T
 // expert when sg != NULL), then the combine into out (accumulate: out += result).
 int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *wb, int e_lo, int e_hi,
                   const float *sg, int sh_lo, int sh_hi, const b200moe_layer *L, float *out, int accumulate,
-                  const PrefillWS &w, cudaStream_t s) {
+                  const PrefillWS &w, cudaStream_t s, int64_t x16_pitch = kH) {
   int rc = ensure_gemm_attrs();
   if (rc) return rc;
   B2_CUDA(cudaMemsetAsync(w.counts, 0, kNE * 4, s));
@@ -1049,7 +1161,7 @@ int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *
                                                                    w.counts, w.plist, w.inv);
   B2_CUDA(cudaGetLastError());
   GemmParams g;
-  k_gather_x<<<4 * g_num_sms, 256, 0, s>>>(9 * T, w.offsets, w.plist, x16, w.x16p);
+  k_gather_x<<<4 * g_num_sms, 256, 0, s>>>(9 * T, w.offsets, w.plist, x16, x16_pitch, w.x16p);
   B2_CUDA(cudaGetLastError());
   rc = gemm_maps(1, L, w.x16p, w.s16, w.y, T, g.m);
   if (rc) return rc;
@@ -1154,6 +1266,61 @@ int b200moe_prefill_status(const void *ws, int T, int *status, void *stream) {
   PrefillWS w = carve_prefill(const_cast<void *>(ws), T);
   B2_CUDA(cudaMemcpyAsync(status, w.err, 4, cudaMemcpyDeviceToHost, (cudaStream_t)stream));
   B2_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  return B200MOE_OK;
+}
+
+int b200moe_ep_pack(const void *x16, const int32_t *ids, const uint16_t *w_bf16, int T, int rank, int world,
+                    void *send_rows, int32_t *pos, void *stream) {
+  if (T <= 0 || T > kMaxTPrefill) return b2host::set_error(B200MOE_EINVAL, "ep_pack: T=%d outside [1, %d]", T, kMaxTPrefill);
+  if (world < 1 || world > kE || kE % world || rank < 0 || rank >= world)
+    return b2host::set_error(B200MOE_EINVAL, "ep_pack: rank %d / world %d (world must divide 256)", rank, world);
+  if (!x16 || !ids || !w_bf16 || !send_rows || !pos)
+    return b2host::set_error(B200MOE_EINVAL, "ep_pack: x16, ids, w_bf16, send_rows and pos are required");
+  if (!a16(x16) || !a16(ids) || !a16(w_bf16) || !a16(send_rows))
+    return b2host::set_error(B200MOE_EINVAL, "ep_pack: pointers must be 16-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  k_ep_plan<<<world, 1024, 0, s>>>(T, ids, w_bf16, rank, world, (uint8_t *)send_rows, pos);
+  B2_CUDA(cudaGetLastError());
+  k_ep_copy<<<T, 256, 0, s>>>(T, (const __half *)x16, world, pos, (uint8_t *)send_rows);
+  B2_CUDA(cudaGetLastError());
+  return B200MOE_OK;
+}
+
+int b200moe_ep_experts(const void *recv_rows, int T, int rank, int world, const float *sg, const b200moe_layer *L,
+                       float *partial, void *ws, size_t ws_bytes, void *stream) {
+  if (world < 1 || world > kE || kE % world || rank < 0 || rank >= world)
+    return b2host::set_error(B200MOE_EINVAL, "ep_experts: rank %d / world %d (world must divide 256)", rank, world);
+  const int64_t R = (int64_t)world * T;
+  if (T <= 0 || R > kMaxTPrefill)
+    return b2host::set_error(B200MOE_EINVAL, "ep_experts: world x T = %lld outside [1, %d]", (long long)R, kMaxTPrefill);
+  if (!recv_rows || !sg || !partial || !ws)
+    return b2host::set_error(B200MOE_EINVAL, "ep_experts: recv_rows, sg, partial and ws are required");
+  if (!a16(recv_rows) || !a16(partial) || !a16(ws))
+    return b2host::set_error(B200MOE_EINVAL, "ep_experts: pointers must be 16-byte aligned");
+  if (ws_bytes < prefill_ws_bytes((int)R))
+    return b2host::set_error(B200MOE_ESIZE, "ep_experts: workspace %zu B < required %zu B (world x T rows)", ws_bytes,
+                             prefill_ws_bytes((int)R));
+  int rc = check_prefill_layer(L, "ep_experts");
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  const PrefillWS w = carve_prefill(ws, (int)R);
+  B2_CUDA(cudaMemsetAsync(w.err, 0, 4, s));
+  k_ep_unpack<<<(unsigned)((R + 255) / 256), 256, 0, s>>>((int)R, (const uint8_t *)recv_rows, w.ids, w.wb);
+  B2_CUDA(cudaGetLastError());
+  const int per = kE / world;
+  return experts_stage((const __half *)recv_rows, (int)R, w.ids, w.wb, rank * per, (rank + 1) * per, sg, rank * T,
+                       rank * T + T, L, partial, 0, w, s, kEpRowHalves);
+}
+
+int b200moe_ep_combine(const float *ret, const int32_t *pos, int T, int world, float *out, int accumulate,
+                       void *stream) {
+  if (T <= 0 || T > kMaxTPrefill || world < 1 || world > kE)
+    return b2host::set_error(B200MOE_EINVAL, "ep_combine: T=%d / world=%d out of range", T, world);
+  if (!ret || !pos || !out) return b2host::set_error(B200MOE_EINVAL, "ep_combine: ret, pos and out are required");
+  if (!a16(ret) || !a16(out)) return b2host::set_error(B200MOE_EINVAL, "ep_combine: pointers must be 16-byte aligned");
+  const int64_t n = (int64_t)T * (kH / 4);
+  k_ep_sum<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(T, world, ret, pos, out, accumulate);
+  B2_CUDA(cudaGetLastError());
   return B200MOE_OK;
 }
 

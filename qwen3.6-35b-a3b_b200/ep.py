@@ -1,28 +1,31 @@
-"""Expert parallelism for the prefill path: one process per GPU, torch.distributed over NCCL.
+"""Expert parallelism for the prefill / large-batch path: one process per GPU over NCCL.
 
 The 256 routed experts are split evenly over the W ranks of the group (256/128/64/32 per GPU at
-W = 1/2/4/8); router and shared expert are replicated. Every rank passes the same number of
-tokens T. For one layer, each rank:
+W = 1/2/4/8); router and shared expert are replicated. Every rank holds T tokens of its own (the
+same T everywhere). The reference runs the whole expert loop in one process
+(``engine/m3_forward.py:447-475``); here one layer is, on every rank:
 
-1. routes its own tokens (``b200moe_moe_route``: fp16 activations, ids, bf16 weights, gate);
-2. dispatch: ``all_gather`` of the fp16 rows, ids and weights -- every rank sees all W*T tokens;
-3. runs its experts on all of them in one ``b200moe_moe_experts`` call: the slots in its
-   expert range for every gathered token, plus the shared expert for its own tokens' rows (one
-   set of GEMM launches). The stage keeps only the slots in range, so each token costs GEMM
-   work on the ranks that own its experts and nothing elsewhere; one f32 partial row per
-   gathered token (its in-range slots summed in ascending expert id, + sg * shared on its own
-   rows, zero when it has none);
-4. combine: ``all_to_all_single`` with equal splits sends the partial rows of rank r's tokens
-   back to rank r, which adds the W partials per token in ascending rank order (ascending
-   expert ranges).
+1. route its own tokens (``b200moe_moe_route``: fp16 rows, ids, bf16 weights, shared gate);
+2. pack (``b200moe_ep_pack``): for each destination rank d, the tokens with at least one slot in
+   d's expert range -- each token once per destination, however many of its slots land there --
+   as dispatch rows (x, ids, weights) in ascending token order; every own token goes to the own
+   block, where the shared expert runs. ``pos[t][d]`` remembers each row's place;
+3. dispatch: one equal-split ``all_to_all_single`` of the [W][T] row blocks (block d to rank d);
+4. experts (``b200moe_ep_experts``): the received rows' slots in this rank's expert range through
+   the Q4_K grouped GEMMs (one set of launches for all sources), summed per row in ascending
+   expert id, plus the gated shared expert on the own block -> one f32 partial row per received
+   row (zero where a row has no work);
+5. combine: an equal-split ``all_to_all_single`` returns block s to rank s, which adds, per token,
+   the partial rows from d = 0, 1, ... in that order (``b200moe_ep_combine``: ascending expert
+   ranges, a fixed association).
 
-No host synchronisation: every size is known from T and W, so the whole layer is a fixed
-sequence of kernels and collectives (capturable in a CUDA graph). Deterministic: every
-addition has a fixed order. Relative to one GPU, only the association of the routed sum
-changes (per-rank partial sums, then the ranks in order).
+Sizes are fixed by T and W, so a step is a fixed sequence of kernels and collectives with no host
+synchronisation: it can be captured in a CUDA graph (buffers are allocated once per T and reused).
+Relative to one GPU only the association of the routed sum changes (per-rank partial sums, then
+the ranks in order), so the outputs agree to f32 rounding and the routing ids are identical.
 
-``route_fn`` / ``experts_fn`` can be replaced (the CPU tests run this exact dispatch/combine code
-on gloo ranks with oracle-backed stage functions).
+The stage functions can be replaced (the CPU tests run this exact sequence of collectives on gloo
+ranks with a host restatement of the three device stages).
 """
 from __future__ import annotations
 
@@ -31,6 +34,8 @@ import torch.distributed as dist
 
 from . import _abi
 from .geometry import E, H, RMS_EPS, TOPK
+
+ROW_BYTES = _abi.EP_ROW_BYTES
 
 
 def device_route_fn(layer, ws):
@@ -48,22 +53,43 @@ def device_route_fn(layer, ws):
     return route
 
 
+def device_pack_fn():
+    """``b200moe_ep_pack``: (send rows [W, T, ROW_BYTES] uint8, pos [T, W] int32)."""
+    def pack(x16, ids, wb, rank, world, send, pos):
+        _abi.ep_pack(x16, ids, wb, x16.shape[0], rank, world, send, pos)
+        return send, pos
+    return pack
+
+
 def device_experts_fn(layer, ws):
-    """``b200moe_moe_experts`` for pre-routed tokens, an expert range and the shared-expert rows
-    ``sh_rows`` = (lo, hi) (sg[t - lo] applies to row t; default all rows)."""
-    def experts(x16, ids, wb, e_lo, e_hi, sg, out, accumulate=False, sh_rows=None):
-        T = x16.shape[0]
-        if T == 0:
-            return out
-        _abi.moe_experts(x16, T, ids, wb, e_lo, e_hi, sg, layer.abi(), out, accumulate, ws(T), sh_rows=sh_rows)
-        return out
+    """``b200moe_ep_experts`` on the received rows (W > 1): partial [W, T, 2048] f32."""
+    def experts(recv, T, rank, world, sg, partial):
+        _abi.ep_experts(recv, T, rank, world, sg, layer.abi(), partial, ws(world * T))
+        return partial
     return experts
+
+
+def device_local_fn(layer, ws):
+    """W = 1: ``b200moe_moe_experts`` over every expert and the shared expert."""
+    def local(x16, ids, wb, sg, out, accumulate):
+        T = x16.shape[0]
+        _abi.moe_experts(x16, T, ids, wb, 0, E, sg, layer.abi(), out, accumulate, ws(T))
+        return out
+    return local
+
+
+def device_combine_fn():
+    def combine(ret, pos, T, world, out, accumulate):
+        _abi.ep_combine(ret, pos, T, world, out, accumulate)
+        return out
+    return combine
 
 
 class ExpertParallelMoE:
     """One MoE layer with its routed experts sharded over a process group."""
 
-    def __init__(self, layer, group=None, route_fn=None, experts_fn=None, device=None):
+    def __init__(self, layer, group=None, route_fn=None, pack_fn=None, experts_fn=None, combine_fn=None,
+                 local_fn=None, device=None):
         self.group = group
         grouped = dist.is_available() and dist.is_initialized()
         self.rank = dist.get_rank(group) if grouped else 0
@@ -79,44 +105,64 @@ class ExpertParallelMoE:
         self.layer = layer
         self.device = device if device is not None else layer.device
         self._ws = {}
+        self._bufs = {}
         self.route_fn = route_fn or device_route_fn(layer, self._workspace)
+        self.pack_fn = pack_fn or device_pack_fn()
         self.experts_fn = experts_fn or device_experts_fn(layer, self._workspace)
+        self.combine_fn = combine_fn or device_combine_fn()
+        self.local_fn = local_fn or device_local_fn(layer, self._workspace)
 
-    def _workspace(self, T):
-        need = _abi.prefill_workspace_size(max(T, 1))
+    def _workspace(self, rows):
+        need = _abi.prefill_workspace_size(max(rows, 1))
         ws = self._ws.get("ws")
         if ws is None or ws.numel() < need:
             ws = torch.empty(need, dtype=torch.uint8, device=self.device)
             self._ws["ws"] = ws
         return ws
 
-    def forward(self, x=None, resid=None):
+    def workspace(self, T):
+        """The prefill workspace the expert stage uses (its status word: ``prefill_status``)."""
+        return self._workspace(self.world * T if self.world > 1 else T)
+
+    def buffers(self, T):
+        """The step's fixed-size buffers for T tokens per rank (allocated once, reused)."""
+        b = self._bufs.get(T)
+        if b is None:
+            W, dev = self.world, self.device
+            b = dict(send=torch.empty((W, T, ROW_BYTES), dtype=torch.uint8, device=dev),
+                     recv=torch.empty((W, T, ROW_BYTES), dtype=torch.uint8, device=dev),
+                     pos=torch.empty((T, W), dtype=torch.int32, device=dev),
+                     partial=torch.empty((W, T, H), dtype=torch.float32, device=dev),
+                     ret=torch.empty((W, T, H), dtype=torch.float32, device=dev))
+            self._bufs[T] = b
+        return b
+
+    def forward(self, x=None, resid=None, out=None, mark=None):
         """``x`` [T, 2048] (bf16/f32) -> (out [T, 2048] f32, ids [T, 8]); T is the same on every
-        rank. With ``resid`` instead of ``x``: routes rmsnorm(resid) and returns resid + out."""
+        rank. With ``resid`` instead of ``x``: routes rmsnorm(resid) and adds the block output to
+        resid in place (returned). ``mark(stage)`` (optional) is called after each stage is
+        enqueued: route, dispatch, experts, combine, sum."""
+        mark = mark or (lambda stage: None)
         x16, ids, wb, sg = self.route_fn(x, resid) if resid is not None else self.route_fn(x)
+        mark("route")
         T = x16.shape[0]
         W = self.world
-        out = torch.zeros((T, H), dtype=torch.float32, device=self.device)
+        dst = resid if resid is not None else (out if out is not None else
+                                               torch.empty((T, H), dtype=torch.float32, device=self.device))
+        acc = resid is not None
         if W == 1:  # every expert is local: routed + shared in one stage call
-            self.experts_fn(x16, ids, wb, 0, E, sg, out)
-        else:
-            # dispatch: all tokens to every rank (rows travel as raw bytes: every backend moves
-            # uint8, not every one moves fp16)
-            xg = torch.empty((W * T, H), dtype=x16.dtype, device=self.device)
-            ig = torch.empty((W * T, TOPK), dtype=ids.dtype, device=self.device)
-            wg = torch.empty((W * T, TOPK), dtype=wb.dtype, device=self.device)
-            for dst, src in ((xg, x16), (ig, ids), (wg, wb)):
-                dist.all_gather_into_tensor(dst.view(torch.uint8), src.contiguous().view(torch.uint8),
-                                            group=self.group)
-            partial = torch.empty((W * T, H), dtype=torch.float32, device=self.device)
-            own = (self.rank * T, (self.rank + 1) * T)  # this rank's rows get sg * shared expert
-            self.experts_fn(xg, ig, wg, self.e_lo, self.e_hi, sg, partial, sh_rows=own)
-            back = torch.empty((W, T, H), dtype=torch.float32, device=self.device)
-            dist.all_to_all_single(back.view(torch.uint8), partial.view(torch.uint8), group=self.group)
-            out = back[0].clone()
-            for r in range(1, W):  # ascending rank = ascending expert range
-                out += back[r]
-        if resid is not None:
-            resid += out
-            return resid, ids
-        return out, ids
+            self.local_fn(x16, ids, wb, sg, dst, acc)
+            for st in ("dispatch", "experts", "combine", "sum"):
+                mark(st)
+            return dst, ids
+        b = self.buffers(T)
+        self.pack_fn(x16, ids, wb, self.rank, W, b["send"], b["pos"])
+        dist.all_to_all_single(b["recv"], b["send"], group=self.group)
+        mark("dispatch")
+        self.experts_fn(b["recv"], T, self.rank, W, sg, b["partial"])
+        mark("experts")
+        dist.all_to_all_single(b["ret"].view(torch.uint8), b["partial"].view(torch.uint8), group=self.group)
+        mark("combine")
+        self.combine_fn(b["ret"], b["pos"], T, W, dst, acc)
+        mark("sum")
+        return dst, ids

@@ -1,9 +1,11 @@
 """Expert-parallel dispatch / combine host logic on CPU gloo ranks (world sizes 2 and 4).
 
 The ranks run b200moe.ep.ExpertParallelMoE unchanged, with CPU stage functions: the declared
-router from the C oracle, and a cheap synthetic expert body (o_e(x) = x * (1 + e/256) + e/64,
-shared = x / 2), so the test exercises exactly the token selection, masking, count exchange,
-all_to_all_single row traffic and the ascending-rank combine. The reference runs the same stage
+router from the C oracle, host restatements of the dispatch-row pack, the receiver's expert stage
+and the ordered combine (the row format of b200moe_ep_pack / b200moe_ep_experts /
+b200moe_ep_combine), and a cheap synthetic expert body (o_e(x) = x * (1 + e/256) + e/64,
+shared = x / 2), so the test exercises exactly the per-destination token selection, the two
+equal-split all_to_all_single exchanges and the ascending-rank combine. The reference runs the same stage
 functions on all tokens in one process; only the association of the routed sum differs.
 """
 import os
@@ -44,7 +46,7 @@ def _stage_fns():
         return (torch.from_numpy(xf.astype(np.float16)), torch.from_numpy(r["ids"].astype(np.int32)),
                 torch.from_numpy(r["w_bf16"].view(np.int16).copy()), torch.from_numpy(sg))
 
-    def experts(x16, ids, wb, e_lo, e_hi, sg, out, accumulate=False, sh_rows=None):
+    def body(x16, ids, wb, e_lo, e_hi, sg, out, accumulate=False, sh_rows=None):
         x = x16.numpy().astype(np.float64)
         idn = ids.numpy()
         w = bf16_bits_to_f32(wb.numpy().view(np.uint16)).astype(np.float64)
@@ -64,7 +66,58 @@ def _stage_fns():
             out.copy_(r32)
         return out
 
-    return route, experts
+    return route, body
+
+
+def _ep_stage_fns():
+    """Host restatements of the three device stages of expert parallelism over the dispatch row
+    format (b200moe_ep_pack / b200moe_ep_experts / b200moe_ep_combine), around the test body."""
+    route, body = _stage_fns()
+    row = 4160
+
+    def pack(x16, ids, wb, rank, world, send, pos):
+        T = x16.shape[0]
+        per = 256 // world
+        sv, idn = send.numpy(), ids.numpy()
+        pos.fill_(-1)
+        for d in range(world):
+            p = 0
+            for t in range(T):
+                if d == rank or ((idn[t] >= d * per) & (idn[t] < (d + 1) * per)).any():
+                    sv[d, p, :4096] = x16[t].numpy().view(np.uint8)
+                    sv[d, p, 4096:4128] = idn[t].astype(np.int32).view(np.uint8)
+                    sv[d, p, 4128:4144] = wb[t].numpy().view(np.uint8)
+                    pos[t, d] = p
+                    p += 1
+            for q in range(p, T):
+                sv[d, q, 4096:4128] = np.full(8, -1, np.int32).view(np.uint8)
+        return send, pos
+
+    def experts(recv, T, rank, world, sg, partial):
+        rv = recv.numpy().reshape(world * T, row)
+        x16 = torch.from_numpy(rv[:, :4096].copy().view(np.float16))
+        ids = torch.from_numpy(rv[:, 4096:4128].copy().view(np.int32))
+        wb = torch.from_numpy(rv[:, 4128:4144].copy().view(np.int16))
+        per = 256 // world
+        out = torch.zeros((world * T, 2048), dtype=torch.float32)
+        body(x16, ids, wb, rank * per, (rank + 1) * per, sg, out, sh_rows=(rank * T, rank * T + T))
+        partial.copy_(out.reshape(world, T, 2048))
+        return partial
+
+    def combine(ret, pos, T, world, out, accumulate):
+        res = torch.zeros((T, 2048), dtype=torch.float32)
+        for t in range(T):
+            for d in range(world):
+                p = int(pos[t, d])
+                if p >= 0:
+                    res[t] += ret[d, p]
+        if accumulate:
+            out += res
+        else:
+            out.copy_(res)
+        return out
+
+    return route, pack, experts, combine
 
 
 def _tokens(world):
@@ -84,9 +137,10 @@ def _worker(rank, world, port, path):
         from conftest import _load_pkg
         _load_pkg()
         from b200moe.ep import ExpertParallelMoE
-        route, experts = _stage_fns()
+        route, pack, experts, combine = _ep_stage_fns()
         x = _tokens(world)[rank * T_PER_RANK:(rank + 1) * T_PER_RANK]
-        ep = ExpertParallelMoE(layer=None, route_fn=route, experts_fn=experts, device=torch.device("cpu"))
+        ep = ExpertParallelMoE(layer=None, route_fn=route, pack_fn=pack, experts_fn=experts, combine_fn=combine,
+                               device=torch.device("cpu"))
         out, ids = ep.forward(x)
         np.savez(path % rank, out=out.numpy(), ids=ids.numpy())
     finally:
@@ -101,11 +155,11 @@ def test_ep_dispatch_combine_matches_single_process(tmp_path, world):
     outs = [np.load(path % r) for r in range(world)]
     ep_out = np.concatenate([o["out"] for o in outs])
     ep_ids = np.concatenate([o["ids"] for o in outs])
-    route, experts = _stage_fns()
+    route, body = _stage_fns()
     x = _tokens(world)
     x16, ids, wb, sg = route(x)
     ref = torch.zeros((x.shape[0], 2048), dtype=torch.float32)
-    experts(x16, ids, wb, 0, 256, sg, ref)
+    body(x16, ids, wb, 0, 256, sg, ref)
     assert (ep_ids == ids.numpy()).all()
     rel = np.linalg.norm(ep_out - ref.numpy()) / np.linalg.norm(ref.numpy())
     assert rel < 1e-6, rel
@@ -140,9 +194,10 @@ def _worker_peer_lost(rank, world, port, path):
     from conftest import _load_pkg
     _load_pkg()
     from b200moe.ep import ExpertParallelMoE
-    route, experts = _stage_fns()
+    route, pack, experts, combine = _ep_stage_fns()
     x = _tokens(world)[:T_PER_RANK]
-    ep = ExpertParallelMoE(layer=None, route_fn=route, experts_fn=experts, device=torch.device("cpu"))
+    ep = ExpertParallelMoE(layer=None, route_fn=route, pack_fn=pack, experts_fn=experts, combine_fn=combine,
+                           device=torch.device("cpu"))
     t0 = time.monotonic()
     try:
         ep.forward(x)

@@ -55,18 +55,18 @@ def test_prefill_vs_oracle(cuda, layer3, T):
 
 
 def test_prefill_config3_4096(cuda, layer3):
-    """Config 3 size (4096 tokens; the shared expert spans 16 tiles of 256 tokens): ids for
-    every token, outputs on a seeded sample of 48 tokens, deterministic across runs."""
-    import torch
+    """Config 3 size (4096 tokens; the shared expert spans 16 tiles of 256 tokens): ids and
+    outputs for every token against the f64 oracle (the achieved margin is printed),
+    deterministic across runs."""
     from b200moe import synth
     xb = synth.tokens(3, 4096, stream=1)
     out, ids = _run(cuda, layer3, xb)
     out2, ids2 = _run(cuda, layer3, xb)
     assert (ids == ids2).all() and np.array_equal(out, out2)
-    sample = np.sort(np.random.default_rng(0).choice(4096, 48, replace=False))
-    _check(xb, out, ids, host_layer(3, 0), sample)
+    c = _check(xb, out, ids, host_layer(3, 0))
+    print("config-3 prefill, all 4096 tokens: rel_l2 %.3e (bar %.0e), max_abs_norm %.3e (bar %.0e)"
+          % (c["rel_l2"], REL_L2, c["max_abs_norm"], MAX_ABS_NORM))
     assert np.isfinite(out).all()
-    del torch
 
 
 def test_prefill_matches_decode_routing_and_output(cuda, layer3):
