@@ -223,27 +223,30 @@ __global__ void __launch_bounds__(32 * kPrepWarps) k_prep(const void *x, int x_d
 }
 
 // ------------------------------------------------------------------------- k_router_gemm
-// CTA: 64 tokens x 64 experts, 128 threads; thread (ty, tx) owns tokens ty + 8i (i < 8) and
-// experts tx + 16j (j < 4): 32 outputs, 128 FMAs per 12 shared-memory vector loads. The K
-// chunks are double-buffered: chunk c+1's x rows arrive by cp.async and its weights are held in
-// registers while chunk c is multiplied.
+// CTA: kTM tokens x 64 experts, 128 threads; thread (ty, tx) owns tokens ty + 8i (i < kTM / 8)
+// and experts tx + 16j (j < 4): with kTM = 64, 32 outputs and 128 FMAs per 12 shared-memory
+// vector loads. Fewer tokens per CTA (kTM 32 or 16) give small batches (an expert-parallel
+// rank's share) enough CTAs to fill the SMs; every output is the same sequence of operations
+// whatever the tile. The K chunks are double-buffered: chunk c+1's x rows arrive by cp.async and
+// its weights are held in registers while chunk c is multiplied.
 constexpr int kRgPitch = 68;                                  // padded row pitch (floats)
 constexpr int kRgBuf = 64 * kRgPitch;                         // one 64 x 64 chunk
 constexpr size_t kRgSmem = (size_t)4 * kRgBuf * sizeof(float);  // x and w, two buffers each
 
-template <bool kF32>
+template <bool kF32, int kTM>
 __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ xn, int T,
                                                      const void *__restrict__ wg_, const float *bias,
                                                      uint16_t *logits) {
+  constexpr int kTI = kTM / 8;  // tokens per thread
   const uint16_t *wg = reinterpret_cast<const uint16_t *>(wg_);  // bf16 router
   const float *wgf = reinterpret_cast<const float *>(wg_);        // f32 router (kF32)
   extern __shared__ __align__(16) float rg_smem[];
   float *xs = rg_smem, *wsm = rg_smem + 2 * kRgBuf;  // [2][64][kRgPitch] each
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-  const int t0 = blockIdx.x * 64, e0 = blockIdx.y * 64;
-  auto load_x = [&](int c, float *dst) {  // 64 rows x 64 floats by cp.async (zero rows past T)
+  const int t0 = blockIdx.x * kTM, e0 = blockIdx.y * 64;
+  auto load_x = [&](int c, float *dst) {  // kTM rows x 64 floats by cp.async (zero rows past T)
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 0; q < kTI; ++q) {
       const int idx = tid + 128 * q;  // 0..1023 float4 slots
       const int row = idx >> 4, col = (idx & 15) * 4;
       const bool in = t0 + row < T;
@@ -289,7 +292,7 @@ __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ x
     cp_async_wait_all();
     __syncthreads();
   }
-  float tot[8][4];
+  float tot[kTI][4];
   for (int c = 0; c < 32; ++c) {
     const int buf = c & 1;
     uint4 un[8];
@@ -298,20 +301,20 @@ __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ x
       load_w(c + 1, un);
     }
     const float *xb = xs + buf * kRgBuf, *wb = wsm + buf * kRgBuf;
-    float acc[8][4];
+    float acc[kTI][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < kTI; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
 #pragma unroll 2
     for (int k = 0; k < 64; k += 4) {  // the chunk's 64 products of every output, in k order
-      float4 xa[8], wa[4];
+      float4 xa[kTI], wa[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) xa[i] = *reinterpret_cast<const float4 *>(xb + (ty + 8 * i) * kRgPitch + k);
+      for (int i = 0; i < kTI; ++i) xa[i] = *reinterpret_cast<const float4 *>(xb + (ty + 8 * i) * kRgPitch + k);
 #pragma unroll
       for (int j = 0; j < 4; ++j) wa[j] = *reinterpret_cast<const float4 *>(wb + (tx + 16 * j) * kRgPitch + k);
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < kTI; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           acc[i][j] = __fmaf_rn(xa[i].x, wa[j].x, acc[i][j]);
@@ -321,7 +324,7 @@ __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ x
         }
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < kTI; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) tot[i][j] = (c == 0) ? acc[i][j] : __fadd_rn(tot[i][j], acc[i][j]);
     if (c + 1 < 32) {
@@ -331,7 +334,7 @@ __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ x
     __syncthreads();  // the next chunk is in place; this chunk's buffers may be refilled
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < kTI; ++i) {
     const int t = t0 + ty + 8 * i;
     if (t >= T) continue;
 #pragma unroll
@@ -987,8 +990,12 @@ int ensure_gemm_attrs() {
   if (done) return B200MOE_OK;
   B2_CUDA(cudaFuncSetAttribute(k_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<1>::kSmem));
   B2_CUDA(cudaFuncSetAttribute(k_gemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<2>::kSmem));
-  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
-  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
+  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<false, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
+  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<true, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
+  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<false, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
+  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<true, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
+  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<false, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
+  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<true, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
   int dev = 0;
   B2_CUDA(cudaGetDevice(&dev));
   B2_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
@@ -1122,6 +1129,27 @@ int check_prefill_layer(const b200moe_layer *L, const char *who, bool experts = 
   return B200MOE_OK;
 }
 
+// The router GEMM with the largest token tile that still gives every SM a CTA.
+template <bool kF32>
+cudaError_t launch_router_gemm_t(const float *xn, int T, const void *wg, const float *bias, uint16_t *logits,
+                                 cudaStream_t s) {
+  const int want = g_num_sms > 0 ? g_num_sms : 148;
+  auto ctas = [&](int tm) { return ((T + tm - 1) / tm) * (kE / 64); };
+  if (ctas(64) >= want)
+    k_router_gemm<kF32, 64><<<dim3((T + 63) / 64, kE / 64), 128, kRgSmem, s>>>(xn, T, wg, bias, logits);
+  else if (ctas(32) >= want)
+    k_router_gemm<kF32, 32><<<dim3((T + 31) / 32, kE / 64), 128, kRgSmem, s>>>(xn, T, wg, bias, logits);
+  else
+    k_router_gemm<kF32, 16><<<dim3((T + 15) / 16, kE / 64), 128, kRgSmem, s>>>(xn, T, wg, bias, logits);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_router_gemm(bool f32, const float *xn, int T, const void *wg, const float *bias, uint16_t *logits,
+                               cudaStream_t s) {
+  return f32 ? launch_router_gemm_t<true>(xn, T, wg, bias, logits, s)
+             : launch_router_gemm_t<false>(xn, T, wg, bias, logits, s);
+}
+
 // Route stage: x (or rmsnorm(resid)) -> x16, ids, wb, sg (each to the given pointer).
 int route_stage(const void *x, int x_dtype, const float *resid, float eps, int T, const b200moe_layer *L,
                 __half *x16, int32_t *ids, uint16_t *wb, float *sg, const PrefillWS &w, cudaStream_t s) {
@@ -1132,13 +1160,7 @@ int route_stage(const void *x, int x_dtype, const float *resid, float eps, int T
                                                                    L->router_f32, resid ? L->norm_w : nullptr,
                                                                    w.xn, x16, sg, w.err);
   B2_CUDA(cudaGetLastError());
-  if (L->router_f32)
-    k_router_gemm<true><<<dim3((T + 63) / 64, kE / 64), 128, kRgSmem, s>>>(w.xn, T, L->router_w, L->logit_bias,
-                                                                           w.logits);
-  else
-    k_router_gemm<false><<<dim3((T + 63) / 64, kE / 64), 128, kRgSmem, s>>>(w.xn, T, L->router_w, L->logit_bias,
-                                                                            w.logits);
-  B2_CUDA(cudaGetLastError());
+  B2_CUDA(launch_router_gemm(L->router_f32 != 0, w.xn, T, L->router_w, L->logit_bias, w.logits, s));
   k_route_tok<<<(T + 7) / 8, 256, 0, s>>>(w.logits, T, ids, wb);
   B2_CUDA(cudaGetLastError());
   return B200MOE_OK;

@@ -193,3 +193,28 @@ def test_block_stages_match_oracle_stages(cuda, layer3):
         assert c["rel_l2"] < REL_L2 and c["max_abs_norm"] < MAX_ABS_NORM, ("expert_raw", k, c)
     g = st["shared_gate_prob"].reshape(T).cpu().numpy().astype(np.float64)
     assert np.max(np.abs(g - ref["shared_gate_prob"])) < 1e-6
+
+
+@pytest.mark.parametrize("T", [300, 2048, 4096])
+def test_route_stage_every_router_tile(cuda, layer3, T):
+    """The prefill router GEMM picks its token tile (64, 32 or 16 tokens per CTA) by batch size,
+    so an expert-parallel rank's share fills the SMs too: 300 tokens take the 16-token tile, 2048
+    the 32-token one, 4096 the 64-token one. Each output is the same declared sequence of
+    operations, so ids and R5 weights are bit-exact against the C restatement at every tile."""
+    import torch
+    from oracle import moe as OM
+    from oracle.bf16 import bf16_bits_to_f32
+    from b200moe import _abi, synth
+    from b200moe.geometry import RMS_EPS
+    xb = synth.tokens(3, T, stream=12)
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).to(cuda)
+    x16 = torch.empty((T, 2048), dtype=torch.float16, device=cuda)
+    ids = torch.empty((T, 8), dtype=torch.int32, device=cuda)
+    wb = torch.empty((T, 8), dtype=torch.int16, device=cuda)
+    sg = torch.empty((T,), dtype=torch.float32, device=cuda)
+    ws = torch.empty(_abi.prefill_workspace_size(T), dtype=torch.uint8, device=cuda)
+    _abi.moe_route(x, _abi.BF16, None, RMS_EPS, T, layer3.abi(), x16, ids, wb, sg, ws)
+    torch.cuda.synchronize()
+    r = OM.router(bf16_bits_to_f32(xb), host_layer(3, 0).wg)
+    assert (ids.cpu().numpy() == r["ids"]).all()
+    assert (wb.cpu().numpy().view(np.uint16) == r["w_bf16"]).all()
