@@ -151,8 +151,9 @@ class ExpertParallelMoE:
                                                torch.empty((T, H), dtype=torch.float32, device=self.device))
         acc = resid is not None
         if W == 1:  # every expert is local: routed + shared in one stage call
+            mark("dispatch")
             self.local_fn(x16, ids, wb, sg, dst, acc)
-            for st in ("dispatch", "experts", "combine", "sum"):
+            for st in ("experts", "combine", "sum"):
                 mark(st)
             return dst, ids
         b = self.buffers(T)

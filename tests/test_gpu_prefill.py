@@ -133,21 +133,20 @@ def test_expert_ranges_as_in_expert_parallelism(cuda, layer3, W):
     sum of the W partial rows in ascending rank order must equal the single-call prefill
     (rel-L2 1e-5: only the association of the routed sum differs)."""
     import torch
-    from b200moe import moe, synth
-    from b200moe.ep import device_experts_fn, device_route_fn
+    from b200moe import _abi, moe, synth
+    from b200moe.ep import device_route_fn
     T = 512
     xb = synth.tokens(3, T, stream=5)
     x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).to(cuda)
     ref, info = moe.moe_block(x, layer3, 0, path="prefill")
     ws = lambda n: moe.prefill_workspace(n, cuda)
     x16, ids, wb, sg = device_route_fn(layer3, ws)(x)
-    experts = device_experts_fn(layer3, ws)
     Tr = T // W
     out = None
     for r in range(W):
         part = torch.empty((T, 2048), dtype=torch.float32, device=cuda)
-        experts(x16, ids, wb, 256 * r // W, 256 * (r + 1) // W, sg[r * Tr:(r + 1) * Tr], part,
-                sh_rows=(r * Tr, (r + 1) * Tr))
+        _abi.moe_experts(x16, T, ids, wb, 256 * r // W, 256 * (r + 1) // W, sg[r * Tr:(r + 1) * Tr], layer3.abi(),
+                         part, False, ws(T), sh_rows=(r * Tr, (r + 1) * Tr))
         out = part if out is None else out + part
     torch.cuda.synchronize()
     assert moe.prefill_status(T, cuda) == 0
