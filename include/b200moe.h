@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define B200MOE_ABI_VERSION 3
+#define B200MOE_ABI_VERSION 4
 #define B200MOE_HIDDEN 2048
 #define B200MOE_EXPERTS 256
 #define B200MOE_TOPK 8
@@ -42,7 +42,8 @@ enum { B200MOE_F32 = 0, B200MOE_BF16 = 1 };
 
 /* GGML block type ids (as stored in GGUF tensor infos): b200moe_dequant's `type`, and
  * b200moe_layer.down_type / sh_type. */
-enum { B200MOE_TYPE_Q8_0 = 8, B200MOE_TYPE_Q4_K = 12, B200MOE_TYPE_Q5_K = 13, B200MOE_TYPE_Q6_K = 14 };
+enum { B200MOE_TYPE_Q8_0 = 8, B200MOE_TYPE_Q4_K = 12, B200MOE_TYPE_Q5_K = 13, B200MOE_TYPE_Q6_K = 14,
+       B200MOE_TYPE_BF16 = 30 };
 
 /* One MoE layer's device-resident weights. `gate_up_expert_stride` is the byte distance
  * between consecutive experts inside `gate` and `up`: 589,824 for the two separate GGUF
@@ -74,6 +75,14 @@ typedef struct b200moe_layer {
                                 format variant, or the gather-GEMV kernels): the grouped GEMMs
                                 (moe_prefill, moe_experts) take Q4_K and refuse such a layer
                                 (B200MOE_EINVAL) */
+    int32_t gate_type;       /* block type of `gate` / `up`: 0 or B200MOE_TYPE_Q4_K, or
+                                B200MOE_TYPE_BF16 for a dense layer as the Hugging Face checkpoint
+                                stores it -- then down_type and sh_type are B200MOE_TYPE_BF16 too:
+                                gate_up [256][1024][2048] (gate = rows 0..511 of each expert, up =
+                                rows 512..1023, gate_up_expert_stride 4 MiB), down [256][2048][512]
+                                (stride 2 MiB), shared gate / up [512][2048], shared down
+                                [2048][512]. A dense layer runs on the gather-GEMV decode kernels
+                                at every token count (speccheck/moe_ref.py's weights) */
 } b200moe_layer;
 
 /* ABI version (B200MOE_ABI_VERSION) and the last error message on this thread. */
@@ -125,6 +134,29 @@ size_t b200moe_decode_workspace_size(int T);
 int b200moe_moe_decode(const void *x, int x_dtype, int T, const b200moe_layer *layer,
                        float *out, int32_t *ids_out, uint16_t *w_out, void *ws,
                        size_t ws_bytes, void *stream);
+
+/* Stage outputs of b200moe_moe_decode_stages; every pointer may be NULL. */
+typedef struct b200moe_stages {
+    int32_t bf16_stages;      /* 1 (dense BF16 layer and bf16 x only): round where
+                                 speccheck/moe_ref.py's "ref" form rounds -- the F.linear outputs
+                                 (router logits, gate, up, expert and shared outputs, shared gate
+                                 pre-sigmoid), silu, the SwiGLU product, each weighted product, the
+                                 running routed sum (ascending expert id), the gated shared output
+                                 and the block output; 0: f32 throughout, as b200moe_moe_decode */
+    uint16_t *router_logits;  /* [T][256] bf16 */
+    float *expert_raw;        /* [T][8][2048] each slot's expert output before weighting, top-k order */
+    float *routed_sum;        /* [T][2048] */
+    float *shared_raw;        /* [T][2048] the shared expert's output before its gate */
+    float *shared_gate;       /* [T] sigmoid(w_sg . x) */
+} b200moe_stages;
+
+/* b200moe_moe_decode on the gather-GEMV kernels with the block's stage tensors written out, for
+ * stage-level parity gates. Replaces speccheck/moe_ref.py:499 moe_block (its stage dictionary:
+ * router_logits, expert_raw, routed_sum, shared_raw, shared_gate_prob, shared_out, combined_out)
+ * on dense BF16 weights, and the stage keys of engine/block_forward.py:670 moe_block. */
+int b200moe_moe_decode_stages(const void *x, int x_dtype, int T, const b200moe_layer *layer,
+                              const b200moe_stages *st, float *out, int32_t *ids_out, uint16_t *w_out,
+                              void *ws, size_t ws_bytes, void *stream);
 
 /* Largest token count b200moe_moe_decode_noalloc accepts. */
 #define B200MOE_NOALLOC_MAX_T 16

@@ -120,9 +120,11 @@ class HostLayer:
     blocks in their own sizes.
     """
 
-    def __init__(self, block_fn, wg, wsg, bias=None, types=None, norm_w=None):
+    def __init__(self, block_fn, wg, wsg, bias=None, types=None, norm_w=None, bf16_weights=False):
         self._block_fn = block_fn     # (kind, first_block, nblocks) -> uint8 [n, block bytes]
         self.types = dict(types or {})
+        # the dense layout: every expert / shared matrix holds the bf16 rounding (RNE) of its decode
+        self.bf16_weights = bool(bf16_weights)
         # post-attention RMSNorm weight as stored (Form A: 1 + w), f32 [2048]; None = 1
         self.norm_w = None if norm_w is None else np.asarray(norm_w, dtype=np.float32).reshape(H)
         keep = lambda a: np.asarray(a) if np.asarray(a).dtype == np.float32 else np.asarray(a, np.uint16)  # noqa
@@ -139,7 +141,11 @@ class HostLayer:
         per = rows * cols // kquants.BLOCK_ELTS[tname]
         first = 0 if kind.startswith("sh_") else e * per
         blocks = self._block_fn(kind, first, per)
-        return kquants.dequant(np.ascontiguousarray(blocks).tobytes(), tname, per).reshape(rows, cols)
+        m = kquants.dequant(np.ascontiguousarray(blocks).tobytes(), tname, per).reshape(rows, cols)
+        if self.bf16_weights:
+            from .bf16 import round_bf16
+            m = round_bf16(m).reshape(rows, cols)
+        return m
 
 
 def silu64(z):

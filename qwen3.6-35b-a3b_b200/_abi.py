@@ -20,7 +20,7 @@ F32, BF16 = 0, 1
 EXPORTS = ("b200moe_abi_version", "b200moe_last_error", "b200moe_q4k_dequant", "b200moe_dequant",
            "b200moe_synth_q4k", "b200moe_router_workspace_size", "b200moe_router",
            "b200moe_decode_workspace_size",
-           "b200moe_moe_decode", "b200moe_moe_decode_noalloc", "b200moe_decode_status",
+           "b200moe_moe_decode", "b200moe_moe_decode_stages", "b200moe_moe_decode_noalloc", "b200moe_decode_status",
            "b200moe_decode_noalloc_status", "b200moe_debug_decode_faults", "b200moe_decode_persistent_info",
            "b200moe_decode_persistent_formats",
            "b200moe_stack_workspace_size",
@@ -47,7 +47,14 @@ class Layer(ctypes.Structure):
                 ("sh_down", ctypes.c_void_p), ("router_w", ctypes.c_void_p),
                 ("sh_gate_w", ctypes.c_void_p), ("logit_bias", ctypes.c_void_p),
                 ("router_f32", ctypes.c_int32), ("norm_w", ctypes.c_void_p),
-                ("down_type", ctypes.c_int32), ("sh_type", ctypes.c_int32)]
+                ("down_type", ctypes.c_int32), ("sh_type", ctypes.c_int32), ("gate_type", ctypes.c_int32)]
+
+
+class Stages(ctypes.Structure):
+    """``struct b200moe_stages``."""
+    _fields_ = [("bf16_stages", ctypes.c_int32), ("router_logits", ctypes.c_void_p),
+                ("expert_raw", ctypes.c_void_p), ("routed_sum", ctypes.c_void_p),
+                ("shared_raw", ctypes.c_void_p), ("shared_gate", ctypes.c_void_p)]
 
 
 _LIB = None
@@ -81,6 +88,9 @@ def lib():
         L.b200moe_decode_workspace_size.argtypes = [i32]
         L.b200moe_moe_decode.restype = i32
         L.b200moe_moe_decode.argtypes = [vp, i32, i32, ctypes.POINTER(Layer), vp, vp, vp, vp, sz, vp]
+        L.b200moe_moe_decode_stages.restype = i32
+        L.b200moe_moe_decode_stages.argtypes = [vp, i32, i32, ctypes.POINTER(Layer), ctypes.POINTER(Stages), vp, vp,
+                                                vp, vp, sz, vp]
         L.b200moe_moe_decode_noalloc.restype = i32
         L.b200moe_moe_decode_noalloc.argtypes = [vp, i32, i32, ctypes.POINTER(Layer), vp, vp, vp, vp]
         L.b200moe_decode_status.restype = i32
@@ -193,6 +203,19 @@ def moe_decode(x, x_dtype: int, T: int, layer: Layer, out, ids_out, w_out, ws, s
     _check("b200moe_moe_decode",
            lib().b200moe_moe_decode(ptr(x), x_dtype, T, ctypes.byref(layer), ptr(out), ptr(ids_out),
                                     ptr(w_out), ptr(ws), ws.numel() * ws.element_size(), _stream(stream)))
+
+
+def moe_decode_stages(x, x_dtype: int, T: int, layer: Layer, bf16_stages: bool, out, ids_out, w_out, ws,
+                      router_logits=None, expert_raw=None, routed_sum=None, shared_raw=None, shared_gate=None,
+                      stream=None):
+    """``b200moe_moe_decode_stages``: the decode path with its stage tensors written out."""
+    p = lambda t: None if t is None else ptr(t).value  # noqa: E731
+    st = Stages(1 if bf16_stages else 0, p(router_logits), p(expert_raw), p(routed_sum), p(shared_raw),
+                p(shared_gate))
+    _check("b200moe_moe_decode_stages",
+           lib().b200moe_moe_decode_stages(ptr(x), x_dtype, T, ctypes.byref(layer), ctypes.byref(st), ptr(out),
+                                           ptr(ids_out), ptr(w_out), ptr(ws), ws.numel() * ws.element_size(),
+                                           _stream(stream)))
 
 
 def decode_persistent_info():

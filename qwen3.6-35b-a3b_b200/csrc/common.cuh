@@ -34,6 +34,10 @@ __device__ __forceinline__ uint16_t f2bf(float f) {  // RNE, canonical NaN
   return (uint16_t)(u >> 16);
 }
 
+__device__ __forceinline__ float bf16r(float f) {  // f rounded to bf16 precision (RNE), as f32
+  return __uint_as_float((uint32_t)f2bf(f) << 16);
+}
+
 __device__ __forceinline__ float f16f(uint32_t h) {  // exact widening
   return __half2float(__ushort_as_half((unsigned short)(h & 0xFFFFu)));
 }

@@ -48,6 +48,7 @@ struct K1Params {
   uint16_t *logits;      // [T][256]
   float *sg;             // [T]
   uint32_t *status;      // decode status word to clear (the call's first router launch), or NULL
+  int bf16_stages;       // 1: the shared gate as speccheck/moe_ref.py's "ref" form rounds it
 };
 
 // R1's declared order for one value: lane L holds chunk L's sequential sum; the 32 chunk
@@ -153,8 +154,10 @@ __global__ void __launch_bounds__(128) k_router(K1Params P) {
     if (gate_cta) {  // shared-expert gate: any summation order (tolerance-checked)
 #pragma unroll
       for (int i = 0; i < 64; ++i) acc = fmaf(v[i], wv[i], acc);
-      const float z = warp_sum(acc);
-      if (lane == 0) P.sg[t] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+      float z = warp_sum(acc);
+      if (P.bf16_stages) z = bf16r(z);  // F.linear in bf16, then sigmoid rounded to bf16
+      const float g = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-z)));
+      if (lane == 0) P.sg[t] = P.bf16_stages ? bf16r(g) : g;
       continue;
     }
 #pragma unroll
@@ -195,6 +198,7 @@ struct K2Params {
   const uint16_t *logits;
   const float *xw;
   float *s;
+  int bf16_stages;  // dense layers: round gate, up, silu(gate) and s to bf16 (moe_ref "ref" form)
 };
 
 // The 8 loads (gate/up x two chunks x {header, quants}) of one row-pair for this lane.
@@ -273,6 +277,52 @@ __global__ void __launch_bounds__(128) k_gateup(K2Params P) {
   }
 }
 
+// Dense (BF16) gate/up rows -- a layer as the Hugging Face checkpoint stores it (fused
+// gate_up [E][1024][2048]: gate = rows 0..511 of an expert, up = rows 512..1023). Same grid and
+// lane split as k_gateup; rows are read straight from global memory (each lane's two chunks are
+// 128 B per row). With bf16_stages the values round where speccheck/moe_ref.py's "ref" form
+// rounds them: F.linear outputs (gate, up), F.silu's output and the product.
+__global__ void __launch_bounds__(128) k_gateup_dense(K2Params P) {
+  __shared__ Route rr;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x / kK2CtasPerToken, r = blockIdx.x % kK2CtasPerToken;
+  const int k = r / kK2CtasPerSlot;
+  const int jbase = (r % kK2CtasPerSlot) * kK2RowsPerCta + warp * kK2RowsPerWarp;
+  const int kb0 = lane >> 3, cc = lane & 7;
+  constexpr int64_t kRow = row_bytes(B200MOE_TYPE_BF16, kH);
+  pdl_wait();
+  pdl_trigger();
+  const uint8_t *gb = P.sh_gate, *ub = P.sh_up;
+  if (k < kK) {  // routed: R2..R5 from the logits (one warp), then this CTA's expert
+    if (warp == 0) route_warp(P.logits + (size_t)t * kE, &rr);
+    __syncthreads();
+    const int e = rr.ids[k];
+    gb = P.gate + (size_t)e * P.stride;
+    ub = P.up + (size_t)e * P.stride;
+  }
+  XChunk X0, X1;
+  load_xchunk(P.xw + (size_t)t * kH, kb0, cc, X0);
+  load_xchunk(P.xw + (size_t)t * kH, kb0 + 4, cc, X1);
+  float *sdst = P.s + ((size_t)t * 9 + k) * kI + jbase;
+#pragma unroll 1
+  for (int jj = 0; jj < kK2RowsPerWarp; ++jj) {
+    const uint8_t *rg = gb + (size_t)(jbase + jj) * kRow, *ru = ub + (size_t)(jbase + jj) * kRow;
+    float g = bf16_chunk_dot(rg, kb0, cc, X0) + bf16_chunk_dot(rg, kb0 + 4, cc, X1);
+    float u = bf16_chunk_dot(ru, kb0, cc, X0) + bf16_chunk_dot(ru, kb0 + 4, cc, X1);
+    g = warp_sum(g);
+    u = warp_sum(u);
+    if (lane == 0) {
+      if (P.bf16_stages) {
+        g = bf16r(g);
+        u = bf16r(u);
+        sdst[jj] = bf16r(__fmul_rn(bf16r(silu_f(g)), u));
+      } else {
+        sdst[jj] = __fmul_rn(silu_f(g), u);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------------- K3
 constexpr int kK3Rows = 8;                       // h rows per CTA
 constexpr int kK3CtasPerToken = kH / kK3Rows;    // 256
@@ -288,6 +338,12 @@ struct K3Params {
   int accumulate;  // 1: out += result (the residual stream)
   int32_t *ids_out;
   uint16_t *w_out;
+  int bf16_stages;     // dense layers: moe_ref's "ref" form -- expert outputs, every weighted
+                       // product, the running routed sum, the gated shared output and the block
+                       // output each rounded to bf16 (the sum in ascending expert id)
+  float *raw_out;      // [T][8][2048] each slot's expert output before weighting (top-k order), or NULL
+  float *routed_out;   // [T][2048] the routed sum, or NULL
+  float *shraw_out;    // [T][2048] the shared expert's output before its gate, or NULL
 };
 
 // kDn: block type of the routed down rows (Q4_K / Q5_K / Q6_K); kSh: of the shared down rows
@@ -333,15 +389,32 @@ __global__ void __launch_bounds__(288) k_down(K3Params P) {
   __syncthreads();
   if (threadIdx.x < kK3Rows) {
     const int hh = threadIdx.x;
-    float acc = 0.0f;
+    float acc = 0.0f, res, shraw = o[8][hh];
+    if (P.bf16_stages) {
+      shraw = bf16r(shraw);
 #pragma unroll
-    for (int i = 0; i < kK; ++i) {
-      const int slot = rr.order[i];
-      acc = __fadd_rn(acc, __fmul_rn(o[slot][hh], bf16f(rr.wb[slot])));
+      for (int i = 0; i < kK; ++i) {
+        const int slot = rr.order[i];
+        acc = bf16r(__fadd_rn(acc, bf16r(__fmul_rn(bf16r(o[slot][hh]), bf16f(rr.wb[slot])))));
+      }
+      res = bf16r(__fadd_rn(acc, bf16r(__fmul_rn(__ldcg(P.sg + t), shraw))));
+    } else {
+#pragma unroll
+      for (int i = 0; i < kK; ++i) {
+        const int slot = rr.order[i];
+        acc = __fadd_rn(acc, __fmul_rn(o[slot][hh], bf16f(rr.wb[slot])));
+      }
+      res = __fadd_rn(acc, __fmul_rn(__ldcg(P.sg + t), shraw));
     }
-    const float res = __fadd_rn(acc, __fmul_rn(__ldcg(P.sg + t), o[8][hh]));
     float *dst = P.out + (size_t)t * kH + h0 + hh;
     *dst = P.accumulate ? __fadd_rn(*dst, res) : res;
+    if (P.routed_out) P.routed_out[(size_t)t * kH + h0 + hh] = acc;
+    if (P.shraw_out) P.shraw_out[(size_t)t * kH + h0 + hh] = shraw;
+    if (P.raw_out) {
+#pragma unroll
+      for (int slot = 0; slot < kK; ++slot)
+        P.raw_out[((size_t)t * kK + slot) * kH + h0 + hh] = P.bf16_stages ? bf16r(o[slot][hh]) : o[slot][hh];
+    }
   }
   if (h0 == 0 && threadIdx.x < kK) {
     if (P.ids_out) P.ids_out[(size_t)t * kK + threadIdx.x] = rr.ids[threadIdx.x];
@@ -420,7 +493,19 @@ int check_layer(const b200moe_layer *L, const char *who) {
   if (!al16(L->gate) || !al16(L->up) || !al16(L->down) || !al16(L->sh_gate) || !al16(L->sh_up) ||
       !al16(L->sh_down) || !al16(L->router_w) || !al16(L->sh_gate_w))
     return b2host::set_error(B200MOE_EINVAL, "%s: weight pointers must be 16-byte aligned", who);
-  const int dt = layer_down_type(L), st = layer_sh_type(L);
+  const int dt = layer_down_type(L), st = layer_sh_type(L), gt = layer_gate_type(L);
+  if (gt == B200MOE_TYPE_BF16) {  // dense: every matrix BF16 as the checkpoint stores it
+    if (dt != B200MOE_TYPE_BF16 || st != B200MOE_TYPE_BF16)
+      return b2host::set_error(B200MOE_EINVAL, "%s: a dense (BF16) layer needs down_type and sh_type BF16(30), got %d / %d",
+                               who, L->down_type, L->sh_type);
+    if (L->gate_up_expert_stride < (int64_t)kI * row_bytes(B200MOE_TYPE_BF16, kH) || (L->gate_up_expert_stride & 15) ||
+        L->down_expert_stride < (int64_t)kH * row_bytes(B200MOE_TYPE_BF16, kI) || (L->down_expert_stride & 15))
+      return b2host::set_error(B200MOE_EINVAL, "%s: dense layer strides %lld / %lld too small or unaligned", who,
+                               (long long)L->gate_up_expert_stride, (long long)L->down_expert_stride);
+    return B200MOE_OK;
+  }
+  if (gt != B200MOE_TYPE_Q4_K)
+    return b2host::set_error(B200MOE_EINVAL, "%s: gate_type %d is not Q4_K(12) or BF16(30)", who, L->gate_type);
   if (dt != B200MOE_TYPE_Q4_K && dt != B200MOE_TYPE_Q5_K && dt != B200MOE_TYPE_Q6_K)
     return b2host::set_error(B200MOE_EINVAL, "%s: down_type %d is not Q4_K(12), Q5_K(13) or Q6_K(14)", who,
                              L->down_type);
@@ -457,13 +542,21 @@ K1Params k1_params(const void *x, int x_dtype, const float *resid, float eps, in
   return p;
 }
 
+// Stage outputs and the arithmetic form of b200moe_moe_decode_stages (NULL: plain decode).
+struct Stages {
+  int bf16;
+  float *raw, *routed, *shraw;
+};
+
 // One layer: K1 -> K2 -> K3 on stream s. x given (resid == NULL) or rmsnorm(resid).
 // `first`: K1 is the first launch of this API call -- its stream predecessor may be any
 // operation (a memcpy node in a captured graph), so it is launched without the PDL attribute.
 int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const b200moe_layer *L, float *out,
-              int32_t *ids_out, uint16_t *w_out, const DecodeWS &w, cudaStream_t s, bool first) {
+              int32_t *ids_out, uint16_t *w_out, const DecodeWS &w, cudaStream_t s, bool first,
+              const Stages *st = nullptr) {
   K1Params p1 = k1_params(x, x_dtype, resid, eps, T, L, w);
   if (first) p1.status = status_word(w);
+  p1.bf16_stages = st ? st->bf16 : 0;
   if (p1.wf32) B2_CUDA(launch(k_router<true>, (unsigned)kK1Ctas, 128, 0, s, !first, p1));
   else B2_CUDA(launch(k_router<false>, (unsigned)kK1Ctas, 128, 0, s, !first, p1));
   K2Params p2;
@@ -475,7 +568,10 @@ int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const 
   p2.logits = w.logits;
   p2.xw = w.xw;
   p2.s = w.s;
-  if (layer_sh_type(L) == B200MOE_TYPE_Q8_0)
+  p2.bf16_stages = st ? st->bf16 : 0;
+  if (layer_dense(L))
+    B2_CUDA(launch(k_gateup_dense, (unsigned)(T * kK2CtasPerToken), 32 * kK2Warps, 0, s, true, p2));
+  else if (layer_sh_type(L) == B200MOE_TYPE_Q8_0)
     B2_CUDA(launch(k_gateup<true>, (unsigned)(T * kK2CtasPerToken), 32 * kK2Warps, 0, s, true, p2));
   else
     B2_CUDA(launch(k_gateup<false>, (unsigned)(T * kK2CtasPerToken), 32 * kK2Warps, 0, s, true, p2));
@@ -490,6 +586,10 @@ int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const 
   p3.accumulate = resid ? 1 : 0;
   p3.ids_out = ids_out;
   p3.w_out = w_out;
+  p3.bf16_stages = st ? st->bf16 : 0;
+  p3.raw_out = st ? st->raw : nullptr;
+  p3.routed_out = st ? st->routed : nullptr;
+  p3.shraw_out = st ? st->shraw : nullptr;
   B2_CUDA(launch_down(L, (unsigned)(T * kK3CtasPerToken), s, p3));
   return B200MOE_OK;
 }
@@ -497,6 +597,7 @@ int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const 
 cudaError_t launch_down(const b200moe_layer *L, unsigned grid, cudaStream_t s, const K3Params &p) {
   constexpr int Q4 = B200MOE_TYPE_Q4_K, Q5 = B200MOE_TYPE_Q5_K, Q6 = B200MOE_TYPE_Q6_K, Q8 = B200MOE_TYPE_Q8_0;
   const int dt = layer_down_type(L);
+  if (layer_dense(L)) return launch(k_down<B200MOE_TYPE_BF16, B200MOE_TYPE_BF16>, grid, 288, 0, s, true, p);
   if (layer_sh_type(L) == Q8) {
     if (dt == Q5) return launch(k_down<Q5, Q8>, grid, 288, 0, s, true, p);
     if (dt == Q6) return launch(k_down<Q6, Q8>, grid, 288, 0, s, true, p);
@@ -603,7 +704,7 @@ int b200moe_moe_decode(const void *x, int x_dtype, int T, const b200moe_layer *l
   if (rc) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   const DecodeWS w = carve(ws, T);
-  if (T == 1 && b2mega::usable(!layer_all_q4k(layer)))
+  if (T == 1 && !layer_dense(layer) && b2mega::usable(!layer_all_q4k(layer)))
     return run_persistent(x, x_dtype, nullptr, 0.f, 1, layer, out, ids_out, w_out, w, s);
   return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, w, s, true);
 }
@@ -624,7 +725,7 @@ int b200moe_moe_decode_noalloc(const void *x, int x_dtype, int T, const b200moe_
   void *scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc) return rc;
-  if (T == 1 && b2mega::usable(!layer_all_q4k(layer)))
+  if (T == 1 && !layer_dense(layer) && b2mega::usable(!layer_all_q4k(layer)))
     return run_persistent(x, x_dtype, nullptr, 0.f, 1, layer, out, ids_out, w_out, carve(scratch, T),
                           (cudaStream_t)stream);
   return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, carve(scratch, T), (cudaStream_t)stream,
@@ -641,6 +742,32 @@ int b200moe_decode_persistent_info(int *ctas, int *cluster) {
   const int C = b2mega::cluster_ctas();
   if (ctas) *ctas = C ? b2mega::kCtas : 0;
   if (cluster) *cluster = C;
+  return B200MOE_OK;
+}
+
+int b200moe_moe_decode_stages(const void *x, int x_dtype, int T, const b200moe_layer *layer,
+                              const b200moe_stages *st, float *out, int32_t *ids_out, uint16_t *w_out, void *ws,
+                              size_t ws_bytes, void *stream) {
+  if (T <= 0 || T > kMaxT) return b2host::set_error(B200MOE_EINVAL, "moe_decode_stages: T=%d outside [1, %d]", T, kMaxT);
+  if (!x || !out || !ws || !st) return b2host::set_error(B200MOE_EINVAL, "moe_decode_stages: x, st, out and ws are required");
+  if (x_dtype != B200MOE_F32 && x_dtype != B200MOE_BF16)
+    return b2host::set_error(B200MOE_EINVAL, "moe_decode_stages: x_dtype %d is neither F32 nor BF16", x_dtype);
+  if (!al16(x) || !al16(out) || !al16(ws)) return b2host::set_error(B200MOE_EINVAL, "moe_decode_stages: pointers must be 16-byte aligned");
+  if (ws_bytes < decode_ws_bytes(T))
+    return b2host::set_error(B200MOE_ESIZE, "moe_decode_stages: workspace %zu B < required %zu B", ws_bytes, decode_ws_bytes(T));
+  int rc = check_layer(layer, "moe_decode_stages");
+  if (rc) return rc;
+  if (st->bf16_stages && (!layer_dense(layer) || x_dtype != B200MOE_BF16))
+    return b2host::set_error(B200MOE_EINVAL, "moe_decode_stages: bf16 stages (moe_ref's \"ref\" form) need a dense "
+                             "BF16 layer and bf16 x");
+  cudaStream_t s = (cudaStream_t)stream;
+  const DecodeWS w = carve(ws, T);
+  const Stages sv = {st->bf16_stages ? 1 : 0, st->expert_raw, st->routed_sum, st->shared_raw};
+  rc = run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, w, s, true, &sv);
+  if (rc) return rc;
+  if (st->router_logits)
+    B2_CUDA(cudaMemcpyAsync(st->router_logits, w.logits, (size_t)T * kE * 2, cudaMemcpyDeviceToDevice, s));
+  if (st->shared_gate) B2_CUDA(cudaMemcpyAsync(st->shared_gate, w.sg, (size_t)T * 4, cudaMemcpyDeviceToDevice, s));
   return B200MOE_OK;
 }
 
@@ -681,14 +808,16 @@ int b200moe_stack_decode(float *resid, int T, const b200moe_layer *layers, int n
   if (ws_bytes < decode_ws_bytes(T))
     return b2host::set_error(B200MOE_ESIZE, "stack_decode: workspace %zu B < required %zu B", ws_bytes, decode_ws_bytes(T));
   bool q4 = true;  // every layer Q4_K throughout (else the persistent kernel's format variant)
+  bool dense = false;  // some layer dense (BF16): the three-kernel path
   for (int l = 0; l < n_layers; ++l) {
     int rc = check_layer(&layers[l], "stack_decode");
     if (rc) return rc;
     q4 = q4 && layer_all_q4k(&layers[l]);
+    dense = dense || layer_dense(&layers[l]);
   }
   cudaStream_t s = (cudaStream_t)stream;
   const DecodeWS w = carve(ws, T);
-  if (T == 1 && b2mega::usable(!q4))
+  if (T == 1 && !dense && b2mega::usable(!q4))
     return run_persistent(nullptr, B200MOE_F32, resid, eps, n_layers, layers, nullptr, ids_out, nullptr, w, s);
   for (int l = 0; l < n_layers; ++l) {
     int rc = run_layer(nullptr, B200MOE_F32, resid, eps, T, &layers[l], nullptr,

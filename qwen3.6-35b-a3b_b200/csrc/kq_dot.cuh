@@ -18,6 +18,8 @@
 //        q = (ql[64G + 32(k&1) + l] >> 4(k>>1)) & 15 | ((qh[32G + l] >> 2k) & 3) << 4
 //        value (d*sc[e>>4])*(q - 32). Blocks only 2-byte aligned: 16-bit loads.
 //   Q8_0  34 B / 32:  f16 d | int8 q[32]; value d*q. Blocks 2-byte aligned: 16-bit loads.
+//   BF16  dense rows as the Hugging Face checkpoint stores them (2 B per weight, exact in f32):
+//        the dense-expert layers speccheck/moe_ref.py takes; rows 16-byte aligned.
 #pragma once
 
 #include "common.cuh"
@@ -26,7 +28,8 @@ namespace b2 {
 
 // Bytes of one row of `n` weights (n a multiple of 256) in GGML block type t (0 = Q4_K).
 __host__ __device__ constexpr int64_t row_bytes(int t, int n) {
-  return t == B200MOE_TYPE_Q5_K   ? (int64_t)n / 256 * 176
+  return t == B200MOE_TYPE_BF16   ? (int64_t)n * 2
+         : t == B200MOE_TYPE_Q5_K ? (int64_t)n / 256 * 176
          : t == B200MOE_TYPE_Q6_K ? (int64_t)n / 256 * 210
          : t == B200MOE_TYPE_Q8_0 ? (int64_t)n / 32 * 34
                                   : (int64_t)n / 256 * 144;
@@ -39,8 +42,16 @@ __host__ __device__ inline int layer_down_type(const b200moe_layer *L) {
 __host__ __device__ inline int layer_sh_type(const b200moe_layer *L) {
   return L->sh_type ? L->sh_type : B200MOE_TYPE_Q4_K;
 }
+__host__ __device__ inline int layer_gate_type(const b200moe_layer *L) {
+  return L->gate_type ? L->gate_type : B200MOE_TYPE_Q4_K;
+}
 __host__ __device__ inline bool layer_all_q4k(const b200moe_layer *L) {
-  return layer_down_type(L) == B200MOE_TYPE_Q4_K && layer_sh_type(L) == B200MOE_TYPE_Q4_K;
+  return layer_gate_type(L) == B200MOE_TYPE_Q4_K && layer_down_type(L) == B200MOE_TYPE_Q4_K &&
+         layer_sh_type(L) == B200MOE_TYPE_Q4_K;
+}
+// A dense layer: every expert and shared matrix in BF16 (the Hugging Face layout).
+__host__ __device__ inline bool layer_dense(const b200moe_layer *L) {
+  return layer_gate_type(L) == B200MOE_TYPE_BF16;
 }
 
 // Load policies: global memory (read-only, streamed: weights are read once per token) and
@@ -136,6 +147,25 @@ __device__ __forceinline__ float q80_chunk_dot(const uint8_t *row, int kb, int c
   return fmaf(d0, al, d1 * ah);
 }
 
+// BF16: the chunk's lo run is the 16 weights at chunk_pos(kb, c), its hi run the 16 weights 32
+// later; each run is one 32-byte read (two 16-byte loads), a plain f32 FMA chain per run.
+template <typename Ld = LdGlobal>
+__device__ __forceinline__ float bf16_chunk_dot(const uint8_t *row, int kb, int c, const XChunk &x) {
+  const uint8_t *p = row + (size_t)chunk_pos(kb, c) * 2;
+  const uint4 l0 = Ld::v16(p), l1 = Ld::v16(p + 16), h0 = Ld::v16(p + 64), h1 = Ld::v16(p + 80);
+  const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+  const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  float al = 0.f, ah = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    al = fmaf(bf16f(lw[i]), x.lo[2 * i], al);
+    al = fmaf(bf16f(lw[i] >> 16), x.lo[2 * i + 1], al);
+    ah = fmaf(bf16f(hw[i]), x.hi[2 * i], ah);
+    ah = fmaf(bf16f(hw[i] >> 16), x.hi[2 * i + 1], ah);
+  }
+  return al + ah;
+}
+
 // Q4_K through a load policy (the same arithmetic as q4k_chunk_dot on registers).
 template <typename Ld = LdGlobal>
 __device__ __forceinline__ float q4k_row_chunk_dot(const uint8_t *row, int kb, int c, const XChunk &x) {
@@ -149,6 +179,7 @@ __device__ __forceinline__ float any_chunk_dot(int type, const uint8_t *row, int
   if (type == B200MOE_TYPE_Q5_K) return q5k_chunk_dot<Ld>(row, kb, c, x);
   if (type == B200MOE_TYPE_Q6_K) return q6k_chunk_dot<Ld>(row, kb, c, x);
   if (type == B200MOE_TYPE_Q8_0) return q80_chunk_dot<Ld>(row, kb, c, x);
+  if (type == B200MOE_TYPE_BF16) return bf16_chunk_dot<Ld>(row, kb, c, x);
   return q4k_row_chunk_dot<Ld>(row, kb, c, x);
 }
 
@@ -158,6 +189,7 @@ __device__ __forceinline__ float row_chunk_dot(const uint8_t *row, int kb, int c
   if constexpr (kT == B200MOE_TYPE_Q5_K) return q5k_chunk_dot(row, kb, c, x);
   else if constexpr (kT == B200MOE_TYPE_Q6_K) return q6k_chunk_dot(row, kb, c, x);
   else if constexpr (kT == B200MOE_TYPE_Q8_0) return q80_chunk_dot(row, kb, c, x);
+  else if constexpr (kT == B200MOE_TYPE_BF16) return bf16_chunk_dot(row, kb, c, x);
   else return q4k_row_chunk_dot(row, kb, c, x);
 }
 

@@ -940,6 +940,8 @@ int launch(const Args &a, cudaStream_t stream) {
     int mode = 0;  // 1: f32 router rows or an applied RMSNorm weight; 2: a layer not Q4_K throughout
     for (int l = 0; l < nl; ++l) {
       p.L[l] = a.layers[l0 + l];
+      if (layer_dense(&p.L[l]))
+        return b2host::set_error(B200MOE_EINVAL, "persistent decode: layer %d is dense (BF16)", l0 + l);
       if (!layer_all_q4k(&p.L[l])) mode = 2;
       else if (mode == 0 && (p.L[l].router_f32 != 0 || (a.resid && p.L[l].norm_w))) mode = 1;
     }

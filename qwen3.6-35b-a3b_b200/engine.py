@@ -19,7 +19,7 @@ import torch
 
 from . import _abi
 from . import synth
-from .geometry import (DOWN_TYPES, E, EXPERT_GATE_BYTES, SHARED_TYPES, TYPE_IDS, Geometry, H, I,
+from .geometry import (DENSE_GATE_UP_STRIDE, DOWN_TYPES, E, EXPERT_GATE_BYTES, SHARED_TYPES, TYPE_IDS, Geometry, H, I,
                        KIND_BLOCKS, KIND_DOWN, KIND_GATE, KIND_SH_DOWN, KIND_SH_GATE, KIND_SH_UP,
                        KIND_UP, Q4K_BYTES, row_bytes, stream_id)
 
@@ -45,7 +45,7 @@ class DeviceLayer:
 
     def __init__(self, gate, up, down, sh_gate, sh_up, sh_down, router_w, sh_gate_w,
                  logit_bias=None, gate_up_stride: int = EXPERT_GATE_BYTES, norm_w=None,
-                 down_type: str = "Q4_K", sh_type: str = "Q4_K"):
+                 down_type: str = "Q4_K", sh_type: str = "Q4_K", gate_type: str = "Q4_K"):
         self.gate, self.up, self.down = gate, up, down
         self.sh_gate, self.sh_up, self.sh_down = sh_gate, sh_up, sh_down
         self.router_w, self.sh_gate_w, self.logit_bias = router_w, sh_gate_w, logit_bias
@@ -58,10 +58,15 @@ class DeviceLayer:
         if norm_w is not None and (norm_w.dtype != torch.float32 or norm_w.numel() != H):
             raise ValueError("norm_w must be f32 [%d]" % H)
         self.norm_w = norm_w
-        if down_type not in DOWN_TYPES or sh_type not in SHARED_TYPES:
-            raise ValueError("down_type %r / sh_type %r: the kernels take down %s, shared %s"
-                             % (down_type, sh_type, "/".join(DOWN_TYPES), "/".join(SHARED_TYPES)))
-        self.down_type, self.sh_type = down_type, sh_type
+        if gate_type == "BF16":  # dense: the Hugging Face layout, every matrix bf16
+            if down_type != "BF16" or sh_type != "BF16":
+                raise ValueError("a dense (BF16) layer has BF16 down and shared matrices, got %s / %s"
+                                 % (down_type, sh_type))
+        elif gate_type != "Q4_K" or down_type not in DOWN_TYPES or sh_type not in SHARED_TYPES:
+            raise ValueError("gate_type %r / down_type %r / sh_type %r: the kernels take gate Q4_K (or a dense "
+                             "BF16 layer), down %s, shared %s" % (gate_type, down_type, sh_type, "/".join(DOWN_TYPES),
+                                                                  "/".join(SHARED_TYPES)))
+        self.down_type, self.sh_type, self.gate_type = down_type, sh_type, gate_type
         self.down_stride = H * row_bytes(down_type, I)   # bytes per expert of ffn_down_exps
         if down.numel() != E * self.down_stride:
             raise ValueError("down holds %d B; %d experts of %s need %d" % (down.numel(), E, down_type,
@@ -76,7 +81,12 @@ class DeviceLayer:
     @property
     def all_q4k(self) -> bool:
         """Every expert and shared matrix is Q4_K (the grouped-GEMM path takes only such layers)."""
-        return self.down_type == "Q4_K" and self.sh_type == "Q4_K"
+        return self.gate_type == "Q4_K" and self.down_type == "Q4_K" and self.sh_type == "Q4_K"
+
+    @property
+    def dense(self) -> bool:
+        """Every expert and shared matrix is bf16 as the Hugging Face checkpoint stores it."""
+        return self.gate_type == "BF16"
 
     # ------------------------------------------------------------------ construction
     @classmethod
@@ -125,6 +135,48 @@ class DeviceLayer:
                        np.ascontiguousarray(norm_w, dtype=np.float32)).to(dev),
                    down_type=down_type, sh_type=sh_type)
 
+    @classmethod
+    def dense(cls, gate_up, down, shared_gate, shared_up, shared_down, router, shared_scalar_gate,
+              logit_bias=None) -> "DeviceLayer":
+        """A dense layer from the Hugging Face checkpoint's bf16 tensors as stored (the roles of
+        ``speccheck/moe_ref.py:184 BlockWeights``): gate_up [256, 1024, 2048] (gate = rows 0..511
+        of each expert, up = rows 512..1023), down [256, 2048, 512], shared gate / up [512, 2048],
+        shared down [2048, 512], router [256, 2048], shared_scalar_gate [1, 2048]. The tensors
+        are used in place (contiguous CUDA bf16), nothing is copied."""
+        want = {"gate_up": (E, 2 * I, H), "down": (E, H, I), "shared_gate": (I, H), "shared_up": (I, H),
+                "shared_down": (H, I), "router": (E, H), "shared_scalar_gate": (1, H)}
+        got = dict(gate_up=gate_up, down=down, shared_gate=shared_gate, shared_up=shared_up,
+                   shared_down=shared_down, router=router, shared_scalar_gate=shared_scalar_gate)
+        for k, t in got.items():
+            if tuple(t.shape) != want[k] or t.dtype != torch.bfloat16 or not t.is_contiguous():
+                raise ValueError("%s: %s %s, want contiguous bf16 %s" % (k, tuple(t.shape), t.dtype, want[k]))
+        u8 = lambda t: t.view(torch.uint8).reshape(-1)  # noqa: E731
+        gu = u8(gate_up)
+        return cls(gu, gu[I * H * 2:], u8(down), u8(shared_gate), u8(shared_up), u8(shared_down),
+                   router, shared_scalar_gate.reshape(H), logit_bias, gate_up_stride=DENSE_GATE_UP_STRIDE,
+                   down_type="BF16", sh_type="BF16", gate_type="BF16")
+
+    @classmethod
+    def synthetic_dense(cls, seed: int, layer: int, device="cuda") -> "DeviceLayer":
+        """The seeded synthetic layer in the dense Hugging Face layout: its Q4_K matrices
+        dequantised to bf16 on the device (b200moe_q4k_dequant, RNE of the exact f32 values) and
+        laid out as moe_ref's tensors."""
+        q = cls.synthetic(seed, layer, device)
+        dev = torch.device(device)
+        deq = lambda t, shape: cls._dequant_bf16(t, shape, dev)  # noqa: E731
+        g = deq(q.gate, (E, I, H))
+        u = deq(q.up, (E, I, H))
+        gate_up = torch.cat([g, u], dim=1).contiguous()
+        del g, u
+        return cls.dense(gate_up, deq(q.down, (E, H, I)), deq(q.sh_gate, (I, H)), deq(q.sh_up, (I, H)),
+                         deq(q.sh_down, (H, I)), q.router_w, q.sh_gate_w.reshape(1, H))
+
+    @staticmethod
+    def _dequant_bf16(blocks, shape, dev):
+        out = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+        _abi.q4k_dequant(blocks, out, _abi.BF16)
+        return out
+
     # ------------------------------------------------------------------ ABI view
     def abi(self) -> _abi.Layer:
         if self._abi is None:
@@ -133,7 +185,7 @@ class DeviceLayer:
                                    self.down_stride, p(self.sh_gate), p(self.sh_up), p(self.sh_down),
                                    p(self.router_w), p(self.sh_gate_w), p(self.logit_bias),
                                    1 if self.router_w.dtype == torch.float32 else 0, p(self.norm_w),
-                                   TYPE_IDS[self.down_type], TYPE_IDS[self.sh_type])
+                                   TYPE_IDS[self.down_type], TYPE_IDS[self.sh_type], TYPE_IDS[self.gate_type])
         return self._abi
 
     @property
@@ -143,7 +195,7 @@ class DeviceLayer:
     def nbytes(self) -> int:
         ts = [self.down, self.sh_gate, self.sh_up, self.sh_down, self.router_w, self.sh_gate_w]
         n = sum(t.numel() * t.element_size() for t in ts)
-        if self.gate_up_stride == 2 * EXPERT_GATE_BYTES:
+        if self.gate_up_stride == 2 * I * row_bytes(self.gate_type, H):  # one fused gate_up stack
             n += self.gate.numel()
         else:
             n += self.gate.numel() + self.up.numel()
@@ -152,7 +204,7 @@ class DeviceLayer:
     # ------------------------------------------------------------------ inspection
     def type_of(self, kind: str) -> str:
         """Block format of ``kind`` (gate / up / down / sh_gate / sh_up / sh_down)."""
-        return "Q4_K" if kind in ("gate", "up") else self.down_type if kind == "down" else self.sh_type
+        return self.gate_type if kind in ("gate", "up") else self.down_type if kind == "down" else self.sh_type
 
     def expert_blocks(self, kind: str, e: int = 0) -> torch.Tensor:
         """The block bytes (device uint8 view) of one expert matrix or of a shared matrix."""
@@ -160,12 +212,14 @@ class DeviceLayer:
             return self.down[e * self.down_stride:(e + 1) * self.down_stride]
         if kind in ("gate", "up"):
             base = self.gate if kind == "gate" else self.up
-            return base[e * self.gate_up_stride: e * self.gate_up_stride + EXPERT_GATE_BYTES]
+            return base[e * self.gate_up_stride: e * self.gate_up_stride + I * row_bytes(self.gate_type, H)]
         return {"sh_gate": self.sh_gate, "sh_up": self.sh_up, "sh_down": self.sh_down}[kind]
 
     def dequant(self, kind: str, e: int = 0, dtype=torch.float32) -> torch.Tensor:
         blocks = self.expert_blocks(kind, e)
         shape = (H, I) if kind.endswith("down") else (I, H)
+        if self.type_of(kind) == "BF16":  # dense rows as stored
+            return blocks.view(torch.bfloat16).reshape(shape).to(dtype)
         out = torch.empty(shape, dtype=dtype, device=blocks.device)
         _abi.dequant(blocks, self.type_of(kind), out, _abi.BF16 if dtype == torch.bfloat16 else _abi.F32)
         return out

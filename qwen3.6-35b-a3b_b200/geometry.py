@@ -26,10 +26,13 @@ ROUTER_BYTES = E * H * 2                # 1,048,576 B bf16
 # Block formats the kernels take (GGML type ids as in GGUF): (bytes, elements) per block. The
 # published Q4_K_M file stores expert gate/up as Q4_K, expert down as Q5_K (Q6_K at three layers)
 # and the shared expert as Q8_0.
-TYPE_IDS = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
-BLOCK_GEOM = {"Q8_0": (34, 32), "Q4_K": (144, 256), "Q5_K": (176, 256), "Q6_K": (210, 256)}
+TYPE_IDS = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "BF16": 30}
+BLOCK_GEOM = {"Q8_0": (34, 32), "Q4_K": (144, 256), "Q5_K": (176, 256), "Q6_K": (210, 256), "BF16": (2, 1)}
 DOWN_TYPES = ("Q4_K", "Q5_K", "Q6_K")      # ffn_down_exps
 SHARED_TYPES = ("Q4_K", "Q8_0")            # ffn_{gate,up,down}_shexp
+# A dense layer (the Hugging Face checkpoint's bf16 tensors, as speccheck/moe_ref.py takes them)
+# has every expert and shared matrix in BF16: gate_up [E, 2I, H] fused, down [E, H, I].
+DENSE_GATE_UP_STRIDE = 2 * I * H * 2    # 4 MiB per expert of the fused gate_up stack
 
 
 def row_bytes(tname: str, n: int) -> int:

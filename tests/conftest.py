@@ -34,9 +34,10 @@ def golden(name):
     return np.load(os.path.join(GOLDEN, name), allow_pickle=False)
 
 
-def host_layer(seed, layer, bias=False):
+def host_layer(seed, layer, bias=False, bf16_weights=False):
     """The oracle's view of synthetic layer (seed, layer): Q4_K from the numpy mirror of
-    the device generator, bf16 tensors from the package's host generators."""
+    the device generator, bf16 tensors from the package's host generators. ``bf16_weights``:
+    the dense layout of the same layer (every matrix the bf16 rounding of its decode)."""
     from oracle import q4k
     from oracle.moe import HostLayer
     from b200moe import synth
@@ -46,7 +47,7 @@ def host_layer(seed, layer, bias=False):
         return q4k.synth_blocks(seed, stream_id(layer, KIND_OF[kind]), first, n)
 
     return HostLayer(blocks, synth.router_w(seed, layer), synth.shared_gate_w(seed, layer),
-                     synth.zipf_bias(seed, layer) if bias else None)
+                     synth.zipf_bias(seed, layer) if bias else None, bf16_weights=bf16_weights)
 
 
 @pytest.fixture(scope="session")

@@ -15,6 +15,12 @@ files committed beside this script:
   duck-typed weight provider that serves the seeded synthetic Q4_K bytes through the
   reference's ``gguf_fast_dequant.dequant_np`` (4 tokens, config-0 field law, seed 0).
 * ``rmsnorm.npz`` -- ``engine/m3_forward.py:303 rmsnorm_a`` (weight 1) on seeded rows.
+* ``moe_ref_t4.npz`` -- ``speccheck/moe_ref.py:499 moe_block`` (the reference's bf16 spec-check
+  block over dense Hugging Face weights) run unchanged in its "ref" and "exact" forms on 4 tokens,
+  with the seeded synthetic layer (seed 0, layer 0) as dense bf16 tensors: the reference's own
+  decoder ``gguf_fast_dequant.dequant_np`` of the Q4_K bytes, rounded to bf16 (RNE). Only the
+  experts the 4 tokens hit are filled (the others are never read). ``python make_golden.py
+  moe_ref`` makes only this.
 * ``kquant_dequant.npz`` -- seeded and edge-case Q5_K, Q6_K and Q8_0 blocks decoded by the
   reference's ``tools/gguf_reader.py:dequant`` (checked identical to
   ``tools/gguf_fast_dequant.py:dequant_np``). ``python make_golden.py kquants`` makes only this.
@@ -210,6 +216,58 @@ def make_block(M3, FD):
     print("moe_block_t4.npz used=%d" % info["used"])
 
 
+def make_moe_ref(FD):
+    import torch
+    if os.path.join(REF_ROOT, "speccheck") not in sys.path:
+        sys.path.insert(0, os.path.join(REF_ROOT, "speccheck"))
+    import moe_ref as MR  # noqa: E402
+    synth, wg, wsg = wg_and_wsg(0, 0)
+    x_bits = synth.tokens(0, 4, stream=2)
+    x = torch.from_numpy(x_bits.view(np.int16).copy()).view(torch.bfloat16)
+    g = MR.Geometry(hidden_size=2048, num_experts=256, top_k=8, moe_intermediate_size=512,
+                    shared_expert_intermediate_size=512, num_hidden_layers=40, mtp_num_hidden_layers=1,
+                    dtype=torch.bfloat16, rms_norm_eps=1e-6)
+
+    def deq(kind, first, n_blocks, shape):
+        raw = synth_layer_blocks(0, 0, kind, first, n_blocks)
+        return torch.from_numpy(FD.dequant_np(raw.tobytes(), "Q4_K", n_blocks * 256).reshape(shape)).to(
+            torch.bfloat16)
+
+    router = torch.from_numpy(wg.view(np.int16).copy()).view(torch.bfloat16).reshape(256, 2048)
+    hit = set()
+    for arm in ("ref", "exact"):
+        hit |= set(int(v) for v in MR.route(x, router, g, MR.Form.named(arm))["topk_ids"].reshape(-1))
+    gate_up = torch.zeros((256, 1024, 2048), dtype=torch.bfloat16)
+    down = torch.zeros((256, 2048, 512), dtype=torch.bfloat16)
+    for e in sorted(hit):
+        gate_up[e, :512] = deq(0, e * 4096, 4096, (512, 2048))
+        gate_up[e, 512:] = deq(1, e * 4096, 4096, (512, 2048))
+        down[e] = deq(2, e * 4096, 4096, (2048, 512))
+    t = {"router": router, "gate_up": gate_up, "down": down, "shared_gate": deq(3, 0, 4096, (512, 2048)),
+         "shared_up": deq(4, 0, 4096, (512, 2048)), "shared_down": deq(5, 0, 4096, (2048, 512)),
+         "shared_scalar_gate": torch.from_numpy(wsg.view(np.int16).copy()).view(torch.bfloat16).reshape(1, 2048)}
+    w = MR.BlockWeights(MR.Block("layer", 0), t)
+    w.shapes_ok(g)
+    torch.set_num_threads(8)
+    ref = MR.moe_block(x, w, g, "ref")
+    exact = MR.moe_block(x, w, g, "exact")
+    bits = lambda v: v.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    np.savez_compressed(os.path.join(HERE, "moe_ref_t4.npz"), x_bits=x_bits, seed=0, layer=0,
+                        wg_sha256=hashlib.sha256(wg.tobytes()).hexdigest(),
+                        wsg_sha256=hashlib.sha256(wsg.tobytes()).hexdigest(),
+                        hit=np.array(sorted(hit), dtype=np.int32),
+                        **{"ref_" + k: bits(ref[k]) for k in ("router_logits", "topk_weights", "expert_raw",
+                                                              "routed_sum", "shared_raw", "shared_gate_prob",
+                                                              "shared_out", "combined_out")},
+                        ref_router_probs=ref["router_probs"].numpy(),
+                        ref_topk_ids=ref["topk_ids"].numpy().astype(np.int32),
+                        exact_topk_ids=exact["topk_ids"].numpy().astype(np.int32),
+                        exact_topk_weights=exact["topk_weights"].numpy(),
+                        exact_routed_sum=exact["routed_sum"].numpy(),
+                        exact_combined_out=exact["combined_out"].numpy())
+    print("moe_ref_t4.npz: %d experts hit" % len(hit))
+
+
 def make_rmsnorm(M3):
     import torch
     M3.load_geometry()
@@ -263,8 +321,12 @@ if __name__ == "__main__":
     if sys.argv[1:] == ["kquants"]:
         make_kquants(GR, FD)
         sys.exit(0)
+    if sys.argv[1:] == ["moe_ref"]:
+        make_moe_ref(FD)
+        sys.exit(0)
     make_kquants(GR, FD)
     make_dequant(GR, FD)
     make_router(M3)
     make_block(M3, FD)
     make_rmsnorm(M3)
+    make_moe_ref(FD)

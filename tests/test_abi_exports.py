@@ -21,7 +21,7 @@ def test_library_exports_every_symbol():
     lib = ctypes.CDLL(_abi.LIB_PATH)
     for name in declared():
         assert hasattr(lib, name), name
-    assert _abi.abi_version() == 3
+    assert _abi.abi_version() == 4
 
 
 def test_errors_without_device_work():
