@@ -493,12 +493,12 @@ def bench_prefill_ep(dev, rank, world, K, W, tf_peak, T_total=4096, seed=3, chec
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         stages = {n: float(v) for n, v in zip(names, tt.tolist())}
     stages["sum_of_stages_eager"] = sum(stages[n] for n in names)
-    status = moe._abi.prefill_status(ep.workspace(T), world * T if world > 1 else T)
+    status = moe._abi.prefill_status(ep.workspace(T), world * T if world > 1 else T) | ep.p2p_status(T)
     flops = 2.0 * T_total * 9 * 3 * 2048 * 512
     res = {"tokens": T_total, "tokens_per_rank": T, "experts_per_rank": 256 // world, "n_gpus": world,
            "ms_per_step": ms, "tok_per_s": T_total / (ms / 1e3), "tflops_per_gpu": flops / world / (ms / 1e3) / 1e12,
            "frac_of_bf16_peak": flops / world / (ms / 1e3) / 1e12 / tf_peak, "timing": how,
-           "stages_ms_max_over_ranks": stages, "status": status}
+           "stages_ms_max_over_ranks": stages, "status": status, "transport": ep.transport}
     if check:
         step()
         ids = torch.empty((T, 8), dtype=torch.int32, device=dev)
@@ -520,7 +520,11 @@ def bench_prefill_ep(dev, rank, world, K, W, tf_peak, T_total=4096, seed=3, chec
                 "finite": bool(torch.isfinite(got).all())}
         if world > 1:
             dist.barrier()
-    del graph, ep, L
+    del graph
+    if world > 1:
+        dist.barrier()
+    ep.close()
+    del ep, L
     torch.cuda.empty_cache()
     return res
 

@@ -297,6 +297,49 @@ int b200moe_ep_experts(const void *recv_rows, int T, int rank, int world, const 
 int b200moe_ep_combine(const float *ret, const int32_t *pos, int T, int world, float *out, int accumulate,
                        void *stream);
 
+/* ---- The same three stages over peer memory (NVLink), for up to 8 ranks of one node: the pack
+ * writes the dispatch rows straight into each destination's receive buffer and the expert
+ * stage's combine writes each partial row straight into its source's return buffer, so only
+ * rows that carry work cross NVLink (no padded all-to-all). Each hand-off ends with a
+ * release-store of this step's epoch into the receiver's flag word for the sender; the next
+ * stage polls its own flag words with acquire loads, bounded (~1 s: status bit 8, then it
+ * proceeds). Buffers are shared once with CUDA IPC (b200moe_ipc_*): plain device memory, no
+ * multicast object, no library kernel ever reads a peer pointer.
+ *
+ * Per rank r (identical layouts on every rank): recv [world][T] dispatch rows, ret [world][T]
+ * [2048] f32, flag_dispatch [world] and flag_return [world] u32 (zeroed once at set-up), epoch
+ * u32 (zeroed once; bumped by each dispatch), status i32. `recv[d]` etc. are rank d's buffers
+ * as mapped in this process (this rank's own at index rank). */
+typedef struct b200moe_ep_peers {
+    int32_t world, rank;
+    void *recv[8];
+    float *ret[8];
+    uint32_t *flag_dispatch[8];
+    uint32_t *flag_return[8];
+    uint32_t *epoch;
+    int32_t *status;
+} b200moe_ep_peers;
+
+/* b200moe_ep_pack into the peers' receive buffers, then the dispatch signal. pos [T][world]. */
+int b200moe_ep_dispatch_p2p(const void *x16, const int32_t *ids, const uint16_t *w_bf16, int T,
+                            const b200moe_ep_peers *peers, int32_t *pos, void *stream);
+/* Wait for every source's rows, b200moe_ep_experts on this rank's receive buffer with each
+ * partial row stored into its source's return buffer (rows without work are not sent), then the
+ * return signal. Workspace: b200moe_prefill_workspace_size(world T). */
+int b200moe_ep_experts_p2p(int T, const float *sg, const b200moe_layer *layer, const b200moe_ep_peers *peers,
+                           void *ws, size_t ws_bytes, void *stream);
+/* Wait for every partial row, then b200moe_ep_combine over this rank's return buffer. */
+int b200moe_ep_combine_p2p(int T, const int32_t *pos, const b200moe_ep_peers *peers, float *out, int accumulate,
+                           void *stream);
+
+/* CUDA IPC for the buffers above (no counterpart in the reference, which runs on one device):
+ * the handle (B200MOE_IPC_HANDLE_BYTES) and offset of the allocation that holds `dptr`; map a
+ * peer's handle into this process (*dptr = its base + offset); unmap. */
+#define B200MOE_IPC_HANDLE_BYTES 64
+int b200moe_ipc_handle(const void *dptr, void *handle, int64_t *offset);
+int b200moe_ipc_open(const void *handle, int64_t offset, void **dptr);
+int b200moe_ipc_close(void *dptr, int64_t offset);
+
 /* Copy the prefill workspace's device status word to *status (synchronises `stream`). Bits:
  * 1 / 2 = a gate_up / down GEMM pipeline wait exceeded its ~1 s budget; 4 = an fp16 tensor-core
  * operand was out of range (|x| or |silu(gate)*up| * 2^-10 above 65504). 0 = ok. */

@@ -27,7 +27,9 @@ EXPORTS = ("b200moe_abi_version", "b200moe_last_error", "b200moe_q4k_dequant", "
            "b200moe_stack_decode",
            "b200moe_prefill_workspace_size", "b200moe_moe_prefill", "b200moe_moe_route",
            "b200moe_moe_experts", "b200moe_prefill_status", "b200moe_ep_pack", "b200moe_ep_experts",
-           "b200moe_ep_combine")
+           "b200moe_ep_combine", "b200moe_ep_dispatch_p2p", "b200moe_ep_experts_p2p", "b200moe_ep_combine_p2p",
+           "b200moe_ipc_handle", "b200moe_ipc_open", "b200moe_ipc_close")
+IPC_HANDLE_BYTES = 64
 
 EP_ROW_BYTES = 4160   # B200MOE_EP_ROW_BYTES: 2048 fp16 x, 8 int32 ids, 8 bf16 weights, 16 B pad
 
@@ -48,6 +50,13 @@ class Layer(ctypes.Structure):
                 ("sh_gate_w", ctypes.c_void_p), ("logit_bias", ctypes.c_void_p),
                 ("router_f32", ctypes.c_int32), ("norm_w", ctypes.c_void_p),
                 ("down_type", ctypes.c_int32), ("sh_type", ctypes.c_int32), ("gate_type", ctypes.c_int32)]
+
+
+class EpPeers(ctypes.Structure):
+    """``struct b200moe_ep_peers``."""
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("recv", ctypes.c_void_p * 8),
+                ("ret", ctypes.c_void_p * 8), ("flag_dispatch", ctypes.c_void_p * 8),
+                ("flag_return", ctypes.c_void_p * 8), ("epoch", ctypes.c_void_p), ("status", ctypes.c_void_p)]
 
 
 class Stages(ctypes.Structure):
@@ -127,6 +136,18 @@ def lib():
         L.b200moe_ep_experts.argtypes = [vp, i32, i32, i32, vp, ctypes.POINTER(Layer), vp, vp, sz, vp]
         L.b200moe_ep_combine.restype = i32
         L.b200moe_ep_combine.argtypes = [vp, vp, i32, i32, vp, i32, vp]
+        L.b200moe_ep_dispatch_p2p.restype = i32
+        L.b200moe_ep_dispatch_p2p.argtypes = [vp, vp, vp, i32, ctypes.POINTER(EpPeers), vp, vp]
+        L.b200moe_ep_experts_p2p.restype = i32
+        L.b200moe_ep_experts_p2p.argtypes = [i32, vp, ctypes.POINTER(Layer), ctypes.POINTER(EpPeers), vp, sz, vp]
+        L.b200moe_ep_combine_p2p.restype = i32
+        L.b200moe_ep_combine_p2p.argtypes = [i32, vp, ctypes.POINTER(EpPeers), vp, i32, vp]
+        L.b200moe_ipc_handle.restype = i32
+        L.b200moe_ipc_handle.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)]
+        L.b200moe_ipc_open.restype = i32
+        L.b200moe_ipc_open.argtypes = [ctypes.c_char_p, ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p)]
+        L.b200moe_ipc_close.restype = i32
+        L.b200moe_ipc_close.argtypes = [vp, ctypes.c_int64]
         _LIB = L
     return _LIB
 
@@ -324,3 +345,38 @@ def ep_combine(ret, pos, T: int, world: int, out, accumulate: bool, stream=None)
     """``b200moe_ep_combine``: out [T, 2048] f32 (+)= ascending-rank sum of the returned partial rows."""
     _check("b200moe_ep_combine", lib().b200moe_ep_combine(ptr(ret), ptr(pos), T, world, ptr(out),
                                                            1 if accumulate else 0, _stream(stream)))
+
+
+def ipc_handle(t):
+    """(64-byte handle, offset) of the CUDA allocation holding tensor ``t``."""
+    buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    off = ctypes.c_int64(0)
+    _check("b200moe_ipc_handle", lib().b200moe_ipc_handle(ptr(t), buf, ctypes.byref(off)))
+    return buf.raw, int(off.value)
+
+
+def ipc_open(handle: bytes, offset: int) -> int:
+    """Map a peer's allocation; returns the device address of its buffer."""
+    p = ctypes.c_void_p(0)
+    _check("b200moe_ipc_open", lib().b200moe_ipc_open(handle, int(offset), ctypes.byref(p)))
+    return int(p.value)
+
+
+def ipc_close(addr: int, offset: int):
+    _check("b200moe_ipc_close", lib().b200moe_ipc_close(ctypes.c_void_p(addr), int(offset)))
+
+
+def ep_dispatch_p2p(x16, ids, w_bf16, T: int, peers: EpPeers, pos, stream=None):
+    _check("b200moe_ep_dispatch_p2p", lib().b200moe_ep_dispatch_p2p(ptr(x16), ptr(ids), ptr(w_bf16), T,
+                                                                     ctypes.byref(peers), ptr(pos), _stream(stream)))
+
+
+def ep_experts_p2p(T: int, sg, layer: Layer, peers: EpPeers, ws, stream=None):
+    _check("b200moe_ep_experts_p2p",
+           lib().b200moe_ep_experts_p2p(T, ptr(sg), ctypes.byref(layer), ctypes.byref(peers), ptr(ws),
+                                        ws.numel() * ws.element_size(), _stream(stream)))
+
+
+def ep_combine_p2p(T: int, pos, peers: EpPeers, out, accumulate: bool, stream=None):
+    _check("b200moe_ep_combine_p2p", lib().b200moe_ep_combine_p2p(T, ptr(pos), ctypes.byref(peers), ptr(out),
+                                                                   1 if accumulate else 0, _stream(stream)))

@@ -154,3 +154,66 @@ int b200moe_synth_q4k(uint64_t seed, uint32_t stream_id, int64_t block0, int64_t
 }
 
 }  // extern "C"
+
+// --------------------------------------------------------------------------------- peer memory
+// CUDA IPC for the peer-memory form of expert parallelism: a rank exports the allocation that
+// holds one of its buffers and the other ranks (other processes, other GPUs of the node) map it,
+// after which their kernels store into it over NVLink. Legacy IPC maps plain device memory:
+// no multicast object is created.
+#include <cuda.h>
+#include <string.h>
+
+namespace {
+using AddrRangeFn = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
+
+int alloc_base(const void *p, void **base) {
+  static AddrRangeFn fn = nullptr;
+  if (!fn) {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    B2_CUDA(cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !f)
+      return b2host::set_error(B200MOE_ECUDA, "cuMemGetAddressRange is not available from the driver");
+    fn = (AddrRangeFn)f;
+  }
+  CUdeviceptr b = 0;
+  size_t n = 0;
+  const CUresult r = fn(&b, &n, (CUdeviceptr)p);
+  if (r != CUDA_SUCCESS) return b2host::set_error(B200MOE_EINVAL, "ipc: %p is not device memory (%d)", p, (int)r);
+  *base = (void *)b;
+  return B200MOE_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int b200moe_ipc_handle(const void *dptr, void *handle, int64_t *offset) {
+  if (!dptr || !handle || !offset) return b2host::set_error(B200MOE_EINVAL, "ipc_handle: NULL argument");
+  void *base = nullptr;
+  int rc = alloc_base(dptr, &base);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  B2_CUDA(cudaIpcGetMemHandle(&h, base));
+  static_assert(sizeof(h) == B200MOE_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  *offset = (int64_t)((const char *)dptr - (const char *)base);
+  return B200MOE_OK;
+}
+
+int b200moe_ipc_open(const void *handle, int64_t offset, void **dptr) {
+  if (!handle || !dptr || offset < 0) return b2host::set_error(B200MOE_EINVAL, "ipc_open: bad argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void *base = nullptr;
+  B2_CUDA(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+  *dptr = (char *)base + offset;
+  return B200MOE_OK;
+}
+
+int b200moe_ipc_close(void *dptr, int64_t offset) {
+  if (!dptr) return B200MOE_OK;
+  B2_CUDA(cudaIpcCloseMemHandle((char *)dptr - offset));
+  return B200MOE_OK;
+}
+
+}  // extern "C"

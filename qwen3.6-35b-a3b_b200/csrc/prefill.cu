@@ -834,19 +834,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
 }
 
 // ------------------------------------------------------------------------- k_combine
+// Expert-parallel return over peer memory: row r of the combine goes to rank r / rows, into its
+// partial-row block of this rank (row (rank rows + r % rows) of that rank's ret buffer); rows
+// without work are not sent.
+constexpr int kMaxPeers = 8;
+struct SegOut {
+  float *base[kMaxPeers];
+  int rows, rank, n;  // n = 0: plain output
+};
+
 __global__ void __launch_bounds__(256) k_combine(int T, const float *y, const int32_t *inv, const int32_t *offsets,
                                                  const float *sg, int sh_lo, int sh_hi, const int32_t *ids,
                                                  const int32_t *order, int e_lo, int e_hi, float *out,
-                                                 int accumulate) {
+                                                 int accumulate, const SegOut seg) {
   const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;  // one float4 of one token
   if (idx >= (int64_t)T * (kH / 4)) return;
   const int t = (int)(idx / (kH / 4)), h = (int)(idx % (kH / 4)) * 4;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  bool work = sg && t >= sh_lo && t < sh_hi;
 #pragma unroll
   for (int i = 0; i < kK; ++i) {
     const int slot = __ldg(order + (size_t)t * kK + i);
     const int e = __ldg(ids + (size_t)t * kK + slot);
     if (e < e_lo || e >= e_hi) continue;
+    work = true;
     const int pos = __ldg(inv + (size_t)t * kK + slot);
     const float4 v = __ldcs(reinterpret_cast<const float4 *>(y + (size_t)pos * kH + h));
     acc.x = __fadd_rn(acc.x, v.x);
@@ -861,6 +872,14 @@ __global__ void __launch_bounds__(256) k_combine(int T, const float *y, const in
     const float4 sh = __ldcs(reinterpret_cast<const float4 *>(y + (size_t)pos * kH + h));
     r = make_float4(__fadd_rn(acc.x, __fmul_rn(g, sh.x)), __fadd_rn(acc.y, __fmul_rn(g, sh.y)),
                     __fadd_rn(acc.z, __fmul_rn(g, sh.z)), __fadd_rn(acc.w, __fmul_rn(g, sh.w)));
+  }
+  if (seg.n) {
+    if (!work) return;
+    const int s = t / seg.rows;
+    float *d = seg.base[s] + ((size_t)seg.rank * seg.rows + (t - s * seg.rows)) * kH + h;
+    *reinterpret_cast<float4 *>(d) = r;
+    __threadfence_system();  // peer stores complete before the return signal
+    return;
   }
   float4 *dst = reinterpret_cast<float4 *>(out + (size_t)t * kH + h);
   if (accumulate) {
@@ -884,12 +903,33 @@ static_assert(kEpRowHalves * 2 == B200MOE_EP_ROW_BYTES, "dispatch row size");
 
 // CTA d = destination: a block-wide scan over the tokens gives every row position; writes pos
 // and the rows' ids / weights (the x values are copied by k_ep_copy).
+// Flag words of the peer form: own_flags [world] receive every rank's epoch; peer_flags[d] is rank
+// d's flag array (this rank writes element `rank` of it).
+struct EpFlags {
+  uint32_t *own_flags;
+  uint32_t *peer_flags[kMaxPeers];
+  const uint32_t *epoch;
+};
+
+// Where the rows for destination d go: block d of the local send buffer (an all-to-all moves it),
+// or -- over peer memory -- straight into block `rank` of rank d's receive buffer.
+struct EpDst {
+  uint8_t *send;                   // local [world][T] rows, or NULL for the peer form
+  uint8_t *peer_recv[kMaxPeers];   // peer form: each rank's receive buffer
+  uint32_t *epoch;                 // peer form: this rank's step counter (bumped by block 0)
+  __device__ uint8_t *block(int d, int rank, int T) const {
+    return send ? send + (size_t)d * T * B200MOE_EP_ROW_BYTES
+                : peer_recv[d] + (size_t)rank * T * B200MOE_EP_ROW_BYTES;
+  }
+};
+
 __global__ void __launch_bounds__(1024) k_ep_plan(int T, const int32_t *ids, const uint16_t *wb, int rank, int world,
-                                                  uint8_t *send, int32_t *pos) {
+                                                  const EpDst dst, int32_t *pos) {
   __shared__ int wsum[32];
   const int d = blockIdx.x, per = kE / world, lo = d * per, hi = lo + per;
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
-  uint8_t *seg = send + (size_t)d * T * B200MOE_EP_ROW_BYTES;
+  if (d == 0 && threadIdx.x == 0 && dst.epoch) *dst.epoch += 1u;  // this step's signal value
+  uint8_t *seg = dst.block(d, rank, T);
   int carry = 0;
   for (int base = 0; base < T; base += 1024) {
     const int t = base + threadIdx.x;
@@ -935,17 +975,47 @@ __global__ void __launch_bounds__(1024) k_ep_plan(int T, const int32_t *ids, con
     reinterpret_cast<int4 *>(row + kEpIdsOff)[0] = none;
     reinterpret_cast<int4 *>(row + kEpIdsOff)[1] = none;
   }
+  if (!dst.send) __threadfence_system();  // peer stores complete before the dispatch signal
 }
 
 // CTA t: token t's 4 KB of x16 into its row at every destination that takes it.
-__global__ void __launch_bounds__(256) k_ep_copy(int T, const __half *x16, int world, const int32_t *pos,
-                                                 uint8_t *send) {
+__global__ void __launch_bounds__(256) k_ep_copy(int T, const __half *x16, int rank, int world, const int32_t *pos,
+                                                 const EpDst dst) {
   const int t = blockIdx.x;
   const uint4 v = __ldg(reinterpret_cast<const uint4 *>(x16 + (size_t)t * kH) + threadIdx.x);
   for (int d = 0; d < world; ++d) {
     const int p = __ldg(pos + (size_t)t * world + d);
-    if (p >= 0)
-      reinterpret_cast<uint4 *>(send + ((size_t)d * T + p) * B200MOE_EP_ROW_BYTES)[threadIdx.x] = v;
+    if (p >= 0) reinterpret_cast<uint4 *>(dst.block(d, rank, T) + (size_t)p * B200MOE_EP_ROW_BYTES)[threadIdx.x] = v;
+  }
+  if (!dst.send) __threadfence_system();
+}
+
+// Peer signalling: lane d stores this step's epoch into rank d's flag word for this rank
+// (release at system scope, after the kernels that wrote into rank d's memory), and the wait
+// polls this rank's own flag words until every peer's epoch has arrived -- bounded: after
+// ~1 s it sets status bit 8 and returns, so a rank that is gone cannot hang this one.
+constexpr int kErrPeer = 8;
+
+__global__ void __launch_bounds__(32) k_ep_signal(int world, int rank, const EpFlags f) {
+  const int d = threadIdx.x;
+  if (d >= world) return;
+  const uint32_t e = *f.epoch;
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f.peer_flags[d] + rank), "r"(e) : "memory");
+}
+
+__global__ void __launch_bounds__(32) k_ep_wait(int world, const EpFlags f, int32_t *status) {
+  const int s = threadIdx.x;
+  if (s >= world) return;
+  const uint32_t e = *f.epoch;
+  const long long t0 = clock64();
+  for (;;) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f.own_flags + s) : "memory");
+    if ((int32_t)(v - e) >= 0) break;
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      atomicOr(status, kErrPeer);
+      break;
+    }
   }
 }
 
@@ -1170,7 +1240,7 @@ int route_stage(const void *x, int x_dtype, const float *resid, float eps, int T
 // expert when sg != NULL), then the combine into out (accumulate: out += result).
 int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *wb, int e_lo, int e_hi,
                   const float *sg, int sh_lo, int sh_hi, const b200moe_layer *L, float *out, int accumulate,
-                  const PrefillWS &w, cudaStream_t s, int64_t x16_pitch = kH) {
+                  const PrefillWS &w, cudaStream_t s, int64_t x16_pitch = kH, const SegOut *seg = nullptr) {
   int rc = ensure_gemm_attrs();
   if (rc) return rc;
   B2_CUDA(cudaMemsetAsync(w.counts, 0, kNE * 4, s));
@@ -1203,7 +1273,8 @@ int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *
   B2_CUDA(cudaGetLastError());
   const int64_t nthreads = (int64_t)T * (kH / 4);
   k_combine<<<(unsigned)((nthreads + 255) / 256), 256, 0, s>>>(T, w.y, w.inv, w.offsets, sg, sh_lo, sh_hi, ids,
-                                                               w.order, e_lo, e_hi, out, accumulate);
+                                                               w.order, e_lo, e_hi, out, accumulate,
+                                                               seg ? *seg : SegOut{});
   B2_CUDA(cudaGetLastError());
   return B200MOE_OK;
 }
@@ -1301,9 +1372,11 @@ int b200moe_ep_pack(const void *x16, const int32_t *ids, const uint16_t *w_bf16,
   if (!a16(x16) || !a16(ids) || !a16(w_bf16) || !a16(send_rows))
     return b2host::set_error(B200MOE_EINVAL, "ep_pack: pointers must be 16-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;
-  k_ep_plan<<<world, 1024, 0, s>>>(T, ids, w_bf16, rank, world, (uint8_t *)send_rows, pos);
+  EpDst dst = {};
+  dst.send = (uint8_t *)send_rows;
+  k_ep_plan<<<world, 1024, 0, s>>>(T, ids, w_bf16, rank, world, dst, pos);
   B2_CUDA(cudaGetLastError());
-  k_ep_copy<<<T, 256, 0, s>>>(T, (const __half *)x16, world, pos, (uint8_t *)send_rows);
+  k_ep_copy<<<T, 256, 0, s>>>(T, (const __half *)x16, rank, world, pos, dst);
   B2_CUDA(cudaGetLastError());
   return B200MOE_OK;
 }
@@ -1342,6 +1415,106 @@ int b200moe_ep_combine(const float *ret, const int32_t *pos, int T, int world, f
   if (!a16(ret) || !a16(out)) return b2host::set_error(B200MOE_EINVAL, "ep_combine: pointers must be 16-byte aligned");
   const int64_t n = (int64_t)T * (kH / 4);
   k_ep_sum<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(T, world, ret, pos, out, accumulate);
+  B2_CUDA(cudaGetLastError());
+  return B200MOE_OK;
+}
+
+}  // extern "C"
+
+// ---- expert parallelism over peer memory (b200moe_ep_peers)
+namespace {
+int check_peers(const b200moe_ep_peers *P, const char *who) {
+  if (!P) return b2host::set_error(B200MOE_EINVAL, "%s: NULL peers", who);
+  if (P->world < 2 || P->world > kMaxPeers || kE % P->world || P->rank < 0 || P->rank >= P->world)
+    return b2host::set_error(B200MOE_EINVAL, "%s: rank %d / world %d (peer form: 2..%d ranks dividing 256)", who,
+                             P->rank, P->world, kMaxPeers);
+  for (int d = 0; d < P->world; ++d)
+    if (!P->recv[d] || !P->ret[d] || !P->flag_dispatch[d] || !P->flag_return[d] || !a16(P->recv[d]) ||
+        !a16(P->ret[d]))
+      return b2host::set_error(B200MOE_EINVAL, "%s: rank %d's buffers are NULL or unaligned", who, d);
+  if (!P->epoch || !P->status) return b2host::set_error(B200MOE_EINVAL, "%s: epoch and status are required", who);
+  return B200MOE_OK;
+}
+
+EpFlags flags_of(const b200moe_ep_peers *P, bool dispatch) {
+  EpFlags f = {};
+  f.own_flags = dispatch ? P->flag_dispatch[P->rank] : P->flag_return[P->rank];
+  for (int d = 0; d < P->world; ++d) f.peer_flags[d] = dispatch ? P->flag_dispatch[d] : P->flag_return[d];
+  f.epoch = P->epoch;
+  return f;
+}
+}  // namespace
+
+extern "C" {
+
+int b200moe_ep_dispatch_p2p(const void *x16, const int32_t *ids, const uint16_t *w_bf16, int T,
+                            const b200moe_ep_peers *peers, int32_t *pos, void *stream) {
+  int rc = check_peers(peers, "ep_dispatch_p2p");
+  if (rc) return rc;
+  if (T <= 0 || (int64_t)T * peers->world > kMaxTPrefill)
+    return b2host::set_error(B200MOE_EINVAL, "ep_dispatch_p2p: T=%d out of range", T);
+  if (!x16 || !ids || !w_bf16 || !pos || !a16(x16) || !a16(ids) || !a16(w_bf16))
+    return b2host::set_error(B200MOE_EINVAL, "ep_dispatch_p2p: x16, ids, w_bf16 (16-byte aligned) and pos are required");
+  cudaStream_t s = (cudaStream_t)stream;
+  EpDst dst = {};
+  for (int d = 0; d < peers->world; ++d) dst.peer_recv[d] = (uint8_t *)peers->recv[d];
+  dst.epoch = peers->epoch;
+  k_ep_plan<<<peers->world, 1024, 0, s>>>(T, ids, w_bf16, peers->rank, peers->world, dst, pos);
+  B2_CUDA(cudaGetLastError());
+  k_ep_copy<<<T, 256, 0, s>>>(T, (const __half *)x16, peers->rank, peers->world, pos, dst);
+  B2_CUDA(cudaGetLastError());
+  k_ep_signal<<<1, 32, 0, s>>>(peers->world, peers->rank, flags_of(peers, true));
+  B2_CUDA(cudaGetLastError());
+  return B200MOE_OK;
+}
+
+int b200moe_ep_experts_p2p(int T, const float *sg, const b200moe_layer *L, const b200moe_ep_peers *peers, void *ws,
+                           size_t ws_bytes, void *stream) {
+  int rc = check_peers(peers, "ep_experts_p2p");
+  if (rc) return rc;
+  const int world = peers->world, rank = peers->rank;
+  const int64_t R = (int64_t)world * T;
+  if (T <= 0 || R > kMaxTPrefill) return b2host::set_error(B200MOE_EINVAL, "ep_experts_p2p: T=%d out of range", T);
+  if (!sg || !ws || !a16(ws)) return b2host::set_error(B200MOE_EINVAL, "ep_experts_p2p: sg and ws are required");
+  if (ws_bytes < prefill_ws_bytes((int)R))
+    return b2host::set_error(B200MOE_ESIZE, "ep_experts_p2p: workspace %zu B < required %zu B", ws_bytes,
+                             prefill_ws_bytes((int)R));
+  rc = check_prefill_layer(L, "ep_experts_p2p");
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  const PrefillWS w = carve_prefill(ws, (int)R);
+  B2_CUDA(cudaMemsetAsync(w.err, 0, 4, s));
+  k_ep_wait<<<1, 32, 0, s>>>(world, flags_of(peers, true), peers->status);  // every source's rows are in
+  B2_CUDA(cudaGetLastError());
+  const uint8_t *recv = (const uint8_t *)peers->recv[rank];
+  k_ep_unpack<<<(unsigned)((R + 255) / 256), 256, 0, s>>>((int)R, recv, w.ids, w.wb);
+  B2_CUDA(cudaGetLastError());
+  SegOut seg = {};
+  for (int d = 0; d < world; ++d) seg.base[d] = peers->ret[d];
+  seg.rows = T;
+  seg.rank = rank;
+  seg.n = world;
+  const int per = kE / world;
+  rc = experts_stage((const __half *)recv, (int)R, w.ids, w.wb, rank * per, (rank + 1) * per, sg, rank * T,
+                     rank * T + T, L, nullptr, 0, w, s, kEpRowHalves, &seg);
+  if (rc) return rc;
+  k_ep_signal<<<1, 32, 0, s>>>(world, rank, flags_of(peers, false));
+  B2_CUDA(cudaGetLastError());
+  return B200MOE_OK;
+}
+
+int b200moe_ep_combine_p2p(int T, const int32_t *pos, const b200moe_ep_peers *peers, float *out, int accumulate,
+                           void *stream) {
+  int rc = check_peers(peers, "ep_combine_p2p");
+  if (rc) return rc;
+  if (T <= 0 || T > kMaxTPrefill || !pos || !out || !a16(out))
+    return b2host::set_error(B200MOE_EINVAL, "ep_combine_p2p: T=%d, pos and a 16-byte aligned out are required", T);
+  cudaStream_t s = (cudaStream_t)stream;
+  k_ep_wait<<<1, 32, 0, s>>>(peers->world, flags_of(peers, false), peers->status);  // every partial row is in
+  B2_CUDA(cudaGetLastError());
+  const int64_t n = (int64_t)T * (kH / 4);
+  k_ep_sum<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(T, peers->world, peers->ret[peers->rank], pos, out,
+                                                       accumulate);
   B2_CUDA(cudaGetLastError());
   return B200MOE_OK;
 }

@@ -10,14 +10,18 @@ same T everywhere). The reference runs the whole expert loop in one process
    d's expert range -- each token once per destination, however many of its slots land there --
    as dispatch rows (x, ids, weights) in ascending token order; every own token goes to the own
    block, where the shared expert runs. ``pos[t][d]`` remembers each row's place;
-3. dispatch: one equal-split ``all_to_all_single`` of the [W][T] row blocks (block d to rank d);
+3. dispatch: the row blocks reach their ranks -- over peer memory (``transport="p2p"``, the
+   default on NVLink GPUs: ``b200moe_ep_dispatch_p2p`` stores only the rows that carry work
+   straight into each destination's receive buffer, then signals it), or as one equal-split
+   ``all_to_all_single`` of the [W][T] blocks (``transport="a2a"``, any backend);
 4. experts (``b200moe_ep_experts``): the received rows' slots in this rank's expert range through
    the Q4_K grouped GEMMs (one set of launches for all sources), summed per row in ascending
    expert id, plus the gated shared expert on the own block -> one f32 partial row per received
    row (zero where a row has no work);
-5. combine: an equal-split ``all_to_all_single`` returns block s to rank s, which adds, per token,
-   the partial rows from d = 0, 1, ... in that order (``b200moe_ep_combine``: ascending expert
-   ranges, a fixed association).
+5. combine: the partial rows go back to their sources -- stored by the expert stage's own combine
+   kernel into each source's return buffer (p2p), or by an equal-split ``all_to_all_single`` --
+   and each rank adds, per token, the partial rows from d = 0, 1, ... in that order
+   (``b200moe_ep_combine``: ascending expert ranges, a fixed association).
 
 Sizes are fixed by T and W, so a step is a fixed sequence of kernels and collectives with no host
 synchronisation: it can be captured in a CUDA graph (buffers are allocated once per T and reused).
@@ -36,6 +40,7 @@ from . import _abi
 from .geometry import E, H, RMS_EPS, TOPK
 
 ROW_BYTES = _abi.EP_ROW_BYTES
+MAX_P2P_RANKS = 8
 
 
 def device_route_fn(layer, ws):
@@ -89,7 +94,7 @@ class ExpertParallelMoE:
     """One MoE layer with its routed experts sharded over a process group."""
 
     def __init__(self, layer, group=None, route_fn=None, pack_fn=None, experts_fn=None, combine_fn=None,
-                 local_fn=None, device=None):
+                 local_fn=None, device=None, transport: str | None = None):
         self.group = group
         grouped = dist.is_available() and dist.is_initialized()
         self.rank = dist.get_rank(group) if grouped else 0
@@ -111,6 +116,14 @@ class ExpertParallelMoE:
         self.experts_fn = experts_fn or device_experts_fn(layer, self._workspace)
         self.combine_fn = combine_fn or device_combine_fn()
         self.local_fn = local_fn or device_local_fn(layer, self._workspace)
+        if transport is None:  # peer memory where the ranks are CUDA devices of one NVLink node
+            nccl = grouped and dist.get_backend(group) == "nccl"
+            transport = "p2p" if (nccl and 1 < self.world <= MAX_P2P_RANKS and pack_fn is None
+                                  and experts_fn is None and combine_fn is None) else "a2a"
+        if transport not in ("p2p", "a2a"):
+            raise ValueError("transport must be p2p or a2a, got %r" % (transport,))
+        self.transport = transport
+        self._peers = {}
 
     def _workspace(self, rows):
         need = _abi.prefill_workspace_size(max(rows, 1))
@@ -137,6 +150,59 @@ class ExpertParallelMoE:
             self._bufs[T] = b
         return b
 
+    def _p2p(self, T):
+        """The peer-memory buffers for T tokens per rank: allocated, shared by CUDA IPC with every
+        rank of the group (a collective: every rank calls it for the same T) and mapped."""
+        st = self._peers.get(T)
+        if st is not None:
+            return st
+        W, dev, r = self.world, self.device, self.rank
+        own = dict(recv=torch.empty((W, T, ROW_BYTES), dtype=torch.uint8, device=dev),
+                   ret=torch.empty((W, T, H), dtype=torch.float32, device=dev),
+                   fd=torch.zeros((W,), dtype=torch.int32, device=dev),
+                   fr=torch.zeros((W,), dtype=torch.int32, device=dev))
+        epoch = torch.zeros((4,), dtype=torch.int32, device=dev)  # [0]: epoch, [1]: status
+        torch.cuda.synchronize(dev)
+        mine = {k: _abi.ipc_handle(t) for k, t in own.items()}
+        every = [None] * W
+        dist.all_gather_object(every, mine, group=self.group)
+        addrs, opened = {}, []
+        for k, t in own.items():
+            row = []
+            for d in range(W):
+                if d == r:
+                    row.append(t.data_ptr())
+                else:
+                    h, off = every[d][k]
+                    a = _abi.ipc_open(h, off)
+                    opened.append((a, off))
+                    row.append(a)
+            addrs[k] = row
+        P = _abi.EpPeers()
+        P.world, P.rank = W, r
+        for d in range(W):
+            P.recv[d], P.ret[d] = addrs["recv"][d], addrs["ret"][d]
+            P.flag_dispatch[d], P.flag_return[d] = addrs["fd"][d], addrs["fr"][d]
+        P.epoch = epoch.data_ptr()
+        P.status = epoch.data_ptr() + 4
+        dist.barrier(group=self.group)  # every rank's flags are zero and mapped before any signal
+        st = dict(own=own, epoch=epoch, peers=P, opened=opened, pos=torch.empty((T, W), dtype=torch.int32,
+                                                                                   device=dev))
+        self._peers[T] = st
+        return st
+
+    def p2p_status(self, T) -> int:
+        """Status word of the peer-memory exchanges for T tokens (bit 8: a peer wait ran out)."""
+        st = self._peers.get(T)
+        return 0 if st is None else int(st["epoch"][1].item())
+
+    def close(self):
+        """Unmap the peers' buffers (call on every rank before the process group is destroyed)."""
+        for st in self._peers.values():
+            for a, off in st["opened"]:
+                _abi.ipc_close(a, off)
+        self._peers.clear()
+
     def forward(self, x=None, resid=None, out=None, mark=None):
         """``x`` [T, 2048] (bf16/f32) -> (out [T, 2048] f32, ids [T, 8]); T is the same on every
         rank. With ``resid`` instead of ``x``: routes rmsnorm(resid) and adds the block output to
@@ -155,6 +221,17 @@ class ExpertParallelMoE:
             self.local_fn(x16, ids, wb, sg, dst, acc)
             for st in ("experts", "combine", "sum"):
                 mark(st)
+            return dst, ids
+        if self.transport == "p2p":
+            st = self._p2p(T)
+            P, pos = st["peers"], st["pos"]
+            _abi.ep_dispatch_p2p(x16, ids, wb, T, P, pos)
+            mark("dispatch")
+            _abi.ep_experts_p2p(T, sg, self.layer.abi(), P, self._workspace(W * T))
+            mark("experts")
+            mark("combine")
+            _abi.ep_combine_p2p(T, pos, P, dst, acc)
+            mark("sum")
             return dst, ids
         b = self.buffers(T)
         self.pack_fn(x16, ids, wb, self.rank, W, b["send"], b["pos"])

@@ -20,6 +20,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=512)
     ap.add_argument("--out", required=True)
+    ap.add_argument("--transport", default=None, choices=[None, "p2p", "a2a"])
     a = ap.parse_args()
     import __graft_entry__ as G
     G.load_package()
@@ -34,9 +35,13 @@ def main():
     xb = synth.tokens(3, a.tokens, stream=7)
     xall = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).to(dev)
     per = a.tokens // world
-    ep = ExpertParallelMoE(L)
-    out, ids = ep.forward(xall[rank * per:(rank + 1) * per])
+    ep = ExpertParallelMoE(L, transport=a.transport)
+    for _ in range(3):  # repeated steps: the peer form's epochs and buffer reuse
+        out, ids = ep.forward(xall[rank * per:(rank + 1) * per])
     torch.cuda.synchronize()
+    p2p_status = ep.p2p_status(per)
+    from b200moe import _abi
+    ep_status = _abi.prefill_status(ep.workspace(per), world * per)
     outs = [torch.empty_like(out) for _ in range(world)]
     idss = [torch.empty_like(ids) for _ in range(world)]
     dist.all_gather(outs, out)
@@ -45,11 +50,14 @@ def main():
         ref, info = moe.moe_block(xall, L, path="prefill")
         torch.cuda.synchronize()
         o = torch.cat(outs)
-        res = dict(world=world, tokens=a.tokens, ids_equal=bool(torch.equal(torch.cat(idss), info["ids"])),
+        res = dict(world=world, tokens=a.tokens, transport=ep.transport, p2p_status=p2p_status,
+                   ids_equal=bool(torch.equal(torch.cat(idss), info["ids"])),
                    rel_l2=float(torch.linalg.norm(o - ref) / torch.linalg.norm(ref)),
-                   finite=bool(torch.isfinite(o).all()), status=moe.prefill_status(a.tokens, dev))
+                   finite=bool(torch.isfinite(o).all()), status=moe.prefill_status(a.tokens, dev) | ep_status)
         with open(a.out, "w") as f:
             json.dump(res, f)
+    dist.barrier()
+    ep.close()
     dist.barrier()
     dist.destroy_process_group()
 
