@@ -128,25 +128,21 @@ struct XChunk {
 __device__ __forceinline__ int chunk_pos(int kb, int c) { return kb * 256 + 64 * (c >> 1) + 16 * (c & 1); }
 
 // get_scale_min_k4 for the two sub-blocks of chunk c (2g and 2g+1), folded with d / dmin.
-// hdr.x = d | dmin<<16, hdr.y/z/w = scale bytes 0-3 / 4-7 / 8-11. Branch-free: for sub-block
-// j with b = j & 3, q[j] / q[j+4] (j < 4) and q[j-4] / q[j] / q[j+4] (j >= 4) are byte b of
-// hdr.y / hdr.z / hdr.w.
+// hdr.x = d | dmin<<16, hdr.y/z/w = scale bytes 0-3 / 4-7 / 8-11. Byte-parallel: one word holds
+// the four 6-bit scales (or mins) of sub-blocks 0-3 or 4-7 -- for j < 4, q[j] & 63 and
+// q[j+4] & 63; for j >= 4, (q[j+4] & 15) | (q[j-4] >> 6) << 4 and (q[j+4] >> 4) | (q[j] >> 6) << 4
+// -- so a chunk's two values are bytes 2(g&1) and 2(g&1)+1 of the word its half selects.
 __device__ __forceinline__ void q4k_scales(const uint4 &h, int c, float &s0, float &m0, float &s1,
                                            float &m1) {
   const float d = f16f(h.x), dmin = f16f(h.x >> 16);
   const int g = c >> 1;
-  const bool lo = g < 2;
-  const int sh0 = 16 * (g & 1), sh1 = sh0 + 8;  // byte 2(g&1) and 2(g&1)+1
-  const uint32_t y0 = (h.y >> sh0) & 0xFFu, z0 = (h.z >> sh0) & 0xFFu, w0 = (h.w >> sh0) & 0xFFu;
-  const uint32_t y1 = (h.y >> sh1) & 0xFFu, z1 = (h.z >> sh1) & 0xFFu, w1 = (h.w >> sh1) & 0xFFu;
-  const uint32_t sc0 = lo ? (y0 & 63u) : ((w0 & 15u) | ((y0 & 0xC0u) >> 2));
-  const uint32_t mm0 = lo ? (z0 & 63u) : ((w0 >> 4) | ((z0 & 0xC0u) >> 2));
-  const uint32_t sc1 = lo ? (y1 & 63u) : ((w1 & 15u) | ((y1 & 0xC0u) >> 2));
-  const uint32_t mm1 = lo ? (z1 & 63u) : ((w1 >> 4) | ((z1 & 0xC0u) >> 2));
-  s0 = d * (float)sc0;
-  m0 = dmin * (float)mm0;
-  s1 = d * (float)sc1;
-  m1 = dmin * (float)mm1;
+  const uint32_t sc = g < 2 ? (h.y & 0x3F3F3F3Fu) : ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u));
+  const uint32_t mn = g < 2 ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
+  const int sh = 16 * (g & 1);
+  s0 = d * (float)((sc >> sh) & 0xFFu);
+  m0 = dmin * (float)((mn >> sh) & 0xFFu);
+  s1 = d * (float)((sc >> (sh + 8)) & 0xFFu);
+  m1 = dmin * (float)((mn >> (sh + 8)) & 0xFFu);
 }
 
 // 4-bit value of byte b (0..3) of a nibble-masked word, as an exact float: 0x4B0000qq is

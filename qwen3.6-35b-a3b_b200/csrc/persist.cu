@@ -749,20 +749,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
     fail = !wait_bar(kBarDn);
     fail = !wait_bar(kBarShDn) || fail;
     if (__syncthreads_or(fail)) { aborted = true; break; }
-    if (warp <= kK) {
-      // reconverge the warp first: thread 0's solo branches (copy issue, barrier arming) can
-      // leave warp 0 split, and a split warp runs this loop once per part
+    {
+      // All 12 warps: warp w < 9 takes rows 0..11 of slot w (routed slots 0..7, the shared expert
+      // 8), warp 9 + i rows 12..15 of slots 3i, 3i + 1, 3i + 2 -- four rows per iteration (two per
+      // half-warp, in flight together), three iterations per warp, so each SM sub-partition runs
+      // the same number of row dots (with one warp per slot, three of them ran a third more).
+      // Each row's dot is the same sequence of operations whichever warp runs it.
+      // Reconverge the warp first: thread 0's solo branches (copy issue, barrier arming) can
+      // leave warp 0 split, and a split warp runs this loop once per part.
       __syncwarp();
-      const int slot = warp;  // warps 0..8: routed slots 0..7, shared expert 8
       const int half = lane >> 4, kb = (lane >> 3) & 1;
       XChunk X;
-      load_xchunk(slot < kK ? s_s + slot * kI : ssh_s, kb, cc, X);
+      if (warp < 9) load_xchunk(warp < kK ? s_s + warp * kI : ssh_s, kb, cc, X);
 #pragma unroll 1
-      for (int it = 0; it < kHr / 4; ++it) {  // rows 2it + half and 2it + 8 + half: two in flight
+      for (int it = 0; it < 3; ++it) {
+        const int slot = warp < 9 ? warp : 3 * (warp - 9) + it;
+        const int rbase = warp < 9 ? 4 * it : 12;
+        if (warp >= 9) load_xchunk(slot < kK ? s_s + slot * kI : ssh_s, kb, cc, X);
         float v[2];
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
-          const int hh = 2 * it + 8 * p + half;
+          const int hh = rbase + 2 * p + half;
           if constexpr (kFmt) {  // the layer's row formats, staged at their own pitch
             const int t = slot < kK ? down_t(l) : sh_t(l);
             const size_t rb = (size_t)row_bytes(t, kI);
@@ -778,7 +785,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
           v[p] = half_warp_sum(v[p]);
-          if ((lane & 15) == 0) o_s[slot * kHr + 2 * it + 8 * p + half] = v[p];
+          if ((lane & 15) == 0) o_s[slot * kHr + rbase + 2 * p + half] = v[p];
         }
       }
     }
