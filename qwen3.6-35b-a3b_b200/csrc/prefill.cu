@@ -7,7 +7,7 @@
 //   k_route_tok   warp per token: R2..R5 -> ids, bf16 routing weights
 //   k_count       per token: the slots whose expert is in the requested range, and their order
 //   k_plan        one CTA: packed row offsets per expert (the shared expert is expert 256 with
-//                 every token), 256-token chunks, and the GEMM tile tables
+//                 every token), near-equal chunks of at most 192 tokens, and the GEMM tile tables
 //   k_fill        thread per assignment: a row in its expert's range (plist), and the
 //                 assignment's row position (inv)
 //   k_gather_x    the x16 rows in assignment-list order (the gate_up GEMM's B operand)
@@ -40,7 +40,7 @@ using namespace b2;
 namespace {
 
 constexpr int kNE = kE + 1;     // 256 routed experts + the shared expert
-constexpr int kChunk = 256;     // tokens per GEMM tile
+constexpr int kChunk = 192;     // tokens per GEMM tile (at most)
 constexpr float kSScale = 1.0f / 1024.0f;  // fp16 storage scale of s = silu(gate) * up
 constexpr int kErrRange = 4;    // status bit: an fp16 operand (x or s) was out of range
 
@@ -62,6 +62,7 @@ struct PrefillWS {
   __half *s16;       // [9T][512]
   float *y;          // [9T][2048] down outputs by row position (routed: times the routing weight)
   int32_t *inv;      // [8T] row position of assignment t * 8 + slot (in-range experts only)
+  float *wrow;       // [9T] routing weight (bf16 value) by row position; 1 for the shared expert's rows
   int32_t *err;      // [1]
 };
 
@@ -74,7 +75,7 @@ size_t prefill_ws_bytes(int T) {
   return al256(t * kH * 4) + al256(t * kH * 2) + al256(t * kE * 2) + al256(t * 4) + al256(t * kK * 4) +
          al256(t * kK * 2) + al256(t * kK * 4) + al256(kNE * 4) + al256((kNE + 1) * 4) + al256(9 * t * 4) +
          al256(9 * t * kH * 2) + al256(mc * 4 * 16) + al256(mc * 16 * 16) + al256(2 * 4) + al256(9 * t * kI * 2) +
-         al256(9 * t * kH * 4) + al256(8 * t * 4) + al256(4);
+         al256(9 * t * kH * 4) + al256(8 * t * 4) + al256(4) + al256(9 * t * 4);
 }
 
 PrefillWS carve_prefill(void *ws, int T) {
@@ -100,6 +101,7 @@ PrefillWS carve_prefill(void *ws, int T) {
   w.y = (float *)take(9 * t * kH * 4);
   w.inv = (int32_t *)take(8 * t * 4);
   w.err = (int32_t *)take(4);
+  w.wrow = (float *)take(9 * t * 4);
   return w;
 }
 
@@ -406,11 +408,11 @@ __global__ void __launch_bounds__(512) k_plan(int n_shared, const int32_t *count
   if (e <= kE) {
     const int cbase = sn[pos] - nch;
     const int r0 = sc[e] - cnt;
-    for (int c = 0; c < nch; ++c) {
-      const int n = min(kChunk, cnt - kChunk * c);
+    for (int c = 0; c < nch; ++c) {  // nch near-equal chunks (at most kChunk rows each)
+      const int a0 = (int)((long long)c * cnt / nch), a1 = (int)((long long)(c + 1) * cnt / nch);
       const int ci = cbase + c;
-      for (int jt = 0; jt < 4; ++jt) tiles1[4 * ci + jt] = make_int4(e, r0 + kChunk * c, n, jt);
-      for (int ht = 0; ht < 16; ++ht) tiles2[16 * ci + ht] = make_int4(e, r0 + kChunk * c, n, ht);
+      for (int jt = 0; jt < 4; ++jt) tiles1[4 * ci + jt] = make_int4(e, r0 + a0, a1 - a0, jt);
+      for (int ht = 0; ht < 16; ++ht) tiles2[16 * ci + ht] = make_int4(e, r0 + a0, a1 - a0, ht);
     }
   }
   if (e == 0) {
@@ -422,11 +424,13 @@ __global__ void __launch_bounds__(512) k_plan(int n_shared, const int32_t *count
 // ------------------------------------------------------------------------- k_fill
 // One thread per assignment a = t * 8 + slot whose expert is in range: it takes a row of its
 // expert's range by an atomic countdown of that expert's count (which ends at zero), and
-// records plist[row] = a, inv[a] = row. The order of rows inside an expert changes no result:
+// records plist[row] = a, inv[a] = row and the row's routing weight wrow[row] (the bf16 value
+// as f32; 1 for the shared expert's rows). The order of rows inside an expert changes no result:
 // every GEMM column, and every token's combine, is computed on its own. Rows from
 // offsets[kE] on are the shared expert's: tokens sh_lo .. sh_hi-1 in order.
-__global__ void __launch_bounds__(256) k_fill(int T, int sh_lo, int sh_hi, const int32_t *ids, int e_lo, int e_hi,
-                                              const int32_t *offsets, int32_t *counts, int32_t *plist, int32_t *inv) {
+__global__ void __launch_bounds__(256) k_fill(int T, int sh_lo, int sh_hi, const int32_t *ids, const uint16_t *wb,
+                                              int e_lo, int e_hi, const int32_t *offsets, int32_t *counts,
+                                              int32_t *plist, int32_t *inv, float *wrow) {
   const int a = blockIdx.x * 256 + threadIdx.x;
   if (a < T * kK) {
     const int e = __ldg(ids + a);
@@ -434,9 +438,14 @@ __global__ void __launch_bounds__(256) k_fill(int T, int sh_lo, int sh_hi, const
       const int row = __ldg(offsets + e) + atomicSub(counts + e, 1) - 1;
       plist[row] = a;
       inv[a] = row;
+      wrow[row] = bf16f(__ldg(wb + a));
     }
   }
-  if (a < sh_hi - sh_lo) plist[__ldg(offsets + kE) + a] = sh_lo + a;
+  if (a < sh_hi - sh_lo) {
+    const int row = __ldg(offsets + kE) + a;
+    plist[row] = sh_lo + a;
+    wrow[row] = 1.0f;
+  }
 }
 
 // ------------------------------------------------------------------------- k_gather_x
@@ -461,9 +470,11 @@ __global__ void __launch_bounds__(256) k_gather_x(int max_rows, const int32_t *o
 // ------------------------------------------------------------------------- grouped GEMM
 // Block of 15 warps, each with one job:
 //   warps 0-3    epilogue: TMEM lanes 32w..32w+31 -> s (gate_up) or y (down)
-//   warps 4-11   dequant: raw Q4_K slab (shared memory) -> fp16 A tile of the K-slab, each
-//                thread a whole row's 64 elements (gate_up) or one half of them (down)
-//   warp 12      TMEM allocation; lane 0 issues tcgen05.mma and the commits
+//   warps 4-11   dequant: raw Q4_K slab (shared memory) -> fp16 A operand of the K-slab in
+//                TMEM (tcgen05.st), each thread one row: the whole slab (gate_up) or half of
+//                its quant bytes (down)
+//   warp 12      TMEM allocation; lane 0 issues tcgen05.mma (A from TMEM, B from shared
+//                memory) and the commits
 //   warp 13      raw producer (lane 0): per K-slab and 128-row weight tile, two TMA loads of
 //                the Q4_K bytes -- the 16-byte block headers and the slab's 32 quant bytes of
 //                all 128 rows -- through 3-D tensor maps (bytes, row, expert)
@@ -475,27 +486,33 @@ __global__ void __launch_bounds__(256) k_gather_x(int max_rows, const int32_t *o
 // No load is multicast. One iteration = one K-slab of 64 of one tile; every role walks the
 // same (tile, slab) sequence: tile = blockIdx.x + j * gridDim.x, slab = 0 .. kKS-1.
 //
+// The A operand lives in TMEM, not shared memory. Shared-memory bandwidth (128 B per cycle per
+// SM) is what bounds this kernel: with A in shared memory a gate_up K-slab moved about 142 KB
+// through it (MMA reads of A and B, the dequant's A writes and raw reads, the TMA writes) and
+// the MMAs ran at half their rate; with A in TMEM it moves about 78 KB.
+//
 // Three rings, each with full/empty mbarriers:
-//   A ring   kAStages x kA x 16 KB   written by the dequant warps (8 arrivals); emptied by the
-//                                    MMA commit
-//   B ring   kBStages x 32 KB        TMA bytes (one arming arrival); emptied by the MMA commit
+//   A stages kAStages x kA x 32 TMEM columns   written by the dequant warps (8 arrivals);
+//                                              emptied by the MMA commit
+//   B ring   kBStages x 24 KB        TMA bytes (one arming arrival); emptied by the MMA commit
 //   raw ring kRStages x kA x 6 KB    TMA bytes (one arming arrival); emptied by the 8 dequant
 //                                    warps once their rows are dequantised
-// The down GEMM double-buffers its 256-column accumulator so the epilogue of one tile
-// overlaps the next tile's main loop; gate_up uses all 512 columns for one tile.
+// TMEM (512 columns): a tile has at most kChunk = 192 tokens, so each 256-column half keeps
+// 64 columns free for the A stages. The down GEMM double-buffers its accumulator (columns 0 and
+// 256) so the epilogue of one tile overlaps the next tile's main loop; gate_up holds gate at 0
+// and up at 256 for one tile.
 //
 // Epilogue writes go out as TMA tensor stores: a warp stages its 32 rows x 16 tokens in
-// shared memory (double-buffered) and lane 0 stores them as one 16-row box of s16 / y rows
-// (a tile's rows are contiguous row positions). A ragged last chunk is split into 8-, 4-, 2-
-// and 1-row boxes, so no store reaches past the tile into another expert's rows. (Plain
-// per-column 128-byte stores ran at ~6 B/cycle per SM: the epilogue, not the MMA, bounded
-// the down GEMM.)
-// 8 dequant warps: measured faster than 16 (0.80 vs 0.87 ms per 4096-token layer), whose extra
-// shared-memory traffic and spinning waiters cost more than the latency they hide.
-#ifndef B2_DQ_WARPS
-#define B2_DQ_WARPS 8
-#endif
-constexpr int kEpiWarps = 4, kDqWarps = B2_DQ_WARPS;
+// shared memory and lane 0 stores them as one 16-row box of s16 / y rows (a tile's rows are
+// contiguous row positions). gate_up stages a whole tile (its single accumulator is released as
+// soon as the last columns are in registers); down alternates two sets of four. A ragged last chunk
+// is split into 8-, 4-, 2- and 1-row boxes, so no store reaches past the tile into another
+// expert's rows. (Plain per-column 128-byte stores ran at ~6 B/cycle per SM: the epilogue, not
+// the MMA, bounded the down GEMM.)
+// 8 dequant warps: 16 were measured slower (0.80 vs 0.87 ms per 4096-token layer, with A in
+// shared memory), their extra traffic and spinning waiters costing more than the latency they
+// hide.
+constexpr int kEpiWarps = 4, kDqWarps = 8;
 constexpr int kDqThreads = 32 * kDqWarps;
 constexpr int kMmaWarp = kEpiWarps + kDqWarps;
 constexpr int kRawWarp = kMmaWarp + 1;
@@ -508,27 +525,35 @@ template <int kMode>
 struct GemmCfg {
   static constexpr int kA = kMode == 1 ? 2 : 1;                // A tiles per stage (gate+up / down)
   static constexpr int kARows = 128 * kA;                       // weight rows per tile
-  static constexpr int kTpr = kDqThreads / kARows;              // dequant threads per row (1, 2 or 4)
-  static constexpr int kHalves = kTpr == 1 ? 2 : 1;             // halves of the row per thread
-  static constexpr int kNkc = kTpr == 1 ? 4 : 8 / kTpr;         // 16-byte chunks per half per thread
+  static constexpr int kTpr = kDqThreads / kARows;              // dequant threads per row (1 or 2)
+  static constexpr int kNw = 8 / kTpr;                          // quant words (4 bytes) of a slab row per thread
   static constexpr int kKS = (kMode == 1 ? kH : kI) / 64;       // K-slabs of 64 per tile
-  static constexpr int kAStages = kMode == 1 ? 2 : 3;
+  static constexpr int kAStages = kMode == 1 ? 2 : 4;           // A stages (in TMEM)
   static constexpr int kBStages = 3;
-  static constexpr int kRStages = 4;
-  static constexpr int kATile = 128 * 128;                      // 128 rows x 128 B
-  static constexpr int kBTile = kChunk * 128;                   // 256 rows x 128 B
+  static constexpr int kRStages = kMode == 1 ? 6 : 8;
+  static constexpr int kBTile = kChunk * 128;                   // kChunk rows x 128 B
   static constexpr int kRawStage = kA * kRawTile;
   static constexpr int kNBuf = kMode == 1 ? 1 : 2;              // TMEM accumulator buffers
-  static constexpr uint32_t kAccCols = kMode == 1 ? 512 : 256;  // columns per buffer
+  static constexpr uint32_t kAccCols = kMode == 1 ? 512 : 256;  // column stride of the buffers
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr int kOffB = 0;                                       // 1024-aligned stages
-  static constexpr int kOffA = kOffB + kBStages * kBTile;
-  static constexpr int kOffRaw = kOffA + kAStages * kA * kATile;
-  static constexpr int kOffMeta = kOffRaw + kRStages * kRawStage;       // epilogue routing weights
-  static constexpr int kStageBytes = 16 * 32 * (kMode == 1 ? 2 : 4);     // one warp's staged chunk
-  static constexpr int kOffStage = kOffMeta + kEpiWarps * kChunk * 4;    // [4 warps][2][16 x 32]
-  static constexpr int kOffBar = kOffStage + kEpiWarps * 2 * kStageBytes;
-  static constexpr size_t kSmem = (size_t)kOffBar + 512 + 1024;         // + barriers, + alignment
+  // TMEM columns of A stage s, tile a (32 columns = one K-slab of 128 rows): the columns
+  // kChunk..255 of each 256-column half, which the accumulators (N <= kChunk) leave free.
+  // gate_up: accumulators gate 0.., up 256..; stages at 192 and 448 (64 columns each).
+  // down: accumulator buffers 0.. and 256..; stages at 192, 224, 448, 480.
+  __host__ __device__ static constexpr uint32_t a_col(int s, int a) {
+    return kMode == 1 ? (uint32_t)(kChunk + 256 * s + 32 * a) : (uint32_t)(kChunk + 256 * (s >> 1) + 32 * (s & 1));
+  }
+  static constexpr int kG = kMode == 1 ? 2 : 4;                       // epilogue: 16-token chunks per group
+  static constexpr int kStageChunks = kMode == 1 ? kChunk / 16 : 2 * kG;  // staged chunks per epilogue warp
+  static constexpr int kStageBytes = 16 * 32 * (kMode == 1 ? 2 : 4);  // one warp's staged chunk
+  static constexpr int kOffB = 0;                                     // 1024-aligned stages
+  static constexpr int kOffRaw = kOffB + kBStages * kBTile;
+  static constexpr int kOffMeta = kOffRaw + kRStages * kRawStage;     // epilogue routing weights
+  static constexpr int kOffStage = kOffMeta + kEpiWarps * kChunk * 4;  // [4 warps][kStageChunks][16 x 32]
+  static constexpr int kOffBar = kOffStage + kEpiWarps * kStageChunks * kStageBytes;
+  static constexpr size_t kSmem = (size_t)kOffBar + 512 + 1024;       // + barriers, + alignment
+  static_assert(kChunk + 64 <= 256 && a_col(kAStages - 1, kA - 1) + 32 <= kTmemCols, "TMEM columns");
+  static_assert(kSmem <= 232448, "shared memory");
 };
 
 // Tensor maps of one launch (kernel parameter space; each 64-byte aligned).
@@ -543,37 +568,45 @@ struct GemmParams {
   GemmMaps m;
   const int4 *tiles;
   const int32_t *ntiles;
-  const int32_t *plist;
+  const float *wrow;
   __half *s16;
-  const uint16_t *wb;
   float *y;
   int32_t *err;
 };
 
-// Chunks kc0 .. kc0+nkc-1 (16 B = 8 elements each) of half h (h = 0: low nibbles, sub-block
-// 2g; h = 1: high nibbles, sub-block 2g+1) of K-slab g of one Q4_K block row -> the A tile
-// row. hd: the block header; qw: the quant words of those chunks (two per chunk).
-template <int nkc>
-__device__ __forceinline__ void dequant_part(const uint4 &hd, const uint32_t (&qw)[2 * nkc], int g, int h, int kc0,
-                                             uint8_t *tile, int row) {
+// nw quant words of K-slab g of one Q4_K block row -> that row's TMEM lane, both halves. Byte j
+// of the slab's 32 quant bytes holds element j (low nibble, sub-block 2g) and element 32+j (high
+// nibble, sub-block 2g+1); element k of the slab sits in column k / 2 of the A stage (even k in
+// the low half). `taddr` addresses the column of this thread's first low-nibble element pair;
+// the high nibbles go 16 columns further. One byte permute feeds both halves: a low nibble ORed
+// into the mantissa of 1024.0 reads as 1024+q, a high nibble (mantissa bits 4..7, unit 1/16 in
+// [64, 128)) ORed into 64.0 reads as 64+q; either subtraction leaves q exactly, and
+// x = fma(q, S, -M) in fp16.
+template <int nw>
+__device__ __forceinline__ void dequant_words(const uint4 &hd, const uint32_t (&qw)[nw], int g, uint32_t taddr) {
   float s0, m0, s1, m1;
   q4k_scales(hd, 2 * g, s0, m0, s1, m1);
-  const __half2 S = __float2half2_rn(h ? s1 : s0), M = __float2half2_rn(h ? -m1 : -m0);
-  const __half2 k1024 = __float2half2_rn(1024.0f);
-  uint8_t *rbase = tile + (row >> 3) * 1024 + (row & 7) * 16 + h * 512 + kc0 * 128;
+  const __half2 S0 = __float2half2_rn(s0), M0 = __float2half2_rn(-m0);
+  const __half2 S1 = __float2half2_rn(s1), M1 = __float2half2_rn(-m1);
+  const __half2 k1024 = __float2half2_rn(1024.0f), k64 = __float2half2_rn(64.0f);
+  uint32_t lo[2 * nw], hi[2 * nw];
 #pragma unroll
-  for (int kc = 0; kc < nkc; ++kc) {
-    uint32_t v[4];
+  for (int i = 0; i < nw; ++i) {
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const uint32_t w = qw[2 * kc + (p >> 1)];
-      const uint32_t pr = __byte_perm(w, 0u, (p & 1) ? 0x4342u : 0x4140u);  // [b, 0, b', 0]
-      const uint32_t q = ((pr >> (4 * h)) & 0x000F000Fu) | 0x64006400u;  // 1024 + q
-      __half2 x = __hsub2(*reinterpret_cast<const __half2 *>(&q), k1024);
-      x = __hfma2(x, S, M);
-      v[p] = *reinterpret_cast<uint32_t *>(&x);
+    for (int p = 0; p < 2; ++p) {
+      const uint32_t pr = __byte_perm(qw[i], 0u, p ? 0x4342u : 0x4140u);  // [b, 0, b', 0]
+      const uint32_t ql = (pr & 0x000F000Fu) | 0x64006400u;
+      const uint32_t qh = (pr & 0x00F000F0u) | 0x54005400u;
+      const __half2 xl = __hfma2(__hsub2(*reinterpret_cast<const __half2 *>(&ql), k1024), S0, M0);
+      const __half2 xh = __hfma2(__hsub2(*reinterpret_cast<const __half2 *>(&qh), k64), S1, M1);
+      lo[2 * i + p] = *reinterpret_cast<const uint32_t *>(&xl);
+      hi[2 * i + p] = *reinterpret_cast<const uint32_t *>(&xh);
     }
-    *reinterpret_cast<uint4 *>(rbase + kc * 128) = make_uint4(v[0], v[1], v[2], v[3]);
+  }
+#pragma unroll
+  for (int j = 0; j < 2 * nw; j += 8) {
+    tmem_st8(taddr + j, lo + j);
+    tmem_st8(taddr + 16 + j, hi + j);
   }
 }
 
@@ -583,7 +616,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *b_ring = smem + C::kOffB;
-  uint8_t *a_ring = smem + C::kOffA;
   uint8_t *raw_ring = smem + C::kOffRaw;
   float *col_w = (float *)(smem + C::kOffMeta);              // [4][kChunk] per epilogue warp
   uint64_t *a_full = (uint64_t *)(smem + C::kOffBar);
@@ -631,36 +663,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
   bool ok = true;
 
   if (warp >= kEpiWarps && warp < kMmaWarp) {  // ----------------------------- dequant
+    // Warp w may write only TMEM lanes 32 (w % 4) .. +31, so a warp's lanes are its tile rows:
+    // thread (group wg, quarter wq, lane) has row 32 wq + lane; gate_up: group wg dequantises A
+    // tile wg (the whole slab of its row); down: group wg takes quant words 4 wg .. 4 wg + 3.
     const int pt = threadIdx.x - 32 * kEpiWarps;
-    const int row = pt / C::kTpr, part = pt % C::kTpr;  // which half (and quarter) of the row's slab
-    const int half = C::kTpr == 1 ? 0 : part / (C::kTpr / 2);
-    const int kc0 = C::kTpr == 1 ? 0 : (part % (C::kTpr / 2)) * C::kNkc;
-    const int tl = row >> 7, tr = row & 127;               // A tile, row within it
+    const int wq = (pt >> 5) & 3, wg = pt >> 7;
+    const int tl = kMode == 1 ? wg : 0, tr = 32 * wq + lane, w0 = kMode == 1 ? 0 : 4 * wg;
+    const uint32_t tlane = tmem + ((uint32_t)(32 * wq) << 16) + 2 * w0;
+    // The words of slab it+1 are read from the raw ring before slab it is dequantised, so the
+    // shared-memory latency overlaps the arithmetic.
+    uint4 hd = make_uint4(0u, 0u, 0u, 0u), hd_n = hd;
+    uint32_t qw[C::kNw], qw_n[C::kNw];
+    auto load = [&](uint32_t j, uint4 &h, uint32_t (&q)[C::kNw]) {
+      const uint8_t *rt = raw_ring + (j % C::kRStages) * C::kRawStage + tl * kRawTile;
+      h = *reinterpret_cast<const uint4 *>(rt + tr * 16);
+      const uint4 *qp = reinterpret_cast<const uint4 *>(rt + kRawHdr + tr * 32 + 4 * w0);
+#pragma unroll
+      for (int i = 0; i < C::kNw / 4; ++i) {
+        const uint4 v = qp[i];
+        q[4 * i] = v.x; q[4 * i + 1] = v.y; q[4 * i + 2] = v.z; q[4 * i + 3] = v.w;
+      }
+      if constexpr (C::kNw == 2) {
+        const uint2 v = *reinterpret_cast<const uint2 *>(qp);
+        q[0] = v.x; q[C::kNw - 1] = v.y;
+      }
+    };
+    // warp-uniform outcomes: a lane that timed out never leaves its warp behind in __syncwarp
+    if (n_it > 0) {
+      if (__all_sync(0xFFFFFFFFu, mbar_wait(r_full, 0))) load(0, hd, qw);
+      else ok = false;
+    }
     for (uint32_t it = 0; it < n_it && ok; ++it) {
       const int ks = it % C::kKS;
       const int s = it % C::kAStages, rs = it % C::kRStages;
-      // warp-uniform outcomes: a lane that timed out never leaves its warp behind in __syncwarp
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(r_full + rs, (it / C::kRStages) & 1))) { ok = false; break; }
-      const uint8_t *rt = raw_ring + rs * C::kRawStage + tl * kRawTile;
-      const uint4 hd = *reinterpret_cast<const uint4 *>(rt + tr * 16);
-      uint32_t qw[2 * C::kNkc];  // the quant words of this thread's chunks (both halves share them)
-      if (C::kNkc == 4) {
-        const uint4 q0 = *reinterpret_cast<const uint4 *>(rt + kRawHdr + tr * 32);
-        const uint4 q1 = *reinterpret_cast<const uint4 *>(rt + kRawHdr + tr * 32 + 16);
-        const uint32_t w8[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-        for (int i = 0; i < 2 * C::kNkc; ++i) qw[i] = w8[i];
-      } else {
-        const uint4 q = *reinterpret_cast<const uint4 *>(rt + kRawHdr + tr * 32 + 8 * kc0);
-        const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int i = 0; i < 2 * C::kNkc; ++i) qw[i] = w4[i];
+      if (it + 1 < n_it) {
+        const uint32_t jn = it + 1;
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(r_full + jn % C::kRStages, (jn / C::kRStages) & 1))) { ok = false; break; }
+        load(jn, hd_n, qw_n);
       }
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(a_empty + s, ((it / C::kAStages) & 1) ^ 1))) { ok = false; break; }
-      uint8_t *at = a_ring + s * (C::kA * C::kATile) + tl * C::kATile;
-#pragma unroll
-      for (int hh = 0; hh < C::kHalves; ++hh) dequant_part<C::kNkc>(hd, qw, ks & 3, half + hh, kc0, at, tr);
-      fence_proxy_async_smem();  // this thread's generic smem writes -> async proxy
+      tc_fence_after();  // the MMAs that read this stage have completed
+      dequant_words<C::kNw>(hd, qw, ks & 3, tlane + C::a_col(s, tl));
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(a_full + s);
@@ -669,6 +714,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
         // that the producer's next TMA load had already overwritten.
         mbar_arrive(r_empty + rs);
       }
+      hd = hd_n;
+#pragma unroll
+      for (int i = 0; i < C::kNw; ++i) qw[i] = qw_n[i];
     }
   } else if (warp == kRawWarp) {  // ----------------------------------------- raw producer
     if (lane == 0) {
@@ -714,42 +762,48 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {  // -------------------------------------------- MMA issue
-    if (lane == 0) {
-      uint32_t it = 0, tcount = 0;
-      for (int ti = blockIdx.x; ti < ntiles && ok; ti += gridDim.x, ++tcount) {
-        const int4 tl = __ldg(P.tiles + ti);
-        const int npad = (tl.z + 15) & ~15;
-        const uint32_t idesc = umma_idesc_f16((uint32_t)npad);
-        const uint32_t buf = tcount % C::kNBuf, use = tcount / C::kNBuf;
-        if (use > 0 && !mbar_wait(acc_empty + buf, (use - 1) & 1)) { ok = false; break; }
+    // The whole warp walks the loop and polls the barriers; one elected lane issues each slab's
+    // MMAs as straight-line code from precomputed addresses, then the commits. (Issued by lane 0
+    // of a diverged warp, with the descriptors built between the MMAs, the same MMAs took 4-8x
+    // their tensor time on B200.)
+    uint32_t it = 0, tcount = 0;
+    const uint64_t bdesc0 = umma_desc_sw128(smem_u32(b_ring));
+    for (int ti = blockIdx.x; ti < ntiles && ok; ti += gridDim.x, ++tcount) {
+      const int4 tl = __ldg(P.tiles + ti);
+      const uint32_t idesc = umma_idesc_f16((uint32_t)((tl.z + 15) & ~15));
+      const uint32_t buf = tcount % C::kNBuf, use = tcount / C::kNBuf;
+      if (use > 0 && !__all_sync(0xFFFFFFFFu, mbar_wait(acc_empty + buf, (use - 1) & 1))) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t dacc = tmem + buf * C::kAccCols;
+      for (int ks = 0; ks < C::kKS; ++ks, ++it) {
+        const int sa = it % C::kAStages, sb = it % C::kBStages;
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(a_full + sa, (it / C::kAStages) & 1))) { ok = false; break; }
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(b_full + sb, (it / C::kBStages) & 1))) { ok = false; break; }
         tc_fence_after();
-        const uint32_t dacc = tmem + buf * C::kAccCols;
-        for (int ks = 0; ks < C::kKS; ++ks, ++it) {
-          const int sa = it % C::kAStages, sb = it % C::kBStages;
-          if (!mbar_wait(a_full + sa, (it / C::kAStages) & 1)) { ok = false; break; }
-          if (!mbar_wait(b_full + sb, (it / C::kBStages) & 1)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t at = smem_u32(a_ring + sa * (C::kA * C::kATile));
-          const uint32_t bt = smem_u32(b_ring + sb * C::kBTile);
+        // B descriptors step by 32 bytes per K = 16 (address field in 16-byte units: +2)
+        const uint64_t bd = bdesc0 + (uint64_t)((sb * C::kBTile) >> 4);
+        const uint32_t at = tmem + C::a_col(sa, 0);
+        if (elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t acc = (ks | kk) != 0;
-            const uint64_t bd = umma_desc_sw128(bt + 32 * kk);
-            umma_f16(dacc, umma_desc(at + 256 * kk), bd, idesc, acc);
-            if (kMode == 1) umma_f16(dacc + 256, umma_desc(at + C::kATile + 256 * kk), bd, idesc, acc);
+            umma_f16_ts(dacc, at + 8 * kk, bd + 2 * kk, idesc, acc);
+            if (kMode == 1) umma_f16_ts(dacc + 256, at + 32 + 8 * kk, bd + 2 * kk, idesc, acc);
           }
           umma_commit(a_empty + sa);
           umma_commit(b_empty + sb);
         }
-        if (!ok) break;
-        umma_commit(acc_full + buf);
+        __syncwarp();
       }
-      umma_commit(drain);  // every MMA this thread issued has completed before TMEM is released
-      if (!mbar_wait(drain, 0)) ok = false;
+      if (!ok) break;
+      if (elect_one()) umma_commit(acc_full + buf);
+      __syncwarp();
     }
+    if (elect_one()) umma_commit(drain);  // every MMA this warp issued has completed before TMEM is released
     __syncwarp();
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait(drain, 0))) ok = false;
   } else {  // ---------------------------------------------------------- epilogue (warps 0-3)
-    uint32_t tcount = 0, chunk = 0;
+    uint32_t tcount = 0, grp = 0;  // grp counts store groups across tiles: it picks the buffer set
     bool range_bad = false;
     uint8_t *stage = smem + C::kOffStage;
     for (int ti = blockIdx.x; ti < ntiles && ok; ti += gridDim.x, ++tcount) {
@@ -758,69 +812,102 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
       const int npad = (n + 15) & ~15;
       const uint32_t buf = tcount % C::kNBuf, use = tcount / C::kNBuf;
       float *ww = col_w + warp * kChunk;
-      if (kMode == 2) {  // this warp's copy of the tile's routing weights, loaded while the MMAs run
-        for (int c = lane; c < n; c += 32) ww[c] = e < kE ? bf16f(__ldg(P.wb + __ldg(P.plist + r0 + c))) : 1.0f;
+      if (kMode == 2) {
+        // this warp's copy of the tile's output scales, loaded while the MMAs run: 2^10 (the s
+        // storage scale undone) times the routing weight, or 2^10 alone for the shared expert.
+        // Both factors are exact in f32, so one rounding of acc * scale equals the rounding of
+        // (acc * 2^10) * weight.
+        float wv[kChunk / 32];
+#pragma unroll
+        for (int j = 0; j < kChunk / 32; ++j)
+          wv[j] = (e < kE && lane + 32 * j < n) ? __ldg(P.wrow + r0 + lane + 32 * j) * (1.0f / kSScale) : (1.0f / kSScale);
+#pragma unroll
+        for (int j = 0; j < kChunk / 32; ++j) ww[lane + 32 * j] = wv[j];
         __syncwarp();
       }
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(acc_full + buf, use & 1))) { ok = false; break; }
       tc_fence_after();
+      if (kMode == 1) {  // the previous tile's stores have read this warp's staging area
+        if (lane == 0) bulk_wait_group_read<0>();
+        __syncwarp();
+      }
       const uint32_t lane_addr = tmem + buf * C::kAccCols + ((uint32_t)(32 * warp) << 16);
       const int col0 = wt * 128 + 32 * warp;  // this warp's first s16 column (gate_up) or y column (down)
-      for (int c0 = 0; c0 < npad; c0 += 16, ++chunk) {
-        float a[16];
-        tmem_ld16(lane_addr + c0, a);
-        float v[16];
-        if (kMode == 1) {
-          float u[16];
-          tmem_ld16(lane_addr + 256 + c0, u);
-          tmem_wait_ld();
+      // Groups of kG 16-token chunks: every TMEM load of the group, one wait, then the group's
+      // stores as one bulk group.
+      for (int c0 = 0; c0 < npad; c0 += 16 * C::kG, ++grp) {
+        const int nc = min(C::kG, (npad - c0) >> 4);  // chunks in this group (warp-uniform)
+        float a[C::kG][16], u[kMode == 1 ? C::kG : 1][16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {  // silu(g) * u, stored as s * 2^-10 (exact scaling)
-            const float sil = __fdividef(a[i], 1.0f + __expf(-a[i]));
-            v[i] = sil * u[i] * kSScale;
-            if (c0 + i < n && !(fabsf(v[i]) <= 65504.0f)) range_bad = true;
-          }
-        } else {
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float o = __fmul_rn(a[i], 1.0f / kSScale);  // undo the s storage scale (exact)
-            v[i] = (e < kE && c0 + i < n) ? __fmul_rn(o, ww[c0 + i]) : o;
+        for (int g = 0; g < C::kG; ++g) {
+          if (g < nc) {
+            tmem_ld16(lane_addr + c0 + 16 * g, a[g]);
+            if (kMode == 1) tmem_ld16(lane_addr + 256 + c0 + 16 * g, u[kMode == 1 ? g : 0]);
           }
         }
-        // stage [16 tokens][32 columns] in this warp's buffer (the store that read it two chunks
-        // ago has finished reading), then one box store (pieces for a ragged tail)
-        uint8_t *stg = stage + (warp * 2 + (chunk & 1)) * C::kStageBytes;
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
+        tmem_wait_ld();
+        if (c0 + 16 * C::kG >= npad) {  // every accumulator column of the tile is in registers: release TMEM
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty + buf);
+        }
+        // gate_up stages the whole tile (one buffer per chunk); down alternates two sets of kG
+        // buffers, the bulk group that read one set two groups ago having finished reading.
+        uint8_t *stg0 = stage + (warp * C::kStageChunks + (kMode == 1 ? (c0 >> 4) : (grp & 1) * C::kG)) * C::kStageBytes;
+        if (kMode == 2) {
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+        }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          if (kMode == 1) reinterpret_cast<__half *>(stg)[i * 32 + lane] = __float2half_rn(v[i]);
-          else reinterpret_cast<float *>(stg)[i * 32 + lane] = v[i];
+        for (int g = 0; g < C::kG; ++g) {
+          if (g < nc) {
+            const int cg = c0 + 16 * g;
+            uint8_t *stg = stg0 + g * C::kStageBytes;
+            if (kMode == 1) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {  // silu(g) * u, stored as s * 2^-10 (exact scaling)
+                const float x = a[g][i];
+                const float v = __fdividef(x, 1.0f + __expf(-x)) * u[kMode == 1 ? g : 0][i] * kSScale;
+                if (cg + i < n && !(fabsf(v) <= 65504.0f)) range_bad = true;
+                reinterpret_cast<__half *>(stg)[i * 32 + lane] = __float2half_rn(v);
+              }
+            } else {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float4 w4 = *reinterpret_cast<const float4 *>(ww + cg + 4 * q);
+                float *d = reinterpret_cast<float *>(stg) + 4 * q * 32 + lane;
+                d[0] = __fmul_rn(a[g][4 * q], w4.x);
+                d[32] = __fmul_rn(a[g][4 * q + 1], w4.y);
+                d[64] = __fmul_rn(a[g][4 * q + 2], w4.z);
+                d[96] = __fmul_rn(a[g][4 * q + 3], w4.w);
+              }
+            }
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          const int m = min(16, n - c0);
-          if (m == 16) {
-            tma_store_2d(&P.m.st[0], col0, r0 + c0, stg);
-          } else {
-            int q = 0;
+          for (int g = 0; g < nc; ++g) {
+            const int cg = c0 + 16 * g, m = min(16, n - cg);
+            uint8_t *stg = stg0 + g * C::kStageBytes;
+            if (m == 16) {
+              tma_store_2d(&P.m.st[0], col0, r0 + cg, stg);
+            } else {
+              int q = 0;
 #pragma unroll
-            for (int p = 1; p < 5; ++p) {  // boxes of 8, 4, 2, 1 rows
-              const int hgt = 16 >> p;
-              if (m & hgt) {
-                tma_store_2d(&P.m.st[p], col0, r0 + c0 + q, stg + q * 32 * (kMode == 1 ? 2 : 4));
-                q += hgt;
+              for (int p = 1; p < 5; ++p) {  // boxes of 8, 4, 2, 1 rows
+                const int hgt = 16 >> p;
+                if (m & hgt) {
+                  tma_store_2d(&P.m.st[p], col0, r0 + cg + q, stg + q * 32 * (kMode == 1 ? 2 : 4));
+                  q += hgt;
+                }
               }
             }
           }
           bulk_commit_group();
         }
       }
-      tc_fence_before();
-      __syncwarp();  // also: this warp's metadata is read before the next tile overwrites it
-      if (lane == 0) mbar_arrive(acc_empty + buf);
+      __syncwarp();  // this warp's metadata is read before the next tile overwrites it
     }
     if (lane == 0) bulk_wait_group_all();  // this warp's stores are complete before the CTA exits
     __syncwarp();
@@ -1249,8 +1336,8 @@ int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *
   if (!sg) sh_lo = sh_hi = 0;
   k_plan<<<1, 512, 0, s>>>(sh_hi - sh_lo, w.counts, w.offsets, w.tiles1, w.tiles2, w.ntiles);
   B2_CUDA(cudaGetLastError());
-  k_fill<<<(unsigned)(((int64_t)T * kK + 255) / 256), 256, 0, s>>>(T, sh_lo, sh_hi, ids, e_lo, e_hi, w.offsets,
-                                                                   w.counts, w.plist, w.inv);
+  k_fill<<<(unsigned)(((int64_t)T * kK + 255) / 256), 256, 0, s>>>(T, sh_lo, sh_hi, ids, wb, e_lo, e_hi, w.offsets,
+                                                                   w.counts, w.plist, w.inv, w.wrow);
   B2_CUDA(cudaGetLastError());
   GemmParams g;
   k_gather_x<<<4 * g_num_sms, 256, 0, s>>>(9 * T, w.offsets, w.plist, x16, x16_pitch, w.x16p);
@@ -1259,9 +1346,8 @@ int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *
   if (rc) return rc;
   g.tiles = w.tiles1;
   g.ntiles = w.ntiles;
-  g.plist = w.plist;
+  g.wrow = w.wrow;
   g.s16 = w.s16;
-  g.wb = wb;
   g.y = w.y;
   g.err = w.err;
   k_gemm<1><<<g_num_sms, kGemmThreads, GemmCfg<1>::kSmem, s>>>(g);
