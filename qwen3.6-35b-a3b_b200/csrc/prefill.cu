@@ -227,82 +227,75 @@ __global__ void __launch_bounds__(32 * kPrepWarps) k_prep(const void *x, int x_d
 // ------------------------------------------------------------------------- k_router_gemm
 // CTA: kTM tokens x 64 experts, 128 threads; thread (ty, tx) owns tokens ty + 8i (i < kTM / 8)
 // and experts tx + 16j (j < 4): with kTM = 64, 32 outputs and 128 FMAs per 12 shared-memory
-// vector loads. Fewer tokens per CTA (kTM 32 or 16) give small batches (an expert-parallel
-// rank's share) enough CTAs to fill the SMs; every output is the same sequence of operations
-// whatever the tile. The K chunks are double-buffered: chunk c+1's x rows arrive by cp.async and
-// its weights are held in registers while chunk c is multiplied.
-constexpr int kRgPitch = 68;                                  // padded row pitch (floats)
-constexpr int kRgBuf = 64 * kRgPitch;                         // one 64 x 64 chunk
-constexpr size_t kRgSmem = (size_t)4 * kRgBuf * sizeof(float);  // x and w, two buffers each
+// loads. The token tile is chosen per call (router_tile) so the busiest SM has the fewest rows;
+// every output is the same sequence of operations whatever the tile.
+// The 32 K chunks stream through a kRgStages-deep cp.async ring (x rows as f32, router rows as
+// stored: bf16 rows are widened in the inner loop, exactly), so a chunk's loads are issued
+// kRgStages - 1 chunks ahead of its use: with small tiles (an expert-parallel rank's few hundred
+// tokens) the chunk's arithmetic is shorter than an L2 round trip.
+constexpr int kRgPitch = 68;   // x and f32 router rows: padded pitch (floats)
+constexpr int kRgPitchB = 72;  // bf16 router rows: padded pitch (bf16; 144 B, 16-byte aligned)
+template <bool kF32>
+constexpr int rg_stages() { return kF32 ? 3 : 4; }
+template <bool kF32, int kTM>
+constexpr int rg_stage_bytes() { return kTM * kRgPitch * 4 + (kF32 ? 64 * kRgPitch * 4 : 64 * kRgPitchB * 2); }
+template <bool kF32, int kTM>
+constexpr size_t rg_smem() { return (size_t)rg_stages<kF32>() * rg_stage_bytes<kF32, kTM>(); }
 
 template <bool kF32, int kTM>
 __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ xn, int T,
                                                      const void *__restrict__ wg_, const float *bias,
                                                      uint16_t *logits) {
   constexpr int kTI = kTM / 8;  // tokens per thread
+  constexpr int kS = rg_stages<kF32>();
+  constexpr int kSB = rg_stage_bytes<kF32, kTM>();
   const uint16_t *wg = reinterpret_cast<const uint16_t *>(wg_);  // bf16 router
   const float *wgf = reinterpret_cast<const float *>(wg_);        // f32 router (kF32)
-  extern __shared__ __align__(16) float rg_smem[];
-  float *xs = rg_smem, *wsm = rg_smem + 2 * kRgBuf;  // [2][64][kRgPitch] each
+  extern __shared__ __align__(16) uint8_t rg_smem_raw[];
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
   const int t0 = blockIdx.x * kTM, e0 = blockIdx.y * 64;
-  auto load_x = [&](int c, float *dst) {  // kTM rows x 64 floats by cp.async (zero rows past T)
+  // stage st: x rows [kTM][kRgPitch] f32, then router rows [64][kRgPitch] f32 or [64][kRgPitchB] bf16
+  auto xs_of = [&](int st) { return reinterpret_cast<float *>(rg_smem_raw + st * kSB); };
+  auto ws_of = [&](int st) { return rg_smem_raw + st * kSB + kTM * kRgPitch * 4; };
+  auto load = [&](int c) {  // chunk c into stage c % kS, as one cp.async group
+    float *xd = xs_of(c % kS);
+    uint8_t *wd = ws_of(c % kS);
 #pragma unroll
-    for (int q = 0; q < kTI; ++q) {
-      const int idx = tid + 128 * q;  // 0..1023 float4 slots
+    for (int q = 0; q < kTI; ++q) {  // kTM rows x 16 slots of 16 B (zero rows past T)
+      const int idx = tid + 128 * q;
       const int row = idx >> 4, col = (idx & 15) * 4;
       const bool in = t0 + row < T;
-      cp_async16(dst + row * kRgPitch + col, xn + (size_t)(in ? t0 + row : 0) * kH + 64 * c + col, in ? 16u : 0u);
+      cp_async16(xd + row * kRgPitch + col, xn + (size_t)(in ? t0 + row : 0) * kH + 64 * c + col, in ? 16u : 0u);
     }
+    if (kF32) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {  // 64 rows x 16 slots
+        const int idx = tid + 128 * q;
+        const int row = idx >> 4, col = (idx & 15) * 4;
+        cp_async16(reinterpret_cast<float *>(wd) + row * kRgPitch + col, wgf + (size_t)(e0 + row) * kH + 64 * c + col, 16u);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {  // 64 rows x 8 slots
+        const int idx = tid + 128 * q;
+        const int row = idx >> 3, col = (idx & 7) * 8;
+        cp_async16(reinterpret_cast<uint16_t *>(wd) + row * kRgPitchB + col, wg + (size_t)(e0 + row) * kH + 64 * c + col, 16u);
+      }
+    }
+  };
+#pragma unroll
+  for (int c = 0; c < kS - 1; ++c) {
+    load(c);
     cp_async_commit();
-  };
-  // a chunk's weights: 64 rows x 64 values, 8 values per slot (bf16: one uint4; f32: two)
-  auto load_w = [&](int c, uint4 (&u)[8]) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int idx = tid + 128 * q;  // 0..511 8-wide slots
-      const size_t off = (size_t)(e0 + (idx >> 3)) * kH + 64 * c + (idx & 7) * 8;
-      if (kF32) {
-        u[2 * q] = __ldg(reinterpret_cast<const uint4 *>(wgf + off));
-        u[2 * q + 1] = __ldg(reinterpret_cast<const uint4 *>(wgf + off + 4));
-      } else {
-        u[q] = __ldg(reinterpret_cast<const uint4 *>(wg + off));
-      }
-    }
-  };
-  auto store_w = [&](const uint4 (&u)[8], float *dst) {  // bf16 -> f32 (exact), or f32 as is
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int idx = tid + 128 * q;
-      float *d = dst + (idx >> 3) * kRgPitch + (idx & 7) * 8;
-      if (kF32) {
-        *reinterpret_cast<uint4 *>(d) = u[2 * q];
-        *reinterpret_cast<uint4 *>(d + 4) = u[2 * q + 1];
-      } else {
-        *reinterpret_cast<float4 *>(d) =
-            make_float4(bf16f(u[q].x), bf16f(u[q].x >> 16), bf16f(u[q].y), bf16f(u[q].y >> 16));
-        *reinterpret_cast<float4 *>(d + 4) =
-            make_float4(bf16f(u[q].z), bf16f(u[q].z >> 16), bf16f(u[q].w), bf16f(u[q].w >> 16));
-      }
-    }
-  };
-  {
-    uint4 u[8];
-    load_x(0, xs);
-    load_w(0, u);
-    store_w(u, wsm);
-    cp_async_wait_all();
-    __syncthreads();
   }
   float tot[kTI][4];
   for (int c = 0; c < 32; ++c) {
-    const int buf = c & 1;
-    uint4 un[8];
-    if (c + 1 < 32) {  // the next chunk, in flight while this one is multiplied
-      load_x(c + 1, xs + (buf ^ 1) * kRgBuf);
-      load_w(c + 1, un);
-    }
-    const float *xb = xs + buf * kRgBuf, *wb = wsm + buf * kRgBuf;
+    cp_async_wait_group<kS - 2>();  // chunk c has landed (this thread's copies) ...
+    __syncthreads();                // ... and everyone's; stage (c - 1) % kS is free again
+    if (c + kS - 1 < 32) load(c + kS - 1);
+    cp_async_commit();              // (an empty group past the end keeps the count uniform)
+    const float *xb = xs_of(c % kS);
+    const uint8_t *wb = ws_of(c % kS);
     float acc[kTI][4];
 #pragma unroll
     for (int i = 0; i < kTI; ++i)
@@ -314,7 +307,15 @@ __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ x
 #pragma unroll
       for (int i = 0; i < kTI; ++i) xa[i] = *reinterpret_cast<const float4 *>(xb + (ty + 8 * i) * kRgPitch + k);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) wa[j] = *reinterpret_cast<const float4 *>(wb + (tx + 16 * j) * kRgPitch + k);
+      for (int j = 0; j < 4; ++j) {
+        if (kF32) {
+          wa[j] = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(wb) + (tx + 16 * j) * kRgPitch + k);
+        } else {  // four bf16 -> f32 (exact): element k in the low half
+          const uint2 u = *reinterpret_cast<const uint2 *>(reinterpret_cast<const uint16_t *>(wb) + (tx + 16 * j) * kRgPitchB + k);
+          wa[j] = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                              __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+        }
+      }
 #pragma unroll
       for (int i = 0; i < kTI; ++i)
 #pragma unroll
@@ -329,12 +330,8 @@ __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ x
     for (int i = 0; i < kTI; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) tot[i][j] = (c == 0) ? acc[i][j] : __fadd_rn(tot[i][j], acc[i][j]);
-    if (c + 1 < 32) {
-      store_w(un, wsm + (buf ^ 1) * kRgBuf);
-      cp_async_wait_all();
-    }
-    __syncthreads();  // the next chunk is in place; this chunk's buffers may be refilled
   }
+  cp_async_wait_all();
 #pragma unroll
   for (int i = 0; i < kTI; ++i) {
     const int t = t0 + ty + 8 * i;
@@ -930,42 +927,58 @@ struct SegOut {
   int rows, rank, n;  // n = 0: plain output
 };
 
+// The CTA's stores into peer memory are performed at system scope before the kernel ends, so the
+// flag that a later kernel on this stream stores (release, system scope) cannot overtake them:
+// the barrier orders every thread's stores before thread 0's fence, which is cumulative over
+// them. One fence per CTA; a fence in every thread cost one NVLink round trip per warp.
+__device__ __forceinline__ void cta_fence_system() {
+  __syncthreads();
+  if (threadIdx.x == 0) __threadfence_system();
+}
+
 __global__ void __launch_bounds__(256) k_combine(int T, const float *y, const int32_t *inv, const int32_t *offsets,
                                                  const float *sg, int sh_lo, int sh_hi, const int32_t *ids,
                                                  const int32_t *order, int e_lo, int e_hi, float *out,
                                                  int accumulate, const SegOut seg) {
   const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;  // one float4 of one token
-  if (idx >= (int64_t)T * (kH / 4)) return;
-  const int t = (int)(idx / (kH / 4)), h = (int)(idx % (kH / 4)) * 4;
+  const bool in = idx < (int64_t)T * (kH / 4);
+  if (!in && !seg.n) return;
+  const int t = in ? (int)(idx / (kH / 4)) : 0, h = in ? (int)(idx % (kH / 4)) * 4 : 0;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  bool work = sg && t >= sh_lo && t < sh_hi;
+  bool work = in && sg && t >= sh_lo && t < sh_hi;
+  if (in) {
 #pragma unroll
-  for (int i = 0; i < kK; ++i) {
-    const int slot = __ldg(order + (size_t)t * kK + i);
-    const int e = __ldg(ids + (size_t)t * kK + slot);
-    if (e < e_lo || e >= e_hi) continue;
-    work = true;
-    const int pos = __ldg(inv + (size_t)t * kK + slot);
-    const float4 v = __ldcs(reinterpret_cast<const float4 *>(y + (size_t)pos * kH + h));
-    acc.x = __fadd_rn(acc.x, v.x);
-    acc.y = __fadd_rn(acc.y, v.y);
-    acc.z = __fadd_rn(acc.z, v.z);
-    acc.w = __fadd_rn(acc.w, v.w);
+    for (int i = 0; i < kK; ++i) {
+      const int slot = __ldg(order + (size_t)t * kK + i);
+      const int e = __ldg(ids + (size_t)t * kK + slot);
+      if (e < e_lo || e >= e_hi) continue;
+      work = true;
+      const int pos = __ldg(inv + (size_t)t * kK + slot);
+      const float4 v = __ldcs(reinterpret_cast<const float4 *>(y + (size_t)pos * kH + h));
+      acc.x = __fadd_rn(acc.x, v.x);
+      acc.y = __fadd_rn(acc.y, v.y);
+      acc.z = __fadd_rn(acc.z, v.z);
+      acc.w = __fadd_rn(acc.w, v.w);
+    }
   }
   float4 r = acc;
-  if (sg && t >= sh_lo && t < sh_hi) {
+  if (in && sg && t >= sh_lo && t < sh_hi) {
     const float g = __ldg(sg + (t - sh_lo));
     const int pos = __ldg(offsets + kE) + (t - sh_lo);  // the shared expert's rows come last
     const float4 sh = __ldcs(reinterpret_cast<const float4 *>(y + (size_t)pos * kH + h));
     r = make_float4(__fadd_rn(acc.x, __fmul_rn(g, sh.x)), __fadd_rn(acc.y, __fmul_rn(g, sh.y)),
                     __fadd_rn(acc.z, __fmul_rn(g, sh.z)), __fadd_rn(acc.w, __fmul_rn(g, sh.w)));
   }
-  if (seg.n) {
-    if (!work) return;
-    const int s = t / seg.rows;
-    float *d = seg.base[s] + ((size_t)seg.rank * seg.rows + (t - s * seg.rows)) * kH + h;
-    *reinterpret_cast<float4 *>(d) = r;
-    __threadfence_system();  // peer stores complete before the return signal
+  if (seg.n) {  // every thread of the CTA reaches the closing fence
+    if (work) {
+      const int s = t / seg.rows;
+      float *b = seg.base[0];
+#pragma unroll
+      for (int k = 1; k < kMaxPeers; ++k)
+        if (k == s) b = seg.base[k];  // (a select, not an indexed copy of the parameter array)
+      *reinterpret_cast<float4 *>(b + ((size_t)seg.rank * seg.rows + (t - s * seg.rows)) * kH + h) = r;
+    }
+    cta_fence_system();
     return;
   }
   float4 *dst = reinterpret_cast<float4 *>(out + (size_t)t * kH + h);
@@ -1005,8 +1018,12 @@ struct EpDst {
   uint8_t *peer_recv[kMaxPeers];   // peer form: each rank's receive buffer
   uint32_t *epoch;                 // peer form: this rank's step counter (bumped by block 0)
   __device__ uint8_t *block(int d, int rank, int T) const {
-    return send ? send + (size_t)d * T * B200MOE_EP_ROW_BYTES
-                : peer_recv[d] + (size_t)rank * T * B200MOE_EP_ROW_BYTES;
+    if (send) return send + (size_t)d * T * B200MOE_EP_ROW_BYTES;
+    uint8_t *b = peer_recv[0];
+#pragma unroll
+    for (int k = 1; k < kMaxPeers; ++k)
+      if (k == d) b = peer_recv[k];  // a select: an indexed read would copy the array to local memory
+    return b + (size_t)rank * T * B200MOE_EP_ROW_BYTES;
   }
 };
 
@@ -1062,7 +1079,7 @@ __global__ void __launch_bounds__(1024) k_ep_plan(int T, const int32_t *ids, con
     reinterpret_cast<int4 *>(row + kEpIdsOff)[0] = none;
     reinterpret_cast<int4 *>(row + kEpIdsOff)[1] = none;
   }
-  if (!dst.send) __threadfence_system();  // peer stores complete before the dispatch signal
+  if (!dst.send) cta_fence_system();  // peer stores complete before the dispatch signal
 }
 
 // CTA t: token t's 4 KB of x16 into its row at every destination that takes it.
@@ -1074,7 +1091,7 @@ __global__ void __launch_bounds__(256) k_ep_copy(int T, const __half *x16, int r
     const int p = __ldg(pos + (size_t)t * world + d);
     if (p >= 0) reinterpret_cast<uint4 *>(dst.block(d, rank, T) + (size_t)p * B200MOE_EP_ROW_BYTES)[threadIdx.x] = v;
   }
-  if (!dst.send) __threadfence_system();
+  if (!dst.send) cta_fence_system();
 }
 
 // Peer signalling: lane d stores this step's epoch into rank d's flag word for this rank
@@ -1142,17 +1159,16 @@ bool a16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
 int g_num_sms = 0;
 
+template <bool kF32>
+cudaError_t router_gemm_attrs();
+
 int ensure_gemm_attrs() {
   static int done = 0;
   if (done) return B200MOE_OK;
   B2_CUDA(cudaFuncSetAttribute(k_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<1>::kSmem));
   B2_CUDA(cudaFuncSetAttribute(k_gemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<2>::kSmem));
-  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<false, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
-  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<true, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
-  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<false, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
-  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<true, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
-  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<false, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
-  B2_CUDA(cudaFuncSetAttribute(k_router_gemm<true, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRgSmem));
+  B2_CUDA(router_gemm_attrs<false>());
+  B2_CUDA(router_gemm_attrs<true>());
   int dev = 0;
   B2_CUDA(cudaGetDevice(&dev));
   B2_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
@@ -1286,18 +1302,59 @@ int check_prefill_layer(const b200moe_layer *L, const char *who, bool experts = 
   return B200MOE_OK;
 }
 
-// The router GEMM with the largest token tile that still gives every SM a CTA.
+// The router GEMM's token tile kTM (8 .. 64 in steps of 8): the one whose busiest SM has the
+// fewest token rows to multiply -- ceil(CTAs / SMs) CTAs of kTM rows -- and of those the
+// largest (more FMAs per shared-memory load). 4096 tokens on 148 SMs: kTM = 56, 296 CTAs, two
+// per SM (64 would give 256 CTAs: 108 SMs with two, 40 with one).
+template <bool kF32, int kTM>
+void router_gemm_launch(const float *xn, int T, const void *wg, const float *bias, uint16_t *logits,
+                        cudaStream_t s) {
+  k_router_gemm<kF32, kTM><<<dim3((T + kTM - 1) / kTM, kE / 64), 128, rg_smem<kF32, kTM>(), s>>>(xn, T, wg, bias, logits);
+}
+
+template <bool kF32, int kTM>
+cudaError_t router_gemm_attr() {
+  return cudaFuncSetAttribute((const void *)k_router_gemm<kF32, kTM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)rg_smem<kF32, kTM>());
+}
+
+template <bool kF32>
+cudaError_t router_gemm_attrs() {
+  const cudaError_t e[8] = {router_gemm_attr<kF32, 8>(),  router_gemm_attr<kF32, 16>(), router_gemm_attr<kF32, 24>(),
+                            router_gemm_attr<kF32, 32>(), router_gemm_attr<kF32, 40>(), router_gemm_attr<kF32, 48>(),
+                            router_gemm_attr<kF32, 56>(), router_gemm_attr<kF32, 64>()};
+  for (cudaError_t x : e)
+    if (x != cudaSuccess) return x;
+  return cudaSuccess;
+}
+
+int router_tile(int T, int sms) {
+  int best = 8;
+  long long best_cost = -1;
+  for (int tm = 8; tm <= 64; tm += 8) {
+    const long long ctas = (long long)((T + tm - 1) / tm) * (kE / 64);
+    const long long cost = (ctas + sms - 1) / sms * tm;
+    if (best_cost < 0 || cost <= best_cost) {
+      best = tm;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
 template <bool kF32>
 cudaError_t launch_router_gemm_t(const float *xn, int T, const void *wg, const float *bias, uint16_t *logits,
                                  cudaStream_t s) {
-  const int want = g_num_sms > 0 ? g_num_sms : 148;
-  auto ctas = [&](int tm) { return ((T + tm - 1) / tm) * (kE / 64); };
-  if (ctas(64) >= want)
-    k_router_gemm<kF32, 64><<<dim3((T + 63) / 64, kE / 64), 128, kRgSmem, s>>>(xn, T, wg, bias, logits);
-  else if (ctas(32) >= want)
-    k_router_gemm<kF32, 32><<<dim3((T + 31) / 32, kE / 64), 128, kRgSmem, s>>>(xn, T, wg, bias, logits);
-  else
-    k_router_gemm<kF32, 16><<<dim3((T + 15) / 16, kE / 64), 128, kRgSmem, s>>>(xn, T, wg, bias, logits);
+  switch (router_tile(T, g_num_sms > 0 ? g_num_sms : 148)) {
+    case 8: router_gemm_launch<kF32, 8>(xn, T, wg, bias, logits, s); break;
+    case 16: router_gemm_launch<kF32, 16>(xn, T, wg, bias, logits, s); break;
+    case 24: router_gemm_launch<kF32, 24>(xn, T, wg, bias, logits, s); break;
+    case 32: router_gemm_launch<kF32, 32>(xn, T, wg, bias, logits, s); break;
+    case 40: router_gemm_launch<kF32, 40>(xn, T, wg, bias, logits, s); break;
+    case 48: router_gemm_launch<kF32, 48>(xn, T, wg, bias, logits, s); break;
+    case 56: router_gemm_launch<kF32, 56>(xn, T, wg, bias, logits, s); break;
+    default: router_gemm_launch<kF32, 64>(xn, T, wg, bias, logits, s); break;
+  }
   return cudaGetLastError();
 }
 
