@@ -346,6 +346,102 @@ __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ x
   }
 }
 
+// ------------------------------------------------------------------------- k_router_rows
+// R1 for few tokens: warp w of CTA (bx, by) owns kEW expert rows (bf16 router: 2, f32: 1) and
+// tokens 8 by .. 8 by + 7. Lane c holds chunk c of each of its rows (64 values per row) in
+// registers and runs the chunk's 64 sequential fmaf for every (row, token) pair side by side
+// (16 independent chains); lane (i, j) then adds the 32 chunk sums of row i, token j left to
+// right. That is the declared order, so every logit equals k_router_gemm's bit for bit. The 8 x
+// rows sit in shared memory with a 68-float pitch per chunk, so the 32 lanes' 16-byte loads
+// spread over every bank. With few tokens the tiled GEMM's 32 chunks wait on L2 one after
+// another (36 us for 8 tokens); here each router row is read once per 8 tokens, every lane's
+// chunk in flight at once.
+constexpr int kRrTok = 8;                                     // tokens per CTA
+constexpr int kRrPitch = 68;                                  // floats per chunk row in shared memory
+constexpr int kRrXBytes = kRrTok * 32 * kRrPitch * 4;         // 69,632
+template <bool kF32>
+constexpr int rr_rows_per_warp() { return kF32 ? 1 : 2; }
+template <bool kF32>
+constexpr size_t rr_smem() { return (size_t)kRrXBytes + 8 * rr_rows_per_warp<kF32>() * kRrTok * 33 * 4; }
+
+template <bool kF32>
+__global__ void __launch_bounds__(256) k_router_rows(const float *__restrict__ xn, int T, const void *__restrict__ wg_,
+                                                     const float *bias, uint16_t *logits) {
+  constexpr int kEW = rr_rows_per_warp<kF32>();
+  extern __shared__ __align__(16) uint8_t rr_smem_raw[];
+  float *xs = reinterpret_cast<float *>(rr_smem_raw);               // [8 tokens][32 chunks][kRrPitch]
+  float *ps = reinterpret_cast<float *>(rr_smem_raw + kRrXBytes);   // [8 warps][kEW][8 tokens][33]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = (blockIdx.x * 8 + warp) * kEW, t0 = blockIdx.y * kRrTok;
+#pragma unroll
+  for (int q = 0; q < kRrTok * 32 * 16 / 256; ++q) {  // 8 rows x 512 slots of 16 B (zero rows past T)
+    const int idx = threadIdx.x + 256 * q;
+    const int j = idx >> 9, c = (idx >> 4) & 31, k = (idx & 15) * 4;
+    const bool in = t0 + j < T;
+    cp_async16(xs + (j * 32 + c) * kRrPitch + k, xn + (size_t)(in ? t0 + j : 0) * kH + 64 * c + k, in ? 16u : 0u);
+  }
+  cp_async_commit();
+  // this lane's chunk of each of the warp's router rows: bf16 pairs, or f32
+  uint32_t w[kEW][kF32 ? 64 : 32];
+#pragma unroll
+  for (int i = 0; i < kEW; ++i) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(wg_) +
+                                                       ((size_t)(e0 + i) * kH + 64 * lane) * (kF32 ? 4 : 2));
+#pragma unroll
+    for (int q = 0; q < (kF32 ? 16 : 8); ++q) {
+      const uint4 v = __ldg(src + q);
+      w[i][4 * q] = v.x; w[i][4 * q + 1] = v.y; w[i][4 * q + 2] = v.z; w[i][4 * q + 3] = v.w;
+    }
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  float acc[kEW][kRrTok];
+#pragma unroll
+  for (int i = 0; i < kEW; ++i)
+#pragma unroll
+    for (int j = 0; j < kRrTok; ++j) acc[i][j] = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 64; k += 4) {  // the chunk's 64 products, in k order
+    float wv[kEW][4];
+#pragma unroll
+    for (int i = 0; i < kEW; ++i) {
+      if (kF32) {
+        wv[i][0] = __uint_as_float(w[i][k]); wv[i][1] = __uint_as_float(w[i][k + 1]);
+        wv[i][2] = __uint_as_float(w[i][k + 2]); wv[i][3] = __uint_as_float(w[i][k + 3]);
+      } else {  // bf16 -> f32 exactly; element k in the low half
+        wv[i][0] = __uint_as_float(w[i][k / 2] << 16); wv[i][1] = __uint_as_float(w[i][k / 2] & 0xFFFF0000u);
+        wv[i][2] = __uint_as_float(w[i][k / 2 + 1] << 16); wv[i][3] = __uint_as_float(w[i][k / 2 + 1] & 0xFFFF0000u);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kRrTok; ++j) {
+      const float4 x = *reinterpret_cast<const float4 *>(xs + (j * 32 + lane) * kRrPitch + k);
+#pragma unroll
+      for (int i = 0; i < kEW; ++i) {
+        acc[i][j] = __fmaf_rn(x.x, wv[i][0], acc[i][j]);
+        acc[i][j] = __fmaf_rn(x.y, wv[i][1], acc[i][j]);
+        acc[i][j] = __fmaf_rn(x.z, wv[i][2], acc[i][j]);
+        acc[i][j] = __fmaf_rn(x.w, wv[i][3], acc[i][j]);
+      }
+    }
+  }
+  float *pw = ps + warp * kEW * kRrTok * 33;
+#pragma unroll
+  for (int i = 0; i < kEW; ++i)
+#pragma unroll
+    for (int j = 0; j < kRrTok; ++j) pw[(i * kRrTok + j) * 33 + lane] = acc[i][j];
+  __syncwarp();
+  const int i = lane / kRrTok, j = lane % kRrTok;
+  if (i < kEW && t0 + j < T) {
+    const float *pr = pw + (i * kRrTok + j) * 33;
+    float tot = pr[0];
+#pragma unroll
+    for (int c = 1; c < 32; ++c) tot = __fadd_rn(tot, pr[c]);
+    if (bias) tot = __fadd_rn(tot, bias[e0 + i]);
+    logits[(size_t)(t0 + j) * kE + e0 + i] = f2bf(tot);
+  }
+}
+
 // ------------------------------------------------------------------------- k_route_tok
 __global__ void __launch_bounds__(256) k_route_tok(const uint16_t *logits, int T, int32_t *ids, uint16_t *wb) {
   __shared__ Route rr[8];
@@ -1169,6 +1265,8 @@ int ensure_gemm_attrs() {
   B2_CUDA(cudaFuncSetAttribute(k_gemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<2>::kSmem));
   B2_CUDA(router_gemm_attrs<false>());
   B2_CUDA(router_gemm_attrs<true>());
+  B2_CUDA(cudaFuncSetAttribute(k_router_rows<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rr_smem<false>()));
+  B2_CUDA(cudaFuncSetAttribute(k_router_rows<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rr_smem<true>()));
   int dev = 0;
   B2_CUDA(cudaGetDevice(&dev));
   B2_CUDA(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
@@ -1358,8 +1456,22 @@ cudaError_t launch_router_gemm_t(const float *xn, int T, const void *wg, const f
   return cudaGetLastError();
 }
 
+// Up to kRouterRowsMaxT tokens take the row kernel, more the tiled GEMM (both give the same
+// bits). Measured route stage, row kernel / tiled GEMM: 34 / 61 us at 8 tokens, 51 / 63 at 256,
+// 72 / 67 at 512.
+#ifndef B2_ROUTER_ROWS_MAX_T
+#define B2_ROUTER_ROWS_MAX_T 384
+#endif
+constexpr int kRouterRowsMaxT = B2_ROUTER_ROWS_MAX_T;
+
 cudaError_t launch_router_gemm(bool f32, const float *xn, int T, const void *wg, const float *bias, uint16_t *logits,
                                cudaStream_t s) {
+  if (T <= kRouterRowsMaxT) {
+    const unsigned ty = (unsigned)((T + kRrTok - 1) / kRrTok);
+    if (f32) k_router_rows<true><<<dim3(kE / (8 * rr_rows_per_warp<true>()), ty), 256, rr_smem<true>(), s>>>(xn, T, wg, bias, logits);
+    else k_router_rows<false><<<dim3(kE / (8 * rr_rows_per_warp<false>()), ty), 256, rr_smem<false>(), s>>>(xn, T, wg, bias, logits);
+    return cudaGetLastError();
+  }
   return f32 ? launch_router_gemm_t<true>(xn, T, wg, bias, logits, s)
              : launch_router_gemm_t<false>(xn, T, wg, bias, logits, s);
 }
