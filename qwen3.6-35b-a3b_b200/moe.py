@@ -78,10 +78,11 @@ def _tokens(g, device) -> tuple:
 
 
 # At and above this many tokens the grouped-GEMM path is used. Measured on the 40-layer stack
-# (config 2 routing law): the decode kernels re-read each token's expert rows, ~0.58 ms per
-# token over 40 layers (5.15 ms at 8 tokens, 9.76 ms at 16), while the grouped GEMMs cost a
-# nearly flat ~6 ms (6.0 ms at 2 tokens, 6.9 ms at 32): they cross near 10 tokens.
-PREFILL_MIN_TOKENS = 10
+# (config 2 routing law, one B200): the decode kernels re-read each token's expert rows, about
+# 0.6 ms per token over 40 layers (1.59 ms at 2 tokens, 2.78 at 4, 3.56 at 6, 4.95 at 8), while
+# the grouped GEMMs cost a nearly flat ~3 ms (2.92 ms at 2 tokens, 3.01 at 4, 3.10 at 6, 3.14 at
+# 8, 3.44 at 32): they cross between 4 and 6 tokens.
+PREFILL_MIN_TOKENS = 5
 
 
 def prefill_workspace(T: int, device) -> torch.Tensor:

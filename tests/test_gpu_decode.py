@@ -34,7 +34,7 @@ def test_decode_vs_oracle(cuda, layer0, T):
     from b200moe import moe, synth
     xb = synth.tokens(0, T, stream=1)
     g = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).reshape(1, T, 2048).to(cuda)
-    out, info = moe.moe_block(g, layer0, 0)
+    out, info = moe.moe_block(g, layer0, 0, path="decode")  # (8, 9 tokens: "auto" takes the GEMMs)
     torch.cuda.synchronize()
     assert out.shape == (1, T, 2048) and out.dtype == torch.float32
     ids = info["ids"].reshape(T, 8).cpu().numpy()
