@@ -457,22 +457,31 @@ __global__ void __launch_bounds__(256) k_route_tok(const uint16_t *logits, int T
 
 // ------------------------------------------------------------------------- k_count
 // Per token: count its slots whose expert lies in [e_lo, e_hi), and the combine order of its
-// 8 slots (ascending expert id; ties cannot occur, top-8 ids are distinct).
+// 8 slots (ascending expert id; ties cannot occur, top-8 ids are distinct). The counts go
+// through a per-CTA histogram in shared memory: one global atomic per (CTA, expert) instead of
+// one per slot on 256 hot addresses.
 __global__ void __launch_bounds__(256) k_count(int T, const int32_t *ids, int e_lo, int e_hi, int32_t *counts,
                                                int32_t *order) {
+  __shared__ int hist[kE];
+  for (int i = threadIdx.x; i < kE; i += 256) hist[i] = 0;
+  __syncthreads();
   const int t = blockIdx.x * 256 + threadIdx.x;
-  if (t >= T) return;
-  int id[kK];
+  if (t < T) {
+    int id[kK];
 #pragma unroll
-  for (int k = 0; k < kK; ++k) id[k] = __ldg(ids + (size_t)t * kK + k);
+    for (int k = 0; k < kK; ++k) id[k] = __ldg(ids + (size_t)t * kK + k);
 #pragma unroll
-  for (int k = 0; k < kK; ++k) {
-    if (id[k] >= e_lo && id[k] < e_hi) atomicAdd(counts + id[k], 1);
-    int rank = 0;
+    for (int k = 0; k < kK; ++k) {
+      if (id[k] >= e_lo && id[k] < e_hi) atomicAdd(&hist[id[k]], 1);
+      int rank = 0;
 #pragma unroll
-    for (int j = 0; j < kK; ++j) rank += (id[j] < id[k] || (id[j] == id[k] && j < k)) ? 1 : 0;
-    order[(size_t)t * kK + rank] = k;
+      for (int j = 0; j < kK; ++j) rank += (id[j] < id[k] || (id[j] == id[k] && j < k)) ? 1 : 0;
+      order[(size_t)t * kK + rank] = k;
+    }
   }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kE; i += 256)
+    if (hist[i]) atomicAdd(counts + i, hist[i]);
 }
 
 // ------------------------------------------------------------------------- k_plan
@@ -498,14 +507,25 @@ __global__ void __launch_bounds__(512) k_plan(int n_shared, const int32_t *count
   }
   if (e < kNE) offsets[e] = sc[e] - cnt;
   if (e == kNE - 1) offsets[kNE] = sc[e];
+  __shared__ int s_nch[kNE], s_cb[kNE], s_r0[kNE], s_cnt[kNE];
   if (e <= kE) {
-    const int cbase = sn[pos] - nch;
-    const int r0 = sc[e] - cnt;
-    for (int c = 0; c < nch; ++c) {  // nch near-equal chunks (at most kChunk rows each)
-      const int a0 = (int)((long long)c * cnt / nch), a1 = (int)((long long)(c + 1) * cnt / nch);
-      const int ci = cbase + c;
-      for (int jt = 0; jt < 4; ++jt) tiles1[4 * ci + jt] = make_int4(e, r0 + a0, a1 - a0, jt);
-      for (int ht = 0; ht < 16; ++ht) tiles2[16 * ci + ht] = make_int4(e, r0 + a0, a1 - a0, ht);
+    s_nch[e] = nch;
+    s_cb[e] = sn[pos] - nch;
+    s_r0[e] = sc[e] - cnt;
+    s_cnt[e] = cnt;
+  }
+  __syncthreads();
+  // The tile tables, a warp per expert: each of the expert's nch near-equal chunks (at most
+  // kChunk rows) gives 4 gate_up tiles and 16 down tiles. (A thread per expert left the shared
+  // expert's T / kChunk chunks to one thread.)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int ee = warp; ee <= kE; ee += 16) {
+    const int nc = s_nch[ee], cb = s_cb[ee], r0 = s_r0[ee], cn = s_cnt[ee];
+    for (int q = lane; q < nc * 20; q += 32) {
+      const int c = q / 20, k = q % 20;
+      const int a0 = (int)((long long)c * cn / nc), a1 = (int)((long long)(c + 1) * cn / nc);
+      if (k < 4) tiles1[4 * (cb + c) + k] = make_int4(ee, r0 + a0, a1 - a0, k);
+      else tiles2[16 * (cb + c) + k - 4] = make_int4(ee, r0 + a0, a1 - a0, k - 4);
     }
   }
   if (e == 0) {
@@ -516,23 +536,35 @@ __global__ void __launch_bounds__(512) k_plan(int n_shared, const int32_t *count
 
 // ------------------------------------------------------------------------- k_fill
 // One thread per assignment a = t * 8 + slot whose expert is in range: it takes a row of its
-// expert's range by an atomic countdown of that expert's count (which ends at zero), and
+// expert's range (the count of that expert ends at zero), and
 // records plist[row] = a, inv[a] = row and the row's routing weight wrow[row] (the bf16 value
 // as f32; 1 for the shared expert's rows). The order of rows inside an expert changes no result:
 // every GEMM column, and every token's combine, is computed on its own. Rows from
 // offsets[kE] on are the shared expert's: tokens sh_lo .. sh_hi-1 in order.
-__global__ void __launch_bounds__(256) k_fill(int T, int sh_lo, int sh_hi, const int32_t *ids, const uint16_t *wb,
-                                              int e_lo, int e_hi, const int32_t *offsets, int32_t *counts,
-                                              int32_t *plist, int32_t *inv, float *wrow) {
-  const int a = blockIdx.x * 256 + threadIdx.x;
+__global__ void __launch_bounds__(1024) k_fill(int T, int sh_lo, int sh_hi, const int32_t *ids, const uint16_t *wb,
+                                               int e_lo, int e_hi, const int32_t *offsets, int32_t *counts,
+                                               int32_t *plist, int32_t *inv, float *wrow) {
+  // The CTA's assignments of each expert take consecutive rows: a shared-memory count, then one
+  // global atomic per (CTA, expert) reserves the range (counting the expert's count down to 0).
+  __shared__ int hist[kE], base[kE];
+  for (int i = threadIdx.x; i < kE; i += 1024) hist[i] = 0;
+  __syncthreads();
+  const int a = blockIdx.x * 1024 + threadIdx.x;
+  int e = -1, li = 0;
   if (a < T * kK) {
-    const int e = __ldg(ids + a);
-    if (e >= e_lo && e < e_hi) {
-      const int row = __ldg(offsets + e) + atomicSub(counts + e, 1) - 1;
-      plist[row] = a;
-      inv[a] = row;
-      wrow[row] = bf16f(__ldg(wb + a));
-    }
+    e = __ldg(ids + a);
+    if (e >= e_lo && e < e_hi) li = atomicAdd(&hist[e], 1);
+    else e = -1;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kE; i += 1024)
+    if (hist[i]) base[i] = atomicSub(counts + i, hist[i]) - hist[i];
+  __syncthreads();
+  if (e >= 0) {
+    const int row = __ldg(offsets + e) + base[e] + li;
+    plist[row] = a;
+    inv[a] = row;
+    wrow[row] = bf16f(__ldg(wb + a));
   }
   if (a < sh_hi - sh_lo) {
     const int row = __ldg(offsets + kE) + a;
@@ -1505,7 +1537,7 @@ int experts_stage(const __half *x16, int T, const int32_t *ids, const uint16_t *
   if (!sg) sh_lo = sh_hi = 0;
   k_plan<<<1, 512, 0, s>>>(sh_hi - sh_lo, w.counts, w.offsets, w.tiles1, w.tiles2, w.ntiles);
   B2_CUDA(cudaGetLastError());
-  k_fill<<<(unsigned)(((int64_t)T * kK + 255) / 256), 256, 0, s>>>(T, sh_lo, sh_hi, ids, wb, e_lo, e_hi, w.offsets,
+  k_fill<<<(unsigned)(((int64_t)T * kK + 1023) / 1024), 1024, 0, s>>>(T, sh_lo, sh_hi, ids, wb, e_lo, e_hi, w.offsets,
                                                                    w.counts, w.plist, w.inv, w.wrow);
   B2_CUDA(cudaGetLastError());
   GemmParams g;
