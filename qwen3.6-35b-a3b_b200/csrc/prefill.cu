@@ -347,35 +347,46 @@ __global__ void __launch_bounds__(128) k_router_gemm(const float *__restrict__ x
 }
 
 // ------------------------------------------------------------------------- k_router_rows
-// R1 for few tokens: warp w of CTA (bx, by) owns kEW expert rows (bf16 router: 2, f32: 1) and
-// tokens 8 by .. 8 by + 7. Lane c holds chunk c of each of its rows (64 values per row) in
-// registers and runs the chunk's 64 sequential fmaf for every (row, token) pair side by side
-// (16 independent chains); lane (i, j) then adds the 32 chunk sums of row i, token j left to
-// right. That is the declared order, so every logit equals k_router_gemm's bit for bit. The 8 x
-// rows sit in shared memory with a 68-float pitch per chunk, so the 32 lanes' 16-byte loads
-// spread over every bank. With few tokens the tiled GEMM's 32 chunks wait on L2 one after
-// another (36 us for 8 tokens); here each router row is read once per 8 tokens, every lane's
-// chunk in flight at once.
+// R1 for up to a few hundred tokens: warp w of CTA (bx, by) owns kEW expert rows (bf16 router:
+// 4 rows, 4 warps per CTA; f32: 1 row, 8 warps) and tokens 8 by .. 8 by + 7. Lane c holds chunk
+// c of each of its rows (64 values per row) in registers and runs the chunk's 64 sequential fmaf
+// for every (row, token) pair side by side (32 independent chains for bf16); lane (i, j) then
+// adds the 32 chunk sums of row i, token j left to right. That is the declared order, so every
+// logit equals k_router_gemm's bit for bit. The 8 x rows sit in shared memory with a 68-float
+// pitch per chunk, so the 32 lanes' 16-byte loads spread over every bank; shared-memory reads
+// bound the kernel, so each x load feeds the warp's kEW rows (measured route stage at 512
+// tokens: 66 us with 2 rows x 8 warps, 63 with 4 x 4). With few tokens the tiled GEMM's 32
+// chunks wait on L2 one after another (36 us for 8 tokens); here each router row is read once
+// per 8 tokens, every lane's chunk in flight at once.
+#ifndef B2_RR_ROWS
+#define B2_RR_ROWS 4
+#endif
+#ifndef B2_RR_WARPS
+#define B2_RR_WARPS 4
+#endif
 constexpr int kRrTok = 8;                                     // tokens per CTA
 constexpr int kRrPitch = 68;                                  // floats per chunk row in shared memory
 constexpr int kRrXBytes = kRrTok * 32 * kRrPitch * 4;         // 69,632
 template <bool kF32>
-constexpr int rr_rows_per_warp() { return kF32 ? 1 : 2; }
+constexpr int rr_rows_per_warp() { return kF32 ? 1 : B2_RR_ROWS; }
 template <bool kF32>
-constexpr size_t rr_smem() { return (size_t)kRrXBytes + 8 * rr_rows_per_warp<kF32>() * kRrTok * 33 * 4; }
+constexpr int rr_warps() { return kF32 ? 8 : B2_RR_WARPS; }
+template <bool kF32>
+constexpr size_t rr_smem() { return (size_t)kRrXBytes + rr_warps<kF32>() * rr_rows_per_warp<kF32>() * kRrTok * 33 * 4; }
 
 template <bool kF32>
-__global__ void __launch_bounds__(256) k_router_rows(const float *__restrict__ xn, int T, const void *__restrict__ wg_,
+__global__ void __launch_bounds__(256, 1) k_router_rows(const float *__restrict__ xn, int T, const void *__restrict__ wg_,
                                                      const float *bias, uint16_t *logits) {
   constexpr int kEW = rr_rows_per_warp<kF32>();
+  constexpr int kNT = 32 * rr_warps<kF32>();
   extern __shared__ __align__(16) uint8_t rr_smem_raw[];
   float *xs = reinterpret_cast<float *>(rr_smem_raw);               // [8 tokens][32 chunks][kRrPitch]
-  float *ps = reinterpret_cast<float *>(rr_smem_raw + kRrXBytes);   // [8 warps][kEW][8 tokens][33]
+  float *ps = reinterpret_cast<float *>(rr_smem_raw + kRrXBytes);   // [warps][kEW][8 tokens][33]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e0 = (blockIdx.x * 8 + warp) * kEW, t0 = blockIdx.y * kRrTok;
+  const int e0 = (blockIdx.x * rr_warps<kF32>() + warp) * kEW, t0 = blockIdx.y * kRrTok;
 #pragma unroll
-  for (int q = 0; q < kRrTok * 32 * 16 / 256; ++q) {  // 8 rows x 512 slots of 16 B (zero rows past T)
-    const int idx = threadIdx.x + 256 * q;
+  for (int q = 0; q < kRrTok * 32 * 16 / kNT; ++q) {  // 8 rows x 512 slots of 16 B (zero rows past T)
+    const int idx = threadIdx.x + kNT * q;
     const int j = idx >> 9, c = (idx >> 4) & 31, k = (idx & 15) * 4;
     const bool in = t0 + j < T;
     cp_async16(xs + (j * 32 + c) * kRrPitch + k, xn + (size_t)(in ? t0 + j : 0) * kH + 64 * c + k, in ? 16u : 0u);
@@ -1489,10 +1500,10 @@ cudaError_t launch_router_gemm_t(const float *xn, int T, const void *wg, const f
 }
 
 // Up to kRouterRowsMaxT tokens take the row kernel, more the tiled GEMM (both give the same
-// bits). Measured route stage, row kernel / tiled GEMM: 34 / 61 us at 8 tokens, 51 / 63 at 256,
-// 72 / 67 at 512.
+// bits). Measured route stage, row kernel / tiled GEMM: 34 / 61 us at 8 tokens, 47 / 63 at 256,
+// 63 / 67 at 512, 89 / 78 at 1024.
 #ifndef B2_ROUTER_ROWS_MAX_T
-#define B2_ROUTER_ROWS_MAX_T 384
+#define B2_ROUTER_ROWS_MAX_T 576
 #endif
 constexpr int kRouterRowsMaxT = B2_ROUTER_ROWS_MAX_T;
 
@@ -1500,8 +1511,12 @@ cudaError_t launch_router_gemm(bool f32, const float *xn, int T, const void *wg,
                                cudaStream_t s) {
   if (T <= kRouterRowsMaxT) {
     const unsigned ty = (unsigned)((T + kRrTok - 1) / kRrTok);
-    if (f32) k_router_rows<true><<<dim3(kE / (8 * rr_rows_per_warp<true>()), ty), 256, rr_smem<true>(), s>>>(xn, T, wg, bias, logits);
-    else k_router_rows<false><<<dim3(kE / (8 * rr_rows_per_warp<false>()), ty), 256, rr_smem<false>(), s>>>(xn, T, wg, bias, logits);
+    if (f32)
+      k_router_rows<true><<<dim3(kE / (rr_warps<true>() * rr_rows_per_warp<true>()), ty), 32 * rr_warps<true>(),
+                            rr_smem<true>(), s>>>(xn, T, wg, bias, logits);
+    else
+      k_router_rows<false><<<dim3(kE / (rr_warps<false>() * rr_rows_per_warp<false>()), ty), 32 * rr_warps<false>(),
+                             rr_smem<false>(), s>>>(xn, T, wg, bias, logits);
     return cudaGetLastError();
   }
   return f32 ? launch_router_gemm_t<true>(xn, T, wg, bias, logits, s)

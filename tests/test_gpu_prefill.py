@@ -209,7 +209,7 @@ def test_block_stages_match_oracle_stages(cuda, layer3):
 
 @pytest.mark.parametrize("T", [17, 300, 1024, 2368, 4096])
 def test_route_stage_every_router_tile(cuda, layer3, T):
-    """The prefill router: up to 384 tokens take the row kernel (a warp per two router rows, a lane
+    """The prefill router: up to 576 tokens take the row kernel (a warp per four router rows, a lane
     per K chunk), more the tiled GEMM, whose token tile (8 .. 64 tokens per CTA) is picked by
     batch size so the busiest SM has the fewest rows: on 148 SMs 17 and 300 tokens take the row
     kernel, 1024 the 32-token tile, 2368 the 64-token one and 4096 the 56-token one. Each output
