@@ -203,8 +203,12 @@ int b200moe_debug_decode_faults(long long wait_budget_cycles, int withhold_cta);
  * b200moe_moe_decode_noalloc and b200moe_stack_decode run one persistent kernel per call
  * (ctas CTAs, one per SM, launched in thread-block clusters of `cluster` CTAs; cluster 1 =
  * a cooperative launch) when the device can keep all of them resident, else the
- * three-kernel-per-layer path (ctas = cluster = 0). Both give identical bits. Introspection
- * only; no counterpart in the reference. Call with the device current. */
+ * three-kernel-per-layer path (ctas = cluster = 0). Both give the same routing ids and weights;
+ * for Q4_K layers the persistent kernel runs the expert dots as exact-product int8 tensor-core
+ * MMAs over a 24-bit fixed-point image of x and s, so its outputs agree with the three-kernel
+ * path's f32 dots to ~1e-6 relative rather than bit for bit (layers in the other block formats:
+ * bit for bit). Every call is deterministic. Introspection only; no counterpart in the
+ * reference. Call with the device current. */
 int b200moe_decode_persistent_info(int *ctas, int *cluster);
 
 /* *formats = 1 when the persistent kernel also runs single-token layers in the other block

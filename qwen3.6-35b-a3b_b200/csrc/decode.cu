@@ -611,7 +611,8 @@ cudaError_t launch_down(const b200moe_layer *L, unsigned grid, cudaStream_t s, c
 constexpr int kMaxT = 1 << 16;
 
 // One token through n_layers layers with the persistent kernel (persist.cu): x mode (one
-// layer, out = block(x)) when resid is NULL, else resid mode. Same bits as run_layer.
+// layer, out = block(x)) when resid is NULL, else resid mode. Same routing as run_layer; the
+// Q4_K expert dots run on the tensor cores there (agreeing with run_layer's to ~1e-6 relative).
 int run_persistent(const void *x, int x_dtype, float *resid, float eps, int n_layers, const b200moe_layer *layers,
                    float *out, int32_t *ids_out, uint16_t *w_out, const DecodeWS &w, cudaStream_t s) {
   b2mega::Args a = {};

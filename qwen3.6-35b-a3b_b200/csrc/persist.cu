@@ -44,15 +44,19 @@
 // sequential reads of the declared orders and the Q4_K chunk gathers are free of bank
 // conflicts.
 //
-// The arithmetic of every value (RMSNorm, R1 logits in the declared chunk order, R2..R5,
-// per-lane Q4_K chunk dots, warp sums, SiLU, combine order, residual add) is the same sequence
-// of operations as the three-kernel path in decode.cu, so both paths give identical bits. Layers
-// in the published file's other block formats (Q5_K / Q6_K down, Q8_0 shared) run in the
-// kMode = 2 instantiation with kq_dot.cuh's chunk dots over the staged rows, likewise
-// bit-identical to the gather-GEMV kernels.
+// RMSNorm, R1 logits in the declared chunk order, R2..R5, SiLU, the combine order and the
+// residual add are the same sequence of operations as the three-kernel path in decode.cu (routing
+// ids and weights bit-identical for the same residual). The Q4_K expert dots of modes 0 / 1 run
+// on the tensor cores (q4k_mma_rows: int8 MMAs over the raw quants and an exact three-digit
+// fixed-point image of x / s, 2^-23 of the vector's largest magnitude), so their values agree
+// with the three-kernel path's f32 dots to ~1e-7 relative rather than bit for bit. Layers in the
+// published file's other block formats (Q5_K / Q6_K down, Q8_0 shared) run in the kMode = 2
+// instantiation with kq_dot.cuh's chunk dots over the staged rows, bit-identical to the
+// gather-GEMV kernels.
 #include <atomic>
 
 #include "common.cuh"
+#include "imma.cuh"
 #include "kq_dot.cuh"
 #include "mega.cuh"
 #include "route.cuh"
@@ -75,6 +79,14 @@ constexpr int kGuChunks = 8;             // routed gate/up arrival chunks (one m
 constexpr int kGuChunk = kQ / kGuChunks; // 4 row pairs per chunk
 constexpr int kPadSeg = 68;              // padded pitch of a 64-float segment
 constexpr int kResPad = kH / 64 * kPadSeg;  // 2176 floats
+// Modes 0 / 1 (tensor-core dots): the three int8 digit planes of x and of each expert's s, each
+// plane 32 bytes longer than its vector so the three planes a fragment load reads start on
+// different banks; the per-K-part row sums (phase G: [36 pairs][gate, up][4 parts], phase D:
+// [9 slots][4 parts][16 rows], f32, one region).
+constexpr int kDigPitchX = kH + 32;
+constexpr int kDigPitchS = kI + 32;
+constexpr int kPartBytes = (kK + 1) * 4 * kHr * 4;
+static_assert((kQ + kJ) * 2 * 4 * 4 <= kPartBytes, "phase G part sums fit the region");
 
 // exchange slots (64-bit words, see mega.cuh): per CTA c, line-aligned, written by c only
 using b2mega::kSlotLogits;  // word 0: logits 2c | 2c+1 << 16
@@ -114,14 +126,26 @@ constexpr int kOffSsh = kOffS + kK * kI * 4;                 // [512] f32 shared
 constexpr int kOffDl = kOffSsh + kI * 4;                     // [2048] f32 gathered deltas
 constexpr int kOffLg = kOffDl + kH * 4;                      // [128] u32 gathered logit pairs
 constexpr int kOffRt = kOffLg + kN * 4;                      // [kRouterBufs][3 rows][slot] router rows
+//
+// Modes 0 / 1 run the Q4_K dots on the tensor cores (see q4k_mma_rows) and stage the gate / up
+// rows so that the eight rows one fragment load touches sit at four different offsets modulo
+// 128 bytes (two rows per offset: two shared-memory wavefronts per 256-byte warp load, the
+// minimum): routed chunk g at g * kChunkPitch (4 rows + 32 bytes, so chunks 2t and 2t+1 differ
+// by 32 bytes), the up array 64 bytes off the gate array. Mode 2 keeps the dense layout.
 template <int kMode>
 struct Lay {
   static constexpr bool kFmt = kMode == 2;
+  static constexpr bool kTc = !kFmt;
   static constexpr int kRouterSlot = kMode >= 1 ? kH * 4 : kH * 2;       // bytes per router row slot
   static constexpr int kRouterBufs = kFmt ? 1 : 2;
-  static constexpr int kOffGu = kOffRt + kRouterBufs * kRtRows * kRouterSlot;  // [36] gate rows, then [36] up rows
+  static constexpr int kOffGu = kOffRt + kRouterBufs * kRtRows * kRouterSlot;  // gate rows, then up rows
+  static constexpr int kChunkPitch = kGuChunk * kRowUp + (kTc ? 32 : 0);       // routed chunk g at g * pitch
+  static constexpr int kShOff = kGuChunks * kChunkPitch;                       // the 4 shared rows (dense)
+  static constexpr int kGuArr = kShOff + kJ * kRowUp;                          // one array: gate or up
+  static constexpr int kUpOff = kGuArr + (kTc ? 64 : 0);                       // up array, from the gate array
+  static constexpr int kGuBytes = kUpOff + kGuArr;
   static constexpr int kShRow = (int)row_bytes(B200MOE_TYPE_Q8_0, kH);   // mode 2: shared gate / up row slot
-  static constexpr int kOffShGu = kOffGu + (kQ + kJ) * kRowPair;         // mode 2: [4] gate rows, then [4] up rows
+  static constexpr int kOffShGu = kOffGu + kGuBytes;                     // mode 2: [4] gate rows, then [4] up rows
   static constexpr int kOffDn = kOffShGu + (kFmt ? 2 * kJ * kShRow : 0);  // [8] routed down slots of 16 rows
   static constexpr int kDnSlot = kHr * (kFmt ? (int)row_bytes(B200MOE_TYPE_Q6_K, kI) : kRowDown);
   static constexpr int kOffDnSh = kOffDn + kK * kDnSlot;                  // the shared expert's 16 down rows
@@ -130,13 +154,24 @@ struct Lay {
   static constexpr int kOffMisc = kOffRr + 128;                           // [3] router row results, [36] s out
   static constexpr int kOffScr = kOffMisc + 256;                          // [12][32] f32 per-warp scratch
   static constexpr int kOffBar = kOffScr + 12 * 32 * 4;                   // mbarriers
-  static constexpr int kSmem = kOffBar + 256;
+  static constexpr int kOffPart = kOffBar + 256;                          // modes 0 / 1: per-K-part row sums
+  static constexpr int kSmem = kOffPart + (kTc ? kPartBytes : 0);
 };
 static_assert(Lay<0>::kOffDnSh == Lay<0>::kOffDn + 8 * kHr * kRowDown && Lay<1>::kOffO == Lay<1>::kOffDnSh + kHr * kRowDown,
               "modes 0 / 1: the [9][16] down rows of one array");
 static_assert(Lay<2>::kSmem <= 232448 && Lay<1>::kSmem <= 232448, "227 KB of shared memory per CTA");
 static_assert(Lay<2>::kOffShGu % 128 == 0 && Lay<2>::kOffDn % 128 == 0 && Lay<2>::kOffDnSh % 128 == 0,
               "bulk-copy destinations");
+static_assert(Lay<2>::kGuBytes == (kQ + kJ) * kRowPair && Lay<2>::kChunkPitch == kGuChunk * kRowUp,
+              "mode 2: the dense gate / up staging");
+static_assert(Lay<0>::kOffGu % 128 == 0 && Lay<1>::kOffGu % 128 == 0 && Lay<0>::kChunkPitch % 128 == 32 &&
+                  Lay<0>::kUpOff % 128 == 64 && Lay<0>::kShOff % 128 == 0 && Lay<0>::kOffDn % 16 == 0 &&
+                  Lay<1>::kOffDn % 16 == 0,
+              "modes 0 / 1: the skewed gate / up staging (bank offsets 0 / 32 / 64 / 96)");
+// Modes 0 / 1: the digit planes of the tensor-core dots. x (2048) lives in the router-row buffer
+// the layer has finished with, s (9 x 512) in the routed gate-row area phase G has finished with.
+static_assert(3 * kDigPitchX + kH / 32 * 4 <= kRtRows * kH * 2, "x digits fit one router-row buffer");
+static_assert(9 * 3 * kDigPitchS + 9 * (kI / 32) * 4 <= Lay<0>::kShOff, "s digits fit the routed gate rows");
 
 // ---------------------------------------------------------------- device helpers
 __device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t *p) {
@@ -229,6 +264,84 @@ __device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t rank) {
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Named barrier 1 over warps 1..11 (warp 0 routes meanwhile).
+__device__ __forceinline__ void bar_sync_g() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads - 32) : "memory"); }
+
+// ---------------------------------------------------------------- tensor-core Q4_K dots (modes 0 / 1)
+// The expert dots of modes 0 / 1 run as exact-product int8 MMAs (imma.cuh: raw quants as A, a
+// three-digit fixed-point image of x or s as B columns 0..2, per-sub-block integer results scaled
+// by the 6-bit scales, the min term from exact per-sub-block sums of the image).
+
+// One warp: the dots of 16 Q4_K rows with v over super-blocks [b0, b1) and, within each, the
+// 32-byte quant groups [j0, j1) (sub-blocks 2j0 .. 2j1-1). Fragment row g = lane / 4 reads row
+// ra, fragment row g + 8 row rb. dig: digit plane 0 (planes at pitch dpitch, element order);
+// sx: per-sub-block sums of n (f32, element order / 32). Lane t = lane % 4 of group g supplies
+// quant bytes 8t..8t+7 of each group (low nibbles: sub-block 2j, high: 2j+1), so MMA index
+// k = 4t + i is element 32 s + 8t + i and k = 16 + 4t + i element 32 s + 8t + 4 + i of sub-block
+// s; the B fragment of lane (g < 3, t) is digit plane g at those elements, one 8-byte load.
+// Returns the sums for ra and rb (in units of v * 2^k), the same in all four lanes of the group.
+__device__ __forceinline__ void q4k_mma_rows(const uint8_t *ra, const uint8_t *rb, const int8_t *dig, int dpitch,
+                                             const float *sx, int b0, int b1, int j0, int j1, float &acc_a,
+                                             float &acc_b) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const uint8_t *dp = reinterpret_cast<const uint8_t *>(dig) + (g < 3 ? g : 0) * dpitch + 8 * t;
+  // lane t holds D columns 2t, 2t+1: digit planes 0 (x 65536) and 1 (x 256) in lane 0, plane 2 in
+  // lane 1 (its second column, and lanes 2 and 3, are zero columns)
+  const float flo = t == 0 ? 65536.0f : (t == 1 ? 1.0f : 0.0f), fhi = t == 0 ? 256.0f : 0.0f;
+  constexpr uint32_t kNib = 0x0F0F0F0Fu;
+  float fa = 0.0f, fb = 0.0f;
+  for (int b = b0; b < b1; ++b) {
+    const uint4 ha = *reinterpret_cast<const uint4 *>(ra + kQB * b);
+    const uint4 hb = *reinterpret_cast<const uint4 *>(rb + kQB * b);
+    // get_scale_min_k4, byte-parallel: byte i of the lo word is sub-block i, of the hi word 4 + i
+    const uint32_t sa_lo = ha.y & 0x3F3F3F3Fu, sa_hi = (ha.w & 0x0F0F0F0Fu) | ((ha.y >> 2) & 0x30303030u);
+    const uint32_t sb_lo = hb.y & 0x3F3F3F3Fu, sb_hi = (hb.w & 0x0F0F0F0Fu) | ((hb.y >> 2) & 0x30303030u);
+    int ia0 = 0, ia1 = 0, ib0 = 0, ib1 = 0;
+#pragma unroll 2
+    for (int j = j0; j < j1; ++j) {
+      const uint2 wa = lds64(ra + kQB * b + 16 + 32 * j + 8 * t);
+      const uint2 wb = lds64(rb + kQB * b + 16 + 32 * j + 8 * t);
+      uint2 x0 = make_uint2(0u, 0u), x1 = make_uint2(0u, 0u);
+      if (g < 3) {
+        x0 = lds64(dp + 256 * b + 64 * j);
+        x1 = lds64(dp + 256 * b + 64 * j + 32);
+      }
+      int d[4], e[4];
+      mma_s8(wa.x & kNib, wb.x & kNib, wa.y & kNib, wb.y & kNib, x0.x, x0.y, d);
+      mma_s8((wa.x >> 4) & kNib, (wb.x >> 4) & kNib, (wa.y >> 4) & kNib, (wb.y >> 4) & kNib, x1.x, x1.y, e);
+      const int sh = 16 * (j & 1);  // sub-blocks 2j, 2j+1: bytes 2(j&1), 2(j&1)+1 of the lo / hi word
+      const uint32_t swa = j < 2 ? sa_lo : sa_hi, swb = j < 2 ? sb_lo : sb_hi;
+      const int sca0 = (int)((swa >> sh) & 0xFFu), sca1 = (int)((swa >> (sh + 8)) & 0xFFu);
+      const int scb0 = (int)((swb >> sh) & 0xFFu), scb1 = (int)((swb >> (sh + 8)) & 0xFFu);
+      ia0 += sca0 * d[0] + sca1 * e[0];
+      ia1 += sca0 * d[1] + sca1 * e[1];
+      ib0 += scb0 * d[2] + scb1 * e[2];
+      ib1 += scb0 * d[3] + scb1 * e[3];
+    }
+    const float da = f16f(ha.x), db = f16f(hb.x);
+    fa = fmaf(da, fmaf(fhi, (float)ia1, flo * (float)ia0), fa);
+    fb = fmaf(db, fmaf(fhi, (float)ib1, flo * (float)ib0), fb);
+    // the min term: lane t takes sub-blocks 2j0 + t, 2j0 + t + 4 (those below 2j1) of both rows
+    const uint32_t ma_lo = ha.z & 0x3F3F3F3Fu, ma_hi = ((ha.w >> 4) & 0x0F0F0F0Fu) | ((ha.z >> 2) & 0x30303030u);
+    const uint32_t mb_lo = hb.z & 0x3F3F3F3Fu, mb_hi = ((hb.w >> 4) & 0x0F0F0F0Fu) | ((hb.z >> 2) & 0x30303030u);
+    const float dma = f16f(ha.x >> 16), dmb = f16f(hb.x >> 16);
+    for (int s = 2 * j0 + t; s < 2 * j1; s += 4) {
+      const int sh = 8 * (s & 3);
+      const float ma = (float)(((s < 4 ? ma_lo : ma_hi) >> sh) & 0xFFu);
+      const float mb = (float)(((s < 4 ? mb_lo : mb_hi) >> sh) & 0xFFu);
+      const float n = sx[8 * b + s];
+      fa = fmaf(-(dma * ma), n, fa);
+      fb = fmaf(-(dmb * mb), n, fb);
+    }
+  }
+  fa += __shfl_xor_sync(0xFFFFFFFFu, fa, 1);
+  fb += __shfl_xor_sync(0xFFFFFFFFu, fb, 1);
+  fa += __shfl_xor_sync(0xFFFFFFFFu, fa, 2);
+  fb += __shfl_xor_sync(0xFFFFFFFFu, fb, 2);
+  acc_a = fa;
+  acc_b = fb;
 }
 
 // x values of chunk (kb, c) from the padded residual, each scaled by rs (and, kGen only, by the
@@ -440,7 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
   uint32_t *lg_s = reinterpret_cast<uint32_t *>(smem + kOffLg);
   uint8_t *rt = smem + kOffRt;
   uint8_t *gu_g = smem + SL::kOffGu;                  // [32 routed + 4 shared] gate rows
-  uint8_t *gu_u = gu_g + (kQ + kJ) * kRowUp;      // the matching up rows
+  uint8_t *gu_u = gu_g + SL::kUpOff;                  // the matching up rows
   uint8_t *dn = smem + SL::kOffDn;                    // [8][16] routed down rows
   uint8_t *dn_sh = smem + SL::kOffDnSh;               // the shared expert's 16 down rows
   uint8_t *shg = smem + SL::kOffShGu, *shu = shg + kJ * SL::kShRow;  // mode 2: shared gate / up rows
@@ -491,8 +604,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
     } else {
       mbar_expect_tx(bar + kBarShGu, kJ * kRowPair);
       const size_t off = (size_t)(kJ * c) * kRowUp;
-      bulk_g2s(gu_g + kQ * kRowUp, (const uint8_t *)P.L[l].sh_gate + off, kJ * kRowUp, bar + kBarShGu, pol_normal);
-      bulk_g2s(gu_u + kQ * kRowUp, (const uint8_t *)P.L[l].sh_up + off, kJ * kRowUp, bar + kBarShGu, pol_normal);
+      bulk_g2s(gu_g + SL::kShOff, (const uint8_t *)P.L[l].sh_gate + off, kJ * kRowUp, bar + kBarShGu, pol_normal);
+      bulk_g2s(gu_u + SL::kShOff, (const uint8_t *)P.L[l].sh_up + off, kJ * kRowUp, bar + kBarShGu, pol_normal);
     }
     armed |= 1u << kBarShGu;
   };
@@ -637,7 +750,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
         const int g = lane >> 1, which = lane & 1;
         const uint8_t *src = (const uint8_t *)(which ? Lp.up : Lp.gate) + (size_t)e * Lp.gate_up_expert_stride +
                              (size_t)(j_c + g * kGuChunk) * kRowUp;
-        bulk_g2s((which ? gu_u : gu_g) + g * kGuChunk * kRowUp, src, kGuChunk * kRowUp, bar + kBarGu0 + g,
+        bulk_g2s((which ? gu_u : gu_g) + g * SL::kChunkPitch, src, kGuChunk * kRowUp, bar + kBarGu0 + g,
                  pol_first);
       }
       __syncwarp();
@@ -654,75 +767,166 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       }
     }
     // ---------------------------------------------------------------- phase G
-    {  // warps 1..11 (warp 0 routes above), two adjacent row pairs per iteration, in arrival
-       // order: items 0..3 are the shared pairs (prefetched), items 4..35 the routed pairs in
-       // chunk order; warp w takes items 2(w-1), 2(w-1)+1, then the same 22 items later
+    {  // warps 1..11 (warp 0 routes above). Mode 2: two adjacent row pairs per iteration, in
+       // arrival order (items 0..3 the shared pairs, items 4..35 the routed pairs in chunk order;
+       // warp w takes items 2(w-1), 2(w-1)+1, then the same 22 items later). Modes 0 / 1: the x
+       // digits, then tensor-core tiles of 8 row pairs (routed pairs 8T..8T+7 = chunks 2T, 2T+1,
+       // split in K quarters: warps 1..8 take T = 0 / 1 then T = 2 / 3) and the shared tile
+       // (K halves: warps 9, 10); per-part row sums go to shared memory.
       uint32_t have = 0;  // bit 0: shared, bit 1 + g: routed chunk g
+      // wait (warp-uniform) for the copy barriers in `need` this thread has not consumed yet
+      auto need_bits = [&](uint32_t need) {
+        for (int bit = 0; bit < 1 + kGuChunks && !fail; ++bit) {
+          if (!(need & ~have & (1u << bit))) continue;
+          fail = !__all_sync(0xFFFFFFFFu, wait_bar(bit == 0 ? kBarShGu : kBarGu0 + bit - 1));
+          have |= 1u << bit;
+        }
+      };
       if (warp > 0) {
         __syncwarp();
         if (warp >= kRtRows) rs = rms_scale();
-        XChunk X0, X1;
-        const float *nw = P.resid ? Lp.norm_w : nullptr;
-        xchunk_pad<kGen>(res_s, rs, nw, kb0, cc, X0);
-        xchunk_pad<kGen>(res_s, rs, nw, kb0 + 4, cc, X1);
-        constexpr int kStep = 2 * (kWarps - 1);
-        for (int ia = 2 * (warp - 1); ia < kJ + kQ && !fail; ia += kStep) {
-          const int ib = ia + 1;  // the second pair of this iteration (if any)
-          const bool two = ib < kJ + kQ;
-          uint32_t need = 1u << (ia < kJ ? 0 : 1 + (ia - kJ) / kGuChunk);
-          if (two) need |= 1u << (ib < kJ ? 0 : 1 + (ib - kJ) / kGuChunk);
-          for (int bit = 0; bit < 1 + kGuChunks; ++bit) {  // warp-uniform outcomes
-            if (!(need & ~have & (1u << bit))) continue;
-            fail = !__all_sync(0xFFFFFFFFu, wait_bar(bit == 0 ? kBarShGu : kBarGu0 + bit - 1));
-            have |= 1u << bit;
+        if constexpr (kFmt) {
+          XChunk X0, X1;
+          const float *nw = P.resid ? Lp.norm_w : nullptr;
+          xchunk_pad<kGen>(res_s, rs, nw, kb0, cc, X0);
+          xchunk_pad<kGen>(res_s, rs, nw, kb0 + 4, cc, X1);
+          constexpr int kStep = 2 * (kWarps - 1);
+          for (int ia = 2 * (warp - 1); ia < kJ + kQ && !fail; ia += kStep) {
+            const int ib = ia + 1;  // the second pair of this iteration (if any)
+            const bool two = ib < kJ + kQ;
+            uint32_t need = 1u << (ia < kJ ? 0 : 1 + (ia - kJ) / kGuChunk);
+            if (two) need |= 1u << (ib < kJ ? 0 : 1 + (ib - kJ) / kGuChunk);
+            for (int bit = 0; bit < 1 + kGuChunks; ++bit) {  // warp-uniform outcomes
+              if (!(need & ~have & (1u << bit))) continue;
+              fail = !__all_sync(0xFFFFFFFFu, wait_bar(bit == 0 ? kBarShGu : kBarGu0 + bit - 1));
+              have |= 1u << bit;
+              if (fail) break;
+            }
             if (fail) break;
-          }
-          if (fail) break;
-          const uint8_t *rowp[2];
-#pragma unroll
-          for (int p = 0; p < 2; ++p) {
-            const int idx = p ? ib : ia;
-            const int row = !two && p ? kQ : (idx < kJ ? kQ + idx : idx - kJ);  // a spare read when !two
-            rowp[p] = gu_g + (size_t)row * kRowUp;
-          }
-          float g[2], u[2];
-          if (kFmt && ia < kJ) {  // mode 2: shared pairs ia, ia + 1 (kJ is even: never mixed with routed)
-            const int st = sh_t(l);
-            const size_t rg = (size_t)row_bytes(st, kH);  // rows staged at their own pitch
-#pragma unroll
+            const uint8_t *rowp[2];
+  #pragma unroll
             for (int p = 0; p < 2; ++p) {
-              const uint8_t *rgp = shg + (size_t)(ia + p) * rg, *rup = shu + (size_t)(ia + p) * rg;
-              g[p] = any_chunk_dot<LdShared>(st, rgp, kb0, cc, X0) + any_chunk_dot<LdShared>(st, rgp, kb0 + 4, cc, X1);
-              u[p] = any_chunk_dot<LdShared>(st, rup, kb0, cc, X0) + any_chunk_dot<LdShared>(st, rup, kb0 + 4, cc, X1);
+              const int idx = p ? ib : ia;
+              const int row = !two && p ? kQ : (idx < kJ ? kQ + idx : idx - kJ);  // a spare read when !two
+              rowp[p] = gu_g + (size_t)row * kRowUp;
             }
-          } else {
-#pragma unroll
-          for (int m = 0; m < 2; ++m) {  // gate rows of both pairs, then their up rows
-            uint4 hq[2][4];
-#pragma unroll
+            float g[2], u[2];
+            if (kFmt && ia < kJ) {  // mode 2: shared pairs ia, ia + 1 (kJ is even: never mixed with routed)
+              const int st = sh_t(l);
+              const size_t rg = (size_t)row_bytes(st, kH);  // rows staged at their own pitch
+  #pragma unroll
+              for (int p = 0; p < 2; ++p) {
+                const uint8_t *rgp = shg + (size_t)(ia + p) * rg, *rup = shu + (size_t)(ia + p) * rg;
+                g[p] = any_chunk_dot<LdShared>(st, rgp, kb0, cc, X0) + any_chunk_dot<LdShared>(st, rgp, kb0 + 4, cc, X1);
+                u[p] = any_chunk_dot<LdShared>(st, rup, kb0, cc, X0) + any_chunk_dot<LdShared>(st, rup, kb0 + 4, cc, X1);
+              }
+            } else {
+  #pragma unroll
+            for (int m = 0; m < 2; ++m) {  // gate rows of both pairs, then their up rows
+              uint4 hq[2][4];
+  #pragma unroll
+              for (int p = 0; p < 2; ++p) {
+                const uint8_t *rp = rowp[p] + m * (size_t)(kQ + kJ) * kRowUp;
+                hq[p][0] = *reinterpret_cast<const uint4 *>(rp + kb0 * kQB);
+                hq[p][1] = *reinterpret_cast<const uint4 *>(rp + kb0 * kQB + 16 + 16 * cc);
+                hq[p][2] = *reinterpret_cast<const uint4 *>(rp + (kb0 + 4) * kQB);
+                hq[p][3] = *reinterpret_cast<const uint4 *>(rp + (kb0 + 4) * kQB + 16 + 16 * cc);
+              }
+  #pragma unroll
+              for (int p = 0; p < 2; ++p) {
+                const float v = q4k_chunk_dot(hq[p][0], hq[p][1], cc, X0) + q4k_chunk_dot(hq[p][2], hq[p][3], cc, X1);
+                if (m == 0) g[p] = v;
+                else u[p] = v;
+              }
+            }
+            }
+  #pragma unroll
             for (int p = 0; p < 2; ++p) {
-              const uint8_t *rp = rowp[p] + m * (size_t)(kQ + kJ) * kRowUp;
-              hq[p][0] = *reinterpret_cast<const uint4 *>(rp + kb0 * kQB);
-              hq[p][1] = *reinterpret_cast<const uint4 *>(rp + kb0 * kQB + 16 + 16 * cc);
-              hq[p][2] = *reinterpret_cast<const uint4 *>(rp + (kb0 + 4) * kQB);
-              hq[p][3] = *reinterpret_cast<const uint4 *>(rp + (kb0 + 4) * kQB + 16 + 16 * cc);
+              g[p] = warp_sum(g[p]);
+              u[p] = warp_sum(u[p]);
             }
-#pragma unroll
-            for (int p = 0; p < 2; ++p) {
-              const float v = q4k_chunk_dot(hq[p][0], hq[p][1], cc, X0) + q4k_chunk_dot(hq[p][2], hq[p][3], cc, X1);
-              if (m == 0) g[p] = v;
-              else u[p] = v;
+            if (lane == 0) {
+              s_out[ia < kJ ? kQ + ia : ia - kJ] = __fmul_rn(silu_f(g[0]), u[0]);
+              if (two) s_out[ib < kJ ? kQ + ib : ib - kJ] = __fmul_rn(silu_f(g[1]), u[1]);
             }
           }
-          }
+        } else {
+          // x = resid * rs (* nw): warp w - 1 takes sub-blocks w - 1, w + 10, ... (lane = element)
+          int8_t *digx = reinterpret_cast<int8_t *>(rt + (size_t)rt_buf(l) * kRtRows * SL::kRouterSlot);
+          float *sxx = reinterpret_cast<float *>(digx + 3 * kDigPitchX);
+          uint32_t *xmax = reinterpret_cast<uint32_t *>(smem + SL::kOffMisc + 160);
+          float *partg = reinterpret_cast<float *>(smem + SL::kOffPart);  // [36 pairs][gate, up][4 parts]
+          const float *nw = P.resid ? Lp.norm_w : nullptr;
+          const int wv = warp - 1;
+          constexpr int kSubs = kH / 32, kPer = (kSubs + kWarps - 2) / (kWarps - 1);
+          float xv[kPer];
+          uint32_t mx = 0;
 #pragma unroll
-          for (int p = 0; p < 2; ++p) {
-            g[p] = warp_sum(g[p]);
-            u[p] = warp_sum(u[p]);
+          for (int i = 0; i < kPer; ++i) {
+            const int sb = wv + (kWarps - 1) * i;
+            float v = 0.0f;
+            if (sb < kSubs) {
+              const int e = 32 * sb + lane;
+              v = __fmul_rn(res_s[pad(e)], rs);
+              if (kGen && nw) v = __fmul_rn(v, __ldg(nw + e));
+            }
+            xv[i] = v;
+            mx = max(mx, __float_as_uint(v) & 0x7FFFFFFFu);
           }
-          if (lane == 0) {
-            s_out[ia < kJ ? kQ + ia : ia - kJ] = __fmul_rn(silu_f(g[0]), u[0]);
-            if (two) s_out[ib < kJ ? kQ + ib : ib - kJ] = __fmul_rn(silu_f(g[1]), u[1]);
+          mx = __reduce_max_sync(0xFFFFFFFFu, mx);
+          if (lane == 0) xmax[wv] = mx;
+          bar_sync_g();
+          uint32_t M = 0;
+#pragma unroll
+          for (int i = 0; i < kWarps - 1; ++i) M = max(M, xmax[i]);
+          const int kx = digit_shift(M);
+          const float upx = pow2i(kx);
+#pragma unroll
+          for (int i = 0; i < kPer; ++i) {
+            const int sb = wv + (kWarps - 1) * i;
+            if (sb < kSubs) {  // warp-uniform
+              const int n = __float2int_rn(__fmul_rn(xv[i], upx));
+              int d0, d1, d2;
+              digits3(n, d0, d1, d2);
+              const int e = 32 * sb + lane;
+              digx[e] = (int8_t)d0;
+              digx[kDigPitchX + e] = (int8_t)d1;
+              digx[2 * kDigPitchX + e] = (int8_t)d2;
+              const int tot = __reduce_add_sync(0xFFFFFFFFu, n);
+              if (lane == 0) sxx[sb] = (float)tot;
+            }
+          }
+          fence_proxy_async_smem();  // a bulk copy refills this buffer two layers on
+          bar_sync_g();
+          const float unx = digit_unscale(M, kx);
+          const int lg = lane >> 2, lt = lane & 3;
+          if (warp <= 8) {
+            // fragment row g: chunk 2T + (g & 1), gate (g >> 1 even) or up, pair-in-chunk g >> 2;
+            // row g + 8: the same chunk and kind, pair-in-chunk 2 + (g >> 2)
+            const int cp = lg & 1, kind = (lg >> 1) & 1, pic = lg >> 2, q = (warp - 1) & 3;
+            for (int it = 0; it < 2 && !fail; ++it) {
+              const int T = 2 * it + ((warp - 1) >> 2), chunk = 2 * T + cp;
+              need_bits(3u << (1 + 2 * T));
+              if (fail) break;
+              const uint8_t *ra = (kind ? gu_u : gu_g) + chunk * SL::kChunkPitch + pic * kRowUp;
+              float va, vb;
+              q4k_mma_rows(ra, ra + 2 * kRowUp, digx, kDigPitchX, sxx, 2 * q, 2 * q + 2, 0, 4, va, vb);
+              if (lt == 0) {
+                const int pa = kGuChunk * chunk + pic;
+                partg[(pa * 2 + kind) * 4 + q] = __fmul_rn(va, unx);
+                partg[((pa + 2) * 2 + kind) * 4 + q] = __fmul_rn(vb, unx);
+              }
+            }
+          } else if (warp <= 10) {
+            // the shared tile: fragment row g = pair g >> 1 (& 3), gate / up by g & 1; rows g + 8 repeat it
+            need_bits(1u);
+            if (!fail) {
+              const int kind = lg & 1, p = (lg >> 1) & 3, h = warp - 9;
+              const uint8_t *ra = (kind ? gu_u : gu_g) + SL::kShOff + p * kRowUp;
+              float va, vb;
+              q4k_mma_rows(ra, ra, digx, kDigPitchX, sxx, 4 * h, 4 * h + 4, 0, 4, va, vb);
+              if (lt == 0) partg[((kQ + p) * 2 + kind) * 4 + h] = __fmul_rn(va, unx);
+            }
           }
         }
       }
@@ -732,8 +936,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
         if (!(have & (2u << g))) fail = !wait_bar(kBarGu0 + g);
     }
     if (__syncthreads_or(fail)) { aborted = true; break; }
-    if (tid < kQ + kJ)  // this CTA's s values: one coalesced store
-      st_tagged(ts + (size_t)c * kSlotS + tid, ep + 2, __float_as_uint(s_out[tid]));
+    if (tid < kQ + kJ) {  // this CTA's s values: one coalesced store
+      float sv;
+      if constexpr (kFmt) {
+        sv = s_out[tid];
+      } else {  // pair tid: its gate and up rows' part sums, added in part order
+        const float *pp = reinterpret_cast<const float *>(smem + SL::kOffPart) + tid * 8;
+        float gs, us;
+        if (tid < kQ) {
+          gs = __fadd_rn(__fadd_rn(__fadd_rn(pp[0], pp[1]), pp[2]), pp[3]);
+          us = __fadd_rn(__fadd_rn(__fadd_rn(pp[4], pp[5]), pp[6]), pp[7]);
+        } else {
+          gs = __fadd_rn(pp[0], pp[1]);
+          us = __fadd_rn(pp[4], pp[5]);
+        }
+        sv = __fmul_rn(silu_f(gs), us);
+      }
+      st_tagged(ts + (size_t)c * kSlotS + tid, ep + 2, __float_as_uint(sv));
+    }
     if (tid == 0 && !last) issue_shared_gu(l + 1);  // this layer's shared gate/up reads are done
     // ---------------------------------------------------------------- phase D
     if (!gather<kSlotS, kQ + kJ>(ts, ep + 2, abort_word, C, r, bar + kBarXS, ph[kBarXS], sl_s, 2, P.budget,
@@ -749,56 +969,125 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
     fail = !wait_bar(kBarDn);
     fail = !wait_bar(kBarShDn) || fail;
     if (__syncthreads_or(fail)) { aborted = true; break; }
-    {
-      // All 12 warps: warp w < 9 takes rows 0..11 of slot w (routed slots 0..7, the shared expert
-      // 8), warp 9 + i rows 12..15 of slots 3i, 3i + 1, 3i + 2 -- four rows per iteration (two per
-      // half-warp, in flight together), three iterations per warp, so each SM sub-partition runs
-      // the same number of row dots (with one warp per slot, three of them ran a third more).
-      // Each row's dot is the same sequence of operations whichever warp runs it.
-      // Reconverge the warp first: thread 0's solo branches (copy issue, barrier arming) can
-      // leave warp 0 split, and a split warp runs this loop once per part.
+    float *partd = reinterpret_cast<float *>(smem + SL::kOffPart);  // modes 0 / 1: [9 slots][4 parts][16 rows]
+    if constexpr (!kFmt) {
+      // Tensor-core down: warp w < 9 turns expert w's s into digits (lane L: elements 16L..16L+15)
+      // in the routed gate-row area, then 36 items (slot, K quarter) of 16 rows, three per warp.
+      // Reconverge the warp first (thread 0's solo branches can leave warp 0 split).
       __syncwarp();
-      const int half = lane >> 4, kb = (lane >> 3) & 1;
-      XChunk X;
-      if (warp < 9) load_xchunk(warp < kK ? s_s + warp * kI : ssh_s, kb, cc, X);
+      int8_t *digs = reinterpret_cast<int8_t *>(gu_g);                           // [9][3 planes][kDigPitchS]
+      float *sxs = reinterpret_cast<float *>(gu_g + (kK + 1) * 3 * kDigPitchS);  // [9][16]
+      float *sinv = reinterpret_cast<float *>(smem + SL::kOffMisc + 208);       // [9]
+      if (warp < kK + 1) {
+        const float *sv = (warp < kK ? s_s + warp * kI : ssh_s) + 16 * lane;
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 f = *reinterpret_cast<const float4 *>(sv + 4 * i);
+          v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+        }
+        uint32_t mx = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) mx = max(mx, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+        mx = __reduce_max_sync(0xFFFFFFFFu, mx);
+        const int ks = digit_shift(mx);
+        const float ups = pow2i(ks);
+        uint32_t pk[3][4] = {};
+        int tot = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int n = __float2int_rn(__fmul_rn(v[i], ups));
+          int d[3];
+          digits3(n, d[0], d[1], d[2]);
+#pragma unroll
+          for (int pl = 0; pl < 3; ++pl) pk[pl][i >> 2] |= ((uint32_t)d[pl] & 0xFFu) << (8 * (i & 3));
+          tot += n;
+        }
+        int8_t *dst = digs + warp * 3 * kDigPitchS + 16 * lane;
+#pragma unroll
+        for (int pl = 0; pl < 3; ++pl)
+          *reinterpret_cast<uint4 *>(dst + pl * kDigPitchS) = make_uint4(pk[pl][0], pk[pl][1], pk[pl][2], pk[pl][3]);
+        tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 1);  // lanes 2i, 2i+1: sub-block i
+        if (!(lane & 1)) sxs[warp * (kI / 32) + (lane >> 1)] = (float)tot;
+        if (lane == 0) sinv[warp] = digit_unscale(mx, ks);
+        fence_proxy_async_smem();  // the next layer's bulk copies land in this area
+      }
+      __syncthreads();
+      const int lg = lane >> 2, lt = lane & 3;
 #pragma unroll 1
       for (int it = 0; it < 3; ++it) {
-        const int slot = warp < 9 ? warp : 3 * (warp - 9) + it;
-        const int rbase = warp < 9 ? 4 * it : 12;
-        if (warp >= 9) load_xchunk(slot < kK ? s_s + slot * kI : ssh_s, kb, cc, X);
-        float v[2];
-#pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          const int hh = rbase + 2 * p + half;
-          if constexpr (kFmt) {  // the layer's row formats, staged at their own pitch
-            const int t = slot < kK ? down_t(l) : sh_t(l);
-            const size_t rb = (size_t)row_bytes(t, kI);
-            const uint8_t *row = (slot < kK ? dn + (size_t)slot * kHr * rb : dn_sh) + (size_t)hh * rb;
-            v[p] = any_chunk_dot<LdShared>(t, row, kb, cc, X);
-          } else {
-            const uint8_t *pp = dn + (size_t)(slot * kHr + hh) * kRowDown + kb * kQB;
-            const uint4 h4 = *reinterpret_cast<const uint4 *>(pp);
-            const uint4 q4 = *reinterpret_cast<const uint4 *>(pp + 16 + 16 * cc);
-            v[p] = q4k_chunk_dot(h4, q4, cc, X);
-          }
-        }
-#pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          v[p] = half_warp_sum(v[p]);
-          if ((lane & 15) == 0) o_s[slot * kHr + rbase + 2 * p + half] = v[p];
+        const int item = warp + kWarps * it;  // 0..35
+        const int slot = item >> 2, q = item & 3, sb = q >> 1, j0 = 2 * (q & 1);
+        const uint8_t *base = slot < kK ? dn + (size_t)slot * kHr * kRowDown : dn_sh;
+        float va, vb;
+        q4k_mma_rows(base + lg * kRowDown, base + (lg + 8) * kRowDown, digs + slot * 3 * kDigPitchS, kDigPitchS,
+                     sxs + slot * (kI / 32), sb, sb + 1, j0, j0 + 2, va, vb);
+        if (lt == 0) {
+          const float un = sinv[slot];
+          partd[(slot * 4 + q) * kHr + lg] = __fmul_rn(va, un);
+          partd[(slot * 4 + q) * kHr + lg + 8] = __fmul_rn(vb, un);
         }
       }
-    }
+    } else
+      {
+        // All 12 warps: warp w < 9 takes rows 0..11 of slot w (routed slots 0..7, the shared expert
+        // 8), warp 9 + i rows 12..15 of slots 3i, 3i + 1, 3i + 2 -- four rows per iteration (two per
+        // half-warp, in flight together), three iterations per warp, so each SM sub-partition runs
+        // the same number of row dots (with one warp per slot, three of them ran a third more).
+        // Each row's dot is the same sequence of operations whichever warp runs it.
+        // Reconverge the warp first: thread 0's solo branches (copy issue, barrier arming) can
+        // leave warp 0 split, and a split warp runs this loop once per part.
+        __syncwarp();
+        const int half = lane >> 4, kb = (lane >> 3) & 1;
+        XChunk X;
+        if (warp < 9) load_xchunk(warp < kK ? s_s + warp * kI : ssh_s, kb, cc, X);
+  #pragma unroll 1
+        for (int it = 0; it < 3; ++it) {
+          const int slot = warp < 9 ? warp : 3 * (warp - 9) + it;
+          const int rbase = warp < 9 ? 4 * it : 12;
+          if (warp >= 9) load_xchunk(slot < kK ? s_s + slot * kI : ssh_s, kb, cc, X);
+          float v[2];
+  #pragma unroll
+          for (int p = 0; p < 2; ++p) {
+            const int hh = rbase + 2 * p + half;
+            if constexpr (kFmt) {  // the layer's row formats, staged at their own pitch
+              const int t = slot < kK ? down_t(l) : sh_t(l);
+              const size_t rb = (size_t)row_bytes(t, kI);
+              const uint8_t *row = (slot < kK ? dn + (size_t)slot * kHr * rb : dn_sh) + (size_t)hh * rb;
+              v[p] = any_chunk_dot<LdShared>(t, row, kb, cc, X);
+            } else {
+              const uint8_t *pp = dn + (size_t)(slot * kHr + hh) * kRowDown + kb * kQB;
+              const uint4 h4 = *reinterpret_cast<const uint4 *>(pp);
+              const uint4 q4 = *reinterpret_cast<const uint4 *>(pp + 16 + 16 * cc);
+              v[p] = q4k_chunk_dot(h4, q4, cc, X);
+            }
+          }
+  #pragma unroll
+          for (int p = 0; p < 2; ++p) {
+            v[p] = half_warp_sum(v[p]);
+            if ((lane & 15) == 0) o_s[slot * kHr + rbase + 2 * p + half] = v[p];
+          }
+        }
+      }
     __syncthreads();
     if (tid < kHr) {
+      // expert `slot`'s output row tid (modes 0 / 1: its four K-part sums, added in part order)
+      auto o_at = [&](int slot) -> float {
+        if constexpr (kFmt) {
+          return o_s[slot * kHr + tid];
+        } else {
+          const float *pp = partd + slot * 4 * kHr + tid;
+          return __fadd_rn(__fadd_rn(__fadd_rn(pp[0], pp[kHr]), pp[2 * kHr]), pp[3 * kHr]);
+        }
+      };
       float acc = 0.0f;
 #pragma unroll
       for (int i = 0; i < kK; ++i) {
         const int slot = rr->order[i];
-        acc = __fadd_rn(acc, __fmul_rn(o_s[slot * kHr + tid], bf16f(rr->wb[slot])));
+        acc = __fadd_rn(acc, __fmul_rn(o_at(slot), bf16f(rr->wb[slot])));
       }
       const float sg = __uint_as_float(row_out[2]);
-      const float res = __fadd_rn(acc, __fmul_rn(sg, o_s[8 * kHr + tid]));
+      const float res = __fadd_rn(acc, __fmul_rn(sg, o_at(kK)));
       const int h = kHr * c + tid;
       if (!last) {
         st_tagged(td + (size_t)c * kSlotDelta + tid, ep + 3, __float_as_uint(res));

@@ -2,14 +2,27 @@
 
 At T = 1 both b200moe_moe_decode and b200moe_stack_decode run the persistent kernel; at T >= 2
 they run the per-token three-kernel path, which treats every token independently. Feeding a
-T = 2 call two copies of the token therefore gives the three-kernel result for it, and the two
-paths must agree BIT FOR BIT (same operations in the same order), ids included. The oracle
-parity of the T = 1 path itself is covered by test_gpu_decode.py and test_gpu_stack.py.
+T = 2 call two copies of the token therefore gives the three-kernel result for it. For Q4_K
+layers the persistent kernel computes the expert dots on the tensor cores with exact integer
+products over a 24-bit fixed-point image of x and s, the three-kernel path in f32 on the CUDA
+cores, so the two agree within the decode parity bar (rel-L2 and max-abs / max|ref| 1e-5 -- both
+are within it of the f64 oracle), with the same routing ids. The oracle parity of the T = 1 path
+itself is covered by test_gpu_decode.py and test_gpu_stack.py; the block-format variant (Q5_K /
+Q6_K / Q8_0 layers) still matches the three-kernel path bit for bit (test_gpu_kquant_layers.py).
 """
 import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
+PATH_REL_L2, PATH_MAX_ABS_NORM = 1e-5, 1e-5
+
+
+def _close(a, b):
+    import torch
+    from oracle import moe as OM
+    c = OM.compare(a.double().cpu().numpy(), b.double().cpu().numpy())
+    print("persistent vs three-kernel path: rel-L2 %.3e, max-abs / max|ref| %.3e" % (c["rel_l2"], c["max_abs_norm"]))
+    return c["rel_l2"] < PATH_REL_L2 and c["max_abs_norm"] < PATH_MAX_ABS_NORM
 
 
 @pytest.fixture(scope="module")
@@ -45,7 +58,7 @@ def test_stack_persistent_equals_three_kernel_path(cuda, engine4):
     moe.moe_stack(b, engine4, ids_out=ids_b)
     torch.cuda.synchronize()
     assert torch.isfinite(a).all()
-    assert torch.equal(a[0], b[0]) and torch.equal(b[0], b[1])
+    assert torch.equal(b[0], b[1]) and _close(a[0], b[0])
     assert torch.equal(ids_a[:, 0], ids_b[:, 0])
 
 
@@ -59,7 +72,7 @@ def test_layer_persistent_equals_three_kernel_path(cuda, engine4, dtype):
     o1, i1 = moe.moe_block(x.reshape(1, 1, 2048), engine4, 2)
     o2, i2 = moe.moe_block(x.repeat(2, 1).reshape(1, 2, 2048), engine4, 2)
     torch.cuda.synchronize()
-    assert torch.equal(o1[0, 0], o2[0, 0]) and torch.equal(i1["ids"][0, 0], i2["ids"][0, 0])
+    assert _close(o1[0, 0], o2[0, 0]) and torch.equal(i1["ids"][0, 0], i2["ids"][0, 0])
 
 
 def test_repeated_calls_and_graph_replay(cuda, engine4):
