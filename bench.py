@@ -560,9 +560,12 @@ def run_b200(args):
         if args.formats == "published" and not _abi.decode_persistent_formats():
             persist_ctas, persist_cluster = 0, 0  # such layers take the three-kernel path
         # the block's own path choice: grouped GEMMs (10 kernels per layer) from
-        # moe.PREFILL_MIN_TOKENS tokens on, else one persistent kernel (T = 1) or 3 per layer
+        # moe.PREFILL_MIN_TOKENS tokens on, else one persistent kernel (T = 1), the grouped
+        # small-batch decode (router, plan, gate/up, down, combine: 5 per layer) for 2..16 tokens
+        # of Q4_K layers, or the three gather-GEMV kernels per layer
         use_prefill = (T >= moe.PREFILL_MIN_TOKENS) if args.path == "auto" else (args.path == "prefill" and T > 1)
-        launches_per_step = 10 * nl if use_prefill else (1 if persist_ctas else 3 * nl)
+        grouped = 2 <= T <= moe.GROUPED_MAX_TOKENS and args.formats == "q4k"
+        launches_per_step = 10 * nl if use_prefill else (1 if persist_ctas else (5 if grouped else 3) * nl)
         stack_fn = moe.moe_stack_prefill if use_prefill else moe.moe_stack
         bytes_per_step = nl * (9 * EXPERT_BYTES * (1 if T == 1 else 0) + ROUTER_BYTES + WSG_BYTES + 2 * T * 2048 * 4)
         ws = (torch.empty(_abi.prefill_workspace_size(T), dtype=torch.uint8, device=dev) if use_prefill

@@ -19,9 +19,16 @@
 // is read once per token. K2 / K3 are templates on the layer's block types: Q5_K / Q6_K down
 // and a Q8_0 shared expert (the published Q4_K_M file) go through kq_dot.cuh's chunk dots,
 // loaded after the dependency resolves.
+// Which kernels run (run_layer): 2..16 tokens of a Q4_K layer take K1 (which then also writes
+// each token's x as int8 digit planes) and the grouped kernels of grouped.cu, which read each
+// distinct expert's rows once for all its tokens; other layers, the stage dumps and the
+// no-allocation entry point (whose static scratch has no room for the grouped buffers) take
+// K1 -> K2 -> K3. A single token takes the persistent kernel (persist.cu) when it is resident.
 #include <mutex>
 
 #include "common.cuh"
+#include "grouped.cuh"
+#include "imma.cuh"
 #include "kq_dot.cuh"
 #include "mega.cuh"
 #include "route.cuh"
@@ -45,6 +52,7 @@ struct K1Params {
   const void *wsg;       // NULL: router only
   int wf32;              // 1: wg / wsg are f32
   float *xw;             // [T][2048] f32 copy of x for K2 (or NULL)
+  uint8_t *xd;           // [T][b2grp::kXBlk] x as digit planes for the grouped path (or NULL)
   uint16_t *logits;      // [T][256]
   float *sg;             // [T]
   uint32_t *status;      // decode status word to clear (the call's first router launch), or NULL
@@ -106,6 +114,40 @@ __device__ __forceinline__ void load_x_slice(const K1Params &P, int t, int lane,
   }
 }
 
+// One token's x (lane L holds elements 64L..64L+63) as the grouped path's digit block
+// (grouped.cuh): three int8 planes of the integer image n = rint(x 2^k), the per-sub-block sums
+// of n (lane L: sub-blocks 2L, 2L+1) and 2^-k (imma.cuh).
+__device__ __forceinline__ void write_digits(const float (&v)[64], uint8_t *blk, int lane) {
+  uint32_t mx = 0;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) mx = max(mx, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+  mx = __reduce_max_sync(0xFFFFFFFFu, mx);
+  const int k = digit_shift(mx);
+  const float up = pow2i(k);
+  int sum[2] = {0, 0};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {  // 16 elements per store
+    uint32_t pk[3][4] = {};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int n = __float2int_rn(__fmul_rn(v[16 * c + i], up));
+      int d[3];
+      digits3(n, d[0], d[1], d[2]);
+#pragma unroll
+      for (int pl = 0; pl < 3; ++pl) pk[pl][i >> 2] |= ((uint32_t)d[pl] & 0xFFu) << (8 * (i & 3));
+      sum[c >> 1] += n;
+    }
+#pragma unroll
+    for (int pl = 0; pl < 3; ++pl)
+      *reinterpret_cast<uint4 *>(blk + pl * b2grp::kXPlane + 64 * lane + 16 * c) =
+          make_uint4(pk[pl][0], pk[pl][1], pk[pl][2], pk[pl][3]);
+  }
+  float *sx = reinterpret_cast<float *>(blk + 3 * b2grp::kXPlane);
+  sx[2 * lane] = (float)sum[0];
+  sx[2 * lane + 1] = (float)sum[1];
+  if (lane == 0) *reinterpret_cast<float *>(blk + b2grp::kXUnOff) = digit_unscale(mx, k);
+}
+
 // kF32: router weights stored as f32 (held as 64 floats per lane) instead of bf16 (32 words).
 template <bool kF32>
 __global__ void __launch_bounds__(128) k_router(K1Params P) {
@@ -150,6 +192,7 @@ __global__ void __launch_bounds__(128) k_router(K1Params P) {
       for (int i = 0; i < 16; ++i)
         *reinterpret_cast<float4 *>(g + 4 * i) = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     }
+    if (blockIdx.x == 0 && warp == 0 && P.xd) write_digits(v, P.xd + (size_t)t * b2grp::kXBlk, lane);
     float acc = 0.0f;
     if (gate_cta) {  // shared-expert gate: any summation order (tolerance-checked)
 #pragma unroll
@@ -446,14 +489,31 @@ struct DecodeWS {
   float *s;
   float *sg;
   void *xchg;  // cross-CTA exchange area of the persistent single-token kernel
+  // the grouped small-batch path (NULL when the workspace has no room for it)
+  uint8_t *xd;
+  void *plan;
+  float *o;
 };
 
-constexpr size_t decode_ws_bytes(int T) {
+// The three-kernel path's workspace (also the no-allocation entry point's static scratch).
+constexpr size_t decode_ws_base(int T) {
   return align256((size_t)T * kH * 4) + align256((size_t)T * kE * 2) + align256((size_t)T * 9 * kI * 4) +
          align256((size_t)T * 4) + align256(b2mega::kScratchBytes);
 }
 
-DecodeWS carve(void *ws, int T) {
+constexpr bool grouped_t(int T) { return T >= 2 && T <= b2grp::kMaxT; }
+
+// The grouped path's buffers, after the base layout: x digit blocks, the plan, the unweighted
+// expert outputs.
+constexpr size_t grouped_ws_extra(int T) {
+  return grouped_t(T) ? align256((size_t)T * b2grp::kXBlk) + align256(b2grp::kPlanBytes) +
+                            align256((size_t)T * (kK + 1) * kH * 4)
+                      : 0;
+}
+
+constexpr size_t decode_ws_bytes(int T) { return decode_ws_base(T) + grouped_ws_extra(T); }
+
+DecodeWS carve(void *ws, int T, bool grouped = true) {
   char *p = (char *)ws;
   DecodeWS w;
   w.xw = (float *)p;
@@ -465,6 +525,17 @@ DecodeWS carve(void *ws, int T) {
   w.sg = (float *)p;
   p += align256((size_t)T * 4);
   w.xchg = p;
+  p += align256(b2mega::kScratchBytes);
+  w.xd = nullptr;
+  w.plan = nullptr;
+  w.o = nullptr;
+  if (grouped && grouped_t(T)) {
+    w.xd = (uint8_t *)p;
+    p += align256((size_t)T * b2grp::kXBlk);
+    w.plan = p;
+    p += align256(b2grp::kPlanBytes);
+    w.o = (float *)p;
+  }
   return w;
 }
 
@@ -554,11 +625,33 @@ struct Stages {
 int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const b200moe_layer *L, float *out,
               int32_t *ids_out, uint16_t *w_out, const DecodeWS &w, cudaStream_t s, bool first,
               const Stages *st = nullptr) {
+  // 2..16 tokens of a Q4_K layer: the grouped path (every distinct expert's rows read once)
+  const bool grouped = !st && w.xd && grouped_t(T) && layer_all_q4k(L);
   K1Params p1 = k1_params(x, x_dtype, resid, eps, T, L, w);
   if (first) p1.status = status_word(w);
   p1.bf16_stages = st ? st->bf16 : 0;
+  if (grouped) {
+    p1.xw = nullptr;
+    p1.xd = w.xd;
+  }
   if (p1.wf32) B2_CUDA(launch(k_router<true>, (unsigned)kK1Ctas, 128, 0, s, !first, p1));
   else B2_CUDA(launch(k_router<false>, (unsigned)kK1Ctas, 128, 0, s, !first, p1));
+  if (grouped) {
+    b2grp::Args ga = {};
+    ga.T = T;
+    ga.layer = L;
+    ga.logits = w.logits;
+    ga.xd = w.xd;
+    ga.sg = w.sg;
+    ga.plan = w.plan;
+    ga.s = w.s;
+    ga.o = w.o;
+    ga.out = resid ? resid : out;
+    ga.accumulate = resid ? 1 : 0;
+    ga.ids_out = ids_out;
+    ga.w_out = w_out;
+    return b2grp::run(ga, s);
+  }
   K2Params p2;
   p2.gate = (const uint8_t *)L->gate;
   p2.up = (const uint8_t *)L->up;
@@ -635,7 +728,7 @@ int run_persistent(const void *x, int x_dtype, float *resid, float eps, int n_la
 // until the process exits). Host code may not use the array's name as a device address, so
 // its address is looked up once per device with cudaGetSymbolAddress and cached.
 constexpr int kNoAllocMaxT = B200MOE_NOALLOC_MAX_T;
-__device__ __align__(256) unsigned char g_noalloc_scratch[decode_ws_bytes(kNoAllocMaxT)];
+__device__ __align__(256) unsigned char g_noalloc_scratch[decode_ws_base(kNoAllocMaxT)];
 
 std::mutex g_noalloc_mu;
 void *g_noalloc_ptr[128] = {};
@@ -727,10 +820,10 @@ int b200moe_moe_decode_noalloc(const void *x, int x_dtype, int T, const b200moe_
   rc = noalloc_scratch(&scratch);
   if (rc) return rc;
   if (T == 1 && !layer_dense(layer) && b2mega::usable(!layer_all_q4k(layer)))
-    return run_persistent(x, x_dtype, nullptr, 0.f, 1, layer, out, ids_out, w_out, carve(scratch, T),
+    return run_persistent(x, x_dtype, nullptr, 0.f, 1, layer, out, ids_out, w_out, carve(scratch, T, false),
                           (cudaStream_t)stream);
-  return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, carve(scratch, T), (cudaStream_t)stream,
-                   true);
+  return run_layer(x, x_dtype, nullptr, 0.f, T, layer, out, ids_out, w_out, carve(scratch, T, false),
+                   (cudaStream_t)stream, true);
 }
 
 int b200moe_decode_persistent_formats(int *formats) {
@@ -785,7 +878,7 @@ int b200moe_decode_noalloc_status(int T, int *status, void *stream) {
   void *scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc) return rc;
-  return read_status(carve(scratch, T), status, (cudaStream_t)stream, "decode_noalloc_status");
+  return read_status(carve(scratch, T, false), status, (cudaStream_t)stream, "decode_noalloc_status");
 }
 
 int b200moe_debug_decode_faults(long long wait_budget_cycles, int withhold_cta) {

@@ -83,6 +83,9 @@ def _tokens(g, device) -> tuple:
 # the grouped GEMMs cost a nearly flat ~3 ms (2.92 ms at 2 tokens, 3.01 at 4, 3.10 at 6, 3.14 at
 # 8, 3.44 at 32): they cross between 4 and 6 tokens.
 PREFILL_MIN_TOKENS = 5
+# The decode path runs 2..GROUPED_MAX_TOKENS tokens of a Q4_K layer on the grouped kernels
+# (csrc/grouped.cu: each distinct expert's rows read once for all its tokens).
+GROUPED_MAX_TOKENS = 16
 
 
 def prefill_workspace(T: int, device) -> torch.Tensor:
