@@ -385,7 +385,8 @@ def bench_config2(eng, dev, K, W, hbm_peak, batches=(1, 8, 32, 64, 256)):
         byts = u * EXPERT_BYTES + EXPERT_BYTES + ROUTER_BYTES + WSG_BYTES + B * 2048 * (2 + 4)
         gbs = byts / (per_layer_ms / 1e3) / 1e9
         path = ("persistent kernel (one layer per launch)" if B == 1 else
-                "decode kernels (3 per layer)" if B < moe.PREFILL_MIN_TOKENS else "grouped GEMMs (10 per layer)")
+                "grouped GEMMs (10 per layer)" if B >= moe.PREFILL_MIN_TOKENS else
+                "grouped decode (5 per layer)" if B <= moe.GROUPED_MAX_TOKENS else "decode kernels (3 per layer)")
         res["b%d" % B] = {"us_per_layer": per_layer_ms * 1e3, "tok_per_s": B / (per_layer_ms / 1e3),
                           "distinct_experts": u, "bytes_per_layer": byts, "achieved_gbs": gbs,
                           "frac": gbs / hbm_peak, "path": path}

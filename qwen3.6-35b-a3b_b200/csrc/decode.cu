@@ -60,16 +60,32 @@ struct K1Params {
 };
 
 // R1's declared order for one value: lane L holds chunk L's sequential sum; the 32 chunk
-// sums are added left to right. Every lane returns the same bits.
-__device__ __forceinline__ float chunk_total(float acc) {
-  float tot = __shfl_sync(0xFFFFFFFFu, acc, 0);
+// sums are added left to right. Every lane returns the same bits. The partials go through the
+// warp's 32-float shared-memory scratch (one store, eight vector loads, 31 dependent adds on
+// lane 0) instead of 31 dependent shuffles.
+__device__ __forceinline__ float chunk_total(float acc, float *scr) {
+  const int lane = threadIdx.x & 31;
+  scr[lane] = acc;
+  __syncwarp();
+  float tot = 0.0f;
+  if (lane == 0) {
+    float v[32];
 #pragma unroll
-  for (int c = 1; c < 32; ++c) tot = __fadd_rn(tot, __shfl_sync(0xFFFFFFFFu, acc, c));
+    for (int i = 0; i < 8; ++i) {
+      const float4 q = reinterpret_cast<const float4 *>(scr)[i];
+      v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
+    }
+    tot = v[0];
+#pragma unroll
+    for (int c = 1; c < 32; ++c) tot = __fadd_rn(tot, v[c]);
+  }
+  tot = __shfl_sync(0xFFFFFFFFu, tot, 0);
+  __syncwarp();
   return tot;
 }
 
 // Lane L's 64 elements [64L, 64L+64) of token t's MoE input x, in registers.
-__device__ __forceinline__ void load_x_slice(const K1Params &P, int t, int lane, float (&v)[64]) {
+__device__ __forceinline__ void load_x_slice(const K1Params &P, int t, int lane, float (&v)[64], float *scr) {
   if (P.resid) {
     const float *r = P.resid + (size_t)t * kH + 64 * lane;
 #pragma unroll
@@ -80,7 +96,7 @@ __device__ __forceinline__ void load_x_slice(const K1Params &P, int t, int lane,
     float ss = 0.0f;
 #pragma unroll
     for (int i = 0; i < 64; ++i) ss = __fmaf_rn(v[i], v[i], ss);
-    const float tot = chunk_total(ss);
+    const float tot = chunk_total(ss, scr);
     const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, 2048.0f), P.eps)));
 #pragma unroll
     for (int i = 0; i < 64; ++i) v[i] = __fmul_rn(v[i], rs);
@@ -151,7 +167,9 @@ __device__ __forceinline__ void write_digits(const float (&v)[64], uint8_t *blk,
 // kF32: router weights stored as f32 (held as 64 floats per lane) instead of bf16 (32 words).
 template <bool kF32>
 __global__ void __launch_bounds__(128) k_router(K1Params P) {
+  __shared__ __align__(16) float scr_all[4][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float *scr = scr_all[warp];
   const bool gate_cta = blockIdx.x == kK1Ctas - 1;
   if (gate_cta && (warp != 0 || !P.wsg)) return;
   const int e = 4 * blockIdx.x + warp;
@@ -185,14 +203,15 @@ __global__ void __launch_bounds__(128) k_router(K1Params P) {
   if (P.status && blockIdx.x == 0 && threadIdx.x == 0) *P.status = 0u;  // no bounded waits on this path
   for (int t = 0; t < P.T; ++t) {
     float v[64];
-    load_x_slice(P, t, lane, v);
+    load_x_slice(P, t, lane, v, scr);
     if (blockIdx.x == 0 && warp == 0 && P.xw) {
       float *g = P.xw + (size_t)t * kH + 64 * lane;
 #pragma unroll
       for (int i = 0; i < 16; ++i)
         *reinterpret_cast<float4 *>(g + 4 * i) = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     }
-    if (blockIdx.x == 0 && warp == 0 && P.xd) write_digits(v, P.xd + (size_t)t * b2grp::kXBlk, lane);
+    // token t's digit block: one warp of router CTA t (at most 16 tokens, 64 router CTAs)
+    if (blockIdx.x == t && warp == 0 && P.xd) write_digits(v, P.xd + (size_t)t * b2grp::kXBlk, lane);
     float acc = 0.0f;
     if (gate_cta) {  // shared-expert gate: any summation order (tolerance-checked)
 #pragma unroll
@@ -205,7 +224,7 @@ __global__ void __launch_bounds__(128) k_router(K1Params P) {
     }
 #pragma unroll
     for (int i = 0; i < 64; ++i) acc = __fmaf_rn(v[i], wv[i], acc);  // R1: sequential over the lane's 64
-    float tot = chunk_total(acc);
+    float tot = chunk_total(acc, scr);
     if (P.bias) tot = __fadd_rn(tot, bias);
     if (lane == 0) P.logits[(size_t)t * kE + e] = f2bf(tot);
   }

@@ -35,7 +35,7 @@ namespace {
 
 constexpr int kMaxPairs = kMaxT / 2;
 constexpr int kMaxU = kK * kMaxT;      // distinct routed experts at most
-constexpr int kGuCtasPerExpert = kI / 32;   // 4 warps x 8 row pairs
+constexpr int kGuCtasPerExpert = kI / 8;    // one 8-pair tile per CTA (a K quarter per warp)
 constexpr int kDnCtasPerExpert = kH / 64;   // 4 warps x 16 down rows
 constexpr uint32_t kNib = 0x0F0F0F0Fu;
 
@@ -60,36 +60,47 @@ __device__ __forceinline__ uint2 ldg64(const uint8_t *p) {
 // ------------------------------------------------------------------------- plan
 __global__ void __launch_bounds__(512) k_plan(const uint16_t *logits, int T, Plan *P) {
   __shared__ Route rr[kMaxT];
-  __shared__ int cnt_s[kE], off_s[kE];
+  __shared__ int cnt_s[kE / 32], off_s[kE / 32];
   const int tid = threadIdx.x, warp = tid >> 5;
   pdl_wait();
   pdl_trigger();
   if (warp < T) route_warp(logits + (size_t)warp * kE, &rr[warp]);
   __syncthreads();
+  // thread e < 256: expert e's token count, then (block-wide exclusive scans in ascending e) its
+  // index among the hit experts and its first entry
+  int c = 0;
   if (tid < kE) {
-    int c = 0;
     for (int t = 0; t < T; ++t)
 #pragma unroll
       for (int k = 0; k < kK; ++k) c += rr[t].ids[k] == tid;
-    cnt_s[tid] = c;
   }
-  __syncthreads();
-  if (tid == 0) {  // ascending expert id
-    int u = 0, o = 0;
-    for (int e = 0; e < kE; ++e) {
-      if (!cnt_s[e]) continue;
-      P->e[u] = e;
-      P->cnt[u] = cnt_s[e];
-      P->off[u] = o;
-      off_s[e] = o;
-      o += cnt_s[e];
-      ++u;
+  const int lane = tid & 31;
+  int hu = c ? 1 : 0, ho = c;  // inclusive warp scans of (hit, count)
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int a = __shfl_up_sync(0xFFFFFFFFu, hu, o), b = __shfl_up_sync(0xFFFFFFFFu, ho, o);
+    if (lane >= o) {
+      hu += a;
+      ho += b;
     }
-    P->n_u = u;
+  }
+  if (tid < kE && lane == 31) {
+    cnt_s[warp] = hu;  // warp totals (reusing the first 16 slots)
+    off_s[warp] = ho;
   }
   __syncthreads();
-  if (tid < kE && cnt_s[tid]) {
-    int o = off_s[tid];
+  int bu = 0, bo = 0;
+  for (int w = 0; w < warp && w < kE / 32; ++w) {
+    bu += cnt_s[w];
+    bo += off_s[w];
+  }
+  const int u = bu + hu - (c ? 1 : 0), o0 = bo + ho - c;
+  if (tid == kE - 1) P->n_u = u + (c ? 1 : 0);
+  if (tid < kE && c) {
+    P->e[u] = tid;
+    P->cnt[u] = c;
+    P->off[u] = o0;
+    int o = o0;
     for (int t = 0; t < T; ++t)
 #pragma unroll
       for (int k = 0; k < kK; ++k)
@@ -118,45 +129,47 @@ __device__ __forceinline__ int entry_of(const Plan *pl, int ue, int off, int i) 
   return ue == 0 ? (i << 4 | kK) : (int)__ldcg(&pl->tk[off + i]);
 }
 
-// One warp, 16 Q4_K rows (ra: MMA rows 0..7 = lane group g, rb: rows 8..15) against the digit
-// blocks dg[i] (i < cnt; block pitch `blk`, plane pitch `pp`, per-sub-block sums at 3 pp) over
-// super-blocks [0, nsb). fa / fb[p]: this lane's partial sums for token 2p + (lane % 4 >= 2) of
-// the pair (rows of ra / rb), to be completed by the xor-1 lane.
+// One warp's rows of one super-block, in registers: the headers of rows ra (MMA rows 0..7 =
+// lane group g) and rb (rows 8..15) and this lane's 8 quant bytes of each 32-byte group.
+struct RowRegs {
+  uint4 ha, hb;
+  uint2 wa[4], wb[4];
+};
+
+__device__ __forceinline__ void load_rows(RowRegs &r, const uint8_t *ra, const uint8_t *rb) {
+  const int t = threadIdx.x & 3;
+  r.ha = ldg_stream(ra);
+  r.hb = ldg_stream(rb);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    r.wa[j] = ldg64(ra + 16 + 32 * j + 8 * t);
+    r.wb[j] = ldg64(rb + 16 + 32 * j + 8 * t);
+  }
+}
+
+// One warp, 16 Q4_K rows over kNsb super-blocks already loaded (rr), against the digit blocks
+// dg[i] (i < cnt; block pitch `blk`, plane pitch `pp`, per-sub-block sums at 3 pp, all in the
+// super-blocks' own coordinates). fa / fb[p]: this lane's partial sums for token
+// 2p + (lane % 4 >= 2) of the pair (rows ra / rb), to be completed by the xor-1 lane.
 template <int kNsb>
-__device__ __forceinline__ void group_rows(const uint8_t *ra, const uint8_t *rb, const uint8_t *dg, int blk, int pp,
-                                           int cnt, float (&fa)[kMaxPairs], float (&fb)[kMaxPairs]) {
+__device__ __forceinline__ void group_rows(const RowRegs (&rr)[kNsb], const uint8_t *dg, int blk, int pp, int cnt,
+                                           float (&fa)[kMaxPairs], float (&fb)[kMaxPairs]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int np = (cnt + 1) >> 1;
   const float flo = (t & 1) ? 1.0f : 65536.0f, fhi = (t & 1) ? 0.0f : 256.0f;
   const int bplane = g & 3, bsel = g >> 2, tsel = t >> 1;
 #pragma unroll
   for (int p = 0; p < kMaxPairs; ++p) fa[p] = fb[p] = 0.0f;
-  // the next super-block's rows are in flight while this one is computed
-  uint4 ha = ldg_stream(ra), hb = ldg_stream(rb);
-  uint2 wa[4], wb[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    wa[j] = ldg64(ra + 16 + 32 * j + 8 * t);
-    wb[j] = ldg64(rb + 16 + 32 * j + 8 * t);
-  }
-#pragma unroll 1
   for (int b = 0; b < kNsb; ++b) {
-    const uint4 ca = ha, cb = hb;
+    const uint4 ca = rr[b].ha, cb = rr[b].hb;
     uint32_t al[4][4], ah[4][4];  // [group][A register]: low / high nibbles
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      al[j][0] = wa[j].x & kNib; al[j][1] = wb[j].x & kNib; al[j][2] = wa[j].y & kNib; al[j][3] = wb[j].y & kNib;
-      ah[j][0] = (wa[j].x >> 4) & kNib; ah[j][1] = (wb[j].x >> 4) & kNib;
-      ah[j][2] = (wa[j].y >> 4) & kNib; ah[j][3] = (wb[j].y >> 4) & kNib;
-    }
-    if (b + 1 < kNsb) {  // ra / rb point at super-block b
-      ha = ldg_stream(ra + kQB);
-      hb = ldg_stream(rb + kQB);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        wa[j] = ldg64(ra + kQB + 16 + 32 * j + 8 * t);
-        wb[j] = ldg64(rb + kQB + 16 + 32 * j + 8 * t);
-      }
+      const uint2 wa = rr[b].wa[j], wb = rr[b].wb[j];
+      al[j][0] = wa.x & kNib; al[j][1] = wb.x & kNib; al[j][2] = wa.y & kNib; al[j][3] = wb.y & kNib;
+      ah[j][0] = (wa.x >> 4) & kNib; ah[j][1] = (wb.x >> 4) & kNib;
+      ah[j][2] = (wa.y >> 4) & kNib; ah[j][3] = (wb.y >> 4) & kNib;
     }
     const Q4kScales sa = q4k_scale_words(ca), sb = q4k_scale_words(cb);
     const float da = f16f(ca.x), db = f16f(cb.x), dma = f16f(ca.x >> 16), dmb = f16f(cb.x >> 16);
@@ -198,8 +211,6 @@ __device__ __forceinline__ void group_rows(const uint8_t *ra, const uint8_t *rb,
         }
       }
     }
-    ra += kQB;
-    rb += kQB;
   }
 }
 
@@ -214,39 +225,64 @@ struct GuParams {
   int T;
 };
 
-__global__ void __launch_bounds__(128) k_gu_grp(GuParams P) {
-  extern __shared__ __align__(16) uint8_t sm[];  // [cnt][kXBlk]
+// CTA = one 8-pair tile of one expert (gate rows on MMA rows 0..7, the matching up rows on
+// 8..15); warp w takes K quarter w (super-blocks 2w, 2w+1), so each warp issues all its row loads
+// at once. Shared memory: per warp, its K quarter of each token's digit block (kSBlk layout);
+// once every warp is done with them, the per-warp part sums [cnt][4][16] in their place.
+__global__ void __launch_bounds__(128, 4) k_gu_grp(GuParams P) {
+  extern __shared__ __align__(16) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int ue = blockIdx.x / kGuCtasPerExpert;
-  const int tile = (blockIdx.x % kGuCtasPerExpert) * 4 + warp;  // row pairs 8 tile .. 8 tile + 7
+  const int ue = blockIdx.x / kGuCtasPerExpert, tile = blockIdx.x % kGuCtasPerExpert;
   pdl_wait();
   pdl_trigger();
   int cnt, off, e;
   if (!expert_of(P.plan, ue, P.T, cnt, off, e)) return;
+  const uint8_t *ra = (e < 0 ? P.sh_gate : P.gate + (size_t)e * P.stride) + (size_t)(8 * tile + g) * kRowUp + 2 * warp * kQB;
+  const uint8_t *rb = (e < 0 ? P.sh_up : P.up + (size_t)e * P.stride) + (size_t)(8 * tile + g) * kRowUp + 2 * warp * kQB;
+  RowRegs rr[2];
+  load_rows(rr[0], ra, rb);
+  load_rows(rr[1], ra + kQB, rb + kQB);
+  // this warp's K quarter of each token's digits: 512 bytes of each plane, 16 sums, 2^-k
+  uint8_t *wsm = sm + (size_t)warp * cnt * kSBlk;
   for (int i = 0; i < cnt; ++i) {
-    const uint4 *src = reinterpret_cast<const uint4 *>(P.xd + (size_t)(entry_of(P.plan, ue, off, i) >> 4) * kXBlk);
-    uint4 *dst = reinterpret_cast<uint4 *>(sm + (size_t)i * kXBlk);
-    for (int q = threadIdx.x; q < kXBlk / 16; q += blockDim.x) dst[q] = __ldcg(src + q);
+    const uint8_t *src = P.xd + (size_t)(entry_of(P.plan, ue, off, i) >> 4) * kXBlk;
+    uint8_t *dst = wsm + (size_t)i * kSBlk;
+#pragma unroll
+    for (int pl = 0; pl < 3; ++pl)
+      *reinterpret_cast<uint4 *>(dst + pl * kSPlane + 16 * lane) =
+          __ldcg(reinterpret_cast<const uint4 *>(src + pl * kXPlane + 512 * warp + 16 * lane));
+    if (lane < 4)
+      *reinterpret_cast<uint4 *>(dst + 3 * kSPlane + 16 * lane) =
+          __ldcg(reinterpret_cast<const uint4 *>(src + 3 * kXPlane + 64 * warp + 16 * lane));
+    if (lane == 4) *reinterpret_cast<float *>(dst + kSUnOff) = __ldcg(reinterpret_cast<const float *>(src + kXUnOff));
   }
-  __syncthreads();
-  const uint8_t *gb = e < 0 ? P.sh_gate : P.gate + (size_t)e * P.stride;
-  const uint8_t *ub = e < 0 ? P.sh_up : P.up + (size_t)e * P.stride;
+  __syncwarp();
   float fa[kMaxPairs], fb[kMaxPairs];
-  group_rows<kH / 256>(gb + (size_t)(8 * tile + g) * kRowUp, ub + (size_t)(8 * tile + g) * kRowUp, sm, kXBlk,
-                       kXPlane, cnt, fa, fb);
+  group_rows<2>(rr, wsm, kSBlk, kSPlane, cnt, fa, fb);
+  __syncthreads();  // every warp's digits are consumed: the part sums take their place
+  float *part = reinterpret_cast<float *>(sm);  // [cnt][4 warps][16 rows]
   const int np = (cnt + 1) >> 1;
 #pragma unroll
   for (int p = 0; p < kMaxPairs; ++p) {
     if (p >= np) break;
-    const float gs = fa[p] + __shfl_xor_sync(0xFFFFFFFFu, fa[p], 1);
-    const float us = fb[p] + __shfl_xor_sync(0xFFFFFFFFu, fb[p], 1);
+    const float va = fa[p] + __shfl_xor_sync(0xFFFFFFFFu, fa[p], 1);
+    const float vb = fb[p] + __shfl_xor_sync(0xFFFFFFFFu, fb[p], 1);
     const int it = 2 * p + (t >> 1);
     if (!(t & 1) && it < cnt) {
-      const int en = entry_of(P.plan, ue, off, it);
-      const float un = *reinterpret_cast<const float *>(sm + (size_t)it * kXBlk + kXUnOff);
-      const float gv = __fmul_rn(gs, un), uv = __fmul_rn(us, un);
-      P.s[((size_t)(en >> 4) * (kK + 1) + (en & 15)) * kI + 8 * tile + g] = __fmul_rn(silu_f(gv), uv);
+      part[(it * 4 + warp) * 16 + g] = va;
+      part[(it * 4 + warp) * 16 + g + 8] = vb;
     }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < cnt * 8; idx += blockDim.x) {  // (token, pair): quarters added in order
+    const int it = idx >> 3, pr = idx & 7;
+    const float *q = part + it * 64;
+    const float gs = __fadd_rn(__fadd_rn(__fadd_rn(q[pr], q[16 + pr]), q[32 + pr]), q[48 + pr]);
+    const float us = __fadd_rn(__fadd_rn(__fadd_rn(q[8 + pr], q[24 + pr]), q[40 + pr]), q[56 + pr]);
+    const int en = entry_of(P.plan, ue, off, it);
+    const float un = __ldcg(reinterpret_cast<const float *>(P.xd + (size_t)(en >> 4) * kXBlk + kXUnOff));
+    P.s[((size_t)(en >> 4) * (kK + 1) + (en & 15)) * kI + 8 * tile + pr] =
+        __fmul_rn(silu_f(__fmul_rn(gs, un)), __fmul_rn(us, un));
   }
 }
 
@@ -261,14 +297,22 @@ struct DnParams {
   int T;
 };
 
-__global__ void __launch_bounds__(128) k_dn_grp(DnParams P) {
+__global__ void __launch_bounds__(128, 4) k_dn_grp(DnParams P) {
   extern __shared__ __align__(16) uint8_t sm[];  // [cnt][kSBlk]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int ue = blockIdx.x / kDnCtasPerExpert;
   const int h0 = (blockIdx.x % kDnCtasPerExpert) * 64 + 16 * warp;
   int cnt, off, e;
-  // the plan is two grids back: complete once the previous grid lets this one start
+  // the plan is two grids back: complete once the previous grid lets this one start, so the
+  // CTA's rows are requested before the s it needs are ready
   const bool live = expert_of(P.plan, ue, P.T, cnt, off, e);
+  RowRegs rr[2];
+  if (live) {
+    const uint8_t *base = e < 0 ? P.sh_down : P.down + (size_t)e * P.stride;
+    const uint8_t *ra = base + (size_t)(h0 + g) * kRowDown, *rb = base + (size_t)(h0 + g + 8) * kRowDown;
+    load_rows(rr[0], ra, rb);
+    load_rows(rr[1], ra + kQB, rb + kQB);
+  }
   pdl_wait();
   pdl_trigger();
   if (!live) return;
@@ -308,10 +352,8 @@ __global__ void __launch_bounds__(128) k_dn_grp(DnParams P) {
     if (lane == 0) *reinterpret_cast<float *>(blk + kSUnOff) = digit_unscale(mx, ks);
   }
   __syncthreads();
-  const uint8_t *base = e < 0 ? P.sh_down : P.down + (size_t)e * P.stride;
   float fa[kMaxPairs], fb[kMaxPairs];
-  group_rows<kI / 256>(base + (size_t)(h0 + g) * kRowDown, base + (size_t)(h0 + g + 8) * kRowDown, sm, kSBlk,
-                       kSPlane, cnt, fa, fb);
+  group_rows<kI / 256>(rr, sm, kSBlk, kSPlane, cnt, fa, fb);
   const int np = (cnt + 1) >> 1;
 #pragma unroll
   for (int p = 0; p < kMaxPairs; ++p) {
@@ -378,6 +420,10 @@ cudaError_t launch_pdl(Kern k, unsigned grid, unsigned block, size_t smem, cudaS
 
 bool g_attr_done[128] = {};
 
+// k_gu_grp's shared memory for up to T tokens per expert: 4 warps' digit quarters + part sums
+constexpr size_t gu_smem(int T) { return (size_t)T * 4 * kSBlk; }
+static_assert(4 * kSBlk >= 4 * 16 * 4, "the part sums fit the digit region");
+
 }  // namespace
 
 int run(const Args &a, cudaStream_t s) {
@@ -385,7 +431,7 @@ int run(const Args &a, cudaStream_t s) {
   int dev = 0;
   B2_CUDA(cudaGetDevice(&dev));
   if (dev >= 0 && dev < 128 && !g_attr_done[dev]) {
-    B2_CUDA(cudaFuncSetAttribute(k_gu_grp, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxT * kXBlk));
+    B2_CUDA(cudaFuncSetAttribute(k_gu_grp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gu_smem(kMaxT)));
     g_attr_done[dev] = true;
   }
   const b200moe_layer *L = a.layer;
@@ -402,7 +448,7 @@ int run(const Args &a, cudaStream_t s) {
   pg.xd = a.xd;
   pg.s = a.s;
   pg.T = a.T;
-  B2_CUDA(launch_pdl(k_gu_grp, experts * kGuCtasPerExpert, 128u, (size_t)a.T * kXBlk, s, pg));
+  B2_CUDA(launch_pdl(k_gu_grp, experts * kGuCtasPerExpert, 128u, gu_smem(a.T), s, pg));
   DnParams pd;
   pd.down = (const uint8_t *)L->down;
   pd.stride = L->down_expert_stride;

@@ -78,11 +78,11 @@ def _tokens(g, device) -> tuple:
 
 
 # At and above this many tokens the grouped-GEMM path is used. Measured on the 40-layer stack
-# (config 2 routing law, one B200): the decode kernels re-read each token's expert rows, about
-# 0.6 ms per token over 40 layers (1.59 ms at 2 tokens, 2.78 at 4, 3.56 at 6, 4.95 at 8), while
-# the grouped GEMMs cost a nearly flat ~3 ms (2.92 ms at 2 tokens, 3.01 at 4, 3.10 at 6, 3.14 at
-# 8, 3.44 at 32): they cross between 4 and 6 tokens.
-PREFILL_MIN_TOKENS = 5
+# (config 2 routing law, one B200): the grouped decode kernels (each distinct expert read once,
+# int8 tensor-core dots) take 1.13 ms at 2 tokens, 1.61 at 4, 2.49 at 8 and 4.81 at 16, the
+# grouped GEMMs a nearly flat ~3 ms (2.92 at 2, 3.01 at 4, 3.19 at 8, 3.31 at 16, 3.44 at 32):
+# they cross between 8 and 16 tokens.
+PREFILL_MIN_TOKENS = 9
 # The decode path runs 2..GROUPED_MAX_TOKENS tokens of a Q4_K layer on the grouped kernels
 # (csrc/grouped.cu: each distinct expert's rows read once for all its tokens).
 GROUPED_MAX_TOKENS = 16
@@ -114,8 +114,10 @@ def moe_block(g: torch.Tensor, E_, layer: int = 0, probe_row=None, out: torch.Te
     ``g``'s leading shape, ``info = {"ids": [B,T,8] int32 (device), "used": int}``.
     Routing is R1-R5 with the cast before the multiply; routed outputs are summed in
     ascending expert id; the shared expert is gated by sigmoid(w_sg . x).
-    ``path``: "decode" (gather-GEMV, f32 CUDA cores), "prefill" (token sort + tcgen05 grouped
-    GEMMs, fp16 operands) or "auto" (prefill from ``PREFILL_MIN_TOKENS`` tokens on). A layer
+    ``path``: "decode" (one token: the persistent kernel; 2..16 tokens of a Q4_K layer: the
+    grouped decode kernels; exact-product int8 tensor-core dots; otherwise the f32 gather-GEMV
+    kernels), "prefill" (token sort + tcgen05 grouped GEMMs, fp16 operands) or "auto" (prefill
+    from ``PREFILL_MIN_TOKENS`` tokens on). A layer
     with Q5_K / Q6_K down or a Q8_0 shared expert (the published Q4_K_M file) runs on the
     decode kernels at every token count; ``path="prefill"`` refuses it. No tokens give empty
     results (as the reference's own loop does), with no device work. ``check=True`` reads the
