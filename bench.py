@@ -473,9 +473,10 @@ def bench_prefill_ep(dev, rank, world, K, W, tf_peak, T_total=4096, seed=3, chec
         ms = float(tt.item())
     # per-stage times: eager steps with an event after each stage
     names = ("route", "dispatch", "experts", "combine", "sum")
-    acc = {n: 0.0 for n in names}
+    per = {n: [] for n in names}
     reps = 5
-    for _ in range(reps):
+    for rep in range(reps + 1):  # the first rep is discarded; the median of the rest is kept
+        # (an eager stage interval also holds any host stall before its launch)
         evs = [torch.cuda.Event(enable_timing=True)]
         evs[0].record()
 
@@ -486,9 +487,10 @@ def bench_prefill_ep(dev, rank, world, K, W, tf_peak, T_total=4096, seed=3, chec
 
         ep.forward(x_loc, out=out, mark=mark)
         torch.cuda.synchronize(dev)
-        for i, n in enumerate(names):
-            acc[n] += evs[i].elapsed_time(evs[i + 1]) / reps
-    stages = {n: acc[n] for n in names}
+        if rep:
+            for i, n in enumerate(names):
+                per[n].append(evs[i].elapsed_time(evs[i + 1]))
+    stages = {n: statistics.median(per[n]) for n in names}
     if world > 1:
         tt = torch.tensor([stages[n] for n in names], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)

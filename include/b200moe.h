@@ -126,9 +126,12 @@ int b200moe_router(const void *x, int x_dtype, int T, const void *router_w, int 
 /* Workspace bytes for b200moe_moe_decode with T tokens. */
 size_t b200moe_decode_workspace_size(int T);
 
-/* One MoE layer over T tokens (the gather-GEMV decode path): out [T][2048] f32 =
+/* One MoE layer over T tokens (the decode paths): out [T][2048] f32 =
  * routed (8 experts, weights R5-cast, summed in ascending expert id) + sigmoid(w_sg.x) *
- * shared expert. ids_out [T][8] / w_out [T][8] bf16 may be NULL.
+ * shared expert. ids_out [T][8] / w_out [T][8] bf16 may be NULL. T = 1 runs the persistent
+ * kernel; 2..16 tokens of a Q4_K layer the grouped kernels (each distinct expert's rows read
+ * once for all its tokens, exact-product int8 tensor-core dots); otherwise the per-token
+ * gather-GEMV kernels.
  * Replaces engine/m3_forward.py:430 moe_block (and the MoE stages of
  * engine/block_forward.py:670 moe_block). */
 int b200moe_moe_decode(const void *x, int x_dtype, int T, const b200moe_layer *layer,

@@ -38,7 +38,9 @@ using namespace b2;
 namespace {
 
 // ------------------------------------------------------------------------- K1
-constexpr int kK1Ctas = kE / 4 + 1;  // 64 router CTAs of 4 warps + 1 shared-gate CTA
+constexpr int kK1Ctas = kE / 4 + 1;  // 64 router CTAs of 4 warps + 1 shared-gate CTA (one row)
+// K1's grid: one row of kK1Ctas CTAs per token up to 16 rows (the rows split the tokens)
+inline dim3 k1_grid(int T) { return dim3((unsigned)kK1Ctas, (unsigned)(T < 16 ? T : 16)); }
 
 struct K1Params {
   const void *x;
@@ -200,8 +202,9 @@ __global__ void __launch_bounds__(128) k_router(K1Params P) {
   const float bias = (!gate_cta && P.bias) ? P.bias[e] : 0.0f;
   pdl_wait();
   pdl_trigger();
-  if (P.status && blockIdx.x == 0 && threadIdx.x == 0) *P.status = 0u;  // no bounded waits on this path
-  for (int t = 0; t < P.T; ++t) {
+  if (P.status && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *P.status = 0u;  // no bounded waits here
+  // CTA row y takes tokens y, y + gridDim.y, ... (each token's arithmetic is the same in any row)
+  for (int t = blockIdx.y; t < P.T; t += gridDim.y) {
     float v[64];
     load_x_slice(P, t, lane, v, scr);
     if (blockIdx.x == 0 && warp == 0 && P.xw) {
@@ -210,8 +213,7 @@ __global__ void __launch_bounds__(128) k_router(K1Params P) {
       for (int i = 0; i < 16; ++i)
         *reinterpret_cast<float4 *>(g + 4 * i) = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     }
-    // token t's digit block: one warp of router CTA t (at most 16 tokens, 64 router CTAs)
-    if (blockIdx.x == t && warp == 0 && P.xd) write_digits(v, P.xd + (size_t)t * b2grp::kXBlk, lane);
+    if (blockIdx.x == 0 && warp == 0 && P.xd) write_digits(v, P.xd + (size_t)t * b2grp::kXBlk, lane);
     float acc = 0.0f;
     if (gate_cta) {  // shared-expert gate: any summation order (tolerance-checked)
 #pragma unroll
@@ -486,9 +488,9 @@ __global__ void __launch_bounds__(288) k_down(K3Params P) {
 
 // ------------------------------------------------------------------------- host side
 template <typename Kern, typename... Args>
-cudaError_t launch(Kern k, unsigned grid, unsigned block, size_t smem, cudaStream_t s, bool pdl, Args... args) {
+cudaError_t launch(Kern k, dim3 grid, unsigned block, size_t smem, cudaStream_t s, bool pdl, Args... args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(block);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -653,8 +655,8 @@ int run_layer(const void *x, int x_dtype, float *resid, float eps, int T, const 
     p1.xw = nullptr;
     p1.xd = w.xd;
   }
-  if (p1.wf32) B2_CUDA(launch(k_router<true>, (unsigned)kK1Ctas, 128, 0, s, !first, p1));
-  else B2_CUDA(launch(k_router<false>, (unsigned)kK1Ctas, 128, 0, s, !first, p1));
+  if (p1.wf32) B2_CUDA(launch(k_router<true>, k1_grid(T), 128, 0, s, !first, p1));
+  else B2_CUDA(launch(k_router<false>, k1_grid(T), 128, 0, s, !first, p1));
   if (grouped) {
     b2grp::Args ga = {};
     ga.T = T;
@@ -796,8 +798,8 @@ int b200moe_router(const void *x, int x_dtype, int T, const void *router_w, int 
   K1Params p1 = k1_params(x, x_dtype, nullptr, 0.f, T, &L, w);
   p1.wsg = nullptr;
   p1.xw = nullptr;
-  if (p1.wf32) B2_CUDA(launch(k_router<true>, (unsigned)kK1Ctas, 128, 0, s, false, p1));
-  else B2_CUDA(launch(k_router<false>, (unsigned)kK1Ctas, 128, 0, s, false, p1));
+  if (p1.wf32) B2_CUDA(launch(k_router<true>, k1_grid(T), 128, 0, s, false, p1));
+  else B2_CUDA(launch(k_router<false>, k1_grid(T), 128, 0, s, false, p1));
   B2_CUDA(launch(k_route_tail, (unsigned)T, 32, 0, s, true, (const uint16_t *)w.logits, ids, w_f32, w_bf16));
   return B200MOE_OK;
 }

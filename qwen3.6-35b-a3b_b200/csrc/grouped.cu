@@ -118,11 +118,12 @@ __device__ __forceinline__ bool expert_of(const Plan *pl, int ue, int T, int &cn
     e = -1;
     return true;
   }
-  if (ue - 1 >= __ldcg(&pl->n_u)) return false;
+  // all four loads in flight at once (index ue - 1 < 8T is inside the arrays either way)
+  const int n_u = __ldcg(&pl->n_u);
   e = __ldcg(&pl->e[ue - 1]);
   cnt = __ldcg(&pl->cnt[ue - 1]);
   off = __ldcg(&pl->off[ue - 1]);
-  return true;
+  return ue - 1 < n_u;
 }
 
 __device__ __forceinline__ int entry_of(const Plan *pl, int ue, int off, int i) {
@@ -244,17 +245,23 @@ __global__ void __launch_bounds__(128, 4) k_gu_grp(GuParams P) {
   load_rows(rr[1], ra + kQB, rb + kQB);
   // this warp's K quarter of each token's digits: 512 bytes of each plane, 16 sums, 2^-k
   uint8_t *wsm = sm + (size_t)warp * cnt * kSBlk;
+  // lane i holds entry i (one load for all tokens); two tokens' loads in flight per step
+  const int my_en = lane < cnt ? entry_of(P.plan, ue, off, lane) : 0;
+#pragma unroll 2
   for (int i = 0; i < cnt; ++i) {
-    const uint8_t *src = P.xd + (size_t)(entry_of(P.plan, ue, off, i) >> 4) * kXBlk;
+    const uint8_t *src = P.xd + (size_t)(__shfl_sync(0xFFFFFFFFu, my_en, i) >> 4) * kXBlk;
     uint8_t *dst = wsm + (size_t)i * kSBlk;
+    uint4 pv[3], sv = make_uint4(0u, 0u, 0u, 0u);
+    float uv = 0.0f;
 #pragma unroll
     for (int pl = 0; pl < 3; ++pl)
-      *reinterpret_cast<uint4 *>(dst + pl * kSPlane + 16 * lane) =
-          __ldcg(reinterpret_cast<const uint4 *>(src + pl * kXPlane + 512 * warp + 16 * lane));
-    if (lane < 4)
-      *reinterpret_cast<uint4 *>(dst + 3 * kSPlane + 16 * lane) =
-          __ldcg(reinterpret_cast<const uint4 *>(src + 3 * kXPlane + 64 * warp + 16 * lane));
-    if (lane == 4) *reinterpret_cast<float *>(dst + kSUnOff) = __ldcg(reinterpret_cast<const float *>(src + kXUnOff));
+      pv[pl] = __ldcg(reinterpret_cast<const uint4 *>(src + pl * kXPlane + 512 * warp + 16 * lane));
+    if (lane < 4) sv = __ldcg(reinterpret_cast<const uint4 *>(src + 3 * kXPlane + 64 * warp + 16 * lane));
+    if (lane == 4) uv = __ldcg(reinterpret_cast<const float *>(src + kXUnOff));
+#pragma unroll
+    for (int pl = 0; pl < 3; ++pl) *reinterpret_cast<uint4 *>(dst + pl * kSPlane + 16 * lane) = pv[pl];
+    if (lane < 4) *reinterpret_cast<uint4 *>(dst + 3 * kSPlane + 16 * lane) = sv;
+    if (lane == 4) *reinterpret_cast<float *>(dst + kSUnOff) = uv;
   }
   __syncwarp();
   float fa[kMaxPairs], fb[kMaxPairs];

@@ -79,7 +79,7 @@ def _tokens(g, device) -> tuple:
 
 # At and above this many tokens the grouped-GEMM path is used. Measured on the 40-layer stack
 # (config 2 routing law, one B200): the grouped decode kernels (each distinct expert read once,
-# int8 tensor-core dots) take 1.13 ms at 2 tokens, 1.61 at 4, 2.49 at 8 and 4.81 at 16, the
+# int8 tensor-core dots) take 1.05 ms at 2 tokens, 1.36 at 4, 2.14 at 8 and 3.68 at 16, the
 # grouped GEMMs a nearly flat ~3 ms (2.92 at 2, 3.01 at 4, 3.19 at 8, 3.31 at 16, 3.44 at 32):
 # they cross between 8 and 16 tokens.
 PREFILL_MIN_TOKENS = 9
