@@ -107,6 +107,9 @@ def parse():
     p.add_argument("--path", choices=["auto", "decode", "prefill"], default="auto",
                    help="stack_decode with T >= 2: the decode kernels or the grouped-GEMM path (auto: the "
                         "block's own choice by token count)")
+    p.add_argument("--law", type=int, choices=[1, 2], default=1,
+                   help="Q4_K field law of the stack: 1 = BASELINE's; 2 = the same blocks with d * 2^-6 and "
+                        "dmin * 2^-2 (centred weights: O(1) residual, diverse routing through the stack)")
     p.add_argument("--zipf", action="store_true",
                    help="config 2's routing law: a per-expert Zipf(1.1) logit bias on every layer")
     p.add_argument("--formats", choices=["q4k", "published"], default="q4k",
@@ -558,6 +561,10 @@ def run_b200(args):
     if args.workload == "stack_decode":
         eng = (published_engine(args.seed, args.layers, dev) if args.formats == "published"
                else DeviceEngine.synthetic(args.seed, args.layers, dev, bias=args.zipf))
+        if args.law == 2 and args.formats == "q4k":
+            for Lw in eng.layers:
+                for t in (Lw.gate, Lw.up, Lw.down, Lw.sh_gate, Lw.sh_up, Lw.sh_down):
+                    synth.law2_blocks_(t)
         nl = args.layers
         persist_ctas, persist_cluster = _abi.decode_persistent_info() if T == 1 else (0, 0)
         if args.formats == "published" and not _abi.decode_persistent_formats():
@@ -757,7 +764,9 @@ def run_b200(args):
                    "prefill": "moe_prefill_tok_per_s", "prefill_ep": "moe_prefill_ep_tok_per_s"}[args.workload],
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
-        "data": ("synthetic (seeded Q4_K, config-0 field law; random-init weights)" if args.formats == "q4k" else
+        "data": (("synthetic (seeded Q4_K, config-0 field law; random-init weights)" if args.law == 1 else
+                  "synthetic (seeded Q4_K, config-0 blocks with d * 2^-6 and dmin * 2^-2: centred weights)")
+                 if args.formats == "q4k" else
                  "synthetic, published-file layout (Q4_K gate/up, Q5_K/Q6_K down, Q8_0 shared, F32 router; "
                  "seeded random block bytes)"),
         "config": {"workload": {"stack_decode": ("published_formats_stack_decode_b%d" if args.formats == "published"
@@ -766,7 +775,7 @@ def run_b200(args):
                                 "layer_decode": "config0_layer_decode_b%d" % T,
                                 "prefill": "config3_prefill_t%d" % T,
                                 "prefill_ep": "config3_prefill_ep_t%d" % (T * world)}[args.workload],
-                   "layers": nl, "batch": T, "seed": args.seed,
+                   "layers": nl, "batch": T, "seed": args.seed, "law": args.law,
                    "parallelism": ("ep%d" % world) if args.workload == "prefill_ep" else "replicas%d" % world,
                    "l2": "inputs larger than L2: distinct token per step, %.0f MB of weights streamed per step"
                          % ((bytes_per_step or 0) / 1e6)},
@@ -802,7 +811,7 @@ def run_b200(args):
 
     # ---------------- nested sub-results (after the headline's timed region)
     if (args.workload == "stack_decode" and args.formats == "q4k" and not args.zipf and T == 1
-            and args.layers == N_LAYERS and not args.no_extras):
+            and args.layers == N_LAYERS and args.law == 1 and not args.no_extras):
         graph = None
         tf_peak = _tf_peak()
         xs = ClockSampler(physical_index(local_rank))

@@ -85,3 +85,34 @@ def zipf_calibrate(seed: int = 2, n_tok: int = 2048, taus=None) -> dict:
         if best is None or d < best[1]:
             best = (tau, d)
     return dict(tau=best[0], l1=best[1])
+
+
+# ---------------------------------------------------------------- a second, centred weight law
+# Under the field law above every Q4_K weight (d sc q - dmin m) has a mean of about +1.2, so a
+# stack of such layers is dominated by one common residual direction after a layer and routing
+# collapses onto the same experts. The second law keeps the seeded blocks and scales each
+# super-block's f16 d by 2^-6 and dmin by 2^-2 (one RNE rounding each), which centres the
+# weights: the residual stays O(1) and routing stays diverse through the stack.
+LAW2_D_SCALE = 2.0 ** -6
+LAW2_DMIN_SCALE = 2.0 ** -2
+
+
+def law2_blocks(blocks: np.ndarray) -> np.ndarray:
+    """Host: a scaled copy of Q4_K blocks (uint8, 144 bytes each)."""
+    b = np.array(blocks, dtype=np.uint8, copy=True).reshape(-1, 144)
+    h = b[:, 0:4].copy().view(np.float16).reshape(-1, 2)
+    h[:, 0] = (h[:, 0] * np.float16(LAW2_D_SCALE)).astype(np.float16)
+    h[:, 1] = (h[:, 1] * np.float16(LAW2_DMIN_SCALE)).astype(np.float16)
+    b[:, 0:4] = h.view(np.uint8).reshape(-1, 4)
+    return b
+
+
+def law2_blocks_(t) -> None:
+    """Device: the same scaling in place on a torch uint8 tensor of Q4_K blocks (the same bytes
+    as law2_blocks: both round the exact product to f16 once, to nearest even)."""
+    import torch
+    b = t.view(-1, 144)
+    h = b[:, 0:4].contiguous().view(torch.float16)
+    h[:, 0] *= LAW2_D_SCALE
+    h[:, 1] *= LAW2_DMIN_SCALE
+    b[:, 0:4] = h.view(torch.uint8)
