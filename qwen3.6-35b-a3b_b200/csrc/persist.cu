@@ -729,6 +729,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
     }
     ph[kBarXLg] ^= 1u;
     if (tid == 0 && !last) mbar_expect_tx(bar + kBarXLg, rx_lg);  // the next layer's logits
+    int e_dn = 0;     // warp 0, lanes 16..23: the expert of slot lane - 16 (its down rows)
     if (warp == 0) {  // lane L: logits 8L .. 8L+7
       const uint4 v = reinterpret_cast<const uint4 *>(lg_s)[lane];
       uint32_t rw[4] = {v.x, v.y, v.z, v.w};
@@ -737,27 +738,36 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       if (lane == 0) {
 #pragma unroll
         for (int g = 0; g < kGuChunks; ++g) mbar_expect_tx(bar + kBarGu0 + g, kGuChunk * kRowPair);
-        mbar_expect_tx(bar + kBarDn, kK * kHr * (uint32_t)row_bytes(down_t(l), kI));
-        armed |= (((1u << kGuChunks) - 1u) << kBarGu0) | (1u << kBarDn);
+        armed |= ((1u << kGuChunks) - 1u) << kBarGu0;
+        if constexpr (kFmt) {
+          mbar_expect_tx(bar + kBarDn, kK * kHr * (uint32_t)row_bytes(down_t(l), kI));
+          armed |= 1u << kBarDn;
+        }
       }
       __syncwarp();
       // Routed bulk copies, one per lane, in the order they are consumed: lanes 0..15 -> chunk
       // lane >> 1 of the gate (even) or up (odd) rows of this CTA's expert; lanes 16..23 -> the
-      // 16 down rows of slot lane - 16 (not needed before the s exchange).
+      // 16 down rows of slot lane - 16 (not needed before the s exchange). Modes 0 / 1 request
+      // the down rows at the start of phase G instead, once the last gate / up chunk has landed,
+      // so they do not share HBM with the gate / up stream (measured 0.642 -> 0.638 ms per
+      // 40-layer token; mode 2, whose CUDA-core gate / up is the bound, keeps them here).
       const int k = lane < 2 * kGuChunks ? slot_c : (lane - 2 * kGuChunks) & 7;
       const int e = __shfl_sync(0xFFFFFFFFu, my_sel, k);
+      e_dn = e;
+      if constexpr (kFmt) {
+        __syncwarp();
+        if (lane >= 2 * kGuChunks && lane < 2 * kGuChunks + kK) {
+          const uint32_t rd = (uint32_t)row_bytes(down_t(l), kI);  // down row bytes at the layer's format
+          const uint8_t *src = (const uint8_t *)Lp.down + (size_t)e * Lp.down_expert_stride + (size_t)(kHr * c) * rd;
+          bulk_g2s(dn + (size_t)k * kHr * rd, src, kHr * rd, bar + kBarDn, pol_first);
+        }
+      }
       if (lane < 2 * kGuChunks) {
         const int g = lane >> 1, which = lane & 1;
         const uint8_t *src = (const uint8_t *)(which ? Lp.up : Lp.gate) + (size_t)e * Lp.gate_up_expert_stride +
                              (size_t)(j_c + g * kGuChunk) * kRowUp;
         bulk_g2s((which ? gu_u : gu_g) + g * SL::kChunkPitch, src, kGuChunk * kRowUp, bar + kBarGu0 + g,
                  pol_first);
-      }
-      __syncwarp();
-      if (lane >= 2 * kGuChunks && lane < 2 * kGuChunks + kK) {
-        const uint32_t rd = (uint32_t)row_bytes(down_t(l), kI);  // down row bytes (kRowDown for Q4_K)
-        const uint8_t *src = (const uint8_t *)Lp.down + (size_t)e * Lp.down_expert_stride + (size_t)(kHr * c) * rd;
-        bulk_g2s(dn + (size_t)k * kHr * rd, src, kHr * rd, bar + kBarDn, pol_first);
       }
       __syncwarp();
       route_finish(rw, mine, rr);  // R2, R4, R5 while the rows stream in
@@ -782,6 +792,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
           have |= 1u << bit;
         }
       };
+      if (!kFmt && warp == 0) {  // modes 0 / 1: the routed down rows, once the last gate / up chunk has landed
+        __syncwarp();
+        need_bits(1u << kGuChunks);
+        if (!fail) {
+          const uint32_t rd = (uint32_t)row_bytes(down_t(l), kI);  // down row bytes (kRowDown for Q4_K)
+          if (lane == 0) {
+            mbar_expect_tx(bar + kBarDn, kK * kHr * rd);
+            armed |= 1u << kBarDn;
+          }
+          __syncwarp();
+          if (lane >= 2 * kGuChunks && lane < 2 * kGuChunks + kK) {
+            const int k = lane - 2 * kGuChunks;
+            const uint8_t *src = (const uint8_t *)Lp.down + (size_t)e_dn * Lp.down_expert_stride + (size_t)(kHr * c) * rd;
+            bulk_g2s(dn + (size_t)k * kHr * rd, src, kHr * rd, bar + kBarDn, pol_first);
+          }
+          __syncwarp();
+        }
+      }
       if (warp > 0) {
         __syncwarp();
         if (warp >= kRtRows) rs = rms_scale();
