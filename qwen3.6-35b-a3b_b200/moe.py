@@ -79,10 +79,10 @@ def _tokens(g, device) -> tuple:
 
 # At and above this many tokens the grouped-GEMM path is used. Measured on the 40-layer stack
 # (config 2 routing law, one B200): the grouped decode kernels (each distinct expert read once,
-# int8 tensor-core dots) take 1.05 ms at 2 tokens, 1.36 at 4, 2.14 at 8 and 3.68 at 16, the
-# grouped GEMMs a nearly flat ~3 ms (2.92 at 2, 3.01 at 4, 3.19 at 8, 3.31 at 16, 3.44 at 32):
-# they cross between 8 and 16 tokens.
-PREFILL_MIN_TOKENS = 9
+# int8 tensor-core dots) take 1.05 ms at 2 tokens, 1.36 at 4, 2.14 at 8, 2.97 at 12 and 3.66 at
+# 16, the grouped GEMMs a nearly flat ~3 ms (2.92 at 2, 3.01 at 4, 3.19 at 8, 3.20 at 12, 3.27 at
+# 16, 3.44 at 32): they cross between 12 and 16 tokens.
+PREFILL_MIN_TOKENS = 13
 # The decode path runs 2..GROUPED_MAX_TOKENS tokens of a Q4_K layer on the grouped kernels
 # (csrc/grouped.cu: each distinct expert's rows read once for all its tokens).
 GROUPED_MAX_TOKENS = 16

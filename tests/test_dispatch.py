@@ -26,7 +26,7 @@ def _layer(down="Q4_K", sh="Q4_K"):
     return mk(down, sh)
 
 
-@pytest.mark.parametrize("T,want", [(1, "decode"), (4, "decode"), (8, "decode"), (9, "prefill"), (64, "prefill")])
+@pytest.mark.parametrize("T,want", [(1, "decode"), (4, "decode"), (12, "decode"), (13, "prefill"), (64, "prefill")])
 def test_q4k_layer_auto_path(rec, T, want):
     import torch
     from b200moe import moe
