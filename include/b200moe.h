@@ -179,6 +179,9 @@ int b200moe_moe_decode_stages(const void *x, int x_dtype, int T, const b200moe_l
  * The looked-up address is cached per device ordinal for the life of the process and does not
  * survive cudaDeviceReset (or any re-creation of the device's primary context): do not call
  * this entry point after such a reset. b200moe_decode_noalloc_status reads its status word.
+ * For 2..16 tokens it runs the per-token gather-GEMV kernels (the grouped kernels' buffers are
+ * not part of the static array), whose outputs agree with b200moe_moe_decode's within the decode
+ * parity bar (same routing ids and weights); one token runs the same persistent kernel.
  * Allocates nothing (no cudaMalloc / cudaFree, no allocating library routine). */
 int b200moe_moe_decode_noalloc(const void *x, int x_dtype, int T, const b200moe_layer *layer,
                                float *out, int32_t *ids_out, uint16_t *w_out, void *stream);
