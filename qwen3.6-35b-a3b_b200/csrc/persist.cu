@@ -754,20 +754,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_mega(const __grid_constant__ Me
       const int k = lane < 2 * kGuChunks ? slot_c : (lane - 2 * kGuChunks) & 7;
       const int e = __shfl_sync(0xFFFFFFFFu, my_sel, k);
       e_dn = e;
-      if constexpr (kFmt) {
-        __syncwarp();
-        if (lane >= 2 * kGuChunks && lane < 2 * kGuChunks + kK) {
-          const uint32_t rd = (uint32_t)row_bytes(down_t(l), kI);  // down row bytes at the layer's format
-          const uint8_t *src = (const uint8_t *)Lp.down + (size_t)e * Lp.down_expert_stride + (size_t)(kHr * c) * rd;
-          bulk_g2s(dn + (size_t)k * kHr * rd, src, kHr * rd, bar + kBarDn, pol_first);
-        }
-      }
       if (lane < 2 * kGuChunks) {
         const int g = lane >> 1, which = lane & 1;
         const uint8_t *src = (const uint8_t *)(which ? Lp.up : Lp.gate) + (size_t)e * Lp.gate_up_expert_stride +
                              (size_t)(j_c + g * kGuChunk) * kRowUp;
         bulk_g2s((which ? gu_u : gu_g) + g * SL::kChunkPitch, src, kGuChunk * kRowUp, bar + kBarGu0 + g,
                  pol_first);
+      }
+      if constexpr (kFmt) {  // mode 2: the down rows right behind the gate / up rows
+        __syncwarp();
+        if (lane >= 2 * kGuChunks && lane < 2 * kGuChunks + kK) {
+          const uint32_t rd = (uint32_t)row_bytes(down_t(l), kI);  // down row bytes at the layer's format
+          const uint8_t *src = (const uint8_t *)Lp.down + (size_t)e * Lp.down_expert_stride + (size_t)(kHr * c) * rd;
+          bulk_g2s(dn + (size_t)k * kHr * rd, src, kHr * rd, bar + kBarDn, pol_first);
+        }
       }
       __syncwarp();
       route_finish(rw, mine, rr);  // R2, R4, R5 while the rows stream in
