@@ -234,15 +234,21 @@ __global__ void __launch_bounds__(128, 4) k_gu_grp(GuParams P) {
   extern __shared__ __align__(16) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int ue = blockIdx.x / kGuCtasPerExpert, tile = blockIdx.x % kGuCtasPerExpert;
+  const size_t row_off = (size_t)(8 * tile + g) * kRowUp + 2 * warp * kQB;
+  RowRegs rr[2];
+  if (ue == 0) {  // the shared expert's rows do not depend on the plan: requested before it is ready
+    load_rows(rr[0], P.sh_gate + row_off, P.sh_up + row_off);
+    load_rows(rr[1], P.sh_gate + row_off + kQB, P.sh_up + row_off + kQB);
+  }
   pdl_wait();
   pdl_trigger();
   int cnt, off, e;
   if (!expert_of(P.plan, ue, P.T, cnt, off, e)) return;
-  const uint8_t *ra = (e < 0 ? P.sh_gate : P.gate + (size_t)e * P.stride) + (size_t)(8 * tile + g) * kRowUp + 2 * warp * kQB;
-  const uint8_t *rb = (e < 0 ? P.sh_up : P.up + (size_t)e * P.stride) + (size_t)(8 * tile + g) * kRowUp + 2 * warp * kQB;
-  RowRegs rr[2];
-  load_rows(rr[0], ra, rb);
-  load_rows(rr[1], ra + kQB, rb + kQB);
+  if (ue != 0) {
+    const uint8_t *ra = P.gate + (size_t)e * P.stride + row_off, *rb = P.up + (size_t)e * P.stride + row_off;
+    load_rows(rr[0], ra, rb);
+    load_rows(rr[1], ra + kQB, rb + kQB);
+  }
   // this warp's K quarter of each token's digits: 512 bytes of each plane, 16 sums, 2^-k
   uint8_t *wsm = sm + (size_t)warp * cnt * kSBlk;
   // lane i holds entry i (one load for all tokens); two tokens' loads in flight per step
