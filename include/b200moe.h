@@ -123,7 +123,8 @@ int b200moe_router(const void *x, int x_dtype, int T, const void *router_w, int 
                    const float *logit_bias, uint16_t *logits, int32_t *ids, float *w_f32,
                    uint16_t *w_bf16, void *ws, size_t ws_bytes, void *stream);
 
-/* Workspace bytes for b200moe_moe_decode with T tokens. */
+/* Workspace bytes for b200moe_moe_decode with T tokens (0 for T outside [1, 65536]). The size
+ * never shrinks as T grows, so a workspace sized for T tokens serves every smaller T. */
 size_t b200moe_decode_workspace_size(int T);
 
 /* One MoE layer over T tokens (the decode paths): out [T][2048] f32 =

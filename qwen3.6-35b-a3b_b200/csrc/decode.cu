@@ -525,11 +525,13 @@ constexpr size_t decode_ws_base(int T) {
 constexpr bool grouped_t(int T) { return T >= 2 && T <= b2grp::kMaxT; }
 
 // The grouped path's buffers, after the base layout: x digit blocks, the plan, the unweighted
-// expert outputs.
+// expert outputs. Above kMaxT tokens (no grouped path) the size keeps the kMaxT figure, so the
+// workspace size never shrinks as T grows: a workspace sized for T tokens serves every smaller T.
 constexpr size_t grouped_ws_extra(int T) {
-  return grouped_t(T) ? align256((size_t)T * b2grp::kXBlk) + align256(b2grp::kPlanBytes) +
-                            align256((size_t)T * (kK + 1) * kH * 4)
-                      : 0;
+  return T < 2 ? 0
+               : align256((size_t)(T < b2grp::kMaxT ? T : b2grp::kMaxT) * b2grp::kXBlk) +
+                     align256(b2grp::kPlanBytes) +
+                     align256((size_t)(T < b2grp::kMaxT ? T : b2grp::kMaxT) * (kK + 1) * kH * 4);
 }
 
 constexpr size_t decode_ws_bytes(int T) { return decode_ws_base(T) + grouped_ws_extra(T); }

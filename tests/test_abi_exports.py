@@ -36,6 +36,18 @@ def test_errors_without_device_work():
     assert L.b200moe_decode_workspace_size(1) > 0
 
 
+def test_workspace_sizes_monotonic():
+    """A workspace sized for T tokens serves every smaller T (the sizes never shrink as T grows,
+    across the grouped path's 16-token limit too), and the stack's size is the decode size."""
+    from b200moe import _abi
+    L = _abi.lib()
+    sizes = [L.b200moe_decode_workspace_size(T) for T in range(1, 70)]
+    assert all(b >= a for a, b in zip(sizes, sizes[1:])), sizes
+    assert all(L.b200moe_stack_workspace_size(T, 40) == L.b200moe_decode_workspace_size(T) for T in (1, 2, 16, 17, 64))
+    # from 2 tokens the grouped path's buffers (digit planes, plan, expert outputs) are included
+    assert sizes[1] - sizes[0] > 2 * 9 * 2048 * 4
+
+
 def test_block_type_validation_without_device_work():
     """The layer's block types and the down stride they imply are checked before any CUDA
     call: unknown types, a Q4_K-sized stride for Q5_K rows, and a grouped-GEMM call on a layer
